@@ -1,0 +1,92 @@
+"""Bottom-right causal attention of new queries over an ancestor chain (K04′).
+
+``chunked_attention(q, k_chunks, v_chunks, scale)``: ``q`` is [T, Hq, d]; the
+key/value chain is the concatenation of the chunks ([S_i, Hkv, d] each,
+ancestors first, the queries' own keys last). Query ``t`` sees keys
+``j <= S - T + t`` (bottom-right alignment): every ancestor key is visible
+and the own chunk is causal. GQA maps query head ``h`` to KV head
+``h // (Hq / Hkv)``. One autograd node holds per-chunk references, so
+retention stays O(total tokens) rather than sum-of-prefixes (reference:
+src/thundersync/engine/streaming.py:1314-1423, ``_ChunkedCausalSDPA``).
+
+On CUDA the forward and backward are this package's kernels: the forward
+writes ``O`` and the row log-sum-exp, the backward recomputes ``P`` from the
+saved LSE (no ``S × T`` buffers) and produces dQ without atomics.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from thundersync_b200.ops._ext import native
+
+
+def attention_reference(q, k, v, scale):
+    """fp32 oracle: [T,Hq,d] x [S,Hkv,d] -> ([T,Hq,d], lse [Hq,T])."""
+    t, hq, d = q.shape
+    s, hkv, _ = k.shape
+    g = hq // hkv
+    qf = q.float().transpose(0, 1)
+    kf = k.float().repeat_interleave(g, dim=1).transpose(0, 1)
+    vf = v.float().repeat_interleave(g, dim=1).transpose(0, 1)
+    logits = torch.matmul(qf, kf.transpose(1, 2)) * scale
+    qi = torch.arange(t, device=q.device)[:, None]
+    kj = torch.arange(s, device=q.device)[None, :]
+    mask = kj <= (s - t + qi)
+    logits = logits.masked_fill(~mask, float("-inf"))
+    lse = torch.logsumexp(logits, dim=-1)
+    p = torch.exp(logits - lse[..., None])
+    out = torch.matmul(p, vf).transpose(0, 1)
+    return out.to(q.dtype), lse
+
+
+class _ChunkedAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, scale, n, *kv):
+        ks, vs = kv[:n], kv[n:]
+        k = ks[0] if n == 1 else torch.cat(ks, 0)
+        v = vs[0] if n == 1 else torch.cat(vs, 0)
+        if q.is_cuda:
+            out, lse = native().attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), float(scale))
+        else:
+            out, lse = attention_reference(q, k, v, scale)
+        ctx.scale = scale
+        ctx.n = n
+        ctx.lens = [t.shape[0] for t in ks]
+        ctx.save_for_backward(q, out, lse, *kv)
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        q, out, lse, *kv = ctx.saved_tensors
+        n = ctx.n
+        ks, vs = kv[:n], kv[n:]
+        k = ks[0] if n == 1 else torch.cat(ks, 0)
+        v = vs[0] if n == 1 else torch.cat(vs, 0)
+        if q.is_cuda:
+            dq, dk, dv = native().attn_bwd(
+                do.contiguous(), q.contiguous(), k.contiguous(), v.contiguous(), out, lse, float(ctx.scale)
+            )
+        else:
+            with torch.enable_grad():
+                q_ = q.detach().requires_grad_(True)
+                k_ = k.detach().requires_grad_(True)
+                v_ = v.detach().requires_grad_(True)
+                o_, _ = attention_reference(q_, k_, v_, ctx.scale)
+                dq, dk, dv = torch.autograd.grad(o_, (q_, k_, v_), do)
+        dks = list(torch.split(dk, ctx.lens, 0))
+        dvs = list(torch.split(dv, ctx.lens, 0))
+        grads = []
+        for i, g in enumerate(dks + dvs):
+            grads.append(g if ctx.needs_input_grad[3 + i] else None)
+        return (dq if ctx.needs_input_grad[0] else None, None, None, *grads)
+
+
+def chunked_attention(q, k_chunks, v_chunks, scale=None):
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    if len(k_chunks) != len(v_chunks) or not k_chunks:
+        raise ValueError("need matching, non-empty key and value chunk lists")
+    return _ChunkedAttention.apply(q, float(scale), len(k_chunks), *k_chunks, *v_chunks)

@@ -1,0 +1,103 @@
+"""Fused QK-norm + RoPE + head split of the QKV projection output.
+
+One pass over ``qkv = x @ [Wq;Wk;Wv]ᵀ`` of shape [T, (Hq + 2·Hkv)·d] produces
+contiguous ``q`` [T, Hq, d] and ``k`` [T, Hkv, d] (per-head RMSNorm, then the
+rotate-half rotary embedding at the given positions) and ``v`` [T, Hkv, d].
+On CUDA the angle ``pos · inv_freq[i]`` is formed in fp32 inside the kernel
+and passed to CUDA's ``sincosf``; no cos/sin tables are materialised. The
+backward reads ``qkv`` again and recomputes the norm statistics.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from thundersync_b200.ops import sink as _sink
+from thundersync_b200.ops._ext import native
+from thundersync_b200.ops.norm import rms_norm_reference
+
+
+def rope_inv_freq(head_dim: int, theta: float, device=None) -> torch.Tensor:
+    """fp32 inverse frequencies ``1 / theta^(2i/d)``, i < d/2 (Qwen3/HF convention)."""
+    idx = torch.arange(0, head_dim, 2, dtype=torch.int64, device=device).float()
+    return 1.0 / (theta ** (idx / head_dim))
+
+
+def _rotate_half(x):
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def qk_norm_rope_reference(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps):
+    """Differentiable fp32 oracle of the fused op."""
+    t = qkv.shape[0]
+    q = qkv[:, : hq * d].reshape(t, hq, d)
+    k = qkv[:, hq * d : (hq + hkv) * d].reshape(t, hkv, d)
+    v = qkv[:, (hq + hkv) * d :].reshape(t, hkv, d)
+    if q_w is not None:
+        q = rms_norm_reference(q, q_w, eps)
+        k = rms_norm_reference(k, k_w, eps)
+    freqs = pos.float()[:, None] * inv_freq.float()[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos, sin = emb.cos()[:, None, :], emb.sin()[:, None, :]
+    qo = (q.float() * cos + _rotate_half(q.float()) * sin).to(qkv.dtype)
+    ko = (k.float() * cos + _rotate_half(k.float()) * sin).to(qkv.dtype)
+    return qo, ko, v.contiguous()
+
+
+class _QKNormRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps):
+        ctx.meta = (hq, hkv, d, eps)
+        ctx.has_norm = q_w is not None
+        if qkv.is_cuda:
+            q, k, v = native().qk_norm_rope_fwd(
+                qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(), hq, hkv, d, float(eps)
+            )
+        else:
+            with torch.no_grad():
+                q, k, v = qk_norm_rope_reference(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps)
+        ctx.save_for_backward(qkv, q_w, k_w, pos, inv_freq)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        qkv, q_w, k_w, pos, inv_freq = ctx.saved_tensors
+        hq, hkv, d, eps = ctx.meta
+        t = qkv.shape[0]
+        dq = torch.zeros(t, hq, d, dtype=qkv.dtype, device=qkv.device) if dq is None else dq.contiguous()
+        dk = torch.zeros(t, hkv, d, dtype=qkv.dtype, device=qkv.device) if dk is None else dk.contiguous()
+        dv = torch.zeros(t, hkv, d, dtype=qkv.dtype, device=qkv.device) if dv is None else dv.contiguous()
+        if qkv.is_cuda:
+            dqkv, dqw, dkw = native().qk_norm_rope_bwd(
+                dq, dk, dv, qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(),
+                hq, hkv, d, float(eps),
+            )
+        else:
+            with torch.enable_grad():
+                qkv_ = qkv.detach().requires_grad_(True)
+                qw_ = None if q_w is None else q_w.detach().requires_grad_(True)
+                kw_ = None if k_w is None else k_w.detach().requires_grad_(True)
+                outs = qk_norm_rope_reference(qkv_, qw_, kw_, pos, inv_freq, hq, hkv, d, eps)
+                ins = [qkv_] + ([qw_, kw_] if qw_ is not None else [])
+                grads = torch.autograd.grad(outs, ins, (dq, dk, dv), allow_unused=True)
+            dqkv = grads[0]
+            dqw = grads[1].float() if qw_ is not None else None
+            dkw = grads[2].float() if kw_ is not None else None
+        gq = gk = None
+        if ctx.has_norm:
+            s = _sink.active()
+            for w, g, idx in ((q_w, dqw, 1), (k_w, dkw, 2)):
+                if not ctx.needs_input_grad[idx]:
+                    continue
+                if s is not None and s.owns(w):
+                    s.add_(w, g)
+                elif idx == 1:
+                    gq = g.to(w.dtype)
+                else:
+                    gk = g.to(w.dtype)
+        return dqkv, gq, gk, None, None, None, None, None, None
+
+
+def qk_norm_rope(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps):
+    return _QKNormRope.apply(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps)
