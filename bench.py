@@ -1,0 +1,377 @@
+"""Streaming-GRPO throughput benchmark (Qwen3-1.7B full fine-tune).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch one process per GPU with torch.distributed.run; every rank
+reads RANK / LOCAL_RANK / WORLD_SIZE / MASTER_* from the environment.
+
+Workload per rank and step (weak scaling: fixed per GPU, 64 groups total at 8
+GPUs): 8 groups x 8 trajectories of a random-init Qwen3-1.7B-architecture
+model in bf16 (fp32 master weights and Adam moments). Prompts are 512 uniform
+token ids, completions uniform in [256, 4096] tokens, every completion token
+scored, rewards Bernoulli(0.3). Each trajectory's completion time is
+Exponential(mean 2 s); trajectories are delivered in that arrival order, as
+fast as the trainer consumes them, so groups interleave exactly as they
+would under streaming arrival.
+
+One step = open every group (prompt forward), then for each arrival:
+append_turn + close_trajectory (reward arrives; the trajectory is
+differentiated and folded), close_group when a group's last reward lands,
+then the DP step (gradient mean across ranks, clip 1.0, AdamW maximize).
+
+Reported: scored completion tokens per second for the whole job (device-timed
+with CUDA events around K steps, max over ranks), and the post-last-reward
+tail: device time from the delivery of the step's last reward to the end of
+the optimizer step. The e2e figure is wall-clock over the same steps through
+the public API, which copies each step's token ids host->device from pinned
+memory and reads the gradient norm back.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import random
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "scored tokens/sec/box per GRPO step"
+BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric
+
+
+# ----------------------------------------------------------------------------- workload
+def make_step(rank: int, step: int, args) -> dict:
+    rng = random.Random(args.seed * 1_000_003 + rank * 10_007 + step)
+    groups = []
+    arrivals = []
+    for g in range(args.groups_per_rank):
+        prompt = [rng.randrange(args.vocab) for _ in range(args.prompt_len)]
+        tids = []
+        for j in range(args.group_size):
+            tid = g * args.group_size + j
+            n = rng.randint(args.min_len, args.max_len)
+            tokens = [rng.randrange(args.vocab) for _ in range(n)]
+            reward = 1.0 if rng.random() < args.reward_p else 0.0
+            t_arrive = rng.expovariate(1.0 / args.mean_arrival_s)
+            arrivals.append((t_arrive, g, tid, tokens, reward))
+            tids.append(tid)
+        groups.append((g, prompt, tids))
+    arrivals.sort(key=lambda a: a[0])
+    scored = sum(len(a[3]) for a in arrivals)
+    tokens = scored + sum(len(p) for _, p, _ in groups)
+    return {"groups": groups, "arrivals": arrivals, "scored": scored, "tokens": tokens}
+
+
+def run_step(trainer, work, tail_start: torch.cuda.Event | None):
+    remaining = {g: len(tids) for g, _, tids in work["groups"]}
+    for g, prompt, tids in work["groups"]:
+        trainer.open_group(g, prompt)
+        trainer.register_group_trajectories(g, tids)
+    n = len(work["arrivals"])
+    for i, (_, g, tid, tokens, reward) in enumerate(work["arrivals"]):
+        trainer.append_turn(g, tid, tokens, [True] * len(tokens))
+        if i == n - 1 and tail_start is not None:
+            tail_start.record()
+        trainer.close_trajectory(tid, reward)
+        remaining[g] -= 1
+        if remaining[g] == 0:
+            trainer.close_group(g)
+    return trainer.step()
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, path: str) -> None:
+        self.path = path
+        self.proc = None
+
+    def start(self) -> None:
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpu_indices: list[int]) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        phys = [int(x) for x in visible.split(",")] if visible else gpu_indices
+        want = {phys[i] if i < len(phys) else i for i in gpu_indices}
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    idx = int(parts[0])
+                except ValueError:
+                    continue
+                if idx not in want:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower() in ("active", "1", "yes"):
+                        reasons.add(name)
+        busy = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
+        return {
+            "sm_mhz": statistics.median(busy) if busy else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ----------------------------------------------------------------------------- arms
+def build_ours(args, device):
+    from thundersync_b200.grpo.data_parallel import DataParallelThunderSync
+    from thundersync_b200.models.qwen3 import PRESETS, Qwen3ForCausalLM
+    from thundersync_b200.engine.streaming import StreamingRun, arena_for
+    from thundersync_b200.parallel.optimizer import FlatAdamW
+
+    torch.manual_seed(args.seed)
+    cfg = PRESETS[args.model]
+    with torch.device(device):
+        model = Qwen3ForCausalLM(cfg)
+    model.to(dtype=torch.bfloat16)
+    arena = arena_for(model)
+    opt = FlatAdamW(arena, lr=args.lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, maximize=True)
+
+    def factory(m):
+        return StreamingRun(m, boundary_cut=True, checkpoint=False, stream_turns=False,
+                            rebuild_block_tokens=args.block_tokens)
+
+    trainer = DataParallelThunderSync.init_from_env(
+        model, opt, run_factory=factory, grad_clip=1.0,
+        source_offload_device=None, source_offload_mode="device_resident",
+    )
+    trainer.configure_binary_rewards()
+    return model, trainer
+
+
+def build_reference(args, device):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "thundersync")):
+        raise RuntimeError("reference not installed under baseline/_ref")
+    sys.path.insert(0, ref)
+    from transformers import AutoConfig, AutoModelForCausalLM
+
+    from thundersync import STREAM_ATTENTION_NAME, register_stream_attention
+    from thundersync.engine.streaming import StreamingRun
+    from thundersync.grpo.data_parallel import DataParallelThunderSync
+
+    from thundersync_b200.models.qwen3 import PRESETS
+
+    c = PRESETS[args.model]
+    register_stream_attention()
+    hf_cfg = AutoConfig.for_model(
+        "qwen3", vocab_size=c.vocab_size, hidden_size=c.hidden_size, intermediate_size=c.intermediate_size,
+        num_hidden_layers=c.num_hidden_layers, num_attention_heads=c.num_attention_heads,
+        num_key_value_heads=c.num_key_value_heads, head_dim=c.head_dim, rms_norm_eps=c.rms_norm_eps,
+        rope_theta=c.rope_theta, tie_word_embeddings=c.tie_word_embeddings,
+        max_position_embeddings=c.max_position_embeddings, initializer_range=c.initializer_range,
+    )
+    torch.manual_seed(args.seed)
+    model = AutoModelForCausalLM.from_config(hf_cfg, attn_implementation=STREAM_ATTENTION_NAME,
+                                             dtype=torch.bfloat16).to(device)
+    model.train()
+    opt = torch.optim.AdamW([p for p in model.parameters() if p.requires_grad], lr=args.lr,
+                            betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, maximize=True)
+
+    def factory(m):
+        return StreamingRun(m, boundary_cut=True, checkpoint=True, stream_turns=False,
+                            rebuild_block_tokens=args.block_tokens)
+
+    if not dist.is_initialized():
+        os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
+        os.environ.setdefault("LOCAL_RANK", "0")
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29500 + os.getpid() % 1000))
+    trainer = DataParallelThunderSync.init_from_env(
+        model, opt, run_factory=factory, grad_clip=1.0,
+        source_offload_device="cpu", source_offload_mode="device_resident",
+    )
+    trainer.configure_binary_rewards()
+    return model, trainer
+
+
+# ----------------------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="qwen3-1.7b")
+    ap.add_argument("--groups-per-rank", type=int, default=8)
+    ap.add_argument("--group-size", type=int, default=8)
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--min-len", type=int, default=256)
+    ap.add_argument("--max-len", type=int, default=4096)
+    ap.add_argument("--reward-p", type=float, default=0.3)
+    ap.add_argument("--mean-arrival-s", type=float, default=2.0)
+    ap.add_argument("--block-tokens", type=int, default=4096)
+    ap.add_argument("--lr", type=float, default=1e-5)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--vocab", type=int, default=151936)
+    ap.add_argument("--clocks-file", default=os.path.join(ROOT, "gpurun_out", "bench_clocks.csv"))
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("at least 3 warm-up steps are required")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=900))
+
+    cfg_block = {
+        "model": f"{args.model} architecture, random init N(0,0.02), bf16 weights, fp32 master/Adam",
+        "global_batch": f"{args.groups_per_rank * world} groups x {args.group_size} trajectories",
+        "seq_len": f"prompt {args.prompt_len} + completion U[{args.min_len},{args.max_len}]",
+        "parallelism": f"dp{world}",
+        "rewards": f"Bernoulli({args.reward_p}), arrival order Exp(mean {args.mean_arrival_s}s)",
+        "l2": "no flush needed: every step streams > 3 GB of weights and GBs of statistics (L2 126 MB)",
+    }
+    try:
+        if args.impl == "ours":
+            model, trainer = build_ours(args, device)
+        else:
+            model, trainer = build_reference(args, device)
+    except Exception as exc:  # reference unavailable -> one JSON line and exit 0
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:300]}))
+            return
+        raise
+
+    works = [make_step(rank, s, args) for s in range(args.warmup + args.steps)]
+    from thundersync_b200.ops import _ext
+
+    for s in range(args.warmup):
+        run_step(trainer, works[s], None)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(args.clocks_file) if rank == 0 else None
+    if sampler:
+        os.makedirs(os.path.dirname(args.clocks_file), exist_ok=True)
+        sampler.start()
+    _ext.reset_launch_counts()
+    tails = []
+    scored_local = 0
+    h2d_local = 0
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    wall0 = time.perf_counter()
+    start.record()
+    for s in range(args.warmup, args.warmup + args.steps):
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        st = run_step(trainer, works[s], t0)
+        t1.record()
+        tails.append((t0, t1))
+        scored_local += works[s]["scored"]
+        h2d_local += works[s]["tokens"] * 8
+        _ = st["global_grad_norm"]  # host read of the step result
+    end.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop(list(range(world))) if sampler else None
+    launches = _ext.launch_counts()["kernels"] if args.impl == "ours" else 0
+    dev_ms = start.elapsed_time(end)
+    tail_ms = sum(a.elapsed_time(b) for a, b in tails) / len(tails)
+    vec = torch.tensor([dev_ms, tail_ms, wall * 1e3, float(scored_local), float(h2d_local)], device=device,
+                       dtype=torch.float64)
+    if world > 1:
+        mx = vec.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vec.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    else:
+        mx, sm = vec, vec
+    dev_ms_max, tail_ms_max, wall_ms_max = float(mx[0]), float(mx[1]), float(mx[2])
+    scored_total = float(sm[3])
+    h2d_total = float(sm[4])
+    if rank == 0:
+        value = scored_total / (dev_ms_max / 1e3)
+        e2e = scored_total / (wall_ms_max / 1e3)
+        out = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "scored tokens/s (whole job)",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_ms_max / args.steps, 2),
+            "tail_ms": round(tail_ms_max, 2),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None if BASELINE_VALUE is None else round(value / BASELINE_VALUE, 4),
+            "dtype": "bf16",
+            "data": "synthetic token ids, random-init weights",
+            "config": cfg_block,
+            "clocks": clocks,
+            "e2e": {
+                "value": round(e2e, 1),
+                "unit": "scored tokens/s (wall clock through the public API)",
+                "h2d_bytes_per_step": int(h2d_total / args.steps),
+                "d2h_bytes_per_step": 4 * world,
+            },
+            "gpu_launches": launches,
+        }
+        if args.impl == "reference":
+            out["impl"] = "reference"
+            out["gpu_launches"] = 0
+        print(json.dumps(out))
+    if hasattr(trainer, "shutdown"):
+        trainer.shutdown()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

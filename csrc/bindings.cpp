@@ -1,0 +1,58 @@
+// Python bindings of the thundersync_b200 native kernels.
+#include "common.h"
+
+namespace ts {
+std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps);
+std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                     const at::Tensor& rstd);
+std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
+                                         const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
+                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d, double eps);
+std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk,
+                                                        const at::Tensor& dv, const at::Tensor& qkv,
+                                                        const c10::optional<at::Tensor>& qw,
+                                                        const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
+                                                        const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
+                                                        int64_t d, double eps);
+at::Tensor swiglu_fwd(const at::Tensor& gu);
+at::Tensor swiglu_bwd(const at::Tensor& da, const at::Tensor& gu);
+void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const at::Tensor& dy, double scale);
+void fold_stats(const c10::optional<at::Tensor>& g1, at::Tensor& g2, const at::Tensor& src, double r);
+void axpby(at::Tensor& out, const at::Tensor& x, const c10::optional<at::Tensor>& y, double a, double b);
+void scale(at::Tensor& x, double s);
+void reduce_into(at::Tensor& out, const std::vector<at::Tensor>& parts);
+std::vector<c10::optional<at::Tensor>> lse_gather(const at::Tensor& logits, const at::Tensor& tgt, bool with_entropy);
+at::Tensor logprob_dlogits(const at::Tensor& logits, const at::Tensor& tgt, const at::Tensor& lse,
+                           const at::Tensor& g_lp, const c10::optional<at::Tensor>& g_ent,
+                           const c10::optional<at::Tensor>& ent, bool out_bf16);
+std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale);
+std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                 const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale);
+at::Tensor sq_norm(const at::Tensor& x);
+std::vector<at::Tensor> clip_coef(const at::Tensor& sq, double max_norm);
+void adamw_flat(at::Tensor& master, at::Tensor& param, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
+                double lr, double b1, double b2, double eps, double wd, int64_t step,
+                const c10::optional<at::Tensor>& scale_t, double scale, bool maximize);
+}  // namespace ts
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "thundersync_b200 native sm_100a kernels";
+  m.def("rms_norm_fwd", &ts::rms_norm_fwd);
+  m.def("rms_norm_bwd", &ts::rms_norm_bwd);
+  m.def("qk_norm_rope_fwd", &ts::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &ts::qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &ts::swiglu_fwd);
+  m.def("swiglu_bwd", &ts::swiglu_bwd);
+  m.def("embedding_bwd_accumulate", &ts::embedding_bwd_accumulate);
+  m.def("fold_stats", &ts::fold_stats);
+  m.def("axpby", &ts::axpby);
+  m.def("scale", &ts::scale);
+  m.def("reduce_into", &ts::reduce_into);
+  m.def("lse_gather", &ts::lse_gather);
+  m.def("logprob_dlogits", &ts::logprob_dlogits);
+  m.def("attn_fwd", &ts::attn_fwd);
+  m.def("attn_bwd", &ts::attn_bwd);
+  m.def("sq_norm", &ts::sq_norm);
+  m.def("clip_coef", &ts::clip_coef);
+  m.def("adamw_flat", &ts::adamw_flat);
+}

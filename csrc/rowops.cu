@@ -1,0 +1,662 @@
+// Row-wise memory-bound kernels: RMSNorm (K12'), fused QK-norm + RoPE,
+// SwiGLU and the deterministic embedding backward.
+//
+// All math is fp32; every output is rounded once to the storage dtype. Weight
+// gradients are reduced without atomics: each CTA writes a partial row and a
+// second kernel sums the partials in CTA order, so results are bitwise
+// reproducible run to run.
+#include "common.cuh"
+#include "common.h"
+
+namespace ts {
+namespace {
+
+constexpr int kWarps = 8;
+
+// ----------------------------------------------------------------- RMSNorm fwd
+// One warp per row; the row stays in registers (V 16-byte vectors per lane).
+template <typename T, int V>
+__global__ void __launch_bounds__(kWarps * 32) rms_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                              T* __restrict__ y, float* __restrict__ rstd,
+                                                              int rows, int H, float eps) {
+  constexpr int E = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + (size_t)row * H;
+  Vec<T> buf[V];
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * 32 + lane) * E;
+    if (c < H) {
+      buf[v] = load_vec(xr + c);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float f = to_f(buf[v].e[e]);
+        ss += f * f;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)H + eps);
+  T* yr = y + (size_t)row * H;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * 32 + lane) * E;
+    if (c < H) {
+      Vec<T> wv = load_vec(w + c);
+      Vec<T> o;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float n = round_to<T>(to_f(buf[v].e[e]) * r);
+        o.e[e] = from_f<T>(to_f(wv.e[e]) * n);
+      }
+      store_vec(yr + c, o);
+    }
+  }
+  if (lane == 0) rstd[row] = r;
+}
+
+// ----------------------------------------------------------------- RMSNorm bwd (dx)
+template <typename T, int V>
+__global__ void __launch_bounds__(kWarps * 32) rms_bwd_dx_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                                 const T* __restrict__ w,
+                                                                 const float* __restrict__ rstd,
+                                                                 T* __restrict__ dx, int rows, int H) {
+  constexpr int E = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float r = rstd[row];
+  const T* xr = x + (size_t)row * H;
+  const T* dyr = dy + (size_t)row * H;
+  Vec<T> xb[V], db[V];
+  float dot = 0.f;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * 32 + lane) * E;
+    if (c < H) {
+      xb[v] = load_vec(xr + c);
+      db[v] = load_vec(dyr + c);
+      Vec<T> wv = load_vec(w + c);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float n = to_f(xb[v].e[e]) * r;
+        float dn = to_f(db[v].e[e]) * to_f(wv.e[e]);
+        dot += dn * n;
+      }
+    }
+  }
+  dot = warp_sum(dot) / (float)H;
+  T* dxr = dx + (size_t)row * H;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * 32 + lane) * E;
+    if (c < H) {
+      Vec<T> wv = load_vec(w + c);
+      Vec<T> o;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float n = to_f(xb[v].e[e]) * r;
+        float dn = to_f(db[v].e[e]) * to_f(wv.e[e]);
+        o.e[e] = from_f<T>(r * (dn - n * dot));
+      }
+      store_vec(dxr + c, o);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- column partial sums
+// partial[chunk, c] = sum over the chunk's rows of dy[r, c] * x[r, c] * rstd[r].
+// Block = 32 x 8 threads: x-dim walks 16-byte column vectors, y-dim rows.
+template <typename T>
+__global__ void __launch_bounds__(256) rms_dw_partial_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                             const float* __restrict__ rstd,
+                                                             float* __restrict__ partial, int rows, int H,
+                                                             int rows_per_chunk) {
+  constexpr int E = Vec<T>::N;
+  __shared__ float red[8][32 * E + 1];
+  const int c = (blockIdx.x * 32 + threadIdx.x) * E;
+  const int r0 = blockIdx.y * rows_per_chunk;
+  const int r1 = min(rows, r0 + rows_per_chunk);
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  if (c < H) {
+    for (int r = r0 + threadIdx.y; r < r1; r += 8) {
+      Vec<T> xv = load_vec(x + (size_t)r * H + c);
+      Vec<T> dv = load_vec(dy + (size_t)r * H + c);
+      const float rs = rstd[r];
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] += to_f(dv.e[e]) * (to_f(xv.e[e]) * rs);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) red[threadIdx.y][threadIdx.x * E + e] = acc[e];
+  __syncthreads();
+  if (threadIdx.y == 0 && c < H) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float s = 0.f;
+      for (int k = 0; k < 8; ++k) s += red[k][threadIdx.x * E + e];
+      partial[(size_t)blockIdx.y * H + c + e] = s;
+    }
+  }
+}
+
+// out[c] = sum_k partial[k, c] in k order.
+__global__ void sum_partials_kernel(const float* __restrict__ partial, float* __restrict__ out, int chunks, int H) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  float s = 0.f;
+  for (int k = 0; k < chunks; ++k) s += partial[(size_t)k * H + c];
+  out[c] = s;
+}
+
+template <typename T, int V>
+void launch_rms_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, float eps) {
+  const int rows = x.size(0), H = x.size(1);
+  dim3 grid((rows + kWarps - 1) / kWarps);
+  rms_fwd_kernel<T, V><<<grid, kWarps * 32, 0, stream()>>>(
+      (const T*)x.data_ptr(), (const T*)w.data_ptr(), (T*)y.data_ptr(), rstd.data_ptr<float>(), rows, H, eps);
+}
+
+template <typename T, int V>
+void launch_rms_dx(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                   at::Tensor& dx) {
+  const int rows = x.size(0), H = x.size(1);
+  dim3 grid((rows + kWarps - 1) / kWarps);
+  rms_bwd_dx_kernel<T, V><<<grid, kWarps * 32, 0, stream()>>>(
+      (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)w.data_ptr(), rstd.data_ptr<float>(),
+      (T*)dx.data_ptr(), rows, H);
+}
+
+template <typename T>
+at::Tensor column_weight_grad(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd) {
+  // dw[c] = sum_r dy[r,c] * x[r,c] * rstd[r], deterministic two-level sum.
+  constexpr int E = Vec<T>::N;
+  const int rows = x.size(0), H = x.size(1);
+  const int col_blocks = (H + 32 * E - 1) / (32 * E);
+  const int target = 2 * sm_count(x.get_device());
+  int chunks = std::max(1, std::min((rows + 7) / 8, target / std::max(col_blocks, 1)));
+  const int rows_per_chunk = (rows + chunks - 1) / chunks;
+  chunks = (rows + rows_per_chunk - 1) / rows_per_chunk;
+  auto partial = at::empty({std::max(chunks, 1), H}, x.options().dtype(at::kFloat));
+  auto dw = at::empty({H}, x.options().dtype(at::kFloat));
+  if (rows == 0) return dw.zero_();
+  rms_dw_partial_kernel<T><<<dim3(col_blocks, chunks), dim3(32, 8), 0, stream()>>>(
+      (const T*)dy.data_ptr(), (const T*)x.data_ptr(), rstd.data_ptr<float>(), partial.data_ptr<float>(), rows, H,
+      rows_per_chunk);
+  sum_partials_kernel<<<(H + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(), chunks,
+                                                              H);
+  return dw;
+}
+
+template <typename T>
+void rms_fwd_dispatch(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, float eps) {
+  constexpr int E = Vec<T>::N;
+  const int H = x.size(1);
+  const int nv = (H + 32 * E - 1) / (32 * E);
+  if (nv <= 1) launch_rms_fwd<T, 1>(x, w, y, rstd, eps);
+  else if (nv <= 2) launch_rms_fwd<T, 2>(x, w, y, rstd, eps);
+  else if (nv <= 4) launch_rms_fwd<T, 4>(x, w, y, rstd, eps);
+  else if (nv <= 8) launch_rms_fwd<T, 8>(x, w, y, rstd, eps);
+  else if (nv <= 12) launch_rms_fwd<T, 12>(x, w, y, rstd, eps);
+  else if (nv <= 16) launch_rms_fwd<T, 16>(x, w, y, rstd, eps);
+  else TS_CHECK(false, "RMSNorm row width ", H, " is too large");
+}
+
+template <typename T>
+void rms_dx_dispatch(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                     at::Tensor& dx) {
+  constexpr int E = Vec<T>::N;
+  const int H = x.size(1);
+  const int nv = (H + 32 * E - 1) / (32 * E);
+  if (nv <= 1) launch_rms_dx<T, 1>(dy, x, w, rstd, dx);
+  else if (nv <= 2) launch_rms_dx<T, 2>(dy, x, w, rstd, dx);
+  else if (nv <= 4) launch_rms_dx<T, 4>(dy, x, w, rstd, dx);
+  else if (nv <= 8) launch_rms_dx<T, 8>(dy, x, w, rstd, dx);
+  else if (nv <= 12) launch_rms_dx<T, 12>(dy, x, w, rstd, dx);
+  else if (nv <= 16) launch_rms_dx<T, 16>(dy, x, w, rstd, dx);
+  else TS_CHECK(false, "RMSNorm row width ", H, " is too large");
+}
+
+// ----------------------------------------------------------------- QK-norm + RoPE
+// One warp per (token, head) row of q or k; lane owns EPL = D/32 consecutive
+// elements, so the rotate-half partner (element i +- D/2) lives on lane ^ 16.
+template <typename T, int D>
+__global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
+    const T* __restrict__ qkv, const T* __restrict__ qw, const T* __restrict__ kw, const int64_t* __restrict__ pos,
+    const float* __restrict__ inv_freq, T* __restrict__ q, T* __restrict__ k, T* __restrict__ v, int tokens, int hq,
+    int hkv, float eps) {
+  constexpr int EPL = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int heads = hq + 2 * hkv;
+  const long long item = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (item >= (long long)tokens * heads) return;
+  const int t = (int)(item / heads);
+  const int h = (int)(item % heads);
+  const T* src = qkv + (size_t)t * heads * D + (size_t)h * D + lane * EPL;
+  float xv[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) xv[e] = to_f(src[e]);
+  if (h >= hq + hkv) {  // value head: plain copy
+    T* dst = v + ((size_t)t * hkv + (h - hq - hkv)) * D + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = from_f<T>(xv[e]);
+    return;
+  }
+  const bool is_q = h < hq;
+  const T* wt = is_q ? qw : kw;
+  float y[EPL];
+  if (wt != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) ss += xv[e] * xv[e];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      float n = round_to<T>(xv[e] * r);
+      y[e] = round_to<T>(to_f(wt[lane * EPL + e]) * n);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) y[e] = xv[e];
+  }
+  const float p = (float)pos[t];
+  T* dst = is_q ? q + ((size_t)t * hq + h) * D + lane * EPL : k + ((size_t)t * hkv + (h - hq)) * D + lane * EPL;
+  const bool low = lane < 16;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
+    const int fi = (lane & 15) * EPL + e;  // frequency index i mod D/2
+    float s, c;
+    sincosf(p * inv_freq[fi], &s, &c);
+    const float rot = low ? -partner : partner;
+    dst[e] = from_f<T>(y[e] * c + rot * s);
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
+    const T* __restrict__ dq, const T* __restrict__ dk, const T* __restrict__ dv, const T* __restrict__ qkv,
+    const T* __restrict__ qw, const T* __restrict__ kw, const int64_t* __restrict__ pos,
+    const float* __restrict__ inv_freq, T* __restrict__ dqkv, float* __restrict__ dqw_part,
+    float* __restrict__ dkw_part, int tokens, int hq, int hkv, float eps, int items_per_block) {
+  constexpr int EPL = D / 32;
+  __shared__ float red_q[kWarps][D];
+  __shared__ float red_k[kWarps][D];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int heads = hq + 2 * hkv;
+  float aq[EPL], ak[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) aq[e] = ak[e] = 0.f;
+  const long long total = (long long)tokens * heads;
+  const long long i0 = (long long)blockIdx.x * items_per_block;
+  const long long i1 = i0 + items_per_block < total ? i0 + items_per_block : total;
+  for (long long item = i0 + warp; item < i1; item += kWarps) {
+    const int t = (int)(item / heads);
+    const int h = (int)(item % heads);
+    T* out = dqkv + (size_t)t * heads * D + (size_t)h * D + lane * EPL;
+    if (h >= hq + hkv) {
+      const T* g = dv + ((size_t)t * hkv + (h - hq - hkv)) * D + lane * EPL;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) out[e] = g[e];
+      continue;
+    }
+    const bool is_q = h < hq;
+    const T* g = is_q ? dq + ((size_t)t * hq + h) * D + lane * EPL : dk + ((size_t)t * hkv + (h - hq)) * D + lane * EPL;
+    const T* src = qkv + (size_t)t * heads * D + (size_t)h * D + lane * EPL;
+    const float p = (float)pos[t];
+    const bool low = lane < 16;
+    float dy[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const float go = to_f(g[e]);
+      const float partner = __shfl_xor_sync(0xffffffffu, go, 16);
+      const int fi = (lane & 15) * EPL + e;
+      float s, c;
+      sincosf(p * inv_freq[fi], &s, &c);
+      // d/dy_i of sum_j go_j * (y_j c_j + rot(y)_j s_j)
+      dy[e] = go * c + (low ? partner : -partner) * s;
+    }
+    const T* wt = is_q ? qw : kw;
+    if (wt == nullptr) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) out[e] = from_f<T>(dy[e]);
+      continue;
+    }
+    float xv[EPL];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      xv[e] = to_f(src[e]);
+      ss += xv[e] * xv[e];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)D + eps);
+    float dot = 0.f;
+    float dn[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const float n = xv[e] * r;
+      dn[e] = dy[e] * to_f(wt[lane * EPL + e]);
+      dot += dn[e] * n;
+      if (is_q) aq[e] += dy[e] * n; else ak[e] += dy[e] * n;
+    }
+    dot = warp_sum(dot) / (float)D;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) out[e] = from_f<T>(r * (dn[e] - xv[e] * r * dot));
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    red_q[warp][lane * EPL + e] = aq[e];
+    red_k[warp][lane * EPL + e] = ak[e];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float sq = 0.f, sk = 0.f;
+    for (int w = 0; w < kWarps; ++w) {
+      sq += red_q[w][c];
+      sk += red_k[w][c];
+    }
+    dqw_part[(size_t)blockIdx.x * D + c] = sq;
+    dkw_part[(size_t)blockIdx.x * D + c] = sk;
+  }
+}
+
+// ----------------------------------------------------------------- SwiGLU
+template <typename T>
+__global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ a, long long rows, int F) {
+  constexpr int E = Vec<T>::N;
+  const long long n_vec = rows * (F / E);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_vec; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / (F / E);
+    const int c = (int)(i % (F / E)) * E;
+    Vec<T> g = load_vec(gu + r * 2 * F + c);
+    Vec<T> u = load_vec(gu + r * 2 * F + F + c);
+    Vec<T> o;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float gf = to_f(g.e[e]);
+      const float sg = 1.f / (1.f + expf(-gf));
+      o.e[e] = from_f<T>(gf * sg * to_f(u.e[e]));
+    }
+    store_vec(a + r * F + c, o);
+  }
+}
+
+template <typename T>
+__global__ void swiglu_bwd_kernel(const T* __restrict__ da, const T* __restrict__ gu, T* __restrict__ dgu,
+                                  long long rows, int F) {
+  constexpr int E = Vec<T>::N;
+  const long long n_vec = rows * (F / E);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_vec; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / (F / E);
+    const int c = (int)(i % (F / E)) * E;
+    Vec<T> g = load_vec(gu + r * 2 * F + c);
+    Vec<T> u = load_vec(gu + r * 2 * F + F + c);
+    Vec<T> d = load_vec(da + r * F + c);
+    Vec<T> og, ou;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float gf = to_f(g.e[e]);
+      const float uf = to_f(u.e[e]);
+      const float df = to_f(d.e[e]);
+      const float sg = 1.f / (1.f + expf(-gf));
+      og.e[e] = from_f<T>(df * uf * (sg * (1.f + gf * (1.f - sg))));
+      ou.e[e] = from_f<T>(df * gf * sg);
+    }
+    store_vec(dgu + r * 2 * F + c, og);
+    store_vec(dgu + r * 2 * F + F + c, ou);
+  }
+}
+
+// ----------------------------------------------------------------- embedding backward
+// ids sorted ascending (with their source rows); the block at the first
+// position of each run of equal ids sums that run's rows in order and adds
+// scale * sum into target[id]. No two blocks touch the same target row.
+template <typename T>
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ order,
+                                     const T* __restrict__ dy, float* __restrict__ target, int n, int D, float scale) {
+  const int i = blockIdx.x;
+  if (i >= n) return;
+  const int64_t id = sorted_ids[i];
+  if (i > 0 && sorted_ids[i - 1] == id) return;
+  int j_end = i + 1;
+  while (j_end < n && sorted_ids[j_end] == id) ++j_end;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float s = 0.f;
+    for (int j = i; j < j_end; ++j) s += to_f(dy[(size_t)order[j] * D + c]);
+    target[(size_t)id * D + c] += scale * s;
+  }
+}
+
+}  // namespace
+
+// =================================================================== host API
+std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps) {
+  check_cuda(x, "x");
+  check_cuda(w, "w");
+  TS_CHECK(x.dim() == 2 && w.dim() == 1 && w.size(0) == x.size(1), "rms_norm_fwd shapes");
+  TS_CHECK(x.scalar_type() == w.scalar_type(), "rms_norm_fwd: x and w dtype differ");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
+  if (x.size(0) == 0) return {y, rstd};
+  const int H = x.size(1);
+  if (x.scalar_type() == at::kBFloat16) {
+    TS_CHECK(H % 8 == 0, "row width must be a multiple of 8");
+    rms_fwd_dispatch<__nv_bfloat16>(x, w, y, rstd, (float)eps);
+  } else if (x.scalar_type() == at::kFloat) {
+    TS_CHECK(H % 4 == 0, "row width must be a multiple of 4");
+    rms_fwd_dispatch<float>(x, w, y, rstd, (float)eps);
+  } else {
+    TS_CHECK(false, "rms_norm_fwd: unsupported dtype");
+  }
+  TS_LAUNCH_CHECK();
+  return {y, rstd};
+}
+
+std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                     const at::Tensor& rstd) {
+  check_cuda(dy, "dy");
+  check_cuda(x, "x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto dx = at::empty_like(x);
+  at::Tensor dw;
+  const int H = x.size(1);
+  if (x.size(0) == 0) return {dx, at::zeros({H}, x.options().dtype(at::kFloat))};
+  if (x.scalar_type() == at::kBFloat16) {
+    TS_CHECK(H % 8 == 0, "row width must be a multiple of 8");
+    rms_dx_dispatch<__nv_bfloat16>(dy, x, w, rstd, dx);
+    dw = column_weight_grad<__nv_bfloat16>(dy, x, rstd);
+  } else if (x.scalar_type() == at::kFloat) {
+    TS_CHECK(H % 4 == 0, "row width must be a multiple of 4");
+    rms_dx_dispatch<float>(dy, x, w, rstd, dx);
+    dw = column_weight_grad<float>(dy, x, rstd);
+  } else {
+    TS_CHECK(false, "rms_norm_bwd: unsupported dtype");
+  }
+  TS_LAUNCH_CHECK();
+  return {dx, dw};
+}
+
+template <typename T, int D>
+static void qk_fwd_launch(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
+                          const c10::optional<at::Tensor>& kw, const at::Tensor& pos, const at::Tensor& inv_freq,
+                          at::Tensor& q, at::Tensor& k, at::Tensor& v, int hq, int hkv, float eps) {
+  const int tokens = qkv.size(0);
+  const long long items = (long long)tokens * (hq + 2 * hkv);
+  const int blocks = (int)((items + kWarps - 1) / kWarps);
+  qk_norm_rope_fwd_kernel<T, D><<<blocks, kWarps * 32, 0, stream()>>>(
+      (const T*)qkv.data_ptr(), qw ? (const T*)qw->data_ptr() : nullptr, kw ? (const T*)kw->data_ptr() : nullptr,
+      pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(), (T*)q.data_ptr(), (T*)k.data_ptr(), (T*)v.data_ptr(),
+      tokens, hq, hkv, eps);
+}
+
+#define TS_DISPATCH_HEAD(D, FN, T, ...)                                \
+  do {                                                                 \
+    if ((D) == 64) FN<T, 64>(__VA_ARGS__);                             \
+    else if ((D) == 128) FN<T, 128>(__VA_ARGS__);                      \
+    else if ((D) == 256) FN<T, 256>(__VA_ARGS__);                      \
+    else TS_CHECK(false, "head_dim ", D, " unsupported (64/128/256)"); \
+  } while (0)
+
+std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
+                                         const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
+                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d,
+                                         double eps) {
+  check_cuda(qkv, "qkv");
+  TS_CHECK(qkv.dim() == 2 && qkv.size(1) == (hq + 2 * hkv) * d, "qkv shape");
+  TS_CHECK(pos.scalar_type() == at::kLong && inv_freq.scalar_type() == at::kFloat, "pos/inv_freq dtype");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const int64_t t = qkv.size(0);
+  auto q = at::empty({t, hq, d}, qkv.options());
+  auto k = at::empty({t, hkv, d}, qkv.options());
+  auto v = at::empty({t, hkv, d}, qkv.options());
+  if (t == 0) return {q, k, v};
+  if (qkv.scalar_type() == at::kBFloat16) {
+    TS_DISPATCH_HEAD(d, qk_fwd_launch, __nv_bfloat16, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps);
+  } else if (qkv.scalar_type() == at::kFloat) {
+    TS_DISPATCH_HEAD(d, qk_fwd_launch, float, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps);
+  } else {
+    TS_CHECK(false, "qk_norm_rope_fwd: unsupported dtype");
+  }
+  TS_LAUNCH_CHECK();
+  return {q, k, v};
+}
+
+template <typename T, int D>
+static void qk_bwd_launch(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv, const at::Tensor& qkv,
+                          const c10::optional<at::Tensor>& qw, const c10::optional<at::Tensor>& kw,
+                          const at::Tensor& pos, const at::Tensor& inv_freq, at::Tensor& dqkv, at::Tensor& pq,
+                          at::Tensor& pk, int hq, int hkv, float eps, int blocks, int per_block) {
+  qk_norm_rope_bwd_kernel<T, D><<<blocks, kWarps * 32, 0, stream()>>>(
+      (const T*)dq.data_ptr(), (const T*)dk.data_ptr(), (const T*)dv.data_ptr(), (const T*)qkv.data_ptr(),
+      qw ? (const T*)qw->data_ptr() : nullptr, kw ? (const T*)kw->data_ptr() : nullptr, pos.data_ptr<int64_t>(),
+      inv_freq.data_ptr<float>(), (T*)dqkv.data_ptr(), pq.data_ptr<float>(), pk.data_ptr<float>(), qkv.size(0), hq,
+      hkv, eps, per_block);
+}
+
+std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk,
+                                                        const at::Tensor& dv, const at::Tensor& qkv,
+                                                        const c10::optional<at::Tensor>& qw,
+                                                        const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
+                                                        const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
+                                                        int64_t d, double eps) {
+  check_cuda(qkv, "qkv");
+  check_cuda(dq, "dq");
+  check_cuda(dk, "dk");
+  check_cuda(dv, "dv");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const int64_t t = qkv.size(0);
+  auto dqkv = at::empty_like(qkv);
+  const long long items = (long long)t * (hq + 2 * hkv);
+  const int target = 4 * sm_count(qkv.get_device());
+  int per_block = (int)std::max<long long>(kWarps, (items + target - 1) / target);
+  int blocks = (int)std::max<long long>(1, (items + per_block - 1) / per_block);
+  auto pq = at::zeros({blocks, d}, qkv.options().dtype(at::kFloat));
+  auto pk = at::zeros({blocks, d}, qkv.options().dtype(at::kFloat));
+  if (t > 0) {
+    if (qkv.scalar_type() == at::kBFloat16) {
+      TS_DISPATCH_HEAD(d, qk_bwd_launch, __nv_bfloat16, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pq, pk, hq, hkv,
+                       (float)eps, blocks, per_block);
+    } else if (qkv.scalar_type() == at::kFloat) {
+      TS_DISPATCH_HEAD(d, qk_bwd_launch, float, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pq, pk, hq, hkv,
+                       (float)eps, blocks, per_block);
+    } else {
+      TS_CHECK(false, "qk_norm_rope_bwd: unsupported dtype");
+    }
+    TS_LAUNCH_CHECK();
+  }
+  c10::optional<at::Tensor> dqw, dkw;
+  if (qw) {
+    auto oq = at::empty({d}, qkv.options().dtype(at::kFloat));
+    auto ok = at::empty({d}, qkv.options().dtype(at::kFloat));
+    sum_partials_kernel<<<(d + 255) / 256, 256, 0, stream()>>>(pq.data_ptr<float>(), oq.data_ptr<float>(), blocks, d);
+    sum_partials_kernel<<<(d + 255) / 256, 256, 0, stream()>>>(pk.data_ptr<float>(), ok.data_ptr<float>(), blocks, d);
+    TS_LAUNCH_CHECK();
+    dqw = oq;
+    dkw = ok;
+  }
+  return {dqkv, dqw, dkw};
+}
+
+at::Tensor swiglu_fwd(const at::Tensor& gu) {
+  check_cuda(gu, "gu");
+  const c10::cuda::CUDAGuard guard(gu.device());
+  const long long rows = gu.numel() / gu.size(-1);
+  const int F = gu.size(-1) / 2;
+  auto sizes = gu.sizes().vec();
+  sizes.back() = F;
+  auto a = at::empty(sizes, gu.options());
+  if (rows == 0) return a;
+  const int blocks = 4 * sm_count(gu.get_device());
+  if (gu.scalar_type() == at::kBFloat16) {
+    TS_CHECK(F % 8 == 0, "ffn width must be a multiple of 8");
+    swiglu_fwd_kernel<__nv_bfloat16><<<blocks, 256, 0, stream()>>>((const __nv_bfloat16*)gu.data_ptr(),
+                                                                     (__nv_bfloat16*)a.data_ptr(), rows, F);
+  } else if (gu.scalar_type() == at::kFloat) {
+    TS_CHECK(F % 4 == 0, "ffn width must be a multiple of 4");
+    swiglu_fwd_kernel<float><<<blocks, 256, 0, stream()>>>((const float*)gu.data_ptr(), (float*)a.data_ptr(), rows, F);
+  } else {
+    TS_CHECK(false, "swiglu_fwd: unsupported dtype");
+  }
+  TS_LAUNCH_CHECK();
+  return a;
+}
+
+at::Tensor swiglu_bwd(const at::Tensor& da, const at::Tensor& gu) {
+  check_cuda(gu, "gu");
+  check_cuda(da, "da");
+  const c10::cuda::CUDAGuard guard(gu.device());
+  const long long rows = gu.numel() / gu.size(-1);
+  const int F = gu.size(-1) / 2;
+  auto dgu = at::empty_like(gu);
+  if (rows == 0) return dgu;
+  const int blocks = 4 * sm_count(gu.get_device());
+  if (gu.scalar_type() == at::kBFloat16) {
+    swiglu_bwd_kernel<__nv_bfloat16><<<blocks, 256, 0, stream()>>>(
+        (const __nv_bfloat16*)da.data_ptr(), (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)dgu.data_ptr(), rows, F);
+  } else if (gu.scalar_type() == at::kFloat) {
+    swiglu_bwd_kernel<float><<<blocks, 256, 0, stream()>>>((const float*)da.data_ptr(), (const float*)gu.data_ptr(),
+                                                           (float*)dgu.data_ptr(), rows, F);
+  } else {
+    TS_CHECK(false, "swiglu_bwd: unsupported dtype");
+  }
+  TS_LAUNCH_CHECK();
+  return dgu;
+}
+
+void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const at::Tensor& dy, double scale) {
+  check_cuda(target, "target");
+  check_cuda(ids, "ids");
+  check_cuda(dy, "dy");
+  TS_CHECK(target.scalar_type() == at::kFloat, "embedding gradient target must be fp32");
+  const c10::cuda::CUDAGuard guard(dy.device());
+  const int n = ids.size(0);
+  if (n == 0) return;
+  const int D = dy.size(1);
+  auto sorted = at::sort(ids, /*stable=*/true, /*dim=*/0, /*descending=*/false);
+  auto sid = std::get<0>(sorted).contiguous();
+  auto order = std::get<1>(sorted).contiguous();
+  const int threads = D >= 1024 ? 512 : 256;
+  if (dy.scalar_type() == at::kBFloat16) {
+    embedding_bwd_kernel<__nv_bfloat16><<<n, threads, 0, stream()>>>(
+        sid.data_ptr<int64_t>(), order.data_ptr<int64_t>(), (const __nv_bfloat16*)dy.data_ptr(),
+        target.data_ptr<float>(), n, D, (float)scale);
+  } else if (dy.scalar_type() == at::kFloat) {
+    embedding_bwd_kernel<float><<<n, threads, 0, stream()>>>(sid.data_ptr<int64_t>(), order.data_ptr<int64_t>(),
+                                                            (const float*)dy.data_ptr(), target.data_ptr<float>(), n,
+                                                            D, (float)scale);
+  } else {
+    TS_CHECK(false, "embedding_bwd: unsupported dtype");
+  }
+  TS_LAUNCH_CHECK();
+}
+
+}  // namespace ts

@@ -1,0 +1,45 @@
+"""Builds the in-tree native extension ``thundersync_b200._C`` for sm_100a.
+
+    python setup.py build_ext --inplace
+
+Every CUDA source is compiled for ``compute_100a``/``sm_100a`` only (B200);
+the explicit ``-gencode`` bypasses torch's own architecture list.
+"""
+
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+SOURCES = sorted(glob.glob(os.path.join("csrc", "*.cu"))) + sorted(glob.glob(os.path.join("csrc", "*.cpp")))
+
+NVCC_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo",
+    "--expt-relaxed-constexpr",
+    "-U__CUDA_NO_HALF_OPERATORS__",
+    "-U__CUDA_NO_HALF_CONVERSIONS__",
+    "-U__CUDA_NO_BFLOAT16_OPERATORS__",
+    "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
+]
+if os.environ.get("TS_BOUNDS_CHECK"):
+    NVCC_FLAGS.append("-DTS_BOUNDS_CHECK=1")
+if os.environ.get("TS_PTXAS_VERBOSE"):
+    NVCC_FLAGS.append("-Xptxas=-v")
+
+setup(
+    name="thundersync_b200_native",
+    ext_modules=[
+        CUDAExtension(
+            "thundersync_b200._C",
+            SOURCES,
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

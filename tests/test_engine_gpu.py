@@ -1,0 +1,60 @@
+"""Streaming GRPO on CUDA (native kernels, bf16) against the CPU fp32 oracle."""
+
+from __future__ import annotations
+
+import copy
+
+import pytest
+import torch
+
+from tests.grpo_fixtures import EPS, advantages, make_batch
+from tests.reference_model import reference_logprobs
+from thundersync_b200.engine.streaming import StreamingRun
+from thundersync_b200.grpo.reward_linear import RewardLinearBackward
+from thundersync_b200.models.qwen3 import PRESETS, Qwen3ForCausalLM
+
+pytestmark = pytest.mark.gpu
+
+CFG = PRESETS["qwen3-1.7b"].with_(num_hidden_layers=2, hidden_size=256, intermediate_size=512,
+                                  num_attention_heads=4, num_key_value_heads=2, vocab_size=2048)
+
+
+def _grads_reference(model, batch):
+    model.zero_grad(set_to_none=True)
+    total = 0.0
+    for g, prompt, trajs in batch:
+        adv = advantages([r for _, _, r in trajs])
+        for (tid, turns, _), a in zip(trajs, adv):
+            total = total + a * reference_logprobs(model, prompt, turns).sum()
+    total.backward()
+    return {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+
+
+@pytest.mark.parametrize("binary,stream_turns", [(True, False), (False, True)])
+def test_gpu_streamed_grpo_matches_fp32_oracle(binary, stream_turns):
+    torch.manual_seed(0)
+    model = Qwen3ForCausalLM(CFG)
+    batch, order = make_batch(0, vocab=CFG.vocab_size, lo=40, hi=200, prompt_len=64, multi_turn=stream_turns)
+    ref = _grads_reference(copy.deepcopy(model), batch)
+    gm = copy.deepcopy(model).to("cuda", torch.bfloat16)
+    run = StreamingRun(gm, boundary_cut=True, stream_turns=stream_turns)
+    bw = RewardLinearBackward(run, gm, eps=EPS, source_offload_mode="device_resident", source_offload_device=None)
+    if binary:
+        bw.configure_binary_rewards()
+    for g, prompt, trajs in batch:
+        bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    for g, (tid, turns, reward) in order:
+        for tk, sc in turns:
+            run.append_turn(g, tid, tk, sc)
+        bw.close_trajectory(tid, reward)
+    for g, _, _ in batch:
+        bw.close_group(g)
+    bw.assert_safe_to_step()
+    num = den = 0.0
+    for n, p in gm.named_parameters():
+        a, b = p.grad.float().cpu(), ref[n]
+        num += float((a - b).pow(2).sum())
+        den += float(b.pow(2).sum())
+        cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)
+        assert cos > 0.98, (n, float(cos))
+    assert (num / den) ** 0.5 < 0.06

@@ -1,0 +1,79 @@
+"""Segment forest, plan and forest log-probs vs per-trajectory reference (CPU fp32)."""
+
+from __future__ import annotations
+
+import random
+
+import torch
+
+from tests.grpo_fixtures import build_model
+from tests.reference_model import reference_logprobs
+from thundersync_b200.engine.plan import compile_plan, visibility_mask
+from thundersync_b200.engine.segments import Segment, Trajectory, build_forest, unshared
+from thundersync_b200.engine.step import forest_logprobs, split_by_trajectory
+
+
+def _batch(seed=0):
+    rng = random.Random(seed)
+    trajs = []
+    tid = 0
+    for g in range(2):
+        prompt = [rng.randrange(512) for _ in range(10)]
+        shared_action = [rng.randrange(512) for _ in range(4)]
+        for j in range(3):
+            segs = [Segment.prompt(prompt)]
+            if j < 2:
+                segs.append(Segment.action(shared_action + [rng.randrange(512) for _ in range(3)]))
+            else:
+                segs.append(Segment.action([rng.randrange(512) for _ in range(5)]))
+            segs.append(Segment.observation([rng.randrange(512) for _ in range(2)]))
+            segs.append(Segment.action([rng.randrange(512) for _ in range(3)]))
+            trajs.append(Trajectory(segs, group_id=g, traj_id=tid))
+            tid += 1
+    return trajs
+
+
+def test_forest_is_exact_and_shares():
+    trajs = _batch()
+    f = build_forest(trajs)
+    for t in trajs:
+        path = f.path_to_root(f.leaf_of[t.traj_id])
+        toks = [x for n in path for x in f.nodes[n].tokens]
+        sc = [x for n in path for x in f.nodes[n].scored]
+        assert toks == t.tokens and sc == t.scored_mask
+    assert f.physical_tokens < f.logical_tokens
+    assert build_forest(unshared(trajs)).physical_tokens == f.logical_tokens
+
+
+def test_plan_mask_matches_subtree_rule():
+    plan = compile_plan(build_forest(_batch()))
+    m = visibility_mask(plan)
+    p = plan.n_physical
+    q = torch.arange(p)[:, None]
+    k = torch.arange(p)[None, :]
+    rule = (k <= q) & (q < plan.subtree_end[None, :])
+    assert torch.equal(m, rule)
+
+
+def test_forest_logprobs_match_per_trajectory_reference():
+    model = build_model(3)
+    trajs = _batch(1)
+    plan = compile_plan(build_forest(trajs))
+    lp = forest_logprobs(model, plan)
+    per = split_by_trajectory(plan, lp)
+    total = 0.0
+    for t in trajs:
+        turns = [(list(s.tokens), [s.scored] * len(s)) for s in t.segments[1:]]
+        ref = reference_logprobs(model, list(t.segments[0].tokens), turns)
+        torch.testing.assert_close(per[t.traj_id], ref, rtol=1e-4, atol=1e-5)
+        total = total + per[t.traj_id].sum() * (t.traj_id + 1)
+    total.backward()
+    got = {n: p.grad.clone() for n, p in model.named_parameters()}
+    model.zero_grad()
+    ref_total = 0.0
+    for t in trajs:
+        turns = [(list(s.tokens), [s.scored] * len(s)) for s in t.segments[1:]]
+        ref_total = ref_total + reference_logprobs(model, list(t.segments[0].tokens), turns).sum() * (t.traj_id + 1)
+    ref_total.backward()
+    for n, p in model.named_parameters():
+        torch.testing.assert_close(got[n], p.grad, rtol=2e-4, atol=2e-6)

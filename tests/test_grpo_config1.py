@@ -96,3 +96,17 @@ def test_version_guard_fires():
         next(model.parameters()).add_(1.0)
     with pytest.raises(RuntimeError, match="version guard|changed inside"):
         bw.close_trajectory(0, 1.0)
+
+
+@pytest.mark.parametrize("binary", [False, True])
+def test_uniform_reward_group(binary):
+    """A group whose rewards are all equal contributes A*G2 (A exactly 0 here)."""
+    model = build_model(4)
+    batch, order = make_batch(4)
+    batch = [(g, p, [(t, turns, 1.0 if g == 0 else r) for t, turns, r in trajs]) for g, p, trajs in batch]
+    rewards = {t: r for _, _, trajs in batch for t, _, r in trajs}
+    order = [(g, (t, turns, rewards[t])) for g, (t, turns, _) in order]
+    ref = _reference_grads(copy.deepcopy(model), batch)
+    got = _streamed_grads(model, batch, order, stream_turns=False, binary=binary)
+    for name, g in ref.items():
+        torch.testing.assert_close(got[name], g, rtol=2e-4, atol=2e-6, msg=name)

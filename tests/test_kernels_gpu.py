@@ -1,0 +1,215 @@
+"""Native sm_100a kernels vs plain-torch fp32 references of the same ops."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / b.norm().clamp_min(1e-12))
+
+
+def test_extension_loaded_from_tree():
+    from thundersync_b200.ops import _ext
+
+    assert _ext.available()
+    assert "thundersync_b200" in _ext.so_path()
+
+
+@pytest.mark.parametrize("rows,h", [(300, 2048), (17, 64), (1000, 2560), (5, 4096)])
+def test_rms_norm(rows, h):
+    from thundersync_b200.ops.norm import rms_norm, rms_norm_reference
+
+    torch.manual_seed(0)
+    x = torch.randn(rows, h, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(h, device=DEV)).to(torch.bfloat16).requires_grad_(True)
+    y = rms_norm(x, w, 1e-6)
+    dy = torch.randn_like(y)
+    gx, gw = torch.autograd.grad(y, (x, w), dy)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    yr = rms_norm_reference(xr, wr, 1e-6)
+    gxr, gwr = torch.autograd.grad(yr, (xr, wr), dy.float())
+    torch.testing.assert_close(y.float(), yr, atol=3e-2, rtol=2e-2)
+    assert _rel(gx, gxr) < 1e-2
+    assert _rel(gw, gwr) < 1e-2
+    # deterministic weight gradient
+    gx2, gw2 = torch.autograd.grad(rms_norm(x, w, 1e-6), (x, w), dy)
+    assert torch.equal(gw, gw2)
+
+
+@pytest.mark.parametrize("d,hq,hkv,norm", [(128, 4, 2, True), (64, 8, 8, True), (128, 2, 1, False), (256, 4, 1, True)])
+def test_qk_norm_rope(d, hq, hkv, norm):
+    from thundersync_b200.ops.rope import qk_norm_rope, qk_norm_rope_reference, rope_inv_freq
+
+    torch.manual_seed(1)
+    t = 77
+    qkv = torch.randn(t, (hq + 2 * hkv) * d, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    qw = (1 + 0.1 * torch.randn(d, device=DEV)).to(torch.bfloat16).requires_grad_(True) if norm else None
+    kw = (1 + 0.1 * torch.randn(d, device=DEV)).to(torch.bfloat16).requires_grad_(True) if norm else None
+    pos = torch.arange(1000, 1000 + t, device=DEV)
+    inv = rope_inv_freq(d, 1e6, DEV)
+    outs = qk_norm_rope(qkv, qw, kw, pos, inv, hq, hkv, d, 1e-6)
+    grads_out = [torch.randn_like(o) for o in outs]
+    ins = [qkv] + ([qw, kw] if norm else [])
+    g = torch.autograd.grad(outs, ins, grads_out)
+    ref_ins = [i.detach().float().requires_grad_(True) for i in ins]
+    r = qk_norm_rope_reference(ref_ins[0], ref_ins[1] if norm else None, ref_ins[2] if norm else None,
+                               pos, inv, hq, hkv, d, 1e-6)
+    gr = torch.autograd.grad(r, ref_ins, [x.float() for x in grads_out])
+    for a, b in zip(outs, r):
+        torch.testing.assert_close(a.float(), b, atol=3e-2, rtol=2e-2)
+    for a, b in zip(g, gr):
+        assert _rel(a, b) < 1.5e-2
+
+
+def test_swiglu():
+    from thundersync_b200.ops.swiglu import swiglu, swiglu_reference
+
+    torch.manual_seed(2)
+    gu = torch.randn(123, 2 * 6144, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    a = swiglu(gu)
+    da = torch.randn_like(a)
+    (g,) = torch.autograd.grad(a, gu, da)
+    gur = gu.detach().float().requires_grad_(True)
+    ar = swiglu_reference(gur)
+    (gr,) = torch.autograd.grad(ar, gur, da.float())
+    torch.testing.assert_close(a.float(), ar, atol=2e-2, rtol=2e-2)
+    assert _rel(g, gr) < 1e-2
+
+
+ATTN_CASES = [
+    (64, 64, 4, 2, 128),
+    (100, 612, 8, 2, 128),
+    (1, 300, 4, 4, 64),
+    (257, 257, 2, 1, 64),
+    (513, 1025, 16, 8, 128),
+    (130, 130, 4, 1, 128),
+]
+
+
+@pytest.mark.parametrize("t,s,hq,hkv,d", ATTN_CASES)
+def test_attention(t, s, hq, hkv, d):
+    from thundersync_b200.ops.attention import attention_reference, chunked_attention
+
+    torch.manual_seed(3)
+    q = torch.randn(t, hq, d, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(s, hkv, d, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(s, hkv, d, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    # ancestors + own chunk
+    split = s - t
+    kc = [k[:split], k[split:]] if split > 0 else [k]
+    vc = [v[:split], v[split:]] if split > 0 else [v]
+    o = chunked_attention(q, kc, vc)
+    do = torch.randn_like(o)
+    gq, gk, gv = torch.autograd.grad(o, (q, k, v), do)
+    qr, kr, vr = (x.detach().float().requires_grad_(True) for x in (q, k, v))
+    orf, _ = attention_reference(qr, kr, vr, 1 / math.sqrt(d))
+    gqr, gkr, gvr = torch.autograd.grad(orf, (qr, kr, vr), do.float())
+    torch.testing.assert_close(o.float(), orf, atol=2e-2, rtol=2e-2)
+    assert _rel(gq, gqr) < 2e-2
+    assert _rel(gk, gkr) < 2e-2
+    assert _rel(gv, gvr) < 2e-2
+    # determinism of the backward
+    gq2, gk2, gv2 = torch.autograd.grad(chunked_attention(q, kc, vc), (q, k, v), do)
+    assert torch.equal(gq, gq2) and torch.equal(gk, gk2) and torch.equal(gv, gv2)
+
+
+@pytest.mark.parametrize("entropy", [False, True])
+def test_lm_head_logprob(entropy):
+    from thundersync_b200.ops.logprob import lm_head_logprob, lm_head_logprob_entropy
+
+    torch.manual_seed(4)
+    n, dmod, vocab = 300, 256, 5003
+    h = (0.5 * torch.randn(n, dmod, device=DEV)).to(torch.bfloat16).requires_grad_(True)
+    w = (0.5 * torch.randn(vocab, dmod, device=DEV)).to(torch.bfloat16).requires_grad_(True)
+    tgt = torch.randint(0, vocab, (n,), device=DEV)
+    hr, wr = h.detach().float().requires_grad_(True), w.detach().float().requires_grad_(True)
+    logits = hr @ wr.t()
+    lsm = torch.log_softmax(logits, -1)
+    lpr = lsm.gather(-1, tgt[:, None]).squeeze(-1)
+    if entropy:
+        lp, ent = lm_head_logprob_entropy(h, w, tgt, rows=128)
+        entr = -(lsm.exp() * lsm).sum(-1)
+        torch.testing.assert_close(ent, entr, atol=2e-3, rtol=2e-3)
+        go, ge = torch.randn_like(lp), torch.randn_like(ent)
+        g = torch.autograd.grad((lp, ent), (h, w), (go, ge))
+        gr = torch.autograd.grad((lpr, entr), (hr, wr), (go, ge))
+    else:
+        lp = lm_head_logprob(h, w, tgt, rows=128)
+        go = torch.randn_like(lp)
+        g = torch.autograd.grad(lp, (h, w), go)
+        gr = torch.autograd.grad(lpr, (hr, wr), go)
+    torch.testing.assert_close(lp, lpr, atol=2e-3, rtol=2e-3)
+    assert _rel(g[0], gr[0]) < 2e-2
+    assert _rel(g[1], gr[1]) < 2e-2
+
+
+def test_fold_kernels():
+    from thundersync_b200.ops.fold import axpby_, fold_, reduce_adjoints
+
+    torch.manual_seed(5)
+    n = 1_000_003
+    g1, g2 = torch.randn(n, device=DEV), torch.randn(n, device=DEV)
+    src = torch.randn(n, device=DEV)
+    e1, e2 = g1.clone() + 0.7 * src, g2.clone() + src
+    fold_(g1, g2, src, 0.7)
+    torch.testing.assert_close(g1, e1)
+    torch.testing.assert_close(g2, e2)
+    out = torch.randn(n, device=DEV)
+    exp = out + 0.3 * g1 - 0.2 * g2
+    axpby_(out, g1, g2, 0.3, -0.2)
+    torch.testing.assert_close(out, exp, atol=1e-5, rtol=1e-5)
+    parts = [torch.randn(n, device=DEV) for _ in range(20)]
+    base = torch.randn(n, device=DEV)
+    exp = base.clone()
+    for p in parts:
+        exp += p
+    got = reduce_adjoints(base.clone(), parts)
+    torch.testing.assert_close(got, exp, atol=1e-5, rtol=1e-5)
+
+
+def test_embedding_backward_deterministic():
+    from thundersync_b200.ops.embedding import embedding
+
+    torch.manual_seed(6)
+    w = torch.randn(1000, 512, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    ids = torch.randint(0, 50, (4000,), device=DEV)
+    y = embedding(ids, w)
+    dy = torch.randn_like(y)
+    (g1,) = torch.autograd.grad(y, w, dy)
+    (g2,) = torch.autograd.grad(embedding(ids, w), w, dy)
+    assert torch.equal(g1, g2)
+    ref = torch.zeros(1000, 512, device=DEV).index_add_(0, ids, dy.float())
+    assert _rel(g1, ref) < 1e-2
+
+
+def test_flat_adamw_matches_torch():
+    from thundersync_b200.ops.sink import ParamArena
+    from thundersync_b200.parallel.optimizer import FlatAdamW
+
+    torch.manual_seed(7)
+    ps = [torch.nn.Parameter(torch.randn(37, 13, device=DEV)), torch.nn.Parameter(torch.randn(100, device=DEV))]
+    ref = [torch.nn.Parameter(p.detach().clone()) for p in ps]
+    arena = ParamArena(ps)
+    opt = FlatAdamW(arena, lr=1e-2, weight_decay=0.1, maximize=True)
+    topt = torch.optim.AdamW(ref, lr=1e-2, weight_decay=0.1, maximize=True)
+    for _ in range(3):
+        grads = [torch.randn_like(p) for p in ps]
+        flat = arena.new_buffer()
+        for p, g in zip(ps, grads):
+            arena.view(flat, p).copy_(g)
+        opt.step(flat)
+        for p, g in zip(ref, grads):
+            p.grad = g
+        topt.step()
+    for p, r in zip(ps, ref):
+        torch.testing.assert_close(p.detach(), r.detach(), atol=1e-5, rtol=1e-5)

@@ -109,6 +109,9 @@ class Segment:
     start: int
     length: int
     past: list[Any] = field(default_factory=list)
+    key_ranges: list[tuple[int, int]] = field(default_factory=list)
+    """Ancestor spans inside the same pack (forest execution): each layer reads
+    ``k[s:e]``/``v[s:e]`` of the pack's own projections after ``past``."""
 
 
 def _weight(mod: torch.nn.Module) -> torch.Tensor:
@@ -185,6 +188,9 @@ class Executor:
         for seg in segs:
             s0, s1 = seg.start, seg.start + seg.length
             ks, vs = seg.past[i] if seg.past and seg.past[i] is not None else ([], [])
+            if seg.key_ranges:
+                ks = [*ks, *(k[a:b] for a, b in seg.key_ranges)]
+                vs = [*vs, *(v[a:b] for a, b in seg.key_ranges)]
             kn_, vn_ = k[s0:s1], v[s0:s1]
             outs.append(chunked_attention(q[s0:s1], [*ks, kn_], [*vs, vn_], scale))
             new_state.append((kn_, vn_))

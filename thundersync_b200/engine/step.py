@@ -1,0 +1,114 @@
+"""Forest step: physical-forest forward and gathered log-probs (C08, C09).
+
+``forest_logprobs(model, plan)`` runs the native executor once over the plan's
+physical token stream; each node is a segment whose attention reads its
+ancestors' spans of the same pass (``Segment.key_ranges``), causal only within
+itself. Only the predecessors of scored tokens reach the fused LM head, and
+the result is indexed logically (``logical_to_slot``) so shared positions
+receive the sum of their logical uses' gradients from autograd. Mirrors
+reference src/thundersync/engine/step.py:383-470.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from thundersync_b200.engine.layers import Segment, executor_for, spec_of
+from thundersync_b200.engine.plan import ExecutionPlan
+from thundersync_b200.engine.streaming import arena_for
+from thundersync_b200.ops.logprob import lm_head_logprob
+
+__all__ = ["forest_logprobs", "split_by_trajectory", "assert_supported", "base_model", "unembedding",
+           "hybrid_layer_kinds", "StepStats"]
+
+
+@dataclass
+class StepStats:
+    physical_tokens: int
+    logical_tokens: int
+    scored_rows: int
+    logical_scored: int
+
+
+def base_model(model: torch.nn.Module) -> torch.nn.Module:
+    inner = getattr(model, "model", None)
+    if inner is None or not hasattr(inner, "layers"):
+        raise TypeError("expected a causal LM with .model.layers")
+    return inner
+
+
+def unembedding(model: torch.nn.Module) -> torch.Tensor:
+    head = getattr(model, "lm_head", None)
+    if head is None:
+        raise TypeError("expected a causal LM with .lm_head")
+    return getattr(head, "base_layer", head).weight
+
+
+def hybrid_layer_kinds(model: torch.nn.Module) -> list[str]:
+    return list(spec_of(model).kinds)
+
+
+def assert_supported(model: torch.nn.Module, *, allow_hybrid: bool = False) -> None:
+    """Refuse models the executor cannot run (recurrent layers off the streaming path)."""
+    base_model(model)
+    unembedding(model)
+    kinds = set(spec_of(model).kinds)
+    unknown = kinds - {"full_attention", "linear_attention"}
+    if unknown:
+        raise NotImplementedError(f"unsupported layer kinds {sorted(unknown)}")
+    if "linear_attention" in kinds and not allow_hybrid:
+        raise NotImplementedError(
+            "recurrent (linear-attention) layers carry state along one chain; the forest path "
+            "shares nodes across branches and is not defined for them -- use StreamingRun"
+        )
+
+
+def forest_logprobs(model: torch.nn.Module, plan: ExecutionPlan, *, gate: bool = True,
+                    stats: list[StepStats] | None = None) -> torch.Tensor:
+    assert_supported(model)
+    dev = next(model.parameters()).device
+    plan = plan.to(dev)
+    ex = executor_for(model, arena_for(model))
+    segs = []
+    for n in range(plan.n_nodes):
+        s, e = int(plan.node_start[n]), int(plan.node_end[n])
+        if e > s:
+            segs.append((s, Segment(s, e - s, [], plan.key_ranges[n][:-1])))
+    segs = [sg for _, sg in sorted(segs, key=lambda x: x[0])]
+    h, _ = ex.run(plan.token_ids, plan.position_ids, segs)
+    w = ex.head_weight()
+    if gate:
+        lp = lm_head_logprob(h.index_select(0, plan.score_src), w, plan.score_tgt)
+    else:  # measurement mode: project every position, then gather
+        lp_all = torch.log_softmax(h.float() @ w.float().t(), -1)
+        lp = lp_all[plan.score_src].gather(-1, plan.score_tgt[:, None]).squeeze(-1)
+    if stats is not None:
+        stats.append(StepStats(plan.n_physical, plan.forest.logical_tokens, plan.n_scored, plan.n_logical_scored))
+    return lp.index_select(0, plan.logical_to_slot)
+
+
+def split_by_trajectory(plan: ExecutionPlan, logical: torch.Tensor) -> dict[int, torch.Tensor]:
+    out: dict[int, torch.Tensor] = {}
+    traj = plan.logical_traj.tolist()
+    start = 0
+    for i in range(1, len(traj) + 1):
+        if i == len(traj) or traj[i] != traj[start]:
+            out[traj[start]] = logical[start:i]
+            start = i
+    for t in plan.forest.trajectories:
+        out.setdefault(t.traj_id, logical.new_zeros(0))
+    return out
+
+
+def forest_context(*_a: Any, **_k: Any):  # kept for API parity: the executor needs no bound context
+    import contextlib
+
+    return contextlib.nullcontext()
+
+
+def register_attention() -> None:
+    """API parity: the forest path calls the native executor directly."""
+    return None

@@ -421,6 +421,10 @@ class RewardLinearBackward:
         main = self._main_grad()
         rewards = {acc.rewards[t] for t in acc.traj_ids}
         uniform = len(rewards) == 1
+        # uniform group: sum_i A_i g_i = A * G2 with the float64 A (exactly 0
+        # when the mean equals the reward) instead of dividing the
+        # statistics' rounding residual by eps
+        a_uni = (next(iter(rewards)) - mean) / std if uniform else 0.0
         if uniform:
             self._report["uniform_reward_groups"] += 1
         adjoints: list[torch.Tensor | None] = []
@@ -431,13 +435,12 @@ class RewardLinearBackward:
             if self._binary:
                 # P holds r=1 sources, N holds r=0 sources
                 if uniform:
-                    a = (rewards.pop() - mean) * inv
-                    axpby_(main, g1, g2, a, a)
+                    axpby_(main, g1, g2, a_uni, a_uni)
                 else:
                     axpby_(main, g1, g2, (1.0 - mean) * inv, -mean * inv)
             else:
                 if uniform:
-                    axpby_(main, g2, None, (next(iter(rewards)) - mean) * inv)
+                    axpby_(main, g2, None, a_uni)
                 else:
                     axpby_(main, g1, g2, inv, -mean * inv)
         n_b = max(len(acc.b2), len(acc.direct_boundary))
@@ -451,13 +454,12 @@ class RewardLinearBackward:
                     p = b1 if b1 is not None else torch.zeros_like(b2)
                     n = b2 if b2 is not None else torch.zeros_like(b1)
                     if uniform:
-                        a = (next(iter(rewards)) - mean) * inv
-                        out = (p + n) * a
+                        out = (p + n) * a_uni
                     else:
                         out = p * ((1.0 - mean) * inv) + n * (-mean * inv)
                 else:
                     if uniform:
-                        out = b2 * ((next(iter(rewards)) - mean) * inv)
+                        out = b2 * a_uni
                     else:
                         bb1 = b1 if b1 is not None else torch.zeros_like(b2)
                         out = (bb1 - mean * b2) * inv

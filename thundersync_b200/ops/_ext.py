@@ -1,12 +1,48 @@
-"""Loader for the in-tree native extension ``thundersync_b200._C``."""
+"""Loader for the in-tree native extension ``thundersync_b200._C``.
+
+``native()`` returns the module behind a thin proxy that counts how many of
+this package's kernels each call launches (``launch_counts``); benchmarks
+report that count for their timed region.
+"""
 
 from __future__ import annotations
 
 import importlib
 import os
+import threading
 from functools import lru_cache
 
 _LOAD_ERROR: BaseException | None = None
+
+# kernels launched per call of each native entry point
+KERNELS_PER_CALL = {
+    "rms_norm_fwd": 1, "rms_norm_bwd": 3, "qk_norm_rope_fwd": 1, "qk_norm_rope_bwd": 3,
+    "swiglu_fwd": 1, "swiglu_bwd": 1, "embedding_bwd_accumulate": 1, "fold_stats": 1, "axpby": 1,
+    "scale": 1, "reduce_into": 1, "lse_gather": 1, "logprob_dlogits": 1, "attn_fwd": 1, "attn_bwd": 3,
+    "sq_norm": 2, "clip_coef": 1, "adamw_flat": 1,
+}
+
+_lock = threading.Lock()
+_calls: dict[str, int] = {}
+
+
+class _Counted:
+    def __init__(self, mod) -> None:
+        self._mod = mod
+        self.__file__ = mod.__file__
+
+    def __getattr__(self, name: str):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+
+        def call(*args, **kwargs):
+            with _lock:
+                _calls[name] = _calls.get(name, 0) + 1
+            return fn(*args, **kwargs)
+
+        call.__name__ = name
+        return call
 
 
 @lru_cache(maxsize=1)
@@ -15,7 +51,7 @@ def _load():
     try:
         import torch  # noqa: F401  (the extension links against torch's libraries)
 
-        return importlib.import_module("thundersync_b200._C")
+        return _Counted(importlib.import_module("thundersync_b200._C"))
     except BaseException as exc:  # pragma: no cover - depends on build state
         _LOAD_ERROR = exc
         return None
@@ -40,3 +76,16 @@ def native():
 def so_path() -> str | None:
     mod = _load()
     return None if mod is None else os.path.abspath(mod.__file__)
+
+
+def reset_launch_counts() -> None:
+    with _lock:
+        _calls.clear()
+
+
+def launch_counts() -> dict[str, int]:
+    """Native calls since the last reset, and the kernel launches they made."""
+    with _lock:
+        calls = dict(_calls)
+    kernels = sum(KERNELS_PER_CALL.get(k, 1) * v for k, v in calls.items())
+    return {"calls": calls, "kernels": kernels}
