@@ -1,0 +1,434 @@
+// Bottom-right causal attention forward on the 5th-generation tensor cores.
+//
+// One CTA computes a 128-query tile of one head:
+//   warp 4      TMA producer: Q once, then K/V 128-key tiles through a
+//               2-stage ring (128B-swizzled boxes of 64 columns)
+//   warp 5      MMA issuer (one thread): S = Q K^T into one of two TMEM
+//               S buffers, O += P V into the TMEM O accumulator; commits
+//               signal the other roles through mbarriers
+//   warps 0-3   softmax: thread r owns query row r; reads its S row from
+//               TMEM, applies the bottom-right mask, online max/sum in the
+//               log2 domain, writes P (bf16) into a double-buffered
+//               K-major SW128 shared tile, and rescales its O row in TMEM
+//               only when the row max moved
+// The tensor core computes S(j+1) while the softmax warps work on S(j), and
+// PV(j) while they work on S(j+1). Epilogue: O / l (bf16) and the natural-log
+// LSE. Every mbarrier wait is bounded (see tc.cuh).
+//
+// Also here: a one-tile UMMA self-test (D = A B^T with K-major B and D = A B
+// with MN-major B) that validates the descriptor encodings on the device.
+#include <cudaTypedefs.h>
+
+#include "common.h"
+#include "tc.cuh"
+
+namespace ts {
+namespace {
+
+typedef __nv_bfloat16 bf16;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+TS_DEVICE void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+TS_DEVICE uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// One-lane wait, result broadcast so the whole warp agrees.
+TS_DEVICE bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = tc::mbar_wait(bar, parity, abort, err, code);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+template <int D>
+struct FwdLayout {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int NB = D / 64;  // 64-column boxes per row
+  static constexpr uint32_t Q = 0;
+  static constexpr uint32_t Q_BYTES = BM * D * 2;
+  static constexpr uint32_t K_BYTES = BN * D * 2;
+  static constexpr uint32_t K0 = Q + Q_BYTES;
+  static constexpr uint32_t V0 = K0 + 2 * K_BYTES;
+  static constexpr uint32_t P0 = V0 + 2 * K_BYTES;
+  static constexpr uint32_t P_BYTES = BM * BN * 2;
+  static constexpr uint32_t BAR = P0 + 2 * P_BYTES;
+  static constexpr uint32_t TOTAL = BAR + 256;
+  // TMEM columns
+  static constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256;
+};
+
+struct FwdBars {
+  uint64_t q, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv;
+  uint32_t tmem_slot;
+  int abort;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                             const __grid_constant__ CUtensorMap tm_k,
+                                                             const __grid_constant__ CUtensorMap tm_v,
+                                                             bf16* __restrict__ out, float* __restrict__ lse,
+                                                             int T, int S, int Hq, int Hkv, float sl2,
+                                                             int* __restrict__ err) {
+  using L = FwdLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  FwdBars* bars = reinterpret_cast<FwdBars*>(smem + L::BAR);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (T + L::BM - 1) / L::BM;
+  const int qt = n_qt - 1 - (int)blockIdx.x;  // longest tiles first
+  const int h = blockIdx.y, hk = h / (Hq / Hkv);
+  const int q0 = qt * L::BM;
+  const int off = S - T;
+  const int kv_end = min(S, q0 + L::BM + off);
+  const int n = (kv_end + L::BN - 1) / L::BN;
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bars->q, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bars->k_full[i], 1);
+      tc::mbar_init(&bars->v_full[i], 1);
+      tc::mbar_init(&bars->kv_empty[i], 1);
+      tc::mbar_init(&bars->s_full[i], 1);
+      tc::mbar_init(&bars->p_full[i], 128);
+    }
+    tc::mbar_init(&bars->pv, 1);
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 5) tc::tmem_alloc(&bars->tmem_slot, 512);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_q);
+      tc::prefetch_tmap(&tm_k);
+      tc::prefetch_tmap(&tm_v);
+      tc::mbar_expect_tx(&bars->q, L::Q_BYTES);
+      for (int b = 0; b < L::NB; ++b)
+        tc::tma_load_2d(smem + L::Q + b * L::BM * 128, &tm_q, h * D + b * 64, q0, &bars->q);
+      for (int j = 0; j < n; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !tc::mbar_wait(&bars->kv_empty[s], ((j - 2) >> 1) & 1, abort, err, 11)) break;
+        tc::mbar_expect_tx(&bars->k_full[s], L::K_BYTES);
+        for (int b = 0; b < L::NB; ++b)
+          tc::tma_load_2d(smem + L::K0 + s * L::K_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN,
+                          &bars->k_full[s]);
+        tc::mbar_expect_tx(&bars->v_full[s], L::K_BYTES);
+        for (int b = 0; b < L::NB; ++b)
+          tc::tma_load_2d(smem + L::V0 + s * L::K_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
+                          &bars->v_full[s]);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
+      const uint32_t id_o = tc::idesc_bf16(128, D, false, true);
+      bool ok = tc::mbar_wait(&bars->q, 0, abort, err, 21);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!tc::mbar_wait(&bars->k_full[s], (j >> 1) & 1, abort, err, 22)) return false;
+        tc::tc_fence_after();
+        const uint32_t kb = sbase + L::K0 + s * L::K_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t boff = (kk >> 2) * 128 * 128 + (kk & 3) * 32;
+          const uint64_t a = tc::sdesc_sw128(sbase + L::Q + boff, 16, 1024);
+          const uint64_t b = tc::sdesc_sw128(kb + boff, 16, 1024);
+          tc::mma_bf16(tmem + (s ? L::S_COL1 : L::S_COL0), a, b, id_s, kk > 0);
+        }
+        tc::mma_commit(&bars->s_full[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < n; ++j) {
+        const int s = j & 1;
+        if (!tc::mbar_wait(&bars->p_full[s], (j >> 1) & 1, abort, err, 23)) break;
+        if (!tc::mbar_wait(&bars->v_full[s], (j >> 1) & 1, abort, err, 24)) break;
+        tc::tc_fence_after();
+        const uint32_t pb = sbase + L::P0 + s * L::P_BYTES;
+        const uint32_t vb = sbase + L::V0 + s * L::K_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < L::BN / 16; ++kk) {
+          const uint64_t a = tc::sdesc_sw128(pb + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t b = tc::sdesc_sw128(vb + kk * 16 * 128, L::BN * 128, 1024);
+          tc::mma_bf16(tmem + L::O_COL, a, b, id_o, j > 0 || kk > 0);
+        }
+        tc::mma_commit(&bars->pv);
+        tc::mma_commit(&bars->kv_empty[s]);
+        if (j + 2 < n) ok = issue_s(j + 2);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 0-3)
+    const int r = threadIdx.x;  // query row within the tile
+    const int qi = q0 + r;
+    const int lim = qi + off;   // keys <= lim are visible
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n && ok; ++j) {
+      const int s = j & 1;
+      if (!warp_wait(&bars->s_full[s], (j >> 1) & 1, abort, err, 31)) { ok = false; break; }
+      tc::tc_fence_after();
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld32(lane_base + (s ? L::S_COL1 : L::S_COL0) + c * 32, sv + c * 32);
+      tc::tmem_ld_wait();
+      const int k0 = j * L::BN;
+      float mx = m;
+      const bool need_mask = (k0 + L::BN - 1 > q0 + off) || (k0 + L::BN > S);
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        float x = sv[i] * sl2;
+        if (need_mask && (k0 + i > lim || k0 + i >= S)) x = -INFINITY;
+        sv[i] = x;
+        mx = fmaxf(mx, x);
+      }
+      const float ref = mx == -INFINITY ? 0.f : mx;
+      const float alpha = exp2f(m - ref);
+      float rs = 0.f;
+      const uint32_t pbase = sbase + L::P0 + s * L::P_BYTES;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        float p[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          p[e] = exp2f(sv[c8 * 8 + e] - ref);
+          rs += p[e];
+        }
+        st_shared_v4(pbase + tc::kmajor_off(r, c8 * 8, 128), pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]),
+                     pack2(p[6], p[7]));
+      }
+      l = l * alpha + rs;
+      if (j > 0) {
+        if (!warp_wait(&bars->pv, (j - 1) & 1, abort, err, 32)) { ok = false; break; }
+        tc::tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            tc::tmem_ld32(lane_base + L::O_COL + c * 32, o);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tc::tmem_st32(lane_base + L::O_COL + c * 32, o);
+          }
+          tc::tmem_st_wait();
+        }
+      }
+      m = mx;
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->p_full[s]);
+    }
+    if (ok && warp_wait(&bars->pv, (n - 1) & 1, abort, err, 33)) {
+      tc::tc_fence_after();
+      const float inv = 1.f / l;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        tc::tmem_ld32(lane_base + L::O_COL + c * 32, o);
+        tc::tmem_ld_wait();
+        if (qi < T) {
+          bf16* dst = out + ((long long)qi * Hq + h) * D + c * 32;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack2(o[i] * inv, o[i + 1] * inv);
+            v.y = pack2(o[i + 2] * inv, o[i + 3] * inv);
+            v.z = pack2(o[i + 4] * inv, o[i + 5] * inv);
+            v.w = pack2(o[i + 6] * inv, o[i + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + i) = v;
+          }
+        }
+      }
+      if (qi < T) lse[(long long)h * T + qi] = (m + log2f(l)) * kLn2;
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ self-test
+// D1 = A * Bk^T (Bk [N][K], K-major), D2 = A * Bm (Bm [K][N], MN-major); 128x128x128.
+__global__ void __launch_bounds__(128, 1) tc_selftest_kernel(const __grid_constant__ CUtensorMap tm_a,
+                                                             const __grid_constant__ CUtensorMap tm_bk,
+                                                             const __grid_constant__ CUtensorMap tm_bm,
+                                                             float* __restrict__ d1, float* __restrict__ d2,
+                                                             int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = tc::smem_addr(smem);
+  // A: 2 boxes x 16 KB, Bk: 2 boxes, Bm: 2 boxes (64-col boxes over N)
+  uint64_t* bar_ld = reinterpret_cast<uint64_t*>(smem + 6 * 16384);
+  uint64_t* bar_mma = bar_ld + 1;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar_ld + 2);
+  int* abort = reinterpret_cast<int*>(bar_ld + 3);
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(bar_ld, 1);
+    tc::mbar_init(bar_mma, 1);
+    *abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 0) tc::tmem_alloc(slot, 256);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *slot;
+  if (threadIdx.x == 0) {
+    tc::mbar_expect_tx(bar_ld, 6 * 16384);
+    for (int b = 0; b < 2; ++b) {
+      tc::tma_load_2d(smem + b * 16384, &tm_a, b * 64, 0, bar_ld);
+      tc::tma_load_2d(smem + 32768 + b * 16384, &tm_bk, b * 64, 0, bar_ld);
+      tc::tma_load_2d(smem + 65536 + b * 16384, &tm_bm, b * 64, 0, bar_ld);
+    }
+    if (tc::mbar_wait(bar_ld, 0, abort, err, 41)) {
+      tc::tc_fence_after();
+      const uint32_t id1 = tc::idesc_bf16(128, 128, false, false);
+      const uint32_t id2 = tc::idesc_bf16(128, 128, false, true);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t boff = (kk >> 2) * 16384 + (kk & 3) * 32;
+        tc::mma_bf16(tmem, tc::sdesc_sw128(sbase + boff, 16, 1024), tc::sdesc_sw128(sbase + 32768 + boff, 16, 1024),
+                     id1, kk > 0);
+        tc::mma_bf16(tmem + 128, tc::sdesc_sw128(sbase + boff, 16, 1024),
+                     tc::sdesc_sw128(sbase + 65536 + kk * 16 * 128, 16384, 1024), id2, kk > 0);
+      }
+      tc::mma_commit(bar_mma);
+    }
+  }
+  __syncwarp();
+  bool ok = warp_wait(bar_mma, 0, abort, err, 42);
+  if (ok) {
+    tc::tc_fence_after();
+    const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
+    const int row = threadIdx.x;
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tc::tmem_ld32(lb + c * 32, v);
+      tc::tmem_ld_wait();
+      for (int i = 0; i < 32; ++i) d1[row * 128 + c * 32 + i] = v[i];
+      tc::tmem_ld32(lb + 128 + c * 32, v);
+      tc::tmem_ld_wait();
+      for (int i = 0; i < 32; ++i) d2[row * 128 + c * 32 + i] = v[i];
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------------ host helpers
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    TS_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q));
+    TS_CHECK(q == cudaDriverEntryPointSuccess && p != nullptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// 2-D bf16 map over [outer][inner] (row stride in elements), 128B-swizzled box of
+// 64 x box_rows. The inner coordinate of every load is a multiple of 8 elements.
+CUtensorMap make_bf16_map(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                          uint32_t box_rows) {
+  TS_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TS_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TS_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", (int)r);
+  return map;
+}
+
+at::Tensor& tc_error_flag(const at::Device& dev) {
+  static std::vector<at::Tensor> flags(64);
+  const int i = dev.index();
+  if (!flags[i].defined()) flags[i] = at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(dev));
+  return flags[i];
+}
+
+at::Tensor tc_status(const at::Tensor& like) { return tc_error_flag(like.device()); }
+
+std::vector<at::Tensor> tc_selftest(const at::Tensor& a, const at::Tensor& bk, const at::Tensor& bm) {
+  check_cuda(a, "a");
+  const c10::cuda::CUDAGuard guard(a.device());
+  TS_CHECK(a.sizes() == at::IntArrayRef({128, 128}) && bk.sizes() == a.sizes() && bm.sizes() == a.sizes(),
+           "selftest takes 128x128 bf16 operands");
+  auto d1 = at::empty({128, 128}, a.options().dtype(at::kFloat));
+  auto d2 = at::empty({128, 128}, a.options().dtype(at::kFloat));
+  CUtensorMap ma = make_bf16_map(a.data_ptr(), 128, 128, 128, 128);
+  CUtensorMap mk = make_bf16_map(bk.data_ptr(), 128, 128, 128, 128);
+  CUtensorMap mm = make_bf16_map(bm.data_ptr(), 128, 128, 128, 128);
+  const int smem = 6 * 16384 + 64 + 1024;
+  TS_CUDA_CHECK(cudaFuncSetAttribute(tc_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  tc_selftest_kernel<<<1, 128, smem, stream()>>>(ma, mk, mm, d1.data_ptr<float>(), d2.data_ptr<float>(),
+                                                 tc_error_flag(a.device()).data_ptr<int>());
+  TS_LAUNCH_CHECK();
+  return {d1, d2};
+}
+
+std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale) {
+  check_cuda(q, "q");
+  check_cuda(k, "k");
+  check_cuda(v, "v");
+  TS_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
+           "attention runs in bf16");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int T = q.size(0), Hq = q.size(1), D = q.size(2), S = k.size(0), Hkv = k.size(1);
+  TS_CHECK(S >= T && Hq % Hkv == 0 && k.sizes() == v.sizes() && k.size(2) == D, "attention shapes");
+  auto o = at::empty_like(q);
+  auto lse = at::empty({Hq, T}, q.options().dtype(at::kFloat));
+  if (T == 0) return {o, lse};
+  CUtensorMap mq = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
+  CUtensorMap mk = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
+  CUtensorMap mv = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
+  dim3 grid((T + 127) / 128, Hq);
+  const float sl2 = (float)scale * kLog2e;
+  int* err = tc_error_flag(q.device()).data_ptr<int>();
+  if (D == 128) {
+    const int smem = FwdLayout<128>::TOTAL + 1024;
+    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attn_fwd_tc_kernel<128><<<grid, 192, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
+                                                           S, Hq, Hkv, sl2, err);
+  } else if (D == 64) {
+    const int smem = FwdLayout<64>::TOTAL + 1024;
+    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attn_fwd_tc_kernel<64><<<grid, 192, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
+                                                          S, Hq, Hkv, sl2, err);
+  } else {
+    TS_CHECK(false, "tcgen05 attention supports head_dim 64 and 128");
+  }
+  TS_LAUNCH_CHECK();
+  return {o, lse};
+}
+
+}  // namespace ts

@@ -33,6 +33,19 @@ std::vector<at::Tensor> clip_coef(const at::Tensor& sq, double max_norm);
 void adamw_flat(at::Tensor& master, at::Tensor& param, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
                 double lr, double b1, double b2, double eps, double wd, int64_t step,
                 const c10::optional<at::Tensor>& scale_t, double scale, bool maximize);
+void symm_barrier(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t slot, int64_t epoch,
+                  at::Tensor& status, double timeout_s);
+at::Tensor symm_reduce(const std::vector<int64_t>& buf_ptrs, int64_t rank, int64_t lo, int64_t hi, double scale,
+                       bool write_all, const at::Tensor& like);
+void symm_norm_put(const at::Tensor& partial, const std::vector<int64_t>& flag_ptrs, int64_t rank,
+                   int64_t norm_offset);
+void symm_adamw_gather(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tensor& grad,
+                       const std::vector<int64_t>& param_ptrs, int64_t lo, double lr, double b1, double b2,
+                       double eps, double wd, int64_t step, bool maximize, const at::Tensor& norm_slots,
+                       double max_norm, at::Tensor& norm_out);
+std::vector<at::Tensor> tc_selftest(const at::Tensor& a, const at::Tensor& bk, const at::Tensor& bm);
+std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale);
+at::Tensor tc_status(const at::Tensor& like);
 }  // namespace ts
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -55,4 +68,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sq_norm", &ts::sq_norm);
   m.def("clip_coef", &ts::clip_coef);
   m.def("adamw_flat", &ts::adamw_flat);
+  m.def("symm_barrier", &ts::symm_barrier);
+  m.def("tc_selftest", &ts::tc_selftest);
+  m.def("attn_fwd_tc", &ts::attn_fwd_tc);
+  m.def("tc_status", &ts::tc_status);
+  m.def("symm_reduce", &ts::symm_reduce);
+  m.def("symm_norm_put", &ts::symm_norm_put);
+  m.def("symm_adamw_gather", &ts::symm_adamw_gather);
 }

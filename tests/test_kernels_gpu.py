@@ -213,3 +213,35 @@ def test_flat_adamw_matches_torch():
         topt.step()
     for p, r in zip(ps, ref):
         torch.testing.assert_close(p.detach(), r.detach(), atol=1e-5, rtol=1e-5)
+
+
+def test_tcgen05_descriptor_selftest():
+    """One 128x128x128 UMMA tile with K-major and MN-major B operands."""
+    from thundersync_b200.ops._ext import native
+
+    torch.manual_seed(8)
+    a = torch.randn(128, 128, device=DEV, dtype=torch.bfloat16)
+    bk = torch.randn(128, 128, device=DEV, dtype=torch.bfloat16)
+    bm = torch.randn(128, 128, device=DEV, dtype=torch.bfloat16)
+    d1, d2 = native().tc_selftest(a, bk, bm)
+    torch.cuda.synchronize()
+    assert int(native().tc_status(a).item()) == 0
+    torch.testing.assert_close(d1, a.float() @ bk.float().t(), atol=1e-2, rtol=1e-3)
+    torch.testing.assert_close(d2, a.float() @ bm.float(), atol=1e-2, rtol=1e-3)
+
+
+@pytest.mark.parametrize("t,s,hq,hkv,d", ATTN_CASES + [(2048, 2560, 16, 8, 128), (300, 4396, 16, 8, 128)])
+def test_attention_tcgen05_forward(t, s, hq, hkv, d):
+    from thundersync_b200.ops._ext import native
+    from thundersync_b200.ops.attention import attention_reference
+
+    torch.manual_seed(9)
+    q = torch.randn(t, hq, d, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(s, hkv, d, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(s, hkv, d, device=DEV, dtype=torch.bfloat16)
+    o, lse = native().attn_fwd_tc(q, k, v, 1 / math.sqrt(d))
+    torch.cuda.synchronize()
+    assert int(native().tc_status(q).item()) == 0
+    orf, lser = attention_reference(q.float(), k.float(), v.float(), 1 / math.sqrt(d))
+    torch.testing.assert_close(o.float(), orf, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(lse, lser, atol=2e-3, rtol=1e-3)

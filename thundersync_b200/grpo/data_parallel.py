@@ -130,10 +130,12 @@ class DataParallelThunderSync:
         self.arena = arena_for(model)
         if self.arena is None:
             raise ValueError("trainable parameters must share one device and dtype")
+        self._sharded_flat = isinstance(optimizer, FlatAdamW) and optimizer.is_sharded
         if reducer is None and self.world_size > 1:
             from thundersync_b200.parallel.reduce import GradientReducer
 
-            reducer = GradientReducer(self.arena.numel, self.device)
+            reducer = GradientReducer(self.arena.numel, self.device, arena=self.arena,
+                                      shard_params=self._sharded_flat)
         self.reducer = reducer
         self._binary_rewards = False
         self._steps_done = 0
@@ -268,6 +270,12 @@ class DataParallelThunderSync:
         self._final_forest = (int(max_tokens_per_microbatch), int(chunk))
 
     @property
+    def final_forest_max_tokens(self) -> int:
+        if self._final_forest is None:
+            raise RuntimeError("the final forest is not configured")
+        return self._final_forest[0]
+
+    @property
     def final_forest_enabled(self) -> bool:
         return self._final_forest is not None
 
@@ -286,12 +294,14 @@ class DataParallelThunderSync:
         prompt = self.run._groups[gid].prompt
         t = self.run._trajs[trajectory_id]
         adv = self.bw.final_advantage(trajectory_id)
-        payload = encode_final_work(trajectory_id, gid, prompt, t.turns, adv)
+        payload = encode_final_work(group_id=gid, trajectory_id=trajectory_id, advantage=adv,
+                                    prompt_tokens=prompt, turns=t.turns)
         if self._price_attention_weight is None:
             n = sum(p.numel() for p in self.model.parameters())
             self._price_attention_weight = attention_weight(self.model.config, n)
-        price = trajectory_price(len(prompt), sum(len(tk) for tk, _ in t.turns), self._price_attention_weight)
-        return trajectory_id, int(price), payload
+        turn_tokens = sum(len(tk) for tk, _ in t.turns)
+        price = trajectory_price(len(prompt), turn_tokens, self._price_attention_weight)
+        return len(prompt) + turn_tokens, int(price), payload
 
     def run_claimed_work(self, payloads: list[bytes]) -> None:
         from thundersync_b200.grpo.final_forest import backward_claimed_payloads
@@ -343,12 +353,16 @@ class DataParallelThunderSync:
         if grad is None:
             grad = self.arena.new_buffer(torch.float32)
         t1 = time.perf_counter()
-        if self.world_size > 1:
-            self.reducer.all_reduce_mean(grad, pre_scale=scale)
+        norm_t = None
+        if self._sharded_flat:
+            norm_t = self._sharded_update(grad, scale)
         else:
-            from thundersync_b200.ops.fold import scale_
+            if self.world_size > 1:
+                self.reducer.all_reduce_mean(grad, pre_scale=scale)
+            else:
+                from thundersync_b200.ops.fold import scale_
 
-            scale_(grad, scale)
+                scale_(grad, scale) if grad.is_cuda else grad.mul_(scale)
         if sync:
             torch.cuda.synchronize(self.device)
         t2 = time.perf_counter()
@@ -357,9 +371,12 @@ class DataParallelThunderSync:
         stats["group_counts_by_rank"] = counts_l
         stats["local_gradient_scale"] = scale
         stats["grad_bytes"] = grad.numel() * grad.element_size()
+        stats["reduction_path"] = None if self.reducer is None else self.reducer.last_path
         if gradient_observer is not None:
             gradient_observer("raw_reduced", grad)
-        if isinstance(self.optimizer, FlatAdamW):
+        if norm_t is not None:
+            norm_value = float(norm_t)
+        elif isinstance(self.optimizer, FlatAdamW):
             sq = global_sq_norm(grad)
             coef, nrm = self.optimizer.clip_coefficient(sq, self.grad_clip)
             self.optimizer.step(grad, clip_coef=coef)
@@ -374,6 +391,8 @@ class DataParallelThunderSync:
             norm_value = float(nrm)
             self.optimizer.step()
             self.optimizer.zero_grad(set_to_none=True)
+        if self.reducer is not None:
+            self.reducer.check()
         if sync:
             torch.cuda.synchronize(self.device)
         t3 = time.perf_counter()
@@ -396,6 +415,36 @@ class DataParallelThunderSync:
         self._new_batch()
         return stats
 
+    def _sharded_update(self, grad: torch.Tensor, scale: float):
+        """ZeRO-1: reduce-scatter, shard-local AdamW, parameter all-gather."""
+        opt: FlatAdamW = self.optimizer
+        red = self.reducer
+        if red is not None and red.native and red.main_grad_buffer() is not None \
+                and grad.data_ptr() == red.main_grad_buffer().data_ptr():
+            lo, hi = red.reduce_scatter_mean(grad, pre_scale=scale)
+            if (lo, hi) != (opt.lo, opt.hi):
+                raise RuntimeError("optimizer shard differs from the reduction shard")
+            norm = opt.step_gather(grad[lo:hi], red.param_ptrs, red.ws.norm_slots, self.grad_clip)
+            red.ws.barrier(2)
+            return norm
+        # portable path: all-reduce, local clip, shard update, parameter all-gather
+        if red is not None:
+            red.all_reduce_mean(grad, pre_scale=scale)
+        sq = global_sq_norm(grad)
+        coef, nrm = opt.clip_coefficient(sq, self.grad_clip)
+        opt.step(grad[opt.lo:opt.hi], clip_coef=coef)
+        if self.world_size > 1:
+            from thundersync_b200.parallel.symm import shard_bounds
+
+            chunk = shard_bounds(self.arena.numel, self.world_size, 0)[1]
+            buf = torch.zeros(chunk * self.world_size, dtype=self.arena.dtype, device=self.arena.device)
+            mine = buf[self.rank * chunk : self.rank * chunk + (opt.hi - opt.lo)]
+            mine.copy_(self.arena.flat[opt.lo:opt.hi])
+            dist.all_gather_into_tensor(buf, buf[self.rank * chunk : (self.rank + 1) * chunk].clone())
+            with torch.no_grad():
+                self.arena.flat.copy_(buf[: self.arena.numel])
+        return nrm
+
     def shutdown(self) -> None:
         if self._shutdown:
             return
@@ -413,6 +462,9 @@ class DataParallelThunderSync:
             old.close()
         self.run = self.run_factory(self.model)
         self.bw = RewardLinearBackward(self.run, self.model, **self._bw_kwargs)
+        buf = None if self.reducer is None else self.reducer.main_grad_buffer()
+        if buf is not None:
+            self.bw.use_main_grad_buffer(buf)
         if self._binary_rewards:
             self.bw.configure_binary_rewards()
         self.bw.set_diagnostic_scope(rank=self.rank, step=self._steps_done + 1)

@@ -161,6 +161,17 @@ class RewardLinearBackward:
             self._main = self.arena.new_buffer(torch.float32)
         return self._main
 
+    def use_main_grad_buffer(self, buf: torch.Tensor) -> None:
+        """Accumulate the batch gradient into ``buf`` (fp32, arena layout, zeroed here).
+
+        The data-parallel trainer passes a peer-mapped buffer so the step's
+        reduction reads and writes it in place over NVLink.
+        """
+        if buf.dtype != torch.float32 or buf.numel() < self.arena.numel:
+            raise ValueError("the main gradient buffer must be fp32 and cover the arena")
+        buf.zero_()
+        self._main = buf[: self.arena.numel]
+
     def main_grad(self) -> torch.Tensor | None:
         """The flat fp32 batch gradient (arena layout); None before any close."""
         return self._main

@@ -49,7 +49,7 @@ class _ChunkedAttention(torch.autograd.Function):
         k = ks[0] if n == 1 else torch.cat(ks, 0)
         v = vs[0] if n == 1 else torch.cat(vs, 0)
         if q.is_cuda:
-            out, lse = native().attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), float(scale))
+            out, lse = native().attn_fwd_tc(q.contiguous(), k.contiguous(), v.contiguous(), float(scale))
         else:
             out, lse = attention_reference(q, k, v, scale)
         ctx.scale = scale

@@ -82,6 +82,17 @@ class ParamArena:
     def owns(self, p: torch.Tensor) -> bool:
         return id(p) in self.offsets and p.data_ptr() == self.flat[self.offsets[id(p)] :].data_ptr()
 
+    def rehome(self, flat: torch.Tensor) -> None:
+        """Move every parameter into ``flat`` (same numel/dtype/device), keeping identity."""
+        if flat.numel() < self.numel or flat.dtype != self.dtype or flat.device != self.device:
+            raise ValueError("replacement arena buffer does not match")
+        with torch.no_grad():
+            flat[: self.numel].copy_(self.flat)
+            for p in self.params:
+                o = self.offsets[id(p)]
+                p.data = flat[o : o + p.numel()].view_as(p)
+        self.flat = flat[: self.numel]
+
     def offset(self, p: torch.Tensor) -> int:
         return self.offsets[id(p)]
 

@@ -59,6 +59,40 @@ class FlatAdamW:
         self.steps = 0
         self.last_norm: torch.Tensor | None = None
 
+    @classmethod
+    def sharded(cls, arena: ParamArena, **kw) -> "FlatAdamW":
+        """ZeRO-1: own only this rank's contiguous shard of the arena (requires a process group)."""
+        import torch.distributed as dist
+
+        from thundersync_b200.parallel.symm import shard_bounds
+
+        world = dist.get_world_size() if dist.is_initialized() else 1
+        rank = dist.get_rank() if dist.is_initialized() else 0
+        return cls(arena, shard=shard_bounds(arena.numel, world, rank), **kw)
+
+    @property
+    def is_sharded(self) -> bool:
+        return (self.lo, self.hi) != (0, self.arena.numel)
+
+    def step_gather(self, grad_shard: torch.Tensor, param_ptrs: list[int], norm_slots: torch.Tensor,
+                    max_norm: float | None) -> torch.Tensor:
+        """Fused AdamW on this shard that writes bf16 params into every rank's arena (native path).
+
+        ``norm_slots`` holds each rank's squared shard norm; the clip
+        coefficient is formed on the device. Returns the global norm (device).
+        """
+        self.steps += 1
+        b1, b2 = self.betas
+        norm = torch.empty(1, dtype=torch.float32, device=self.master.device)
+        native().symm_adamw_gather(
+            self.master, self.exp_avg, self.exp_avg_sq, grad_shard, param_ptrs, self.lo, self.lr, b1, b2,
+            self.eps, self.weight_decay, self.steps, self.maximize, norm_slots,
+            -1.0 if max_norm is None else float(max_norm), norm,
+        )
+        with torch.no_grad():
+            self.arena.flat[:0].add_(0)
+        return norm
+
     @property
     def param_groups(self):  # enough of torch's optimizer surface for schedulers/loggers
         return [{"lr": self.lr, "betas": self.betas, "eps": self.eps, "weight_decay": self.weight_decay,

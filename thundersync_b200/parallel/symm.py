@@ -1,0 +1,149 @@
+"""Symmetric-memory workspace and the native NVLink collectives (N0-N3, host side).
+
+Buffers are allocated and peer-mapped through torch's symmetric-memory
+allocator (``torch.distributed._symmetric_memory``: VMM allocations whose
+handles are exchanged over the process group's store); every collective
+itself is this package's kernel (``csrc/comm.cu``) reading and writing peer
+memory over NVLink:
+
+* ``barrier``            bounded-wait flag barrier; a peer that never arrives
+                         sets a device status word instead of hanging
+                         (``check()`` raises :class:`CollectiveTimeout`);
+* ``all_reduce_mean``    in-place deterministic two-shot all-reduce of a flat
+                         fp32 buffer with the pre-scale fused into the load;
+* ``reduce_scatter``     the first half only, plus the squared norm of each
+                         reduced shard exchanged through the flag buffer;
+* ``adamw_gather``       fused AdamW on this rank's shard that writes the
+                         bf16 parameters straight into every rank's
+                         parameter buffer (ZeRO-1 all-gather fused with the
+                         fp32->bf16 cast).
+
+All reductions sum ranks in a fixed order, so every rank holds bitwise
+identical results. No TMA multicast is used anywhere.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from thundersync_b200.ops._ext import native
+
+__all__ = ["SymmetricWorkspace", "NativeAllReduce", "CollectiveTimeout", "shard_bounds"]
+
+_SLOTS = 64
+_MAX_RANKS = 8
+_NORM_OFFSET = _SLOTS * _MAX_RANKS  # u32 index where the fp32 norm slots start
+
+
+class CollectiveTimeout(RuntimeError):
+    """A device-side wait ran out: the named peer never arrived."""
+
+
+def shard_bounds(numel: int, world: int, rank: int, align: int = 4) -> tuple[int, int]:
+    chunk = -(-numel // world)
+    chunk = -(-chunk // align) * align
+    lo = min(numel, rank * chunk)
+    return lo, min(numel, lo + chunk)
+
+
+def _group_name(group) -> str:
+    g = group if group is not None else dist.group.WORLD
+    return g.group_name
+
+
+class SymmetricWorkspace:
+    """Peer-mapped buffers of one process group on this rank's device."""
+
+    def __init__(self, device: torch.device, group=None, *, timeout_s: float = 30.0) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self._symm = symm_mem
+        self.device = device
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > _MAX_RANKS:
+            raise ValueError(f"the native collectives support up to {_MAX_RANKS} ranks")
+        self.timeout_s = float(timeout_s)
+        name = _group_name(group)
+        try:
+            symm_mem.enable_symm_mem_for_group(name)
+        except Exception:
+            pass
+        self._name = name
+        self.flags, self.flag_ptrs = self.alloc(_NORM_OFFSET + _MAX_RANKS, torch.int32)
+        self.flags.zero_()
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self._epochs = [0] * _SLOTS
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+
+    def alloc(self, numel: int, dtype: torch.dtype) -> tuple[torch.Tensor, list[int]]:
+        t = self._symm.empty(numel, dtype=dtype, device=self.device)
+        hdl = self._symm.rendezvous(t, self._name)
+        return t, [int(p) for p in hdl.buffer_ptrs]
+
+    @property
+    def norm_slots(self) -> torch.Tensor:
+        return self.flags[_NORM_OFFSET : _NORM_OFFSET + self.world].view(torch.float32)
+
+    def barrier(self, slot: int = 0) -> None:
+        self._epochs[slot] += 1
+        native().symm_barrier(self.flag_ptrs, self.rank, slot, self._epochs[slot], self.status, self.timeout_s)
+
+    def check(self) -> None:
+        code = int(self.status.item())
+        if code:
+            raise CollectiveTimeout(
+                f"rank {self.rank}: native collective wait expired waiting for rank {code - 1000} "
+                f"(timeout {self.timeout_s} s)"
+            )
+
+    def all_reduce_mean(self, buf: torch.Tensor, ptrs: list[int], *, pre_scale: float = 1.0) -> None:
+        """In place: ``buf`` (symmetric fp32) becomes mean over ranks of ``pre_scale * buf``."""
+        lo, hi = shard_bounds(buf.numel(), self.world, self.rank)
+        self.barrier(0)
+        native().symm_reduce(ptrs, self.rank, lo, hi, pre_scale / self.world, True, buf)
+        self.barrier(1)
+
+    def reduce_scatter(self, buf: torch.Tensor, ptrs: list[int], *, pre_scale: float = 1.0) -> tuple[int, int]:
+        """This rank's shard of ``buf`` becomes the mean; its squared norm goes to every rank's slot."""
+        lo, hi = shard_bounds(buf.numel(), self.world, self.rank)
+        self.barrier(0)
+        partial = native().symm_reduce(ptrs, self.rank, lo, hi, pre_scale / self.world, False, buf)
+        native().symm_norm_put(partial, self.flag_ptrs, self.rank, _NORM_OFFSET)
+        self.barrier(1)
+        return lo, hi
+
+    def close(self) -> None:
+        self.flags = None
+
+
+class NativeAllReduce:
+    """All-reduce of a caller's (non-symmetric) flat fp32 buffer through a symmetric bucket."""
+
+    def __init__(self, ws: SymmetricWorkspace, bucket_elems: int) -> None:
+        self.ws = ws
+        self.bucket_elems = -(-bucket_elems // (4 * ws.world)) * 4 * ws.world
+        self.bucket, self.ptrs = ws.alloc(self.bucket_elems, torch.float32)
+
+    @classmethod
+    def create(cls, bucket_elems: int, device: torch.device, group=None) -> "NativeAllReduce":
+        return cls(SymmetricWorkspace(device, group), bucket_elems)
+
+    def all_reduce_mean(self, grad: torch.Tensor, *, pre_scale: float = 1.0) -> None:
+        n = grad.numel()
+        b = self.bucket_elems
+        for lo in range(0, n, b):
+            hi = min(n, lo + b)
+            view = self.bucket[: hi - lo]
+            view.copy_(grad[lo:hi])
+            if hi - lo < b:
+                self.bucket[hi - lo :].zero_()
+            self.ws.all_reduce_mean(self.bucket, self.ptrs, pre_scale=pre_scale)
+            grad[lo:hi].copy_(view)
+        self.ws.check()
+
+    def close(self) -> None:
+        self.ws.close()

@@ -1,1 +1,1 @@
-"""scheduling"""
+"""Source admission and cross-rank work claims (host side)."""
