@@ -265,6 +265,445 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_consta
   }
 }
 
+// ------------------------------------------------------------------ backward
+// delta[h, i] = sum_d dO[i,h,d] * O[i,h,d] (fp32), one warp per (i, h).
+__global__ void attn_delta_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dout, float* __restrict__ delta,
+                                  int T, int Hq, int D) {
+  const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (item >= (long long)T * Hq) return;
+  const int i = (int)(item / Hq), h = (int)(item % Hq);
+  const bf16* po = o + item * D;
+  const bf16* pd = dout + item * D;
+  float s = 0.f;
+  for (int d = lane * 2; d < D; d += 64) {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(po + d));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(pd + d));
+    s += a.x * b.x + a.y * b.y;
+  }
+  s = warp_sum(s);
+  if (lane == 0) delta[(long long)h * T + i] = s;
+}
+
+// dK/dV: CTA = 128 keys of one KV head; thread r of warps 0-3 owns key row r.
+// Per step (query head, 64-query tile): S^T = K Q^T and dP^T = V dO^T into a
+// TMEM buffer pair; the compute warps form P^T = exp2(S^T*sl2 - lse2) and
+// dS^T = P^T (dP^T - delta) as bf16 K-major tiles; the MMA thread accumulates
+// dV += P^T dO and dK += dS^T Q into TMEM, which hold them across all steps.
+template <int D>
+struct DkvLayout {
+  static constexpr int BN = 128, BQ = 64, NB = D / 64;
+  static constexpr uint32_t KV_BYTES = BN * D * 2;
+  static constexpr uint32_t QT_BYTES = BQ * D * 2;
+  static constexpr uint32_t K = 0, V = KV_BYTES;
+  static constexpr uint32_t Q0 = 2 * KV_BYTES;               // [2] Q tiles
+  static constexpr uint32_t O0 = Q0 + 2 * QT_BYTES;          // [2] dO tiles
+  static constexpr uint32_t P0 = O0 + 2 * QT_BYTES;          // [2] P^T tiles (128 x 64 bf16)
+  static constexpr uint32_t PT_BYTES = BN * BQ * 2;
+  static constexpr uint32_t DS0 = P0 + 2 * PT_BYTES;         // [2] dS^T tiles
+  static constexpr uint32_t LD0 = DS0 + 2 * PT_BYTES;        // [2][2][BQ] floats: lse2, delta
+  static constexpr uint32_t BAR = LD0 + 2 * 2 * BQ * 4;
+  static constexpr uint32_t TOTAL = BAR + 256;
+  static constexpr uint32_t DK_COL = 0, DV_COL = D, ST_COL0 = 2 * D;  // ST/DPT pairs follow
+};
+
+struct DkvBars {
+  uint64_t kv, q_full[2], s_full[2], p_full[2], mma_done[2], fin;
+  uint32_t tmem_slot;
+  int abort;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dk, bf16* __restrict__ dv,
+    int T, int S, int Hq, int Hkv, float scale, int* __restrict__ err) {
+  using L = DkvLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DkvBars* bars = reinterpret_cast<DkvBars*>(smem + L::BAR);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hk = blockIdx.y, grp = Hq / Hkv;
+  const int k0 = blockIdx.x * L::BN;
+  const int off = S - T;
+  const float sl2 = scale * kLog2e;
+  int qstart = k0 - off;
+  if (qstart < 0) qstart = 0;
+  qstart = (qstart / L::BQ) * L::BQ;
+  const int n_qt = qstart < T ? (T - qstart + L::BQ - 1) / L::BQ : 0;
+  const int total = n_qt * grp;
+  volatile int* abort = &bars->abort;
+  float* ld = reinterpret_cast<float*>(smem + L::LD0);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bars->kv, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bars->q_full[i], 2);
+      tc::mbar_init(&bars->s_full[i], 1);
+      tc::mbar_init(&bars->p_full[i], 128);
+      tc::mbar_init(&bars->mma_done[i], 1);
+    }
+    tc::mbar_init(&bars->fin, 1);
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 5) tc::tmem_alloc(&bars->tmem_slot, 512);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 4) {
+    // producer: K, V once; per step Q and dO tiles (TMA) plus lse2 / delta (plain loads)
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars->kv, 2 * L::KV_BYTES);
+      for (int b = 0; b < L::NB; ++b) {
+        tc::tma_load_2d(smem + L::K + b * L::BN * 128, &tm_k, hk * D + b * 64, k0, &bars->kv);
+        tc::tma_load_2d(smem + L::V + b * L::BN * 128, &tm_v, hk * D + b * 64, k0, &bars->kv);
+      }
+    }
+    for (int i = 0; i < total; ++i) {
+      const int st = i & 1;
+      if (i >= 2 && !warp_wait(&bars->mma_done[st], ((i - 2) >> 1) & 1, abort, err, 51)) break;
+      const int hh = hk * grp + i / n_qt;
+      const int qt = qstart + (i % n_qt) * L::BQ;
+      if (lane == 0) {
+        tc::mbar_expect_tx(&bars->q_full[st], 2 * L::QT_BYTES);
+        for (int b = 0; b < L::NB; ++b) {
+          tc::tma_load_2d(smem + L::Q0 + st * L::QT_BYTES + b * L::BQ * 128, &tm_q, hh * D + b * 64, qt,
+                          &bars->q_full[st]);
+          tc::tma_load_2d(smem + L::O0 + st * L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qt,
+                          &bars->q_full[st]);
+        }
+      }
+      for (int c = lane; c < L::BQ; c += 32) {
+        const int qi = qt + c;
+        ld[(st * 2 + 0) * L::BQ + c] = qi < T ? lse[(long long)hh * T + qi] * kLog2e : 0.f;
+        ld[(st * 2 + 1) * L::BQ + c] = qi < T ? delta[(long long)hh * T + qi] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->q_full[st]);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t id_s = tc::idesc_bf16(128, L::BQ, false, false);
+      const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
+      bool ok = tc::mbar_wait(&bars->kv, 0, abort, err, 61);
+      auto issue_s = [&](int i) -> bool {
+        const int st = i & 1;
+        if (!tc::mbar_wait(&bars->q_full[st], (i >> 1) & 1, abort, err, 62)) return false;
+        tc::tc_fence_after();
+        const uint32_t qb = sbase + L::Q0 + st * L::QT_BYTES, ob = sbase + L::O0 + st * L::QT_BYTES;
+        const uint32_t col = L::ST_COL0 + st * 2 * L::BQ;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t kv_off = (kk >> 2) * L::BN * 128 + (kk & 3) * 32;
+          const uint32_t q_off = (kk >> 2) * L::BQ * 128 + (kk & 3) * 32;
+          tc::mma_bf16(tmem + col, tc::sdesc_sw128(sbase + L::K + kv_off, 16, 1024),
+                       tc::sdesc_sw128(qb + q_off, 16, 1024), id_s, kk > 0);
+          tc::mma_bf16(tmem + col + L::BQ, tc::sdesc_sw128(sbase + L::V + kv_off, 16, 1024),
+                       tc::sdesc_sw128(ob + q_off, 16, 1024), id_s, kk > 0);
+        }
+        tc::mma_commit(&bars->s_full[st]);
+        return true;
+      };
+      if (ok && total > 0) ok = issue_s(0);
+      if (ok && total > 1) ok = issue_s(1);
+      for (int i = 0; ok && i < total; ++i) {
+        const int st = i & 1;
+        if (!tc::mbar_wait(&bars->p_full[st], (i >> 1) & 1, abort, err, 63)) break;
+        tc::tc_fence_after();
+        const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
+        const uint32_t qb = sbase + L::Q0 + st * L::QT_BYTES, ob = sbase + L::O0 + st * L::QT_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < L::BQ / 16; ++kk) {
+          const uint64_t ap = tc::sdesc_sw128(pb + kk * 32, 16, 1024);
+          const uint64_t ad = tc::sdesc_sw128(db + kk * 32, 16, 1024);
+          const uint64_t bo = tc::sdesc_sw128(ob + kk * 16 * 128, L::BQ * 128, 1024);
+          const uint64_t bq = tc::sdesc_sw128(qb + kk * 16 * 128, L::BQ * 128, 1024);
+          tc::mma_bf16(tmem + L::DV_COL, ap, bo, id_acc, i > 0 || kk > 0);
+          tc::mma_bf16(tmem + L::DK_COL, ad, bq, id_acc, i > 0 || kk > 0);
+        }
+        tc::mma_commit(&bars->mma_done[st]);
+        if (i + 2 < total) ok = issue_s(i + 2);
+      }
+      if (ok) tc::mma_commit(&bars->fin);
+    }
+  } else {
+    const int r = threadIdx.x;
+    const int kr = k0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    bool ok = true;
+    for (int i = 0; i < total && ok; ++i) {
+      const int st = i & 1;
+      const int qt = qstart + (i % n_qt) * L::BQ;
+      if (!warp_wait(&bars->q_full[st], (i >> 1) & 1, abort, err, 71)) { ok = false; break; }
+      if (!warp_wait(&bars->s_full[st], (i >> 1) & 1, abort, err, 72)) { ok = false; break; }
+      if (i >= 2 && !warp_wait(&bars->mma_done[st], ((i - 2) >> 1) & 1, abort, err, 73)) { ok = false; break; }
+      tc::tc_fence_after();
+      float sv[64], dp[64];
+      const uint32_t col = L::ST_COL0 + st * 2 * L::BQ;
+      tc::tmem_ld32(lane_base + col, sv);
+      tc::tmem_ld32(lane_base + col + 32, sv + 32);
+      tc::tmem_ld32(lane_base + col + L::BQ, dp);
+      tc::tmem_ld32(lane_base + col + L::BQ + 32, dp + 32);
+      tc::tmem_ld_wait();
+      const float* l2 = ld + (st * 2 + 0) * L::BQ;
+      const float* dl = ld + (st * 2 + 1) * L::BQ;
+      const bool full = (qt >= kr - off) && (qt + L::BQ <= T) && kr < S;
+      const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
+#pragma unroll
+      for (int c8 = 0; c8 < L::BQ / 8; ++c8) {
+        float p[8], ds[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = c8 * 8 + e;
+          const int qi = qt + c;
+          const bool vis = full || (qi < T && kr < S && kr <= qi + off);
+          p[e] = vis ? exp2f(sv[c] * sl2 - l2[c]) : 0.f;
+          ds[e] = p[e] * (dp[c] - dl[c]);
+        }
+        const uint32_t o8 = tc::kmajor_off(r, c8 * 8, 128);
+        st_shared_v4(pb + o8, pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]), pack2(p[6], p[7]));
+        st_shared_v4(db + o8, pack2(ds[0], ds[1]), pack2(ds[2], ds[3]), pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->p_full[st]);
+    }
+    if (ok && total > 0 && warp_wait(&bars->fin, 0, abort, err, 74)) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float a[32], b[32];
+        tc::tmem_ld32(lane_base + L::DK_COL + c * 32, a);
+        tc::tmem_ld32(lane_base + L::DV_COL + c * 32, b);
+        tc::tmem_ld_wait();
+        if (kr < S) {
+          bf16* pk = dk + ((long long)kr * Hkv + hk) * D + c * 32;
+          bf16* pv = dv + ((long long)kr * Hkv + hk) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 u, w;
+            u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
+            u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
+            w.x = pack2(b[x], b[x + 1]); w.y = pack2(b[x + 2], b[x + 3]);
+            w.z = pack2(b[x + 4], b[x + 5]); w.w = pack2(b[x + 6], b[x + 7]);
+            *reinterpret_cast<uint4*>(pk + x) = u;
+            *reinterpret_cast<uint4*>(pv + x) = w;
+          }
+        }
+      }
+    } else if (ok && total == 0 && kr < S) {
+      // no query sees these keys
+      for (int c = 0; c < D; c += 8) {
+        *reinterpret_cast<uint4*>(dk + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(dv + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ: CTA = 128 queries of one head; thread r of warps 0-3 owns query row r.
+// Per 64-key tile: S = Q K^T and dP = dO V^T into a TMEM buffer pair, the
+// compute warps form dS = P (dP - delta) (bf16, K-major), the MMA thread
+// accumulates dQ += dS K into TMEM.
+template <int D>
+struct DqLayout {
+  static constexpr int BM = 128, BN = 64, NB = D / 64;
+  static constexpr uint32_t Q_BYTES = BM * D * 2;
+  static constexpr uint32_t KT_BYTES = BN * D * 2;
+  static constexpr uint32_t Q = 0, O = Q_BYTES;
+  static constexpr uint32_t K0 = 2 * Q_BYTES;             // [2] K tiles
+  static constexpr uint32_t V0 = K0 + 2 * KT_BYTES;       // [2] V tiles
+  static constexpr uint32_t DS0 = V0 + 2 * KT_BYTES;      // [2] dS tiles (128 x 64)
+  static constexpr uint32_t DS_BYTES = BM * BN * 2;
+  static constexpr uint32_t BAR = DS0 + 2 * DS_BYTES;
+  static constexpr uint32_t TOTAL = BAR + 256;
+  static constexpr uint32_t DQ_COL = 0, S_COL0 = D;
+};
+
+struct DqBars {
+  uint64_t q, kv_full[2], s_full[2], p_full[2], mma_done[2], fin;
+  uint32_t tmem_slot;
+  int abort;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1) attn_bwd_dq_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T, int S, int Hq,
+    int Hkv, float scale, int* __restrict__ err) {
+  using L = DqLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DqBars* bars = reinterpret_cast<DqBars*>(smem + L::BAR);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (T + L::BM - 1) / L::BM;
+  const int qt = n_qt - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, hk = h / (Hq / Hkv);
+  const int q0 = qt * L::BM;
+  const int off = S - T;
+  const int kv_end = min(S, q0 + L::BM + off);
+  const int n = (kv_end + L::BN - 1) / L::BN;
+  const float sl2 = scale * kLog2e;
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bars->q, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bars->kv_full[i], 1);
+      tc::mbar_init(&bars->s_full[i], 1);
+      tc::mbar_init(&bars->p_full[i], 128);
+      tc::mbar_init(&bars->mma_done[i], 1);
+    }
+    tc::mbar_init(&bars->fin, 1);
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 5) tc::tmem_alloc(&bars->tmem_slot, 512);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars->q, 2 * L::Q_BYTES);
+      for (int b = 0; b < L::NB; ++b) {
+        tc::tma_load_2d(smem + L::Q + b * L::BM * 128, &tm_q, h * D + b * 64, q0, &bars->q);
+        tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, q0, &bars->q);
+      }
+      for (int j = 0; j < n; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !tc::mbar_wait(&bars->mma_done[st], ((j - 2) >> 1) & 1, abort, err, 81)) break;
+        tc::mbar_expect_tx(&bars->kv_full[st], 2 * L::KT_BYTES);
+        for (int b = 0; b < L::NB; ++b) {
+          tc::tma_load_2d(smem + L::K0 + st * L::KT_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN,
+                          &bars->kv_full[st]);
+          tc::tma_load_2d(smem + L::V0 + st * L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
+                          &bars->kv_full[st]);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
+      const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
+      bool ok = tc::mbar_wait(&bars->q, 0, abort, err, 91);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!tc::mbar_wait(&bars->kv_full[st], (j >> 1) & 1, abort, err, 92)) return false;
+        tc::tc_fence_after();
+        const uint32_t kb = sbase + L::K0 + st * L::KT_BYTES, vb = sbase + L::V0 + st * L::KT_BYTES;
+        const uint32_t col = L::S_COL0 + st * 2 * L::BN;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t q_off = (kk >> 2) * L::BM * 128 + (kk & 3) * 32;
+          const uint32_t k_off = (kk >> 2) * L::BN * 128 + (kk & 3) * 32;
+          tc::mma_bf16(tmem + col, tc::sdesc_sw128(sbase + L::Q + q_off, 16, 1024),
+                       tc::sdesc_sw128(kb + k_off, 16, 1024), id_s, kk > 0);
+          tc::mma_bf16(tmem + col + L::BN, tc::sdesc_sw128(sbase + L::O + q_off, 16, 1024),
+                       tc::sdesc_sw128(vb + k_off, 16, 1024), id_s, kk > 0);
+        }
+        tc::mma_commit(&bars->s_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < n; ++j) {
+        const int st = j & 1;
+        if (!tc::mbar_wait(&bars->p_full[st], (j >> 1) & 1, abort, err, 93)) break;
+        tc::tc_fence_after();
+        const uint32_t db = sbase + L::DS0 + st * L::DS_BYTES;
+        const uint32_t kb = sbase + L::K0 + st * L::KT_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < L::BN / 16; ++kk) {
+          tc::mma_bf16(tmem + L::DQ_COL, tc::sdesc_sw128(db + kk * 32, 16, 1024),
+                       tc::sdesc_sw128(kb + kk * 16 * 128, L::BN * 128, 1024), id_acc, j > 0 || kk > 0);
+        }
+        tc::mma_commit(&bars->mma_done[st]);
+        if (j + 2 < n) ok = issue_s(j + 2);
+      }
+      if (ok) tc::mma_commit(&bars->fin);
+    }
+  } else {
+    const int r = threadIdx.x;
+    const int qi = q0 + r;
+    const int lim = qi + off;
+    const float l2 = qi < T ? lse[(long long)h * T + qi] * kLog2e : 0.f;
+    const float dl = qi < T ? delta[(long long)h * T + qi] : 0.f;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    bool ok = true;
+    for (int j = 0; j < n && ok; ++j) {
+      const int st = j & 1;
+      if (!warp_wait(&bars->s_full[st], (j >> 1) & 1, abort, err, 101)) { ok = false; break; }
+      if (j >= 2 && !warp_wait(&bars->mma_done[st], ((j - 2) >> 1) & 1, abort, err, 102)) { ok = false; break; }
+      tc::tc_fence_after();
+      float sv[64], dp[64];
+      const uint32_t col = L::S_COL0 + st * 2 * L::BN;
+      tc::tmem_ld32(lane_base + col, sv);
+      tc::tmem_ld32(lane_base + col + 32, sv + 32);
+      tc::tmem_ld32(lane_base + col + L::BN, dp);
+      tc::tmem_ld32(lane_base + col + L::BN + 32, dp + 32);
+      tc::tmem_ld_wait();
+      const int k0 = j * L::BN;
+      const bool full = (k0 + L::BN - 1 <= q0 + off) && (k0 + L::BN <= S) && qi < T;
+      const uint32_t db = sbase + L::DS0 + st * L::DS_BYTES;
+#pragma unroll
+      for (int c8 = 0; c8 < L::BN / 8; ++c8) {
+        float ds[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = c8 * 8 + e;
+          const int key = k0 + c;
+          const bool vis = full || (qi < T && key < S && key <= lim);
+          const float p = vis ? exp2f(sv[c] * sl2 - l2) : 0.f;
+          ds[e] = p * (dp[c] - dl);
+        }
+        st_shared_v4(db + tc::kmajor_off(r, c8 * 8, 128), pack2(ds[0], ds[1]), pack2(ds[2], ds[3]),
+                     pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->p_full[st]);
+    }
+    if (ok && warp_wait(&bars->fin, 0, abort, err, 103)) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float a[32];
+        tc::tmem_ld32(lane_base + L::DQ_COL + c * 32, a);
+        tc::tmem_ld_wait();
+        if (qi < T) {
+          bf16* pq = dq + ((long long)qi * Hq + h) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 u;
+            u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
+            u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
+            *reinterpret_cast<uint4*>(pq + x) = u;
+          }
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
 // ------------------------------------------------------------------ self-test
 // D1 = A * Bk^T (Bk [N][K], K-major), D2 = A * Bm (Bm [K][N], MN-major); 128x128x128.
 __global__ void __launch_bounds__(128, 1) tc_selftest_kernel(const __grid_constant__ CUtensorMap tm_a,
@@ -429,6 +868,61 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
   }
   TS_LAUNCH_CHECK();
   return {o, lse};
+}
+
+std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                    const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale) {
+  check_cuda(q, "q");
+  check_cuda(k, "k");
+  check_cuda(v, "v");
+  check_cuda(o, "o");
+  check_cuda(dout, "dout");
+  check_cuda(lse, "lse");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int T = q.size(0), Hq = q.size(1), D = q.size(2), S = k.size(0), Hkv = k.size(1);
+  TS_CHECK(S >= T && Hq % Hkv == 0 && (D == 64 || D == 128), "attention backward shapes");
+  auto dq = at::empty_like(q);
+  auto dk = at::empty_like(k);
+  auto dv = at::empty_like(v);
+  if (T == 0) return {dq, dk.zero_(), dv.zero_()};
+  auto delta = at::empty({Hq, T}, q.options().dtype(at::kFloat));
+  const long long items = (long long)T * Hq;
+  attn_delta_kernel<<<(int)((items + 7) / 8), 256, 0, stream()>>>((const bf16*)o.data_ptr(),
+                                                                  (const bf16*)dout.data_ptr(),
+                                                                  delta.data_ptr<float>(), T, Hq, D);
+  int* err = tc_error_flag(q.device()).data_ptr<int>();
+  CUtensorMap mq64 = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 64);
+  CUtensorMap mo64 = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 64);
+  CUtensorMap mk128 = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
+  CUtensorMap mv128 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
+  CUtensorMap mq128 = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
+  CUtensorMap mo128 = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
+  CUtensorMap mk64 = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
+  CUtensorMap mv64 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
+  dim3 g1((S + 127) / 128, Hkv), g2((T + 127) / 128, Hq);
+  if (D == 128) {
+    const int s1 = DkvLayout<128>::TOTAL + 1024, s2 = DqLayout<128>::TOTAL + 1024;
+    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
+    attn_bwd_dkdv_tc_kernel<128><<<g1, 192, s1, stream()>>>(mq64, mk128, mv128, mo64, lse.data_ptr<float>(),
+                                                            delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
+                                                            (bf16*)dv.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
+    attn_bwd_dq_tc_kernel<128><<<g2, 192, s2, stream()>>>(mq128, mk64, mv64, mo128, lse.data_ptr<float>(),
+                                                          delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq,
+                                                          Hkv, (float)scale, err);
+  } else {
+    const int s1 = DkvLayout<64>::TOTAL + 1024, s2 = DqLayout<64>::TOTAL + 1024;
+    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
+    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
+    attn_bwd_dkdv_tc_kernel<64><<<g1, 192, s1, stream()>>>(mq64, mk128, mv128, mo64, lse.data_ptr<float>(),
+                                                           delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
+                                                           (bf16*)dv.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
+    attn_bwd_dq_tc_kernel<64><<<g2, 192, s2, stream()>>>(mq128, mk64, mv64, mo128, lse.data_ptr<float>(),
+                                                         delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq,
+                                                         Hkv, (float)scale, err);
+  }
+  TS_LAUNCH_CHECK();
+  return {dq, dk, dv};
 }
 
 }  // namespace ts

@@ -46,6 +46,8 @@ void symm_adamw_gather(at::Tensor& master, at::Tensor& m, at::Tensor& v, const a
 std::vector<at::Tensor> tc_selftest(const at::Tensor& a, const at::Tensor& bk, const at::Tensor& bm);
 std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale);
 at::Tensor tc_status(const at::Tensor& like);
+std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                    const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale);
 }  // namespace ts
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -72,6 +74,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_selftest", &ts::tc_selftest);
   m.def("attn_fwd_tc", &ts::attn_fwd_tc);
   m.def("tc_status", &ts::tc_status);
+  m.def("attn_bwd_tc", &ts::attn_bwd_tc);
   m.def("symm_reduce", &ts::symm_reduce);
   m.def("symm_norm_put", &ts::symm_norm_put);
   m.def("symm_adamw_gather", &ts::symm_adamw_gather);

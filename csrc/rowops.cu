@@ -145,13 +145,24 @@ __global__ void __launch_bounds__(256) rms_dw_partial_kernel(const T* __restrict
   }
 }
 
-// out[c] = sum_k partial[k, c] in k order.
-__global__ void sum_partials_kernel(const float* __restrict__ partial, float* __restrict__ out, int chunks, int H) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= H) return;
+// out[c] = sum_k partial[k, c]: block (32 x 8) covers 32 columns; warp row y
+// sums chunks y, y+8, ... and the 8 row sums are added in y order, so the
+// result is the same every run.
+__global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restrict__ partial, float* __restrict__ out,
+                                                           int chunks, int H) {
+  __shared__ float red[8][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  for (int k = 0; k < chunks; ++k) s += partial[(size_t)k * H + c];
-  out[c] = s;
+  if (c < H)
+    for (int k = threadIdx.y; k < chunks; k += 8) s += partial[(size_t)k * H + c];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
+    out[c] = t;
+  }
 }
 
 template <typename T, int V>
@@ -188,8 +199,8 @@ at::Tensor column_weight_grad(const at::Tensor& dy, const at::Tensor& x, const a
   rms_dw_partial_kernel<T><<<dim3(col_blocks, chunks), dim3(32, 8), 0, stream()>>>(
       (const T*)dy.data_ptr(), (const T*)x.data_ptr(), rstd.data_ptr<float>(), partial.data_ptr<float>(), rows, H,
       rows_per_chunk);
-  sum_partials_kernel<<<(H + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(), chunks,
-                                                              H);
+  sum_partials_kernel<<<(H + 31) / 32, dim3(32, 8), 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
+                                                                     chunks, H);
   return dw;
 }
 
@@ -577,8 +588,10 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
   if (qw) {
     auto oq = at::empty({d}, qkv.options().dtype(at::kFloat));
     auto ok = at::empty({d}, qkv.options().dtype(at::kFloat));
-    sum_partials_kernel<<<(d + 255) / 256, 256, 0, stream()>>>(pq.data_ptr<float>(), oq.data_ptr<float>(), blocks, d);
-    sum_partials_kernel<<<(d + 255) / 256, 256, 0, stream()>>>(pk.data_ptr<float>(), ok.data_ptr<float>(), blocks, d);
+    sum_partials_kernel<<<(d + 31) / 32, dim3(32, 8), 0, stream()>>>(pq.data_ptr<float>(), oq.data_ptr<float>(), blocks,
+                                                                    d);
+    sum_partials_kernel<<<(d + 31) / 32, dim3(32, 8), 0, stream()>>>(pk.data_ptr<float>(), ok.data_ptr<float>(), blocks,
+                                                                    d);
     TS_LAUNCH_CHECK();
     dqw = oq;
     dkw = ok;

@@ -245,3 +245,28 @@ def test_attention_tcgen05_forward(t, s, hq, hkv, d):
     orf, lser = attention_reference(q.float(), k.float(), v.float(), 1 / math.sqrt(d))
     torch.testing.assert_close(o.float(), orf, atol=2e-2, rtol=2e-2)
     torch.testing.assert_close(lse, lser, atol=2e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("t,s,hq,hkv,d", ATTN_CASES + [(2048, 2560, 16, 8, 128), (300, 4396, 16, 8, 128)])
+def test_attention_tcgen05_backward(t, s, hq, hkv, d):
+    from thundersync_b200.ops._ext import native
+    from thundersync_b200.ops.attention import attention_reference
+
+    torch.manual_seed(10)
+    q = torch.randn(t, hq, d, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(s, hkv, d, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(s, hkv, d, device=DEV, dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(d)
+    o, lse = native().attn_fwd_tc(q, k, v, scale)
+    do = torch.randn_like(o)
+    dq, dk, dv = native().attn_bwd_tc(do, q, k, v, o, lse, scale)
+    torch.cuda.synchronize()
+    assert int(native().tc_status(q).item()) == 0
+    qr, kr, vr = (x.float().requires_grad_(True) for x in (q, k, v))
+    orf, _ = attention_reference(qr, kr, vr, scale)
+    gq, gk, gv = torch.autograd.grad(orf, (qr, kr, vr), do.float())
+    assert _rel(dq, gq) < 2e-2
+    assert _rel(dk, gk) < 2e-2
+    assert _rel(dv, gv) < 2e-2
+    dq2, dk2, dv2 = native().attn_bwd_tc(do, q, k, v, o, lse, scale)
+    assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)

@@ -66,7 +66,7 @@ class _ChunkedAttention(torch.autograd.Function):
         k = ks[0] if n == 1 else torch.cat(ks, 0)
         v = vs[0] if n == 1 else torch.cat(vs, 0)
         if q.is_cuda:
-            dq, dk, dv = native().attn_bwd(
+            dq, dk, dv = native().attn_bwd_tc(
                 do.contiguous(), q.contiguous(), k.contiguous(), v.contiguous(), out, lse, float(ctx.scale)
             )
         else:
