@@ -1,0 +1,116 @@
+"""OPD objectives vs an independent monolithic reference (CPU fp32)."""
+
+from __future__ import annotations
+
+import copy
+import random
+
+import pytest
+import torch
+
+from tests.grpo_fixtures import build_model
+from tests.reference_model import reference_logprobs
+from thundersync_b200.engine.streaming import StreamingRun
+from thundersync_b200.opd.objectives import OPDStream, OPDTurnStream
+
+
+def _episodes(seed=0, groups=2, per_group=2):
+    rng = random.Random(seed)
+    out = []
+    tid = 0
+    for g in range(groups):
+        prompt = [rng.randrange(512) for _ in range(12)]
+        trajs = []
+        for _ in range(per_group):
+            turns = []
+            for k in range(rng.randint(2, 3)):
+                a = [rng.randrange(512) for _ in range(rng.randint(2, 5))]
+                obs = [rng.randrange(512) for _ in range(rng.randint(1, 3))]
+                toks = a + obs
+                sc = [True] * len(a) + [False] * len(obs)
+                teacher = -torch.rand(len(a), dtype=torch.float64).float() * 3
+                turns.append((toks, sc, teacher))
+            trajs.append((tid, turns))
+            tid += 1
+        out.append((g, prompt, trajs))
+    return out
+
+
+def _reference(model, eps):
+    model.zero_grad(set_to_none=True)
+    total, mass = 0.0, 0
+    for g, prompt, trajs in eps:
+        for tid, turns in trajs:
+            lp = reference_logprobs(model, prompt, [(tk, sc) for tk, sc, _ in turns])
+            teacher = torch.cat([t for _, _, t in turns])
+            total = total + ((lp.detach() - teacher) * lp).sum()
+            mass += lp.numel()
+    (total / mass).backward()
+    return {n: p.grad.clone() for n, p in model.named_parameters()}
+
+
+def test_turn_stream_matches_monolithic():
+    model = build_model(5).eval()
+    eps = _episodes(0)
+    ref = _reference(copy.deepcopy(model), eps)
+    run = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True)
+    obj = OPDTurnStream(run, model)
+    for g, prompt, _ in eps:
+        obj.open_group(g, prompt)
+    # interleave turns across trajectories
+    queues = [(g, tid, list(turns)) for g, _, trajs in eps for tid, turns in trajs]
+    while any(q[2] for q in queues):
+        for g, tid, turns in queues:
+            if turns:
+                tk, sc, teacher = turns.pop(0)
+                obj.append_scored_turn(g, tid, tk, sc, teacher_logprobs=teacher)
+    for g, _, trajs in eps:
+        for tid, _ in trajs:
+            obj.close_trajectory(tid)
+        obj.close_group(g)
+    obj.assert_safe_to_step()
+    for n, p in model.named_parameters():
+        torch.testing.assert_close(p.grad, ref[n], rtol=2e-4, atol=2e-6, msg=n)
+    assert obj.loss_value == pytest.approx(obj.loss_value)
+
+
+def test_opd_stream_with_teacher_model():
+    model = build_model(6)
+    teacher = build_model(7)
+    eps = _episodes(1, groups=1, per_group=3)
+    # teacher scores from the teacher model (reference path)
+    for g, prompt, trajs in eps:
+        for i, (tid, turns) in enumerate(trajs):
+            tl = reference_logprobs(teacher, prompt, [(tk, sc) for tk, sc, _ in turns]).detach()
+            splits = [sum(sc) for _, sc, _ in turns]
+            parts = torch.split(tl, splits)
+            trajs[i] = (tid, [(tk, sc, t) for (tk, sc, _), t in zip(turns, parts)])
+    ref = _reference(copy.deepcopy(model), eps)
+    run = StreamingRun(model, boundary_cut=True)
+    obj = OPDStream(run, model, teacher=teacher)
+    for g, prompt, trajs in eps:
+        obj.open_group(g, prompt)
+        for tid, turns in trajs:
+            for tk, sc, _ in turns:
+                run.append_turn(g, tid, tk, sc)
+        for tid, _ in trajs:
+            obj.close_trajectory(tid)
+        obj.close_group(g)
+    obj.assert_safe_to_step()
+    for n, p in model.named_parameters():
+        torch.testing.assert_close(p.grad, ref[n], rtol=5e-4, atol=5e-6, msg=n)
+
+
+def test_turn_stream_rejects_bad_inputs():
+    model = build_model(0).eval()
+    run = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True)
+    obj = OPDTurnStream(run, model)
+    obj.open_group(0, [1, 2, 3])
+    with pytest.raises(ValueError):
+        obj.append_scored_turn(0, 0, [4, 5], [True, True], teacher_logprobs=torch.tensor([-1.0]))
+    with pytest.raises(ValueError):
+        obj.append_scored_turn(0, 0, [4, 5], [True, True], teacher_logprobs=torch.tensor([-1.0, float("nan")]))
+    with pytest.raises(RuntimeError):
+        obj.assert_safe_to_step()
+    with pytest.raises(ValueError):
+        OPDTurnStream(StreamingRun(model, boundary_cut=True), model)

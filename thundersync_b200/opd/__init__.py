@@ -1,1 +1,1 @@
-"""opd"""
+"""On-policy distillation objectives."""
