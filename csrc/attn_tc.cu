@@ -1,16 +1,17 @@
 // Bottom-right causal attention forward on the 5th-generation tensor cores.
 //
 // One CTA computes a 128-query tile of one head:
-//   warp 4      TMA producer: Q once, then K/V 128-key tiles through a
+//   warp 8      TMA producer: Q once, then K/V 128-key tiles through a
 //               2-stage ring (128B-swizzled boxes of 64 columns)
-//   warp 5      MMA issuer (one thread): S = Q K^T into one of two TMEM
+//   warp 9      MMA issuer (one thread): S = Q K^T into one of two TMEM
 //               S buffers, O += P V into the TMEM O accumulator; commits
 //               signal the other roles through mbarriers
-//   warps 0-3   softmax: thread r owns query row r; reads its S row from
-//               TMEM, applies the bottom-right mask, online max/sum in the
-//               log2 domain, writes P (bf16) into a double-buffered
-//               K-major SW128 shared tile, and rescales its O row in TMEM
-//               only when the row max moved
+//   warps 0-7   softmax: a pair of warps owns 32 query rows (one TMEM
+//               sub-partition); both read the full S row for the max, each
+//               exponentiates one 64-column half (online max/sum in the log2
+//               domain, bottom-right mask), writes its half of P (bf16) into
+//               a double-buffered K-major SW128 shared tile, and rescales its
+//               half of the O row in TMEM only when the row max moved
 // The tensor core computes S(j+1) while the softmax warps work on S(j), and
 // PV(j) while they work on S(j+1). Epilogue: O / l (bf16) and the natural-log
 // LSE. Every mbarrier wait is bounded (see tc.cuh).
@@ -56,7 +57,8 @@ struct FwdLayout {
   static constexpr uint32_t P0 = V0 + 2 * K_BYTES;
   static constexpr uint32_t P_BYTES = BM * BN * 2;
   static constexpr uint32_t BAR = P0 + 2 * P_BYTES;
-  static constexpr uint32_t TOTAL = BAR + 256;
+  static constexpr uint32_t RED = BAR + 256;  // [2][128] floats: the pair's partial row sums
+  static constexpr uint32_t TOTAL = RED + 1024;
   // TMEM columns
   static constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256;
 };
@@ -68,7 +70,7 @@ struct FwdBars {
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+__global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                              const __grid_constant__ CUtensorMap tm_k,
                                                              const __grid_constant__ CUtensorMap tm_v,
                                                              bf16* __restrict__ out, float* __restrict__ lse,
@@ -96,18 +98,18 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_consta
       tc::mbar_init(&bars->v_full[i], 1);
       tc::mbar_init(&bars->kv_empty[i], 1);
       tc::mbar_init(&bars->s_full[i], 1);
-      tc::mbar_init(&bars->p_full[i], 128);
+      tc::mbar_init(&bars->p_full[i], 256);
     }
     tc::mbar_init(&bars->pv, 1);
     bars->abort = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 5) tc::tmem_alloc(&bars->tmem_slot, 512);
+  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tc::prefetch_tmap(&tm_q);
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_consta
                           &bars->v_full[s]);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
@@ -171,11 +173,16 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_consta
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax (warps 0-3)
-    const int r = threadIdx.x;  // query row within the tile
+    // ------------------------------------------------------------ softmax (warps 0-7)
+    // warp w owns rows of TMEM sub-partition (w & 3); both warps of a pair read
+    // the whole S row for the max, but each exponentiates, sums and stores
+    // only its 64-column half (hc) and rescales half of the O row.
+    const int r = (warp & 3) * 32 + lane;
+    const int hc = warp >> 2;
     const int qi = q0 + r;
     const int lim = qi + off;   // keys <= lim are visible
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    float* lsum = reinterpret_cast<float*>(smem + L::RED);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n && ok; ++j) {
@@ -183,33 +190,42 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_consta
       if (!warp_wait(&bars->s_full[s], (j >> 1) & 1, abort, err, 31)) { ok = false; break; }
       tc::tc_fence_after();
       float sv[128];
+      const uint32_t scol = s ? L::S_COL1 : L::S_COL0;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tc::tmem_ld32(lane_base + (s ? L::S_COL1 : L::S_COL0) + c * 32, sv + c * 32);
+      for (int c = 0; c < 4; ++c) tc::tmem_ld32(lane_base + scol + c * 32, sv + c * 32);
       tc::tmem_ld_wait();
       const int k0 = j * L::BN;
-      float mx = m;
-      const bool need_mask = (k0 + L::BN - 1 > q0 + off) || (k0 + L::BN > S);
+      int nvis = min(lim, S - 1) - k0 + 1;  // visible columns of this tile for this row
+      nvis = nvis < 0 ? 0 : (nvis > L::BN ? L::BN : nvis);
+      float raw = -INFINITY;
+      if (nvis == L::BN) {
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        float x = sv[i] * sl2;
-        if (need_mask && (k0 + i > lim || k0 + i >= S)) x = -INFINITY;
-        sv[i] = x;
-        mx = fmaxf(mx, x);
+        for (int i = 0; i < 128; ++i) raw = fmaxf(raw, sv[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) raw = fmaxf(raw, i < nvis ? sv[i] : -INFINITY);
       }
+      const float mx = fmaxf(m, raw * sl2);
       const float ref = mx == -INFINITY ? 0.f : mx;
       const float alpha = exp2f(m - ref);
+      // this warp's 64-column half, reloaded into registers with static indices
+      tc::tmem_ld32(lane_base + scol + hc * 64, sv);
+      tc::tmem_ld32(lane_base + scol + hc * 64 + 32, sv + 32);
+      tc::tmem_ld_wait();
+      const int nv_half = nvis - hc * 64;
       float rs = 0.f;
       const uint32_t pbase = sbase + L::P0 + s * L::P_BYTES;
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
+      for (int c8 = 0; c8 < 8; ++c8) {
         float p[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          p[e] = exp2f(sv[c8 * 8 + e] - ref);
+          const int i = c8 * 8 + e;
+          p[e] = i < nv_half ? exp2f(fmaf(sv[i], sl2, -ref)) : 0.f;
           rs += p[e];
         }
-        st_shared_v4(pbase + tc::kmajor_off(r, c8 * 8, 128), pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]),
-                     pack2(p[6], p[7]));
+        st_shared_v4(pbase + tc::kmajor_off(r, hc * 64 + c8 * 8, 128), pack2(p[0], p[1]), pack2(p[2], p[3]),
+                     pack2(p[4], p[5]), pack2(p[6], p[7]));
       }
       l = l * alpha + rs;
       if (j > 0) {
@@ -217,7 +233,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_consta
         tc::tc_fence_after();
         if (__any_sync(0xffffffffu, alpha < 1.f)) {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
             float o[32];
             tc::tmem_ld32(lane_base + L::O_COL + c * 32, o);
             tc::tmem_ld_wait();
@@ -233,11 +249,15 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_consta
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->p_full[s]);
     }
+    // the pair's half sums: exchanged once through shared memory
+    lsum[hc * 128 + r] = l;
+    asm volatile("bar.sync 1, 256;\n" ::: "memory");
+    const float lt = lsum[r] + lsum[128 + r];
     if (ok && warp_wait(&bars->pv, (n - 1) & 1, abort, err, 33)) {
       tc::tc_fence_after();
-      const float inv = 1.f / l;
+      const float inv = 1.f / lt;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
         float o[32];
         tc::tmem_ld32(lane_base + L::O_COL + c * 32, o);
         tc::tmem_ld_wait();
@@ -254,12 +274,12 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc_kernel(const __grid_consta
           }
         }
       }
-      if (qi < T) lse[(long long)h * T + qi] = (m + log2f(l)) * kLn2;
+      if (qi < T && hc == 0) lse[(long long)h * T + qi] = (m + log2f(lt)) * kLn2;
     }
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -314,7 +334,7 @@ struct DkvBars {
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
+__global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
     const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dk, bf16* __restrict__ dv,
@@ -342,19 +362,19 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&bars->q_full[i], 2);
       tc::mbar_init(&bars->s_full[i], 1);
-      tc::mbar_init(&bars->p_full[i], 128);
+      tc::mbar_init(&bars->p_full[i], 256);
       tc::mbar_init(&bars->mma_done[i], 1);
     }
     tc::mbar_init(&bars->fin, 1);
     bars->abort = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 5) tc::tmem_alloc(&bars->tmem_slot, 512);
+  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // producer: K, V once; per step Q and dO tiles (TMA) plus lse2 / delta (plain loads)
     if (lane == 0) {
       tc::mbar_expect_tx(&bars->kv, 2 * L::KV_BYTES);
@@ -385,7 +405,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->q_full[st]);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       const uint32_t id_s = tc::idesc_bf16(128, L::BQ, false, false);
       const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
@@ -431,9 +451,12 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
       if (ok) tc::mma_commit(&bars->fin);
     }
   } else {
-    const int r = threadIdx.x;
+    // warps 0-7: warp w reads TMEM lanes of sub-partition (w & 3) and handles
+    // query columns [32 * (w >> 2), +32) of each step
+    const int r = (warp & 3) * 32 + lane;
+    const int hc = warp >> 2;
     const int kr = k0 + r;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool ok = true;
     for (int i = 0; i < total && ok; ++i) {
       const int st = i & 1;
@@ -442,29 +465,28 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
       if (!warp_wait(&bars->s_full[st], (i >> 1) & 1, abort, err, 72)) { ok = false; break; }
       if (i >= 2 && !warp_wait(&bars->mma_done[st], ((i - 2) >> 1) & 1, abort, err, 73)) { ok = false; break; }
       tc::tc_fence_after();
-      float sv[64], dp[64];
-      const uint32_t col = L::ST_COL0 + st * 2 * L::BQ;
+      float sv[32], dp[32];
+      const uint32_t col = L::ST_COL0 + st * 2 * L::BQ + hc * 32;
       tc::tmem_ld32(lane_base + col, sv);
-      tc::tmem_ld32(lane_base + col + 32, sv + 32);
       tc::tmem_ld32(lane_base + col + L::BQ, dp);
-      tc::tmem_ld32(lane_base + col + L::BQ + 32, dp + 32);
       tc::tmem_ld_wait();
-      const float* l2 = ld + (st * 2 + 0) * L::BQ;
-      const float* dl = ld + (st * 2 + 1) * L::BQ;
-      const bool full = (qt >= kr - off) && (qt + L::BQ <= T) && kr < S;
+      const float* l2 = ld + (st * 2 + 0) * L::BQ + hc * 32;
+      const float* dl = ld + (st * 2 + 1) * L::BQ + hc * 32;
+      const int qc0 = qt + hc * 32;
+      const bool full = (qc0 >= kr - off) && (qc0 + 32 <= T) && kr < S;
       const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
 #pragma unroll
-      for (int c8 = 0; c8 < L::BQ / 8; ++c8) {
+      for (int c8 = 0; c8 < 4; ++c8) {
         float p[8], ds[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int c = c8 * 8 + e;
-          const int qi = qt + c;
+          const int qi = qc0 + c;
           const bool vis = full || (qi < T && kr < S && kr <= qi + off);
           p[e] = vis ? exp2f(sv[c] * sl2 - l2[c]) : 0.f;
           ds[e] = p[e] * (dp[c] - dl[c]);
         }
-        const uint32_t o8 = tc::kmajor_off(r, c8 * 8, 128);
+        const uint32_t o8 = tc::kmajor_off(r, hc * 32 + c8 * 8, 128);
         st_shared_v4(pb + o8, pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]), pack2(p[6], p[7]));
         st_shared_v4(db + o8, pack2(ds[0], ds[1]), pack2(ds[2], ds[3]), pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
       }
@@ -475,7 +497,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
     if (ok && total > 0 && warp_wait(&bars->fin, 0, abort, err, 74)) {
       tc::tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
         float a[32], b[32];
         tc::tmem_ld32(lane_base + L::DK_COL + c * 32, a);
         tc::tmem_ld32(lane_base + L::DV_COL + c * 32, b);
@@ -496,8 +518,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
         }
       }
     } else if (ok && total == 0 && kr < S) {
-      // no query sees these keys
-      for (int c = 0; c < D; c += 8) {
+      for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 8) {
         *reinterpret_cast<uint4*>(dk + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(dv + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
       }
@@ -505,7 +526,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dkdv_tc_kernel(
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -537,7 +558,7 @@ struct DqBars {
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1) attn_bwd_dq_tc_kernel(
+__global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
     const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T, int S, int Hq,
@@ -563,19 +584,19 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dq_tc_kernel(
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&bars->kv_full[i], 1);
       tc::mbar_init(&bars->s_full[i], 1);
-      tc::mbar_init(&bars->p_full[i], 128);
+      tc::mbar_init(&bars->p_full[i], 256);
       tc::mbar_init(&bars->mma_done[i], 1);
     }
     tc::mbar_init(&bars->fin, 1);
     bars->abort = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 5) tc::tmem_alloc(&bars->tmem_slot, 512);
+  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       tc::mbar_expect_tx(&bars->q, 2 * L::Q_BYTES);
       for (int b = 0; b < L::NB; ++b) {
@@ -594,7 +615,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dq_tc_kernel(
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
       const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
@@ -636,30 +657,30 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dq_tc_kernel(
       if (ok) tc::mma_commit(&bars->fin);
     }
   } else {
-    const int r = threadIdx.x;
+    // warps 0-7: sub-partition (w & 3) rows, key columns [32 * (w >> 2), +32)
+    const int r = (warp & 3) * 32 + lane;
+    const int hc = warp >> 2;
     const int qi = q0 + r;
     const int lim = qi + off;
     const float l2 = qi < T ? lse[(long long)h * T + qi] * kLog2e : 0.f;
     const float dl = qi < T ? delta[(long long)h * T + qi] : 0.f;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool ok = true;
     for (int j = 0; j < n && ok; ++j) {
       const int st = j & 1;
       if (!warp_wait(&bars->s_full[st], (j >> 1) & 1, abort, err, 101)) { ok = false; break; }
       if (j >= 2 && !warp_wait(&bars->mma_done[st], ((j - 2) >> 1) & 1, abort, err, 102)) { ok = false; break; }
       tc::tc_fence_after();
-      float sv[64], dp[64];
-      const uint32_t col = L::S_COL0 + st * 2 * L::BN;
+      float sv[32], dp[32];
+      const uint32_t col = L::S_COL0 + st * 2 * L::BN + hc * 32;
       tc::tmem_ld32(lane_base + col, sv);
-      tc::tmem_ld32(lane_base + col + 32, sv + 32);
       tc::tmem_ld32(lane_base + col + L::BN, dp);
-      tc::tmem_ld32(lane_base + col + L::BN + 32, dp + 32);
       tc::tmem_ld_wait();
-      const int k0 = j * L::BN;
-      const bool full = (k0 + L::BN - 1 <= q0 + off) && (k0 + L::BN <= S) && qi < T;
+      const int k0 = j * L::BN + hc * 32;
+      const bool full = (k0 + 31 <= q0 + off) && (k0 + 32 <= S) && qi < T;
       const uint32_t db = sbase + L::DS0 + st * L::DS_BYTES;
 #pragma unroll
-      for (int c8 = 0; c8 < L::BN / 8; ++c8) {
+      for (int c8 = 0; c8 < 4; ++c8) {
         float ds[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -669,7 +690,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dq_tc_kernel(
           const float p = vis ? exp2f(sv[c] * sl2 - l2) : 0.f;
           ds[e] = p * (dp[c] - dl);
         }
-        st_shared_v4(db + tc::kmajor_off(r, c8 * 8, 128), pack2(ds[0], ds[1]), pack2(ds[2], ds[3]),
+        st_shared_v4(db + tc::kmajor_off(r, hc * 32 + c8 * 8, 128), pack2(ds[0], ds[1]), pack2(ds[2], ds[3]),
                      pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
       }
       tc::fence_async_smem();
@@ -679,7 +700,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dq_tc_kernel(
     if (ok && warp_wait(&bars->fin, 0, abort, err, 103)) {
       tc::tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
         float a[32];
         tc::tmem_ld32(lane_base + L::DQ_COL + c * 32, a);
         tc::tmem_ld_wait();
@@ -698,7 +719,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dq_tc_kernel(
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -856,12 +877,12 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
   if (D == 128) {
     const int smem = FwdLayout<128>::TOTAL + 1024;
     TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attn_fwd_tc_kernel<128><<<grid, 192, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
+    attn_fwd_tc_kernel<128><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
                                                            S, Hq, Hkv, sl2, err);
   } else if (D == 64) {
     const int smem = FwdLayout<64>::TOTAL + 1024;
     TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attn_fwd_tc_kernel<64><<<grid, 192, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
+    attn_fwd_tc_kernel<64><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
                                                           S, Hq, Hkv, sl2, err);
   } else {
     TS_CHECK(false, "tcgen05 attention supports head_dim 64 and 128");
@@ -904,20 +925,20 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
     const int s1 = DkvLayout<128>::TOTAL + 1024, s2 = DqLayout<128>::TOTAL + 1024;
     TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
     TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
-    attn_bwd_dkdv_tc_kernel<128><<<g1, 192, s1, stream()>>>(mq64, mk128, mv128, mo64, lse.data_ptr<float>(),
+    attn_bwd_dkdv_tc_kernel<128><<<g1, 320, s1, stream()>>>(mq64, mk128, mv128, mo64, lse.data_ptr<float>(),
                                                             delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
                                                             (bf16*)dv.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
-    attn_bwd_dq_tc_kernel<128><<<g2, 192, s2, stream()>>>(mq128, mk64, mv64, mo128, lse.data_ptr<float>(),
+    attn_bwd_dq_tc_kernel<128><<<g2, 320, s2, stream()>>>(mq128, mk64, mv64, mo128, lse.data_ptr<float>(),
                                                           delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq,
                                                           Hkv, (float)scale, err);
   } else {
     const int s1 = DkvLayout<64>::TOTAL + 1024, s2 = DqLayout<64>::TOTAL + 1024;
     TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
     TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
-    attn_bwd_dkdv_tc_kernel<64><<<g1, 192, s1, stream()>>>(mq64, mk128, mv128, mo64, lse.data_ptr<float>(),
+    attn_bwd_dkdv_tc_kernel<64><<<g1, 320, s1, stream()>>>(mq64, mk128, mv128, mo64, lse.data_ptr<float>(),
                                                            delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
                                                            (bf16*)dv.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
-    attn_bwd_dq_tc_kernel<64><<<g2, 192, s2, stream()>>>(mq128, mk64, mv64, mo128, lse.data_ptr<float>(),
+    attn_bwd_dq_tc_kernel<64><<<g2, 320, s2, stream()>>>(mq128, mk64, mv64, mo128, lse.data_ptr<float>(),
                                                          delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq,
                                                          Hkv, (float)scale, err);
   }
