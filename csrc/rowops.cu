@@ -7,6 +7,7 @@
 // reproducible run to run.
 #include "common.cuh"
 #include "common.h"
+#include "noalloc.h"
 
 namespace ts {
 namespace {
@@ -673,3 +674,111 @@ void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const a
 }
 
 }  // namespace ts
+
+// =================================================================== allocation-free entry point
+// ts_rms_norm_bwd_noalloc (declared in noalloc.h) runs the same three kernels
+// as rms_norm_bwd, but its per-chunk weight-gradient partials live in the
+// file-scope array below instead of a caching-allocator buffer.
+//
+// * The array is a fixed 2 MiB (TS_NOALLOC_RMS_MAX_CHUNKS x
+//   TS_NOALLOC_RMS_MAX_COLS floats); every GPU that loads this library holds
+//   it until the process exits.
+// * Host code cannot pass the array's name to a kernel (on the host it is only
+//   a stand-in symbol), so the first call on each device, with that device
+//   current, looks up its device address with cudaGetSymbolAddress and caches
+//   it. Make that first call before any stream capture.
+// * Every call shares the one array and the last call's contents stay in it.
+//   Each call writes every partial it later reads, so nothing has to start at
+//   zero; calls whose kernels overlap on the GPU (different streams without
+//   ordering) race on the array and must be serialised by the caller.
+// * No cudaMalloc, cudaFree or allocating library routine is called.
+namespace ts {
+namespace {
+
+static __device__ __align__(256) float g_noalloc_rms_partial[TS_NOALLOC_RMS_MAX_CHUNKS * TS_NOALLOC_RMS_MAX_COLS];
+
+float* g_noalloc_rms_ptr[64] = {nullptr};
+thread_local char g_noalloc_msg[256] = "";
+
+int noalloc_fail(int code, const char* msg) {
+  snprintf(g_noalloc_msg, sizeof(g_noalloc_msg), "%s", msg);
+  return code;
+}
+
+template <typename T, int V>
+void noalloc_dx(const T* dy, const T* x, const T* w, const float* rstd, T* dx, int rows, int H, cudaStream_t st) {
+  rms_bwd_dx_kernel<T, V><<<(rows + kWarps - 1) / kWarps, kWarps * 32, 0, st>>>(dy, x, w, rstd, dx, rows, H);
+}
+
+template <typename T>
+int noalloc_run(const T* dy, const T* x, const T* w, const float* rstd, T* dx, float* dw, int rows, int H,
+                float* partial, int device, cudaStream_t st) {
+  constexpr int E = Vec<T>::N;
+  const int nv = (H + 32 * E - 1) / (32 * E);
+  if (nv <= 1) noalloc_dx<T, 1>(dy, x, w, rstd, dx, rows, H, st);
+  else if (nv <= 2) noalloc_dx<T, 2>(dy, x, w, rstd, dx, rows, H, st);
+  else if (nv <= 4) noalloc_dx<T, 4>(dy, x, w, rstd, dx, rows, H, st);
+  else if (nv <= 8) noalloc_dx<T, 8>(dy, x, w, rstd, dx, rows, H, st);
+  else if (nv <= 12) noalloc_dx<T, 12>(dy, x, w, rstd, dx, rows, H, st);
+  else if (nv <= 16) noalloc_dx<T, 16>(dy, x, w, rstd, dx, rows, H, st);
+  else return noalloc_fail(3, "ts_rms_norm_bwd_noalloc: row width too large for the register path");
+  const int col_blocks = (H + 32 * E - 1) / (32 * E);
+  const int target = 2 * sm_count(device);
+  int chunks = std::max(1, std::min((rows + 7) / 8, target / std::max(col_blocks, 1)));
+  chunks = std::min(chunks, TS_NOALLOC_RMS_MAX_CHUNKS);
+  const int rows_per_chunk = (rows + chunks - 1) / chunks;
+  chunks = (rows + rows_per_chunk - 1) / rows_per_chunk;
+  rms_dw_partial_kernel<T><<<dim3(col_blocks, chunks), dim3(32, 8), 0, st>>>(dy, x, rstd, partial, rows, H,
+                                                                            rows_per_chunk);
+  sum_partials_kernel<<<(H + 31) / 32, dim3(32, 8), 0, st>>>(partial, dw, chunks, H);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return noalloc_fail(5, cudaGetErrorString(e));
+  return 0;
+}
+
+}  // namespace
+}  // namespace ts
+
+extern "C" __attribute__((visibility("default"))) const char* ts_noalloc_last_error(void) {
+  return ts::g_noalloc_msg;
+}
+
+extern "C" __attribute__((visibility("default"))) int ts_rms_norm_bwd_noalloc(const void* dy, const void* x,
+                                                                            const void* w, const float* rstd,
+                                                                            void* dx, float* dw, int rows, int cols,
+                                                                            int dtype, void* stream) {
+  using namespace ts;
+  g_noalloc_msg[0] = '\0';
+  if (rows < 0 || cols <= 0) return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: rows must be >= 0 and cols > 0");
+  if (cols > TS_NOALLOC_RMS_MAX_COLS) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "ts_rms_norm_bwd_noalloc: cols=%d exceeds the fixed scratch limit of %d columns", cols,
+             TS_NOALLOC_RMS_MAX_COLS);
+    return noalloc_fail(2, buf);
+  }
+  if (dtype != 0 && dtype != 1) return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: dtype must be 0 (bf16) or 1 (fp32)");
+  if ((dtype == 0 && cols % 8) || (dtype == 1 && cols % 4))
+    return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: cols must be a multiple of 8 (bf16) or 4 (fp32)");
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    return noalloc_fail(4, "ts_rms_norm_bwd_noalloc: no current CUDA device");
+  if (g_noalloc_rms_ptr[device] == nullptr) {
+    // once per device, with that device current: the array's device address
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_rms_partial);
+    if (e != cudaSuccess || p == nullptr) return noalloc_fail(4, cudaGetErrorString(e));
+    g_noalloc_rms_ptr[device] = static_cast<float*>(p);
+  }
+  if (rows == 0) {
+    return cudaMemsetAsync(dw, 0, sizeof(float) * cols, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? 0
+               : noalloc_fail(5, "ts_rms_norm_bwd_noalloc: clearing dw failed");
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == 0)
+    return noalloc_run<__nv_bfloat16>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w,
+                                      rstd, (__nv_bfloat16*)dx, dw, rows, cols, g_noalloc_rms_ptr[device], device,
+                                      st);
+  return noalloc_run<float>((const float*)dy, (const float*)x, (const float*)w, rstd, (float*)dx, dw, rows, cols,
+                            g_noalloc_rms_ptr[device], device, st);
+}
