@@ -1,10 +1,11 @@
-"""Symmetric-memory workspace and the native NVLink collectives (N0-N3, host side).
+"""Peer-mapped workspace and the native NVLink collectives (N0-N3, host side).
 
-Buffers are allocated and peer-mapped through torch's symmetric-memory
-allocator (``torch.distributed._symmetric_memory``: VMM allocations whose
-handles are exchanged over the process group's store); every collective
-itself is this package's kernel (``csrc/comm.cu``) reading and writing peer
-memory over NVLink:
+Buffers are dedicated ``cudaMalloc`` allocations exported with CUDA IPC
+handles; the handles are exchanged through the process group and every peer
+opens them, so each rank holds device pointers to every rank's buffer
+(``csrc/ipc.cpp``; plain peer mappings, no multicast objects). Every
+collective is this package's kernel (``csrc/comm.cu``) reading and writing
+peer memory over NVLink:
 
 * ``barrier``            bounded-wait flag barrier; a peer that never arrives
                          sets a device status word instead of hanging
@@ -47,18 +48,10 @@ def shard_bounds(numel: int, world: int, rank: int, align: int = 4) -> tuple[int
     return lo, min(numel, lo + chunk)
 
 
-def _group_name(group) -> str:
-    g = group if group is not None else dist.group.WORLD
-    return g.group_name
-
-
 class SymmetricWorkspace:
     """Peer-mapped buffers of one process group on this rank's device."""
 
     def __init__(self, device: torch.device, group=None, *, timeout_s: float = 30.0) -> None:
-        import torch.distributed._symmetric_memory as symm_mem
-
-        self._symm = symm_mem
         self.device = device
         self.group = group
         self.rank = dist.get_rank(group)
@@ -66,23 +59,32 @@ class SymmetricWorkspace:
         if self.world > _MAX_RANKS:
             raise ValueError(f"the native collectives support up to {_MAX_RANKS} ranks")
         self.timeout_s = float(timeout_s)
-        name = _group_name(group)
-        try:
-            symm_mem.enable_symm_mem_for_group(name)
-        except Exception:
-            pass
-        self._name = name
+        self._owned: list[torch.Tensor] = []
+        self._opened: list[int] = []
         self.flags, self.flag_ptrs = self.alloc(_NORM_OFFSET + _MAX_RANKS, torch.int32)
-        self.flags.zero_()
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self._epochs = [0] * _SLOTS
         torch.cuda.synchronize(device)
         dist.barrier(group)
 
     def alloc(self, numel: int, dtype: torch.dtype) -> tuple[torch.Tensor, list[int]]:
-        t = self._symm.empty(numel, dtype=dtype, device=self.device)
-        hdl = self._symm.rendezvous(t, self._name)
-        return t, [int(p) for p in hdl.buffer_ptrs]
+        """A zeroed buffer on every rank; returns (local tensor, every rank's device pointer)."""
+        esize = torch.empty(0, dtype=dtype).element_size()
+        nbytes = -(-numel * esize // 256) * 256
+        raw, handle = native().ipc_alloc(nbytes, self.device.index)
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(int(raw.data_ptr()))
+            else:
+                p = int(native().ipc_open(h, self.device.index))
+                self._opened.append(p)
+                ptrs.append(p)
+        self._owned.append(raw)
+        t = raw.view(dtype)[:numel]
+        return t, ptrs
 
     @property
     def norm_slots(self) -> torch.Tensor:
@@ -117,6 +119,16 @@ class SymmetricWorkspace:
         return lo, hi
 
     def close(self) -> None:
+        """Unmap peers, wait for every rank to do the same, then free local buffers."""
+        if self.flags is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            native().ipc_close(p)
+        self._opened.clear()
+        if dist.is_initialized():
+            dist.barrier(self.group)
+        self._owned.clear()
         self.flags = None
 
 
