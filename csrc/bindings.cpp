@@ -2,18 +2,19 @@
 #include "common.h"
 
 namespace ts {
-std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps);
+std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, bool unit);
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                     const at::Tensor& rstd);
+                                     const at::Tensor& rstd, bool unit);
 std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
                                          const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
-                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d, double eps);
+                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d, double eps,
+                                         bool unit);
 std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk,
                                                         const at::Tensor& dv, const at::Tensor& qkv,
                                                         const c10::optional<at::Tensor>& qw,
                                                         const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
-                                                        int64_t d, double eps);
+                                                        int64_t d, double eps, bool unit);
 at::Tensor swiglu_fwd(const at::Tensor& gu);
 at::Tensor swiglu_bwd(const at::Tensor& da, const at::Tensor& gu);
 void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const at::Tensor& dy, double scale);
@@ -48,10 +49,20 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
 at::Tensor tc_status(const at::Tensor& like);
 std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                     const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale);
+void register_ipc(pybind11::module& m);
+std::vector<at::Tensor> conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& tail);
+std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& dtail_out, const at::Tensor& x,
+                                        const at::Tensor& w, const at::Tensor& tail);
+std::vector<at::Tensor> gdn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                                const at::Tensor& beta, const at::Tensor& state);
+std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& dfinal, const at::Tensor& q,
+                                const at::Tensor& k, const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta,
+                                const at::Tensor& saved);
 }  // namespace ts
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "thundersync_b200 native sm_100a kernels";
+  ts::register_ipc(m);
   m.def("rms_norm_fwd", &ts::rms_norm_fwd);
   m.def("rms_norm_bwd", &ts::rms_norm_bwd);
   m.def("qk_norm_rope_fwd", &ts::qk_norm_rope_fwd);
@@ -78,4 +89,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_reduce", &ts::symm_reduce);
   m.def("symm_norm_put", &ts::symm_norm_put);
   m.def("symm_adamw_gather", &ts::symm_adamw_gather);
+  m.def("conv1d_silu_fwd", &ts::conv1d_silu_fwd);
+  m.def("conv1d_silu_bwd", &ts::conv1d_silu_bwd);
+  m.def("gdn_fwd", &ts::gdn_fwd);
+  m.def("gdn_bwd", &ts::gdn_bwd);
 }

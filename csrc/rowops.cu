@@ -19,7 +19,7 @@ constexpr int kWarps = 8;
 template <typename T, int V>
 __global__ void __launch_bounds__(kWarps * 32) rms_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                               T* __restrict__ y, float* __restrict__ rstd,
-                                                              int rows, int H, float eps) {
+                                                              int rows, int H, float eps, int unit) {
   constexpr int E = Vec<T>::N;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
@@ -50,8 +50,12 @@ __global__ void __launch_bounds__(kWarps * 32) rms_fwd_kernel(const T* __restric
       Vec<T> o;
 #pragma unroll
       for (int e = 0; e < E; ++e) {
-        float n = round_to<T>(to_f(buf[v].e[e]) * r);
-        o.e[e] = from_f<T>(to_f(wv.e[e]) * n);
+        if (unit) {  // (1 + w) * x * rstd, one rounding
+          o.e[e] = from_f<T>(to_f(buf[v].e[e]) * r * (1.f + to_f(wv.e[e])));
+        } else {     // w * round(x * rstd)
+          float n = round_to<T>(to_f(buf[v].e[e]) * r);
+          o.e[e] = from_f<T>(to_f(wv.e[e]) * n);
+        }
       }
       store_vec(yr + c, o);
     }
@@ -64,7 +68,7 @@ template <typename T, int V>
 __global__ void __launch_bounds__(kWarps * 32) rms_bwd_dx_kernel(const T* __restrict__ dy, const T* __restrict__ x,
                                                                  const T* __restrict__ w,
                                                                  const float* __restrict__ rstd,
-                                                                 T* __restrict__ dx, int rows, int H) {
+                                                                 T* __restrict__ dx, int rows, int H, float woff) {
   constexpr int E = Vec<T>::N;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
@@ -84,7 +88,7 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_dx_kernel(const T* __rest
 #pragma unroll
       for (int e = 0; e < E; ++e) {
         float n = to_f(xb[v].e[e]) * r;
-        float dn = to_f(db[v].e[e]) * to_f(wv.e[e]);
+        float dn = to_f(db[v].e[e]) * (to_f(wv.e[e]) + woff);
         dot += dn * n;
       }
     }
@@ -100,7 +104,7 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_dx_kernel(const T* __rest
 #pragma unroll
       for (int e = 0; e < E; ++e) {
         float n = to_f(xb[v].e[e]) * r;
-        float dn = to_f(db[v].e[e]) * to_f(wv.e[e]);
+        float dn = to_f(db[v].e[e]) * (to_f(wv.e[e]) + woff);
         o.e[e] = from_f<T>(r * (dn - n * dot));
       }
       store_vec(dxr + c, o);
@@ -167,21 +171,21 @@ __global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restri
 }
 
 template <typename T, int V>
-void launch_rms_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, float eps) {
+void launch_rms_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, float eps, int unit) {
   const int rows = x.size(0), H = x.size(1);
   dim3 grid((rows + kWarps - 1) / kWarps);
   rms_fwd_kernel<T, V><<<grid, kWarps * 32, 0, stream()>>>(
-      (const T*)x.data_ptr(), (const T*)w.data_ptr(), (T*)y.data_ptr(), rstd.data_ptr<float>(), rows, H, eps);
+      (const T*)x.data_ptr(), (const T*)w.data_ptr(), (T*)y.data_ptr(), rstd.data_ptr<float>(), rows, H, eps, unit);
 }
 
 template <typename T, int V>
 void launch_rms_dx(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
-                   at::Tensor& dx) {
+                   at::Tensor& dx, float woff) {
   const int rows = x.size(0), H = x.size(1);
   dim3 grid((rows + kWarps - 1) / kWarps);
   rms_bwd_dx_kernel<T, V><<<grid, kWarps * 32, 0, stream()>>>(
       (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)w.data_ptr(), rstd.data_ptr<float>(),
-      (T*)dx.data_ptr(), rows, H);
+      (T*)dx.data_ptr(), rows, H, woff);
 }
 
 template <typename T>
@@ -206,31 +210,31 @@ at::Tensor column_weight_grad(const at::Tensor& dy, const at::Tensor& x, const a
 }
 
 template <typename T>
-void rms_fwd_dispatch(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, float eps) {
+void rms_fwd_dispatch(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, float eps, int unit) {
   constexpr int E = Vec<T>::N;
   const int H = x.size(1);
   const int nv = (H + 32 * E - 1) / (32 * E);
-  if (nv <= 1) launch_rms_fwd<T, 1>(x, w, y, rstd, eps);
-  else if (nv <= 2) launch_rms_fwd<T, 2>(x, w, y, rstd, eps);
-  else if (nv <= 4) launch_rms_fwd<T, 4>(x, w, y, rstd, eps);
-  else if (nv <= 8) launch_rms_fwd<T, 8>(x, w, y, rstd, eps);
-  else if (nv <= 12) launch_rms_fwd<T, 12>(x, w, y, rstd, eps);
-  else if (nv <= 16) launch_rms_fwd<T, 16>(x, w, y, rstd, eps);
+  if (nv <= 1) launch_rms_fwd<T, 1>(x, w, y, rstd, eps, unit);
+  else if (nv <= 2) launch_rms_fwd<T, 2>(x, w, y, rstd, eps, unit);
+  else if (nv <= 4) launch_rms_fwd<T, 4>(x, w, y, rstd, eps, unit);
+  else if (nv <= 8) launch_rms_fwd<T, 8>(x, w, y, rstd, eps, unit);
+  else if (nv <= 12) launch_rms_fwd<T, 12>(x, w, y, rstd, eps, unit);
+  else if (nv <= 16) launch_rms_fwd<T, 16>(x, w, y, rstd, eps, unit);
   else TS_CHECK(false, "RMSNorm row width ", H, " is too large");
 }
 
 template <typename T>
 void rms_dx_dispatch(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
-                     at::Tensor& dx) {
+                     at::Tensor& dx, float woff) {
   constexpr int E = Vec<T>::N;
   const int H = x.size(1);
   const int nv = (H + 32 * E - 1) / (32 * E);
-  if (nv <= 1) launch_rms_dx<T, 1>(dy, x, w, rstd, dx);
-  else if (nv <= 2) launch_rms_dx<T, 2>(dy, x, w, rstd, dx);
-  else if (nv <= 4) launch_rms_dx<T, 4>(dy, x, w, rstd, dx);
-  else if (nv <= 8) launch_rms_dx<T, 8>(dy, x, w, rstd, dx);
-  else if (nv <= 12) launch_rms_dx<T, 12>(dy, x, w, rstd, dx);
-  else if (nv <= 16) launch_rms_dx<T, 16>(dy, x, w, rstd, dx);
+  if (nv <= 1) launch_rms_dx<T, 1>(dy, x, w, rstd, dx, woff);
+  else if (nv <= 2) launch_rms_dx<T, 2>(dy, x, w, rstd, dx, woff);
+  else if (nv <= 4) launch_rms_dx<T, 4>(dy, x, w, rstd, dx, woff);
+  else if (nv <= 8) launch_rms_dx<T, 8>(dy, x, w, rstd, dx, woff);
+  else if (nv <= 12) launch_rms_dx<T, 12>(dy, x, w, rstd, dx, woff);
+  else if (nv <= 16) launch_rms_dx<T, 16>(dy, x, w, rstd, dx, woff);
   else TS_CHECK(false, "RMSNorm row width ", H, " is too large");
 }
 
@@ -241,7 +245,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
     const T* __restrict__ qkv, const T* __restrict__ qw, const T* __restrict__ kw, const int64_t* __restrict__ pos,
     const float* __restrict__ inv_freq, T* __restrict__ q, T* __restrict__ k, T* __restrict__ v, int tokens, int hq,
-    int hkv, float eps) {
+    int hkv, float eps, int unit, int rot_lanes) {
   constexpr int EPL = D / 32;
   const int lane = threadIdx.x & 31;
   const int heads = hq + 2 * hkv;
@@ -270,8 +274,8 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
     const float r = rsqrtf(ss / (float)D + eps);
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
-      float n = round_to<T>(xv[e] * r);
-      y[e] = round_to<T>(to_f(wt[lane * EPL + e]) * n);
+      const float wv = to_f(wt[lane * EPL + e]);
+      y[e] = unit ? round_to<T>(xv[e] * r * (1.f + wv)) : round_to<T>(wv * round_to<T>(xv[e] * r));
     }
   } else {
 #pragma unroll
@@ -279,15 +283,23 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
   }
   const float p = (float)pos[t];
   T* dst = is_q ? q + ((size_t)t * hq + h) * D + lane * EPL : k + ((size_t)t * hkv + (h - hq)) * D + lane * EPL;
-  const bool low = lane < 16;
+  // rotary over the first rot_lanes * EPL dims; the rotate-half partner of an
+  // element sits half_mask lanes away; the remaining dims pass through
+  const int half_mask = rot_lanes >> 1;
+  const bool rotary = lane < rot_lanes;
+  const bool low = (lane & half_mask) == 0;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
-    const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
-    const int fi = (lane & 15) * EPL + e;  // frequency index i mod D/2
-    float s, c;
-    sincosf(p * inv_freq[fi], &s, &c);
-    const float rot = low ? -partner : partner;
-    dst[e] = from_f<T>(y[e] * c + rot * s);
+    const float partner = __shfl_xor_sync(0xffffffffu, y[e], half_mask);
+    if (rotary) {
+      const int fi = (lane & (half_mask - 1)) * EPL + e;  // frequency index
+      float s, c;
+      sincosf(p * inv_freq[fi], &s, &c);
+      const float rot = low ? -partner : partner;
+      dst[e] = from_f<T>(y[e] * c + rot * s);
+    } else {
+      dst[e] = from_f<T>(y[e]);
+    }
   }
 }
 
@@ -296,7 +308,7 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
     const T* __restrict__ dq, const T* __restrict__ dk, const T* __restrict__ dv, const T* __restrict__ qkv,
     const T* __restrict__ qw, const T* __restrict__ kw, const int64_t* __restrict__ pos,
     const float* __restrict__ inv_freq, T* __restrict__ dqkv, float* __restrict__ dqw_part,
-    float* __restrict__ dkw_part, int tokens, int hq, int hkv, float eps, int items_per_block) {
+    float* __restrict__ dkw_part, int tokens, int hq, int hkv, float eps, int items_per_block, int unit, int rot_lanes) {
   constexpr int EPL = D / 32;
   __shared__ float red_q[kWarps][D];
   __shared__ float red_k[kWarps][D];
@@ -323,17 +335,23 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
     const T* g = is_q ? dq + ((size_t)t * hq + h) * D + lane * EPL : dk + ((size_t)t * hkv + (h - hq)) * D + lane * EPL;
     const T* src = qkv + (size_t)t * heads * D + (size_t)h * D + lane * EPL;
     const float p = (float)pos[t];
-    const bool low = lane < 16;
+    const int half_mask = rot_lanes >> 1;
+    const bool rotary = lane < rot_lanes;
+    const bool low = (lane & half_mask) == 0;
     float dy[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
       const float go = to_f(g[e]);
-      const float partner = __shfl_xor_sync(0xffffffffu, go, 16);
-      const int fi = (lane & 15) * EPL + e;
-      float s, c;
-      sincosf(p * inv_freq[fi], &s, &c);
-      // d/dy_i of sum_j go_j * (y_j c_j + rot(y)_j s_j)
-      dy[e] = go * c + (low ? partner : -partner) * s;
+      const float partner = __shfl_xor_sync(0xffffffffu, go, half_mask);
+      if (rotary) {
+        const int fi = (lane & (half_mask - 1)) * EPL + e;
+        float s, c;
+        sincosf(p * inv_freq[fi], &s, &c);
+        // d/dy_i of sum_j go_j * (y_j c_j + rot(y)_j s_j)
+        dy[e] = go * c + (low ? partner : -partner) * s;
+      } else {
+        dy[e] = go;
+      }
     }
     const T* wt = is_q ? qw : kw;
     if (wt == nullptr) {
@@ -355,7 +373,7 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
       const float n = xv[e] * r;
-      dn[e] = dy[e] * to_f(wt[lane * EPL + e]);
+      dn[e] = dy[e] * (to_f(wt[lane * EPL + e]) + (unit ? 1.f : 0.f));
       dot += dn[e] * n;
       if (is_q) aq[e] += dy[e] * n; else ak[e] += dy[e] * n;
     }
@@ -450,7 +468,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ sorted_ids, con
 }  // namespace
 
 // =================================================================== host API
-std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps) {
+std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, bool unit) {
   check_cuda(x, "x");
   check_cuda(w, "w");
   TS_CHECK(x.dim() == 2 && w.dim() == 1 && w.size(0) == x.size(1), "rms_norm_fwd shapes");
@@ -462,10 +480,10 @@ std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, d
   const int H = x.size(1);
   if (x.scalar_type() == at::kBFloat16) {
     TS_CHECK(H % 8 == 0, "row width must be a multiple of 8");
-    rms_fwd_dispatch<__nv_bfloat16>(x, w, y, rstd, (float)eps);
+    rms_fwd_dispatch<__nv_bfloat16>(x, w, y, rstd, (float)eps, unit ? 1 : 0);
   } else if (x.scalar_type() == at::kFloat) {
     TS_CHECK(H % 4 == 0, "row width must be a multiple of 4");
-    rms_fwd_dispatch<float>(x, w, y, rstd, (float)eps);
+    rms_fwd_dispatch<float>(x, w, y, rstd, (float)eps, unit ? 1 : 0);
   } else {
     TS_CHECK(false, "rms_norm_fwd: unsupported dtype");
   }
@@ -474,7 +492,7 @@ std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, d
 }
 
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                     const at::Tensor& rstd) {
+                                     const at::Tensor& rstd, bool unit) {
   check_cuda(dy, "dy");
   check_cuda(x, "x");
   const c10::cuda::CUDAGuard guard(x.device());
@@ -484,11 +502,11 @@ std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, 
   if (x.size(0) == 0) return {dx, at::zeros({H}, x.options().dtype(at::kFloat))};
   if (x.scalar_type() == at::kBFloat16) {
     TS_CHECK(H % 8 == 0, "row width must be a multiple of 8");
-    rms_dx_dispatch<__nv_bfloat16>(dy, x, w, rstd, dx);
+    rms_dx_dispatch<__nv_bfloat16>(dy, x, w, rstd, dx, unit ? 1.f : 0.f);
     dw = column_weight_grad<__nv_bfloat16>(dy, x, rstd);
   } else if (x.scalar_type() == at::kFloat) {
     TS_CHECK(H % 4 == 0, "row width must be a multiple of 4");
-    rms_dx_dispatch<float>(dy, x, w, rstd, dx);
+    rms_dx_dispatch<float>(dy, x, w, rstd, dx, unit ? 1.f : 0.f);
     dw = column_weight_grad<float>(dy, x, rstd);
   } else {
     TS_CHECK(false, "rms_norm_bwd: unsupported dtype");
@@ -500,14 +518,15 @@ std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, 
 template <typename T, int D>
 static void qk_fwd_launch(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
                           const c10::optional<at::Tensor>& kw, const at::Tensor& pos, const at::Tensor& inv_freq,
-                          at::Tensor& q, at::Tensor& k, at::Tensor& v, int hq, int hkv, float eps) {
+                          at::Tensor& q, at::Tensor& k, at::Tensor& v, int hq, int hkv, float eps, int unit,
+                          int rot_lanes) {
   const int tokens = qkv.size(0);
   const long long items = (long long)tokens * (hq + 2 * hkv);
   const int blocks = (int)((items + kWarps - 1) / kWarps);
   qk_norm_rope_fwd_kernel<T, D><<<blocks, kWarps * 32, 0, stream()>>>(
       (const T*)qkv.data_ptr(), qw ? (const T*)qw->data_ptr() : nullptr, kw ? (const T*)kw->data_ptr() : nullptr,
       pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(), (T*)q.data_ptr(), (T*)k.data_ptr(), (T*)v.data_ptr(),
-      tokens, hq, hkv, eps);
+      tokens, hq, hkv, eps, unit, rot_lanes);
 }
 
 #define TS_DISPATCH_HEAD(D, FN, T, ...)                                \
@@ -521,8 +540,13 @@ static void qk_fwd_launch(const at::Tensor& qkv, const c10::optional<at::Tensor>
 std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
                                          const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                          const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d,
-                                         double eps) {
+                                         double eps, bool unit) {
   check_cuda(qkv, "qkv");
+  const int epl = (int)d / 32;
+  const int rot_lanes = (int)(2 * inv_freq.numel()) / epl;
+  TS_CHECK(2 * inv_freq.numel() <= d && (2 * inv_freq.numel()) % (2 * epl) == 0 && rot_lanes >= 2 &&
+               (rot_lanes & (rot_lanes - 1)) == 0,
+           "rotary dims must be a power-of-two multiple of 2 * head_dim / 32");
   TS_CHECK(qkv.dim() == 2 && qkv.size(1) == (hq + 2 * hkv) * d, "qkv shape");
   TS_CHECK(pos.scalar_type() == at::kLong && inv_freq.scalar_type() == at::kFloat, "pos/inv_freq dtype");
   const c10::cuda::CUDAGuard guard(qkv.device());
@@ -532,9 +556,11 @@ std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optio
   auto v = at::empty({t, hkv, d}, qkv.options());
   if (t == 0) return {q, k, v};
   if (qkv.scalar_type() == at::kBFloat16) {
-    TS_DISPATCH_HEAD(d, qk_fwd_launch, __nv_bfloat16, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps);
+    TS_DISPATCH_HEAD(d, qk_fwd_launch, __nv_bfloat16, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps,
+                     unit ? 1 : 0, rot_lanes);
   } else if (qkv.scalar_type() == at::kFloat) {
-    TS_DISPATCH_HEAD(d, qk_fwd_launch, float, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps);
+    TS_DISPATCH_HEAD(d, qk_fwd_launch, float, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps, unit ? 1 : 0,
+                     rot_lanes);
   } else {
     TS_CHECK(false, "qk_norm_rope_fwd: unsupported dtype");
   }
@@ -546,12 +572,13 @@ template <typename T, int D>
 static void qk_bwd_launch(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv, const at::Tensor& qkv,
                           const c10::optional<at::Tensor>& qw, const c10::optional<at::Tensor>& kw,
                           const at::Tensor& pos, const at::Tensor& inv_freq, at::Tensor& dqkv, at::Tensor& pq,
-                          at::Tensor& pk, int hq, int hkv, float eps, int blocks, int per_block) {
+                          at::Tensor& pk, int hq, int hkv, float eps, int blocks, int per_block, int unit,
+                          int rot_lanes) {
   qk_norm_rope_bwd_kernel<T, D><<<blocks, kWarps * 32, 0, stream()>>>(
       (const T*)dq.data_ptr(), (const T*)dk.data_ptr(), (const T*)dv.data_ptr(), (const T*)qkv.data_ptr(),
       qw ? (const T*)qw->data_ptr() : nullptr, kw ? (const T*)kw->data_ptr() : nullptr, pos.data_ptr<int64_t>(),
       inv_freq.data_ptr<float>(), (T*)dqkv.data_ptr(), pq.data_ptr<float>(), pk.data_ptr<float>(), qkv.size(0), hq,
-      hkv, eps, per_block);
+      hkv, eps, per_block, unit, rot_lanes);
 }
 
 std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk,
@@ -559,8 +586,9 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
                                                         const c10::optional<at::Tensor>& qw,
                                                         const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
-                                                        int64_t d, double eps) {
+                                                        int64_t d, double eps, bool unit) {
   check_cuda(qkv, "qkv");
+  const int rot_lanes = (int)(2 * inv_freq.numel()) / ((int)d / 32);
   check_cuda(dq, "dq");
   check_cuda(dk, "dk");
   check_cuda(dv, "dv");
@@ -576,10 +604,10 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
   if (t > 0) {
     if (qkv.scalar_type() == at::kBFloat16) {
       TS_DISPATCH_HEAD(d, qk_bwd_launch, __nv_bfloat16, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pq, pk, hq, hkv,
-                       (float)eps, blocks, per_block);
+                       (float)eps, blocks, per_block, unit ? 1 : 0, rot_lanes);
     } else if (qkv.scalar_type() == at::kFloat) {
       TS_DISPATCH_HEAD(d, qk_bwd_launch, float, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pq, pk, hq, hkv,
-                       (float)eps, blocks, per_block);
+                       (float)eps, blocks, per_block, unit ? 1 : 0, rot_lanes);
     } else {
       TS_CHECK(false, "qk_norm_rope_bwd: unsupported dtype");
     }
@@ -707,7 +735,7 @@ int noalloc_fail(int code, const char* msg) {
 
 template <typename T, int V>
 void noalloc_dx(const T* dy, const T* x, const T* w, const float* rstd, T* dx, int rows, int H, cudaStream_t st) {
-  rms_bwd_dx_kernel<T, V><<<(rows + kWarps - 1) / kWarps, kWarps * 32, 0, st>>>(dy, x, w, rstd, dx, rows, H);
+  rms_bwd_dx_kernel<T, V><<<(rows + kWarps - 1) / kWarps, kWarps * 32, 0, st>>>(dy, x, w, rstd, dx, rows, H, 0.f);
 }
 
 template <typename T>

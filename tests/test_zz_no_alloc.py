@@ -40,8 +40,8 @@ def test_noalloc_rms_norm_backward_matches_regular_entry_point():
         x = torch.randn(rows, cols, device="cuda", dtype=torch.bfloat16)
         w = (1 + 0.1 * torch.randn(cols, device="cuda")).to(torch.bfloat16)
         dy = torch.randn(rows, cols, device="cuda", dtype=torch.bfloat16)
-        _, rstd = native().rms_norm_fwd(x, w, 1e-6)
-        dx_ref, dw_ref = native().rms_norm_bwd(dy, x, w, rstd)
+        _, rstd = native().rms_norm_fwd(x, w, 1e-6, False)
+        dx_ref, dw_ref = native().rms_norm_bwd(dy, x, w, rstd, False)
         dx = torch.empty_like(x)
         dw = torch.empty(cols, device="cuda", dtype=torch.float32)
         stream = torch.cuda.current_stream().cuda_stream

@@ -47,6 +47,8 @@ class ModelSpec:
     qk_norm: bool
     kinds: tuple[str, ...]
     attn_gate: bool = False  # hybrid full-attention layers gate their output
+    rotary_dim: int = 0  # dims of each head that rotate (0 = all)
+    unit_norm: bool = False  # zero-centred (1 + w) RMSNorms (Qwen3.5)
 
     @property
     def attention_layers(self) -> list[int]:
@@ -74,13 +76,18 @@ def spec_of(model: torch.nn.Module) -> ModelSpec:
     layers = model.model.layers
     kinds = []
     for i, layer in enumerate(layers):
-        kind = getattr(layer, "layer_kind", None)
+        kind = getattr(layer, "layer_kind", None) or getattr(layer, "layer_type", None)
         if kind is None:
             types = _cfg_get(cfg, "layer_types", None)
             kind = types[i] if types else "full_attention"
         kinds.append(kind)
     first_attn = next((layers[i] for i, k in enumerate(kinds) if k == "full_attention"), None)
     qk_norm = bool(first_attn is not None and getattr(first_attn.self_attn, "q_norm", None) is not None)
+    attn_gate = False
+    if first_attn is not None:
+        qw = _weight(first_attn.self_attn.q_proj)
+        attn_gate = qw.shape[0] == 2 * heads * head_dim
+    factor = float(_cfg_get(cfg, "partial_rotary_factor", 1.0))
     return ModelSpec(
         n_layers=len(layers),
         hidden=hidden,
@@ -93,8 +100,15 @@ def spec_of(model: torch.nn.Module) -> ModelSpec:
         tied=bool(_cfg_get(cfg, "tie_word_embeddings", False)),
         qk_norm=qk_norm,
         kinds=tuple(kinds),
-        attn_gate=bool(_cfg_get(cfg, "attn_output_gate", False)),
+        attn_gate=attn_gate,
+        rotary_dim=int(head_dim * factor),
+        unit_norm=_is_unit(model.model.norm),
     )
+
+
+def _is_unit(norm_module) -> bool:
+    return bool(getattr(norm_module, "unit_offset", False)) or type(norm_module).__name__ in (
+        "Qwen3_5RMSNorm", "Qwen3NextRMSNorm")
 
 
 @dataclass
@@ -136,16 +150,19 @@ class Executor:
     def inv_freq(self, device: torch.device) -> torch.Tensor:
         t = self._inv_freq.get(device)
         if t is None:
-            t = rope_inv_freq(self.spec.head_dim, self.spec.rope_theta, device)
+            t = rope_inv_freq(self.spec.rotary_dim or self.spec.head_dim, self.spec.rope_theta, device)
             self._inv_freq[device] = t
         return t
 
     def embed(self, ids: torch.Tensor) -> torch.Tensor:
         return embedding(ids, self.model.model.embed_tokens.weight)
 
+    def norm(self, mod, x: torch.Tensor) -> torch.Tensor:
+        eps = getattr(mod, "variance_epsilon", None) or getattr(mod, "eps", None) or self.spec.eps
+        return rms_norm(x, mod.weight, eps, unit_offset=_is_unit(mod))
+
     def final_norm(self, h: torch.Tensor) -> torch.Tensor:
-        n = self.model.model.norm
-        return rms_norm(h, n.weight, getattr(n, "variance_epsilon", self.spec.eps))
+        return self.norm(self.model.model.norm, h)
 
     def head_weight(self) -> torch.Tensor:
         return _weight(self.model.lm_head)
@@ -164,7 +181,7 @@ class Executor:
         layer = self.model.model.layers[i]
         sa = layer.self_attn
         hq, hkv, d = spec.n_heads, spec.n_kv, spec.head_dim
-        x = rms_norm(h, layer.input_layernorm.weight, spec.eps)
+        x = self.norm(layer.input_layernorm, h)
         if spec.attn_gate:
             # Hybrid gated attention: q_proj emits [q, gate] per head.
             qg = self.proj(x, [sa.q_proj])
@@ -180,7 +197,7 @@ class Executor:
         kn = getattr(sa, "k_norm", None)
         q, k, v = qk_norm_rope(
             qkv, None if qn is None else qn.weight, None if kn is None else kn.weight,
-            pos, self.inv_freq(h.device), hq, hkv, d, spec.eps,
+            pos, self.inv_freq(h.device), hq, hkv, d, spec.eps, unit_offset=qn is not None and _is_unit(qn),
         )
         scale = 1.0 / math.sqrt(d)
         outs = []
@@ -204,7 +221,7 @@ class Executor:
 
     def mlp(self, layer, h: torch.Tensor) -> torch.Tensor:
         mlp = layer.mlp
-        x = rms_norm(h, layer.post_attention_layernorm.weight, self.spec.eps)
+        x = self.norm(layer.post_attention_layernorm, h)
         gu = self.proj(x, [mlp.gate_proj, mlp.up_proj])
         return h + self.proj(swiglu(gu), [mlp.down_proj])
 

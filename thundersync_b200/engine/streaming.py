@@ -39,7 +39,7 @@ import torch
 from thundersync_b200.engine.boundary import Boundary
 from thundersync_b200.engine.layers import Executor, Segment, executor_for
 from thundersync_b200.ops.logprob import lm_head_logprob
-from thundersync_b200.ops.sink import GradSink, ParamArena, grad_sink
+from thundersync_b200.ops.sink import GradSink, ParamArena, grad_sink, install_redirect_hooks
 
 __all__ = ["StreamingRun", "STREAM_ATTENTION_NAME", "register_stream_attention", "arena_for", "live_runs"]
 
@@ -240,6 +240,7 @@ class StreamingRun:
         self._traj_group: dict[int, int] = {}
         self._shared: list[_SharedNode] = []
         self._trainable = [p for p in model.parameters() if p.requires_grad]
+        install_redirect_hooks(self._trainable)
         self._versions = {id(p): p._version for p in self._trainable}
         self._capture_source: Any = None
         self._param_adjoint_staged: dict[Any, list[tuple[torch.Tensor, torch.Tensor]]] = {}

@@ -16,17 +16,19 @@ from thundersync_b200.ops import sink as _sink
 from thundersync_b200.ops._ext import native
 
 
-def _ref_forward(x2: torch.Tensor, w: torch.Tensor, eps: float):
+def _ref_forward(x2: torch.Tensor, w: torch.Tensor, eps: float, unit: bool = False):
     xf = x2.float()
     rstd = torch.rsqrt(xf.pow(2).mean(-1) + eps)
+    if unit:
+        return (xf * rstd[:, None] * (1.0 + w.float())).to(x2.dtype), rstd
     n = (xf * rstd[:, None]).to(x2.dtype)
     y = (w.float() * n.float()).to(x2.dtype)
     return y, rstd
 
 
-def _ref_backward(dy2, x2, w, rstd):
+def _ref_backward(dy2, x2, w, rstd, unit: bool = False):
     n = x2.float() * rstd[:, None]
-    dn = dy2.float() * w.float()
+    dn = dy2.float() * (w.float() + 1.0 if unit else w.float())
     dx = rstd[:, None] * (dn - n * (dn * n).mean(-1, keepdim=True))
     dw = (dy2.float() * n).sum(0)
     return dx.to(x2.dtype), dw
@@ -34,17 +36,18 @@ def _ref_backward(dy2, x2, w, rstd):
 
 class _RMSNorm(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w, eps):
+    def forward(ctx, x, w, eps, unit):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1])
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         if x2.is_cuda:
-            y, rstd = native().rms_norm_fwd(x2, w.contiguous(), float(eps))
+            y, rstd = native().rms_norm_fwd(x2, w.contiguous(), float(eps), bool(unit))
         else:
-            y, rstd = _ref_forward(x2, w, eps)
+            y, rstd = _ref_forward(x2, w, eps, unit)
         ctx.save_for_backward(x2, w, rstd)
         ctx.shape = shape
+        ctx.unit = unit
         return y.view(shape)
 
     @staticmethod
@@ -54,9 +57,9 @@ class _RMSNorm(torch.autograd.Function):
         if not dy2.is_contiguous():
             dy2 = dy2.contiguous()
         if dy2.is_cuda:
-            dx, dw = native().rms_norm_bwd(dy2, x2, w.contiguous(), rstd)
+            dx, dw = native().rms_norm_bwd(dy2, x2, w.contiguous(), rstd, bool(ctx.unit))
         else:
-            dx, dw = _ref_backward(dy2, x2, w, rstd)
+            dx, dw = _ref_backward(dy2, x2, w, rstd, ctx.unit)
         dw_out = None
         if ctx.needs_input_grad[1]:
             s = _sink.active()
@@ -64,15 +67,20 @@ class _RMSNorm(torch.autograd.Function):
                 s.add_(w, dw)
             else:
                 dw_out = dw.to(w.dtype)
-        return dx.view(ctx.shape), dw_out, None
+        return dx.view(ctx.shape), dw_out, None, None
 
 
-def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    return _RMSNorm.apply(x, weight, eps)
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, unit_offset: bool = False) -> torch.Tensor:
+    """``unit_offset``: the weight is stored zero-centred and applied as ``1 + w``
+    with a single fp32 rounding (Qwen3.5 convention)."""
+    return _RMSNorm.apply(x, weight, eps, unit_offset)
 
 
-def rms_norm_reference(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+def rms_norm_reference(x: torch.Tensor, weight: torch.Tensor, eps: float, unit_offset: bool = False) -> torch.Tensor:
     """Differentiable plain-torch oracle (fp32 math, same roundings)."""
     xf = x.float()
-    n = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
+    r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    if unit_offset:
+        return (xf * r * (1.0 + weight.float())).to(x.dtype)
+    n = (xf * r).to(x.dtype)
     return (weight.float() * n.float()).to(x.dtype)

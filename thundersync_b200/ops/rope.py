@@ -17,10 +17,10 @@ from thundersync_b200.ops._ext import native
 from thundersync_b200.ops.norm import rms_norm_reference
 
 
-def rope_inv_freq(head_dim: int, theta: float, device=None) -> torch.Tensor:
-    """fp32 inverse frequencies ``1 / theta^(2i/d)``, i < d/2 (Qwen3/HF convention)."""
-    idx = torch.arange(0, head_dim, 2, dtype=torch.int64, device=device).float()
-    return 1.0 / (theta ** (idx / head_dim))
+def rope_inv_freq(rotary_dim: int, theta: float, device=None) -> torch.Tensor:
+    """fp32 inverse frequencies ``1 / theta^(2i/r)``, i < r/2, r = rotary dims (HF convention)."""
+    idx = torch.arange(0, rotary_dim, 2, dtype=torch.int64, device=device).float()
+    return 1.0 / (theta ** (idx / rotary_dim))
 
 
 def _rotate_half(x):
@@ -28,42 +28,49 @@ def _rotate_half(x):
     return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
 
 
-def qk_norm_rope_reference(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps):
-    """Differentiable fp32 oracle of the fused op."""
+def qk_norm_rope_reference(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit_offset=False):
+    """Differentiable fp32 oracle of the fused op (rotary over the first 2*len(inv_freq) dims)."""
     t = qkv.shape[0]
     q = qkv[:, : hq * d].reshape(t, hq, d)
     k = qkv[:, hq * d : (hq + hkv) * d].reshape(t, hkv, d)
     v = qkv[:, (hq + hkv) * d :].reshape(t, hkv, d)
     if q_w is not None:
-        q = rms_norm_reference(q, q_w, eps)
-        k = rms_norm_reference(k, k_w, eps)
+        q = rms_norm_reference(q, q_w, eps, unit_offset)
+        k = rms_norm_reference(k, k_w, eps, unit_offset)
+    rd = 2 * inv_freq.shape[0]
     freqs = pos.float()[:, None] * inv_freq.float()[None, :]
     emb = torch.cat((freqs, freqs), dim=-1)
     cos, sin = emb.cos()[:, None, :], emb.sin()[:, None, :]
-    qo = (q.float() * cos + _rotate_half(q.float()) * sin).to(qkv.dtype)
-    ko = (k.float() * cos + _rotate_half(k.float()) * sin).to(qkv.dtype)
-    return qo, ko, v.contiguous()
+
+    def rot(x):
+        xr = x[..., :rd].float()
+        out = xr * cos + _rotate_half(xr) * sin
+        if rd == d:
+            return out.to(qkv.dtype)
+        return torch.cat((out, x[..., rd:].float()), -1).to(qkv.dtype)
+
+    return rot(q), rot(k), v.contiguous()
 
 
 class _QKNormRope(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps):
-        ctx.meta = (hq, hkv, d, eps)
+    def forward(ctx, qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit):
+        ctx.meta = (hq, hkv, d, eps, unit)
         ctx.has_norm = q_w is not None
         if qkv.is_cuda:
             q, k, v = native().qk_norm_rope_fwd(
-                qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(), hq, hkv, d, float(eps)
+                qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(), hq, hkv, d, float(eps), bool(unit)
             )
         else:
             with torch.no_grad():
-                q, k, v = qk_norm_rope_reference(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps)
+                q, k, v = qk_norm_rope_reference(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit)
         ctx.save_for_backward(qkv, q_w, k_w, pos, inv_freq)
         return q, k, v
 
     @staticmethod
     def backward(ctx, dq, dk, dv):
         qkv, q_w, k_w, pos, inv_freq = ctx.saved_tensors
-        hq, hkv, d, eps = ctx.meta
+        hq, hkv, d, eps, unit = ctx.meta
         t = qkv.shape[0]
         dq = torch.zeros(t, hq, d, dtype=qkv.dtype, device=qkv.device) if dq is None else dq.contiguous()
         dk = torch.zeros(t, hkv, d, dtype=qkv.dtype, device=qkv.device) if dk is None else dk.contiguous()
@@ -71,14 +78,14 @@ class _QKNormRope(torch.autograd.Function):
         if qkv.is_cuda:
             dqkv, dqw, dkw = native().qk_norm_rope_bwd(
                 dq, dk, dv, qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(),
-                hq, hkv, d, float(eps),
+                hq, hkv, d, float(eps), bool(unit),
             )
         else:
             with torch.enable_grad():
                 qkv_ = qkv.detach().requires_grad_(True)
                 qw_ = None if q_w is None else q_w.detach().requires_grad_(True)
                 kw_ = None if k_w is None else k_w.detach().requires_grad_(True)
-                outs = qk_norm_rope_reference(qkv_, qw_, kw_, pos, inv_freq, hq, hkv, d, eps)
+                outs = qk_norm_rope_reference(qkv_, qw_, kw_, pos, inv_freq, hq, hkv, d, eps, unit)
                 ins = [qkv_] + ([qw_, kw_] if qw_ is not None else [])
                 grads = torch.autograd.grad(outs, ins, (dq, dk, dv), allow_unused=True)
             dqkv = grads[0]
@@ -96,8 +103,10 @@ class _QKNormRope(torch.autograd.Function):
                     gq = g.to(w.dtype)
                 else:
                     gk = g.to(w.dtype)
-        return dqkv, gq, gk, None, None, None, None, None, None
+        return dqkv, gq, gk, None, None, None, None, None, None, None
 
 
-def qk_norm_rope(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps):
-    return _QKNormRope.apply(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps)
+def qk_norm_rope(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit_offset: bool = False):
+    """Rotary over the first ``2 * len(inv_freq)`` dims of each head (all dims for Qwen3,
+    a quarter for Qwen3.5's partial rotary); ``unit_offset`` selects (1 + w) norms."""
+    return _QKNormRope.apply(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit_offset)

@@ -38,6 +38,34 @@ def grad_sink(sink: "GradSink | None"):
         _ACTIVE = prev
 
 
+def _redirect_hook(p: torch.Tensor) -> None:
+    s = _ACTIVE
+    if s is None or p.grad is None or not s.owns(p):
+        return
+    g = p.grad
+    p.grad = None
+    s.add_(p, g)
+
+
+def install_redirect_hooks(params) -> None:
+    """Send gradients that autograd accumulates into ``param.grad`` to the active sink.
+
+    Native ops deposit weight gradients into the sink themselves; parameters
+    consumed by plain torch ops (decay logits, conv weights returned through
+    autograd, adapters) reach ``AccumulateGrad`` instead. This hook moves such
+    a contribution into the sink (with the sink's scale) the moment it lands.
+    With no sink active it does nothing.
+    """
+    for p in params:
+        if getattr(p, "_ts_redirect", False):
+            continue
+        p.register_post_accumulate_grad_hook(_redirect_hook)
+        try:
+            p._ts_redirect = True
+        except Exception:
+            pass
+
+
 class ParamArena:
     """All trainable parameters re-homed into one contiguous flat buffer.
 
