@@ -20,6 +20,16 @@ def _rms(x, w, eps):
     return (w.float() * n.float()).to(x.dtype)
 
 
+def _lin(x, mod):
+    """``mod(x)`` for a plain or LoRA (PEFT-layout) linear, in plain torch."""
+    base = getattr(mod, "base_layer", None)
+    if base is None:
+        return F.linear(x, mod.weight)
+    a, b = mod.lora_A["default"].weight, mod.lora_B["default"].weight
+    low = F.linear(F.linear(x.to(a.dtype), a), b) * mod.scaling["default"]
+    return (F.linear(x, base.weight).to(low.dtype) + low).to(x.dtype)
+
+
 def _rope(x, pos, theta):
     d = x.shape[-1]
     inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.int64).float() / d))
@@ -42,9 +52,9 @@ def hidden_states(model, ids: torch.Tensor) -> torch.Tensor:
     for layer in model.model.layers:
         sa = layer.self_attn
         x = _rms(h, layer.input_layernorm.weight, eps)
-        q = F.linear(x, sa.q_proj.weight).view(t, hq, d)
-        k = F.linear(x, sa.k_proj.weight).view(t, hkv, d)
-        v = F.linear(x, sa.v_proj.weight).view(t, hkv, d)
+        q = _lin(x, sa.q_proj).view(t, hq, d)
+        k = _lin(x, sa.k_proj).view(t, hkv, d)
+        v = _lin(x, sa.v_proj).view(t, hkv, d)
         if sa.q_norm is not None:
             q = _rms(q, sa.q_norm.weight, eps)
             k = _rms(k, sa.k_norm.weight, eps)
@@ -55,11 +65,11 @@ def hidden_states(model, ids: torch.Tensor) -> torch.Tensor:
         s = q.transpose(0, 1).float() @ kf.transpose(1, 2) / math.sqrt(d)
         s = s.masked_fill(~mask, float("-inf"))
         o = (torch.softmax(s, -1) @ vf).transpose(0, 1).reshape(t, hq * d).to(h.dtype)
-        h = h + F.linear(o, sa.o_proj.weight)
+        h = h + _lin(o, sa.o_proj)
         x = _rms(h, layer.post_attention_layernorm.weight, eps)
-        gt, up = F.linear(x, layer.mlp.gate_proj.weight), F.linear(x, layer.mlp.up_proj.weight)
+        gt, up = _lin(x, layer.mlp.gate_proj), _lin(x, layer.mlp.up_proj)
         a = (F.silu(gt.float()) * up.float()).to(h.dtype)
-        h = h + F.linear(a, layer.mlp.down_proj.weight)
+        h = h + _lin(a, layer.mlp.down_proj)
     return _rms(h, model.model.norm.weight, eps)
 
 
