@@ -217,9 +217,28 @@ def build_reference(args, device):
         os.environ.setdefault("LOCAL_RANK", "0")
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", str(29500 + os.getpid() % 1000))
+    # Statistic placement as the reference's own builder does it for
+    # device-resident sources with statistic_device "auto"
+    # (grpo/runtime.py statistic_placement): as many open groups' fp32 (G1, G2)
+    # pairs on the device as its device_statistic_slots finds room for, the
+    # rest on the host. Host-only statistics for 8 open groups need ~109 GB per
+    # rank, which two ranks on one box do not have.
+    from thundersync.grpo.device_statistics import device_statistic_slots
+
+    trainable = [p for p in model.parameters() if p.requires_grad]
+    src = sum(p.numel() * p.element_size() for p in trainable)
+    slots = device_statistic_slots(
+        device_total_bytes=int(torch.cuda.get_device_properties(device).total_memory),
+        parameter_bytes=sum(p.numel() * p.element_size() for p in model.parameters())
+        + sum(b.numel() * b.element_size() for b in model.buffers()),
+        gradient_bytes=src, optimizer_state_bytes=2 * src, source_bytes=src, device_held_sources=1,
+        statistic_pair_bytes=2 * sum(p.numel() * 4 for p in trainable), reserve_bytes=0,
+        open_groups=args.groups_per_rank,
+    )
     trainer = DataParallelThunderSync.init_from_env(
         model, opt, run_factory=factory, grad_clip=1.0,
         source_offload_device="cpu", source_offload_mode="device_resident",
+        statistic_device=device, device_statistic_slots=slots,
     )
     trainer.configure_binary_rewards()
     return model, trainer

@@ -50,6 +50,7 @@ at::Tensor tc_status(const at::Tensor& like);
 std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                     const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale);
 void register_ipc(pybind11::module& m);
+void register_pinned(pybind11::module& m);
 std::vector<at::Tensor> conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& tail);
 std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& dtail_out, const at::Tensor& x,
                                         const at::Tensor& w, const at::Tensor& tail);
@@ -63,6 +64,7 @@ std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& dfinal
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "thundersync_b200 native sm_100a kernels";
   ts::register_ipc(m);
+  ts::register_pinned(m);
   m.def("rms_norm_fwd", &ts::rms_norm_fwd);
   m.def("rms_norm_bwd", &ts::rms_norm_bwd);
   m.def("qk_norm_rope_fwd", &ts::qk_norm_rope_fwd);

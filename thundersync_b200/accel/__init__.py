@@ -1,1 +1,1 @@
-"""accel"""
+"""Kernel-facing helpers with the reference's ``accel`` names (see each module)."""

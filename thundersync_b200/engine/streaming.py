@@ -536,6 +536,11 @@ class StreamingRun:
             self._forward_turns(this)
             pending = rest
 
+    def trajectory_tokens(self, traj_id: int) -> int:
+        """Tokens of a trajectory's own branch (its turns, not the shared prompt)."""
+        t = self._trajs[traj_id]
+        return sum(len(tk) for tk, _ in t.turns)
+
     def forward_deferred_turns(self, traj_id: int) -> None:
         t = self._trajs[traj_id]
         if t.forwarded_turns < len(t.turns):

@@ -58,6 +58,7 @@ class _GroupAccum:
     g2: torch.Tensor | None = None  # or N in binary mode
     b1: list[torch.Tensor | None] = field(default_factory=list)
     b2: list[torch.Tensor | None] = field(default_factory=list)
+    slot: Any = None  # device statistic home, when the pool had one
     direct: bool = False
     direct_boundary: list[torch.Tensor | None] = field(default_factory=list)
     prepared: dict[int, Any] = field(default_factory=dict)
@@ -127,6 +128,13 @@ class RewardLinearBackward:
         self.combine_known_reward_sources = combine_known_reward_sources
         self.defer_group_close = defer_group_close
         self._binary = False
+        self._stat_slots = int(device_statistic_slots or 0)
+        from thundersync_b200.grpo.close_profiler import ClosePackProfiler
+
+        self._close_profiler = ClosePackProfiler.from_env()
+        self._profile_rank = int(__import__("os").environ.get("RANK", "0"))
+        self._profile_step = 0
+        self._stat_pool = None
         self._groups: dict[int, _GroupAccum] = {}
         self._traj_group: dict[int, int] = {}
         self._main: torch.Tensor | None = None
@@ -154,6 +162,10 @@ class RewardLinearBackward:
 
     def set_diagnostic_scope(self, **scope: Any) -> None:
         self._scope.update(scope)
+        if "rank" in scope:
+            self._profile_rank = int(scope["rank"])
+        if "step" in scope:
+            self._profile_step = int(scope["step"])
 
     # ------------------------------------------------------------ buffers
     def _main_grad(self) -> torch.Tensor:
@@ -178,6 +190,26 @@ class RewardLinearBackward:
 
     def _stat(self) -> torch.Tensor:
         return torch.zeros(self.arena.numel, dtype=torch.float32, device=self.statistic_device)
+
+    def _stat_pair(self, acc) -> tuple[torch.Tensor, torch.Tensor]:
+        """(reward-weighted, unit) statistics of a group: a preallocated device home when one is free."""
+        if self._stat_slots and self.statistic_device.type == "cuda":
+            if self._stat_pool is None:
+                from thundersync_b200.grpo.device_statistics import DeviceStatisticPool
+
+                self._stat_pool = DeviceStatisticPool(self.arena.numel, torch.float32, slots=self._stat_slots,
+                                                      device=self.statistic_device)
+            slot = self._stat_pool.acquire(acc.gid)
+            if slot is not None:
+                acc.slot = slot
+                return slot.reward, slot.unit
+        return self._stat(), self._stat()
+
+    def _drop_stats(self, acc) -> None:
+        acc.g1 = acc.g2 = None
+        if acc.slot is not None:
+            self._stat_pool.release(acc.slot)
+            acc.slot = None
 
     # ------------------------------------------------------------ groups
     def open_group(self, group_id: int, prompt: list[int], traj_ids: list[int]) -> None:
@@ -222,9 +254,21 @@ class RewardLinearBackward:
             if reward is None or not math.isfinite(float(reward)):
                 raise ValueError(f"trajectory {tid} closed without a finite reward")
             norm.append((int(tid), float(reward), w))
-        for tid, reward, w in norm:
-            self._record(tid, reward)
-            self._differentiate(tid, reward, w)
+        prof = self._close_profiler
+        window = False
+        if prof is not None:
+            toks = [self.run.trajectory_tokens(t) for t, _, _ in norm]
+            if prof.selects(rank=self._profile_rank, step=self._profile_step, branch_tokens=toks):
+                prof.start(rank=self._profile_rank, step=self._profile_step,
+                           trajectory_ids=[t for t, _, _ in norm], branch_tokens=toks)
+                window = True
+        try:
+            for tid, reward, w in norm:
+                self._record(tid, reward)
+                self._differentiate(tid, reward, w)
+        finally:
+            if window:
+                prof.stop()
 
     def prepare_trajectory(self, traj_id: int, token_weights=None) -> None:
         self.prepare_trajectories([(traj_id, token_weights)] if token_weights is not None else [traj_id])
@@ -335,7 +379,7 @@ class RewardLinearBackward:
         if self._binary and self.statistic_device == self.run.device:
             # The sink is the statistic itself: P for r = 1, N for r = 0.
             if acc.g2 is None:
-                acc.g1, acc.g2 = self._stat(), self._stat()
+                acc.g1, acc.g2 = self._stat_pair(acc)
             target = acc.g1 if reward == 1.0 else acc.g2
             bnd = self._backward_source(tid, w, GradSink(self.arena, target))
             self._fold_boundary(acc, reward, bnd)
@@ -354,7 +398,7 @@ class RewardLinearBackward:
     def _fold(self, acc: _GroupAccum, tid: int, reward: float, src: torch.Tensor, bnd) -> None:
         t0 = time.perf_counter()
         if acc.g2 is None:
-            acc.g1, acc.g2 = self._stat(), self._stat()
+            acc.g1, acc.g2 = self._stat_pair(acc)
         src_dev = src if src.device == acc.g2.device else src.to(acc.g2.device)
         if self._binary:
             (acc.g1 if reward == 1.0 else acc.g2).add_(src_dev)
@@ -478,7 +522,7 @@ class RewardLinearBackward:
             if d is not None:
                 out = d if out is None else out + d
             adjoints.append(out)
-        acc.g1 = acc.g2 = None
+        self._drop_stats(acc)
         acc.b1 = acc.b2 = []
         acc.direct_boundary = []
         boundary = self.run._groups[group_id].boundary
@@ -550,7 +594,7 @@ class RewardLinearBackward:
     def abort(self) -> None:
         self._aborted = True
         for gid, acc in self._groups.items():
-            acc.g1 = acc.g2 = None
+            self._drop_stats(acc)
             acc.prepared.clear()
             self.run.free_group(gid)
             acc.done = True

@@ -76,4 +76,8 @@ class _LoRALinear(torch.autograd.Function):
 def lora_linear(x: torch.Tensor, mod: torch.nn.Module, adapter: str = "default") -> torch.Tensor:
     """``mod(x)`` for a PEFT-layout LoRA module (``base_layer`` + ``lora_A``/``lora_B``)."""
     w, a, b, s = lora_parts(mod, adapter)
+    if getattr(mod, "_thundersync_fused", False):  # merged-weight mode (accel.fused_lora)
+        from thundersync_b200.accel.fused_lora import FusedLoRALinear
+
+        return FusedLoRALinear.apply(x, w, a, b, s)
     return _LoRALinear.apply(x, w, a, b, s)
