@@ -264,6 +264,9 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--vocab", type=int, default=151936)
     ap.add_argument("--clocks-file", default=os.path.join(ROOT, "gpurun_out", "bench_clocks.csv"))
+    ap.add_argument("--profile-out", default=None,
+                    help="after the timed region, run one more step under torch.profiler and write the per-kernel "
+                         "CUDA time table to this file (rank 0; not part of any reported number)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("at least 3 warm-up steps are required")
@@ -300,7 +303,7 @@ def main() -> None:
             return
         raise
 
-    works = [make_step(rank, s, args) for s in range(args.warmup + args.steps)]
+    works = [make_step(rank, s, args) for s in range(args.warmup + args.steps + (1 if args.profile_out else 0))]
     from thundersync_b200.ops import _ext
 
     for s in range(args.warmup):
@@ -385,6 +388,17 @@ def main() -> None:
             out["impl"] = "reference"
             out["gpu_launches"] = 0
         print(json.dumps(out))
+    if args.profile_out:
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            run_step(trainer, works[-1], None)
+            torch.cuda.synchronize()
+        if rank == 0:
+            with open(args.profile_out, "w") as fh:
+                fh.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=45,
+                                                   max_name_column_width=100))
     if hasattr(trainer, "shutdown"):
         trainer.shutdown()
     if world > 1:

@@ -45,6 +45,16 @@ TS_DEVICE bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, in
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+// Optional per-step timeline of one CTA (blockIdx 0,0) of the backward
+// kernels: clock64 stamps [role][step][event], switched on from the host for a
+// diagnostic run and off otherwise (one predicated branch per stamp).
+__device__ int g_attn_trace_on = 0;
+__device__ long long g_attn_trace[4 * 128 * 8];
+#define TS_TRACE(role, step, ev)                                                      \
+  do {                                                                                \
+    if (trace && (step) < 128) g_attn_trace[((role) * 128 + (step)) * 8 + (ev)] = clock64(); \
+  } while (0)
+
 template <int D>
 struct FwdLayout {
   static constexpr int BM = 128, BN = 128;
@@ -310,25 +320,30 @@ __global__ void attn_delta_kernel(const bf16* __restrict__ o, const bf16* __rest
 // TMEM buffer pair; the compute warps form P^T = exp2(S^T*sl2 - lse2) and
 // dS^T = P^T (dP^T - delta) as bf16 K-major tiles; the MMA thread accumulates
 // dV += P^T dO and dK += dS^T Q into TMEM, which hold them across all steps.
+// Q/dO tiles run NQ = 3 stages ahead so their TMA latency stays off the MMA
+// thread's critical path; P^T/dS^T and the TMEM S^T/dP^T pairs are double
+// buffered.
 template <int D>
 struct DkvLayout {
-  static constexpr int BN = 128, BQ = 64, NB = D / 64;
+  static constexpr int BN = 128, BQ = 64, NB = D / 64, NQ = 3;
   static constexpr uint32_t KV_BYTES = BN * D * 2;
   static constexpr uint32_t QT_BYTES = BQ * D * 2;
   static constexpr uint32_t K = 0, V = KV_BYTES;
-  static constexpr uint32_t Q0 = 2 * KV_BYTES;               // [2] Q tiles
-  static constexpr uint32_t O0 = Q0 + 2 * QT_BYTES;          // [2] dO tiles
-  static constexpr uint32_t P0 = O0 + 2 * QT_BYTES;          // [2] P^T tiles (128 x 64 bf16)
+  static constexpr uint32_t Q0 = 2 * KV_BYTES;               // [NQ] Q tiles
+  static constexpr uint32_t O0 = Q0 + NQ * QT_BYTES;         // [NQ] dO tiles
+  static constexpr uint32_t P0 = O0 + NQ * QT_BYTES;         // [2] P^T tiles (128 x 64 bf16)
   static constexpr uint32_t PT_BYTES = BN * BQ * 2;
   static constexpr uint32_t DS0 = P0 + 2 * PT_BYTES;         // [2] dS^T tiles
-  static constexpr uint32_t LD0 = DS0 + 2 * PT_BYTES;        // [2][2][BQ] floats: lse2, delta
-  static constexpr uint32_t BAR = LD0 + 2 * 2 * BQ * 4;
+  static constexpr uint32_t LD0 = DS0 + 2 * PT_BYTES;        // [NQ][2][BQ] floats: lse2, delta
+  static constexpr uint32_t BAR = LD0 + NQ * 2 * BQ * 4;
   static constexpr uint32_t TOTAL = BAR + 256;
   static constexpr uint32_t DK_COL = 0, DV_COL = D, ST_COL0 = 2 * D;  // ST/DPT pairs follow
 };
 
+static_assert(DkvLayout<128>::TOTAL + 1024 <= 232448, "dK/dV shared memory exceeds 227 KB");
+
 struct DkvBars {
-  uint64_t kv, q_full[2], s_full[2], p_full[2], mma_done[2], fin;
+  uint64_t kv, q_full[3], q_empty[3], s_full[2], p_full[2], mma_done[2], fin;
   uint32_t tmem_slot;
   int abort;
 };
@@ -356,11 +371,15 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
   const int total = n_qt * grp;
   volatile int* abort = &bars->abort;
   float* ld = reinterpret_cast<float*>(smem + L::LD0);
+  const bool trace = g_attn_trace_on && blockIdx.x == 0 && blockIdx.y == 0;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(&bars->kv, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < L::NQ; ++i) {
       tc::mbar_init(&bars->q_full[i], 2);
+      tc::mbar_init(&bars->q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&bars->s_full[i], 1);
       tc::mbar_init(&bars->p_full[i], 256);
       tc::mbar_init(&bars->mma_done[i], 1);
@@ -384,26 +403,29 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
       }
     }
     for (int i = 0; i < total; ++i) {
-      const int st = i & 1;
-      if (i >= 2 && !warp_wait(&bars->mma_done[st], ((i - 2) >> 1) & 1, abort, err, 51)) break;
+      const int qs = i % L::NQ;
+      if (lane == 0) TS_TRACE(0, i, 0);
+      if (i >= L::NQ && !warp_wait(&bars->q_empty[qs], ((i - L::NQ) / L::NQ) & 1, abort, err, 51)) break;
+      if (lane == 0) TS_TRACE(0, i, 1);
       const int hh = hk * grp + i / n_qt;
       const int qt = qstart + (i % n_qt) * L::BQ;
       if (lane == 0) {
-        tc::mbar_expect_tx(&bars->q_full[st], 2 * L::QT_BYTES);
+        tc::mbar_expect_tx(&bars->q_full[qs], 2 * L::QT_BYTES);
         for (int b = 0; b < L::NB; ++b) {
-          tc::tma_load_2d(smem + L::Q0 + st * L::QT_BYTES + b * L::BQ * 128, &tm_q, hh * D + b * 64, qt,
-                          &bars->q_full[st]);
-          tc::tma_load_2d(smem + L::O0 + st * L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qt,
-                          &bars->q_full[st]);
+          tc::tma_load_2d(smem + L::Q0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_q, hh * D + b * 64, qt,
+                          &bars->q_full[qs]);
+          tc::tma_load_2d(smem + L::O0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qt,
+                          &bars->q_full[qs]);
         }
       }
       for (int c = lane; c < L::BQ; c += 32) {
         const int qi = qt + c;
-        ld[(st * 2 + 0) * L::BQ + c] = qi < T ? lse[(long long)hh * T + qi] * kLog2e : 0.f;
-        ld[(st * 2 + 1) * L::BQ + c] = qi < T ? delta[(long long)hh * T + qi] : 0.f;
+        ld[(qs * 2 + 0) * L::BQ + c] = qi < T ? lse[(long long)hh * T + qi] * kLog2e : 0.f;
+        ld[(qs * 2 + 1) * L::BQ + c] = qi < T ? delta[(long long)hh * T + qi] : 0.f;
       }
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars->q_full[st]);
+      if (lane == 0) tc::mbar_arrive(&bars->q_full[qs]);
+      if (lane == 0) TS_TRACE(0, i, 2);
     }
   } else if (warp == 9) {
     if (lane == 0) {
@@ -411,10 +433,12 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
       const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
       bool ok = tc::mbar_wait(&bars->kv, 0, abort, err, 61);
       auto issue_s = [&](int i) -> bool {
-        const int st = i & 1;
-        if (!tc::mbar_wait(&bars->q_full[st], (i >> 1) & 1, abort, err, 62)) return false;
+        const int st = i & 1, qs = i % L::NQ;
+        TS_TRACE(1, i, 3);
+        if (!tc::mbar_wait(&bars->q_full[qs], (i / L::NQ) & 1, abort, err, 62)) return false;
+        TS_TRACE(1, i, 4);
         tc::tc_fence_after();
-        const uint32_t qb = sbase + L::Q0 + st * L::QT_BYTES, ob = sbase + L::O0 + st * L::QT_BYTES;
+        const uint32_t qb = sbase + L::Q0 + qs * L::QT_BYTES, ob = sbase + L::O0 + qs * L::QT_BYTES;
         const uint32_t col = L::ST_COL0 + st * 2 * L::BQ;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -426,16 +450,19 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
                        tc::sdesc_sw128(ob + q_off, 16, 1024), id_s, kk > 0);
         }
         tc::mma_commit(&bars->s_full[st]);
+        TS_TRACE(1, i, 5);
         return true;
       };
       if (ok && total > 0) ok = issue_s(0);
       if (ok && total > 1) ok = issue_s(1);
       for (int i = 0; ok && i < total; ++i) {
-        const int st = i & 1;
+        const int st = i & 1, qs = i % L::NQ;
+        TS_TRACE(1, i, 0);
         if (!tc::mbar_wait(&bars->p_full[st], (i >> 1) & 1, abort, err, 63)) break;
+        TS_TRACE(1, i, 1);
         tc::tc_fence_after();
         const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
-        const uint32_t qb = sbase + L::Q0 + st * L::QT_BYTES, ob = sbase + L::O0 + st * L::QT_BYTES;
+        const uint32_t qb = sbase + L::Q0 + qs * L::QT_BYTES, ob = sbase + L::O0 + qs * L::QT_BYTES;
 #pragma unroll
         for (int kk = 0; kk < L::BQ / 16; ++kk) {
           const uint64_t ap = tc::sdesc_sw128(pb + kk * 32, 16, 1024);
@@ -446,6 +473,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
           tc::mma_bf16(tmem + L::DK_COL, ad, bq, id_acc, i > 0 || kk > 0);
         }
         tc::mma_commit(&bars->mma_done[st]);
+        tc::mma_commit(&bars->q_empty[qs]);
+        TS_TRACE(1, i, 2);
         if (i + 2 < total) ok = issue_s(i + 2);
       }
       if (ok) tc::mma_commit(&bars->fin);
@@ -459,19 +488,25 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool ok = true;
     for (int i = 0; i < total && ok; ++i) {
-      const int st = i & 1;
+      const int st = i & 1, qs = i % L::NQ;
       const int qt = qstart + (i % n_qt) * L::BQ;
-      if (!warp_wait(&bars->q_full[st], (i >> 1) & 1, abort, err, 71)) { ok = false; break; }
+      const bool tw = threadIdx.x == 0;
+      if (tw) TS_TRACE(2, i, 0);
+      if (!warp_wait(&bars->q_full[qs], (i / L::NQ) & 1, abort, err, 71)) { ok = false; break; }
+      if (tw) TS_TRACE(2, i, 1);
       if (!warp_wait(&bars->s_full[st], (i >> 1) & 1, abort, err, 72)) { ok = false; break; }
+      if (tw) TS_TRACE(2, i, 2);
       if (i >= 2 && !warp_wait(&bars->mma_done[st], ((i - 2) >> 1) & 1, abort, err, 73)) { ok = false; break; }
+      if (tw) TS_TRACE(2, i, 3);
       tc::tc_fence_after();
       float sv[32], dp[32];
       const uint32_t col = L::ST_COL0 + st * 2 * L::BQ + hc * 32;
       tc::tmem_ld32(lane_base + col, sv);
       tc::tmem_ld32(lane_base + col + L::BQ, dp);
       tc::tmem_ld_wait();
-      const float* l2 = ld + (st * 2 + 0) * L::BQ + hc * 32;
-      const float* dl = ld + (st * 2 + 1) * L::BQ + hc * 32;
+      if (tw) TS_TRACE(2, i, 4);
+      const float* l2 = ld + (qs * 2 + 0) * L::BQ + hc * 32;
+      const float* dl = ld + (qs * 2 + 1) * L::BQ + hc * 32;
       const int qc0 = qt + hc * 32;
       const bool full = (qc0 >= kr - off) && (qc0 + 32 <= T) && kr < S;
       const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
@@ -490,9 +525,11 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
         st_shared_v4(pb + o8, pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]), pack2(p[6], p[7]));
         st_shared_v4(db + o8, pack2(ds[0], ds[1]), pack2(ds[2], ds[3]), pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
       }
+      if (tw) TS_TRACE(2, i, 5);
       tc::fence_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->p_full[st]);
+      if (tw) TS_TRACE(2, i, 6);
     }
     if (ok && total > 0 && warp_wait(&bars->fin, 0, abort, err, 74)) {
       tc::tc_fence_after();
@@ -536,23 +573,27 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
 // Per 64-key tile: S = Q K^T and dP = dO V^T into a TMEM buffer pair, the
 // compute warps form dS = P (dP - delta) (bf16, K-major), the MMA thread
 // accumulates dQ += dS K into TMEM.
+// K/V tiles run NK = 4 stages ahead of the MMA thread; dS tiles and the TMEM
+// S/dP pairs are double buffered.
 template <int D>
 struct DqLayout {
-  static constexpr int BM = 128, BN = 64, NB = D / 64;
+  static constexpr int BM = 128, BN = 64, NB = D / 64, NK = 4;
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KT_BYTES = BN * D * 2;
   static constexpr uint32_t Q = 0, O = Q_BYTES;
-  static constexpr uint32_t K0 = 2 * Q_BYTES;             // [2] K tiles
-  static constexpr uint32_t V0 = K0 + 2 * KT_BYTES;       // [2] V tiles
-  static constexpr uint32_t DS0 = V0 + 2 * KT_BYTES;      // [2] dS tiles (128 x 64)
+  static constexpr uint32_t K0 = 2 * Q_BYTES;             // [NK] K tiles
+  static constexpr uint32_t V0 = K0 + NK * KT_BYTES;      // [NK] V tiles
+  static constexpr uint32_t DS0 = V0 + NK * KT_BYTES;     // [2] dS tiles (128 x 64)
   static constexpr uint32_t DS_BYTES = BM * BN * 2;
   static constexpr uint32_t BAR = DS0 + 2 * DS_BYTES;
   static constexpr uint32_t TOTAL = BAR + 256;
   static constexpr uint32_t DQ_COL = 0, S_COL0 = D;
 };
 
+static_assert(DqLayout<128>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
+
 struct DqBars {
-  uint64_t q, kv_full[2], s_full[2], p_full[2], mma_done[2], fin;
+  uint64_t q, kv_full[4], kv_empty[4], s_full[2], p_full[2], mma_done[2], fin;
   uint32_t tmem_slot;
   int abort;
 };
@@ -581,8 +622,11 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
 
   if (threadIdx.x == 0) {
     tc::mbar_init(&bars->q, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < L::NK; ++i) {
       tc::mbar_init(&bars->kv_full[i], 1);
+      tc::mbar_init(&bars->kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&bars->s_full[i], 1);
       tc::mbar_init(&bars->p_full[i], 256);
       tc::mbar_init(&bars->mma_done[i], 1);
@@ -604,14 +648,14 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
         tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, q0, &bars->q);
       }
       for (int j = 0; j < n; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !tc::mbar_wait(&bars->mma_done[st], ((j - 2) >> 1) & 1, abort, err, 81)) break;
-        tc::mbar_expect_tx(&bars->kv_full[st], 2 * L::KT_BYTES);
+        const int ks = j % L::NK;
+        if (j >= L::NK && !tc::mbar_wait(&bars->kv_empty[ks], ((j - L::NK) / L::NK) & 1, abort, err, 81)) break;
+        tc::mbar_expect_tx(&bars->kv_full[ks], 2 * L::KT_BYTES);
         for (int b = 0; b < L::NB; ++b) {
-          tc::tma_load_2d(smem + L::K0 + st * L::KT_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN,
-                          &bars->kv_full[st]);
-          tc::tma_load_2d(smem + L::V0 + st * L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
-                          &bars->kv_full[st]);
+          tc::tma_load_2d(smem + L::K0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN,
+                          &bars->kv_full[ks]);
+          tc::tma_load_2d(smem + L::V0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
+                          &bars->kv_full[ks]);
         }
       }
     }
@@ -621,10 +665,10 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
       const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
       bool ok = tc::mbar_wait(&bars->q, 0, abort, err, 91);
       auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!tc::mbar_wait(&bars->kv_full[st], (j >> 1) & 1, abort, err, 92)) return false;
+        const int st = j & 1, ks = j % L::NK;
+        if (!tc::mbar_wait(&bars->kv_full[ks], (j / L::NK) & 1, abort, err, 92)) return false;
         tc::tc_fence_after();
-        const uint32_t kb = sbase + L::K0 + st * L::KT_BYTES, vb = sbase + L::V0 + st * L::KT_BYTES;
+        const uint32_t kb = sbase + L::K0 + ks * L::KT_BYTES, vb = sbase + L::V0 + ks * L::KT_BYTES;
         const uint32_t col = L::S_COL0 + st * 2 * L::BN;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -641,17 +685,18 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
       if (ok) ok = issue_s(0);
       if (ok && n > 1) ok = issue_s(1);
       for (int j = 0; ok && j < n; ++j) {
-        const int st = j & 1;
+        const int st = j & 1, ks = j % L::NK;
         if (!tc::mbar_wait(&bars->p_full[st], (j >> 1) & 1, abort, err, 93)) break;
         tc::tc_fence_after();
         const uint32_t db = sbase + L::DS0 + st * L::DS_BYTES;
-        const uint32_t kb = sbase + L::K0 + st * L::KT_BYTES;
+        const uint32_t kb = sbase + L::K0 + ks * L::KT_BYTES;
 #pragma unroll
         for (int kk = 0; kk < L::BN / 16; ++kk) {
           tc::mma_bf16(tmem + L::DQ_COL, tc::sdesc_sw128(db + kk * 32, 16, 1024),
                        tc::sdesc_sw128(kb + kk * 16 * 128, L::BN * 128, 1024), id_acc, j > 0 || kk > 0);
         }
         tc::mma_commit(&bars->mma_done[st]);
+        tc::mma_commit(&bars->kv_empty[ks]);
         if (j + 2 < n) ok = issue_s(j + 2);
       }
       if (ok) tc::mma_commit(&bars->fin);
@@ -889,6 +934,22 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
   }
   TS_LAUNCH_CHECK();
   return {o, lse};
+}
+
+void attn_trace_enable(bool on) {
+  const int v = on ? 1 : 0;
+  TS_CUDA_CHECK(cudaMemcpyToSymbol(g_attn_trace_on, &v, sizeof(int)));
+  if (on) {
+    void* p = nullptr;
+    TS_CUDA_CHECK(cudaGetSymbolAddress(&p, g_attn_trace));
+    TS_CUDA_CHECK(cudaMemset(p, 0, sizeof(long long) * 4 * 128 * 8));
+  }
+}
+
+at::Tensor attn_trace_read() {
+  auto out = at::empty({4, 128, 8}, at::TensorOptions().dtype(at::kLong));
+  TS_CUDA_CHECK(cudaMemcpyFromSymbol(out.data_ptr<int64_t>(), g_attn_trace, sizeof(long long) * 4 * 128 * 8));
+  return out;
 }
 
 std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,

@@ -51,6 +51,8 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
                                     const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale);
 void register_ipc(pybind11::module& m);
 void register_pinned(pybind11::module& m);
+void attn_trace_enable(bool on);
+at::Tensor attn_trace_read();
 std::vector<at::Tensor> conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& tail);
 std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& dtail_out, const at::Tensor& x,
                                         const at::Tensor& w, const at::Tensor& tail);
@@ -94,5 +96,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv1d_silu_fwd", &ts::conv1d_silu_fwd);
   m.def("conv1d_silu_bwd", &ts::conv1d_silu_bwd);
   m.def("gdn_fwd", &ts::gdn_fwd);
+  m.def("attn_trace_enable", &ts::attn_trace_enable);
+  m.def("attn_trace_read", &ts::attn_trace_read);
   m.def("gdn_bwd", &ts::gdn_bwd);
 }

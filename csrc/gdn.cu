@@ -30,88 +30,152 @@ namespace {
 typedef __nv_bfloat16 bf16;
 
 // ------------------------------------------------------------------ conv1d
+// Row r of the padded input [tail; x] (r in [0, T+K-1)) is tail row r for
+// r < K-1, else x row r-K+1. Output t reads padded rows t..t+K-1.
+// Each thread owns two adjacent channels of one row chunk and walks the rows
+// with a sliding window, so every input row is read once per chunk (plus a
+// K-1 row halo) and all loads/stores are coalesced bf16x2 across channels.
+constexpr int kConvRows = 64;
+
+struct Pad {
+  const bf16* x;
+  const bf16* tail;
+  int C, K;
+  __device__ __forceinline__ float2 at(int r, int c) const {
+    const __nv_bfloat162 v = r < K - 1 ? *reinterpret_cast<const __nv_bfloat162*>(tail + (long long)r * C + c)
+                                       : *reinterpret_cast<const __nv_bfloat162*>(x + (long long)(r - K + 1) * C + c);
+    return __bfloat1622float2(v);
+  }
+};
+
+TS_DEVICE float silu_of(float a) { return a / (1.f + expf(-a)); }
+TS_DEVICE float dsilu_of(float a) {
+  const float s = 1.f / (1.f + expf(-a));
+  return s * (1.f + a * (1.f - s));
+}
+
 template <int K>
 __global__ void conv1d_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, const bf16* __restrict__ tail,
                                   bf16* __restrict__ y, bf16* __restrict__ new_tail, int T, int C) {
-  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  const long long total = (long long)(T + K - 1) * C;
-  if (idx >= total) return;
-  const int r = (int)(idx / C), c = (int)(idx % C);  // r indexes [tail; x] rows
-  auto in = [&](int row) -> float {
-    return row < K - 1 ? __bfloat162float(tail[(long long)row * C + c]) : __bfloat162float(x[(long long)(row - K + 1) * C + c]);
-  };
-  if (r >= T) {  // the last K-1 rows of [tail; x] become the new tail
-    new_tail[(long long)(r - T) * C + c] = __float2bfloat16_rn(in(r));
-  } else {
-    float acc = 0.f;
-#pragma unroll
-    for (int j = 0; j < K; ++j) acc += __bfloat162float(w[c * K + j]) * in(r + j);
-    const float s = 1.f / (1.f + expf(-acc));
-    y[(long long)r * C + c] = __float2bfloat16_rn(acc * s);
-  }
-}
-
-// dx / dtail: in-row t' gets sum_j w[j] * dpre[t' - j] plus the new-tail gradient
-template <int K>
-__global__ void conv1d_bwd_dx_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ dtail_out,
-                                     const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                     const bf16* __restrict__ tail, bf16* __restrict__ dx, bf16* __restrict__ dtail,
-                                     int T, int C) {
-  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  const long long total = (long long)(T + K - 1) * C;
-  if (idx >= total) return;
-  const int rr = (int)(idx / C), c = (int)(idx % C);
-  auto in = [&](int row) -> float {
-    return row < K - 1 ? __bfloat162float(tail[(long long)row * C + c]) : __bfloat162float(x[(long long)(row - K + 1) * C + c]);
-  };
-  float acc = 0.f;
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
-    const int t = rr - j;
-    if (t < 0 || t >= T) continue;
-    float pre = 0.f;
-#pragma unroll
-    for (int i = 0; i < K; ++i) pre += __bfloat162float(w[c * K + i]) * in(t + i);
-    const float s = 1.f / (1.f + expf(-pre));
-    const float dpre = __bfloat162float(dy[(long long)t * C + c]) * s * (1.f + pre * (1.f - s));
-    acc += __bfloat162float(w[c * K + j]) * dpre;
-  }
-  if (rr >= T) acc += __bfloat162float(dtail_out[(long long)(rr - T) * C + c]);
-  if (rr < K - 1) dtail[(long long)rr * C + c] = __float2bfloat16_rn(acc);
-  else dx[(long long)(rr - K + 1) * C + c] = __float2bfloat16_rn(acc);
-}
-
-// dw partials: block (c-block of 128 channels, row chunk); partial[chunk][c][j]
-template <int K>
-__global__ void conv1d_bwd_dw_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
-                                     const bf16* __restrict__ w, const bf16* __restrict__ tail,
-                                     float* __restrict__ partial, int T, int C, int rows_per_chunk) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int c = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (c >= C) return;
-  const int t0 = blockIdx.y * rows_per_chunk, t1 = min(T, t0 + rows_per_chunk);
-  auto in = [&](int row) -> float {
-    return row < K - 1 ? __bfloat162float(tail[(long long)row * C + c]) : __bfloat162float(x[(long long)(row - K + 1) * C + c]);
-  };
-  float wv[K], acc[K];
+  const Pad in{x, tail, C, K};
+  float w0[K], w1[K];
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    wv[j] = __bfloat162float(w[c * K + j]);
-    acc[j] = 0.f;
+    w0[j] = __bfloat162float(w[c * K + j]);
+    w1[j] = __bfloat162float(w[(c + 1) * K + j]);
   }
+  const int t0 = blockIdx.y * kConvRows, t1 = min(T, t0 + kConvRows);
+  float2 win[K];
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) win[j] = t0 + j < T + K - 1 ? in.at(t0 + j, c) : make_float2(0.f, 0.f);
   for (int t = t0; t < t1; ++t) {
-    float win[K], pre = 0.f;
+    win[K - 1] = in.at(t + K - 1, c);
+    float a0 = 0.f, a1 = 0.f;
 #pragma unroll
     for (int j = 0; j < K; ++j) {
-      win[j] = in(t + j);
-      pre += wv[j] * win[j];
+      a0 += w0[j] * win[j].x;
+      a1 += w1[j] * win[j].y;
     }
-    const float s = 1.f / (1.f + expf(-pre));
-    const float dpre = __bfloat162float(dy[(long long)t * C + c]) * s * (1.f + pre * (1.f - s));
+    *reinterpret_cast<__nv_bfloat162*>(y + (long long)t * C + c) = __floats2bfloat162_rn(silu_of(a0), silu_of(a1));
 #pragma unroll
-    for (int j = 0; j < K; ++j) acc[j] += dpre * win[j];
+    for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+  }
+  if (blockIdx.y == gridDim.y - 1) {  // the last K-1 padded rows become the new tail
+    for (int r = 0; r < K - 1; ++r) {
+      const float2 v = in.at(T + r, c);
+      *reinterpret_cast<__nv_bfloat162*>(new_tail + (long long)r * C + c) = __floats2bfloat162_rn(v.x, v.y);
+    }
+  }
+}
+
+// One pass per (channel pair, row chunk): dpre[t] = dy[t] * silu'(pre[t]);
+// d(pad)[r] = sum_j w[j] dpre[r-j] (+ the new tail's gradient for r >= T);
+// dw partial[chunk][c][j] = sum_t dpre[t] * pad[t+j] over the chunk's t.
+template <int K>
+__global__ void conv1d_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ dtail_out,
+                                  const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                  const bf16* __restrict__ tail, bf16* __restrict__ dx, bf16* __restrict__ dtail,
+                                  float* __restrict__ partial, int T, int C) {
+  const int c = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (c >= C) return;
+  const Pad in{x, tail, C, K};
+  const int R = T + K - 1;
+  float w0[K], w1[K], g0[K], g1[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    w0[j] = __bfloat162float(w[c * K + j]);
+    w1[j] = __bfloat162float(w[(c + 1) * K + j]);
+    g0[j] = g1[j] = 0.f;
+  }
+  // padded rows owned by this chunk: [r0, r1); the last chunk also owns the tail rows >= T
+  const int r0 = blockIdx.y * kConvRows;
+  const int r1 = blockIdx.y == gridDim.y - 1 ? R : min(R, r0 + kConvRows);
+  auto dpre_at = [&](int t, float2& v, float2 (&pw)[K]) {
+    // pw: padded rows t..t+K-1
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      a0 += w0[j] * pw[j].x;
+      a1 += w1[j] * pw[j].y;
+    }
+    const float2 d = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dy + (long long)t * C + c));
+    v = make_float2(d.x * dsilu_of(a0), d.y * dsilu_of(a1));
+  };
+  // dq[k] holds dpre[r - k] for the current r (k = 0..K-1), zero outside [0, T)
+  float2 dq[K];
+  float2 win[K];  // padded rows r .. r+K-1
+#pragma unroll
+  for (int k = 0; k < K; ++k) dq[k] = make_float2(0.f, 0.f);
+  // warm-up: dpre[r0-K+1 .. r0-1] into dq[K-1 .. 1]
+  for (int k = K - 1; k >= 1; --k) {
+    const int t = r0 - k;
+    if (t >= 0 && t < T) {
+      float2 pw[K];
+#pragma unroll
+      for (int j = 0; j < K; ++j) pw[j] = in.at(t + j, c);
+      dpre_at(t, dq[k], pw);
+    }
   }
 #pragma unroll
-  for (int j = 0; j < K; ++j) partial[((long long)blockIdx.y * C + c) * K + j] = acc[j];
+  for (int j = 0; j < K - 1; ++j) win[j] = r0 + j < R ? in.at(r0 + j, c) : make_float2(0.f, 0.f);
+  for (int r = r0; r < r1; ++r) {
+    win[K - 1] = r + K - 1 < R ? in.at(r + K - 1, c) : make_float2(0.f, 0.f);
+    float2 cur = make_float2(0.f, 0.f);
+    if (r < T) {
+      dpre_at(r, cur, win);
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        g0[j] += cur.x * win[j].x;
+        g1[j] += cur.y * win[j].y;
+      }
+    }
+    dq[0] = cur;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      s0 += w0[j] * dq[j].x;
+      s1 += w1[j] * dq[j].y;
+    }
+    if (r >= T) {
+      const float2 d = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dtail_out + (long long)(r - T) * C + c));
+      s0 += d.x;
+      s1 += d.y;
+    }
+    __nv_bfloat162* dst = r < K - 1 ? reinterpret_cast<__nv_bfloat162*>(dtail + (long long)r * C + c)
+                                    : reinterpret_cast<__nv_bfloat162*>(dx + (long long)(r - K + 1) * C + c);
+    *dst = __floats2bfloat162_rn(s0, s1);
+#pragma unroll
+    for (int k = K - 1; k >= 1; --k) dq[k] = dq[k - 1];
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+  }
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    partial[((long long)blockIdx.y * C + c) * K + j] = g0[j];
+    partial[((long long)blockIdx.y * C + c + 1) * K + j] = g1[j];
+  }
 }
 
 __global__ void conv1d_dw_sum_kernel(const float* __restrict__ partial, float* __restrict__ dw, int chunks, int n) {
@@ -458,12 +522,14 @@ std::vector<at::Tensor> conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w
   const c10::cuda::CUDAGuard guard(x.device());
   const int T = x.size(0), C = x.size(1), K = w.size(1);
   TS_CHECK(K == 4, "conv1d kernel width 4 supported");
+  TS_CHECK(C % 2 == 0, "conv1d needs an even channel count");
   auto y = at::empty_like(x);
   auto nt = at::empty({K - 1, C}, x.options());
-  const long long total = (long long)(T + K - 1) * C;
-  conv1d_fwd_kernel<4><<<(int)((total + 255) / 256), 256, 0, stream()>>>(
-      (const bf16*)x.data_ptr(), (const bf16*)w.data_ptr(), (const bf16*)tail.data_ptr(), (bf16*)y.data_ptr(),
-      (bf16*)nt.data_ptr(), T, C);
+  const int threads = 128;
+  const dim3 grid((C / 2 + threads - 1) / threads, std::max(1, (T + kConvRows - 1) / kConvRows));
+  conv1d_fwd_kernel<4><<<grid, threads, 0, stream()>>>((const bf16*)x.data_ptr(), (const bf16*)w.data_ptr(),
+                                                       (const bf16*)tail.data_ptr(), (bf16*)y.data_ptr(),
+                                                       (bf16*)nt.data_ptr(), T, C);
   TS_LAUNCH_CHECK();
   return {y, nt};
 }
@@ -475,22 +541,18 @@ std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& 
   check_cuda(x, "x");
   const c10::cuda::CUDAGuard guard(x.device());
   const int T = x.size(0), C = x.size(1), K = w.size(1);
+  TS_CHECK(K == 4 && C % 2 == 0, "conv1d backward supports width 4 and even channel counts");
   auto dx = at::empty_like(x);
   auto dtail = at::empty_like(tail);
-  const long long total = (long long)(T + K - 1) * C;
-  conv1d_bwd_dx_kernel<4><<<(int)((total + 255) / 256), 256, 0, stream()>>>(
-      (const bf16*)dy.data_ptr(), (const bf16*)dtail_out.data_ptr(), (const bf16*)x.data_ptr(),
-      (const bf16*)w.data_ptr(), (const bf16*)tail.data_ptr(), (bf16*)dx.data_ptr(), (bf16*)dtail.data_ptr(), T, C);
-  const int cblocks = (C + 127) / 128;
-  int chunks = std::max(1, std::min(T, (2 * sm_count(x.get_device())) / std::max(cblocks, 1)));
-  const int rpc = (T + chunks - 1) / std::max(chunks, 1);
-  chunks = T > 0 ? (T + rpc - 1) / rpc : 1;
-  auto partial = at::zeros({chunks, C, K}, x.options().dtype(at::kFloat));
+  const int R = T + K - 1;
+  const int chunks = std::max(1, (R + kConvRows - 1) / kConvRows);
+  auto partial = at::empty({chunks, C, K}, x.options().dtype(at::kFloat));
   auto dw = at::empty({C, K}, x.options().dtype(at::kFloat));
-  if (T > 0)
-    conv1d_bwd_dw_kernel<4><<<dim3(cblocks, chunks), 128, 0, stream()>>>(
-        (const bf16*)dy.data_ptr(), (const bf16*)x.data_ptr(), (const bf16*)w.data_ptr(), (const bf16*)tail.data_ptr(),
-        partial.data_ptr<float>(), T, C, rpc);
+  const int threads = 128;
+  conv1d_bwd_kernel<4><<<dim3((C / 2 + threads - 1) / threads, chunks), threads, 0, stream()>>>(
+      (const bf16*)dy.data_ptr(), (const bf16*)dtail_out.data_ptr(), (const bf16*)x.data_ptr(),
+      (const bf16*)w.data_ptr(), (const bf16*)tail.data_ptr(), (bf16*)dx.data_ptr(), (bf16*)dtail.data_ptr(),
+      partial.data_ptr<float>(), T, C);
   conv1d_dw_sum_kernel<<<(C * K + 255) / 256, 256, 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
                                                                    chunks, C * K);
   TS_LAUNCH_CHECK();

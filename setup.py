@@ -8,6 +8,7 @@ the explicit ``-gencode`` bypasses torch's own architecture list.
 
 import glob
 import os
+import subprocess
 
 from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
@@ -31,6 +32,19 @@ if os.environ.get("TS_BOUNDS_CHECK"):
 if os.environ.get("TS_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
 
+HOST_TOOLS = {
+    # host-side helper executables, built beside the package modules that run them
+    os.path.join("thundersync_b200", "rollout", "ts_netguard"): os.path.join("csrc", "host", "netguard.c"),
+}
+
+
+class Build(BuildExtension.with_options(use_ninja=True)):
+    def run(self):
+        for out, src in HOST_TOOLS.items():
+            subprocess.check_call(["gcc", "-O2", "-Wall", "-o", os.path.join(ROOT, out), os.path.join(ROOT, src)])
+        super().run()
+
+
 setup(
     name="thundersync_b200_native",
     ext_modules=[
@@ -41,5 +55,5 @@ setup(
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
         )
     ],
-    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    cmdclass={"build_ext": Build},
 )

@@ -254,9 +254,17 @@ class StreamingRun:
 
     # ------------------------------------------------------------ helpers
     def _ids(self, values: Iterable[int]) -> torch.Tensor:
-        t = torch.tensor(list(values), dtype=torch.long)
+        """Token ids on the run's device, copied from page-locked host memory."""
+        if isinstance(values, torch.Tensor):
+            t = values.to(dtype=torch.long).reshape(-1)
+            if t.device == self.device:
+                return t
+        else:
+            t = torch.tensor(list(values), dtype=torch.long)
         if self.device.type == "cuda":
-            return t.pin_memory().to(self.device, non_blocking=True)
+            if not t.is_pinned():
+                t = t.pin_memory()
+            return t.to(self.device, non_blocking=True)
         return t.to(self.device)
 
     def _positions(self, start: int, n: int) -> torch.Tensor:

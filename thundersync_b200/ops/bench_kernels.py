@@ -1,0 +1,153 @@
+"""Micro-benchmarks of this package's CUDA kernels (CUDA-event timing).
+
+``python -m thundersync_b200.ops.bench_kernels attn --mode bwd --t 2048 --s 2560``
+times one kernel family on the current GPU after warm-up, with inputs
+allocated once, and prints one line per measurement (milliseconds and the
+achieved TFLOP/s or GB/s against the algorithmic work). It is also the small,
+self-contained case that kernel profiles are captured on.
+
+Families: ``attn`` (bottom-right causal GQA attention; fwd, or fwd+bwd),
+``rms`` (RMSNorm fwd/bwd), ``lse`` (log-sum-exp/gather over fp32 logits),
+``gdn`` (gated delta rule fwd/bwd), ``conv`` (causal conv1d + SiLU fwd/bwd).
+"""
+
+from __future__ import annotations
+
+import argparse
+import math
+
+import torch
+
+from thundersync_b200.ops._ext import native
+
+
+def _time(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def bench_attn(args) -> None:
+    t, s, hq, hkv, d = args.t, args.s, args.hq, args.hkv, args.d
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(t, hq, d, device="cuda", dtype=torch.bfloat16, generator=g)
+    k = torch.randn(s, hkv, d, device="cuda", dtype=torch.bfloat16, generator=g)
+    v = torch.randn(s, hkv, d, device="cuda", dtype=torch.bfloat16, generator=g)
+    scale = 1 / math.sqrt(d)
+    flops = 4 * hq * d * (t * (s - t) + t * (t + 1) / 2)  # two GEMMs over the visible (q, k) pairs
+    ext = native()
+    o, lse = ext.attn_fwd_tc(q, k, v, scale)
+    ms = _time(lambda: ext.attn_fwd_tc(q, k, v, scale), args.iters)
+    print(f"attn fwd T={t} S={s} Hq={hq} Hkv={hkv} D={d}: {ms:.3f} ms  {flops / ms / 1e9:.1f} TFLOP/s")
+    if args.mode == "bwd":
+        do = torch.randn(o.shape, device="cuda", dtype=torch.bfloat16, generator=g)
+        ms = _time(lambda: ext.attn_bwd_tc(do, q, k, v, o, lse, scale), args.iters)
+        print(f"attn bwd: {ms:.3f} ms  {2.5 * flops / ms / 1e9:.1f} TFLOP/s (5 GEMM-equivalents)")
+        if args.trace:
+            ext.attn_trace_enable(True)
+            ext.attn_bwd_tc(do, q, k, v, o, lse, scale)
+            torch.cuda.synchronize()
+            ext.attn_trace_enable(False)
+            _print_trace(ext.attn_trace_read())
+    print("kernel status", int(ext.tc_status(q).item()))
+
+
+def _print_trace(tr) -> None:
+    """Per-step clock64 deltas of the dK/dV kernel's first CTA (producer / MMA / compute warp 0)."""
+    t = tr.clone()
+    base = int(t[t > 0].min()) if bool((t > 0).any()) else 0
+    t = torch.where(t > 0, t - base, torch.zeros_like(t))
+    names = {0: "prod[wait_empty,got_empty,issued]", 1: "mma[wait_p,got_p,dkdv_issued,wait_q,got_q,s_issued]",
+             2: "cmp[start,q,s,mma_done,tmem_ld,computed,arrived]"}
+    for role, name in names.items():
+        print("role", name)
+        for i in range(0, 24):
+            row = [int(x) for x in t[role, i, :7].tolist()]
+            if any(row):
+                print(f"  step {i:3d}: " + " ".join(f"{x:9d}" for x in row))
+    cmp = t[2]
+    steps = int((cmp[:, 6] > 0).sum())
+    if steps > 2:
+        d = lambda a, b: float((cmp[2:steps, b] - cmp[2:steps, a]).double().mean())  # noqa: E731
+        print(f"compute: wait_s {d(1, 2):.0f}  wait_mma_done {d(2, 3):.0f}  tmem_ld {d(3, 4):.0f}  "
+              f"math+st {d(4, 5):.0f}  arrive {d(5, 6):.0f}  cycle {float((cmp[3:steps, 0] - cmp[2:steps - 1, 0]).double().mean()):.0f}")
+
+
+def bench_rms(args) -> None:
+    x = torch.randn(args.rows, args.cols, device="cuda", dtype=torch.bfloat16)
+    w = torch.rand(args.cols, device="cuda", dtype=torch.bfloat16)
+    ext = native()
+    y, r = ext.rms_norm_fwd(x, w, 1e-6, False)
+    ms = _time(lambda: ext.rms_norm_fwd(x, w, 1e-6, False), args.iters)
+    gb = 2 * x.numel() * 2 / 1e9
+    print(f"rms fwd {args.rows}x{args.cols}: {ms:.3f} ms  {gb / ms * 1e3:.0f} GB/s")
+    dy = torch.randn_like(x)
+    ms = _time(lambda: ext.rms_norm_bwd(dy, x, w, r, False), args.iters)
+    print(f"rms bwd: {ms:.3f} ms  {1.5 * gb / ms * 1e3:.0f} GB/s")
+
+
+def bench_lse(args) -> None:
+    logits = torch.randn(args.rows, args.cols, device="cuda", dtype=torch.float32)
+    tgt = torch.randint(0, args.cols, (args.rows,), device="cuda")
+    ext = native()
+    ms = _time(lambda: ext.lse_gather(logits, tgt, False), args.iters)
+    print(f"lse {args.rows}x{args.cols}: {ms:.3f} ms  {logits.numel() * 4 / ms / 1e6:.0f} GB/s")
+
+
+def bench_gdn(args) -> None:
+    t, h = args.t, args.h
+    q = torch.randn(t, h, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(t, h, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(t, h, 128, device="cuda", dtype=torch.bfloat16)
+    gg = -torch.rand(t, h, device="cuda") * 0.1
+    beta = torch.rand(t, h, device="cuda")
+    s0 = torch.zeros(h, 128, 128, device="cuda")
+    ext = native()
+    o, fin, saved = ext.gdn_fwd(q, k, v, gg, beta, s0)
+    ms = _time(lambda: ext.gdn_fwd(q, k, v, gg, beta, s0), args.iters)
+    print(f"gdn fwd T={t} H={h}: {ms:.3f} ms  {t / ms * 1e3:.0f} tokens/s")
+    do = torch.randn_like(o)
+    ms = _time(lambda: ext.gdn_bwd(do, torch.zeros_like(fin), q, k, v, gg, beta, saved), args.iters)
+    print(f"gdn bwd: {ms:.3f} ms")
+
+
+def bench_conv(args) -> None:
+    x = torch.randn(args.rows, args.cols, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(args.cols, 4, device="cuda", dtype=torch.bfloat16)
+    tail = torch.zeros(3, args.cols, device="cuda", dtype=torch.bfloat16)
+    ext = native()
+    y, nt = ext.conv1d_silu_fwd(x, w, tail)
+    ms = _time(lambda: ext.conv1d_silu_fwd(x, w, tail), args.iters)
+    print(f"conv fwd {args.rows}x{args.cols}: {ms:.3f} ms  {2 * x.numel() * 2 / ms / 1e6:.0f} GB/s")
+    dy = torch.randn_like(y)
+    ms = _time(lambda: ext.conv1d_silu_bwd(dy, torch.zeros_like(nt), x, w, tail), args.iters)
+    print(f"conv bwd: {ms:.3f} ms")
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv"])
+    ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
+    ap.add_argument("--t", type=int, default=2048)
+    ap.add_argument("--s", type=int, default=2560)
+    ap.add_argument("--hq", type=int, default=16)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--d", type=int, default=128)
+    ap.add_argument("--h", type=int, default=16)
+    ap.add_argument("--rows", type=int, default=16384)
+    ap.add_argument("--cols", type=int, default=2048)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--trace", action="store_true", help="print the dK/dV kernel's per-step timeline")
+    args = ap.parse_args(argv)
+    {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv}[args.family](args)
+
+
+if __name__ == "__main__":
+    main()
