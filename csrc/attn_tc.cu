@@ -33,6 +33,13 @@ constexpr float kLn2 = 0.6931471805599453f;
 TS_DEVICE void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
+// 2^x with the SM's native ex2 unit (flush-to-zero); inputs here are <= 0 after the
+// max/LSE shift, and outputs below the normal range contribute nothing in bf16.
+TS_DEVICE float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 TS_DEVICE uint32_t pack2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -231,7 +238,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int i = c8 * 8 + e;
-          p[e] = i < nv_half ? exp2f(fmaf(sv[i], sl2, -ref)) : 0.f;
+          p[e] = i < nv_half ? ex2(fmaf(sv[i], sl2, -ref)) : 0.f;
           rs += p[e];
         }
         st_shared_v4(pbase + tc::kmajor_off(r, hc * 64 + c8 * 8, 128), pack2(p[0], p[1]), pack2(p[2], p[3]),
@@ -505,10 +512,20 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
       tc::tmem_ld32(lane_base + col + L::BQ, dp);
       tc::tmem_ld_wait();
       if (tw) TS_TRACE(2, i, 4);
-      const float* l2 = ld + (qs * 2 + 0) * L::BQ + hc * 32;
-      const float* dl = ld + (qs * 2 + 1) * L::BQ + hc * 32;
+      // this step's 32 query columns: lse2 and delta into registers (broadcast
+      // shared loads), and the visible range [lo, hi) of column indices
+      float l2[32], dl[32];
+      const float4* l2v = reinterpret_cast<const float4*>(ld + (qs * 2 + 0) * L::BQ + hc * 32);
+      const float4* dlv = reinterpret_cast<const float4*>(ld + (qs * 2 + 1) * L::BQ + hc * 32);
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        const float4 a = l2v[x], b = dlv[x];
+        l2[4 * x] = a.x; l2[4 * x + 1] = a.y; l2[4 * x + 2] = a.z; l2[4 * x + 3] = a.w;
+        dl[4 * x] = b.x; dl[4 * x + 1] = b.y; dl[4 * x + 2] = b.z; dl[4 * x + 3] = b.w;
+      }
       const int qc0 = qt + hc * 32;
-      const bool full = (qc0 >= kr - off) && (qc0 + 32 <= T) && kr < S;
+      const int lo = kr < S ? kr - off - qc0 : 32;  // query qc0+c sees key kr iff c >= lo
+      const int hi = T - qc0;                       // and c < hi (query exists)
       const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
@@ -516,9 +533,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int c = c8 * 8 + e;
-          const int qi = qc0 + c;
-          const bool vis = full || (qi < T && kr < S && kr <= qi + off);
-          p[e] = vis ? exp2f(sv[c] * sl2 - l2[c]) : 0.f;
+          p[e] = (c >= lo && c < hi) ? ex2(fmaf(sv[c], sl2, -l2[c])) : 0.f;
           ds[e] = p[e] * (dp[c] - dl[c]);
         }
         const uint32_t o8 = tc::kmajor_off(r, hc * 32 + c8 * 8, 128);
@@ -722,7 +737,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
       tc::tmem_ld32(lane_base + col + L::BN, dp);
       tc::tmem_ld_wait();
       const int k0 = j * L::BN + hc * 32;
-      const bool full = (k0 + 31 <= q0 + off) && (k0 + 32 <= S) && qi < T;
+      // key k0+c is visible iff c < nvis (key <= lim, key < S, query exists)
+      const int nvis = qi < T ? min(lim, S - 1) - k0 + 1 : 0;
       const uint32_t db = sbase + L::DS0 + st * L::DS_BYTES;
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
@@ -730,9 +746,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int c = c8 * 8 + e;
-          const int key = k0 + c;
-          const bool vis = full || (qi < T && key < S && key <= lim);
-          const float p = vis ? exp2f(sv[c] * sl2 - l2) : 0.f;
+          const float p = c < nvis ? ex2(fmaf(sv[c], sl2, -l2)) : 0.f;
           ds[e] = p * (dp[c] - dl);
         }
         st_shared_v4(db + tc::kmajor_off(r, hc * 32 + c8 * 8, 128), pack2(ds[0], ds[1]), pack2(ds[2], ds[3]),
