@@ -392,13 +392,14 @@ def main() -> None:
         from torch.profiler import ProfilerActivity, profile
 
         torch.cuda.synchronize()
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], with_stack=False) as prof:
             run_step(trainer, works[-1], None)
             torch.cuda.synchronize()
         if rank == 0:
             with open(args.profile_out, "w") as fh:
                 fh.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=45,
                                                    max_name_column_width=100))
+            prof.export_chrome_trace(args.profile_out + ".trace.json")
     if hasattr(trainer, "shutdown"):
         trainer.shutdown()
     if world > 1:

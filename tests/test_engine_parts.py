@@ -164,3 +164,27 @@ def test_sharded_step_equals_unsharded_adamw():
         for got, want in zip(outs[r][0], ref):
             assert torch.allclose(got, want.detach(), atol=1e-6)
     assert outs[0][1]["owned_param_count"] + outs[1][1]["owned_param_count"] == len(shapes)
+
+
+def test_single_node_dense_layer_matches_op_by_op():
+    """The one-node layer op gives bitwise the op-by-op values and gradients (CPU)."""
+    from tests.grpo_fixtures import build_model
+    from thundersync_b200.engine.layers import Executor, Segment
+
+    model = build_model(0)
+    ids = torch.randint(0, 512, (20,))
+    pos = torch.arange(20)
+    res = []
+    for fused in (True, False):
+        model.zero_grad(set_to_none=True)
+        ex = Executor(model)
+        ex.fused_layers = fused
+        # two segments: a 8-token prompt whose K/V the 12-token continuation reads
+        h0, st0 = ex.run(ids[:8], pos[:8], [Segment(0, 8, [])])
+        past = st0[0]
+        h1, _ = ex.run(ids[8:], pos[8:], [Segment(0, 12, [([k], [v]) for (k, v) in past])])
+        (h0.square().sum() + h1.pow(3).sum()).backward()
+        res.append((h1.detach(), {n: p.grad.clone() for n, p in model.named_parameters()}))
+    assert torch.equal(res[0][0], res[1][0])
+    for n in res[0][1]:
+        assert torch.equal(res[0][1][n], res[1][1][n]), n

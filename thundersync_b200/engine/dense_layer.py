@@ -1,0 +1,182 @@
+"""One autograd node per dense decoder layer (C16, the per-layer executor op).
+
+A Qwen3 decoder layer is eleven ops (norm, fused QKV projection, QK-norm +
+RoPE, attention, output projection, residual, norm, fused gate/up, SwiGLU,
+down projection, residual). Run as separate autograd nodes, each costs a
+Python ``Function.apply`` in the forward and an engine dispatch plus a Python
+backward in the backward — for short trajectories that host work, not the
+GPU, sets the pace. ``DenseLayer`` runs the same op implementations (their
+``forward``/``backward`` static methods, with a lightweight context object)
+inside a single autograd node: same kernels, same numerics, same gradient
+sink behaviour, one node per layer.
+
+Inputs are the residual stream ``h``, the ancestor K/V chunks of every
+segment (gradient channels to earlier segments and prompts) and the layer's
+parameters; outputs are the new residual stream and the layer's fresh K and
+V for the whole pack (each segment's slice is its state for descendants).
+The reference's layer ops play the same role (src/thundersync/engine/
+streaming.py:2209-2570, ``_SegLayerCkpt`` and friends).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import torch
+
+from thundersync_b200.ops.attention import _ChunkedAttention
+from thundersync_b200.ops.linear import _Linear
+from thundersync_b200.ops.norm import _RMSNorm
+from thundersync_b200.ops.rope import _QKNormRope
+from thundersync_b200.ops.swiglu import _SwiGLU
+
+__all__ = ["DenseLayer", "dense_layer"]
+
+
+class _Ctx:
+    """The parts of an autograd context the op implementations use."""
+
+    __slots__ = ("needs_input_grad", "saved_tensors", "__dict__")
+
+    def __init__(self, needs: tuple[bool, ...]) -> None:
+        self.needs_input_grad = needs
+        self.saved_tensors = ()
+
+    def save_for_backward(self, *tensors) -> None:
+        self.saved_tensors = tensors
+
+
+class DenseLayer(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, pos, inv_freq, meta, *tensors):
+        # meta: (hq, hkv, d, eps, scale, segs, n_past, qkv_fused, gu_fused, has_qk_norm)
+        hq, hkv, d, eps, scale, segs, n_past, qkv_fused, gu_fused, has_qk = meta
+        past = tensors[:n_past]
+        p = list(tensors[n_past:])
+        ln1, wq, wk, wv = p[0], p[1], p[2], p[3]
+        i = 4
+        qn = kn = None
+        if has_qk:
+            qn, kn = p[4], p[5]
+            i = 6
+        wo, ln2, wg, wu, wd = p[i:i + 5]
+        need_w = any(ctx.needs_input_grad[4 + n_past:])
+        t = h.shape[0]
+
+        c_n1 = _Ctx((True, need_w, False, False))
+        x1 = _RMSNorm.forward(c_n1, h, ln1, eps, False)
+        c_qkv = _Ctx((True, False, need_w, need_w, need_w))
+        qkv = _Linear.forward(c_qkv, x1, qkv_fused, wq, wk, wv)
+        c_rope = _Ctx((True, need_w, need_w) + (False,) * 7)
+        q, k, v = _QKNormRope.forward(c_rope, qkv, qn, kn, pos, inv_freq, hq, hkv, d, eps, False)
+        # attention per segment: [ancestor chunks..., own-pack key ranges..., own slice]
+        c_att = []
+        outs = []
+        pi = 0
+        for (s0, s1, npast, kranges) in segs:
+            pk = list(past[pi:pi + npast])
+            pv = list(past[n_past // 2 + pi:n_past // 2 + pi + npast])
+            pi += npast
+            ks = pk + [k[a:b] for a, b in kranges] + [k[s0:s1]]
+            vs = pv + [v[a:b] for a, b in kranges] + [v[s0:s1]]
+            n = len(ks)
+            c = _Ctx((True, False, False) + (True,) * (2 * n))
+            outs.append(_ChunkedAttention.forward(c, q[s0:s1], scale, n, *ks, *vs))
+            c_att.append((c, s0, s1, npast, kranges))
+        covered = sum(b - a for a, b, _, _ in segs)
+        if covered < t:  # pack padding rows: no attention output
+            outs.append(q.new_zeros(t - covered, hq, d))
+        o = outs[0] if len(outs) == 1 else torch.cat(outs, 0)
+        o = o.reshape(t, hq * d)
+        c_o = _Ctx((True, False, need_w))
+        h1 = h + _Linear.forward(c_o, o, None, wo)
+        c_n2 = _Ctx((True, need_w, False, False))
+        x2 = _RMSNorm.forward(c_n2, h1, ln2, eps, False)
+        c_gu = _Ctx((True, False, need_w, need_w))
+        gu = _Linear.forward(c_gu, x2, gu_fused, wg, wu)
+        c_sw = _Ctx((True,))
+        a = _SwiGLU.forward(c_sw, gu)
+        c_dn = _Ctx((True, False, need_w))
+        out = h1 + _Linear.forward(c_dn, a, None, wd)
+        ctx.stages = (c_n1, c_qkv, c_rope, c_att, c_o, c_n2, c_gu, c_sw, c_dn)
+        ctx.meta = meta
+        ctx.t = t
+        return out, k, v
+
+    @staticmethod
+    def backward(ctx, dout, dk_out, dv_out):
+        c_n1, c_qkv, c_rope, c_att, c_o, c_n2, c_gu, c_sw, c_dn = ctx.stages
+        hq, hkv, d, eps, scale, segs, n_past, qkv_fused, gu_fused, has_qk = ctx.meta
+        t = ctx.t
+        # h_out = h1 + down(swiglu(gu(norm2(h1))))
+        da, _, gwd = _Linear.backward(c_dn, dout)
+        dgu = _SwiGLU.backward(c_sw, da)
+        dx2, _, gwg, gwu = _Linear.backward(c_gu, dgu)
+        dh1_n, gln2, _, _ = _RMSNorm.backward(c_n2, dx2)
+        dh1 = dout + dh1_n
+        # h1 = h + o_proj(o)
+        do_, _, gwo = _Linear.backward(c_o, dh1)
+        do_ = do_.reshape(t, hq, d)
+        covered = sum(s1 - s0 for _, s0, s1, _, _ in c_att)
+        single = len(c_att) == 1 and covered == t
+        dq = None if single else torch.zeros(t, hq, d, dtype=do_.dtype, device=do_.device)
+        dk = torch.zeros(t, hkv, d, dtype=do_.dtype, device=do_.device) if dk_out is None else dk_out.clone()
+        dv = torch.zeros(t, hkv, d, dtype=do_.dtype, device=do_.device) if dv_out is None else dv_out.clone()
+        dpast_k: list[Any] = []
+        dpast_v: list[Any] = []
+        for c, s0, s1, npast, kranges in c_att:
+            g = _ChunkedAttention.backward(c, do_[s0:s1])
+            n = npast + len(kranges) + 1
+            gq = g[0]
+            gks = g[3:3 + n]
+            gvs = g[3 + n:3 + 2 * n]
+            if dq is None:
+                dq = gq
+            else:
+                dq[s0:s1] = gq
+            dpast_k.extend(gks[:npast])
+            dpast_v.extend(gvs[:npast])
+            for j, (a, b) in enumerate(kranges):
+                dk[a:b] += gks[npast + j]
+                dv[a:b] += gvs[npast + j]
+            dk[s0:s1] += gks[-1]
+            dv[s0:s1] += gvs[-1]
+        dqkv, gqn, gkn, *_ = _QKNormRope.backward(c_rope, dq, dk, dv)
+        dx1, _, gwq, gwk, gwv = _Linear.backward(c_qkv, dqkv)
+        dh_n, gln1, _, _ = _RMSNorm.backward(c_n1, dx1)
+        dh = dh1 + dh_n
+        ctx.stages = None
+        params = [gln1, gwq, gwk, gwv] + ([gqn, gkn] if has_qk else []) + [gwo, gln2, gwg, gwu, gwd]
+        return (dh, None, None, None, *dpast_k, *dpast_v, *params)
+
+
+def dense_layer(ex, i: int, h: torch.Tensor, pos: torch.Tensor, segs) -> tuple[torch.Tensor, list]:
+    """Run dense attention layer ``i`` of executor ``ex`` as one autograd node; returns (h, per-seg (k, v))."""
+    spec = ex.spec
+    layer = ex.model.model.layers[i]
+    sa, mlp = layer.self_attn, layer.mlp
+    qn = getattr(sa, "q_norm", None)
+    kn = getattr(sa, "k_norm", None)
+    has_qk = qn is not None
+    weights_qkv = [sa.q_proj.weight, sa.k_proj.weight, sa.v_proj.weight]
+    weights_gu = [mlp.gate_proj.weight, mlp.up_proj.weight]
+    arena = ex.arena
+    qkv_fused = arena.fused_weight(weights_qkv) if arena is not None else None
+    gu_fused = arena.fused_weight(weights_gu) if arena is not None else None
+    past_k, past_v, seg_meta = [], [], []
+    for seg in segs:
+        ks, vs = seg.past[i] if seg.past and seg.past[i] is not None else ([], [])
+        past_k.extend(ks)
+        past_v.extend(vs)
+        seg_meta.append((seg.start, seg.start + seg.length, len(ks), tuple(seg.key_ranges)))
+    eps = getattr(layer.input_layernorm, "variance_epsilon", None) or spec.eps
+    meta = (spec.n_heads, spec.n_kv, spec.head_dim, eps, 1.0 / math.sqrt(spec.head_dim), tuple(seg_meta),
+            len(past_k) + len(past_v), qkv_fused, gu_fused, has_qk)
+    params = [layer.input_layernorm.weight, *weights_qkv]
+    if has_qk:
+        params += [qn.weight, kn.weight]
+    params += [sa.o_proj.weight, layer.post_attention_layernorm.weight, *weights_gu, mlp.down_proj.weight]
+    out, k, v = DenseLayer.apply(h, pos, ex.inv_freq(h.device), meta, *past_k, *past_v, *params)
+    new_state = [(k[s.start:s.start + s.length], v[s.start:s.start + s.length]) for s in segs]
+    return out, new_state

@@ -145,6 +145,9 @@ class Executor:
         self.spec = spec_of(model)
         self.arena = arena
         self._inv_freq: dict[torch.device, torch.Tensor] = {}
+        # one autograd node per dense layer (engine/dense_layer.py); False runs op by op
+        self.fused_layers = True
+        self._dense_ok: dict[int, bool] = {}
 
     # ------------------------------------------------------------ pieces
     def inv_freq(self, device: torch.device) -> torch.Tensor:
@@ -176,9 +179,29 @@ class Executor:
         return linear(x, [_weight(m) for m in mods], self.arena)
 
     # ------------------------------------------------------------ layers
+    def _plain_dense(self, layer) -> bool:
+        """A Qwen3 layer the single-node layer op covers (no gate, no LoRA, weight-scaled norms)."""
+        key = id(layer)
+        got = self._dense_ok.get(key)
+        if got is None:
+            sa, mlp = layer.self_attn, layer.mlp
+            mods = [sa.q_proj, sa.k_proj, sa.v_proj, sa.o_proj, mlp.gate_proj, mlp.up_proj, mlp.down_proj]
+            norms = [layer.input_layernorm, layer.post_attention_layernorm]
+            qn = getattr(sa, "q_norm", None)
+            if qn is not None:
+                norms.append(qn)
+            got = (not self.spec.attn_gate and not any(_is_lora(m) for m in mods)
+                   and not any(_is_unit(n) for n in norms))
+            self._dense_ok[key] = got
+        return got
+
     def attention_layer(self, i: int, h: torch.Tensor, pos: torch.Tensor, segs: list[Segment]):
         spec = self.spec
         layer = self.model.model.layers[i]
+        if self.fused_layers and self._plain_dense(layer):
+            from thundersync_b200.engine.dense_layer import dense_layer
+
+            return dense_layer(self, i, h, pos, segs)
         sa = layer.self_attn
         hq, hkv, d = spec.n_heads, spec.n_kv, spec.head_dim
         x = self.norm(layer.input_layernorm, h)
@@ -211,6 +234,9 @@ class Executor:
             kn_, vn_ = k[s0:s1], v[s0:s1]
             outs.append(chunked_attention(q[s0:s1], [*ks, kn_], [*vs, vn_], scale))
             new_state.append((kn_, vn_))
+        covered = sum(seg.length for seg in segs)
+        if covered < qkv.shape[0]:  # pack padding rows: no attention output
+            outs.append(q.new_zeros(qkv.shape[0] - covered, hq, d))
         o = outs[0] if len(outs) == 1 else torch.cat(outs, 0)
         o = o.reshape(o.shape[0], hq * d)
         if gate is not None:

@@ -48,6 +48,9 @@ STREAM_ATTENTION_NAME = "thundersync_stream"
 _LIVE: "list[Any]" = []
 
 
+PACK_ROW_MULTIPLE = 128
+
+
 def register_stream_attention() -> None:
     """Kept for API compatibility with HF-hooked callers.
 
@@ -271,9 +274,22 @@ class StreamingRun:
         return torch.arange(start, start + n, dtype=torch.long, device=self.device)
 
     def _run_pack(self, ids: torch.Tensor, pos: torch.Tensor, segs: list[Segment]):
+        # On CUDA the pack's row count is padded to a multiple of PACK_ROW_MULTIPLE
+        # (token 0 at position 0; no segment covers those rows, so they receive no
+        # attention, produce no state and get zero gradient): every GEMM then
+        # sees one of a few dozen shapes, and the library's per-shape algorithm
+        # selection, which costs hundreds of microseconds of host time for a new
+        # shape, is paid once per shape instead of once per trajectory.
+        t = ids.shape[0]
+        pad = (-t) % PACK_ROW_MULTIPLE if ids.is_cuda else 0
+        if pad:
+            ids = torch.cat((ids, ids.new_zeros(pad)))
+            pos = torch.cat((pos, pos.new_zeros(pad)))
         if self.checkpoint and torch.is_grad_enabled():
-            return self._run_pack_checkpointed(ids, pos, segs)
-        return self.exec.run(ids, pos, segs)
+            h, states = self._run_pack_checkpointed(ids, pos, segs)
+        else:
+            h, states = self.exec.run(ids, pos, segs)
+        return (h[:t] if pad else h), states
 
     def _run_pack_checkpointed(self, ids, pos, segs):
         """Per-layer activation checkpointing; fresh K/V are checkpoint outputs."""

@@ -242,6 +242,9 @@ def gated_deltanet_layer(ex, layer, i: int, h: torch.Tensor, segs):
         core, state = gated_delta_rule(q, k, v, g[s0:s1], beta[s0:s1], state0)
         outs.append(core)
         finals.append((state, tail))
+    covered = sum(seg.length for seg in segs)
+    if covered < h.shape[0]:  # pack padding rows: no mixer output
+        outs.append(outs[0].new_zeros(h.shape[0] - covered, *outs[0].shape[1:]))
     core = outs[0] if len(outs) == 1 else torch.cat(outs, 0)  # [T, Hv, dv]
     t_all = core.shape[0]
     normed = rms_norm(core.reshape(-1, mix.head_v_dim), mix.norm.weight, mix.norm.variance_epsilon)

@@ -44,6 +44,8 @@ class _Counted:
             return fn(*args, **kwargs)
 
         call.__name__ = name
+        # cached on the instance: later lookups skip __getattr__ entirely
+        object.__setattr__(self, name, call)
         return call
 
 

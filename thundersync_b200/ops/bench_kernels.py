@@ -131,9 +131,34 @@ def bench_conv(args) -> None:
     print(f"conv bwd: {ms:.3f} ms")
 
 
+def bench_gemm_host(args) -> None:
+    """Host (CPU) cost of one library GEMM call: repeated shape vs a new row count every call."""
+    import time
+
+    w = torch.randn(6144, 2048, device="cuda", dtype=torch.bfloat16)
+    xs = [torch.randn(1000 + 7 * i, 2048, device="cuda", dtype=torch.bfloat16) for i in range(200)]
+    acc = torch.zeros(6144, 2048, device="cuda", dtype=torch.float32)
+    for name, seq in (("same", [xs[0]] * 200), ("varying", xs)):
+        for fn_name, fn in (("linear", lambda x: torch.nn.functional.linear(x, w)),
+                            ("addmm_fp32", lambda x: torch.addmm(acc, w.new_empty(6144, x.shape[0]).normal_() if False
+                                                                 else torch.empty(6144, x.shape[0], device="cuda",
+                                                                                  dtype=torch.bfloat16), x,
+                                                                 out_dtype=torch.float32, out=acc))):
+            fn(seq[0])
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for x in seq:
+                fn(x)
+            t1 = time.perf_counter()
+            torch.cuda.synchronize()
+            t2 = time.perf_counter()
+            print(f"{fn_name:10s} {name:8s}: host {1e6 * (t1 - t0) / len(seq):7.1f} us/call, "
+                  f"device+host {1e6 * (t2 - t0) / len(seq):7.1f} us/call")
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv"])
+    ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host"])
     ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
     ap.add_argument("--t", type=int, default=2048)
     ap.add_argument("--s", type=int, default=2560)
@@ -146,7 +171,8 @@ def main(argv=None) -> None:
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--trace", action="store_true", help="print the dK/dV kernel's per-step timeline")
     args = ap.parse_args(argv)
-    {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv}[args.family](args)
+    {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
+     "gemm_host": bench_gemm_host}[args.family](args)
 
 
 if __name__ == "__main__":

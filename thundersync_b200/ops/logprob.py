@@ -142,14 +142,31 @@ def _check(hidden, weight, target):
         raise ValueError(f"weight {tuple(weight.shape)} does not match hidden dim {hidden.shape[1]}")
 
 
+ROW_MULTIPLE = 128
+
+
+def _padded(hidden, target):
+    """On CUDA, zero-pad the rows to a multiple of ROW_MULTIPLE (the GEMM shapes then repeat)."""
+    n = hidden.shape[0]
+    pad = (-n) % ROW_MULTIPLE if hidden.is_cuda else 0
+    if not pad:
+        return hidden, target, n, 0
+    return (torch.cat((hidden, hidden.new_zeros(pad, hidden.shape[1]))),
+            torch.cat((target, target.new_zeros(pad))), n, pad)
+
+
 def lm_head_logprob(hidden, weight, target, *, rows: int = DEFAULT_ROWS):
     _check(hidden, weight, target)
-    return _LMHeadLogprob.apply(hidden, weight, target, rows, False)
+    h, t, n, pad = _padded(hidden, target)
+    lp = _LMHeadLogprob.apply(h, weight, t, rows, False)
+    return lp[:n] if pad else lp
 
 
 def lm_head_logprob_entropy(hidden, weight, target, *, rows: int = DEFAULT_ROWS):
     _check(hidden, weight, target)
-    return _LMHeadLogprob.apply(hidden, weight, target, rows, True)
+    h, t, n, pad = _padded(hidden, target)
+    lp, ent = _LMHeadLogprob.apply(h, weight, t, rows, True)
+    return (lp[:n], ent[:n]) if pad else (lp, ent)
 
 
 def naive_logprob(hidden, weight, target):
