@@ -95,6 +95,23 @@ TS_DEVICE void tmem_ld32(uint32_t addr, float* v) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+TS_DEVICE void tmem_ld16(uint32_t addr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(addr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// cols = 32 or 16 columns of this warp's 32 lanes
+template <int COLS>
+TS_DEVICE void tmem_ld(uint32_t addr, float* v) {
+  static_assert(COLS == 32 || COLS == 16, "tmem_ld covers 16 or 32 columns");
+  if constexpr (COLS == 32) tmem_ld32(addr, v);
+  else tmem_ld16(addr, v);
+}
 TS_DEVICE void tmem_st32(uint32_t addr, const float* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"

@@ -67,3 +67,26 @@ def test_hybrid_gpu_streamed_grpo_matches_fp32_oracle():
         if e > 0.08:
             bad.append((n, e))
     assert not bad, bad
+
+
+def test_hybrid_gpu_head_dim_256():
+    """The config-5 attention geometry (head_dim 256, partial rotary) on the GPU kernels."""
+    cfg = CFG.with_(head_dim=256, num_attention_heads=4, num_key_value_heads=1)
+    torch.manual_seed(1)
+    ref_model = HybridForCausalLM(cfg)
+    model = copy.deepcopy(ref_model).to("cuda", torch.bfloat16)
+    rng = random.Random(9)
+    prompt = [rng.randrange(1024) for _ in range(100)]
+    turns = [([rng.randrange(1024) for _ in range(150)], [True] * 150)]
+    run = StreamingRun(model, boundary_cut=True)
+    bw = RewardLinearBackward(run, model)
+    bw.open_group(0, prompt, [0, 1])
+    for tid in (0, 1):
+        run.append_turn(0, tid, turns[0][0][: 150 - 40 * tid], [True] * (150 - 40 * tid))
+        got = run.logprobs(tid).float().cpu()
+        want = _lp(ref_model, prompt, [(turns[0][0][: 150 - 40 * tid], [True] * (150 - 40 * tid))]).detach()
+        assert (got - want).abs().max().item() < 0.15
+        bw.close_trajectory(tid, float(tid))
+    bw.close_group(0)
+    bw.assert_safe_to_step()
+    assert all(p.grad is None or torch.isfinite(p.grad).all() for p in model.parameters())

@@ -88,6 +88,8 @@ def test_swiglu():
 
 ATTN_CASES = [
     (64, 64, 4, 2, 128),
+    (130, 300, 4, 2, 256),
+    (257, 257, 2, 1, 256),
     (100, 612, 8, 2, 128),
     (1, 300, 4, 4, 64),
     (257, 257, 2, 1, 64),
