@@ -64,8 +64,10 @@ __device__ long long g_attn_trace[4 * 128 * 8];
 
 template <int D>
 struct FwdLayout {
-  static constexpr int BM = 128, BN = 128;
-  static constexpr int NB = D / 64;  // 64-column boxes per row
+  // D = 256 halves the key tile so two K/V stages still fit in shared memory
+  static constexpr int BM = 128, BN = D <= 128 ? 128 : 64;
+  static constexpr int HALF = BN / 2;  // key columns each softmax warp of a pair exponentiates
+  static constexpr int NB = D / 64;    // 64-column boxes per row
   static constexpr uint32_t Q = 0;
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t K_BYTES = BN * D * 2;
@@ -79,6 +81,7 @@ struct FwdLayout {
   // TMEM columns
   static constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256;
 };
+static_assert(FwdLayout<256>::TOTAL + 1024 <= 232448, "forward shared memory exceeds 227 KB");
 
 struct FwdBars {
   uint64_t q, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv;
@@ -161,9 +164,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         const uint32_t kb = sbase + L::K0 + s * L::K_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t boff = (kk >> 2) * 128 * 128 + (kk & 3) * 32;
-          const uint64_t a = tc::sdesc_sw128(sbase + L::Q + boff, 16, 1024);
-          const uint64_t b = tc::sdesc_sw128(kb + boff, 16, 1024);
+          const uint32_t qoff = (kk >> 2) * L::BM * 128 + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * L::BN * 128 + (kk & 3) * 32;
+          const uint64_t a = tc::sdesc_sw128(sbase + L::Q + qoff, 16, 1024);
+          const uint64_t b = tc::sdesc_sw128(kb + koff, 16, 1024);
           tc::mma_bf16(tmem + (s ? L::S_COL1 : L::S_COL0), a, b, id_s, kk > 0);
         }
         tc::mma_commit(&bars->s_full[s]);
@@ -180,7 +184,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         const uint32_t vb = sbase + L::V0 + s * L::K_BYTES;
 #pragma unroll
         for (int kk = 0; kk < L::BN / 16; ++kk) {
-          const uint64_t a = tc::sdesc_sw128(pb + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = tc::sdesc_sw128(pb + (kk >> 2) * L::BM * 128 + (kk & 3) * 32, 16, 1024);
           const uint64_t b = tc::sdesc_sw128(vb + kk * 16 * 128, L::BN * 128, 1024);
           tc::mma_bf16(tmem + L::O_COL, a, b, id_o, j > 0 || kk > 0);
         }
@@ -206,10 +210,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       const int s = j & 1;
       if (!warp_wait(&bars->s_full[s], (j >> 1) & 1, abort, err, 31)) { ok = false; break; }
       tc::tc_fence_after();
-      float sv[128];
+      float sv[L::BN];
       const uint32_t scol = s ? L::S_COL1 : L::S_COL0;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tc::tmem_ld32(lane_base + scol + c * 32, sv + c * 32);
+      for (int c = 0; c < L::BN / 32; ++c) tc::tmem_ld32(lane_base + scol + c * 32, sv + c * 32);
       tc::tmem_ld_wait();
       const int k0 = j * L::BN;
       int nvis = min(lim, S - 1) - k0 + 1;  // visible columns of this tile for this row
@@ -217,23 +221,23 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       float raw = -INFINITY;
       if (nvis == L::BN) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) raw = fmaxf(raw, sv[i]);
+        for (int i = 0; i < L::BN; ++i) raw = fmaxf(raw, sv[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) raw = fmaxf(raw, i < nvis ? sv[i] : -INFINITY);
+        for (int i = 0; i < L::BN; ++i) raw = fmaxf(raw, i < nvis ? sv[i] : -INFINITY);
       }
       const float mx = fmaxf(m, raw * sl2);
       const float ref = mx == -INFINITY ? 0.f : mx;
       const float alpha = exp2f(m - ref);
-      // this warp's 64-column half, reloaded into registers with static indices
-      tc::tmem_ld32(lane_base + scol + hc * 64, sv);
-      tc::tmem_ld32(lane_base + scol + hc * 64 + 32, sv + 32);
+      // this warp's half of the tile's columns, reloaded into registers with static indices
+#pragma unroll
+      for (int c = 0; c < L::HALF / 32; ++c) tc::tmem_ld32(lane_base + scol + hc * L::HALF + c * 32, sv + c * 32);
       tc::tmem_ld_wait();
-      const int nv_half = nvis - hc * 64;
+      const int nv_half = nvis - hc * L::HALF;
       float rs = 0.f;
       const uint32_t pbase = sbase + L::P0 + s * L::P_BYTES;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
+      for (int c8 = 0; c8 < L::HALF / 8; ++c8) {
         float p[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -241,7 +245,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
           p[e] = i < nv_half ? ex2(fmaf(sv[i], sl2, -ref)) : 0.f;
           rs += p[e];
         }
-        st_shared_v4(pbase + tc::kmajor_off(r, hc * 64 + c8 * 8, 128), pack2(p[0], p[1]), pack2(p[2], p[3]),
+        st_shared_v4(pbase + tc::kmajor_off(r, hc * L::HALF + c8 * 8, 128), pack2(p[0], p[1]), pack2(p[2], p[3]),
                      pack2(p[4], p[5]), pack2(p[6], p[7]));
       }
       l = l * alpha + rs;
@@ -322,32 +326,56 @@ __global__ void attn_delta_kernel(const bf16* __restrict__ o, const bf16* __rest
   if (lane == 0) delta[(long long)h * T + i] = s;
 }
 
+// Sum of the per-split fp32 dK/dV partials in split order, scaled and rounded to bf16.
+__global__ void attn_split_sum_kernel(const float* __restrict__ part, bf16* __restrict__ out, long long n,
+                                      int nsplit, float scale) {
+  const long long i4 = (blockIdx.x * (long long)blockDim.x + threadIdx.x) * 4;
+  if (i4 >= n) return;
+  float4 acc = *reinterpret_cast<const float4*>(part + i4);
+  for (int z = 1; z < nsplit; ++z) {
+    const float4 v = *reinterpret_cast<const float4*>(part + (long long)z * n + i4);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  uint2 o;
+  o.x = pack2(acc.x * scale, acc.y * scale);
+  o.y = pack2(acc.z * scale, acc.w * scale);
+  *reinterpret_cast<uint2*>(out + i4) = o;
+}
+
 // dK/dV: CTA = 128 keys of one KV head; thread r of warps 0-3 owns key row r.
 // Per step (query head, 64-query tile): S^T = K Q^T and dP^T = V dO^T into a
 // TMEM buffer pair; the compute warps form P^T = exp2(S^T*sl2 - lse2) and
 // dS^T = P^T (dP^T - delta) as bf16 K-major tiles; the MMA thread accumulates
 // dV += P^T dO and dK += dS^T Q into TMEM, which hold them across all steps.
-// Q/dO tiles run NQ = 3 stages ahead so their TMA latency stays off the MMA
+// Q/dO tiles run NQ stages ahead so their TMA latency stays off the MMA
 // thread's critical path; P^T/dS^T and the TMEM S^T/dP^T pairs are double
-// buffered.
-template <int D>
+// buffered. MODE 0 accumulates dK and dV together (head dims up to 128); for
+// D = 256 the two accumulators alone fill TMEM, so MODE 1 (dK) and MODE 2 (dV)
+// run as two launches over 32-query tiles, each keeping only the tile it needs.
+template <int D, int MODE = 0>
 struct DkvLayout {
-  static constexpr int BN = 128, BQ = 64, NB = D / 64, NQ = 3;
+  static constexpr int BN = 128, BQ = D <= 128 ? 64 : 32, NB = D / 64, NQ = D <= 128 ? 3 : 2;
+  static constexpr int CW = BQ / 2;                          // query columns per compute warp
+  static constexpr bool WANT_DK = MODE != 2, WANT_DV = MODE != 1;
+  static constexpr bool WANT_P = WANT_DV, WANT_DS = WANT_DK;
   static constexpr uint32_t KV_BYTES = BN * D * 2;
   static constexpr uint32_t QT_BYTES = BQ * D * 2;
   static constexpr uint32_t K = 0, V = KV_BYTES;
   static constexpr uint32_t Q0 = 2 * KV_BYTES;               // [NQ] Q tiles
   static constexpr uint32_t O0 = Q0 + NQ * QT_BYTES;         // [NQ] dO tiles
-  static constexpr uint32_t P0 = O0 + NQ * QT_BYTES;         // [2] P^T tiles (128 x 64 bf16)
-  static constexpr uint32_t PT_BYTES = BN * BQ * 2;
-  static constexpr uint32_t DS0 = P0 + 2 * PT_BYTES;         // [2] dS^T tiles
-  static constexpr uint32_t LD0 = DS0 + 2 * PT_BYTES;        // [NQ][2][BQ] floats: lse2, delta
+  static constexpr uint32_t PT_BYTES = BN * 64 * 2;          // one 128-byte-row K-major tile
+  static constexpr uint32_t P0 = O0 + NQ * QT_BYTES;         // [2] P^T tiles
+  static constexpr uint32_t DS0 = P0 + (WANT_P ? 2 * PT_BYTES : 0);  // [2] dS^T tiles
+  static constexpr uint32_t LD0 = DS0 + (WANT_DS ? 2 * PT_BYTES : 0);  // [NQ][2][BQ] floats: lse2, delta
   static constexpr uint32_t BAR = LD0 + NQ * 2 * BQ * 4;
   static constexpr uint32_t TOTAL = BAR + 256;
-  static constexpr uint32_t DK_COL = 0, DV_COL = D, ST_COL0 = 2 * D;  // ST/DPT pairs follow
+  static constexpr uint32_t DK_COL = 0, DV_COL = MODE == 0 ? D : 0;
+  static constexpr uint32_t ST_COL0 = MODE == 0 ? 2 * D : D;  // ST/DPT pairs follow
 };
 
 static_assert(DkvLayout<128>::TOTAL + 1024 <= 232448, "dK/dV shared memory exceeds 227 KB");
+static_assert(DkvLayout<256, 1>::TOTAL + 1024 <= 232448, "dK shared memory exceeds 227 KB");
+static_assert(DkvLayout<256, 2>::TOTAL + 1024 <= 232448, "dV shared memory exceeds 227 KB");
 
 struct DkvBars {
   uint64_t kv, q_full[3], q_empty[3], s_full[2], p_full[2], mma_done[2], fin;
@@ -355,19 +383,24 @@ struct DkvBars {
   int abort;
 };
 
-template <int D>
+template <int D, int MODE>
 __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
     const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dk, bf16* __restrict__ dv,
-    int T, int S, int Hq, int Hkv, float scale, int* __restrict__ err) {
-  using L = DkvLayout<D>;
+    float* __restrict__ part_k, float* __restrict__ part_v, int T, int S, int Hq, int Hkv, float scale,
+    int* __restrict__ err) {
+  using L = DkvLayout<D, MODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   DkvBars* bars = reinterpret_cast<DkvBars*>(smem + L::BAR);
   const uint32_t sbase = tc::smem_addr(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hk = blockIdx.y, grp = Hq / Hkv;
+  // blockIdx.z splits the query heads of this KV head across CTAs; with more
+  // than one split each CTA writes fp32 partial sums that a second kernel adds
+  // in split order (deterministic) and rounds.
+  const int hk = blockIdx.y, nsplit = gridDim.z, grp = Hq / Hkv / nsplit;
+  const int hbase = hk * (Hq / Hkv) + blockIdx.z * grp;
   const int k0 = blockIdx.x * L::BN;
   const int off = S - T;
   const float sl2 = scale * kLog2e;
@@ -378,7 +411,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
   const int total = n_qt * grp;
   volatile int* abort = &bars->abort;
   float* ld = reinterpret_cast<float*>(smem + L::LD0);
-  const bool trace = g_attn_trace_on && blockIdx.x == 0 && blockIdx.y == 0;
+  const bool trace = g_attn_trace_on && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(&bars->kv, 1);
@@ -403,10 +436,11 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
   if (warp == 8) {
     // producer: K, V once; per step Q and dO tiles (TMA) plus lse2 / delta (plain loads)
     if (lane == 0) {
-      tc::mbar_expect_tx(&bars->kv, 2 * L::KV_BYTES);
+      tc::mbar_expect_tx(&bars->kv, (L::WANT_DK ? 2 : 1) * L::KV_BYTES);
       for (int b = 0; b < L::NB; ++b) {
         tc::tma_load_2d(smem + L::K + b * L::BN * 128, &tm_k, hk * D + b * 64, k0, &bars->kv);
-        tc::tma_load_2d(smem + L::V + b * L::BN * 128, &tm_v, hk * D + b * 64, k0, &bars->kv);
+        if constexpr (L::WANT_DK)
+          tc::tma_load_2d(smem + L::V + b * L::BN * 128, &tm_v, hk * D + b * 64, k0, &bars->kv);
       }
     }
     for (int i = 0; i < total; ++i) {
@@ -414,7 +448,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
       if (lane == 0) TS_TRACE(0, i, 0);
       if (i >= L::NQ && !warp_wait(&bars->q_empty[qs], ((i - L::NQ) / L::NQ) & 1, abort, err, 51)) break;
       if (lane == 0) TS_TRACE(0, i, 1);
-      const int hh = hk * grp + i / n_qt;
+      const int hh = hbase + i / n_qt;
       const int qt = qstart + (i % n_qt) * L::BQ;
       if (lane == 0) {
         tc::mbar_expect_tx(&bars->q_full[qs], 2 * L::QT_BYTES);
@@ -453,8 +487,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
           const uint32_t q_off = (kk >> 2) * L::BQ * 128 + (kk & 3) * 32;
           tc::mma_bf16(tmem + col, tc::sdesc_sw128(sbase + L::K + kv_off, 16, 1024),
                        tc::sdesc_sw128(qb + q_off, 16, 1024), id_s, kk > 0);
-          tc::mma_bf16(tmem + col + L::BQ, tc::sdesc_sw128(sbase + L::V + kv_off, 16, 1024),
-                       tc::sdesc_sw128(ob + q_off, 16, 1024), id_s, kk > 0);
+          if constexpr (L::WANT_DK)
+            tc::mma_bf16(tmem + col + L::BQ, tc::sdesc_sw128(sbase + L::V + kv_off, 16, 1024),
+                         tc::sdesc_sw128(ob + q_off, 16, 1024), id_s, kk > 0);
         }
         tc::mma_commit(&bars->s_full[st]);
         TS_TRACE(1, i, 5);
@@ -476,8 +511,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
           const uint64_t ad = tc::sdesc_sw128(db + kk * 32, 16, 1024);
           const uint64_t bo = tc::sdesc_sw128(ob + kk * 16 * 128, L::BQ * 128, 1024);
           const uint64_t bq = tc::sdesc_sw128(qb + kk * 16 * 128, L::BQ * 128, 1024);
-          tc::mma_bf16(tmem + L::DV_COL, ap, bo, id_acc, i > 0 || kk > 0);
-          tc::mma_bf16(tmem + L::DK_COL, ad, bq, id_acc, i > 0 || kk > 0);
+          if constexpr (L::WANT_DV) tc::mma_bf16(tmem + L::DV_COL, ap, bo, id_acc, i > 0 || kk > 0);
+          if constexpr (L::WANT_DK) tc::mma_bf16(tmem + L::DK_COL, ad, bq, id_acc, i > 0 || kk > 0);
         }
         tc::mma_commit(&bars->mma_done[st]);
         tc::mma_commit(&bars->q_empty[qs]);
@@ -506,39 +541,42 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
       if (i >= 2 && !warp_wait(&bars->mma_done[st], ((i - 2) >> 1) & 1, abort, err, 73)) { ok = false; break; }
       if (tw) TS_TRACE(2, i, 3);
       tc::tc_fence_after();
-      float sv[32], dp[32];
-      const uint32_t col = L::ST_COL0 + st * 2 * L::BQ + hc * 32;
-      tc::tmem_ld32(lane_base + col, sv);
-      tc::tmem_ld32(lane_base + col + L::BQ, dp);
+      constexpr int CW = L::CW;
+      float sv[CW], dp[CW];
+      const uint32_t col = L::ST_COL0 + st * 2 * L::BQ + hc * CW;
+      tc::tmem_ld<CW>(lane_base + col, sv);
+      if constexpr (L::WANT_DK) tc::tmem_ld<CW>(lane_base + col + L::BQ, dp);
       tc::tmem_ld_wait();
       if (tw) TS_TRACE(2, i, 4);
-      // this step's 32 query columns: lse2 and delta into registers (broadcast
+      // this step's query columns: lse2 and delta into registers (broadcast
       // shared loads), and the visible range [lo, hi) of column indices
-      float l2[32], dl[32];
-      const float4* l2v = reinterpret_cast<const float4*>(ld + (qs * 2 + 0) * L::BQ + hc * 32);
-      const float4* dlv = reinterpret_cast<const float4*>(ld + (qs * 2 + 1) * L::BQ + hc * 32);
+      float l2[CW], dl[CW];
+      const float4* l2v = reinterpret_cast<const float4*>(ld + (qs * 2 + 0) * L::BQ + hc * CW);
+      const float4* dlv = reinterpret_cast<const float4*>(ld + (qs * 2 + 1) * L::BQ + hc * CW);
 #pragma unroll
-      for (int x = 0; x < 8; ++x) {
+      for (int x = 0; x < CW / 4; ++x) {
         const float4 a = l2v[x], b = dlv[x];
         l2[4 * x] = a.x; l2[4 * x + 1] = a.y; l2[4 * x + 2] = a.z; l2[4 * x + 3] = a.w;
         dl[4 * x] = b.x; dl[4 * x + 1] = b.y; dl[4 * x + 2] = b.z; dl[4 * x + 3] = b.w;
       }
-      const int qc0 = qt + hc * 32;
-      const int lo = kr < S ? kr - off - qc0 : 32;  // query qc0+c sees key kr iff c >= lo
+      const int qc0 = qt + hc * CW;
+      const int lo = kr < S ? kr - off - qc0 : CW;  // query qc0+c sees key kr iff c >= lo
       const int hi = T - qc0;                       // and c < hi (query exists)
       const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
 #pragma unroll
-      for (int c8 = 0; c8 < 4; ++c8) {
+      for (int c8 = 0; c8 < CW / 8; ++c8) {
         float p[8], ds[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int c = c8 * 8 + e;
           p[e] = (c >= lo && c < hi) ? ex2(fmaf(sv[c], sl2, -l2[c])) : 0.f;
-          ds[e] = p[e] * (dp[c] - dl[c]);
+          if constexpr (L::WANT_DK) ds[e] = p[e] * (dp[c] - dl[c]);
         }
-        const uint32_t o8 = tc::kmajor_off(r, hc * 32 + c8 * 8, 128);
-        st_shared_v4(pb + o8, pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]), pack2(p[6], p[7]));
-        st_shared_v4(db + o8, pack2(ds[0], ds[1]), pack2(ds[2], ds[3]), pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
+        const uint32_t o8 = tc::kmajor_off(r, hc * CW + c8 * 8, 128);
+        if constexpr (L::WANT_P)
+          st_shared_v4(pb + o8, pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]), pack2(p[6], p[7]));
+        if constexpr (L::WANT_DS)
+          st_shared_v4(db + o8, pack2(ds[0], ds[1]), pack2(ds[2], ds[3]), pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
       }
       if (tw) TS_TRACE(2, i, 5);
       tc::fence_async_smem();
@@ -551,28 +589,50 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
 #pragma unroll
       for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
         float a[32], b[32];
-        tc::tmem_ld32(lane_base + L::DK_COL + c * 32, a);
-        tc::tmem_ld32(lane_base + L::DV_COL + c * 32, b);
+        if constexpr (L::WANT_DK) tc::tmem_ld32(lane_base + L::DK_COL + c * 32, a);
+        if constexpr (L::WANT_DV) tc::tmem_ld32(lane_base + L::DV_COL + c * 32, b);
         tc::tmem_ld_wait();
-        if (kr < S) {
+        if (kr < S && nsplit > 1) {
+          const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 4) {
+            if constexpr (L::WANT_DK)
+              *reinterpret_cast<float4*>(part_k + o + x) = make_float4(a[x], a[x + 1], a[x + 2], a[x + 3]);
+            if constexpr (L::WANT_DV)
+              *reinterpret_cast<float4*>(part_v + o + x) = make_float4(b[x], b[x + 1], b[x + 2], b[x + 3]);
+          }
+        } else if (kr < S) {
           bf16* pk = dk + ((long long)kr * Hkv + hk) * D + c * 32;
           bf16* pv = dv + ((long long)kr * Hkv + hk) * D + c * 32;
 #pragma unroll
           for (int x = 0; x < 32; x += 8) {
-            uint4 u, w;
-            u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
-            u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
-            w.x = pack2(b[x], b[x + 1]); w.y = pack2(b[x + 2], b[x + 3]);
-            w.z = pack2(b[x + 4], b[x + 5]); w.w = pack2(b[x + 6], b[x + 7]);
-            *reinterpret_cast<uint4*>(pk + x) = u;
-            *reinterpret_cast<uint4*>(pv + x) = w;
+            if constexpr (L::WANT_DK) {
+              uint4 u;
+              u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
+              u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
+              *reinterpret_cast<uint4*>(pk + x) = u;
+            }
+            if constexpr (L::WANT_DV) {
+              uint4 w;
+              w.x = pack2(b[x], b[x + 1]); w.y = pack2(b[x + 2], b[x + 3]);
+              w.z = pack2(b[x + 4], b[x + 5]); w.w = pack2(b[x + 6], b[x + 7]);
+              *reinterpret_cast<uint4*>(pv + x) = w;
+            }
           }
         }
       }
+    } else if (ok && total == 0 && kr < S && nsplit > 1) {
+      const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D;
+      for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 4) {
+        if constexpr (L::WANT_DK) *reinterpret_cast<float4*>(part_k + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+        if constexpr (L::WANT_DV) *reinterpret_cast<float4*>(part_v + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     } else if (ok && total == 0 && kr < S) {
       for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 8) {
-        *reinterpret_cast<uint4*>(dk + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(dv + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
+        if constexpr (L::WANT_DK)
+          *reinterpret_cast<uint4*>(dk + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
+        if constexpr (L::WANT_DV)
+          *reinterpret_cast<uint4*>(dv + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
       }
     }
   }
@@ -592,20 +652,23 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
 // S/dP pairs are double buffered.
 template <int D>
 struct DqLayout {
-  static constexpr int BM = 128, BN = 64, NB = D / 64, NK = 4;
+  // D = 256: 32-key tiles and 2 stages keep Q, dO and the K/V ring inside 227 KB
+  static constexpr int BM = 128, BN = D <= 128 ? 64 : 32, NB = D / 64, NK = D <= 128 ? 4 : 2;
+  static constexpr int CW = BN / 2;  // key columns per compute warp
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KT_BYTES = BN * D * 2;
   static constexpr uint32_t Q = 0, O = Q_BYTES;
   static constexpr uint32_t K0 = 2 * Q_BYTES;             // [NK] K tiles
   static constexpr uint32_t V0 = K0 + NK * KT_BYTES;      // [NK] V tiles
-  static constexpr uint32_t DS0 = V0 + NK * KT_BYTES;     // [2] dS tiles (128 x 64)
-  static constexpr uint32_t DS_BYTES = BM * BN * 2;
+  static constexpr uint32_t DS0 = V0 + NK * KT_BYTES;     // [2] dS tiles (128 rows of 128 bytes)
+  static constexpr uint32_t DS_BYTES = BM * 64 * 2;
   static constexpr uint32_t BAR = DS0 + 2 * DS_BYTES;
   static constexpr uint32_t TOTAL = BAR + 256;
   static constexpr uint32_t DQ_COL = 0, S_COL0 = D;
 };
 
 static_assert(DqLayout<128>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
+static_assert(DqLayout<256>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
 
 struct DqBars {
   uint64_t q, kv_full[4], kv_empty[4], s_full[2], p_full[2], mma_done[2], fin;
@@ -731,17 +794,18 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
       if (!warp_wait(&bars->s_full[st], (j >> 1) & 1, abort, err, 101)) { ok = false; break; }
       if (j >= 2 && !warp_wait(&bars->mma_done[st], ((j - 2) >> 1) & 1, abort, err, 102)) { ok = false; break; }
       tc::tc_fence_after();
-      float sv[32], dp[32];
-      const uint32_t col = L::S_COL0 + st * 2 * L::BN + hc * 32;
-      tc::tmem_ld32(lane_base + col, sv);
-      tc::tmem_ld32(lane_base + col + L::BN, dp);
+      constexpr int CW = L::CW;
+      float sv[CW], dp[CW];
+      const uint32_t col = L::S_COL0 + st * 2 * L::BN + hc * CW;
+      tc::tmem_ld<CW>(lane_base + col, sv);
+      tc::tmem_ld<CW>(lane_base + col + L::BN, dp);
       tc::tmem_ld_wait();
-      const int k0 = j * L::BN + hc * 32;
+      const int k0 = j * L::BN + hc * CW;
       // key k0+c is visible iff c < nvis (key <= lim, key < S, query exists)
       const int nvis = qi < T ? min(lim, S - 1) - k0 + 1 : 0;
       const uint32_t db = sbase + L::DS0 + st * L::DS_BYTES;
 #pragma unroll
-      for (int c8 = 0; c8 < 4; ++c8) {
+      for (int c8 = 0; c8 < CW / 8; ++c8) {
         float ds[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -749,7 +813,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
           const float p = c < nvis ? ex2(fmaf(sv[c], sl2, -l2)) : 0.f;
           ds[e] = p * (dp[c] - dl);
         }
-        st_shared_v4(db + tc::kmajor_off(r, hc * 32 + c8 * 8, 128), pack2(ds[0], ds[1]), pack2(ds[2], ds[3]),
+        st_shared_v4(db + tc::kmajor_off(r, hc * CW + c8 * 8, 128), pack2(ds[0], ds[1]), pack2(ds[2], ds[3]),
                      pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
       }
       tc::fence_async_smem();
@@ -928,8 +992,9 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
   auto lse = at::empty({Hq, T}, q.options().dtype(at::kFloat));
   if (T == 0) return {o, lse};
   CUtensorMap mq = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
-  CUtensorMap mk = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
-  CUtensorMap mv = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
+  const uint32_t kv_rows = D <= 128 ? 128 : 64;
+  CUtensorMap mk = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, kv_rows);
+  CUtensorMap mv = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, kv_rows);
   dim3 grid((T + 127) / 128, Hq);
   const float sl2 = (float)scale * kLog2e;
   int* err = tc_error_flag(q.device()).data_ptr<int>();
@@ -943,8 +1008,13 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
     TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attn_fwd_tc_kernel<64><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
                                                           S, Hq, Hkv, sl2, err);
+  } else if (D == 256) {
+    const int smem = FwdLayout<256>::TOTAL + 1024;
+    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attn_fwd_tc_kernel<256><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
+                                                           S, Hq, Hkv, sl2, err);
   } else {
-    TS_CHECK(false, "tcgen05 attention supports head_dim 64 and 128");
+    TS_CHECK(false, "tcgen05 attention supports head_dim 64, 128 and 256");
   }
   TS_LAUNCH_CHECK();
   return {o, lse};
@@ -966,6 +1036,52 @@ at::Tensor attn_trace_read() {
   return out;
 }
 
+namespace {
+template <int D, int MODE>
+void launch_dkdv(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+                 const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dk, at::Tensor& dv, int T, int S, int Hq,
+                 int Hkv, double scale, int* err) {
+  // split the query heads of a KV head across CTAs while the grid is under one
+  // wave of SMs (the split costs an fp32 partial round trip and a sum kernel,
+  // which a grid of a wave or more does not win back)
+  const int grp = Hq / Hkv;
+  const int want = sm_count(dk.get_device());
+  int nsplit = 1;
+  while (nsplit * 2 <= grp && grp % (nsplit * 2) == 0 && (int)(g.x * g.y) * nsplit < want) nsplit *= 2;
+  g.z = nsplit;
+  at::Tensor pk, pv;
+  float* ppk = nullptr;
+  float* ppv = nullptr;
+  if (nsplit > 1) {
+    if (MODE != 2) pk = at::empty({nsplit, S, Hkv, D}, dk.options().dtype(at::kFloat)), ppk = pk.data_ptr<float>();
+    if (MODE != 1) pv = at::empty({nsplit, S, Hkv, D}, dv.options().dtype(at::kFloat)), ppv = pv.data_ptr<float>();
+  }
+  const int smem = DkvLayout<D, MODE>::TOTAL + 1024;
+  TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<D, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem));
+  attn_bwd_dkdv_tc_kernel<D, MODE><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
+                                                               delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
+                                                               (bf16*)dv.data_ptr(), ppk, ppv, T, S, Hq, Hkv,
+                                                               (float)scale, err);
+  if (nsplit > 1) {
+    const long long n = (long long)S * Hkv * D;
+    const int blocks = (int)((n / 4 + 255) / 256);
+    if (ppk) attn_split_sum_kernel<<<blocks, 256, 0, stream()>>>(ppk, (bf16*)dk.data_ptr(), n, nsplit, (float)scale);
+    if (ppv) attn_split_sum_kernel<<<blocks, 256, 0, stream()>>>(ppv, (bf16*)dv.data_ptr(), n, nsplit, 1.f);
+  }
+}
+
+template <int D>
+void launch_dq(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+               const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, int T, int S, int Hq, int Hkv,
+               double scale, int* err) {
+  const int smem = DqLayout<D>::TOTAL + 1024;
+  TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  attn_bwd_dq_tc_kernel<D><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(), delta.data_ptr<float>(),
+                                                       (bf16*)dq.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
+}
+}  // namespace
+
 std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                     const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale) {
   check_cuda(q, "q");
@@ -976,7 +1092,7 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
   check_cuda(lse, "lse");
   const c10::cuda::CUDAGuard guard(q.device());
   const int T = q.size(0), Hq = q.size(1), D = q.size(2), S = k.size(0), Hkv = k.size(1);
-  TS_CHECK(S >= T && Hq % Hkv == 0 && (D == 64 || D == 128), "attention backward shapes");
+  TS_CHECK(S >= T && Hq % Hkv == 0 && (D == 64 || D == 128 || D == 256), "attention backward shapes");
   auto dq = at::empty_like(q);
   auto dk = at::empty_like(k);
   auto dv = at::empty_like(v);
@@ -987,35 +1103,27 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
                                                                   (const bf16*)dout.data_ptr(),
                                                                   delta.data_ptr<float>(), T, Hq, D);
   int* err = tc_error_flag(q.device()).data_ptr<int>();
-  CUtensorMap mq64 = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 64);
-  CUtensorMap mo64 = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 64);
+  const uint32_t bq = D <= 128 ? 64 : 32;   // dK/dV query tile
+  const uint32_t bn = D <= 128 ? 64 : 32;   // dQ key tile
+  CUtensorMap mq_t = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, bq);
+  CUtensorMap mo_t = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, bq);
   CUtensorMap mk128 = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
   CUtensorMap mv128 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
   CUtensorMap mq128 = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
   CUtensorMap mo128 = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
-  CUtensorMap mk64 = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
-  CUtensorMap mv64 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
+  CUtensorMap mk_t = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, bn);
+  CUtensorMap mv_t = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, bn);
   dim3 g1((S + 127) / 128, Hkv), g2((T + 127) / 128, Hq);
   if (D == 128) {
-    const int s1 = DkvLayout<128>::TOTAL + 1024, s2 = DqLayout<128>::TOTAL + 1024;
-    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
-    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
-    attn_bwd_dkdv_tc_kernel<128><<<g1, 320, s1, stream()>>>(mq64, mk128, mv128, mo64, lse.data_ptr<float>(),
-                                                            delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
-                                                            (bf16*)dv.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
-    attn_bwd_dq_tc_kernel<128><<<g2, 320, s2, stream()>>>(mq128, mk64, mv64, mo128, lse.data_ptr<float>(),
-                                                          delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq,
-                                                          Hkv, (float)scale, err);
+    launch_dkdv<128, 0>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
+    launch_dq<128>(g2, mq128, mk_t, mv_t, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
+  } else if (D == 64) {
+    launch_dkdv<64, 0>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
+    launch_dq<64>(g2, mq128, mk_t, mv_t, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   } else {
-    const int s1 = DkvLayout<64>::TOTAL + 1024, s2 = DqLayout<64>::TOTAL + 1024;
-    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s1));
-    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s2));
-    attn_bwd_dkdv_tc_kernel<64><<<g1, 320, s1, stream()>>>(mq64, mk128, mv128, mo64, lse.data_ptr<float>(),
-                                                           delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
-                                                           (bf16*)dv.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
-    attn_bwd_dq_tc_kernel<64><<<g2, 320, s2, stream()>>>(mq128, mk64, mv64, mo128, lse.data_ptr<float>(),
-                                                         delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq,
-                                                         Hkv, (float)scale, err);
+    launch_dkdv<256, 1>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
+    launch_dkdv<256, 2>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
+    launch_dq<256>(g2, mq128, mk_t, mv_t, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   }
   TS_LAUNCH_CHECK();
   return {dq, dk, dv};

@@ -8,13 +8,16 @@ std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, 
 std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
                                          const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                          const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d, double eps,
-                                         bool unit);
+                                         bool unit, const c10::optional<at::Tensor>& cos_tab,
+                                         const c10::optional<at::Tensor>& sin_tab);
 std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk,
                                                         const at::Tensor& dv, const at::Tensor& qkv,
                                                         const c10::optional<at::Tensor>& qw,
                                                         const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
-                                                        int64_t d, double eps, bool unit);
+                                                        int64_t d, double eps, bool unit,
+                                                        const c10::optional<at::Tensor>& cos_tab,
+                                                        const c10::optional<at::Tensor>& sin_tab);
 at::Tensor swiglu_fwd(const at::Tensor& gu);
 at::Tensor swiglu_bwd(const at::Tensor& da, const at::Tensor& gu);
 void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const at::Tensor& dy, double scale);
@@ -52,6 +55,8 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
 void register_ipc(pybind11::module& m);
 void register_pinned(pybind11::module& m);
 void attn_trace_enable(bool on);
+void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
+             double alpha);
 at::Tensor attn_trace_read();
 std::vector<at::Tensor> conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& tail);
 std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& dtail_out, const at::Tensor& x,
@@ -69,8 +74,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   ts::register_pinned(m);
   m.def("rms_norm_fwd", &ts::rms_norm_fwd);
   m.def("rms_norm_bwd", &ts::rms_norm_bwd);
-  m.def("qk_norm_rope_fwd", &ts::qk_norm_rope_fwd);
-  m.def("qk_norm_rope_bwd", &ts::qk_norm_rope_bwd);
+  m.def("qk_norm_rope_fwd", &ts::qk_norm_rope_fwd, pybind11::arg("qkv"), pybind11::arg("qw"), pybind11::arg("kw"),
+        pybind11::arg("pos"), pybind11::arg("inv_freq"), pybind11::arg("hq"), pybind11::arg("hkv"), pybind11::arg("d"),
+        pybind11::arg("eps"), pybind11::arg("unit"), pybind11::arg("cos_tab") = pybind11::none(),
+        pybind11::arg("sin_tab") = pybind11::none());
+  m.def("qk_norm_rope_bwd", &ts::qk_norm_rope_bwd, pybind11::arg("dq"), pybind11::arg("dk"), pybind11::arg("dv"),
+        pybind11::arg("qkv"), pybind11::arg("qw"), pybind11::arg("kw"), pybind11::arg("pos"), pybind11::arg("inv_freq"),
+        pybind11::arg("hq"), pybind11::arg("hkv"), pybind11::arg("d"), pybind11::arg("eps"), pybind11::arg("unit"),
+        pybind11::arg("cos_tab") = pybind11::none(), pybind11::arg("sin_tab") = pybind11::none());
   m.def("swiglu_fwd", &ts::swiglu_fwd);
   m.def("swiglu_bwd", &ts::swiglu_bwd);
   m.def("embedding_bwd_accumulate", &ts::embedding_bwd_accumulate);
@@ -97,6 +108,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv1d_silu_bwd", &ts::conv1d_silu_bwd);
   m.def("gdn_fwd", &ts::gdn_fwd);
   m.def("attn_trace_enable", &ts::attn_trace_enable);
+  m.def("gemm_tc", &ts::gemm_tc);
   m.def("attn_trace_read", &ts::attn_trace_read);
   m.def("gdn_bwd", &ts::gdn_bwd);
 }

@@ -1,0 +1,306 @@
+// tcgen05 GEMM for the projection shapes of the decoder (S4).
+//
+//   C[M, N] (op)= A[M, K] · B[K, N]
+//
+// A is K-major ([M][K] row-major) or M-major ([K][M] row-major, i.e. a
+// transposed operand); B is K-major ([N][K] row-major, an nn.Linear weight)
+// or N-major ([K][N] row-major). That covers y = x·Wᵀ (A, B K-major),
+// dx = dy·W (B N-major) and dW = dyᵀ·x (A M-major, B N-major) without a
+// transpose copy. The epilogue writes bf16, writes fp32, or adds into an fp32
+// C (the gradient-sink accumulate: beta = 1).
+//
+// Persistent kernel, one CTA per SM, 128 x 256 output tiles, 64-deep K
+// blocks in a 4-stage TMA ring:
+//   warp 0  TMA producer (one elected lane)
+//   warp 1  MMA issuer (one elected lane): tcgen05.mma into one of two TMEM
+//           accumulators (2 x 256 columns), so the epilogue of tile i overlaps
+//           the main loop of tile i+1
+//   warps 2-5  epilogue: tcgen05.ld of its 32-lane TMEM sub-partition (rows),
+//           convert, store
+// Every wait is bounded (tc::mbar_wait); TMEM is always freed.
+#include "common.cuh"
+#include "common.h"
+#include "tc.cuh"
+
+#include <cuda.h>
+
+namespace ts {
+
+CUtensorMap make_bf16_map(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                          uint32_t box_rows);
+at::Tensor& tc_error_flag(const at::Device& dev);
+
+namespace {
+
+typedef __nv_bfloat16 bf16;
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kBarOff = kStages * kStageBytes;  // 192 KB
+constexpr uint32_t kSmem = kBarOff + 256;
+
+enum Epi { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
+
+struct GemmBars {
+  uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
+  uint32_t tmem_slot;
+  int abort;
+};
+
+TS_DEVICE uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// tile t -> (m block, n block), grouped so that consecutive tiles of a CTA
+// wave share B columns (L2 reuse of the weight)
+TS_DEVICE void tile_coords(int t, int mt, int nt, int& mb, int& nb) {
+  constexpr int G = 8;
+  const int per_group = G * nt;
+  const int g = t / per_group;
+  const int first_m = g * G;
+  const int gm = min(G, mt - first_m);
+  const int r = t % per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
+                                                         const __grid_constant__ CUtensorMap tm_b, void* __restrict__ c,
+                                                         int M, int N, int K, int ldc, float alpha,
+                                                         int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  GemmBars* bars = reinterpret_cast<GemmBars*>(smem + kBarOff);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = (M + kBM - 1) / kBM, nt = (N + kBN - 1) / kBN, kt = (K + kBK - 1) / kBK;
+  const int tiles = mt * nt;
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&bars->full[s], 1);
+      tc::mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&bars->acc_full[b], 1);
+      tc::mbar_init(&bars->acc_empty[b], 128);
+    }
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) tc::tmem_alloc(&bars->tmem_slot, 512);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_a);
+      tc::prefetch_tmap(&tm_b);
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, mt, nt, mb, nb);
+        for (int kb = 0; kb < kt; ++kb, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages && !tc::mbar_wait(&bars->empty[s], ((it - kStages) / kStages) & 1, abort, err, 201))
+            goto producer_done;
+          tc::mbar_expect_tx(&bars->full[s], kStageBytes);
+          uint8_t* a = smem + s * kStageBytes;
+          uint8_t* b = a + kABytes;
+          if constexpr (!A_MN) {
+            tc::tma_load_2d(a, &tm_a, kb * kBK, mb * kBM, &bars->full[s]);  // box 64 (k) x 128 (m)
+          } else {
+            // [K][M]: two boxes of 64 m-columns x 64 k-rows
+            tc::tma_load_2d(a, &tm_a, mb * kBM, kb * kBK, &bars->full[s]);
+            tc::tma_load_2d(a + 64 * 128, &tm_a, mb * kBM + 64, kb * kBK, &bars->full[s]);
+          }
+          if constexpr (!B_MN) {
+            tc::tma_load_2d(b, &tm_b, kb * kBK, nb * kBN, &bars->full[s]);  // box 64 (k) x 256 (n)
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBN / 64; ++j)  // [K][N]: four boxes of 64 n-columns x 64 k-rows
+              tc::tma_load_2d(b + j * 64 * 128, &tm_b, nb * kBN + j * 64, kb * kBK, &bars->full[s]);
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_bf16(kBM, kBN, A_MN, B_MN);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (local >= 2 && !tc::mbar_wait(&bars->acc_empty[buf], ((local - 2) >> 1) & 1, abort, err, 211)) break;
+        tc::tc_fence_after();
+        const uint32_t acc = tmem + buf * kBN;
+        for (int kb = 0; kb < kt; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!tc::mbar_wait(&bars->full[s], (it / kStages) & 1, abort, err, 212)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a = sbase + s * kStageBytes;
+          const uint32_t b = a + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // K-major: +32 bytes per 16-element K step; MN-major: +16 rows of 128 bytes
+            const uint64_t ad = A_MN ? tc::sdesc_sw128(a + kk * 16 * 128, 64 * 128, 1024)
+                                     : tc::sdesc_sw128(a + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? tc::sdesc_sw128(b + kk * 16 * 128, 64 * 128, 1024)
+                                     : tc::sdesc_sw128(b + kk * 32, 16, 1024);
+            tc::mma_bf16(acc, ad, bd, idesc, kb > 0 || kk > 0);
+          }
+          tc::mma_commit(&bars->empty[s]);
+        }
+        if (ok) tc::mma_commit(&bars->acc_full[buf]);
+      }
+    }
+  } else {
+    // epilogue warps 2..5: TMEM sub-partition (warp & 3) -> rows 32*(warp&3) .. +32
+    const int sub = warp & 3;
+    const int row_in_tile = sub * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(sub * 32) << 16);
+    int local = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      bool ok = true;
+      if ((threadIdx.x & 31) == 0) ok = tc::mbar_wait(&bars->acc_full[buf], (local >> 1) & 1, abort, err, 221);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      tc::tc_fence_after();
+      int mb, nb;
+      tile_coords(t, mt, nt, mb, nb);
+      const int row = mb * kBM + row_in_tile;
+      const int col0 = nb * kBN;
+#pragma unroll 1
+      for (int cc = 0; cc < kBN; cc += 32) {
+        float v[32];
+        tc::tmem_ld32(lane_base + buf * kBN + cc, v);
+        tc::tmem_ld_wait();
+        const int col = col0 + cc;
+        if (row < M && col < N) {
+          const bool full = col + 32 <= N;
+          if constexpr (EPI == kStoreBf16) {
+            bf16* p = reinterpret_cast<bf16*>(c) + (long long)row * ldc + col;
+            if (full) {
+#pragma unroll
+              for (int x = 0; x < 32; x += 8) {
+                uint4 u;
+                u.x = pack_bf16(alpha * v[x], alpha * v[x + 1]);
+                u.y = pack_bf16(alpha * v[x + 2], alpha * v[x + 3]);
+                u.z = pack_bf16(alpha * v[x + 4], alpha * v[x + 5]);
+                u.w = pack_bf16(alpha * v[x + 6], alpha * v[x + 7]);
+                *reinterpret_cast<uint4*>(p + x) = u;
+              }
+            } else {
+#pragma unroll
+              for (int x = 0; x < 32; ++x)
+                if (col + x < N) p[x] = __float2bfloat16_rn(alpha * v[x]);
+            }
+          } else {
+            float* p = reinterpret_cast<float*>(c) + (long long)row * ldc + col;
+            if (full) {
+#pragma unroll
+              for (int x = 0; x < 32; x += 4) {
+                float4 o = make_float4(alpha * v[x], alpha * v[x + 1], alpha * v[x + 2], alpha * v[x + 3]);
+                if constexpr (EPI == kAccumF32) {
+                  const float4 prev = *reinterpret_cast<const float4*>(p + x);
+                  o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
+                }
+                *reinterpret_cast<float4*>(p + x) = o;
+              }
+            } else {
+#pragma unroll
+              for (int x = 0; x < 32; ++x)
+                if (col + x < N) p[x] = (EPI == kAccumF32 ? p[x] : 0.f) + alpha * v[x];
+            }
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->acc_empty[buf]);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int ldc, float alpha,
+            int device) {
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int grid = std::max(1, std::min(tiles, sm_count(device)));
+  const int smem = kSmem + 1024;
+  TS_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem));
+  gemm_tc_kernel<A_MN, B_MN, EPI><<<grid, 192, smem, stream()>>>(ma, mb, c, M, N, K, ldc, alpha,
+                                                                  tc_error_flag(at::Device(at::kCUDA, device))
+                                                                      .data_ptr<int>());
+}
+
+}  // namespace
+
+// out (op)= a · b, with a = a_t ? aᵀ : a and b = b_t ? bᵀ : b as seen by the
+// math: a_t = false takes a as [M, K]; a_t = true takes a as [K, M].
+// b_t = true takes b as [N, K] (nn.Linear weight); b_t = false as [K, N].
+// mode 0: out bf16 [M, N] = alpha·a·b; mode 1: out fp32 = alpha·a·b;
+// mode 2: out fp32 += alpha·a·b.
+void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
+             double alpha) {
+  check_cuda(a, "a");
+  check_cuda(b, "b");
+  check_cuda(out, "out");
+  TS_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_tc takes bf16 operands");
+  TS_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm_tc takes matrices");
+  const int M = a_t ? a.size(1) : a.size(0);
+  const int K = a_t ? a.size(0) : a.size(1);
+  const int N = b_t ? b.size(0) : b.size(1);
+  TS_CHECK((b_t ? b.size(1) : b.size(0)) == K, "gemm_tc inner dimensions differ");
+  TS_CHECK(out.size(0) == M && out.size(1) == N, "gemm_tc output shape");
+  TS_CHECK(mode == 0 ? out.scalar_type() == at::kBFloat16 : out.scalar_type() == at::kFloat, "gemm_tc output dtype");
+  // 16-byte TMA strides for every operand layout and 16-byte vector stores of C rows
+  TS_CHECK(K % 8 == 0 && N % 8 == 0 && (!a_t || M % 8 == 0), "gemm_tc needs K, N (and M when a is [K, M]) "
+           "to be multiples of 8");
+  const c10::cuda::CUDAGuard guard(a.device());
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    if (mode != 2) out.zero_();
+    return;
+  }
+  // tensor maps: inner dimension first; boxes of 64 inner elements
+  const CUtensorMap ma = a_t ? make_bf16_map(a.data_ptr(), M, K, M, 64) : make_bf16_map(a.data_ptr(), K, M, K, 128);
+  const CUtensorMap mb = b_t ? make_bf16_map(b.data_ptr(), K, N, K, 256) : make_bf16_map(b.data_ptr(), N, K, N, 64);
+  const int dev = a.get_device();
+  void* c = out.data_ptr();
+  const float al = (float)alpha;
+#define TS_GEMM_CASE(AM, BM)                                                          \
+  if (mode == 0) launch<AM, BM, kStoreBf16>(ma, mb, c, M, N, K, (int)N, al, dev);    \
+  else if (mode == 1) launch<AM, BM, kStoreF32>(ma, mb, c, M, N, K, (int)N, al, dev); \
+  else launch<AM, BM, kAccumF32>(ma, mb, c, M, N, K, (int)N, al, dev);
+  if (!a_t && b_t) {
+    TS_GEMM_CASE(false, false)
+  } else if (!a_t && !b_t) {
+    TS_GEMM_CASE(false, true)
+  } else if (a_t && !b_t) {
+    TS_GEMM_CASE(true, true)
+  } else {
+    TS_GEMM_CASE(true, false)
+  }
+#undef TS_GEMM_CASE
+  TS_LAUNCH_CHECK();
+}
+
+}  // namespace ts

@@ -244,7 +244,8 @@ void rms_dx_dispatch(const at::Tensor& dy, const at::Tensor& x, const at::Tensor
 template <typename T, int D>
 __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
     const T* __restrict__ qkv, const T* __restrict__ qw, const T* __restrict__ kw, const int64_t* __restrict__ pos,
-    const float* __restrict__ inv_freq, T* __restrict__ q, T* __restrict__ k, T* __restrict__ v, int tokens, int hq,
+    const float* __restrict__ inv_freq, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab,
+    int tab_len, T* __restrict__ q, T* __restrict__ k, T* __restrict__ v, int tokens, int hq,
     int hkv, float eps, int unit, int rot_lanes) {
   constexpr int EPL = D / 32;
   const int lane = threadIdx.x & 31;
@@ -281,7 +282,10 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
 #pragma unroll
     for (int e = 0; e < EPL; ++e) y[e] = xv[e];
   }
-  const float p = (float)pos[t];
+  const int64_t pi = pos[t];
+  const float p = (float)pi;
+  const int nfreq = rot_lanes * EPL / 2;
+  const bool tab = pi >= 0 && pi < tab_len;
   T* dst = is_q ? q + ((size_t)t * hq + h) * D + lane * EPL : k + ((size_t)t * hkv + (h - hq)) * D + lane * EPL;
   // rotary over the first rot_lanes * EPL dims; the rotate-half partner of an
   // element sits half_mask lanes away; the remaining dims pass through
@@ -294,7 +298,12 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
     if (rotary) {
       const int fi = (lane & (half_mask - 1)) * EPL + e;  // frequency index
       float s, c;
-      sincosf(p * inv_freq[fi], &s, &c);
+      if (tab) {  // cos/sin of the fp32 angle, precomputed per (position, frequency)
+        c = cos_tab[pi * nfreq + fi];
+        s = sin_tab[pi * nfreq + fi];
+      } else {
+        sincosf(p * inv_freq[fi], &s, &c);
+      }
       const float rot = low ? -partner : partner;
       dst[e] = from_f<T>(y[e] * c + rot * s);
     } else {
@@ -307,7 +316,8 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
     const T* __restrict__ dq, const T* __restrict__ dk, const T* __restrict__ dv, const T* __restrict__ qkv,
     const T* __restrict__ qw, const T* __restrict__ kw, const int64_t* __restrict__ pos,
-    const float* __restrict__ inv_freq, T* __restrict__ dqkv, float* __restrict__ dqw_part,
+    const float* __restrict__ inv_freq, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab,
+    int tab_len, T* __restrict__ dqkv, float* __restrict__ dqw_part,
     float* __restrict__ dkw_part, int tokens, int hq, int hkv, float eps, int items_per_block, int unit, int rot_lanes) {
   constexpr int EPL = D / 32;
   __shared__ float red_q[kWarps][D];
@@ -334,7 +344,10 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
     const bool is_q = h < hq;
     const T* g = is_q ? dq + ((size_t)t * hq + h) * D + lane * EPL : dk + ((size_t)t * hkv + (h - hq)) * D + lane * EPL;
     const T* src = qkv + (size_t)t * heads * D + (size_t)h * D + lane * EPL;
-    const float p = (float)pos[t];
+    const int64_t pi = pos[t];
+    const float p = (float)pi;
+    const int nfreq = rot_lanes * EPL / 2;
+    const bool tab = pi >= 0 && pi < tab_len;
     const int half_mask = rot_lanes >> 1;
     const bool rotary = lane < rot_lanes;
     const bool low = (lane & half_mask) == 0;
@@ -346,7 +359,12 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
       if (rotary) {
         const int fi = (lane & (half_mask - 1)) * EPL + e;
         float s, c;
-        sincosf(p * inv_freq[fi], &s, &c);
+        if (tab) {
+          c = cos_tab[pi * nfreq + fi];
+          s = sin_tab[pi * nfreq + fi];
+        } else {
+          sincosf(p * inv_freq[fi], &s, &c);
+        }
         // d/dy_i of sum_j go_j * (y_j c_j + rot(y)_j s_j)
         dy[e] = go * c + (low ? partner : -partner) * s;
       } else {
@@ -519,14 +537,14 @@ template <typename T, int D>
 static void qk_fwd_launch(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
                           const c10::optional<at::Tensor>& kw, const at::Tensor& pos, const at::Tensor& inv_freq,
                           at::Tensor& q, at::Tensor& k, at::Tensor& v, int hq, int hkv, float eps, int unit,
-                          int rot_lanes) {
+                          int rot_lanes, const float* ct, const float* st, int tl) {
   const int tokens = qkv.size(0);
   const long long items = (long long)tokens * (hq + 2 * hkv);
   const int blocks = (int)((items + kWarps - 1) / kWarps);
   qk_norm_rope_fwd_kernel<T, D><<<blocks, kWarps * 32, 0, stream()>>>(
       (const T*)qkv.data_ptr(), qw ? (const T*)qw->data_ptr() : nullptr, kw ? (const T*)kw->data_ptr() : nullptr,
-      pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(), (T*)q.data_ptr(), (T*)k.data_ptr(), (T*)v.data_ptr(),
-      tokens, hq, hkv, eps, unit, rot_lanes);
+      pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(), ct, st, tl, (T*)q.data_ptr(), (T*)k.data_ptr(),
+      (T*)v.data_ptr(), tokens, hq, hkv, eps, unit, rot_lanes);
 }
 
 #define TS_DISPATCH_HEAD(D, FN, T, ...)                                \
@@ -540,7 +558,15 @@ static void qk_fwd_launch(const at::Tensor& qkv, const c10::optional<at::Tensor>
 std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
                                          const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                          const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d,
-                                         double eps, bool unit) {
+                                         double eps, bool unit, const c10::optional<at::Tensor>& cos_tab,
+                                         const c10::optional<at::Tensor>& sin_tab) {
+  const float* ct = cos_tab ? cos_tab->data_ptr<float>() : nullptr;
+  const float* st = sin_tab ? sin_tab->data_ptr<float>() : nullptr;
+  const int tl = cos_tab ? (int)cos_tab->size(0) : 0;
+  TS_CHECK(!cos_tab || (sin_tab && cos_tab->is_contiguous() && sin_tab->is_contiguous() &&
+                        cos_tab->size(1) == inv_freq.numel() && sin_tab->sizes() == cos_tab->sizes() &&
+                        cos_tab->scalar_type() == at::kFloat),
+           "rope tables must be fp32 [positions, rotary_dim / 2] cos and sin");
   check_cuda(qkv, "qkv");
   const int epl = (int)d / 32;
   const int rot_lanes = (int)(2 * inv_freq.numel()) / epl;
@@ -557,10 +583,10 @@ std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optio
   if (t == 0) return {q, k, v};
   if (qkv.scalar_type() == at::kBFloat16) {
     TS_DISPATCH_HEAD(d, qk_fwd_launch, __nv_bfloat16, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps,
-                     unit ? 1 : 0, rot_lanes);
+                     unit ? 1 : 0, rot_lanes, ct, st, tl);
   } else if (qkv.scalar_type() == at::kFloat) {
     TS_DISPATCH_HEAD(d, qk_fwd_launch, float, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps, unit ? 1 : 0,
-                     rot_lanes);
+                     rot_lanes, ct, st, tl);
   } else {
     TS_CHECK(false, "qk_norm_rope_fwd: unsupported dtype");
   }
@@ -573,11 +599,11 @@ static void qk_bwd_launch(const at::Tensor& dq, const at::Tensor& dk, const at::
                           const c10::optional<at::Tensor>& qw, const c10::optional<at::Tensor>& kw,
                           const at::Tensor& pos, const at::Tensor& inv_freq, at::Tensor& dqkv, at::Tensor& pq,
                           at::Tensor& pk, int hq, int hkv, float eps, int blocks, int per_block, int unit,
-                          int rot_lanes) {
+                          int rot_lanes, const float* ct, const float* st, int tl) {
   qk_norm_rope_bwd_kernel<T, D><<<blocks, kWarps * 32, 0, stream()>>>(
       (const T*)dq.data_ptr(), (const T*)dk.data_ptr(), (const T*)dv.data_ptr(), (const T*)qkv.data_ptr(),
       qw ? (const T*)qw->data_ptr() : nullptr, kw ? (const T*)kw->data_ptr() : nullptr, pos.data_ptr<int64_t>(),
-      inv_freq.data_ptr<float>(), (T*)dqkv.data_ptr(), pq.data_ptr<float>(), pk.data_ptr<float>(), qkv.size(0), hq,
+      inv_freq.data_ptr<float>(), ct, st, tl, (T*)dqkv.data_ptr(), pq.data_ptr<float>(), pk.data_ptr<float>(), qkv.size(0), hq,
       hkv, eps, per_block, unit, rot_lanes);
 }
 
@@ -586,8 +612,13 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
                                                         const c10::optional<at::Tensor>& qw,
                                                         const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
-                                                        int64_t d, double eps, bool unit) {
+                                                        int64_t d, double eps, bool unit,
+                                                        const c10::optional<at::Tensor>& cos_tab,
+                                                        const c10::optional<at::Tensor>& sin_tab) {
   check_cuda(qkv, "qkv");
+  const float* ct = cos_tab ? cos_tab->data_ptr<float>() : nullptr;
+  const float* st = sin_tab ? sin_tab->data_ptr<float>() : nullptr;
+  const int tl = cos_tab ? (int)cos_tab->size(0) : 0;
   const int rot_lanes = (int)(2 * inv_freq.numel()) / ((int)d / 32);
   check_cuda(dq, "dq");
   check_cuda(dk, "dk");
@@ -604,10 +635,10 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
   if (t > 0) {
     if (qkv.scalar_type() == at::kBFloat16) {
       TS_DISPATCH_HEAD(d, qk_bwd_launch, __nv_bfloat16, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pq, pk, hq, hkv,
-                       (float)eps, blocks, per_block, unit ? 1 : 0, rot_lanes);
+                       (float)eps, blocks, per_block, unit ? 1 : 0, rot_lanes, ct, st, tl);
     } else if (qkv.scalar_type() == at::kFloat) {
       TS_DISPATCH_HEAD(d, qk_bwd_launch, float, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pq, pk, hq, hkv,
-                       (float)eps, blocks, per_block, unit ? 1 : 0, rot_lanes);
+                       (float)eps, blocks, per_block, unit ? 1 : 0, rot_lanes, ct, st, tl);
     } else {
       TS_CHECK(false, "qk_norm_rope_bwd: unsupported dtype");
     }

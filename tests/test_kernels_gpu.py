@@ -272,3 +272,24 @@ def test_attention_tcgen05_backward(t, s, hq, hkv, d):
     assert _rel(dv, gv) < 2e-2
     dq2, dk2, dv2 = native().attn_bwd_tc(do, q, k, v, o, lse, scale)
     assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 512, 128), (304, 200, 72), (2304, 4096, 2048), (128, 151936 // 8, 256)])
+@pytest.mark.parametrize("a_t,b_t", [(False, True), (False, False), (True, False), (True, True)])
+def test_gemm_tcgen05(m, n, k, a_t, b_t):
+    from thundersync_b200.ops.gemm import gemm, gemm_accumulate
+
+    torch.manual_seed(m + n + k)
+    a = torch.randn((k, m) if a_t else (m, k), device=DEV, dtype=torch.bfloat16)
+    b = torch.randn((n, k) if b_t else (k, n), device=DEV, dtype=torch.bfloat16)
+    ref = (a.float().t() if a_t else a.float()) @ (b.float().t() if b_t else b.float())
+    got = gemm(a, b, a_t=a_t, b_t=b_t, out_dtype=torch.float32)
+    assert _rel(got, ref) < 1e-5
+    got16 = gemm(a, b, a_t=a_t, b_t=b_t, alpha=0.5)
+    assert _rel(got16, 0.5 * ref) < 1e-2
+    acc = torch.ones(m, n, device=DEV)
+    gemm_accumulate(acc, a, b, a_t=a_t, b_t=b_t, alpha=2.0)
+    assert _rel(acc, 1.0 + 2.0 * ref) < 1e-5
+    from thundersync_b200.ops._ext import native
+
+    assert int(native().tc_status(a).item()) == 0

@@ -8,7 +8,9 @@ self-contained case that kernel profiles are captured on.
 
 Families: ``attn`` (bottom-right causal GQA attention; fwd, or fwd+bwd),
 ``rms`` (RMSNorm fwd/bwd), ``lse`` (log-sum-exp/gather over fp32 logits),
-``gdn`` (gated delta rule fwd/bwd), ``conv`` (causal conv1d + SiLU fwd/bwd).
+``gdn`` (gated delta rule fwd/bwd), ``conv`` (causal conv1d + SiLU fwd/bwd),
+``swiglu``, ``rope`` (QK-norm + RoPE), ``dlogits``, ``adamw``, ``fold``
+(GRPO statistic folds), and ``gemm_host`` (host cost of a library GEMM call).
 """
 
 from __future__ import annotations
@@ -131,6 +133,102 @@ def bench_conv(args) -> None:
     print(f"conv bwd: {ms:.3f} ms")
 
 
+def bench_swiglu(args) -> None:
+    gu = torch.randn(args.rows, 2 * args.cols, device="cuda", dtype=torch.bfloat16)
+    ext = native()
+    a = ext.swiglu_fwd(gu)
+    ms = _time(lambda: ext.swiglu_fwd(gu), args.iters)
+    print(f"swiglu fwd {args.rows}x{args.cols}: {ms:.3f} ms  {3 * a.numel() * 2 / ms / 1e6:.0f} GB/s")
+    ms = _time(lambda: ext.swiglu_bwd(a, gu), args.iters)
+    print(f"swiglu bwd: {ms:.3f} ms  {5 * a.numel() * 2 / ms / 1e6:.0f} GB/s")
+
+
+def bench_rope(args) -> None:
+    hq, hkv, d = args.hq, args.hkv, args.d
+    qkv = torch.randn(args.rows, (hq + 2 * hkv) * d, device="cuda", dtype=torch.bfloat16)
+    qw = torch.rand(d, device="cuda", dtype=torch.bfloat16)
+    kw = torch.rand(d, device="cuda", dtype=torch.bfloat16)
+    pos = torch.arange(args.rows, device="cuda")
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, device="cuda").float() / d))
+    from thundersync_b200.ops.rope import rope_tables
+
+    ext = native()
+    ct, st = rope_tables(inv)
+    q, k, v = ext.qk_norm_rope_fwd(qkv, qw, kw, pos, inv, hq, hkv, d, 1e-6, False, ct, st)
+    ms = _time(lambda: ext.qk_norm_rope_fwd(qkv, qw, kw, pos, inv, hq, hkv, d, 1e-6, False, ct, st), args.iters)
+    print(f"qk_norm_rope fwd {args.rows} rows: {ms:.3f} ms  {2 * qkv.numel() * 2 / ms / 1e6:.0f} GB/s")
+    ms = _time(lambda: ext.qk_norm_rope_bwd(q, k, v, qkv, qw, kw, pos, inv, hq, hkv, d, 1e-6, False, ct, st),
+               args.iters)
+    print(f"qk_norm_rope bwd: {ms:.3f} ms  {3 * qkv.numel() * 2 / ms / 1e6:.0f} GB/s")
+
+
+def bench_dlogits(args) -> None:
+    logits = torch.randn(args.rows, args.cols, device="cuda", dtype=torch.float32)
+    tgt = torch.randint(0, args.cols, (args.rows,), device="cuda")
+    ext = native()
+    lp, lse, _ = ext.lse_gather(logits, tgt, False)
+    g = torch.randn(args.rows, device="cuda")
+    ms = _time(lambda: ext.logprob_dlogits(logits, tgt, lse, g, None, None, True), args.iters)
+    print(f"dlogits {args.rows}x{args.cols}: {ms:.3f} ms  {logits.numel() * 6 / ms / 1e6:.0f} GB/s")
+
+
+def bench_adamw(args) -> None:
+    n = args.rows * args.cols
+    master = torch.randn(n, device="cuda")
+    param = master.to(torch.bfloat16)
+    grad = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    ext = native()
+    ms = _time(lambda: ext.adamw_flat(master, param, grad, m, v, 1e-5, 0.9, 0.999, 1e-8, 0.0, 1, None, 1.0, True),
+               args.iters)
+    print(f"adamw {n} elems: {ms:.3f} ms  {n * 18 / ms / 1e6:.0f} GB/s")
+
+
+def bench_fold(args) -> None:
+    n = args.rows * args.cols
+    g1 = torch.zeros(n, device="cuda")
+    g2 = torch.zeros(n, device="cuda")
+    src = torch.randn(n, device="cuda")
+    ext = native()
+    ms = _time(lambda: ext.fold_stats(g1, g2, src, 1.0), args.iters)
+    print(f"fold {n} elems: {ms:.3f} ms  {n * 20 / ms / 1e6:.0f} GB/s")
+    ms = _time(lambda: ext.axpby(g1, g2, src, 0.5, -0.25), args.iters)
+    print(f"axpby {n} elems: {ms:.3f} ms  {n * 16 / ms / 1e6:.0f} GB/s")
+
+
+def bench_gemm(args) -> None:
+    """tcgen05 GEMM vs the library GEMM on the decoder's projection shapes (M = padded tokens)."""
+    from thundersync_b200.ops.gemm import gemm, gemm_accumulate
+
+    m = args.rows
+    shapes = [("qkv fwd", 4096, 2048), ("o fwd", 2048, 2048), ("gate/up fwd", 12288, 2048), ("down fwd", 2048, 6144),
+              ("lm head chunk", 151936, 2048)]
+    for name, n, k in shapes:
+        x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16)
+        flops = 2.0 * m * n * k
+        t_ours = _time(lambda: gemm(x, w), args.iters)
+        t_lib = _time(lambda: torch.nn.functional.linear(x, w), args.iters)
+        print(f"{name:14s} {m}x{n}x{k}: tcgen05 {flops / t_ours / 1e9:7.1f} TFLOP/s, library {flops / t_lib / 1e9:7.1f}")
+    for name, n, k in (("dW qkv", 4096, 2048), ("dW gate/up", 12288, 2048)):
+        dy = torch.randn(m, n, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        acc = torch.zeros(n, k, device="cuda")
+        flops = 2.0 * m * n * k
+        t_ours = _time(lambda: gemm_accumulate(acc, dy, x, a_t=True, b_t=False), args.iters)
+        t_lib = _time(lambda: torch.addmm(acc, dy.t(), x, out_dtype=torch.float32, out=acc), args.iters)
+        print(f"{name:14s} {n}x{k}x{m} (fp32 +=): tcgen05 {flops / t_ours / 1e9:7.1f} TFLOP/s, "
+              f"library {flops / t_lib / 1e9:7.1f}")
+    for name, n, k in (("dx qkv", 2048, 4096), ("dx down", 6144, 2048)):
+        dy = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(k, n, device="cuda", dtype=torch.bfloat16)
+        flops = 2.0 * m * n * k
+        t_ours = _time(lambda: gemm(dy, w, b_t=False), args.iters)
+        t_lib = _time(lambda: dy.matmul(w), args.iters)
+        print(f"{name:14s} {m}x{n}x{k}: tcgen05 {flops / t_ours / 1e9:7.1f} TFLOP/s, library {flops / t_lib / 1e9:7.1f}")
+
+
 def bench_gemm_host(args) -> None:
     """Host (CPU) cost of one library GEMM call: repeated shape vs a new row count every call."""
     import time
@@ -158,7 +256,8 @@ def bench_gemm_host(args) -> None:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host"])
+    ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host", "swiglu", "rope", "dlogits",
+                                       "adamw", "fold", "gemm"])
     ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
     ap.add_argument("--t", type=int, default=2048)
     ap.add_argument("--s", type=int, default=2560)
@@ -172,7 +271,8 @@ def main(argv=None) -> None:
     ap.add_argument("--trace", action="store_true", help="print the dK/dV kernel's per-step timeline")
     args = ap.parse_args(argv)
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
-     "gemm_host": bench_gemm_host}[args.family](args)
+     "gemm_host": bench_gemm_host, "swiglu": bench_swiglu, "rope": bench_rope, "dlogits": bench_dlogits,
+     "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm}[args.family](args)
 
 
 if __name__ == "__main__":

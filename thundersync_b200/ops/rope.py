@@ -52,14 +52,37 @@ def qk_norm_rope_reference(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit_o
     return rot(q), rot(k), v.contiguous()
 
 
+ROPE_TABLE_POSITIONS = 65536
+_TABLES: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def rope_tables(inv_freq: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 cos/sin of ``position * inv_freq`` for positions below ROPE_TABLE_POSITIONS, cached per device.
+
+    The angle is formed in fp32 exactly as the Hugging Face rotary embedding
+    forms it, so the kernels read the same cos/sin values that model computes;
+    positions past the table fall back to in-kernel sincos.
+    """
+    key = (inv_freq.device, inv_freq.data_ptr(), inv_freq.numel())
+    got = _TABLES.get(key)
+    if got is None:
+        pos = torch.arange(ROPE_TABLE_POSITIONS, device=inv_freq.device, dtype=torch.float32)
+        ang = pos[:, None] * inv_freq.float()[None, :]
+        got = (ang.cos().contiguous(), ang.sin().contiguous())
+        _TABLES[key] = got
+    return got
+
+
 class _QKNormRope(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit):
         ctx.meta = (hq, hkv, d, eps, unit)
         ctx.has_norm = q_w is not None
         if qkv.is_cuda:
+            ct, st = rope_tables(inv_freq)
             q, k, v = native().qk_norm_rope_fwd(
-                qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(), hq, hkv, d, float(eps), bool(unit)
+                qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(), hq, hkv, d, float(eps), bool(unit),
+                ct, st,
             )
         else:
             with torch.no_grad():
@@ -76,9 +99,10 @@ class _QKNormRope(torch.autograd.Function):
         dk = torch.zeros(t, hkv, d, dtype=qkv.dtype, device=qkv.device) if dk is None else dk.contiguous()
         dv = torch.zeros(t, hkv, d, dtype=qkv.dtype, device=qkv.device) if dv is None else dv.contiguous()
         if qkv.is_cuda:
+            ct, st = rope_tables(inv_freq)
             dqkv, dqw, dkw = native().qk_norm_rope_bwd(
                 dq, dk, dv, qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(),
-                hq, hkv, d, float(eps), bool(unit),
+                hq, hkv, d, float(eps), bool(unit), ct, st,
             )
         else:
             with torch.enable_grad():
