@@ -58,6 +58,11 @@ void attn_trace_enable(bool on);
 void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
              double alpha);
 at::Tensor attn_trace_read();
+std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
+                                      bool with_entropy);
+at::Tensor lmhead_dlogits_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt, const at::Tensor& lse,
+                             const at::Tensor& glp, const c10::optional<at::Tensor>& gent,
+                             const c10::optional<at::Tensor>& ent);
 std::vector<at::Tensor> conv1d_silu_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& tail);
 std::vector<at::Tensor> conv1d_silu_bwd(const at::Tensor& dy, const at::Tensor& dtail_out, const at::Tensor& x,
                                         const at::Tensor& w, const at::Tensor& tail);
@@ -109,6 +114,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_fwd", &ts::gdn_fwd);
   m.def("attn_trace_enable", &ts::attn_trace_enable);
   m.def("gemm_tc", &ts::gemm_tc);
+  m.def("lmhead_lse_tc", &ts::lmhead_lse_tc);
+  m.def("lmhead_dlogits_tc", &ts::lmhead_dlogits_tc);
   m.def("attn_trace_read", &ts::attn_trace_read);
   m.def("gdn_bwd", &ts::gdn_bwd);
 }

@@ -41,7 +41,33 @@ constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kBarOff = kStages * kStageBytes;  // 192 KB
 constexpr uint32_t kSmem = kBarOff + 256;
 
-enum Epi { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
+enum Epi { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2, kLse = 3, kDlogits = 4 };
+
+// Per-row data of the LM-head epilogues (C = hidden · Wᵀ are the logits).
+// kLse: per (row, N tile) online max / sum of exp / sum of exp·x partials and
+//   the target's logit, reduced by lse_reduce_kernel; the [rows, V] logits
+//   never reach memory.
+// kDlogits: dlogits = g·(onehot(target) − softmax) (entropy adds
+//   −p·g_H·(log p + H)), written as bf16.
+struct LmArgs {
+  const int64_t* tgt;
+  float* pm;   // [rows][ntiles] tile max (log2 units)
+  float* ps;   // [rows][ntiles] sum of 2^(x·log2e − m)
+  float* pt;   // [rows][ntiles] sum of 2^(x·log2e − m) · x  (entropy), or null
+  float* tlogit;  // [rows] logit of the target
+  const float* lse;
+  const float* glp;
+  const float* gent;  // or null
+  const float* ent;   // or null
+  int ntiles;
+};
+constexpr float kLog2eF = 1.4426950408889634f;
+
+TS_DEVICE float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 struct GemmBars {
   uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
@@ -71,7 +97,7 @@ template <bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
                                                          const __grid_constant__ CUtensorMap tm_b, void* __restrict__ c,
                                                          int M, int N, int K, int ldc, float alpha,
-                                                         int* __restrict__ err) {
+                                                         int* __restrict__ err, LmArgs lm) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   GemmBars* bars = reinterpret_cast<GemmBars*>(smem + kBarOff);
@@ -181,12 +207,83 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       tile_coords(t, mt, nt, mb, nb);
       const int row = mb * kBM + row_in_tile;
       const int col0 = nb * kBN;
+      // LM-head row state (one row per thread)
+      float run_m = -INFINITY, run_s = 0.f, run_t = 0.f, row_lse = 0.f, row_g = 0.f, row_ge = 0.f, row_h = 0.f;
+      int64_t row_tgt = -1;
+      if constexpr (EPI == kLse || EPI == kDlogits) {
+        if (row < M) {
+          row_tgt = lm.tgt[row];
+          if constexpr (EPI == kDlogits) {
+            row_lse = lm.lse[row];
+            row_g = lm.glp[row];
+            if (lm.gent != nullptr) {
+              row_ge = lm.gent[row];
+              row_h = lm.ent[row];
+            }
+          }
+        }
+      }
 #pragma unroll 1
       for (int cc = 0; cc < kBN; cc += 32) {
         float v[32];
         tc::tmem_ld32(lane_base + buf * kBN + cc, v);
         tc::tmem_ld_wait();
         const int col = col0 + cc;
+        if constexpr (EPI == kLse) {
+          if (row < M && col < N) {
+            float cm = -INFINITY;
+#pragma unroll
+            for (int x = 0; x < 32; ++x) {
+              if (col + x < N) cm = fmaxf(cm, v[x] * kLog2eF);
+              if (col + x == row_tgt) lm.tlogit[row] = v[x];
+            }
+            if (cm > run_m) {
+              const float r = ex2f(run_m - cm);
+              run_s *= r;
+              run_t *= r;
+              run_m = cm;
+            }
+#pragma unroll
+            for (int x = 0; x < 32; ++x) {
+              if (col + x < N) {
+                const float e = ex2f(fmaf(v[x], kLog2eF, -run_m));
+                run_s += e;
+                run_t = fmaf(e, v[x], run_t);
+              }
+            }
+          }
+          continue;
+        }
+        if constexpr (EPI == kDlogits) {
+          if (row < M && col < N) {
+            bf16* p = reinterpret_cast<bf16*>(c) + (long long)row * ldc + col;
+            const float l2 = row_lse * kLog2eF;
+            float d[32];
+#pragma unroll
+            for (int x = 0; x < 32; ++x) {
+              const float pr = ex2f(fmaf(v[x], kLog2eF, -l2));
+              float g = row_g;
+              if (lm.gent != nullptr) g += row_ge * ((v[x] - row_lse) + row_h);
+              d[x] = -pr * g + (col + x == row_tgt ? row_g : 0.f);
+            }
+            if (col + 32 <= N) {
+#pragma unroll
+              for (int x = 0; x < 32; x += 8) {
+                uint4 u;
+                u.x = pack_bf16(d[x], d[x + 1]);
+                u.y = pack_bf16(d[x + 2], d[x + 3]);
+                u.z = pack_bf16(d[x + 4], d[x + 5]);
+                u.w = pack_bf16(d[x + 6], d[x + 7]);
+                *reinterpret_cast<uint4*>(p + x) = u;
+              }
+            } else {
+#pragma unroll
+              for (int x = 0; x < 32; ++x)
+                if (col + x < N) p[x] = __float2bfloat16_rn(d[x]);
+            }
+          }
+          continue;
+        }
         if (row < M && col < N) {
           const bool full = col + 32 <= N;
           if constexpr (EPI == kStoreBf16) {
@@ -226,6 +323,14 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           }
         }
       }
+      if constexpr (EPI == kLse) {
+        if (row < M) {
+          const long long o = (long long)row * lm.ntiles + nb;
+          lm.pm[o] = run_m;
+          lm.ps[o] = run_s;
+          if (lm.pt != nullptr) lm.pt[o] = run_t;
+        }
+      }
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->acc_empty[buf]);
     }
@@ -240,7 +345,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 
 template <bool A_MN, bool B_MN, int EPI>
 void launch(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int ldc, float alpha,
-            int device) {
+            int device, LmArgs lm = LmArgs{}) {
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int grid = std::max(1, std::min(tiles, sm_count(device)));
   const int smem = kSmem + 1024;
@@ -248,10 +353,98 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N,
                                      smem));
   gemm_tc_kernel<A_MN, B_MN, EPI><<<grid, 192, smem, stream()>>>(ma, mb, c, M, N, K, ldc, alpha,
                                                                   tc_error_flag(at::Device(at::kCUDA, device))
-                                                                      .data_ptr<int>());
+                                                                      .data_ptr<int>(),
+                                                                  lm);
+}
+
+// One warp per row: combine the tile partials into lse (and entropy), lp = target logit − lse.
+__global__ void lse_reduce_kernel(const float* __restrict__ pm, const float* __restrict__ ps,
+                                  const float* __restrict__ pt, const float* __restrict__ tlogit,
+                                  float* __restrict__ lp, float* __restrict__ lse, float* __restrict__ ent, int rows,
+                                  int ntiles) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* m = pm + (long long)row * ntiles;
+  const float* sm = ps + (long long)row * ntiles;
+  float mx = -INFINITY;
+  for (int i = lane; i < ntiles; i += 32) mx = fmaxf(mx, m[i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float s = 0.f, t = 0.f;
+  for (int i = lane; i < ntiles; i += 32) {
+    const float r = ex2f(m[i] - mx);
+    s = fmaf(sm[i], r, s);
+    if (pt != nullptr) t = fmaf(pt[(long long)row * ntiles + i], r, t);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    t += __shfl_xor_sync(0xffffffffu, t, o);
+  }
+  if (lane == 0) {
+    const float l = (mx + log2f(s)) * 0.6931471805599453f;  // natural-log LSE
+    lse[row] = l;
+    lp[row] = tlogit[row] - l;
+    if (ent != nullptr) ent[row] = l - t / s;
+  }
 }
 
 }  // namespace
+
+// Fused LM-head forward: lp[r] = log softmax(h W^T)[r, tgt[r]] (+ entropy), lse[r];
+// h [R, D] bf16, w [V, D] bf16; the logits never reach memory.
+std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
+                                      bool with_entropy) {
+  check_cuda(h, "h");
+  check_cuda(w, "w");
+  check_cuda(tgt, "tgt");
+  TS_CHECK(h.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && tgt.scalar_type() == at::kLong,
+           "lmhead_lse_tc takes bf16 h, w and int64 targets");
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int R = h.size(0), D = h.size(1), V = w.size(0);
+  TS_CHECK(w.size(1) == D && D % 8 == 0 && V % 8 == 0, "lmhead_lse_tc shapes");
+  auto f32 = h.options().dtype(at::kFloat);
+  auto lp = at::empty({R}, f32), lse = at::empty({R}, f32);
+  auto ent = with_entropy ? at::empty({R}, f32) : at::Tensor();
+  if (R == 0) return {lp, lse, ent};
+  const int ntiles = (V + kBN - 1) / kBN;
+  auto pm = at::empty({R, ntiles}, f32), ps = at::empty({R, ntiles}, f32);
+  auto pt = with_entropy ? at::empty({R, ntiles}, f32) : at::Tensor();
+  auto tl = at::zeros({R}, f32);
+  LmArgs lm{tgt.data_ptr<int64_t>(), pm.data_ptr<float>(), ps.data_ptr<float>(),
+            with_entropy ? pt.data_ptr<float>() : nullptr, tl.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr,
+            ntiles};
+  const CUtensorMap ma = make_bf16_map(h.data_ptr(), D, R, D, 128);
+  const CUtensorMap mb = make_bf16_map(w.data_ptr(), D, V, D, 256);
+  launch<false, false, kLse>(ma, mb, nullptr, R, V, D, V, 1.f, h.get_device(), lm);
+  lse_reduce_kernel<<<(R + 7) / 8, 256, 0, stream()>>>(pm.data_ptr<float>(), ps.data_ptr<float>(),
+                                                       with_entropy ? pt.data_ptr<float>() : nullptr,
+                                                       tl.data_ptr<float>(), lp.data_ptr<float>(),
+                                                       lse.data_ptr<float>(),
+                                                       with_entropy ? ent.data_ptr<float>() : nullptr, R, ntiles);
+  TS_LAUNCH_CHECK();
+  return {lp, lse, ent};
+}
+
+// Fused LM-head backward epilogue: dlogits [R, V] bf16 from recomputed logits.
+at::Tensor lmhead_dlogits_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt, const at::Tensor& lse,
+                             const at::Tensor& glp, const c10::optional<at::Tensor>& gent,
+                             const c10::optional<at::Tensor>& ent) {
+  check_cuda(h, "h");
+  check_cuda(w, "w");
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int R = h.size(0), D = h.size(1), V = w.size(0);
+  auto d = at::empty({R, V}, h.options());
+  if (R == 0) return d;
+  LmArgs lm{tgt.data_ptr<int64_t>(), nullptr, nullptr, nullptr, nullptr, lse.data_ptr<float>(), glp.data_ptr<float>(),
+            gent ? gent->data_ptr<float>() : nullptr, ent ? ent->data_ptr<float>() : nullptr, 0};
+  const CUtensorMap ma = make_bf16_map(h.data_ptr(), D, R, D, 128);
+  const CUtensorMap mb = make_bf16_map(w.data_ptr(), D, V, D, 256);
+  launch<false, false, kDlogits>(ma, mb, d.data_ptr(), R, V, D, V, 1.f, h.get_device(), lm);
+  TS_LAUNCH_CHECK();
+  return d;
+}
 
 // out (op)= a · b, with a = a_t ? aᵀ : a and b = b_t ? bᵀ : b as seen by the
 // math: a_t = false takes a as [M, K]; a_t = true takes a as [K, M].

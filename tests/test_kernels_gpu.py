@@ -155,6 +155,50 @@ def test_lm_head_logprob(entropy):
     assert _rel(g[1], gr[1]) < 2e-2
 
 
+@pytest.mark.parametrize("entropy", [False, True])
+@pytest.mark.parametrize("n,dmod,vocab", [(300, 256, 5008), (1000, 2048, 151936)])
+def test_lm_head_fused_tcgen05(entropy, n, dmod, vocab):
+    """The tcgen05 LSE/dlogits epilogues against an fp32 PyTorch reference and the unfused path."""
+    from thundersync_b200.ops import logprob as L
+
+    assert L._fused_ok(torch.empty(1, dmod, device=DEV, dtype=torch.bfloat16),
+                       torch.empty(vocab, dmod, device=DEV, dtype=torch.bfloat16))
+    torch.manual_seed(14)
+    h = (0.5 * torch.randn(n, dmod, device=DEV) / dmod ** 0.25).to(torch.bfloat16).requires_grad_(True)
+    w = (0.5 * torch.randn(vocab, dmod, device=DEV) / dmod ** 0.25).to(torch.bfloat16).requires_grad_(True)
+    tgt = torch.randint(0, vocab, (n,), device=DEV)
+    hr, wr = h.detach().float().requires_grad_(True), w.detach().float().requires_grad_(True)
+    lsm = torch.log_softmax(hr @ wr.t(), -1)
+    lpr = lsm.gather(-1, tgt[:, None]).squeeze(-1)
+    entr = -(lsm.exp() * lsm).sum(-1)
+    go, ge = torch.randn(n, device=DEV), torch.randn(n, device=DEV)
+
+    def run():
+        if entropy:
+            lp, ent = L.lm_head_logprob_entropy(h, w, tgt, rows=512)
+            return (lp, ent) + torch.autograd.grad((lp, ent), (h, w), (go, ge))
+        lp = L.lm_head_logprob(h, w, tgt, rows=512)
+        return (lp, None) + torch.autograd.grad(lp, (h, w), go)
+
+    lp, ent, gh, gw = run()
+    if entropy:
+        gr = torch.autograd.grad((lpr, entr), (hr, wr), (go, ge))
+        torch.testing.assert_close(ent, entr, atol=3e-3, rtol=3e-3)
+    else:
+        gr = torch.autograd.grad(lpr, (hr, wr), go)
+    torch.testing.assert_close(lp, lpr, atol=3e-3, rtol=3e-3)
+    assert _rel(gh, gr[0]) < 2e-2
+    assert _rel(gw, gr[1]) < 2e-2
+    # the unfused (cuBLAS logits + row kernel) path agrees
+    L.FUSED_TC = False
+    try:
+        lp2, ent2, gh2, gw2 = run()
+    finally:
+        L.FUSED_TC = True
+    torch.testing.assert_close(lp, lp2, atol=2e-3, rtol=2e-3)
+    assert _rel(gh, gh2) < 1e-2 and _rel(gw, gw2) < 1e-2
+
+
 def test_fold_kernels():
     from thundersync_b200.ops.fold import axpby_, fold_, reduce_adjoints
 

@@ -10,7 +10,9 @@ Families: ``attn`` (bottom-right causal GQA attention; fwd, or fwd+bwd),
 ``rms`` (RMSNorm fwd/bwd), ``lse`` (log-sum-exp/gather over fp32 logits),
 ``gdn`` (gated delta rule fwd/bwd), ``conv`` (causal conv1d + SiLU fwd/bwd),
 ``swiglu``, ``rope`` (QK-norm + RoPE), ``dlogits``, ``adamw``, ``fold``
-(GRPO statistic folds), and ``gemm_host`` (host cost of a library GEMM call).
+(GRPO statistic folds), ``gemm`` (tcgen05 GEMM vs the library at decoder
+shapes), ``lmhead`` (fused tcgen05 LM-head logprob fwd+bwd vs the unfused
+cuBLAS-logits path) and ``gemm_host`` (host cost of a library GEMM call).
 """
 
 from __future__ import annotations
@@ -229,6 +231,27 @@ def bench_gemm(args) -> None:
         print(f"{name:14s} {m}x{n}x{k}: tcgen05 {flops / t_ours / 1e9:7.1f} TFLOP/s, library {flops / t_lib / 1e9:7.1f}")
 
 
+def bench_lmhead(args) -> None:
+    """LM-head logprob forward and forward+backward: fused tcgen05 epilogues vs cuBLAS logits + row kernels."""
+    from thundersync_b200.ops import logprob as L
+
+    n, dmod, vocab = args.rows, args.cols, 151936
+    h = (torch.randn(n, dmod, device="cuda") / dmod ** 0.5).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(vocab, dmod, device="cuda") / dmod ** 0.25).to(torch.bfloat16).requires_grad_(True)
+    tgt = torch.randint(0, vocab, (n,), device="cuda")
+    g = torch.randn(n, device="cuda")
+    flops = 2.0 * n * dmod * vocab
+    for fused in (True, False):
+        L.FUSED_TC = fused
+        with torch.no_grad():
+            t_f = _time(lambda: L.lm_head_logprob(h, w, tgt), args.iters)
+        t_fb = _time(lambda: torch.autograd.grad(L.lm_head_logprob(h, w, tgt), (h, w), g), args.iters)
+        name = "fused tcgen05" if fused else "cuBLAS+rows"
+        print(f"lmhead {name:14s} {n}x{dmod}x{vocab}: fwd {t_f:.3f} ms ({flops / t_f / 1e9:.0f} TFLOP/s), "
+              f"fwd+bwd {t_fb:.3f} ms ({4 * flops / t_fb / 1e9:.0f} TFLOP/s of 4 GEMMs)")
+    L.FUSED_TC = True
+
+
 def bench_gemm_host(args) -> None:
     """Host (CPU) cost of one library GEMM call: repeated shape vs a new row count every call."""
     import time
@@ -257,7 +280,7 @@ def bench_gemm_host(args) -> None:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host", "swiglu", "rope", "dlogits",
-                                       "adamw", "fold", "gemm"])
+                                       "adamw", "fold", "gemm", "lmhead"])
     ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
     ap.add_argument("--t", type=int, default=2048)
     ap.add_argument("--s", type=int, default=2560)
@@ -272,7 +295,8 @@ def main(argv=None) -> None:
     args = ap.parse_args(argv)
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
      "gemm_host": bench_gemm_host, "swiglu": bench_swiglu, "rope": bench_rope, "dlogits": bench_dlogits,
-     "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm}[args.family](args)
+     "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm,
+     "lmhead": bench_lmhead}[args.family](args)
 
 
 if __name__ == "__main__":

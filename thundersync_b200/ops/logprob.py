@@ -7,6 +7,12 @@ block's logits, forms ``dlogits = g·(onehot − softmax)`` (entropy variant:
 ``−p·(g_lp + g_H·(log p + H)) + g_lp·onehot``) in one native pass, and
 produces ``dH`` and the fp32-accumulated ``dW``. Same contract as the
 reference's ``_FusedLinearLogprob`` (src/thundersync/accel/fused_logprob.py:61-308).
+
+On CUDA with bf16 operands both passes run as tcgen05 GEMMs whose epilogue
+consumes the logits tile straight out of tensor memory: the forward keeps an
+online max / sum-of-exp (and sum of exp·x for the entropy) per row and N tile,
+reduced by a second small kernel; the backward's epilogue writes bf16
+``dlogits`` directly. The fp32 [rows, V] logits never reach HBM.
 """
 
 from __future__ import annotations
@@ -17,6 +23,14 @@ from thundersync_b200.ops import sink as _sink
 from thundersync_b200.ops._ext import native
 
 DEFAULT_ROWS = 2048
+# tcgen05 GEMM with fused log-sum-exp / dlogits epilogues on CUDA bf16 (False: cuBLAS logits + row kernels)
+FUSED_TC = True
+
+
+def _fused_ok(hidden: torch.Tensor, weight: torch.Tensor) -> bool:
+    return (FUSED_TC and hidden.is_cuda and hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+            and hidden.shape[1] % 8 == 0 and weight.shape[0] % 8 == 0 and hidden.is_contiguous()
+            and weight.is_contiguous())
 
 
 def _logits_fp32(h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -55,8 +69,17 @@ class _LMHeadLogprob(torch.autograd.Function):
                          device=hidden.device)
         lse = torch.empty_like(lp)
         ent = torch.empty_like(lp) if with_entropy else None
+        fused = _fused_ok(hidden, weight)
         for r0 in range(0, n, rows):
             r1 = min(n, r0 + rows)
+            if fused:
+                a, b, c = native().lmhead_lse_tc(hidden[r0:r1], weight, target[r0:r1].contiguous(),
+                                                 bool(with_entropy))
+                lp[r0:r1] = a
+                lse[r0:r1] = b
+                if with_entropy:
+                    ent[r0:r1] = c
+                continue
             logits = _logits_fp32(hidden[r0:r1], weight)
             if logits.is_cuda and logits.dtype == torch.float32:
                 a, b, c = native().lse_gather(logits, target[r0:r1].contiguous(), bool(with_entropy))
@@ -96,11 +119,22 @@ class _LMHeadLogprob(torch.autograd.Function):
         if need_w and not sink_w:
             dw_acc = torch.zeros(weight.shape, dtype=torch.float32 if weight.dtype != torch.float64 else torch.float64,
                                  device=weight.device)
+        fused = _fused_ok(hidden, weight)
         for r0 in range(0, n, ctx.rows):
             r1 = min(n, r0 + ctx.rows)
             h = hidden[r0:r1]
-            logits = _logits_fp32(h, weight)
-            if logits.is_cuda and logits.dtype == torch.float32:
+            if fused:
+                d = native().lmhead_dlogits_tc(
+                    h, weight, target[r0:r1].contiguous(), lse[r0:r1].contiguous(), g_lp[r0:r1],
+                    None if g_ent is None else g_ent[r0:r1],
+                    None if ent is None else ent[r0:r1].contiguous(),
+                )
+                logits = None
+            else:
+                logits = _logits_fp32(h, weight)
+            if fused:
+                pass
+            elif logits.is_cuda and logits.dtype == torch.float32:
                 d = native().logprob_dlogits(
                     logits, target[r0:r1].contiguous(), lse[r0:r1].contiguous(), g_lp[r0:r1],
                     None if g_ent is None else g_ent[r0:r1],
