@@ -4,7 +4,7 @@
 namespace ts {
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, bool unit);
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                     const at::Tensor& rstd, bool unit);
+                                     const at::Tensor& rstd, bool unit, const c10::optional<at::Tensor>& dres);
 std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
                                          const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                          const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d, double eps,
@@ -58,6 +58,7 @@ void attn_trace_enable(bool on);
 void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
              double alpha);
 at::Tensor attn_trace_read();
+int64_t gemm_tc_pair(int64_t on);
 std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
                                       bool with_entropy);
 at::Tensor lmhead_dlogits_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt, const at::Tensor& lse,
@@ -78,7 +79,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   ts::register_ipc(m);
   ts::register_pinned(m);
   m.def("rms_norm_fwd", &ts::rms_norm_fwd);
-  m.def("rms_norm_bwd", &ts::rms_norm_bwd);
+  m.def("rms_norm_bwd", &ts::rms_norm_bwd, pybind11::arg("dy"), pybind11::arg("x"), pybind11::arg("w"),
+        pybind11::arg("rstd"), pybind11::arg("unit"), pybind11::arg("dres") = pybind11::none());
   m.def("qk_norm_rope_fwd", &ts::qk_norm_rope_fwd, pybind11::arg("qkv"), pybind11::arg("qw"), pybind11::arg("kw"),
         pybind11::arg("pos"), pybind11::arg("inv_freq"), pybind11::arg("hq"), pybind11::arg("hkv"), pybind11::arg("d"),
         pybind11::arg("eps"), pybind11::arg("unit"), pybind11::arg("cos_tab") = pybind11::none(),
@@ -115,6 +117,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_trace_enable", &ts::attn_trace_enable);
   m.def("gemm_tc", &ts::gemm_tc);
   m.def("lmhead_lse_tc", &ts::lmhead_lse_tc);
+  m.def("gemm_tc_pair", &ts::gemm_tc_pair);
   m.def("lmhead_dlogits_tc", &ts::lmhead_dlogits_tc);
   m.def("attn_trace_read", &ts::attn_trace_read);
   m.def("gdn_bwd", &ts::gdn_bwd);

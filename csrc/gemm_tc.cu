@@ -93,6 +93,138 @@ TS_DEVICE void tile_coords(int t, int mt, int nt, int& mb, int& nb) {
   nb = r / gm;
 }
 
+// Epilogue of one output tile for the calling thread's row: reads the row's kBN fp32 accumulator
+// columns from tensor memory at `tacc` (32 at a time) and stores / accumulates / reduces them.
+template <int EPI>
+TS_DEVICE void epilogue_tile(uint32_t tacc, int row, int nb, int M, int N, int ldc, float alpha, void* c,
+                             const LmArgs& lm) {
+  const int col0 = nb * kBN;
+  // LM-head row state (one row per thread)
+  float run_m = -INFINITY, run_s = 0.f, run_t = 0.f, row_lse = 0.f, row_g = 0.f, row_ge = 0.f, row_h = 0.f;
+  int64_t row_tgt = -1;
+  if constexpr (EPI == kLse || EPI == kDlogits) {
+    if (row < M) {
+      row_tgt = lm.tgt[row];
+      if constexpr (EPI == kDlogits) {
+        row_lse = lm.lse[row];
+        row_g = lm.glp[row];
+        if (lm.gent != nullptr) {
+          row_ge = lm.gent[row];
+          row_h = lm.ent[row];
+        }
+      }
+    }
+  }
+#pragma unroll 1
+  for (int cc = 0; cc < kBN; cc += 32) {
+    float v[32];
+    tc::tmem_ld32(tacc + cc, v);
+    tc::tmem_ld_wait();
+    const int col = col0 + cc;
+    if constexpr (EPI == kLse) {
+      if (row < M && col < N) {
+        float cm = -INFINITY;
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          if (col + x < N) cm = fmaxf(cm, v[x] * kLog2eF);
+          if (col + x == row_tgt) lm.tlogit[row] = v[x];
+        }
+        if (cm > run_m) {
+          const float r = ex2f(run_m - cm);
+          run_s *= r;
+          run_t *= r;
+          run_m = cm;
+        }
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          if (col + x < N) {
+            const float e = ex2f(fmaf(v[x], kLog2eF, -run_m));
+            run_s += e;
+            run_t = fmaf(e, v[x], run_t);
+          }
+        }
+      }
+      continue;
+    }
+    if constexpr (EPI == kDlogits) {
+      if (row < M && col < N) {
+        bf16* p = reinterpret_cast<bf16*>(c) + (long long)row * ldc + col;
+        const float l2 = row_lse * kLog2eF;
+        float d[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          const float pr = ex2f(fmaf(v[x], kLog2eF, -l2));
+          float g = row_g;
+          if (lm.gent != nullptr) g += row_ge * ((v[x] - row_lse) + row_h);
+          d[x] = -pr * g + (col + x == row_tgt ? row_g : 0.f);
+        }
+        if (col + 32 <= N) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 u;
+            u.x = pack_bf16(d[x], d[x + 1]);
+            u.y = pack_bf16(d[x + 2], d[x + 3]);
+            u.z = pack_bf16(d[x + 4], d[x + 5]);
+            u.w = pack_bf16(d[x + 6], d[x + 7]);
+            *reinterpret_cast<uint4*>(p + x) = u;
+          }
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x)
+            if (col + x < N) p[x] = __float2bfloat16_rn(d[x]);
+        }
+      }
+      continue;
+    }
+    if (row < M && col < N) {
+      const bool full = col + 32 <= N;
+      if constexpr (EPI == kStoreBf16) {
+        bf16* p = reinterpret_cast<bf16*>(c) + (long long)row * ldc + col;
+        if (full) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 u;
+            u.x = pack_bf16(alpha * v[x], alpha * v[x + 1]);
+            u.y = pack_bf16(alpha * v[x + 2], alpha * v[x + 3]);
+            u.z = pack_bf16(alpha * v[x + 4], alpha * v[x + 5]);
+            u.w = pack_bf16(alpha * v[x + 6], alpha * v[x + 7]);
+            *reinterpret_cast<uint4*>(p + x) = u;
+          }
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x)
+            if (col + x < N) p[x] = __float2bfloat16_rn(alpha * v[x]);
+        }
+      } else {
+        float* p = reinterpret_cast<float*>(c) + (long long)row * ldc + col;
+        if (full) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 4) {
+            float4 o = make_float4(alpha * v[x], alpha * v[x + 1], alpha * v[x + 2], alpha * v[x + 3]);
+            if constexpr (EPI == kAccumF32) {
+              const float4 prev = *reinterpret_cast<const float4*>(p + x);
+              o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
+            }
+            *reinterpret_cast<float4*>(p + x) = o;
+          }
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x)
+            if (col + x < N) p[x] = (EPI == kAccumF32 ? p[x] : 0.f) + alpha * v[x];
+        }
+      }
+    }
+  }
+  if constexpr (EPI == kLse) {
+    if (row < M) {
+      const long long o = (long long)row * lm.ntiles + nb;
+      lm.pm[o] = run_m;
+      lm.ps[o] = run_s;
+      if (lm.pt != nullptr) lm.pt[o] = run_t;
+    }
+  }
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
                                                          const __grid_constant__ CUtensorMap tm_b, void* __restrict__ c,
@@ -205,132 +337,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       tc::tc_fence_after();
       int mb, nb;
       tile_coords(t, mt, nt, mb, nb);
-      const int row = mb * kBM + row_in_tile;
-      const int col0 = nb * kBN;
-      // LM-head row state (one row per thread)
-      float run_m = -INFINITY, run_s = 0.f, run_t = 0.f, row_lse = 0.f, row_g = 0.f, row_ge = 0.f, row_h = 0.f;
-      int64_t row_tgt = -1;
-      if constexpr (EPI == kLse || EPI == kDlogits) {
-        if (row < M) {
-          row_tgt = lm.tgt[row];
-          if constexpr (EPI == kDlogits) {
-            row_lse = lm.lse[row];
-            row_g = lm.glp[row];
-            if (lm.gent != nullptr) {
-              row_ge = lm.gent[row];
-              row_h = lm.ent[row];
-            }
-          }
-        }
-      }
-#pragma unroll 1
-      for (int cc = 0; cc < kBN; cc += 32) {
-        float v[32];
-        tc::tmem_ld32(lane_base + buf * kBN + cc, v);
-        tc::tmem_ld_wait();
-        const int col = col0 + cc;
-        if constexpr (EPI == kLse) {
-          if (row < M && col < N) {
-            float cm = -INFINITY;
-#pragma unroll
-            for (int x = 0; x < 32; ++x) {
-              if (col + x < N) cm = fmaxf(cm, v[x] * kLog2eF);
-              if (col + x == row_tgt) lm.tlogit[row] = v[x];
-            }
-            if (cm > run_m) {
-              const float r = ex2f(run_m - cm);
-              run_s *= r;
-              run_t *= r;
-              run_m = cm;
-            }
-#pragma unroll
-            for (int x = 0; x < 32; ++x) {
-              if (col + x < N) {
-                const float e = ex2f(fmaf(v[x], kLog2eF, -run_m));
-                run_s += e;
-                run_t = fmaf(e, v[x], run_t);
-              }
-            }
-          }
-          continue;
-        }
-        if constexpr (EPI == kDlogits) {
-          if (row < M && col < N) {
-            bf16* p = reinterpret_cast<bf16*>(c) + (long long)row * ldc + col;
-            const float l2 = row_lse * kLog2eF;
-            float d[32];
-#pragma unroll
-            for (int x = 0; x < 32; ++x) {
-              const float pr = ex2f(fmaf(v[x], kLog2eF, -l2));
-              float g = row_g;
-              if (lm.gent != nullptr) g += row_ge * ((v[x] - row_lse) + row_h);
-              d[x] = -pr * g + (col + x == row_tgt ? row_g : 0.f);
-            }
-            if (col + 32 <= N) {
-#pragma unroll
-              for (int x = 0; x < 32; x += 8) {
-                uint4 u;
-                u.x = pack_bf16(d[x], d[x + 1]);
-                u.y = pack_bf16(d[x + 2], d[x + 3]);
-                u.z = pack_bf16(d[x + 4], d[x + 5]);
-                u.w = pack_bf16(d[x + 6], d[x + 7]);
-                *reinterpret_cast<uint4*>(p + x) = u;
-              }
-            } else {
-#pragma unroll
-              for (int x = 0; x < 32; ++x)
-                if (col + x < N) p[x] = __float2bfloat16_rn(d[x]);
-            }
-          }
-          continue;
-        }
-        if (row < M && col < N) {
-          const bool full = col + 32 <= N;
-          if constexpr (EPI == kStoreBf16) {
-            bf16* p = reinterpret_cast<bf16*>(c) + (long long)row * ldc + col;
-            if (full) {
-#pragma unroll
-              for (int x = 0; x < 32; x += 8) {
-                uint4 u;
-                u.x = pack_bf16(alpha * v[x], alpha * v[x + 1]);
-                u.y = pack_bf16(alpha * v[x + 2], alpha * v[x + 3]);
-                u.z = pack_bf16(alpha * v[x + 4], alpha * v[x + 5]);
-                u.w = pack_bf16(alpha * v[x + 6], alpha * v[x + 7]);
-                *reinterpret_cast<uint4*>(p + x) = u;
-              }
-            } else {
-#pragma unroll
-              for (int x = 0; x < 32; ++x)
-                if (col + x < N) p[x] = __float2bfloat16_rn(alpha * v[x]);
-            }
-          } else {
-            float* p = reinterpret_cast<float*>(c) + (long long)row * ldc + col;
-            if (full) {
-#pragma unroll
-              for (int x = 0; x < 32; x += 4) {
-                float4 o = make_float4(alpha * v[x], alpha * v[x + 1], alpha * v[x + 2], alpha * v[x + 3]);
-                if constexpr (EPI == kAccumF32) {
-                  const float4 prev = *reinterpret_cast<const float4*>(p + x);
-                  o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
-                }
-                *reinterpret_cast<float4*>(p + x) = o;
-              }
-            } else {
-#pragma unroll
-              for (int x = 0; x < 32; ++x)
-                if (col + x < N) p[x] = (EPI == kAccumF32 ? p[x] : 0.f) + alpha * v[x];
-            }
-          }
-        }
-      }
-      if constexpr (EPI == kLse) {
-        if (row < M) {
-          const long long o = (long long)row * lm.ntiles + nb;
-          lm.pm[o] = run_m;
-          lm.ps[o] = run_s;
-          if (lm.pt != nullptr) lm.pt[o] = run_t;
-        }
-      }
+      epilogue_tile<EPI>(lane_base + buf * kBN, mb * kBM + row_in_tile, nb, M, N, ldc, alpha, c, lm);
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->acc_empty[buf]);
     }
@@ -341,6 +348,198 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
+}
+
+// ------------------------------------------------------------------ CTA-pair kernel (cta_group::2)
+// A cluster of two CTAs on two SMs computes a 256 x 256 tile: each CTA
+// stages 128 rows of A and 128 rows (N) of B per K block, the even CTA
+// issues tcgen05.mma.cta_group::2 (M = 256) over both CTAs' shared memory,
+// and each CTA's tensor memory receives its 128 rows of the accumulator.
+// Per SM that halves the B bytes staged per MMA against the single-CTA
+// 128 x 256 tile (32 KB instead of 48 KB per 64-deep K block). Every TMA
+// load of the pair counts its bytes on the even CTA's `full` barrier; the
+// MMA completion arrives on the `empty` / `acc_full` barriers of both CTAs;
+// the eight epilogue warps of the pair arrive on the even CTA's
+// `acc_empty`. Loads have no multicast: each CTA reads its own rows.
+constexpr int kStagesP = 6;
+constexpr uint32_t kBHalfBytes = 128 * kBK * 2;                 // 16 KB
+constexpr uint32_t kStagePBytes = kABytes + kBHalfBytes;        // 32 KB per CTA
+constexpr uint32_t kBarOffP = kStagesP * kStagePBytes;          // 192 KB
+constexpr uint32_t kSmemP = kBarOffP + 256;
+static_assert(kSmemP + 1024 <= 232448, "pair GEMM shared memory");
+
+struct PairBars {
+  uint64_t full[kStagesP], empty[kStagesP], acc_full[2], acc_empty[2];
+  uint32_t tmem_slot;
+  int abort;
+};
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     void* __restrict__ c, int M, int N, int K, int ldc, float alpha, int* __restrict__ err,
+                     LmArgs lm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + kBarOffP);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_rank();
+  const int mt = (M + 2 * kBM - 1) / (2 * kBM), nt = (N + kBN - 1) / kBN, kt = (K + kBK - 1) / kBK;
+  const int tiles = mt * nt;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesP; ++s) {
+      tc::mbar_init(&bars->full[s], 1);
+      tc::mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&bars->acc_full[b], 1);
+      tc::mbar_init(&bars->acc_empty[b], 8);  // one arrival per epilogue warp of the pair
+    }
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) tc::tmem_alloc_pair(&bars->tmem_slot, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // both CTAs' barriers exist before any remote arrive or byte count
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_a);
+      tc::prefetch_tmap(&tm_b);
+      int it = 0;
+      for (int t = cid; t < tiles; t += ncl) {
+        int mb, nb;
+        tile_coords(t, mt, nt, mb, nb);
+        const int arow = mb * 2 * kBM + (int)rank * kBM;
+        const int bcol = nb * kBN + (int)rank * (kBN / 2);
+        for (int kb = 0; kb < kt; ++kb, ++it) {
+          const int s = it % kStagesP;
+          if (it >= kStagesP && !tc::mbar_wait(&bars->empty[s], ((it - kStagesP) / kStagesP) & 1, abort, err, 231))
+            goto producer_done;
+          if (rank == 0) tc::mbar_expect_tx(&bars->full[s], 2 * kStagePBytes);
+          const uint32_t full0 = tc::map_cluster(tc::smem_addr(&bars->full[s]), 0);
+          uint8_t* a = smem + s * kStagePBytes;
+          uint8_t* b = a + kABytes;
+          if constexpr (!A_MN) {
+            tc::tma_load_2d_pair(a, &tm_a, kb * kBK, arow, full0);  // box 64 (k) x 128 (m)
+          } else {
+            tc::tma_load_2d_pair(a, &tm_a, arow, kb * kBK, full0);  // [K][M]: 2 boxes of 64 m x 64 k
+            tc::tma_load_2d_pair(a + 64 * 128, &tm_a, arow + 64, kb * kBK, full0);
+          }
+          if constexpr (!B_MN) {
+            tc::tma_load_2d_pair(b, &tm_b, kb * kBK, bcol, full0);  // box 64 (k) x 128 (n)
+          } else {
+            tc::tma_load_2d_pair(b, &tm_b, bcol, kb * kBK, full0);  // [K][N]: 2 boxes of 64 n x 64 k
+            tc::tma_load_2d_pair(b + 64 * 128, &tm_b, bcol + 64, kb * kBK, full0);
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = tc::idesc_bf16(2 * kBM, kBN, A_MN, B_MN);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < tiles; t += ncl, ++local) {
+        const int buf = local & 1;
+        if (local >= 2 && !tc::mbar_wait(&bars->acc_empty[buf], ((local - 2) >> 1) & 1, abort, err, 241)) break;
+        tc::tc_fence_after();
+        const uint32_t acc = tmem + buf * kBN;
+        for (int kb = 0; kb < kt; ++kb, ++it) {
+          const int s = it % kStagesP;
+          if (!tc::mbar_wait(&bars->full[s], (it / kStagesP) & 1, abort, err, 242)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a = sbase + s * kStagePBytes;
+          const uint32_t b = a + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? tc::sdesc_sw128(a + kk * 16 * 128, 64 * 128, 1024)
+                                     : tc::sdesc_sw128(a + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? tc::sdesc_sw128(b + kk * 16 * 128, 64 * 128, 1024)
+                                     : tc::sdesc_sw128(b + kk * 32, 16, 1024);
+            tc::mma_bf16_pair(acc, ad, bd, idesc, kb > 0 || kk > 0);
+          }
+          tc::mma_commit_pair(&bars->empty[s]);
+        }
+        if (ok) tc::mma_commit_pair(&bars->acc_full[buf]);
+      }
+    }
+  } else {
+    const int sub = warp & 3;
+    const uint32_t lane_base = tmem + ((uint32_t)(sub * 32) << 16);
+    const uint32_t acc_empty0 = tc::map_cluster(tc::smem_addr(&bars->acc_empty[0]), 0);
+    const uint32_t acc_empty1 = tc::map_cluster(tc::smem_addr(&bars->acc_empty[1]), 0);
+    int local = 0;
+    for (int t = cid; t < tiles; t += ncl, ++local) {
+      const int buf = local & 1;
+      bool ok = true;
+      if (lane == 0) ok = tc::mbar_wait(&bars->acc_full[buf], (local >> 1) & 1, abort, err, 251);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      tc::tc_fence_after();
+      int mb, nb;
+      tile_coords(t, mt, nt, mb, nb);
+      const int row = mb * 2 * kBM + (int)rank * kBM + sub * 32 + lane;
+      epilogue_tile<EPI>(lane_base + buf * kBN, row, nb, M, N, ldc, alpha, c, lm);
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cluster(buf ? acc_empty1 : acc_empty0);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // no CTA leaves while its pair may still read its shared memory or arrive on it
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+// 0: single-CTA 128 x 256 tiles; 1: CTA-pair 256 x 256 tiles (default)
+int g_gemm_pair = 1;
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int ldc, float alpha,
+                 int device, LmArgs lm) {
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
+  const int smem = kSmemP + 1024;
+  static int resident[16] = {0};  // co-resident CTA pairs per device (persistent grid size)
+  int& pairs = resident[device & 15];
+  if (pairs == 0) {
+    TS_CUDA_CHECK(cudaFuncSetAttribute(gemm_pair_kernel<A_MN, B_MN, EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * sm_count(device));
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<A_MN, B_MN, EPI>, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = sm_count(device) / 2;
+    }
+    pairs = std::min(n, sm_count(device) / 2);
+  }
+  const int clusters = std::max(1, std::min(tiles, pairs));
+  gemm_pair_kernel<A_MN, B_MN, EPI><<<2 * clusters, 192, smem, stream()>>>(
+      ma, mb, c, M, N, K, ldc, alpha, tc_error_flag(at::Device(at::kCUDA, device)).data_ptr<int>(), lm);
 }
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -392,6 +591,13 @@ __global__ void lse_reduce_kernel(const float* __restrict__ pm, const float* __r
 
 }  // namespace
 
+// Select the GEMM kernel: 1 = CTA-pair 256 x 256 tiles, 0 = single-CTA 128 x 256 tiles. Returns the previous value.
+int64_t gemm_tc_pair(int64_t on) {
+  const int prev = g_gemm_pair;
+  if (on >= 0) g_gemm_pair = on ? 1 : 0;
+  return prev;
+}
+
 // Fused LM-head forward: lp[r] = log softmax(h W^T)[r, tgt[r]] (+ entropy), lse[r];
 // h [R, D] bf16, w [V, D] bf16; the logits never reach memory.
 std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
@@ -415,9 +621,11 @@ std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, 
   LmArgs lm{tgt.data_ptr<int64_t>(), pm.data_ptr<float>(), ps.data_ptr<float>(),
             with_entropy ? pt.data_ptr<float>() : nullptr, tl.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr,
             ntiles};
+  const bool pair = g_gemm_pair != 0;
   const CUtensorMap ma = make_bf16_map(h.data_ptr(), D, R, D, 128);
-  const CUtensorMap mb = make_bf16_map(w.data_ptr(), D, V, D, 256);
-  launch<false, false, kLse>(ma, mb, nullptr, R, V, D, V, 1.f, h.get_device(), lm);
+  const CUtensorMap mb = make_bf16_map(w.data_ptr(), D, V, D, pair ? 128 : 256);
+  if (pair) launch_pair<false, false, kLse>(ma, mb, nullptr, R, V, D, V, 1.f, h.get_device(), lm);
+  else launch<false, false, kLse>(ma, mb, nullptr, R, V, D, V, 1.f, h.get_device(), lm);
   lse_reduce_kernel<<<(R + 7) / 8, 256, 0, stream()>>>(pm.data_ptr<float>(), ps.data_ptr<float>(),
                                                        with_entropy ? pt.data_ptr<float>() : nullptr,
                                                        tl.data_ptr<float>(), lp.data_ptr<float>(),
@@ -439,9 +647,11 @@ at::Tensor lmhead_dlogits_tc(const at::Tensor& h, const at::Tensor& w, const at:
   if (R == 0) return d;
   LmArgs lm{tgt.data_ptr<int64_t>(), nullptr, nullptr, nullptr, nullptr, lse.data_ptr<float>(), glp.data_ptr<float>(),
             gent ? gent->data_ptr<float>() : nullptr, ent ? ent->data_ptr<float>() : nullptr, 0};
+  const bool pair = g_gemm_pair != 0;
   const CUtensorMap ma = make_bf16_map(h.data_ptr(), D, R, D, 128);
-  const CUtensorMap mb = make_bf16_map(w.data_ptr(), D, V, D, 256);
-  launch<false, false, kDlogits>(ma, mb, d.data_ptr(), R, V, D, V, 1.f, h.get_device(), lm);
+  const CUtensorMap mb = make_bf16_map(w.data_ptr(), D, V, D, pair ? 128 : 256);
+  if (pair) launch_pair<false, false, kDlogits>(ma, mb, d.data_ptr(), R, V, D, V, 1.f, h.get_device(), lm);
+  else launch<false, false, kDlogits>(ma, mb, d.data_ptr(), R, V, D, V, 1.f, h.get_device(), lm);
   TS_LAUNCH_CHECK();
   return d;
 }
@@ -474,15 +684,24 @@ void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t
     return;
   }
   // tensor maps: inner dimension first; boxes of 64 inner elements
+  const bool pair = g_gemm_pair != 0;
   const CUtensorMap ma = a_t ? make_bf16_map(a.data_ptr(), M, K, M, 64) : make_bf16_map(a.data_ptr(), K, M, K, 128);
-  const CUtensorMap mb = b_t ? make_bf16_map(b.data_ptr(), K, N, K, 256) : make_bf16_map(b.data_ptr(), N, K, N, 64);
+  const CUtensorMap mb = b_t ? make_bf16_map(b.data_ptr(), K, N, K, pair ? 128 : 256)
+                             : make_bf16_map(b.data_ptr(), N, K, N, 64);
   const int dev = a.get_device();
   void* c = out.data_ptr();
   const float al = (float)alpha;
-#define TS_GEMM_CASE(AM, BM)                                                          \
-  if (mode == 0) launch<AM, BM, kStoreBf16>(ma, mb, c, M, N, K, (int)N, al, dev);    \
-  else if (mode == 1) launch<AM, BM, kStoreF32>(ma, mb, c, M, N, K, (int)N, al, dev); \
-  else launch<AM, BM, kAccumF32>(ma, mb, c, M, N, K, (int)N, al, dev);
+  const LmArgs none{};
+#define TS_GEMM_CASE(AM, BM)                                                                                  \
+  if (pair) {                                                                                                 \
+    if (mode == 0) launch_pair<AM, BM, kStoreBf16>(ma, mb, c, M, N, K, (int)N, al, dev, none);               \
+    else if (mode == 1) launch_pair<AM, BM, kStoreF32>(ma, mb, c, M, N, K, (int)N, al, dev, none);           \
+    else launch_pair<AM, BM, kAccumF32>(ma, mb, c, M, N, K, (int)N, al, dev, none);                          \
+  } else {                                                                                                    \
+    if (mode == 0) launch<AM, BM, kStoreBf16>(ma, mb, c, M, N, K, (int)N, al, dev);                          \
+    else if (mode == 1) launch<AM, BM, kStoreF32>(ma, mb, c, M, N, K, (int)N, al, dev);                      \
+    else launch<AM, BM, kAccumF32>(ma, mb, c, M, N, K, (int)N, al, dev);                                     \
+  }
   if (!a_t && b_t) {
     TS_GEMM_CASE(false, false)
   } else if (!a_t && !b_t) {

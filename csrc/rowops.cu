@@ -112,6 +112,89 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_dx_kernel(const T* __rest
   }
 }
 
+// ----------------------------------------------------------------- RMSNorm bwd (dx + dw partials)
+// One pass over dy and x: each warp walks rows blockIdx.x*kWarps + warp,
+// + gridDim.x*kWarps, ...; it writes dx (+ dres, the residual branch's
+// gradient, added before the single rounding) and keeps the weight-gradient
+// column sums of its rows in registers. The block's warps are then added in
+// warp order in shared memory and the block writes one partial row; the
+// partial rows are summed in block order by sum_partials_kernel. The grid
+// size depends only on the row count and the SM count, so the sums are
+// reproducible run to run.
+template <typename T, int V>
+__global__ void __launch_bounds__(kWarps * 32) rms_bwd_fused_kernel(
+    const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w, const float* __restrict__ rstd,
+    const T* __restrict__ dres, T* __restrict__ dx, float* __restrict__ partial, int rows, int H, float woff) {
+  extern __shared__ float red[];
+  constexpr int E = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float acc[V][E];
+#pragma unroll
+  for (int v = 0; v < V; ++v)
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[v][e] = 0.f;
+  for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
+    const float r = rstd[row];
+    const T* xr = x + (size_t)row * H;
+    const T* dyr = dy + (size_t)row * H;
+    Vec<T> xb[V], db[V];
+    float dot = 0.f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * 32 + lane) * E;
+      if (c < H) {
+        xb[v] = load_vec(xr + c);
+        db[v] = load_vec(dyr + c);
+        Vec<T> wv = load_vec(w + c);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float n = to_f(xb[v].e[e]) * r;
+          const float d = to_f(db[v].e[e]);
+          dot += d * (to_f(wv.e[e]) + woff) * n;
+          acc[v][e] += d * n;
+        }
+      }
+    }
+    dot = warp_sum(dot) / (float)H;
+    T* dxr = dx + (size_t)row * H;
+    const T* rr = dres == nullptr ? nullptr : dres + (size_t)row * H;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * 32 + lane) * E;
+      if (c < H) {
+        Vec<T> wv = load_vec(w + c);
+        Vec<T> res;
+        if (rr != nullptr) res = load_vec(rr + c);
+        Vec<T> o;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float n = to_f(xb[v].e[e]) * r;
+          const float dn = to_f(db[v].e[e]) * (to_f(wv.e[e]) + woff);
+          float g = r * (dn - n * dot);
+          if (rr != nullptr) g += to_f(res.e[e]);
+          o.e[e] = from_f<T>(g);
+        }
+        store_vec(dxr + c, o);
+      }
+    }
+  }
+  for (int k = 0; k < kWarps; ++k) {
+    if (warp == k) {
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const int c = (v * 32 + lane) * E;
+        if (c < H) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) red[c + e] = k == 0 ? acc[v][e] : red[c + e] + acc[v][e];
+        }
+      }
+    }
+    __syncthreads();
+  }
+  for (int c = threadIdx.x; c < H; c += blockDim.x) partial[(size_t)blockIdx.x * H + c] = red[c];
+}
+
 // ----------------------------------------------------------------- column partial sums
 // partial[chunk, c] = sum over the chunk's rows of dy[r, c] * x[r, c] * rstd[r].
 // Block = 32 x 8 threads: x-dim walks 16-byte column vectors, y-dim rows.
@@ -221,6 +304,35 @@ void rms_fwd_dispatch(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, a
   else if (nv <= 12) launch_rms_fwd<T, 12>(x, w, y, rstd, eps, unit);
   else if (nv <= 16) launch_rms_fwd<T, 16>(x, w, y, rstd, eps, unit);
   else TS_CHECK(false, "RMSNorm row width ", H, " is too large");
+}
+
+template <typename T, int V>
+at::Tensor launch_rms_bwd_fused(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                const at::Tensor& rstd, const T* dres, at::Tensor& dx, float woff) {
+  const int rows = x.size(0), H = x.size(1);
+  const int grid = std::max(1, std::min((rows + kWarps - 1) / kWarps, sm_count(x.get_device())));
+  auto partial = at::empty({grid, H}, x.options().dtype(at::kFloat));
+  auto dw = at::empty({H}, x.options().dtype(at::kFloat));
+  rms_bwd_fused_kernel<T, V><<<grid, kWarps * 32, H * sizeof(float), stream()>>>(
+      (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)w.data_ptr(), rstd.data_ptr<float>(), dres,
+      (T*)dx.data_ptr(), partial.data_ptr<float>(), rows, H, woff);
+  sum_partials_kernel<<<(H + 31) / 32, dim3(32, 8), 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
+                                                                     grid, H);
+  return dw;
+}
+
+// dx (+ dres) and dw in two launches for rows up to 8 vectors per lane; empty tensor otherwise.
+template <typename T>
+at::Tensor rms_bwd_fused_dispatch(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                  const at::Tensor& rstd, const T* dres, at::Tensor& dx, float woff) {
+  constexpr int E = Vec<T>::N;
+  const int H = x.size(1);
+  const int nv = (H + 32 * E - 1) / (32 * E);
+  if (nv <= 1) return launch_rms_bwd_fused<T, 1>(dy, x, w, rstd, dres, dx, woff);
+  if (nv <= 2) return launch_rms_bwd_fused<T, 2>(dy, x, w, rstd, dres, dx, woff);
+  if (nv <= 4) return launch_rms_bwd_fused<T, 4>(dy, x, w, rstd, dres, dx, woff);
+  if (nv <= 8) return launch_rms_bwd_fused<T, 8>(dy, x, w, rstd, dres, dx, woff);
+  return at::Tensor();
 }
 
 template <typename T>
@@ -509,23 +621,39 @@ std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, d
   return {y, rstd};
 }
 
+// dres (optional): gradient of a residual branch added to dx before its rounding.
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                     const at::Tensor& rstd, bool unit) {
+                                     const at::Tensor& rstd, bool unit, const c10::optional<at::Tensor>& dres) {
   check_cuda(dy, "dy");
   check_cuda(x, "x");
   const c10::cuda::CUDAGuard guard(x.device());
   auto dx = at::empty_like(x);
   at::Tensor dw;
   const int H = x.size(1);
+  if (dres) {
+    TS_CHECK(dres->is_contiguous() && dres->sizes() == x.sizes() && dres->scalar_type() == x.scalar_type(),
+             "rms_norm_bwd: dres must be a contiguous tensor shaped and typed like x");
+  }
   if (x.size(0) == 0) return {dx, at::zeros({H}, x.options().dtype(at::kFloat))};
   if (x.scalar_type() == at::kBFloat16) {
     TS_CHECK(H % 8 == 0, "row width must be a multiple of 8");
-    rms_dx_dispatch<__nv_bfloat16>(dy, x, w, rstd, dx, unit ? 1.f : 0.f);
-    dw = column_weight_grad<__nv_bfloat16>(dy, x, rstd);
+    using T = __nv_bfloat16;
+    dw = rms_bwd_fused_dispatch<T>(dy, x, w, rstd, dres ? (const T*)dres->data_ptr() : nullptr, dx,
+                                   unit ? 1.f : 0.f);
+    if (!dw.defined()) {
+      rms_dx_dispatch<T>(dy, x, w, rstd, dx, unit ? 1.f : 0.f);
+      dw = column_weight_grad<T>(dy, x, rstd);
+      if (dres) dx.add_(*dres);
+    }
   } else if (x.scalar_type() == at::kFloat) {
     TS_CHECK(H % 4 == 0, "row width must be a multiple of 4");
-    rms_dx_dispatch<float>(dy, x, w, rstd, dx, unit ? 1.f : 0.f);
-    dw = column_weight_grad<float>(dy, x, rstd);
+    dw = rms_bwd_fused_dispatch<float>(dy, x, w, rstd, dres ? dres->data_ptr<float>() : nullptr, dx,
+                                       unit ? 1.f : 0.f);
+    if (!dw.defined()) {
+      rms_dx_dispatch<float>(dy, x, w, rstd, dx, unit ? 1.f : 0.f);
+      dw = column_weight_grad<float>(dy, x, rstd);
+      if (dres) dx.add_(*dres);
+    }
   } else {
     TS_CHECK(false, "rms_norm_bwd: unsupported dtype");
   }

@@ -180,5 +180,58 @@ TS_DEVICE uint32_t kmajor_off(int row, int col, int rows) {
 
 TS_DEVICE uint32_t elect_lane0() { return (threadIdx.x & 31) == 0; }
 
+// ------------------------------------------------------------------ CTA pairs (cluster of 2, cta_group::2)
+TS_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `local` (a shared::cta address) in cluster CTA `rank`
+TS_DEVICE uint32_t map_cluster(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+// every thread of every CTA of the cluster
+TS_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+TS_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile load into this CTA's shared memory whose completion bytes are counted on
+// an mbarrier of either CTA of the pair (`bar_cluster` is a shared::cluster address).
+TS_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];\n" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+TS_DEVICE void tmem_alloc_pair(uint32_t* slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(slot)), "r"(cols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::);
+}
+TS_DEVICE void tmem_dealloc_pair(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(base), "r"(cols));
+}
+// D[256 x N] (+)= A · B over the CTA pair: each CTA holds 128 rows of A and N/2 rows of B at the same
+// shared-memory offsets, and 128 rows of D in its tensor memory. Issued by the even CTA.
+TS_DEVICE void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u));
+}
+// arrive once on the mbarrier at the same offset in both CTAs of the pair when the issued MMAs complete
+TS_DEVICE void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n" ::"r"(
+          smem_addr(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
 }  // namespace tc
 }  // namespace ts

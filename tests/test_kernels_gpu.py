@@ -44,6 +44,14 @@ def test_rms_norm(rows, h):
     # deterministic weight gradient
     gx2, gw2 = torch.autograd.grad(rms_norm(x, w, 1e-6), (x, w), dy)
     assert torch.equal(gw, gw2)
+    # residual-branch gradient added inside the kernel before the single rounding of dx
+    from thundersync_b200.ops._ext import native
+
+    _, rstd = native().rms_norm_fwd(x.detach(), w.detach(), 1e-6, False)
+    dres = torch.randn_like(dy)
+    dx_r, dw_r = native().rms_norm_bwd(dy, x.detach(), w.detach(), rstd, False, dres)
+    torch.testing.assert_close(dx_r.float(), (gxr + dres.float()), atol=2e-2, rtol=1e-2)
+    assert torch.equal(dw_r, native().rms_norm_bwd(dy, x.detach(), w.detach(), rstd, False)[1])
 
 
 @pytest.mark.parametrize("d,hq,hkv,norm", [(128, 4, 2, True), (64, 8, 8, True), (128, 2, 1, False), (256, 4, 1, True)])
@@ -318,9 +326,22 @@ def test_attention_tcgen05_backward(t, s, hq, hkv, d):
     assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)
 
 
+@pytest.mark.parametrize("pair", [True, False])
 @pytest.mark.parametrize("m,n,k", [(256, 512, 128), (304, 200, 72), (2304, 4096, 2048), (128, 151936 // 8, 256)])
 @pytest.mark.parametrize("a_t,b_t", [(False, True), (False, False), (True, False), (True, True)])
-def test_gemm_tcgen05(m, n, k, a_t, b_t):
+def test_gemm_tcgen05(m, n, k, a_t, b_t, pair):
+    """Single-CTA and CTA-pair (cta_group::2) kernels against an fp32 PyTorch matmul."""
+    from thundersync_b200.ops._ext import native
+    from thundersync_b200.ops.gemm import gemm, gemm_accumulate
+
+    prev = native().gemm_tc_pair(1 if pair else 0)
+    try:
+        _check_gemm(m, n, k, a_t, b_t)
+    finally:
+        native().gemm_tc_pair(prev)
+
+
+def _check_gemm(m, n, k, a_t, b_t):
     from thundersync_b200.ops.gemm import gemm, gemm_accumulate
 
     torch.manual_seed(m + n + k)

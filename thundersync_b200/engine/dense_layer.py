@@ -90,7 +90,7 @@ class DenseLayer(torch.autograd.Function):
         o = outs[0] if len(outs) == 1 else torch.cat(outs, 0)
         o = o.reshape(t, hq * d)
         c_o = _Ctx((True, False, need_w))
-        h1 = h + _Linear.forward(c_o, o, None, wo)
+        h1 = _Linear.forward_residual(c_o, o, None, h, wo)
         c_n2 = _Ctx((True, need_w, False, False))
         x2 = _RMSNorm.forward(c_n2, h1, ln2, eps, False)
         c_gu = _Ctx((True, False, need_w, need_w))
@@ -98,10 +98,13 @@ class DenseLayer(torch.autograd.Function):
         c_sw = _Ctx((True,))
         a = _SwiGLU.forward(c_sw, gu)
         c_dn = _Ctx((True, False, need_w))
-        out = h1 + _Linear.forward(c_dn, a, None, wd)
+        out = _Linear.forward_residual(c_dn, a, None, h1, wd)
         ctx.stages = (c_n1, c_qkv, c_rope, c_att, c_o, c_n2, c_gu, c_sw, c_dn)
+        # K/V outputs that no descendant reads get None gradients, not zero-filled tensors
+        ctx.set_materialize_grads(False)
         ctx.meta = meta
         ctx.t = t
+        ctx.out_shape, ctx.out_dtype, ctx.out_device = out.shape, out.dtype, out.device
         return out, k, v
 
     @staticmethod
@@ -109,17 +112,28 @@ class DenseLayer(torch.autograd.Function):
         c_n1, c_qkv, c_rope, c_att, c_o, c_n2, c_gu, c_sw, c_dn = ctx.stages
         hq, hkv, d, eps, scale, segs, n_past, qkv_fused, gu_fused, has_qk = ctx.meta
         t = ctx.t
+        if dout is None:
+            dout = torch.zeros(ctx.out_shape, dtype=ctx.out_dtype, device=ctx.out_device)
         # h_out = h1 + down(swiglu(gu(norm2(h1))))
         da, _, gwd = _Linear.backward(c_dn, dout)
         dgu = _SwiGLU.backward(c_sw, da)
         dx2, _, gwg, gwu = _Linear.backward(c_gu, dgu)
-        dh1_n, gln2, _, _ = _RMSNorm.backward(c_n2, dx2)
-        dh1 = dout + dh1_n
+        dh1, gln2, _, _ = _RMSNorm.backward_residual(c_n2, dx2, dout)
         # h1 = h + o_proj(o)
         do_, _, gwo = _Linear.backward(c_o, dh1)
         do_ = do_.reshape(t, hq, d)
         covered = sum(s1 - s0 for _, s0, s1, _, _ in c_att)
         single = len(c_att) == 1 and covered == t
+        if single and not c_att[0][4]:
+            # one segment over the whole pack, no own-pack key ranges: the attention gradients are the outputs
+            c, s0, s1, npast, _ = c_att[0]
+            g = _ChunkedAttention.backward(c, do_)
+            n = npast + 1
+            gks, gvs = g[3:3 + n], g[3 + n:3 + 2 * n]
+            dk = gks[-1] if dk_out is None else dk_out + gks[-1]
+            dv = gvs[-1] if dv_out is None else dv_out + gvs[-1]
+            return DenseLayer._finish(ctx, g[0], dk, dv, list(gks[:npast]), list(gvs[:npast]), dh1, gln2, gwo,
+                                      gwg, gwu, gwd)
         dq = None if single else torch.zeros(t, hq, d, dtype=do_.dtype, device=do_.device)
         dk = torch.zeros(t, hkv, d, dtype=do_.dtype, device=do_.device) if dk_out is None else dk_out.clone()
         dv = torch.zeros(t, hkv, d, dtype=do_.dtype, device=do_.device) if dv_out is None else dv_out.clone()
@@ -142,10 +156,15 @@ class DenseLayer(torch.autograd.Function):
                 dv[a:b] += gvs[npast + j]
             dk[s0:s1] += gks[-1]
             dv[s0:s1] += gvs[-1]
+        return DenseLayer._finish(ctx, dq, dk, dv, dpast_k, dpast_v, dh1, gln2, gwo, gwg, gwu, gwd)
+
+    @staticmethod
+    def _finish(ctx, dq, dk, dv, dpast_k, dpast_v, dh1, gln2, gwo, gwg, gwu, gwd):
+        c_n1, c_qkv, c_rope = ctx.stages[:3]
+        has_qk = ctx.meta[9]
         dqkv, gqn, gkn, *_ = _QKNormRope.backward(c_rope, dq, dk, dv)
         dx1, _, gwq, gwk, gwv = _Linear.backward(c_qkv, dqkv)
-        dh_n, gln1, _, _ = _RMSNorm.backward(c_n1, dx1)
-        dh = dh1 + dh_n
+        dh, gln1, _, _ = _RMSNorm.backward_residual(c_n1, dx1, dh1)
         ctx.stages = None
         params = [gln1, gwq, gwk, gwv] + ([gqn, gkn] if has_qk else []) + [gwo, gln2, gwg, gwu, gwd]
         return (dh, None, None, None, *dpast_k, *dpast_v, *params)

@@ -200,7 +200,18 @@ def bench_fold(args) -> None:
 
 
 def bench_gemm(args) -> None:
-    """tcgen05 GEMM vs the library GEMM on the decoder's projection shapes (M = padded tokens)."""
+    """tcgen05 GEMM (CTA-pair, then single-CTA kernel) vs the library GEMM on the decoder's projection shapes."""
+    ext = native()
+    for pair in (1, 0):
+        prev = ext.gemm_tc_pair(pair)
+        print(f"-- tcgen05 kernel: {'CTA pair, 256x256 tiles' if pair else 'single CTA, 128x256 tiles'}")
+        try:
+            _bench_gemm_shapes(args)
+        finally:
+            ext.gemm_tc_pair(prev)
+
+
+def _bench_gemm_shapes(args) -> None:
     from thundersync_b200.ops.gemm import gemm, gemm_accumulate
 
     m = args.rows

@@ -20,13 +20,23 @@ from thundersync_b200.ops import sink as _sink
 class _Linear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, fused, *weights):
+        return _Linear.forward_residual(ctx, x, fused, None, *weights)
+
+    @staticmethod
+    def forward_residual(ctx, x, fused, residual, *weights):
+        """``residual + x @ Wᵀ``; on CUDA the add is the GEMM's C operand (one rounding, no separate kernel)."""
         if fused is not None:
             w = fused
         elif len(weights) == 1:
             w = weights[0]
         else:
             w = torch.cat(weights, 0)
-        y = F.linear(x, w)
+        if residual is None:
+            y = F.linear(x, w)
+        elif x.is_cuda and x.dim() == 2:
+            y = torch.addmm(residual, x, w.t())
+        else:
+            y = residual + F.linear(x, w)
         ctx.save_for_backward(x, w)
         ctx.n_weights = len(weights)
         ctx.rows = [t.shape[0] for t in weights]

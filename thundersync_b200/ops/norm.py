@@ -52,14 +52,23 @@ class _RMSNorm(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
+        return _RMSNorm.backward_residual(ctx, dy, None)
+
+    @staticmethod
+    def backward_residual(ctx, dy, dres):
+        """The VJP with ``dres`` (a residual branch's gradient, shaped like x) added to dx; on CUDA the add is
+        fused into the kernel before the single rounding of dx."""
         x2, w, rstd = ctx.saved_tensors
         dy2 = dy.reshape(x2.shape)
         if not dy2.is_contiguous():
             dy2 = dy2.contiguous()
         if dy2.is_cuda:
-            dx, dw = native().rms_norm_bwd(dy2, x2, w.contiguous(), rstd, bool(ctx.unit))
+            r2 = None if dres is None else dres.reshape(x2.shape).contiguous()
+            dx, dw = native().rms_norm_bwd(dy2, x2, w.contiguous(), rstd, bool(ctx.unit), r2)
         else:
             dx, dw = _ref_backward(dy2, x2, w, rstd, ctx.unit)
+            if dres is not None:
+                dx = dres.reshape(dx.shape) + dx
         dw_out = None
         if ctx.needs_input_grad[1]:
             s = _sink.active()
