@@ -267,6 +267,9 @@ def main() -> None:
     ap.add_argument("--profile-out", default=None,
                     help="after the timed region, run one more step under torch.profiler and write the per-kernel "
                          "CUDA time table to this file (rank 0; not part of any reported number)")
+    ap.add_argument("--cprofile-out", default=None,
+                    help="after the timed region, run one more step under cProfile and write the host-side "
+                         "function table (by own time) to this file (rank 0; not part of any reported number)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("at least 3 warm-up steps are required")
@@ -303,7 +306,8 @@ def main() -> None:
             return
         raise
 
-    works = [make_step(rank, s, args) for s in range(args.warmup + args.steps + (1 if args.profile_out else 0))]
+    extra = (1 if args.profile_out else 0) + (1 if args.cprofile_out else 0)
+    works = [make_step(rank, s, args) for s in range(args.warmup + args.steps + extra)]
     from thundersync_b200.ops import _ext
 
     for s in range(args.warmup):
@@ -400,6 +404,28 @@ def main() -> None:
                 fh.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=45,
                                                    max_name_column_width=100))
             prof.export_chrome_trace(args.profile_out + ".trace.json")
+    if args.cprofile_out:
+        import cProfile
+        import io
+        import pstats
+
+        torch.cuda.synchronize()
+        pr = cProfile.Profile()
+        t0 = time.perf_counter()
+        pr.enable()
+        run_step(trainer, works[-1], None)
+        pr.disable()
+        host_s = time.perf_counter() - t0
+        torch.cuda.synchronize()
+        total_s = time.perf_counter() - t0
+        if rank == 0:
+            buf = io.StringIO()
+            st = pstats.Stats(pr, stream=buf)
+            buf.write(f"host (profiled) {host_s:.3f} s, to device idle {total_s:.3f} s\n")
+            st.sort_stats("tottime").print_stats(60)
+            st.sort_stats("cumulative").print_stats(60)
+            with open(args.cprofile_out, "w") as fh:
+                fh.write(buf.getvalue())
     if hasattr(trainer, "shutdown"):
         trainer.shutdown()
     if world > 1:

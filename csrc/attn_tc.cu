@@ -979,7 +979,17 @@ std::vector<at::Tensor> tc_selftest(const at::Tensor& a, const at::Tensor& bk, c
   return {d1, d2};
 }
 
-std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale) {
+// out (optional): a contiguous bf16 tensor shaped like q that receives O (e.g. rows of a larger buffer).
+static at::Tensor out_or_new(const c10::optional<at::Tensor>& out, const at::Tensor& like, const char* what) {
+  if (!out) return at::empty_like(like);
+  TS_CHECK(out->is_contiguous() && out->sizes() == like.sizes() && out->scalar_type() == like.scalar_type() &&
+               out->device() == like.device(),
+           what, " must be a contiguous tensor shaped, typed and placed like its input");
+  return *out;
+}
+
+std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
+                                    const c10::optional<at::Tensor>& out) {
   check_cuda(q, "q");
   check_cuda(k, "k");
   check_cuda(v, "v");
@@ -988,7 +998,8 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
   const c10::cuda::CUDAGuard guard(q.device());
   const int T = q.size(0), Hq = q.size(1), D = q.size(2), S = k.size(0), Hkv = k.size(1);
   TS_CHECK(S >= T && Hq % Hkv == 0 && k.sizes() == v.sizes() && k.size(2) == D, "attention shapes");
-  auto o = at::empty_like(q);
+  TS_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), "attention inputs must be contiguous");
+  auto o = out_or_new(out, q, "attention out");
   auto lse = at::empty({Hq, T}, q.options().dtype(at::kFloat));
   if (T == 0) return {o, lse};
   CUtensorMap mq = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
@@ -1041,13 +1052,25 @@ template <int D, int MODE>
 void launch_dkdv(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
                  const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dk, at::Tensor& dv, int T, int S, int Hq,
                  int Hkv, double scale, int* err) {
-  // split the query heads of a KV head across CTAs while the grid is under one
-  // wave of SMs (the split costs an fp32 partial round trip and a sum kernel,
-  // which a grid of a wave or more does not win back)
+  // split the query heads of a KV head across CTAs when that fills the SMs'
+  // waves markedly better (the split costs an fp32 partial round trip and a
+  // sum kernel): e.g. 168 CTAs on 148 SMs run as two waves at 57% occupancy,
+  // 336 as three at 76%
   const int grp = Hq / Hkv;
-  const int want = sm_count(dk.get_device());
+  const int sms = sm_count(dk.get_device());
+  const int ctas = (int)(g.x * g.y);
+  auto util = [&](int n) {
+    const int c = ctas * n;
+    return (double)c / (double)(((c + sms - 1) / sms) * sms);
+  };
   int nsplit = 1;
-  while (nsplit * 2 <= grp && grp % (nsplit * 2) == 0 && (int)(g.x * g.y) * nsplit < want) nsplit *= 2;
+  double best = util(1);
+  for (int n = 2; n <= grp && grp % n == 0; n *= 2) {
+    if (util(n) > best * 1.15) {
+      best = util(n);
+      nsplit = n;
+    }
+  }
   g.z = nsplit;
   at::Tensor pk, pv;
   float* ppk = nullptr;
@@ -1082,8 +1105,11 @@ void launch_dq(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUten
 }
 }  // namespace
 
+// dq/dk/dv (optional): contiguous tensors shaped like q/k/v that receive the gradients.
 std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
-                                    const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale) {
+                                    const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale,
+                                    const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
+                                    const c10::optional<at::Tensor>& dv_out) {
   check_cuda(q, "q");
   check_cuda(k, "k");
   check_cuda(v, "v");
@@ -1093,9 +1119,11 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
   const c10::cuda::CUDAGuard guard(q.device());
   const int T = q.size(0), Hq = q.size(1), D = q.size(2), S = k.size(0), Hkv = k.size(1);
   TS_CHECK(S >= T && Hq % Hkv == 0 && (D == 64 || D == 128 || D == 256), "attention backward shapes");
-  auto dq = at::empty_like(q);
-  auto dk = at::empty_like(k);
-  auto dv = at::empty_like(v);
+  TS_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous() && dout.is_contiguous(),
+           "attention backward inputs must be contiguous");
+  auto dq = out_or_new(dq_out, q, "attention dq");
+  auto dk = out_or_new(dk_out, k, "attention dk");
+  auto dv = out_or_new(dv_out, v, "attention dv");
   if (T == 0) return {dq, dk.zero_(), dv.zero_()};
   auto delta = at::empty({Hq, T}, q.options().dtype(at::kFloat));
   const long long items = (long long)T * Hq;

@@ -4,12 +4,15 @@
 namespace ts {
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, bool unit);
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                     const at::Tensor& rstd, bool unit, const c10::optional<at::Tensor>& dres);
+                                     const at::Tensor& rstd, bool unit, const c10::optional<at::Tensor>& dres,
+                                     const c10::optional<at::Tensor>& dw_acc, double dw_scale);
 std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optional<at::Tensor>& qw,
                                          const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                          const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d, double eps,
                                          bool unit, const c10::optional<at::Tensor>& cos_tab,
-                                         const c10::optional<at::Tensor>& sin_tab);
+                                         const c10::optional<at::Tensor>& sin_tab,
+                                         const c10::optional<at::Tensor>& k_out,
+                                         const c10::optional<at::Tensor>& v_out);
 std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk,
                                                         const at::Tensor& dv, const at::Tensor& qkv,
                                                         const c10::optional<at::Tensor>& qw,
@@ -17,7 +20,9 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
                                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
                                                         int64_t d, double eps, bool unit,
                                                         const c10::optional<at::Tensor>& cos_tab,
-                                                        const c10::optional<at::Tensor>& sin_tab);
+                                                        const c10::optional<at::Tensor>& sin_tab,
+                                                        const c10::optional<at::Tensor>& dqw_acc,
+                                                        const c10::optional<at::Tensor>& dkw_acc, double dw_scale);
 at::Tensor swiglu_fwd(const at::Tensor& gu);
 at::Tensor swiglu_bwd(const at::Tensor& da, const at::Tensor& gu);
 void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const at::Tensor& dy, double scale);
@@ -48,10 +53,13 @@ void symm_adamw_gather(at::Tensor& master, at::Tensor& m, at::Tensor& v, const a
                        double eps, double wd, int64_t step, bool maximize, const at::Tensor& norm_slots,
                        double max_norm, at::Tensor& norm_out);
 std::vector<at::Tensor> tc_selftest(const at::Tensor& a, const at::Tensor& bk, const at::Tensor& bm);
-std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale);
+std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
+                                    const c10::optional<at::Tensor>& out);
 at::Tensor tc_status(const at::Tensor& like);
 std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
-                                    const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale);
+                                    const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale,
+                                    const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
+                                    const c10::optional<at::Tensor>& dv_out);
 void register_ipc(pybind11::module& m);
 void register_pinned(pybind11::module& m);
 void attn_trace_enable(bool on);
@@ -80,15 +88,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   ts::register_pinned(m);
   m.def("rms_norm_fwd", &ts::rms_norm_fwd);
   m.def("rms_norm_bwd", &ts::rms_norm_bwd, pybind11::arg("dy"), pybind11::arg("x"), pybind11::arg("w"),
-        pybind11::arg("rstd"), pybind11::arg("unit"), pybind11::arg("dres") = pybind11::none());
+        pybind11::arg("rstd"), pybind11::arg("unit"), pybind11::arg("dres") = pybind11::none(),
+        pybind11::arg("dw_acc") = pybind11::none(), pybind11::arg("dw_scale") = 1.0);
   m.def("qk_norm_rope_fwd", &ts::qk_norm_rope_fwd, pybind11::arg("qkv"), pybind11::arg("qw"), pybind11::arg("kw"),
         pybind11::arg("pos"), pybind11::arg("inv_freq"), pybind11::arg("hq"), pybind11::arg("hkv"), pybind11::arg("d"),
         pybind11::arg("eps"), pybind11::arg("unit"), pybind11::arg("cos_tab") = pybind11::none(),
-        pybind11::arg("sin_tab") = pybind11::none());
+        pybind11::arg("sin_tab") = pybind11::none(),
+        pybind11::arg("k_out") = pybind11::none(), pybind11::arg("v_out") = pybind11::none());
   m.def("qk_norm_rope_bwd", &ts::qk_norm_rope_bwd, pybind11::arg("dq"), pybind11::arg("dk"), pybind11::arg("dv"),
         pybind11::arg("qkv"), pybind11::arg("qw"), pybind11::arg("kw"), pybind11::arg("pos"), pybind11::arg("inv_freq"),
         pybind11::arg("hq"), pybind11::arg("hkv"), pybind11::arg("d"), pybind11::arg("eps"), pybind11::arg("unit"),
-        pybind11::arg("cos_tab") = pybind11::none(), pybind11::arg("sin_tab") = pybind11::none());
+        pybind11::arg("cos_tab") = pybind11::none(), pybind11::arg("sin_tab") = pybind11::none(),
+        pybind11::arg("dqw_acc") = pybind11::none(), pybind11::arg("dkw_acc") = pybind11::none(),
+        pybind11::arg("dw_scale") = 1.0);
   m.def("swiglu_fwd", &ts::swiglu_fwd);
   m.def("swiglu_bwd", &ts::swiglu_bwd);
   m.def("embedding_bwd_accumulate", &ts::embedding_bwd_accumulate);
@@ -105,9 +117,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_flat", &ts::adamw_flat);
   m.def("symm_barrier", &ts::symm_barrier);
   m.def("tc_selftest", &ts::tc_selftest);
-  m.def("attn_fwd_tc", &ts::attn_fwd_tc);
+  m.def("attn_fwd_tc", &ts::attn_fwd_tc, pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"),
+        pybind11::arg("scale"), pybind11::arg("out") = pybind11::none());
   m.def("tc_status", &ts::tc_status);
-  m.def("attn_bwd_tc", &ts::attn_bwd_tc);
+  m.def("attn_bwd_tc", &ts::attn_bwd_tc, pybind11::arg("dout"), pybind11::arg("q"), pybind11::arg("k"),
+        pybind11::arg("v"), pybind11::arg("o"), pybind11::arg("lse"), pybind11::arg("scale"),
+        pybind11::arg("dq") = pybind11::none(), pybind11::arg("dk") = pybind11::none(),
+        pybind11::arg("dv") = pybind11::none());
   m.def("symm_reduce", &ts::symm_reduce);
   m.def("symm_norm_put", &ts::symm_norm_put);
   m.def("symm_adamw_gather", &ts::symm_adamw_gather);

@@ -113,28 +113,29 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_dx_kernel(const T* __rest
 }
 
 // ----------------------------------------------------------------- RMSNorm bwd (dx + dw partials)
-// One pass over dy and x: each warp walks rows blockIdx.x*kWarps + warp,
-// + gridDim.x*kWarps, ...; it writes dx (+ dres, the residual branch's
-// gradient, added before the single rounding) and keeps the weight-gradient
-// column sums of its rows in registers. The block's warps are then added in
-// warp order in shared memory and the block writes one partial row; the
-// partial rows are summed in block order by sum_partials_kernel. The grid
-// size depends only on the row count and the SM count, so the sums are
-// reproducible run to run.
+// One pass over dy and x, one row per warp: the warp writes dx (+ dres, the
+// residual branch's gradient, added before the single rounding) and stores
+// its row's weight-gradient terms dy·x·rstd in its own shared-memory row;
+// after one barrier the block's threads add the kWarps rows in warp order and
+// the block writes one partial row, which sum_partials_kernel adds up in
+// block order. Shared and partial rows use the lane-major order
+// p = (v*E + e)*32 + lane for column (v*32 + lane)*E + e, so consecutive
+// lanes touch consecutive words. The grid size depends only on the row count,
+// so the sums are reproducible run to run. No per-lane accumulators stay live
+// across the row, which keeps the kernel near 100 registers (two or more
+// blocks per SM; an accumulating form at 163 registers ran one).
 template <typename T, int V>
 __global__ void __launch_bounds__(kWarps * 32) rms_bwd_fused_kernel(
     const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w, const float* __restrict__ rstd,
     const T* __restrict__ dres, T* __restrict__ dx, float* __restrict__ partial, int rows, int H, float woff) {
-  extern __shared__ float red[];
+  extern __shared__ float red[];  // [kWarps][P]
   constexpr int E = Vec<T>::N;
+  constexpr int P = V * 32 * E;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  float acc[V][E];
-#pragma unroll
-  for (int v = 0; v < V; ++v)
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[v][e] = 0.f;
-  for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
+  const int row = blockIdx.x * kWarps + warp;
+  float* mine = red + warp * P;
+  if (row < rows) {
     const float r = rstd[row];
     const T* xr = x + (size_t)row * H;
     const T* dyr = dy + (size_t)row * H;
@@ -152,8 +153,11 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_fused_kernel(
           const float n = to_f(xb[v].e[e]) * r;
           const float d = to_f(db[v].e[e]);
           dot += d * (to_f(wv.e[e]) + woff) * n;
-          acc[v][e] += d * n;
+          mine[(v * E + e) * 32 + lane] = d * n;
         }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) mine[(v * E + e) * 32 + lane] = 0.f;
       }
     }
     dot = warp_sum(dot) / (float)H;
@@ -178,21 +182,16 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_fused_kernel(
         store_vec(dxr + c, o);
       }
     }
+  } else {
+    for (int q = lane; q < P; q += 32) mine[q] = 0.f;
   }
-  for (int k = 0; k < kWarps; ++k) {
-    if (warp == k) {
+  __syncthreads();
+  for (int q = threadIdx.x; q < P; q += blockDim.x) {
+    float acc = 0.f;
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        const int c = (v * 32 + lane) * E;
-        if (c < H) {
-#pragma unroll
-          for (int e = 0; e < E; ++e) red[c + e] = k == 0 ? acc[v][e] : red[c + e] + acc[v][e];
-        }
-      }
-    }
-    __syncthreads();
+    for (int k = 0; k < kWarps; ++k) acc += red[k * P + q];
+    partial[(size_t)blockIdx.x * P + q] = acc;
   }
-  for (int c = threadIdx.x; c < H; c += blockDim.x) partial[(size_t)blockIdx.x * H + c] = red[c];
 }
 
 // ----------------------------------------------------------------- column partial sums
@@ -236,20 +235,28 @@ __global__ void __launch_bounds__(256) rms_dw_partial_kernel(const T* __restrict
 // out[c] = sum_k partial[k, c]: block (32 x 8) covers 32 columns; warp row y
 // sums chunks y, y+8, ... and the 8 row sums are added in y order, so the
 // result is the same every run.
+// lane_e > 0: partial rows are in the lane-major order of rms_bwd_fused_kernel (row length H, an index
+// p there is column ((p / 32) / lane_e * 32 + p % 32) * lane_e + (p / 32) % lane_e; out has `cols` entries).
 __global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restrict__ partial, float* __restrict__ out,
-                                                           int chunks, int H) {
+                                                           int chunks, int H, float scale = 1.f, int accumulate = 0,
+                                                           int lane_e = 0, int cols = 0) {
   __shared__ float red[8][33];
-  const int c = blockIdx.x * 32 + threadIdx.x;
+  const int p = blockIdx.x * 32 + threadIdx.x;
+  int c = p;
+  if (lane_e > 0) {
+    const int ve = p >> 5;
+    c = ((ve / lane_e) * 32 + (p & 31)) * lane_e + ve % lane_e;
+  }
   float s = 0.f;
-  if (c < H)
-    for (int k = threadIdx.y; k < chunks; k += 8) s += partial[(size_t)k * H + c];
+  if (p < H)
+    for (int k = threadIdx.y; k < chunks; k += 8) s += partial[(size_t)k * H + p];
   red[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
-  if (threadIdx.y == 0 && c < H) {
+  if (threadIdx.y == 0 && p < H && (lane_e == 0 || c < cols)) {
     float t = 0.f;
 #pragma unroll
     for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
-    out[c] = t;
+    out[c] = accumulate ? out[c] + scale * t : t;  // accumulate: into a gradient sink, scaled
   }
 }
 
@@ -308,30 +315,45 @@ void rms_fwd_dispatch(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, a
 
 template <typename T, int V>
 at::Tensor launch_rms_bwd_fused(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                const at::Tensor& rstd, const T* dres, at::Tensor& dx, float woff) {
+                                const at::Tensor& rstd, const T* dres, at::Tensor& dx, float woff,
+                                const c10::optional<at::Tensor>& dw_acc, float dw_scale) {
   const int rows = x.size(0), H = x.size(1);
-  const int grid = std::max(1, std::min((rows + kWarps - 1) / kWarps, sm_count(x.get_device())));
-  auto partial = at::empty({grid, H}, x.options().dtype(at::kFloat));
-  auto dw = at::empty({H}, x.options().dtype(at::kFloat));
-  rms_bwd_fused_kernel<T, V><<<grid, kWarps * 32, H * sizeof(float), stream()>>>(
+  // one row per warp: enough warps in flight to cover memory latency (a grid capped at one block per SM,
+  // with each warp walking many rows, ran twice as long)
+  const int grid = std::max(1, (rows + kWarps - 1) / kWarps);
+  constexpr int E = Vec<T>::N;
+  constexpr int P = V * 32 * E;  // lane-major partial row length
+  auto partial = at::empty({grid, P}, x.options().dtype(at::kFloat));
+  auto dw = dw_acc ? *dw_acc : at::empty({H}, x.options().dtype(at::kFloat));
+  const int smem = kWarps * P * (int)sizeof(float);
+  static bool configured[16] = {false};
+  bool& done = configured[x.get_device() & 15];
+  if (!done) {
+    TS_CUDA_CHECK(cudaFuncSetAttribute(rms_bwd_fused_kernel<T, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    TS_CUDA_CHECK(cudaFuncSetAttribute(rms_bwd_fused_kernel<T, V>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       100));
+    done = true;
+  }
+  rms_bwd_fused_kernel<T, V><<<grid, kWarps * 32, smem, stream()>>>(
       (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)w.data_ptr(), rstd.data_ptr<float>(), dres,
       (T*)dx.data_ptr(), partial.data_ptr<float>(), rows, H, woff);
-  sum_partials_kernel<<<(H + 31) / 32, dim3(32, 8), 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
-                                                                     grid, H);
+  sum_partials_kernel<<<(P + 31) / 32, dim3(32, 8), 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
+                                                                     grid, P, dw_scale, dw_acc ? 1 : 0, E, H);
   return dw;
 }
 
 // dx (+ dres) and dw in two launches for rows up to 8 vectors per lane; empty tensor otherwise.
 template <typename T>
 at::Tensor rms_bwd_fused_dispatch(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                  const at::Tensor& rstd, const T* dres, at::Tensor& dx, float woff) {
+                                  const at::Tensor& rstd, const T* dres, at::Tensor& dx, float woff,
+                                  const c10::optional<at::Tensor>& acc, float sc) {
   constexpr int E = Vec<T>::N;
   const int H = x.size(1);
   const int nv = (H + 32 * E - 1) / (32 * E);
-  if (nv <= 1) return launch_rms_bwd_fused<T, 1>(dy, x, w, rstd, dres, dx, woff);
-  if (nv <= 2) return launch_rms_bwd_fused<T, 2>(dy, x, w, rstd, dres, dx, woff);
-  if (nv <= 4) return launch_rms_bwd_fused<T, 4>(dy, x, w, rstd, dres, dx, woff);
-  if (nv <= 8) return launch_rms_bwd_fused<T, 8>(dy, x, w, rstd, dres, dx, woff);
+  if (nv <= 1) return launch_rms_bwd_fused<T, 1>(dy, x, w, rstd, dres, dx, woff, acc, sc);
+  if (nv <= 2) return launch_rms_bwd_fused<T, 2>(dy, x, w, rstd, dres, dx, woff, acc, sc);
+  if (nv <= 4) return launch_rms_bwd_fused<T, 4>(dy, x, w, rstd, dres, dx, woff, acc, sc);
+  if (nv <= 8) return launch_rms_bwd_fused<T, 8>(dy, x, w, rstd, dres, dx, woff, acc, sc);
   return at::Tensor();
 }
 
@@ -430,7 +452,8 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
     const T* __restrict__ qw, const T* __restrict__ kw, const int64_t* __restrict__ pos,
     const float* __restrict__ inv_freq, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab,
     int tab_len, T* __restrict__ dqkv, float* __restrict__ dqw_part,
-    float* __restrict__ dkw_part, int tokens, int hq, int hkv, float eps, int items_per_block, int unit, int rot_lanes) {
+    float* __restrict__ dkw_part, int tokens, int hq, int hkv, float eps, int items_per_block, int unit, int rot_lanes,
+    int part_stride) {
   constexpr int EPL = D / 32;
   __shared__ float red_q[kWarps][D];
   __shared__ float red_k[kWarps][D];
@@ -523,8 +546,8 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
       sq += red_q[w][c];
       sk += red_k[w][c];
     }
-    dqw_part[(size_t)blockIdx.x * D + c] = sq;
-    dkw_part[(size_t)blockIdx.x * D + c] = sk;
+    dqw_part[(size_t)blockIdx.x * part_stride + c] = sq;
+    dkw_part[(size_t)blockIdx.x * part_stride + c] = sk;
   }
 }
 
@@ -622,8 +645,10 @@ std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, d
 }
 
 // dres (optional): gradient of a residual branch added to dx before its rounding.
+// dw_acc (optional, fp32 [H]): the weight gradient is added into it (times dw_scale) and returned.
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
-                                     const at::Tensor& rstd, bool unit, const c10::optional<at::Tensor>& dres) {
+                                     const at::Tensor& rstd, bool unit, const c10::optional<at::Tensor>& dres,
+                                     const c10::optional<at::Tensor>& dw_acc, double dw_scale) {
   check_cuda(dy, "dy");
   check_cuda(x, "x");
   const c10::cuda::CUDAGuard guard(x.device());
@@ -634,25 +659,32 @@ std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, 
     TS_CHECK(dres->is_contiguous() && dres->sizes() == x.sizes() && dres->scalar_type() == x.scalar_type(),
              "rms_norm_bwd: dres must be a contiguous tensor shaped and typed like x");
   }
-  if (x.size(0) == 0) return {dx, at::zeros({H}, x.options().dtype(at::kFloat))};
+  if (dw_acc) {
+    TS_CHECK(dw_acc->scalar_type() == at::kFloat && dw_acc->is_contiguous() && dw_acc->numel() == H,
+             "rms_norm_bwd: dw_acc must be a contiguous fp32 tensor of the row width");
+  }
+  const float sc = (float)dw_scale;
+  if (x.size(0) == 0) return {dx, dw_acc ? *dw_acc : at::zeros({H}, x.options().dtype(at::kFloat))};
   if (x.scalar_type() == at::kBFloat16) {
     TS_CHECK(H % 8 == 0, "row width must be a multiple of 8");
     using T = __nv_bfloat16;
     dw = rms_bwd_fused_dispatch<T>(dy, x, w, rstd, dres ? (const T*)dres->data_ptr() : nullptr, dx,
-                                   unit ? 1.f : 0.f);
+                                   unit ? 1.f : 0.f, dw_acc, sc);
     if (!dw.defined()) {
       rms_dx_dispatch<T>(dy, x, w, rstd, dx, unit ? 1.f : 0.f);
       dw = column_weight_grad<T>(dy, x, rstd);
       if (dres) dx.add_(*dres);
+      if (dw_acc) dw = dw_acc->add_(dw, sc);
     }
   } else if (x.scalar_type() == at::kFloat) {
     TS_CHECK(H % 4 == 0, "row width must be a multiple of 4");
     dw = rms_bwd_fused_dispatch<float>(dy, x, w, rstd, dres ? dres->data_ptr<float>() : nullptr, dx,
-                                       unit ? 1.f : 0.f);
+                                       unit ? 1.f : 0.f, dw_acc, sc);
     if (!dw.defined()) {
       rms_dx_dispatch<float>(dy, x, w, rstd, dx, unit ? 1.f : 0.f);
       dw = column_weight_grad<float>(dy, x, rstd);
       if (dres) dx.add_(*dres);
+      if (dw_acc) dw = dw_acc->add_(dw, sc);
     }
   } else {
     TS_CHECK(false, "rms_norm_bwd: unsupported dtype");
@@ -687,7 +719,9 @@ std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optio
                                          const c10::optional<at::Tensor>& kw, const at::Tensor& pos,
                                          const at::Tensor& inv_freq, int64_t hq, int64_t hkv, int64_t d,
                                          double eps, bool unit, const c10::optional<at::Tensor>& cos_tab,
-                                         const c10::optional<at::Tensor>& sin_tab) {
+                                         const c10::optional<at::Tensor>& sin_tab,
+                                         const c10::optional<at::Tensor>& k_out,
+                                         const c10::optional<at::Tensor>& v_out) {
   const float* ct = cos_tab ? cos_tab->data_ptr<float>() : nullptr;
   const float* st = sin_tab ? sin_tab->data_ptr<float>() : nullptr;
   const int tl = cos_tab ? (int)cos_tab->size(0) : 0;
@@ -706,8 +740,16 @@ std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optio
   const c10::cuda::CUDAGuard guard(qkv.device());
   const int64_t t = qkv.size(0);
   auto q = at::empty({t, hq, d}, qkv.options());
-  auto k = at::empty({t, hkv, d}, qkv.options());
-  auto v = at::empty({t, hkv, d}, qkv.options());
+  // k_out / v_out: contiguous [t, hkv, d] destinations (rows of a key/value buffer that also holds ancestors)
+  for (const auto* o : {&k_out, &v_out}) {
+    if (*o) {
+      TS_CHECK((*o)->is_contiguous() && (*o)->dim() == 3 && (*o)->size(0) == t && (*o)->size(1) == hkv &&
+                   (*o)->size(2) == d && (*o)->scalar_type() == qkv.scalar_type() && (*o)->device() == qkv.device(),
+               "qk_norm_rope_fwd: k_out / v_out must be contiguous [t, hkv, d] tensors like qkv");
+    }
+  }
+  auto k = k_out ? *k_out : at::empty({t, hkv, d}, qkv.options());
+  auto v = v_out ? *v_out : at::empty({t, hkv, d}, qkv.options());
   if (t == 0) return {q, k, v};
   if (qkv.scalar_type() == at::kBFloat16) {
     TS_DISPATCH_HEAD(d, qk_fwd_launch, __nv_bfloat16, qkv, qw, kw, pos, inv_freq, q, k, v, hq, hkv, (float)eps,
@@ -725,14 +767,14 @@ std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const c10::optio
 template <typename T, int D>
 static void qk_bwd_launch(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv, const at::Tensor& qkv,
                           const c10::optional<at::Tensor>& qw, const c10::optional<at::Tensor>& kw,
-                          const at::Tensor& pos, const at::Tensor& inv_freq, at::Tensor& dqkv, at::Tensor& pq,
-                          at::Tensor& pk, int hq, int hkv, float eps, int blocks, int per_block, int unit,
+                          const at::Tensor& pos, const at::Tensor& inv_freq, at::Tensor& dqkv, at::Tensor& pqk,
+                          int hq, int hkv, float eps, int blocks, int per_block, int unit,
                           int rot_lanes, const float* ct, const float* st, int tl) {
   qk_norm_rope_bwd_kernel<T, D><<<blocks, kWarps * 32, 0, stream()>>>(
       (const T*)dq.data_ptr(), (const T*)dk.data_ptr(), (const T*)dv.data_ptr(), (const T*)qkv.data_ptr(),
       qw ? (const T*)qw->data_ptr() : nullptr, kw ? (const T*)kw->data_ptr() : nullptr, pos.data_ptr<int64_t>(),
-      inv_freq.data_ptr<float>(), ct, st, tl, (T*)dqkv.data_ptr(), pq.data_ptr<float>(), pk.data_ptr<float>(), qkv.size(0), hq,
-      hkv, eps, per_block, unit, rot_lanes);
+      inv_freq.data_ptr<float>(), ct, st, tl, (T*)dqkv.data_ptr(), pqk.data_ptr<float>(), pqk.data_ptr<float>() + D,
+      qkv.size(0), hq, hkv, eps, per_block, unit, rot_lanes, 2 * D);
 }
 
 std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk,
@@ -742,7 +784,9 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
                                                         const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
                                                         int64_t d, double eps, bool unit,
                                                         const c10::optional<at::Tensor>& cos_tab,
-                                                        const c10::optional<at::Tensor>& sin_tab) {
+                                                        const c10::optional<at::Tensor>& sin_tab,
+                                                        const c10::optional<at::Tensor>& dqw_acc,
+                                                        const c10::optional<at::Tensor>& dkw_acc, double dw_scale) {
   check_cuda(qkv, "qkv");
   const float* ct = cos_tab ? cos_tab->data_ptr<float>() : nullptr;
   const float* st = sin_tab ? sin_tab->data_ptr<float>() : nullptr;
@@ -758,14 +802,14 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
   const int target = 4 * sm_count(qkv.get_device());
   int per_block = (int)std::max<long long>(kWarps, (items + target - 1) / target);
   int blocks = (int)std::max<long long>(1, (items + per_block - 1) / per_block);
-  auto pq = at::zeros({blocks, d}, qkv.options().dtype(at::kFloat));
-  auto pk = at::zeros({blocks, d}, qkv.options().dtype(at::kFloat));
+  // every block writes its whole partial row: [q-norm weight | k-norm weight] partials side by side
+  auto pqk = at::empty({blocks, 2 * d}, qkv.options().dtype(at::kFloat));
   if (t > 0) {
     if (qkv.scalar_type() == at::kBFloat16) {
-      TS_DISPATCH_HEAD(d, qk_bwd_launch, __nv_bfloat16, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pq, pk, hq, hkv,
+      TS_DISPATCH_HEAD(d, qk_bwd_launch, __nv_bfloat16, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pqk, hq, hkv,
                        (float)eps, blocks, per_block, unit ? 1 : 0, rot_lanes, ct, st, tl);
     } else if (qkv.scalar_type() == at::kFloat) {
-      TS_DISPATCH_HEAD(d, qk_bwd_launch, float, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pq, pk, hq, hkv,
+      TS_DISPATCH_HEAD(d, qk_bwd_launch, float, dq, dk, dv, qkv, qw, kw, pos, inv_freq, dqkv, pqk, hq, hkv,
                        (float)eps, blocks, per_block, unit ? 1 : 0, rot_lanes, ct, st, tl);
     } else {
       TS_CHECK(false, "qk_norm_rope_bwd: unsupported dtype");
@@ -774,12 +818,33 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
   }
   c10::optional<at::Tensor> dqw, dkw;
   if (qw) {
-    auto oq = at::empty({d}, qkv.options().dtype(at::kFloat));
-    auto ok = at::empty({d}, qkv.options().dtype(at::kFloat));
-    sum_partials_kernel<<<(d + 31) / 32, dim3(32, 8), 0, stream()>>>(pq.data_ptr<float>(), oq.data_ptr<float>(), blocks,
-                                                                    d);
-    sum_partials_kernel<<<(d + 31) / 32, dim3(32, 8), 0, stream()>>>(pk.data_ptr<float>(), ok.data_ptr<float>(), blocks,
-                                                                    d);
+    if (t == 0) pqk.zero_();
+    for (const auto* acc : {&dqw_acc, &dkw_acc}) {
+      if (*acc) {
+        TS_CHECK((*acc)->scalar_type() == at::kFloat && (*acc)->is_contiguous() && (*acc)->numel() == d,
+                 "qk_norm_rope_bwd: weight-gradient targets must be contiguous fp32 tensors of the head size");
+      }
+    }
+    at::Tensor oq, ok;
+    const bool adjacent = dqw_acc && dkw_acc && dkw_acc->data_ptr<float>() == dqw_acc->data_ptr<float>() + d;
+    if (adjacent || (!dqw_acc && !dkw_acc)) {
+      // one reduction over both weights (sink targets that sit back to back, or fresh outputs)
+      at::Tensor both = adjacent ? at::from_blob(dqw_acc->data_ptr<float>(), {2 * d}, dqw_acc->options())
+                                 : at::empty({2 * d}, qkv.options().dtype(at::kFloat));
+      sum_partials_kernel<<<(2 * d + 31) / 32, dim3(32, 8), 0, stream()>>>(
+          pqk.data_ptr<float>(), both.data_ptr<float>(), blocks, 2 * d, (float)dw_scale, adjacent ? 1 : 0);
+      oq = adjacent ? *dqw_acc : both.narrow(0, 0, d);
+      ok = adjacent ? *dkw_acc : both.narrow(0, d, d);
+    } else {
+      auto pq = pqk.narrow(1, 0, d).contiguous();
+      auto pk = pqk.narrow(1, d, d).contiguous();
+      oq = dqw_acc ? *dqw_acc : at::empty({d}, qkv.options().dtype(at::kFloat));
+      ok = dkw_acc ? *dkw_acc : at::empty({d}, qkv.options().dtype(at::kFloat));
+      sum_partials_kernel<<<(d + 31) / 32, dim3(32, 8), 0, stream()>>>(pq.data_ptr<float>(), oq.data_ptr<float>(),
+                                                                      blocks, d, (float)dw_scale, dqw_acc ? 1 : 0);
+      sum_partials_kernel<<<(d + 31) / 32, dim3(32, 8), 0, stream()>>>(pk.data_ptr<float>(), ok.data_ptr<float>(),
+                                                                      blocks, d, (float)dw_scale, dkw_acc ? 1 : 0);
+    }
     TS_LAUNCH_CHECK();
     dqw = oq;
     dkw = ok;

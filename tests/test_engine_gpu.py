@@ -58,3 +58,38 @@ def test_gpu_streamed_grpo_matches_fp32_oracle(binary, stream_turns):
         cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)
         assert cos > 0.98, (n, float(cos))
     assert (num / den) ** 0.5 < 0.06
+
+
+@pytest.mark.parametrize("prompt_len,cont_len", [(128, 200), (96, 75)])
+def test_gpu_single_node_layer_matches_op_by_op(prompt_len, cont_len):
+    """On CUDA the one-node dense layer (ancestor and own keys in one buffer, outputs written in place,
+    padded pack rows) agrees with the op-by-op path, including gradients that reach the prompt's K/V."""
+    from thundersync_b200.engine.layers import Executor, Segment
+
+    cfg = PRESETS["qwen3-1.7b"].with_(num_hidden_layers=2, hidden_size=512, intermediate_size=1024,
+                                      num_attention_heads=4, num_key_value_heads=2, head_dim=128, vocab_size=1024)
+    torch.manual_seed(3)
+    model = Qwen3ForCausalLM(cfg).to("cuda", torch.bfloat16)
+    ids = torch.randint(0, cfg.vocab_size, (prompt_len + cont_len,), device="cuda")
+    pos = torch.arange(prompt_len + cont_len, device="cuda")
+    res = []
+    for fused in (True, False):
+        model.zero_grad(set_to_none=True)
+        ex = Executor(model)
+        ex.fused_layers = fused
+        def padded(x):  # pack rows padded to a multiple of 128 as the streaming engine pads them
+            return torch.cat((x, x.new_zeros((-x.shape[0]) % 128)))
+
+        h0, st0 = ex.run(padded(ids[:prompt_len]), padded(pos[:prompt_len]), [Segment(0, prompt_len, [])])
+        past = st0[0]
+        h1, _ = ex.run(padded(ids[prompt_len:]), padded(pos[prompt_len:]),
+                       [Segment(0, cont_len, [([k], [v]) for (k, v) in past])])
+        h0, h1 = h0[:prompt_len], h1[:cont_len]
+        (h0.float().square().mean() + h1.float().pow(3).mean()).backward()
+        res.append((h1.detach().float(), {n: p.grad.float().clone() for n, p in model.named_parameters()
+                                          if p.grad is not None}))
+    assert float((res[0][0] - res[1][0]).norm() / res[1][0].norm()) < 2e-2
+    assert res[0][1].keys() == res[1][1].keys()
+    for n in res[0][1]:
+        a, b = res[0][1][n], res[1][1][n]
+        assert float((a - b).norm() / b.norm().clamp_min(1e-12)) < 3e-2, n

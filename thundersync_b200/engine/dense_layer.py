@@ -25,6 +25,7 @@ from typing import Any
 
 import torch
 
+from thundersync_b200.ops._ext import native
 from thundersync_b200.ops.attention import _ChunkedAttention
 from thundersync_b200.ops.linear import _Linear
 from thundersync_b200.ops.norm import _RMSNorm
@@ -68,7 +69,34 @@ class DenseLayer(torch.autograd.Function):
         x1 = _RMSNorm.forward(c_n1, h, ln1, eps, False)
         c_qkv = _Ctx((True, False, need_w, need_w, need_w))
         qkv = _Linear.forward(c_qkv, x1, qkv_fused, wq, wk, wv)
-        c_rope = _Ctx((True, need_w, need_w) + (False,) * 7)
+        c_rope = _Ctx((True, need_w, need_w) + (False,) * 9)
+        # one segment from row 0 with no own-pack key ranges (a trajectory or prompt pack): on CUDA the
+        # ancestors' keys/values and this pack's are laid out in one buffer, the rope kernel writes the
+        # pack's rows in place and attention reads / writes every operand where it lives (no concatenation,
+        # no zero-filled gradient buffers beyond the padding rows)
+        fast = (h.is_cuda and len(segs) == 1 and segs[0][0] == 0 and not segs[0][3]
+                and segs[0][2] == n_past // 2)
+        ctx.fast = fast
+        if fast:
+            npast = segs[0][2]
+            pk, pv = past[:npast], past[npast:]
+            sp = sum(x.shape[0] for x in pk)
+            kbuf = h.new_empty(sp + t, hkv, d)
+            vbuf = h.new_empty(sp + t, hkv, d)
+            if npast:
+                torch.cat(pk, 0, out=kbuf[:sp])
+                torch.cat(pv, 0, out=vbuf[:sp])
+            q, k, v = _QKNormRope.forward(c_rope, qkv, qn, kn, pos, inv_freq, hq, hkv, d, eps, False,
+                                          kbuf[sp:], vbuf[sp:])
+            cov = segs[0][1]
+            o = q.new_empty(t, hq, d)
+            _, lse = native().attn_fwd_tc(q[:cov], kbuf[:sp + cov], vbuf[:sp + cov], scale, o[:cov])
+            if cov < t:  # pack padding rows: no attention output
+                o[cov:].zero_()
+            ctx.att = (q, kbuf, vbuf, o, lse, sp, cov, [x.shape[0] for x in pk])
+            c_att = None
+            return DenseLayer._forward_tail(ctx, h, o, t, hq, d, eps, need_w, c_n1, c_qkv, c_rope, c_att,
+                                            wo, ln2, wg, wu, wd, gu_fused, meta, k, v)
         q, k, v = _QKNormRope.forward(c_rope, qkv, qn, kn, pos, inv_freq, hq, hkv, d, eps, False)
         # attention per segment: [ancestor chunks..., own-pack key ranges..., own slice]
         c_att = []
@@ -88,6 +116,12 @@ class DenseLayer(torch.autograd.Function):
         if covered < t:  # pack padding rows: no attention output
             outs.append(q.new_zeros(t - covered, hq, d))
         o = outs[0] if len(outs) == 1 else torch.cat(outs, 0)
+        return DenseLayer._forward_tail(ctx, h, o, t, hq, d, eps, need_w, c_n1, c_qkv, c_rope, c_att,
+                                        wo, ln2, wg, wu, wd, gu_fused, meta, k, v)
+
+    @staticmethod
+    def _forward_tail(ctx, h, o, t, hq, d, eps, need_w, c_n1, c_qkv, c_rope, c_att, wo, ln2, wg, wu, wd, gu_fused,
+                      meta, k, v):
         o = o.reshape(t, hq * d)
         c_o = _Ctx((True, False, need_w))
         h1 = _Linear.forward_residual(c_o, o, None, h, wo)
@@ -122,6 +156,26 @@ class DenseLayer(torch.autograd.Function):
         # h1 = h + o_proj(o)
         do_, _, gwo = _Linear.backward(c_o, dh1)
         do_ = do_.reshape(t, hq, d)
+        if ctx.fast:
+            q, kbuf, vbuf, o, lse, sp, cov, lens = ctx.att
+            ctx.att = None
+            dq = torch.empty_like(q)
+            dkbuf = torch.empty_like(kbuf)
+            dvbuf = torch.empty_like(vbuf)
+            if cov < t:
+                dq[cov:].zero_()
+                dkbuf[sp + cov:].zero_()
+                dvbuf[sp + cov:].zero_()
+            native().attn_bwd_tc(do_[:cov].contiguous(), q[:cov], kbuf[:sp + cov], vbuf[:sp + cov], o[:cov], lse,
+                                 scale, dq[:cov], dkbuf[:sp + cov], dvbuf[:sp + cov])
+            dk, dv = dkbuf[sp:], dvbuf[sp:]
+            if dk_out is not None:
+                dk.add_(dk_out)
+            if dv_out is not None:
+                dv.add_(dv_out)
+            dpast_k = list(torch.split(dkbuf[:sp], lens, 0)) if lens else []
+            dpast_v = list(torch.split(dvbuf[:sp], lens, 0)) if lens else []
+            return DenseLayer._finish(ctx, dq, dk, dv, dpast_k, dpast_v, dh1, gln2, gwo, gwg, gwu, gwd)
         covered = sum(s1 - s0 for _, s0, s1, _, _ in c_att)
         single = len(c_att) == 1 and covered == t
         if single and not c_att[0][4]:

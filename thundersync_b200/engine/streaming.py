@@ -337,9 +337,12 @@ class StreamingRun:
         if not idx:
             return hs.new_zeros(0, dtype=torch.float32)
         rows = torch.cat((last[None], hs[:-1]), 0) if hs.shape[0] > 0 else last[None]
-        sel = torch.tensor(idx, dtype=torch.long, device=self.device)
         tgt = self._ids([tokens[j] for j in idx])
-        return lm_head_logprob(rows.index_select(0, sel), self.weight, tgt)
+        if idx[-1] - idx[0] + 1 == len(idx):  # one contiguous run (every completion token scored): a view
+            picked = rows[idx[0]:idx[-1] + 1]
+        else:  # index copied from page-locked memory: no host wait on the device queue
+            picked = rows.index_select(0, self._ids(idx))
+        return lm_head_logprob(picked, self.weight, tgt)
 
     # ------------------------------------------------------------ groups
     def open_group(self, group_id: int, prompt_tokens: list[int]) -> None:

@@ -16,7 +16,7 @@ _LOAD_ERROR: BaseException | None = None
 
 # kernels launched per call of each native entry point
 KERNELS_PER_CALL = {
-    "rms_norm_fwd": 1, "rms_norm_bwd": 3, "qk_norm_rope_fwd": 1, "qk_norm_rope_bwd": 3,
+    "rms_norm_fwd": 1, "rms_norm_bwd": 2, "qk_norm_rope_fwd": 1, "qk_norm_rope_bwd": 2,
     "swiglu_fwd": 1, "swiglu_bwd": 1, "embedding_bwd_accumulate": 1, "fold_stats": 1, "axpby": 1,
     "scale": 1, "reduce_into": 1, "lse_gather": 1, "logprob_dlogits": 1, "attn_fwd": 1, "attn_bwd": 3,
     "sq_norm": 2, "clip_coef": 1, "adamw_flat": 1,

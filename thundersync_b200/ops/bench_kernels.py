@@ -94,7 +94,25 @@ def bench_rms(args) -> None:
     print(f"rms fwd {args.rows}x{args.cols}: {ms:.3f} ms  {gb / ms * 1e3:.0f} GB/s")
     dy = torch.randn_like(x)
     ms = _time(lambda: ext.rms_norm_bwd(dy, x, w, r, False), args.iters)
-    print(f"rms bwd: {ms:.3f} ms  {1.5 * gb / ms * 1e3:.0f} GB/s")
+    print(f"rms bwd (one pass, dx + weight partials): {ms:.3f} ms  {1.5 * gb / ms * 1e3:.0f} GB/s")
+    res = torch.randn_like(x)
+    ms = _time(lambda: ext.rms_norm_bwd(dy, x, w, r, False, res), args.iters)
+    print(f"rms bwd + residual gradient: {ms:.3f} ms  {2 * gb / ms * 1e3:.0f} GB/s")
+    # the allocation-free entry point runs the three-kernel form (dx; column partials; ordered sum)
+    import ctypes
+
+    from thundersync_b200.ops._ext import so_path
+
+    fn = ctypes.CDLL(so_path()).ts_rms_norm_bwd_noalloc
+    fn.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    dx = torch.empty_like(x)
+    dw = torch.empty(args.cols, device="cuda", dtype=torch.float32)
+    st = torch.cuda.current_stream().cuda_stream
+    if args.cols <= 4096 and args.rows <= 128 * 1024:
+        ms = _time(lambda: fn(dy.data_ptr(), x.data_ptr(), w.data_ptr(), r.data_ptr(), dx.data_ptr(),
+                              dw.data_ptr(), args.rows, args.cols, 0, st), args.iters)
+        print(f"rms bwd (three kernels): {ms:.3f} ms  {1.5 * gb / ms * 1e3:.0f} GB/s")
 
 
 def bench_lse(args) -> None:

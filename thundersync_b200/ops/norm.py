@@ -62,20 +62,27 @@ class _RMSNorm(torch.autograd.Function):
         dy2 = dy.reshape(x2.shape)
         if not dy2.is_contiguous():
             dy2 = dy2.contiguous()
+        s = _sink.active() if ctx.needs_input_grad[1] else None
+        into_sink = s is not None and s.owns(w)
         if dy2.is_cuda:
             r2 = None if dres is None else dres.reshape(x2.shape).contiguous()
-            dx, dw = native().rms_norm_bwd(dy2, x2, w.contiguous(), rstd, bool(ctx.unit), r2)
+            # a sink-owned weight's gradient is summed straight into the sink by the kernel's final reduction
+            acc = s.view(w) if into_sink and s.view(w).dtype == torch.float32 else None
+            dx, dw = native().rms_norm_bwd(dy2, x2, w.contiguous(), rstd, bool(ctx.unit), r2, acc,
+                                           float(s.scale) if acc is not None else 1.0)
+            if acc is not None:
+                s.deposits += 1
+                into_sink = False
+                dw = None
         else:
             dx, dw = _ref_backward(dy2, x2, w, rstd, ctx.unit)
             if dres is not None:
                 dx = dres.reshape(dx.shape) + dx
         dw_out = None
-        if ctx.needs_input_grad[1]:
-            s = _sink.active()
-            if s is not None and s.owns(w):
-                s.add_(w, dw)
-            else:
-                dw_out = dw.to(w.dtype)
+        if into_sink:
+            s.add_(w, dw)
+        elif ctx.needs_input_grad[1] and dw is not None and not (s is not None and s.owns(w)):
+            dw_out = dw.to(w.dtype)
         return dx.view(ctx.shape), dw_out, None, None
 
 

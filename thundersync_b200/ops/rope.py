@@ -75,14 +75,16 @@ def rope_tables(inv_freq: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 class _QKNormRope(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit):
+    def forward(ctx, qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit, k_out=None, v_out=None):
+        # k_out / v_out (CUDA): [t, hkv, d] destinations for k and v, e.g. the tail rows of a buffer whose
+        # head rows hold the ancestors' keys, so attention reads one contiguous key range without a copy
         ctx.meta = (hq, hkv, d, eps, unit)
         ctx.has_norm = q_w is not None
         if qkv.is_cuda:
             ct, st = rope_tables(inv_freq)
             q, k, v = native().qk_norm_rope_fwd(
                 qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(), hq, hkv, d, float(eps), bool(unit),
-                ct, st,
+                ct, st, k_out, v_out,
             )
         else:
             with torch.no_grad():
@@ -98,11 +100,20 @@ class _QKNormRope(torch.autograd.Function):
         dq = torch.zeros(t, hq, d, dtype=qkv.dtype, device=qkv.device) if dq is None else dq.contiguous()
         dk = torch.zeros(t, hkv, d, dtype=qkv.dtype, device=qkv.device) if dk is None else dk.contiguous()
         dv = torch.zeros(t, hkv, d, dtype=qkv.dtype, device=qkv.device) if dv is None else dv.contiguous()
+        s = _sink.active() if ctx.has_norm else None
+        acc_q = acc_k = None
         if qkv.is_cuda:
             ct, st = rope_tables(inv_freq)
+            # sink-owned norm weights: the kernel's final reduction adds the gradient straight into the sink
+            if s is not None:
+                if ctx.needs_input_grad[1] and s.owns(q_w) and s.view(q_w).dtype == torch.float32:
+                    acc_q = s.view(q_w)
+                if ctx.needs_input_grad[2] and s.owns(k_w) and s.view(k_w).dtype == torch.float32:
+                    acc_k = s.view(k_w)
             dqkv, dqw, dkw = native().qk_norm_rope_bwd(
                 dq, dk, dv, qkv.contiguous(), q_w, k_w, pos.contiguous(), inv_freq.contiguous(),
-                hq, hkv, d, float(eps), bool(unit), ct, st,
+                hq, hkv, d, float(eps), bool(unit), ct, st, acc_q, acc_k,
+                float(s.scale) if s is not None else 1.0,
             )
         else:
             with torch.enable_grad():
@@ -117,17 +128,18 @@ class _QKNormRope(torch.autograd.Function):
             dkw = grads[2].float() if kw_ is not None else None
         gq = gk = None
         if ctx.has_norm:
-            s = _sink.active()
-            for w, g, idx in ((q_w, dqw, 1), (k_w, dkw, 2)):
+            for w, g, idx, acc in ((q_w, dqw, 1, acc_q), (k_w, dkw, 2, acc_k)):
                 if not ctx.needs_input_grad[idx]:
                     continue
-                if s is not None and s.owns(w):
+                if acc is not None:
+                    s.deposits += 1
+                elif s is not None and s.owns(w):
                     s.add_(w, g)
                 elif idx == 1:
                     gq = g.to(w.dtype)
                 else:
                     gk = g.to(w.dtype)
-        return dqkv, gq, gk, None, None, None, None, None, None, None
+        return dqkv, gq, gk, None, None, None, None, None, None, None, None, None
 
 
 def qk_norm_rope(qkv, q_w, k_w, pos, inv_freq, hq, hkv, d, eps, unit_offset: bool = False):
