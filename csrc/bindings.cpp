@@ -66,6 +66,12 @@ void attn_trace_enable(bool on);
 void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
              double alpha);
 at::Tensor attn_trace_read();
+std::vector<at::Tensor> gdn_chunk_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                      const at::Tensor& g, const at::Tensor& beta, const at::Tensor& state);
+std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& dfinal, const at::Tensor& q,
+                                      const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                                      const at::Tensor& beta, const at::Tensor& starts, const at::Tensor& delta,
+                                      const at::Tensor& tsv, const at::Tensor& psv);
 int64_t gemm_tc_pair(int64_t on);
 std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
                                       bool with_entropy);
@@ -137,4 +143,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lmhead_dlogits_tc", &ts::lmhead_dlogits_tc);
   m.def("attn_trace_read", &ts::attn_trace_read);
   m.def("gdn_bwd", &ts::gdn_bwd);
+  m.def("gdn_chunk_fwd", &ts::gdn_chunk_fwd);
+  m.def("gdn_chunk_bwd", &ts::gdn_chunk_bwd);
 }

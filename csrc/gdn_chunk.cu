@@ -1,0 +1,927 @@
+// Chunked (WY-form) gated delta rule, forward and backward (K09', S9).
+//
+// Per head, over chunks of C = 64 tokens with the chunk-start state S0
+// ([dk, dv] = [128, 128], fp32), G the in-chunk inclusive cumsum of the log
+// decay g and γ = G_C:
+//
+//   A_ij = β_i e^{G_i−G_j} (k_i·k_j) (i > j),  T = (I + A)^{-1}
+//   W = T diag(β e^G) K,  U = T diag(β) V,  δ = U − W S0
+//   P_ij = e^{G_i−G_j} (q_i·k_j) (j ≤ i)
+//   O = diag(e^G) Q S0 + P δ,  S_C = e^γ S0 + Kᵀ diag(e^{γ−G}) δ
+//
+// with q, k L2-normalised (q also scaled by dk^-1/2) inside the kernels.
+// The serial dependency runs over chunks, not tokens:
+//
+//   gdn_wy_kernel        chunk-parallel: A, T, W, U
+//   gdn_state_fwd_kernel serial over chunks, one CTA per (head, 32 state
+//                        columns): δ, the chunk-start states, the inter-chunk
+//                        output diag(e^G) Q S0, the final state
+//   gdn_out_kernel       chunk-parallel: P and O = O_inter + P δ
+//   gdn_state_bwd_kernel serial over chunks in reverse, per (head, 32 columns):
+//                        dζ = Tᵀ(Pᵀ dO + diag(e^{γ−G}) K dS') and the state
+//                        gradient entering each chunk
+//   gdn_grads_state_kernel / gdn_grads_local_kernel  chunk-parallel: dq, dk,
+//                        dv, dβ, dg (terms through S0 / dS', then the C x C
+//                        terms, the reverse cumsum and the L2-norm VJP)
+//
+// The algebra and the hand-derived backward are the ones of
+// thundersync_b200/ops/gdn_chunked.py (checked there against autograd through
+// the token recurrence). All arithmetic is fp32 on the CUDA cores: the chunk
+// products are small (64 x 128 x 128) and sit on the serial chain, where
+// latency, not tensor throughput, bounds the time; fp32 operands keep the
+// final state within 1e-3 of the fp32 recurrence.
+#include "common.cuh"
+#include "common.h"
+
+namespace ts {
+namespace {
+
+constexpr int C = 64;          // chunk length
+constexpr int D = 128;         // dk = dv
+constexpr int NT = 256;        // threads per CTA
+constexpr int SL = 32;         // state columns per CTA in the serial kernels
+constexpr int LD = D + 1;      // padded leading dimensions (odd: conflict-free column walks)
+constexpr int LC = C + 1;
+constexpr int LS = SL + 1;
+constexpr float kNormEps = 1e-6f;
+
+typedef __nv_bfloat16 bf16;
+
+// acc[r][c] += Σ_k a(i, k) · b(k, j) for this thread's rows i = ti + r·(M/TM) and columns
+// j = tj + c·(N/TN); a(i, k) = TA ? A[k·lda + i] : A[i·lda + k], b(k, j) = TB ? B[j·ldb + k] : B[k·ldb + j].
+template <int M, int N, int TM, int TN, bool TA, bool TB>
+TS_DEVICE void mm_acc(float (&acc)[TM][TN], const float* A, int lda, const float* B, int ldb, int K) {
+  constexpr int RM = M / TM, RN = N / TN;
+  static_assert(RM * RN == NT, "tile shape must cover the CTA");
+  const int ti = threadIdx.x / RN, tj = threadIdx.x % RN;
+#pragma unroll 4
+  for (int k = 0; k < K; ++k) {
+    float a[TM], b[TN];
+#pragma unroll
+    for (int r = 0; r < TM; ++r) a[r] = TA ? A[k * lda + ti + r * RM] : A[(ti + r * RM) * lda + k];
+#pragma unroll
+    for (int c = 0; c < TN; ++c) b[c] = TB ? B[(tj + c * RN) * ldb + k] : B[k * ldb + tj + c * RN];
+#pragma unroll
+    for (int r = 0; r < TM; ++r)
+#pragma unroll
+      for (int c = 0; c < TN; ++c) acc[r][c] = fmaf(a[r], b[c], acc[r][c]);
+  }
+}
+
+template <int M, int N, int TM, int TN>
+struct Tile {
+  static constexpr int RM = M / TM, RN = N / TN;
+  TS_DEVICE static int row(int r) { return threadIdx.x / RN + r * RM; }
+  TS_DEVICE static int col(int c) { return threadIdx.x % RN + c * RN; }
+};
+
+template <int TM, int TN>
+TS_DEVICE void zero(float (&acc)[TM][TN]) {
+#pragma unroll
+  for (int r = 0; r < TM; ++r)
+#pragma unroll
+    for (int c = 0; c < TN; ++c) acc[r][c] = 0.f;
+}
+
+// rows [0, n) of a [T, H, D] bf16 tensor (head h, from token t0) into dst[C][LD] fp32, rows >= n zeroed;
+// with norm: rows are L2-normalised (rsqrt(|x|² + eps)) and scaled by `scale`
+TS_DEVICE void load_rows(float* dst, const bf16* __restrict__ src, int t0, int n, int H, int h, bool norm,
+                         float scale, float* rnorm = nullptr) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < C; r += NT / 32) {
+    float x[D / 32];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < D / 32; ++e) {
+      x[e] = r < n ? __bfloat162float(src[((size_t)(t0 + r) * H + h) * D + lane + 32 * e]) : 0.f;
+      ss += x[e] * x[e];
+    }
+    float m = scale;
+    if (norm) {
+      ss = warp_sum(ss);
+      const float rs = rsqrtf(ss + kNormEps);
+      m = rs * scale;
+      if (rnorm != nullptr && lane == 0) rnorm[r] = rs;
+    }
+#pragma unroll
+    for (int e = 0; e < D / 32; ++e) dst[r * LD + lane + 32 * e] = x[e] * m;
+  }
+}
+
+// rows of an fp32 [T, H, D] tensor, columns [c0, c0 + W) into dst[C][ld]
+template <int W>
+TS_DEVICE void load_f32(float* dst, int ld, const float* __restrict__ src, int t0, int n, int H, int h, int c0) {
+  for (int i = threadIdx.x; i < C * W; i += NT) {
+    const int r = i / W, c = i % W;
+    dst[r * ld + c] = r < n ? src[((size_t)(t0 + r) * H + h) * D + c0 + c] : 0.f;
+  }
+}
+template <int W>
+TS_DEVICE void load_bf16(float* dst, int ld, const bf16* __restrict__ src, int t0, int n, int H, int h, int c0) {
+  for (int i = threadIdx.x; i < C * W; i += NT) {
+    const int r = i / W, c = i % W;
+    dst[r * ld + c] = r < n ? __bfloat162float(src[((size_t)(t0 + r) * H + h) * D + c0 + c]) : 0.f;
+  }
+}
+
+// per-chunk scalars: G (inclusive cumsum of g), e^G, β, and γ = G at the last valid row
+struct ChunkScalars {
+  float G[C], eG[C], b[C];
+};
+TS_DEVICE void load_scalars(ChunkScalars& s, const float* __restrict__ g, const float* __restrict__ beta, int t0,
+                            int n, int H, int h) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float g0 = lane < n ? g[(size_t)(t0 + lane) * H + h] : 0.f;
+    float g1 = lane + 32 < n ? g[(size_t)(t0 + lane + 32) * H + h] : 0.f;
+    // inclusive warp scans, then offset the upper half
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float a0 = __shfl_up_sync(0xffffffffu, g0, o);
+      const float a1 = __shfl_up_sync(0xffffffffu, g1, o);
+      if (lane >= o) {
+        g0 += a0;
+        g1 += a1;
+      }
+    }
+    g1 += __shfl_sync(0xffffffffu, g0, 31);
+    s.G[lane] = g0;
+    s.G[lane + 32] = g1;
+    s.eG[lane] = __expf(g0);
+    s.eG[lane + 32] = __expf(g1);
+    s.b[lane] = lane < n ? beta[(size_t)(t0 + lane) * H + h] : 0.f;
+    s.b[lane + 32] = lane + 32 < n ? beta[(size_t)(t0 + lane + 32) * H + h] : 0.f;
+  }
+}
+
+// ------------------------------------------------------------------ forward 1: WY factors
+struct WySmem {
+  float K[C * LD];
+  float V[C * LD];
+  float A[C * LC];
+  float T[C * LC];
+  ChunkScalars s;
+};
+
+__global__ void __launch_bounds__(NT) gdn_wy_kernel(const bf16* __restrict__ k, const bf16* __restrict__ v,
+                                                    const float* __restrict__ g, const float* __restrict__ beta,
+                                                    float* __restrict__ w_out, float* __restrict__ u_out,
+                                                    float* __restrict__ t_out, int Tn, int H) {
+  extern __shared__ float smem_f[];
+  WySmem& sm = *reinterpret_cast<WySmem*>(smem_f);
+  const int ch = blockIdx.x, h = blockIdx.y;
+  const int t0 = ch * C, n = min(C, Tn - t0);
+  load_rows(sm.K, k, t0, n, H, h, true, 1.f);
+  load_rows(sm.V, v, t0, n, H, h, false, 1.f);
+  load_scalars(sm.s, g, beta, t0, n, H, h);
+  __syncthreads();
+  {  // A = strictly lower β_i e^{G_i − G_j} (k_i·k_j)
+    using Tl = Tile<C, C, 4, 4>;
+    float acc[4][4];
+    zero(acc);
+    mm_acc<C, C, 4, 4, false, true>(acc, sm.K, LD, sm.K, LD, D);
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int i = Tl::row(r), j = Tl::col(c);
+        sm.A[i * LC + j] = (i > j && i < n) ? sm.s.b[i] * __expf(sm.s.G[i] - sm.s.G[j]) * acc[r][c] : 0.f;
+      }
+  }
+  __syncthreads();
+  // T = (I + A)^{-1}: unit lower triangular; thread c owns column c and walks the rows in order
+  if (threadIdx.x < C) {
+    const int c = threadIdx.x;
+    for (int i = 0; i < C; ++i) {
+      float x = i == c ? 1.f : 0.f;
+      if (i > c) {
+        for (int j = c; j < i; ++j) x = fmaf(-sm.A[i * LC + j], sm.T[j * LC + c], x);
+      }
+      sm.T[i * LC + c] = x;
+    }
+  }
+  // row scales: K rows by β e^G, V rows by β
+  for (int i = threadIdx.x; i < C * D; i += NT) {
+    const int r = i / D, c = i % D;
+    sm.K[r * LD + c] *= sm.s.b[r] * sm.s.eG[r];
+    sm.V[r * LD + c] *= sm.s.b[r];
+  }
+  __syncthreads();
+  using Tw = Tile<C, D, 4, 8>;
+  {
+    float acc[4][8];
+    zero(acc);
+    mm_acc<C, D, 4, 8, false, false>(acc, sm.T, LC, sm.K, LD, C);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = Tw::row(r);
+      if (i < n)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) w_out[((size_t)(t0 + i) * H + h) * D + Tw::col(c)] = acc[r][c];
+    }
+  }
+  {
+    float acc[4][8];
+    zero(acc);
+    mm_acc<C, D, 4, 8, false, false>(acc, sm.T, LC, sm.V, LD, C);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = Tw::row(r);
+      if (i < n)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) u_out[((size_t)(t0 + i) * H + h) * D + Tw::col(c)] = acc[r][c];
+    }
+  }
+  float* tt = t_out + ((size_t)ch * H + h) * C * C;
+  for (int i = threadIdx.x; i < C * C; i += NT) tt[i] = sm.T[(i / C) * LC + (i % C)];
+}
+
+// ------------------------------------------------------------------ forward 2: the serial state pass
+struct StateFwdSmem {
+  float S[D * LS];   // state slice [128][32]
+  float M[C * LD];   // W chunk, then K chunk
+  float Q[C * LD];
+  float Dl[C * LS];  // δ slice
+  ChunkScalars s;
+};
+
+__global__ void __launch_bounds__(NT) gdn_state_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                           const float* __restrict__ g,
+                                                           const float* __restrict__ beta,
+                                                           const float* __restrict__ w, const float* __restrict__ u,
+                                                           const float* __restrict__ s_in, float* __restrict__ s_out,
+                                                           float* __restrict__ starts, float* __restrict__ delta,
+                                                           float* __restrict__ o_inter, int Tn, int H) {
+  extern __shared__ float smem_f[];
+  StateFwdSmem& sm = *reinterpret_cast<StateFwdSmem*>(smem_f);
+  const int h = blockIdx.x, j0 = blockIdx.y * SL;
+  const int nch = (Tn + C - 1) / C;
+  const float qscale = rsqrtf((float)D);
+  for (int i = threadIdx.x; i < D * SL; i += NT) sm.S[(i / SL) * LS + i % SL] = s_in[((size_t)h * D + i / SL) * D + j0 + i % SL];
+  __syncthreads();
+  for (int ch = 0; ch < nch; ++ch) {
+    const int t0 = ch * C, n = min(C, Tn - t0);
+    float* st = starts + ((size_t)ch * H + h) * D * D;
+    for (int i = threadIdx.x; i < D * SL; i += NT) st[(i / SL) * D + j0 + i % SL] = sm.S[(i / SL) * LS + i % SL];
+    load_f32<D>(sm.M, LD, w, t0, n, H, h, 0);
+    load_f32<SL>(sm.Dl, LS, u, t0, n, H, h, j0);
+    load_rows(sm.Q, q, t0, n, H, h, true, qscale);
+    load_scalars(sm.s, g, beta, t0, n, H, h);
+    __syncthreads();
+    using Td = Tile<C, SL, 2, 4>;
+    {  // δ = U − W S ; O_inter = diag(e^G) Q S
+      float acc[2][4], aq[2][4];
+      zero(acc);
+      zero(aq);
+      mm_acc<C, SL, 2, 4, false, false>(acc, sm.M, LD, sm.S, LS, D);
+      mm_acc<C, SL, 2, 4, false, false>(aq, sm.Q, LD, sm.S, LS, D);
+      __syncthreads();  // every read of W and S for this chunk is done
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int i = Td::row(r);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = Td::col(c);
+          const float d = i < n ? sm.Dl[i * LS + j] - acc[r][c] : 0.f;
+          sm.Dl[i * LS + j] = d;
+          if (i < n) {
+            const size_t o = ((size_t)(t0 + i) * H + h) * D + j0 + j;
+            delta[o] = d;
+            o_inter[o] = sm.s.eG[i] * aq[r][c];
+          }
+        }
+      }
+    }
+    load_rows(sm.M, k, t0, n, H, h, true, 1.f);
+    __syncthreads();
+    // δ rows scaled by e^{γ − G}
+    const float gam = sm.s.G[n - 1];
+    for (int i = threadIdx.x; i < C * SL; i += NT) {
+      const int r = i / SL;
+      sm.Dl[r * LS + i % SL] *= r < n ? __expf(gam - sm.s.G[r]) : 0.f;
+    }
+    __syncthreads();
+    {  // S = e^γ S + Kᵀ (e^{γ−G} δ)
+      using Ts = Tile<D, SL, 4, 4>;
+      float acc[4][4];
+      zero(acc);
+      mm_acc<D, SL, 4, 4, true, false>(acc, sm.M, LD, sm.Dl, LS, C);
+      const float eg = __expf(gam);
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float& x = sm.S[Ts::row(r) * LS + Ts::col(c)];
+          x = fmaf(eg, x, acc[r][c]);
+        }
+    }
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < D * SL; i += NT) s_out[((size_t)h * D + i / SL) * D + j0 + i % SL] = sm.S[(i / SL) * LS + i % SL];
+}
+
+// ------------------------------------------------------------------ forward 3: intra-chunk output
+struct OutSmem {
+  float Q[C * LD];
+  float K[C * LD];   // K, then δ
+  float P[C * LC];
+  ChunkScalars s;
+};
+
+__global__ void __launch_bounds__(NT) gdn_out_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                     const float* __restrict__ g, const float* __restrict__ beta,
+                                                     const float* __restrict__ delta,
+                                                     const float* __restrict__ o_inter, bf16* __restrict__ o,
+                                                     float* __restrict__ p_out, int Tn, int H) {
+  extern __shared__ float smem_f[];
+  OutSmem& sm = *reinterpret_cast<OutSmem*>(smem_f);
+  const int ch = blockIdx.x, h = blockIdx.y;
+  const int t0 = ch * C, n = min(C, Tn - t0);
+  load_rows(sm.Q, q, t0, n, H, h, true, rsqrtf((float)D));
+  load_rows(sm.K, k, t0, n, H, h, true, 1.f);
+  load_scalars(sm.s, g, beta, t0, n, H, h);
+  __syncthreads();
+  {
+    using Tl = Tile<C, C, 4, 4>;
+    float acc[4][4];
+    zero(acc);
+    mm_acc<C, C, 4, 4, false, true>(acc, sm.Q, LD, sm.K, LD, D);
+    float* pp = p_out + ((size_t)ch * H + h) * C * C;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int i = Tl::row(r), j = Tl::col(c);
+        const float x = (j <= i && i < n) ? __expf(sm.s.G[i] - sm.s.G[j]) * acc[r][c] : 0.f;
+        sm.P[i * LC + j] = x;
+        pp[i * C + j] = x;
+      }
+  }
+  __syncthreads();
+  load_f32<D>(sm.K, LD, delta, t0, n, H, h, 0);
+  __syncthreads();
+  using Tw = Tile<C, D, 4, 8>;
+  float acc[4][8];
+  zero(acc);
+  mm_acc<C, D, 4, 8, false, false>(acc, sm.P, LC, sm.K, LD, C);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = Tw::row(r);
+    if (i < n)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const size_t x = ((size_t)(t0 + i) * H + h) * D + Tw::col(c);
+        o[x] = __float2bfloat16_rn(o_inter[x] + acc[r][c]);
+      }
+  }
+}
+
+// ------------------------------------------------------------------ backward 1: the serial state-gradient pass
+struct StateBwdSmem {
+  float dS[D * LS];
+  float K[C * LD];
+  float Q[C * LD];
+  float P[C * LC];   // P, then T
+  float dO[C * LS];
+  float dd[C * LS];
+  ChunkScalars s;
+};
+
+__global__ void __launch_bounds__(NT) gdn_state_bwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                           const float* __restrict__ g,
+                                                           const float* __restrict__ beta,
+                                                           const bf16* __restrict__ dout,
+                                                           const float* __restrict__ p_sv, const float* __restrict__ t_sv,
+                                                           const float* __restrict__ dfinal,
+                                                           float* __restrict__ ds_sv, float* __restrict__ dz_out,
+                                                           float* __restrict__ dstate, int Tn, int H) {
+  extern __shared__ float smem_f[];
+  StateBwdSmem& sm = *reinterpret_cast<StateBwdSmem*>(smem_f);
+  const int h = blockIdx.x, j0 = blockIdx.y * SL;
+  const int nch = (Tn + C - 1) / C;
+  const float qscale = rsqrtf((float)D);
+  for (int i = threadIdx.x; i < D * SL; i += NT) sm.dS[(i / SL) * LS + i % SL] = dfinal[((size_t)h * D + i / SL) * D + j0 + i % SL];
+  __syncthreads();
+  for (int ch = nch - 1; ch >= 0; --ch) {
+    const int t0 = ch * C, n = min(C, Tn - t0);
+    float* dsv = ds_sv + ((size_t)ch * H + h) * D * D;
+    for (int i = threadIdx.x; i < D * SL; i += NT) dsv[(i / SL) * D + j0 + i % SL] = sm.dS[(i / SL) * LS + i % SL];
+    load_rows(sm.K, k, t0, n, H, h, true, 1.f);
+    load_rows(sm.Q, q, t0, n, H, h, true, qscale);
+    load_bf16<SL>(sm.dO, LS, dout, t0, n, H, h, j0);
+    load_scalars(sm.s, g, beta, t0, n, H, h);
+    {
+      const float* pp = p_sv + ((size_t)ch * H + h) * C * C;
+      for (int i = threadIdx.x; i < C * C; i += NT) sm.P[(i / C) * LC + i % C] = pp[i];
+    }
+    __syncthreads();
+    const float gam = sm.s.G[n - 1];
+    using Td = Tile<C, SL, 2, 4>;
+    {  // dd = Pᵀ dO + diag(e^{γ−G}) K dS'
+      float a1[2][4], a2[2][4];
+      zero(a1);
+      zero(a2);
+      mm_acc<C, SL, 2, 4, true, false>(a1, sm.P, LC, sm.dO, LS, C);
+      mm_acc<C, SL, 2, 4, false, false>(a2, sm.K, LD, sm.dS, LS, D);
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int i = Td::row(r);
+        const float e = i < n ? __expf(gam - sm.s.G[i]) : 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sm.dd[i * LS + Td::col(c)] = i < n ? a1[r][c] + e * a2[r][c] : 0.f;
+      }
+    }
+    __syncthreads();
+    {
+      const float* tt = t_sv + ((size_t)ch * H + h) * C * C;
+      for (int i = threadIdx.x; i < C * C; i += NT) sm.P[(i / C) * LC + i % C] = tt[i];
+    }
+    __syncthreads();
+    {  // dζ = Tᵀ dd, stored; then rows scaled by e^G β for the state term
+      float a[2][4];
+      zero(a);
+      mm_acc<C, SL, 2, 4, true, false>(a, sm.P, LC, sm.dd, LS, C);
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int i = Td::row(r);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = Td::col(c);
+          if (i < n) dz_out[((size_t)(t0 + i) * H + h) * D + j0 + j] = a[r][c];
+          sm.dd[i * LS + j] = i < n ? a[r][c] * sm.s.eG[i] * sm.s.b[i] : 0.f;
+          sm.dO[i * LS + j] *= i < n ? sm.s.eG[i] : 0.f;
+        }
+      }
+    }
+    __syncthreads();
+    {  // dS = e^γ dS' + Qᵀ diag(e^G) dO − Kᵀ diag(e^G β) dζ
+      using Ts = Tile<D, SL, 4, 4>;
+      float a[4][4], b[4][4];
+      zero(a);
+      zero(b);
+      mm_acc<D, SL, 4, 4, true, false>(a, sm.Q, LD, sm.dO, LS, C);
+      mm_acc<D, SL, 4, 4, true, false>(b, sm.K, LD, sm.dd, LS, C);
+      const float eg = __expf(gam);
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float& x = sm.dS[Ts::row(r) * LS + Ts::col(c)];
+          x = eg * x + a[r][c] - b[r][c];
+        }
+    }
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < D * SL; i += NT) dstate[((size_t)h * D + i / SL) * D + j0 + i % SL] = sm.dS[(i / SL) * LS + i % SL];
+}
+
+// ------------------------------------------------------------------ backward 2: terms through S0 and dS'
+// Per chunk: with R = V − diag(e^G) K S0 and dR = diag(β) dζ,
+//   dQ̂ += diag(e^G) dO S0ᵀ,  dK̂ += −diag(e^G) dR S0ᵀ + diag(e^{γ−G}) δ dS'ᵀ
+//   dβ_i += Σ_v dζ_iv R_iv
+//   dG_i += −e^{G_i} Σ_v (K S0)_iv dR_iv + e^{G_i} Σ_v dO_iv (Q S0)_iv − E_i,  E_i = e^{γ−G_i} Σ_v (K dS')_iv δ_iv
+//   dγ    = e^γ ⟨S0, dS'⟩ + Σ_i E_i
+struct GradStateSmem {
+  float S[D * LD];   // S0, then dS'
+  float K[C * LD];
+  float Q[C * LD];   // Q, then δ
+  float X[C * LD];   // dO
+  float Z[C * LD];   // dζ
+  float rowacc[C][4];
+  float red[NT / 32];
+  ChunkScalars s;
+};
+
+__global__ void __launch_bounds__(NT) gdn_grads_state_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v, const float* __restrict__ g,
+    const float* __restrict__ beta, const bf16* __restrict__ dout, const float* __restrict__ starts,
+    const float* __restrict__ ds_sv, const float* __restrict__ delta, const float* __restrict__ dz,
+    float* __restrict__ dqh, float* __restrict__ dkh, float* __restrict__ dbeta, float* __restrict__ dG,
+    float* __restrict__ dgam, int Tn, int H) {
+  extern __shared__ float smem_f[];
+  GradStateSmem& sm = *reinterpret_cast<GradStateSmem*>(smem_f);
+  const int ch = blockIdx.x, h = blockIdx.y;
+  const int t0 = ch * C, n = min(C, Tn - t0);
+  const float* S0 = starts + ((size_t)ch * H + h) * D * D;
+  for (int i = threadIdx.x; i < D * D; i += NT) sm.S[(i / D) * LD + i % D] = S0[i];
+  load_rows(sm.K, k, t0, n, H, h, true, 1.f);
+  load_rows(sm.Q, q, t0, n, H, h, true, rsqrtf((float)D));
+  load_bf16<D>(sm.X, LD, dout, t0, n, H, h, 0);
+  load_f32<D>(sm.Z, LD, dz, t0, n, H, h, 0);
+  load_scalars(sm.s, g, beta, t0, n, H, h);
+  for (int i = threadIdx.x; i < C * 4; i += NT) sm.rowacc[i / 4][i % 4] = 0.f;
+  __syncthreads();
+  using Tw = Tile<C, D, 4, 8>;
+  float dq[4][8], dk[4][8];
+  float rb[4] = {0.f, 0.f, 0.f, 0.f}, rg[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    float ks[4][8], qs[4][8];
+    zero(ks);
+    zero(qs);
+    mm_acc<C, D, 4, 8, false, false>(ks, sm.K, LD, sm.S, LD, D);   // K S0
+    mm_acc<C, D, 4, 8, false, false>(qs, sm.Q, LD, sm.S, LD, D);   // Q S0
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = Tw::row(r);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int j = Tw::col(c);
+        const float vv = i < n ? __bfloat162float(v[((size_t)(t0 + i) * H + h) * D + j]) : 0.f;
+        const float z = sm.Z[i * LD + j];
+        const float R = vv - sm.s.eG[i] * ks[r][c];
+        rb[r] = fmaf(z, R, rb[r]);
+        rg[r] += -sm.s.eG[i] * ks[r][c] * sm.s.b[i] * z + sm.s.eG[i] * sm.X[i * LD + j] * qs[r][c];
+      }
+    }
+  }
+  zero(dq);
+  zero(dk);
+  mm_acc<C, D, 4, 8, false, true>(dq, sm.X, LD, sm.S, LD, D);   // dO S0ᵀ
+  mm_acc<C, D, 4, 8, false, true>(dk, sm.Z, LD, sm.S, LD, D);   // dζ S0ᵀ
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = Tw::row(r);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      dq[r][c] *= sm.s.eG[i];
+      dk[r][c] *= -sm.s.eG[i] * sm.s.b[i];
+    }
+  }
+  // e^γ ⟨S0, dS'⟩ (this chunk's dS' is read straight from global memory)
+  const float* dSp = ds_sv + ((size_t)ch * H + h) * D * D;
+  float dot = 0.f;
+  for (int i = threadIdx.x; i < D * D; i += NT) dot = fmaf(sm.S[(i / D) * LD + i % D], dSp[i], dot);
+  __syncthreads();  // S0 and Q no longer needed
+  for (int i = threadIdx.x; i < D * D; i += NT) sm.S[(i / D) * LD + i % D] = dSp[i];
+  load_f32<D>(sm.Q, LD, delta, t0, n, H, h, 0);
+  __syncthreads();
+  const float gam = sm.s.G[n - 1];
+  float re[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    float kd[4][8], dd[4][8];
+    zero(kd);
+    zero(dd);
+    mm_acc<C, D, 4, 8, false, false>(kd, sm.K, LD, sm.S, LD, D);   // K dS'
+    mm_acc<C, D, 4, 8, false, true>(dd, sm.Q, LD, sm.S, LD, D);    // δ dS'ᵀ
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = Tw::row(r);
+      const float e = i < n ? __expf(gam - sm.s.G[i]) : 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        re[r] = fmaf(kd[r][c], sm.Q[i * LD + Tw::col(c)], re[r]);
+        dk[r][c] = fmaf(e, dd[r][c], dk[r][c]);
+      }
+      re[r] *= e;
+    }
+  }
+  // row sums over the 16 threads that share each row (tj = tid % 16 within the same ti)
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+#pragma unroll
+    for (int o = 8; o; o >>= 1) {
+      rb[r] += __shfl_xor_sync(0xffffffffu, rb[r], o);
+      rg[r] += __shfl_xor_sync(0xffffffffu, rg[r], o);
+      re[r] += __shfl_xor_sync(0xffffffffu, re[r], o);
+    }
+  }
+  if ((threadIdx.x % Tw::RN) == 0) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = Tw::row(r);
+      sm.rowacc[i][0] = rb[r];
+      sm.rowacc[i][1] = rg[r] - re[r];
+      sm.rowacc[i][2] = re[r];
+    }
+  }
+  // dγ: e^γ ⟨S0, dS'⟩ + Σ_i E_i
+  dot = warp_sum(dot);
+  if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = dot;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < NT / 32; ++w) tot += sm.red[w];
+    float es = 0.f;
+    for (int i = 0; i < n; ++i) es += sm.rowacc[i][2];
+    dgam[(size_t)ch * H + h] = __expf(gam) * tot + es;
+  }
+  for (int i = threadIdx.x; i < n; i += NT) {
+    dbeta[(size_t)(t0 + i) * H + h] = sm.rowacc[i][0];
+    dG[(size_t)(t0 + i) * H + h] = sm.rowacc[i][1];
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = Tw::row(r);
+    if (i < n)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const size_t x = ((size_t)(t0 + i) * H + h) * D + Tw::col(c);
+        dqh[x] = dq[r][c];
+        dkh[x] = dk[r][c];
+      }
+  }
+}
+
+// ------------------------------------------------------------------ backward 3: C x C terms, cumsum, L2-norm VJP
+// dA = −dζ δᵀ (i > j), dP = dO δᵀ (j ≤ i); with A, P the forward's matrices:
+//   dM = dA ⊙ β_i e^{G_i−G_j},  dN = dP ⊙ e^{G_i−G_j}
+//   dK̂ += dM K + dMᵀ K + dNᵀ Q,  dQ̂ += dN K
+//   dβ_i += Σ_j dA_ij e^{G_i−G_j} (k_i·k_j),  dG += rowsum(dA⊙A) − colsum(dA⊙A) + rowsum(dP⊙P) − colsum(dP⊙P)
+//   dg = reverse cumsum of dG (+ dγ at the last row); dv = β ⊙ dζ
+struct GradLocalSmem {
+  float K[C * LD];
+  float Q[C * LD];
+  float X[C * LD];   // dO, then dζ
+  float Y[C * LD];   // δ
+  float dM[C * LC];
+  float dN[C * LC];
+  float rowacc[C][2];
+  ChunkScalars s;
+};
+
+__global__ void __launch_bounds__(NT) gdn_grads_local_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
+    const float* __restrict__ beta, const bf16* __restrict__ dout, const float* __restrict__ delta,
+    const float* __restrict__ dz, const float* __restrict__ dqh, const float* __restrict__ dkh,
+    const float* __restrict__ dbeta_s, const float* __restrict__ dG_s, const float* __restrict__ dgam,
+    bf16* __restrict__ dq, bf16* __restrict__ dk, bf16* __restrict__ dv, float* __restrict__ dg,
+    float* __restrict__ dbeta, int Tn, int H) {
+  extern __shared__ float smem_f[];
+  GradLocalSmem& sm = *reinterpret_cast<GradLocalSmem*>(smem_f);
+  const int ch = blockIdx.x, h = blockIdx.y;
+  const int t0 = ch * C, n = min(C, Tn - t0);
+  load_rows(sm.K, k, t0, n, H, h, true, 1.f);
+  load_rows(sm.Q, q, t0, n, H, h, true, rsqrtf((float)D));
+  load_bf16<D>(sm.X, LD, dout, t0, n, H, h, 0);
+  load_f32<D>(sm.Y, LD, delta, t0, n, H, h, 0);
+  load_scalars(sm.s, g, beta, t0, n, H, h);
+  for (int i = threadIdx.x; i < C * 2; i += NT) sm.rowacc[i / 2][i % 2] = 0.f;
+  __syncthreads();
+  using Tl = Tile<C, C, 4, 4>;
+  float pdp[4][4];
+  {  // dP = dO δᵀ and P = e^{G_i−G_j} q_i·k_j (j ≤ i)
+    float dp[4][4], qk[4][4];
+    zero(dp);
+    zero(qk);
+    mm_acc<C, C, 4, 4, false, true>(dp, sm.X, LD, sm.Y, LD, D);
+    mm_acc<C, C, 4, 4, false, true>(qk, sm.Q, LD, sm.K, LD, D);
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int i = Tl::row(r), j = Tl::col(c);
+        const bool on = j <= i && i < n;
+        const float e = on ? __expf(sm.s.G[i] - sm.s.G[j]) : 0.f;
+        sm.dN[i * LC + j] = on ? dp[r][c] * e : 0.f;
+        pdp[r][c] = on ? dp[r][c] * e * qk[r][c] : 0.f;
+      }
+  }
+  __syncthreads();
+  load_f32<D>(sm.X, LD, dz, t0, n, H, h, 0);  // dO -> dζ
+  __syncthreads();
+  float ada[4][4];
+  {  // dA = −dζ δᵀ (i > j); A = β_i e^{G_i−G_j} k_i·k_j
+    float da[4][4], kk[4][4];
+    zero(da);
+    zero(kk);
+    mm_acc<C, C, 4, 4, false, true>(da, sm.X, LD, sm.Y, LD, D);
+    mm_acc<C, C, 4, 4, false, true>(kk, sm.K, LD, sm.K, LD, D);
+    float rbeta[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = Tl::row(r);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int j = Tl::col(c);
+        const bool on = i > j && i < n;
+        const float el = on ? __expf(sm.s.G[i] - sm.s.G[j]) : 0.f;
+        const float dA = on ? -da[r][c] : 0.f;
+        sm.dM[i * LC + j] = dA * sm.s.b[i] * el;
+        ada[r][c] = dA * sm.s.b[i] * el * kk[r][c];
+        rbeta[r] = fmaf(dA * el, kk[r][c], rbeta[r]);
+      }
+    }
+    // row sums over the 16 threads of a row, then atomics-free accumulation through shared memory
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int o = 8; o; o >>= 1) rbeta[r] += __shfl_xor_sync(0xffffffffu, rbeta[r], o);
+    if ((threadIdx.x % Tl::RN) == 0)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) sm.rowacc[Tl::row(r)][0] = rbeta[r];
+  }
+  __syncthreads();
+  // dG partial from the C x C terms: rowsum − colsum of (dA⊙A + dP⊙P); a column j's sum is over
+  // the threads holding rows of column j — gather through the dN-sized scratch in Y (δ is no longer needed)
+  {
+    float* Mx = sm.Y;  // [C][LC] view
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) Mx[Tl::row(r) * LC + Tl::col(c)] = ada[r][c] + pdp[r][c];
+  }
+  __syncthreads();
+  if (threadIdx.x < C) {
+    const int i = threadIdx.x;
+    const float* Mx = sm.Y;
+    float rs = 0.f, cs = 0.f;
+    for (int j = 0; j < C; ++j) {
+      rs += Mx[i * LC + j];
+      cs += Mx[j * LC + i];
+    }
+    sm.rowacc[i][1] = rs - cs;
+  }
+  __syncthreads();
+  // dG total and the reverse cumsum (one warp, two values per lane)
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float a0 = 0.f, a1 = 0.f;
+    if (lane < n) a0 = dG_s[(size_t)(t0 + lane) * H + h] + sm.rowacc[lane][1];
+    if (lane + 32 < n) a1 = dG_s[(size_t)(t0 + lane + 32) * H + h] + sm.rowacc[lane + 32][1];
+    if (lane == n - 1) a0 += dgam[(size_t)ch * H + h];
+    if (lane + 32 == n - 1) a1 += dgam[(size_t)ch * H + h];
+    // reverse inclusive scan over 64 values: suffix sums
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float b0 = __shfl_down_sync(0xffffffffu, a0, o);
+      const float b1 = __shfl_down_sync(0xffffffffu, a1, o);
+      if (lane + o < 32) {
+        a0 += b0;
+        a1 += b1;
+      }
+    }
+    a0 += __shfl_sync(0xffffffffu, a1, 0);
+    if (lane < n) dg[(size_t)(t0 + lane) * H + h] = a0;
+    if (lane + 32 < n) dg[(size_t)(t0 + lane + 32) * H + h] = a1;
+  }
+  for (int i = threadIdx.x; i < n; i += NT)
+    dbeta[(size_t)(t0 + i) * H + h] = dbeta_s[(size_t)(t0 + i) * H + h] + sm.rowacc[i][0];
+  // dv = β ⊙ dζ
+  for (int i = threadIdx.x; i < n * D; i += NT) {
+    const int r = i / D, c = i % D;
+    dv[((size_t)(t0 + r) * H + h) * D + c] = __float2bfloat16_rn(sm.s.b[r] * sm.X[r * LD + c]);
+  }
+  // dK̂ += dM K + dMᵀ K + dNᵀ Q ;  dQ̂ += dN K
+  using Tw = Tile<C, D, 4, 8>;
+  float ak[4][8], aq[4][8];
+  zero(ak);
+  zero(aq);
+  mm_acc<C, D, 4, 8, false, false>(ak, sm.dM, LC, sm.K, LD, C);
+  mm_acc<C, D, 4, 8, true, false>(ak, sm.dM, LC, sm.K, LD, C);
+  mm_acc<C, D, 4, 8, true, false>(ak, sm.dN, LC, sm.Q, LD, C);
+  mm_acc<C, D, 4, 8, false, false>(aq, sm.dN, LC, sm.K, LD, C);
+  __syncthreads();
+  // add the state terms, then stage dq̂ (scaled by dk^-1/2) and dk̂ rows in shared memory for the L2-norm VJP
+  const float qscale = rsqrtf((float)D);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = Tw::row(r);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int j = Tw::col(c);
+      const size_t x = ((size_t)(t0 + i) * H + h) * D + j;
+      const float sq = i < n ? dqh[x] : 0.f, sk = i < n ? dkh[x] : 0.f;
+      sm.Q[i * LD + j] = (aq[r][c] + sq) * qscale;
+      sm.X[i * LD + j] = ak[r][c] + sk;
+    }
+  }
+  __syncthreads();
+  // L2-norm VJP per row: dx = r dy − r³ x (x·dy), r = rsqrt(|x|² + eps); one warp per row
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int rr = warp; rr < n; rr += NT / 32) {
+    for (int which = 0; which < 2; ++which) {
+      const bf16* src = which == 0 ? q : k;
+      const float* dy = which == 0 ? sm.Q : sm.X;
+      bf16* dst = which == 0 ? dq : dk;
+      float x[D / 32], ss = 0.f, xd = 0.f;
+#pragma unroll
+      for (int e = 0; e < D / 32; ++e) {
+        x[e] = __bfloat162float(src[((size_t)(t0 + rr) * H + h) * D + lane + 32 * e]);
+        ss += x[e] * x[e];
+        xd += x[e] * dy[rr * LD + lane + 32 * e];
+      }
+      ss = warp_sum(ss);
+      xd = warp_sum(xd);
+      const float r = rsqrtf(ss + kNormEps);
+      const float r3 = r * r * r;
+#pragma unroll
+      for (int e = 0; e < D / 32; ++e)
+        dst[((size_t)(t0 + rr) * H + h) * D + lane + 32 * e] =
+            __float2bfloat16_rn(r * dy[rr * LD + lane + 32 * e] - r3 * x[e] * xd);
+    }
+  }
+}
+
+template <typename K>
+void set_smem(K kernel, size_t bytes) {
+  TS_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+}
+
+}  // namespace
+
+// q, k, v [T, H, 128] bf16; g, beta [T, H] fp32; state [H, 128, 128] fp32.
+// Returns (o, final_state, saved...) where saved = (starts, delta, T factors, P).
+std::vector<at::Tensor> gdn_chunk_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                      const at::Tensor& g, const at::Tensor& beta, const at::Tensor& state) {
+  check_cuda(q, "q");
+  TS_CHECK(q.dim() == 3 && q.size(2) == D && k.sizes() == q.sizes() && v.sizes() == q.sizes(),
+           "gdn_chunk_fwd: q, k, v must be [T, H, 128]");
+  TS_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16 &&
+               g.scalar_type() == at::kFloat && beta.scalar_type() == at::kFloat && state.scalar_type() == at::kFloat,
+           "gdn_chunk_fwd: bf16 q/k/v, fp32 g/beta/state");
+  TS_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && g.is_contiguous() && beta.is_contiguous() &&
+               state.is_contiguous(),
+           "gdn_chunk_fwd: contiguous inputs");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int Tn = q.size(0), H = q.size(1);
+  const int nch = (Tn + C - 1) / C;
+  auto f32 = q.options().dtype(at::kFloat);
+  auto o = at::empty_like(v);
+  auto fin = at::empty_like(state);
+  auto starts = at::empty({std::max(nch, 1), H, D, D}, f32);
+  auto delta = at::empty({Tn, H, D}, f32);
+  auto tsv = at::empty({std::max(nch, 1), H, C, C}, f32);
+  auto psv = at::empty({std::max(nch, 1), H, C, C}, f32);
+  if (Tn == 0) {
+    fin.copy_(state);
+    return {o, fin, starts, delta, tsv, psv};
+  }
+  auto w = at::empty({Tn, H, D}, f32);
+  auto u = at::empty({Tn, H, D}, f32);
+  auto oint = at::empty({Tn, H, D}, f32);
+  const bf16* qp = (const bf16*)q.data_ptr();
+  const bf16* kp = (const bf16*)k.data_ptr();
+  const bf16* vp = (const bf16*)v.data_ptr();
+  set_smem(gdn_wy_kernel, sizeof(WySmem));
+  gdn_wy_kernel<<<dim3(nch, H), NT, sizeof(WySmem), stream()>>>(kp, vp, g.data_ptr<float>(), beta.data_ptr<float>(),
+                                                                 w.data_ptr<float>(), u.data_ptr<float>(),
+                                                                 tsv.data_ptr<float>(), Tn, H);
+  set_smem(gdn_state_fwd_kernel, sizeof(StateFwdSmem));
+  gdn_state_fwd_kernel<<<dim3(H, D / SL), NT, sizeof(StateFwdSmem), stream()>>>(
+      qp, kp, g.data_ptr<float>(), beta.data_ptr<float>(), w.data_ptr<float>(), u.data_ptr<float>(),
+      state.data_ptr<float>(), fin.data_ptr<float>(), starts.data_ptr<float>(), delta.data_ptr<float>(),
+      oint.data_ptr<float>(), Tn, H);
+  set_smem(gdn_out_kernel, sizeof(OutSmem));
+  gdn_out_kernel<<<dim3(nch, H), NT, sizeof(OutSmem), stream()>>>(qp, kp, g.data_ptr<float>(), beta.data_ptr<float>(),
+                                                                   delta.data_ptr<float>(), oint.data_ptr<float>(),
+                                                                   (bf16*)o.data_ptr(), psv.data_ptr<float>(), Tn, H);
+  TS_LAUNCH_CHECK();
+  return {o, fin, starts, delta, tsv, psv};
+}
+
+// Returns (dq, dk, dv, dg, dbeta, dstate).
+std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& dfinal, const at::Tensor& q,
+                                      const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                                      const at::Tensor& beta, const at::Tensor& starts, const at::Tensor& delta,
+                                      const at::Tensor& tsv, const at::Tensor& psv) {
+  check_cuda(q, "q");
+  TS_CHECK(dout.is_contiguous() && dfinal.is_contiguous() && dout.scalar_type() == at::kBFloat16 &&
+               dfinal.scalar_type() == at::kFloat && dout.sizes() == q.sizes(),
+           "gdn_chunk_bwd: contiguous bf16 dout shaped like q, fp32 dfinal");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int Tn = q.size(0), H = q.size(1);
+  const int nch = (Tn + C - 1) / C;
+  auto f32 = q.options().dtype(at::kFloat);
+  auto dq = at::empty_like(q);
+  auto dk = at::empty_like(k);
+  auto dv = at::empty_like(v);
+  auto dg = at::empty({Tn, H}, f32);
+  auto dbeta = at::empty({Tn, H}, f32);
+  auto dstate = at::empty_like(dfinal);
+  if (Tn == 0) {
+    dstate.copy_(dfinal);
+    return {dq, dk, dv, dg, dbeta, dstate};
+  }
+  auto dssv = at::empty({nch, H, D, D}, f32);
+  auto dz = at::empty({Tn, H, D}, f32);
+  auto dqh = at::empty({Tn, H, D}, f32);
+  auto dkh = at::empty({Tn, H, D}, f32);
+  auto dbs = at::empty({Tn, H}, f32);
+  auto dGs = at::empty({Tn, H}, f32);
+  auto dgam = at::empty({nch, H}, f32);
+  const bf16* qp = (const bf16*)q.data_ptr();
+  const bf16* kp = (const bf16*)k.data_ptr();
+  const bf16* dop = (const bf16*)dout.data_ptr();
+  set_smem(gdn_state_bwd_kernel, sizeof(StateBwdSmem));
+  gdn_state_bwd_kernel<<<dim3(H, D / SL), NT, sizeof(StateBwdSmem), stream()>>>(
+      qp, kp, g.data_ptr<float>(), beta.data_ptr<float>(), dop, psv.data_ptr<float>(), tsv.data_ptr<float>(),
+      dfinal.data_ptr<float>(), dssv.data_ptr<float>(), dz.data_ptr<float>(), dstate.data_ptr<float>(), Tn, H);
+  set_smem(gdn_grads_state_kernel, sizeof(GradStateSmem));
+  gdn_grads_state_kernel<<<dim3(nch, H), NT, sizeof(GradStateSmem), stream()>>>(
+      qp, kp, (const bf16*)v.data_ptr(), g.data_ptr<float>(), beta.data_ptr<float>(), dop, starts.data_ptr<float>(),
+      dssv.data_ptr<float>(), delta.data_ptr<float>(), dz.data_ptr<float>(), dqh.data_ptr<float>(),
+      dkh.data_ptr<float>(), dbs.data_ptr<float>(), dGs.data_ptr<float>(), dgam.data_ptr<float>(), Tn, H);
+  set_smem(gdn_grads_local_kernel, sizeof(GradLocalSmem));
+  gdn_grads_local_kernel<<<dim3(nch, H), NT, sizeof(GradLocalSmem), stream()>>>(
+      qp, kp, g.data_ptr<float>(), beta.data_ptr<float>(), dop, delta.data_ptr<float>(), dz.data_ptr<float>(),
+      dqh.data_ptr<float>(), dkh.data_ptr<float>(), dbs.data_ptr<float>(), dGs.data_ptr<float>(),
+      dgam.data_ptr<float>(), (bf16*)dq.data_ptr(), (bf16*)dk.data_ptr(), (bf16*)dv.data_ptr(),
+      dg.data_ptr<float>(), dbeta.data_ptr<float>(), Tn, H);
+  TS_LAUNCH_CHECK();
+  return {dq, dk, dv, dg, dbeta, dstate};
+}
+
+}  // namespace ts

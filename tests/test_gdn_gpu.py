@@ -63,3 +63,36 @@ def test_gated_delta_rule_matches_reference(t, h):
     assert _rel(fin, finr) < 1e-3
     for got, ref in zip((q, k, v, g, beta, s0), ins):
         assert _rel(got.grad, ref.grad) < 2e-2, (got.shape, _rel(got.grad, ref.grad))
+
+
+@pytest.mark.parametrize("t,h", [(1000, 3), (64, 2), (129, 1)])
+def test_chunked_gated_delta_rule_matches_recurrent_kernels(t, h):
+    """The chunked WY-form kernels against the token-recurrent kernels and the fp32 reference."""
+    from thundersync_b200.ops import gdn as G
+
+    torch.manual_seed(11 * t + h)
+    d = 128
+    q = torch.randn(t, h, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(t, h, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(t, h, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    g = (-torch.rand(t, h, device="cuda") * 0.2).requires_grad_(True)
+    beta = torch.rand(t, h, device="cuda").requires_grad_(True)
+    s0 = (torch.randn(h, d, d, device="cuda") * 0.05).requires_grad_(True)
+    do = torch.randn(t, h, d, device="cuda", dtype=torch.bfloat16)
+    dfin = torch.randn(h, d, d, device="cuda") * 0.1
+    res = []
+    for chunked in (True, False):
+        G.CHUNKED = chunked
+        try:
+            o, fin = G.gated_delta_rule(q, k, v, g, beta, s0)
+            grads = torch.autograd.grad((o, fin), (q, k, v, g, beta, s0), (do, dfin))
+        finally:
+            G.CHUNKED = True
+        res.append((o, fin) + tuple(grads))
+    ins = [a.detach().float().requires_grad_(True) for a in (q, k, v, g, beta, s0)]
+    orf, finr = gated_delta_rule_reference(*ins)
+    gr = torch.autograd.grad((orf.float(), finr), ins, (do.float(), dfin))
+    assert _rel(res[0][0], orf) < 1e-2
+    assert _rel(res[0][1], finr) < 1e-3
+    for a, b, r in zip(res[0][2:], res[1][2:], gr):
+        assert _rel(a, r) < 2e-2, (a.shape, _rel(a, r), _rel(b, r))

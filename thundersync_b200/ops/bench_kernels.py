@@ -12,7 +12,9 @@ Families: ``attn`` (bottom-right causal GQA attention; fwd, or fwd+bwd),
 ``swiglu``, ``rope`` (QK-norm + RoPE), ``dlogits``, ``adamw``, ``fold``
 (GRPO statistic folds), ``gemm`` (tcgen05 GEMM vs the library at decoder
 shapes), ``lmhead`` (fused tcgen05 LM-head logprob fwd+bwd vs the unfused
-cuBLAS-logits path) and ``gemm_host`` (host cost of a library GEMM call).
+cuBLAS-logits path), ``baselines`` (attention vs FlashAttention-2, the reference's
+GPU path without FA4, and the gated delta rule timed alone) and
+``gemm_host`` (host cost of a library GEMM call).
 """
 
 from __future__ import annotations
@@ -113,6 +115,55 @@ def bench_rms(args) -> None:
         ms = _time(lambda: fn(dy.data_ptr(), x.data_ptr(), w.data_ptr(), r.data_ptr(), dx.data_ptr(),
                               dw.data_ptr(), args.rows, args.cols, 0, st), args.iters)
         print(f"rms bwd (three kernels): {ms:.3f} ms  {1.5 * gb / ms * 1e3:.0f} GB/s")
+
+
+def bench_baselines(args) -> None:
+    """The reference's GPU baselines on this box, next to this package's kernels: attention against
+    FlashAttention-2 (the reference's path when FA4 is absent; bottom-right causal, GQA). The gated delta rule
+    is timed alone: FLA's chunked Triton kernel, the reference's hybrid-layer path, faulted on this box."""
+    from thundersync_b200.ops.attention import chunked_attention
+    from thundersync_b200.ops.gdn import gated_delta_rule
+
+    torch.manual_seed(0)
+    for t, s, hq, hkv, d in ((args.t, args.s, args.hq, args.hkv, 128), (args.t, args.s, 16, 2, 256)):
+        q = torch.randn(t, hq, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        k = torch.randn(s, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        v = torch.randn(s, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        do = torch.randn(t, hq, d, device="cuda", dtype=torch.bfloat16)
+        pairs = t * (s - t) + t * (t + 1) / 2
+        flops = 4.0 * pairs * hq * d
+        with torch.no_grad():
+            f_ours = _time(lambda: chunked_attention(q, [k], [v]), args.iters)
+        b_ours = _time(lambda: torch.autograd.grad(chunked_attention(q, [k], [v]), (q, k, v), do), args.iters)
+        line = (f"attention T={t} S={s} {hq}/{hkv} heads d={d}: ours fwd {f_ours:.3f} ms "
+                f"({flops / f_ours / 1e9:.0f} TFLOP/s), fwd+bwd {b_ours:.3f} ms ({3.5 * flops / b_ours / 1e9:.0f})")
+        try:
+            from flash_attn import flash_attn_func
+
+            q4, k4, v4, do4 = q[None], k[None], v[None], do[None]
+            with torch.no_grad():
+                f_fa = _time(lambda: flash_attn_func(q4, k4, v4, causal=True), args.iters)
+            b_fa = _time(lambda: torch.autograd.grad(flash_attn_func(q4, k4, v4, causal=True), (q4, k4, v4), do4),
+                         args.iters)
+            line += (f"; FlashAttention-2 fwd {f_fa:.3f} ms ({flops / f_fa / 1e9:.0f}), "
+                     f"fwd+bwd {b_fa:.3f} ms ({3.5 * flops / b_fa / 1e9:.0f})")
+        except Exception as exc:  # noqa: BLE001 - report, do not fail the other lines
+            line += f"; FlashAttention-2 unavailable ({type(exc).__name__}: {exc})"[:160]
+        print(line)
+    t, h, dk = args.t, args.h, 128
+    q = torch.randn(t, h, dk, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(t, h, dk, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(t, h, dk, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    g = (-torch.rand(t, h, device="cuda") * 0.3).requires_grad_(True)
+    beta = torch.rand(t, h, device="cuda").requires_grad_(True)
+    s0 = torch.zeros(h, dk, dk, device="cuda", requires_grad=True)
+    do = torch.randn(t, h, dk, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        f_ours = _time(lambda: gated_delta_rule(q, k, v, g, beta, s0), args.iters)
+    b_ours = _time(lambda: torch.autograd.grad(gated_delta_rule(q, k, v, g, beta, s0)[0], (q, k, v, g, beta, s0), do),
+                   args.iters)
+    # FLA's chunked Triton kernel is not run: on this box it raised "misaligned address" (a device fault)
+    print(f"gated delta rule T={t} H={h} dk=dv={dk}: ours fwd {f_ours:.3f} ms, fwd+bwd {b_ours:.3f} ms")
 
 
 def bench_lse(args) -> None:
@@ -309,7 +360,7 @@ def bench_gemm_host(args) -> None:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host", "swiglu", "rope", "dlogits",
-                                       "adamw", "fold", "gemm", "lmhead"])
+                                       "adamw", "fold", "gemm", "lmhead", "baselines"])
     ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
     ap.add_argument("--t", type=int, default=2048)
     ap.add_argument("--s", type=int, default=2560)
@@ -325,7 +376,7 @@ def main(argv=None) -> None:
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
      "gemm_host": bench_gemm_host, "swiglu": bench_swiglu, "rope": bench_rope, "dlogits": bench_dlogits,
      "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm,
-     "lmhead": bench_lmhead}[args.family](args)
+     "lmhead": bench_lmhead, "baselines": bench_baselines}[args.family](args)
 
 
 if __name__ == "__main__":

@@ -110,10 +110,25 @@ def gated_delta_rule_reference(q, k, v, g, beta, state=None):
     return o.to(q.dtype), s
 
 
+# CUDA, dk = dv = 128: the chunked WY-form kernels (serial over 64-token chunks); otherwise the
+# token-recurrent kernels
+CHUNKED = True
+
+
+def _chunked_ok(q, v) -> bool:
+    return CHUNKED and q.is_cuda and q.shape[-1] == 128 and v.shape[-1] == 128 and q.dtype == torch.bfloat16
+
+
 class _GDN(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, g, beta, state):
-        if q.is_cuda:
+        ctx.chunked = _chunked_ok(q, v)
+        if ctx.chunked:
+            o, final, *saved = native().gdn_chunk_fwd(
+                q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(), beta.float().contiguous(),
+                state.float().contiguous())
+            ctx.save_for_backward(q, k, v, g, beta, state, *saved)
+        elif q.is_cuda:
             o, final, ckpt = native().gdn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
                                               beta.float().contiguous(), state.contiguous())
             ctx.save_for_backward(q, k, v, g, beta, state, ckpt)
@@ -131,6 +146,11 @@ class _GDN(torch.autograd.Function):
             do = torch.zeros(v.shape, dtype=v.dtype, device=v.device)
         if dfinal is None:
             dfinal = torch.zeros_like(state)
+        if ctx.chunked:
+            dq, dk, dv, dg, dbeta, dstate = native().gdn_chunk_bwd(
+                do.to(q.dtype).contiguous(), dfinal.float().contiguous(), q.contiguous(), k.contiguous(),
+                v.contiguous(), g.float().contiguous(), beta.float().contiguous(), *saved[6:])
+            return dq, dk, dv, dg.to(g.dtype), dbeta.to(beta.dtype), dstate.to(state.dtype)
         if q.is_cuda:
             ckpt = saved[6]
             dq, dk, dv, dg, dbeta, dstate = native().gdn_bwd(
