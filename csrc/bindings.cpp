@@ -71,7 +71,8 @@ std::vector<at::Tensor> gdn_chunk_fwd(const at::Tensor& q, const at::Tensor& k, 
 std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& dfinal, const at::Tensor& q,
                                       const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
                                       const at::Tensor& beta, const at::Tensor& starts, const at::Tensor& delta,
-                                      const at::Tensor& tsv, const at::Tensor& psv);
+                                      const at::Tensor& tsv, const at::Tensor& psv, const at::Tensor& kd,
+                                      const at::Tensor& kb);
 int64_t gemm_tc_pair(int64_t on);
 std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
                                       bool with_entropy);

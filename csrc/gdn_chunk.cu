@@ -12,14 +12,16 @@
 // with q, k L2-normalised (q also scaled by dk^-1/2) inside the kernels.
 // The serial dependency runs over chunks, not tokens:
 //
-//   gdn_wy_kernel        chunk-parallel: A, T, W, U
-//   gdn_state_fwd_kernel serial over chunks, one CTA per (head, 32 state
-//                        columns): δ, the chunk-start states, the inter-chunk
-//                        output diag(e^G) Q S0, the final state
-//   gdn_out_kernel       chunk-parallel: P and O = O_inter + P δ
-//   gdn_state_bwd_kernel serial over chunks in reverse, per (head, 32 columns):
-//                        dζ = Tᵀ(Pᵀ dO + diag(e^{γ−G}) K dS') and the state
-//                        gradient entering each chunk
+//   gdn_wy_kernel        chunk-parallel: A, T, W, U and the row-scaled keys
+//                        Kd = diag(e^{γ−G}) K, Kb = diag(β e^G) K
+//   gdn_state_fwd_kernel serial over chunks, one CTA per (head, 16 state
+//                        columns), two products per chunk (δ = U − W S0,
+//                        S_C = e^γ S0 + Kdᵀ δ) with the next chunk's operands
+//                        streaming in by cp.async: δ, chunk-start states, final state
+//   gdn_out_kernel       chunk-parallel: P and O = diag(e^G) Q S0 + P δ
+//   gdn_bwd_pre_kernel   chunk-parallel: X1 = Pᵀ dO, X2 = Qᵀ diag(e^G) dO
+//   gdn_state_bwd_kernel serial over chunks in reverse, per (head, 16 columns):
+//                        dζ = Tᵀ(X1 + Kd dS'), dS0 = e^γ dS' + X2 − Kbᵀ dζ
 //   gdn_grads_state_kernel / gdn_grads_local_kernel  chunk-parallel: dq, dk,
 //                        dv, dβ, dg (terms through S0 / dS', then the C x C
 //                        terms, the reverse cumsum and the L2-norm VJP)
@@ -39,10 +41,8 @@ namespace {
 constexpr int C = 64;          // chunk length
 constexpr int D = 128;         // dk = dv
 constexpr int NT = 256;        // threads per CTA
-constexpr int SL = 32;         // state columns per CTA in the serial kernels
 constexpr int LD = D + 1;      // padded leading dimensions (odd: conflict-free column walks)
 constexpr int LC = C + 1;
-constexpr int LS = SL + 1;
 constexpr float kNormEps = 1e-6f;
 
 typedef __nv_bfloat16 bf16;
@@ -166,7 +166,8 @@ struct WySmem {
 __global__ void __launch_bounds__(NT) gdn_wy_kernel(const bf16* __restrict__ k, const bf16* __restrict__ v,
                                                     const float* __restrict__ g, const float* __restrict__ beta,
                                                     float* __restrict__ w_out, float* __restrict__ u_out,
-                                                    float* __restrict__ t_out, int Tn, int H) {
+                                                    float* __restrict__ t_out, float* __restrict__ kd_out,
+                                                    float* __restrict__ kb_out, int Tn, int H) {
   extern __shared__ float smem_f[];
   WySmem& sm = *reinterpret_cast<WySmem*>(smem_f);
   const int ch = blockIdx.x, h = blockIdx.y;
@@ -200,11 +201,21 @@ __global__ void __launch_bounds__(NT) gdn_wy_kernel(const bf16* __restrict__ k, 
       sm.T[i * LC + c] = x;
     }
   }
-  // row scales: K rows by β e^G, V rows by β
-  for (int i = threadIdx.x; i < C * D; i += NT) {
-    const int r = i / D, c = i % D;
-    sm.K[r * LD + c] *= sm.s.b[r] * sm.s.eG[r];
-    sm.V[r * LD + c] *= sm.s.b[r];
+  // row scales: K rows by β e^G (kept: the state-gradient pass reads them), V rows by β; K rows by
+  // e^{γ−G} go out for the state update
+  {
+    const float gam = sm.s.G[n - 1];
+    for (int i = threadIdx.x; i < C * D; i += NT) {
+      const int r = i / D, c = i % D;
+      const float x = sm.K[r * LD + c];
+      if (r < n) {
+        const size_t o = ((size_t)(t0 + r) * H + h) * D + c;
+        kd_out[o] = x * __expf(gam - sm.s.G[r]);
+        kb_out[o] = x * sm.s.b[r] * sm.s.eG[r];
+      }
+      sm.K[r * LD + c] = x * sm.s.b[r] * sm.s.eG[r];
+      sm.V[r * LD + c] *= sm.s.b[r];
+    }
   }
   __syncthreads();
   using Tw = Tile<C, D, 4, 8>;
@@ -236,93 +247,128 @@ __global__ void __launch_bounds__(NT) gdn_wy_kernel(const bf16* __restrict__ k, 
   for (int i = threadIdx.x; i < C * C; i += NT) tt[i] = sm.T[(i / C) * LC + (i % C)];
 }
 
+// ------------------------------------------------------------------ asynchronous row copies
+TS_DEVICE void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+TS_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+TS_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+// rows [0, C) (zero-filled from n) of W floats per row, from src + row·row_stride + c0, into dst[C][ld]
+template <int W>
+TS_DEVICE void prefetch_rows(float* dst, int ld, const float* __restrict__ src, size_t row_stride, int n, int c0) {
+  constexpr int V = W / 4;  // 16-byte pieces per row
+  for (int i = threadIdx.x; i < C * V; i += NT) {
+    const int r = i / V, c = (i % V) * 4;
+    cp_async16(dst + r * ld + c, src + (size_t)(r < n ? r : 0) * row_stride + c0 + c, r < n);
+  }
+}
+
 // ------------------------------------------------------------------ forward 2: the serial state pass
+// One CTA per (head, 16 state columns); per chunk only two products sit on the chain:
+//   δ = U − W S,  S ← e^γ S + Kdᵀ δ   (Kd = diag(e^{γ−G}) K from gdn_wy_kernel)
+// The next chunk's W, Kd and U slice stream into the other shared-memory buffer while this chunk computes.
+constexpr int SF = 16;         // state columns per CTA
+constexpr int LW = D + 4;      // 16-byte aligned rows for the asynchronous copies
+constexpr int LU = SF + 4;
 struct StateFwdSmem {
-  float S[D * LS];   // state slice [128][32]
-  float M[C * LD];   // W chunk, then K chunk
-  float Q[C * LD];
-  float Dl[C * LS];  // δ slice
-  ChunkScalars s;
+  float S[D * (SF + 1)];
+  float W[2][C * LW];
+  float K[2][C * LW];
+  float U[2][C * LU];   // U slice, then δ
+  float G[C];
 };
 
-__global__ void __launch_bounds__(NT) gdn_state_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                           const float* __restrict__ g,
-                                                           const float* __restrict__ beta,
+__global__ void __launch_bounds__(NT) gdn_state_fwd_kernel(const float* __restrict__ g,
                                                            const float* __restrict__ w, const float* __restrict__ u,
+                                                           const float* __restrict__ kd,
                                                            const float* __restrict__ s_in, float* __restrict__ s_out,
                                                            float* __restrict__ starts, float* __restrict__ delta,
-                                                           float* __restrict__ o_inter, int Tn, int H) {
-  extern __shared__ float smem_f[];
+                                                           int Tn, int H) {
+  extern __shared__ __align__(16) float smem_f[];
   StateFwdSmem& sm = *reinterpret_cast<StateFwdSmem*>(smem_f);
-  const int h = blockIdx.x, j0 = blockIdx.y * SL;
+  constexpr int LSF = SF + 1;
+  const int h = blockIdx.x, j0 = blockIdx.y * SF;
   const int nch = (Tn + C - 1) / C;
-  const float qscale = rsqrtf((float)D);
-  for (int i = threadIdx.x; i < D * SL; i += NT) sm.S[(i / SL) * LS + i % SL] = s_in[((size_t)h * D + i / SL) * D + j0 + i % SL];
-  __syncthreads();
+  const size_t rs = (size_t)H * D;
+  for (int i = threadIdx.x; i < D * SF; i += NT) sm.S[(i / SF) * LSF + i % SF] = s_in[((size_t)h * D + i / SF) * D + j0 + i % SF];
+  auto issue = [&](int ch) {
+    const int t0 = ch * C, n = min(C, Tn - t0), b = ch & 1;
+    const size_t base = (size_t)t0 * rs + (size_t)h * D;
+    prefetch_rows<D>(sm.W[b], LW, w + base, rs, n, 0);
+    prefetch_rows<D>(sm.K[b], LW, kd + base, rs, n, 0);
+    prefetch_rows<SF>(sm.U[b], LU, u + base, rs, n, j0);
+    cp_async_commit();
+  };
+  issue(0);
   for (int ch = 0; ch < nch; ++ch) {
-    const int t0 = ch * C, n = min(C, Tn - t0);
+    const int t0 = ch * C, n = min(C, Tn - t0), b = ch & 1;
+    if (ch + 1 < nch) {
+      issue(ch + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     float* st = starts + ((size_t)ch * H + h) * D * D;
-    for (int i = threadIdx.x; i < D * SL; i += NT) st[(i / SL) * D + j0 + i % SL] = sm.S[(i / SL) * LS + i % SL];
-    load_f32<D>(sm.M, LD, w, t0, n, H, h, 0);
-    load_f32<SL>(sm.Dl, LS, u, t0, n, H, h, j0);
-    load_rows(sm.Q, q, t0, n, H, h, true, qscale);
-    load_scalars(sm.s, g, beta, t0, n, H, h);
+    for (int i = threadIdx.x; i < D * SF; i += NT) st[(i / SF) * D + j0 + i % SF] = sm.S[(i / SF) * LSF + i % SF];
+    if (threadIdx.x < 32) {  // in-chunk cumsum of g (γ = G at the last valid row)
+      const int lane = threadIdx.x;
+      float g0 = lane < n ? g[(size_t)(t0 + lane) * H + h] : 0.f;
+      float g1 = lane + 32 < n ? g[(size_t)(t0 + lane + 32) * H + h] : 0.f;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float a0 = __shfl_up_sync(0xffffffffu, g0, o), a1 = __shfl_up_sync(0xffffffffu, g1, o);
+        if (lane >= o) g0 += a0, g1 += a1;
+      }
+      g1 += __shfl_sync(0xffffffffu, g0, 31);
+      sm.G[lane] = g0;
+      sm.G[lane + 32] = g1;
+    }
     __syncthreads();
-    using Td = Tile<C, SL, 2, 4>;
-    {  // δ = U − W S ; O_inter = diag(e^G) Q S
-      float acc[2][4], aq[2][4];
+    using Td = Tile<C, SF, 2, 2>;
+    {  // δ = U − W S
+      float acc[2][2];
       zero(acc);
-      zero(aq);
-      mm_acc<C, SL, 2, 4, false, false>(acc, sm.M, LD, sm.S, LS, D);
-      mm_acc<C, SL, 2, 4, false, false>(aq, sm.Q, LD, sm.S, LS, D);
-      __syncthreads();  // every read of W and S for this chunk is done
+      mm_acc<C, SF, 2, 2, false, false>(acc, sm.W[b], LW, sm.S, LSF, D);
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const int i = Td::row(r);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           const int j = Td::col(c);
-          const float d = i < n ? sm.Dl[i * LS + j] - acc[r][c] : 0.f;
-          sm.Dl[i * LS + j] = d;
-          if (i < n) {
-            const size_t o = ((size_t)(t0 + i) * H + h) * D + j0 + j;
-            delta[o] = d;
-            o_inter[o] = sm.s.eG[i] * aq[r][c];
-          }
+          const float d = i < n ? sm.U[b][i * LU + j] - acc[r][c] : 0.f;
+          sm.U[b][i * LU + j] = d;
+          if (i < n) delta[((size_t)(t0 + i) * H + h) * D + j0 + j] = d;
         }
       }
     }
-    load_rows(sm.M, k, t0, n, H, h, true, 1.f);
     __syncthreads();
-    // δ rows scaled by e^{γ − G}
-    const float gam = sm.s.G[n - 1];
-    for (int i = threadIdx.x; i < C * SL; i += NT) {
-      const int r = i / SL;
-      sm.Dl[r * LS + i % SL] *= r < n ? __expf(gam - sm.s.G[r]) : 0.f;
-    }
-    __syncthreads();
-    {  // S = e^γ S + Kᵀ (e^{γ−G} δ)
-      using Ts = Tile<D, SL, 4, 4>;
-      float acc[4][4];
+    {  // S = e^γ S + Kdᵀ δ
+      using Ts = Tile<D, SF, 4, 2>;
+      float acc[4][2];
       zero(acc);
-      mm_acc<D, SL, 4, 4, true, false>(acc, sm.M, LD, sm.Dl, LS, C);
-      const float eg = __expf(gam);
-      __syncthreads();
+      mm_acc<D, SF, 4, 2, true, false>(acc, sm.K[b], LW, sm.U[b], LU, C);
+      const float eg = __expf(sm.G[n - 1]);
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float& x = sm.S[Ts::row(r) * LS + Ts::col(c)];
-          x = fmaf(eg, x, acc[r][c]);
+        for (int c = 0; c < 2; ++c) {
+          float& x = sm.S[Ts::row(r) * LSF + Ts::col(c)];
+          x = fmaf(eg, x, acc[r][c]);  // each element is read and written by its own thread only
         }
     }
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < D * SL; i += NT) s_out[((size_t)h * D + i / SL) * D + j0 + i % SL] = sm.S[(i / SL) * LS + i % SL];
+  for (int i = threadIdx.x; i < D * SF; i += NT) s_out[((size_t)h * D + i / SF) * D + j0 + i % SF] = sm.S[(i / SF) * LSF + i % SF];
 }
 
-// ------------------------------------------------------------------ forward 3: intra-chunk output
+// ------------------------------------------------------------------ forward 3: outputs (chunk-parallel)
+// O = diag(e^G) Q S0 + P δ with S0 the chunk-start state; P is also kept for the backward.
 struct OutSmem {
+  float S[D * LD];
   float Q[C * LD];
   float K[C * LD];   // K, then δ
   float P[C * LC];
@@ -331,13 +377,14 @@ struct OutSmem {
 
 __global__ void __launch_bounds__(NT) gdn_out_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                      const float* __restrict__ g, const float* __restrict__ beta,
-                                                     const float* __restrict__ delta,
-                                                     const float* __restrict__ o_inter, bf16* __restrict__ o,
-                                                     float* __restrict__ p_out, int Tn, int H) {
+                                                     const float* __restrict__ delta, const float* __restrict__ starts,
+                                                     bf16* __restrict__ o, float* __restrict__ p_out, int Tn, int H) {
   extern __shared__ float smem_f[];
   OutSmem& sm = *reinterpret_cast<OutSmem*>(smem_f);
   const int ch = blockIdx.x, h = blockIdx.y;
   const int t0 = ch * C, n = min(C, Tn - t0);
+  const float* S0 = starts + ((size_t)ch * H + h) * D * D;
+  for (int i = threadIdx.x; i < D * D; i += NT) sm.S[(i / D) * LD + i % D] = S0[i];
   load_rows(sm.Q, q, t0, n, H, h, true, rsqrtf((float)D));
   load_rows(sm.K, k, t0, n, H, h, true, 1.f);
   load_scalars(sm.s, g, beta, t0, n, H, h);
@@ -358,124 +405,196 @@ __global__ void __launch_bounds__(NT) gdn_out_kernel(const bf16* __restrict__ q,
         pp[i * C + j] = x;
       }
   }
-  __syncthreads();
-  load_f32<D>(sm.K, LD, delta, t0, n, H, h, 0);
-  __syncthreads();
   using Tw = Tile<C, D, 4, 8>;
   float acc[4][8];
   zero(acc);
-  mm_acc<C, D, 4, 8, false, false>(acc, sm.P, LC, sm.K, LD, C);
+  mm_acc<C, D, 4, 8, false, false>(acc, sm.Q, LD, sm.S, LD, D);   // Q S0
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[r][c] *= sm.s.eG[Tw::row(r)];
+  __syncthreads();
+  load_f32<D>(sm.K, LD, delta, t0, n, H, h, 0);
+  __syncthreads();
+  mm_acc<C, D, 4, 8, false, false>(acc, sm.P, LC, sm.K, LD, C);   // + P δ
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int i = Tw::row(r);
     if (i < n)
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const size_t x = ((size_t)(t0 + i) * H + h) * D + Tw::col(c);
-        o[x] = __float2bfloat16_rn(o_inter[x] + acc[r][c]);
-      }
+      for (int c = 0; c < 8; ++c) o[((size_t)(t0 + i) * H + h) * D + Tw::col(c)] = __float2bfloat16_rn(acc[r][c]);
   }
 }
 
-// ------------------------------------------------------------------ backward 1: the serial state-gradient pass
-struct StateBwdSmem {
-  float dS[D * LS];
-  float K[C * LD];
+// ------------------------------------------------------------------ backward 0: chain-free terms (chunk-parallel)
+// X1 = Pᵀ dO  [C, D]  and  X2 = Qᵀ diag(e^G) dO  [D, D] per chunk: the parts of the state-gradient
+// recursion that do not depend on the state gradient.
+struct BwdPreSmem {
   float Q[C * LD];
-  float P[C * LC];   // P, then T
-  float dO[C * LS];
-  float dd[C * LS];
+  float X[C * LD];   // dO
+  float P[C * LC];
   ChunkScalars s;
 };
 
-__global__ void __launch_bounds__(NT) gdn_state_bwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                           const float* __restrict__ g,
-                                                           const float* __restrict__ beta,
-                                                           const bf16* __restrict__ dout,
-                                                           const float* __restrict__ p_sv, const float* __restrict__ t_sv,
+__global__ void __launch_bounds__(NT) gdn_bwd_pre_kernel(const bf16* __restrict__ q, const float* __restrict__ g,
+                                                         const float* __restrict__ beta,
+                                                         const bf16* __restrict__ dout, const float* __restrict__ p_sv,
+                                                         float* __restrict__ x1, float* __restrict__ x2, int Tn,
+                                                         int H) {
+  extern __shared__ float smem_f[];
+  BwdPreSmem& sm = *reinterpret_cast<BwdPreSmem*>(smem_f);
+  const int ch = blockIdx.x, h = blockIdx.y;
+  const int t0 = ch * C, n = min(C, Tn - t0);
+  load_rows(sm.Q, q, t0, n, H, h, true, rsqrtf((float)D));
+  load_bf16<D>(sm.X, LD, dout, t0, n, H, h, 0);
+  load_scalars(sm.s, g, beta, t0, n, H, h);
+  {
+    const float* pp = p_sv + ((size_t)ch * H + h) * C * C;
+    for (int i = threadIdx.x; i < C * C; i += NT) sm.P[(i / C) * LC + i % C] = pp[i];
+  }
+  __syncthreads();
+  {
+    using Tw = Tile<C, D, 4, 8>;
+    float acc[4][8];
+    zero(acc);
+    mm_acc<C, D, 4, 8, true, false>(acc, sm.P, LC, sm.X, LD, C);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = Tw::row(r);
+      if (i < n)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) x1[((size_t)(t0 + i) * H + h) * D + Tw::col(c)] = acc[r][c];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < C * D; i += NT) sm.X[(i / D) * LD + i % D] *= sm.s.eG[i / D];
+  __syncthreads();
+  using Tq = Tile<D, D, 8, 8>;
+  float acc[8][8];
+  zero(acc);
+  mm_acc<D, D, 8, 8, true, false>(acc, sm.Q, LD, sm.X, LD, C);
+  float* xx = x2 + ((size_t)ch * H + h) * D * D;
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) xx[Tq::row(r) * D + Tq::col(c)] = acc[r][c];
+}
+
+// ------------------------------------------------------------------ backward 1: the serial state-gradient pass
+// One CTA per (head, 16 columns), chunks in reverse; per chunk:
+//   dd = X1 + Kd dS',  dζ = Tᵀ dd,  dS ← e^γ dS' + X2 − Kbᵀ dζ
+// (Kd = diag(e^{γ−G}) K, Kb = diag(β e^G) K), with the next chunk's operands streaming in meanwhile.
+constexpr int LT = C + 4;
+struct StateBwdSmem {
+  float dS[D * (SF + 1)];
+  float Kd[2][C * LW];
+  float Kb[2][C * LW];
+  float T[2][C * LT];
+  float X1[2][C * LU];   // X1 slice, then dd
+  float X2[2][D * LU];
+  float dz[C * (SF + 1)];
+  float G[C];
+};
+
+__global__ void __launch_bounds__(NT) gdn_state_bwd_kernel(const float* __restrict__ g,
+                                                           const float* __restrict__ kd, const float* __restrict__ kb,
+                                                           const float* __restrict__ t_sv,
+                                                           const float* __restrict__ x1, const float* __restrict__ x2,
                                                            const float* __restrict__ dfinal,
                                                            float* __restrict__ ds_sv, float* __restrict__ dz_out,
                                                            float* __restrict__ dstate, int Tn, int H) {
-  extern __shared__ float smem_f[];
+  extern __shared__ __align__(16) float smem_f[];
   StateBwdSmem& sm = *reinterpret_cast<StateBwdSmem*>(smem_f);
-  const int h = blockIdx.x, j0 = blockIdx.y * SL;
+  constexpr int LSF = SF + 1;
+  const int h = blockIdx.x, j0 = blockIdx.y * SF;
   const int nch = (Tn + C - 1) / C;
-  const float qscale = rsqrtf((float)D);
-  for (int i = threadIdx.x; i < D * SL; i += NT) sm.dS[(i / SL) * LS + i % SL] = dfinal[((size_t)h * D + i / SL) * D + j0 + i % SL];
-  __syncthreads();
+  const size_t rs = (size_t)H * D;
+  for (int i = threadIdx.x; i < D * SF; i += NT) sm.dS[(i / SF) * LSF + i % SF] = dfinal[((size_t)h * D + i / SF) * D + j0 + i % SF];
+  auto issue = [&](int ch) {
+    const int t0 = ch * C, n = min(C, Tn - t0), b = ch & 1;
+    const size_t base = (size_t)t0 * rs + (size_t)h * D;
+    prefetch_rows<D>(sm.Kd[b], LW, kd + base, rs, n, 0);
+    prefetch_rows<D>(sm.Kb[b], LW, kb + base, rs, n, 0);
+    prefetch_rows<C>(sm.T[b], LT, t_sv + ((size_t)ch * H + h) * C * C, C, C, 0);
+    prefetch_rows<SF>(sm.X1[b], LU, x1 + base, rs, n, j0);
+    // X2 rows are the D state rows: two C-row halves
+    const float* xx = x2 + ((size_t)ch * H + h) * D * D;
+    prefetch_rows<SF>(sm.X2[b], LU, xx, D, C, j0);
+    prefetch_rows<SF>(sm.X2[b] + C * LU, LU, xx + (size_t)C * D, D, C, j0);
+    cp_async_commit();
+  };
+  issue(nch - 1);
   for (int ch = nch - 1; ch >= 0; --ch) {
-    const int t0 = ch * C, n = min(C, Tn - t0);
+    const int t0 = ch * C, n = min(C, Tn - t0), b = ch & 1;
+    if (ch > 0) {
+      issue(ch - 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     float* dsv = ds_sv + ((size_t)ch * H + h) * D * D;
-    for (int i = threadIdx.x; i < D * SL; i += NT) dsv[(i / SL) * D + j0 + i % SL] = sm.dS[(i / SL) * LS + i % SL];
-    load_rows(sm.K, k, t0, n, H, h, true, 1.f);
-    load_rows(sm.Q, q, t0, n, H, h, true, qscale);
-    load_bf16<SL>(sm.dO, LS, dout, t0, n, H, h, j0);
-    load_scalars(sm.s, g, beta, t0, n, H, h);
-    {
-      const float* pp = p_sv + ((size_t)ch * H + h) * C * C;
-      for (int i = threadIdx.x; i < C * C; i += NT) sm.P[(i / C) * LC + i % C] = pp[i];
-    }
-    __syncthreads();
-    const float gam = sm.s.G[n - 1];
-    using Td = Tile<C, SL, 2, 4>;
-    {  // dd = Pᵀ dO + diag(e^{γ−G}) K dS'
-      float a1[2][4], a2[2][4];
-      zero(a1);
-      zero(a2);
-      mm_acc<C, SL, 2, 4, true, false>(a1, sm.P, LC, sm.dO, LS, C);
-      mm_acc<C, SL, 2, 4, false, false>(a2, sm.K, LD, sm.dS, LS, D);
+    for (int i = threadIdx.x; i < D * SF; i += NT) dsv[(i / SF) * D + j0 + i % SF] = sm.dS[(i / SF) * LSF + i % SF];
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      float g0 = lane < n ? g[(size_t)(t0 + lane) * H + h] : 0.f;
+      float g1 = lane + 32 < n ? g[(size_t)(t0 + lane + 32) * H + h] : 0.f;
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int i = Td::row(r);
-        const float e = i < n ? __expf(gam - sm.s.G[i]) : 0.f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) sm.dd[i * LS + Td::col(c)] = i < n ? a1[r][c] + e * a2[r][c] : 0.f;
+      for (int o = 1; o < 32; o <<= 1) {
+        const float a0 = __shfl_up_sync(0xffffffffu, g0, o), a1 = __shfl_up_sync(0xffffffffu, g1, o);
+        if (lane >= o) g0 += a0, g1 += a1;
       }
+      g1 += __shfl_sync(0xffffffffu, g0, 31);
+      sm.G[lane] = g0;
+      sm.G[lane + 32] = g1;
     }
     __syncthreads();
-    {
-      const float* tt = t_sv + ((size_t)ch * H + h) * C * C;
-      for (int i = threadIdx.x; i < C * C; i += NT) sm.P[(i / C) * LC + i % C] = tt[i];
-    }
-    __syncthreads();
-    {  // dζ = Tᵀ dd, stored; then rows scaled by e^G β for the state term
-      float a[2][4];
-      zero(a);
-      mm_acc<C, SL, 2, 4, true, false>(a, sm.P, LC, sm.dd, LS, C);
-      __syncthreads();
+    using Td = Tile<C, SF, 2, 2>;
+    {  // dd = X1 + Kd dS'
+      float acc[2][2];
+      zero(acc);
+      mm_acc<C, SF, 2, 2, false, false>(acc, sm.Kd[b], LW, sm.dS, LSF, D);
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int i = Td::row(r);
+      for (int r = 0; r < 2; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int j = Td::col(c);
-          if (i < n) dz_out[((size_t)(t0 + i) * H + h) * D + j0 + j] = a[r][c];
-          sm.dd[i * LS + j] = i < n ? a[r][c] * sm.s.eG[i] * sm.s.b[i] : 0.f;
-          sm.dO[i * LS + j] *= i < n ? sm.s.eG[i] : 0.f;
+        for (int c = 0; c < 2; ++c) {
+          const int i = Td::row(r), j = Td::col(c);
+          sm.X1[b][i * LU + j] = i < n ? sm.X1[b][i * LU + j] + acc[r][c] : 0.f;
         }
-      }
     }
     __syncthreads();
-    {  // dS = e^γ dS' + Qᵀ diag(e^G) dO − Kᵀ diag(e^G β) dζ
-      using Ts = Tile<D, SL, 4, 4>;
-      float a[4][4], b[4][4];
-      zero(a);
-      zero(b);
-      mm_acc<D, SL, 4, 4, true, false>(a, sm.Q, LD, sm.dO, LS, C);
-      mm_acc<D, SL, 4, 4, true, false>(b, sm.K, LD, sm.dd, LS, C);
-      const float eg = __expf(gam);
-      __syncthreads();
+    {  // dζ = Tᵀ dd
+      float acc[2][2];
+      zero(acc);
+      mm_acc<C, SF, 2, 2, true, false>(acc, sm.T[b], LT, sm.X1[b], LU, C);
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int i = Td::row(r), j = Td::col(c);
+          const float z = i < n ? acc[r][c] : 0.f;
+          sm.dz[i * LSF + j] = z;
+          if (i < n) dz_out[((size_t)(t0 + i) * H + h) * D + j0 + j] = z;
+        }
+    }
+    __syncthreads();
+    {  // dS = e^γ dS' + X2 − Kbᵀ dζ
+      using Ts = Tile<D, SF, 4, 2>;
+      float acc[4][2];
+      zero(acc);
+      mm_acc<D, SF, 4, 2, true, false>(acc, sm.Kb[b], LW, sm.dz, LSF, C);
+      const float eg = __expf(sm.G[n - 1]);
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float& x = sm.dS[Ts::row(r) * LS + Ts::col(c)];
-          x = eg * x + a[r][c] - b[r][c];
+        for (int c = 0; c < 2; ++c) {
+          const int i = Ts::row(r), j = Ts::col(c);
+          float& x = sm.dS[i * LSF + j];
+          x = eg * x + sm.X2[b][i * LU + j] - acc[r][c];
         }
     }
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < D * SL; i += NT) dstate[((size_t)h * D + i / SL) * D + j0 + i % SL] = sm.dS[(i / SL) * LS + i % SL];
+  for (int i = threadIdx.x; i < D * SF; i += NT) dstate[((size_t)h * D + i / SF) * D + j0 + i % SF] = sm.dS[(i / SF) * LSF + i % SF];
 }
 
 // ------------------------------------------------------------------ backward 2: terms through S0 and dS'
@@ -823,7 +942,7 @@ void set_smem(K kernel, size_t bytes) {
 }  // namespace
 
 // q, k, v [T, H, 128] bf16; g, beta [T, H] fp32; state [H, 128, 128] fp32.
-// Returns (o, final_state, saved...) where saved = (starts, delta, T factors, P).
+// Returns (o, final_state, saved...) with saved = (chunk-start states, δ, T factors, P, Kd, Kb).
 std::vector<at::Tensor> gdn_chunk_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                       const at::Tensor& g, const at::Tensor& beta, const at::Tensor& state) {
   check_cuda(q, "q");
@@ -845,38 +964,40 @@ std::vector<at::Tensor> gdn_chunk_fwd(const at::Tensor& q, const at::Tensor& k, 
   auto delta = at::empty({Tn, H, D}, f32);
   auto tsv = at::empty({std::max(nch, 1), H, C, C}, f32);
   auto psv = at::empty({std::max(nch, 1), H, C, C}, f32);
+  auto kd = at::empty({Tn, H, D}, f32);
+  auto kb = at::empty({Tn, H, D}, f32);
   if (Tn == 0) {
     fin.copy_(state);
-    return {o, fin, starts, delta, tsv, psv};
+    return {o, fin, starts, delta, tsv, psv, kd, kb};
   }
   auto w = at::empty({Tn, H, D}, f32);
   auto u = at::empty({Tn, H, D}, f32);
-  auto oint = at::empty({Tn, H, D}, f32);
   const bf16* qp = (const bf16*)q.data_ptr();
   const bf16* kp = (const bf16*)k.data_ptr();
   const bf16* vp = (const bf16*)v.data_ptr();
   set_smem(gdn_wy_kernel, sizeof(WySmem));
   gdn_wy_kernel<<<dim3(nch, H), NT, sizeof(WySmem), stream()>>>(kp, vp, g.data_ptr<float>(), beta.data_ptr<float>(),
                                                                  w.data_ptr<float>(), u.data_ptr<float>(),
-                                                                 tsv.data_ptr<float>(), Tn, H);
+                                                                 tsv.data_ptr<float>(), kd.data_ptr<float>(),
+                                                                 kb.data_ptr<float>(), Tn, H);
   set_smem(gdn_state_fwd_kernel, sizeof(StateFwdSmem));
-  gdn_state_fwd_kernel<<<dim3(H, D / SL), NT, sizeof(StateFwdSmem), stream()>>>(
-      qp, kp, g.data_ptr<float>(), beta.data_ptr<float>(), w.data_ptr<float>(), u.data_ptr<float>(),
-      state.data_ptr<float>(), fin.data_ptr<float>(), starts.data_ptr<float>(), delta.data_ptr<float>(),
-      oint.data_ptr<float>(), Tn, H);
+  gdn_state_fwd_kernel<<<dim3(H, D / SF), NT, sizeof(StateFwdSmem), stream()>>>(
+      g.data_ptr<float>(), w.data_ptr<float>(), u.data_ptr<float>(), kd.data_ptr<float>(), state.data_ptr<float>(),
+      fin.data_ptr<float>(), starts.data_ptr<float>(), delta.data_ptr<float>(), Tn, H);
   set_smem(gdn_out_kernel, sizeof(OutSmem));
   gdn_out_kernel<<<dim3(nch, H), NT, sizeof(OutSmem), stream()>>>(qp, kp, g.data_ptr<float>(), beta.data_ptr<float>(),
-                                                                   delta.data_ptr<float>(), oint.data_ptr<float>(),
+                                                                   delta.data_ptr<float>(), starts.data_ptr<float>(),
                                                                    (bf16*)o.data_ptr(), psv.data_ptr<float>(), Tn, H);
   TS_LAUNCH_CHECK();
-  return {o, fin, starts, delta, tsv, psv};
+  return {o, fin, starts, delta, tsv, psv, kd, kb};
 }
 
 // Returns (dq, dk, dv, dg, dbeta, dstate).
 std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& dfinal, const at::Tensor& q,
                                       const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
                                       const at::Tensor& beta, const at::Tensor& starts, const at::Tensor& delta,
-                                      const at::Tensor& tsv, const at::Tensor& psv) {
+                                      const at::Tensor& tsv, const at::Tensor& psv, const at::Tensor& kd,
+                                      const at::Tensor& kb) {
   check_cuda(q, "q");
   TS_CHECK(dout.is_contiguous() && dfinal.is_contiguous() && dout.scalar_type() == at::kBFloat16 &&
                dfinal.scalar_type() == at::kFloat && dout.sizes() == q.sizes(),
@@ -896,6 +1017,8 @@ std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& 
     return {dq, dk, dv, dg, dbeta, dstate};
   }
   auto dssv = at::empty({nch, H, D, D}, f32);
+  auto x1 = at::empty({Tn, H, D}, f32);
+  auto x2 = at::empty({nch, H, D, D}, f32);
   auto dz = at::empty({Tn, H, D}, f32);
   auto dqh = at::empty({Tn, H, D}, f32);
   auto dkh = at::empty({Tn, H, D}, f32);
@@ -905,10 +1028,15 @@ std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& 
   const bf16* qp = (const bf16*)q.data_ptr();
   const bf16* kp = (const bf16*)k.data_ptr();
   const bf16* dop = (const bf16*)dout.data_ptr();
+  set_smem(gdn_bwd_pre_kernel, sizeof(BwdPreSmem));
+  gdn_bwd_pre_kernel<<<dim3(nch, H), NT, sizeof(BwdPreSmem), stream()>>>(
+      qp, g.data_ptr<float>(), beta.data_ptr<float>(), dop, psv.data_ptr<float>(), x1.data_ptr<float>(),
+      x2.data_ptr<float>(), Tn, H);
   set_smem(gdn_state_bwd_kernel, sizeof(StateBwdSmem));
-  gdn_state_bwd_kernel<<<dim3(H, D / SL), NT, sizeof(StateBwdSmem), stream()>>>(
-      qp, kp, g.data_ptr<float>(), beta.data_ptr<float>(), dop, psv.data_ptr<float>(), tsv.data_ptr<float>(),
-      dfinal.data_ptr<float>(), dssv.data_ptr<float>(), dz.data_ptr<float>(), dstate.data_ptr<float>(), Tn, H);
+  gdn_state_bwd_kernel<<<dim3(H, D / SF), NT, sizeof(StateBwdSmem), stream()>>>(
+      g.data_ptr<float>(), kd.data_ptr<float>(), kb.data_ptr<float>(), tsv.data_ptr<float>(), x1.data_ptr<float>(),
+      x2.data_ptr<float>(), dfinal.data_ptr<float>(), dssv.data_ptr<float>(), dz.data_ptr<float>(),
+      dstate.data_ptr<float>(), Tn, H);
   set_smem(gdn_grads_state_kernel, sizeof(GradStateSmem));
   gdn_grads_state_kernel<<<dim3(nch, H), NT, sizeof(GradStateSmem), stream()>>>(
       qp, kp, (const bf16*)v.data_ptr(), g.data_ptr<float>(), beta.data_ptr<float>(), dop, starts.data_ptr<float>(),

@@ -183,12 +183,18 @@ def bench_gdn(args) -> None:
     beta = torch.rand(t, h, device="cuda")
     s0 = torch.zeros(h, 128, 128, device="cuda")
     ext = native()
-    o, fin, saved = ext.gdn_fwd(q, k, v, gg, beta, s0)
-    ms = _time(lambda: ext.gdn_fwd(q, k, v, gg, beta, s0), args.iters)
-    print(f"gdn fwd T={t} H={h}: {ms:.3f} ms  {t / ms * 1e3:.0f} tokens/s")
+    o, fin, *saved = ext.gdn_chunk_fwd(q, k, v, gg, beta, s0)
+    ms = _time(lambda: ext.gdn_chunk_fwd(q, k, v, gg, beta, s0), args.iters)
+    print(f"gdn chunked fwd T={t} H={h}: {ms:.3f} ms  {t / ms * 1e3:.0f} tokens/s")
     do = torch.randn_like(o)
-    ms = _time(lambda: ext.gdn_bwd(do, torch.zeros_like(fin), q, k, v, gg, beta, saved), args.iters)
-    print(f"gdn bwd: {ms:.3f} ms")
+    dfin = torch.zeros_like(fin)
+    ms = _time(lambda: ext.gdn_chunk_bwd(do, dfin, q, k, v, gg, beta, *saved), args.iters)
+    print(f"gdn chunked bwd: {ms:.3f} ms")
+    o, fin, ck = ext.gdn_fwd(q, k, v, gg, beta, s0)
+    ms = _time(lambda: ext.gdn_fwd(q, k, v, gg, beta, s0), args.iters)
+    print(f"gdn token-recurrent fwd: {ms:.3f} ms")
+    ms = _time(lambda: ext.gdn_bwd(do, dfin, q, k, v, gg, beta, ck), args.iters)
+    print(f"gdn token-recurrent bwd: {ms:.3f} ms")
 
 
 def bench_conv(args) -> None:
