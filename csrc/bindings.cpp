@@ -74,6 +74,8 @@ std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& 
                                       const at::Tensor& tsv, const at::Tensor& psv, const at::Tensor& kd,
                                       const at::Tensor& kb);
 int64_t gemm_tc_pair(int64_t on);
+void gemm_tc_cat(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& a2,
+                 const c10::optional<at::Tensor>& b2, bool a_t, bool b_t, int64_t mode, double alpha);
 std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
                                       bool with_entropy);
 at::Tensor lmhead_dlogits_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt, const at::Tensor& lse,
@@ -141,6 +143,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tc", &ts::gemm_tc);
   m.def("lmhead_lse_tc", &ts::lmhead_lse_tc);
   m.def("gemm_tc_pair", &ts::gemm_tc_pair);
+  m.def("gemm_tc_cat", &ts::gemm_tc_cat);
   m.def("lmhead_dlogits_tc", &ts::lmhead_dlogits_tc);
   m.def("attn_trace_read", &ts::attn_trace_read);
   m.def("gdn_bwd", &ts::gdn_bwd);

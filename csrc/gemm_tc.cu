@@ -227,7 +227,10 @@ TS_DEVICE void epilogue_tile(uint32_t tacc, int row, int nb, int M, int N, int l
 
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
-                                                         const __grid_constant__ CUtensorMap tm_b, void* __restrict__ c,
+                                                         const __grid_constant__ CUtensorMap tm_b,
+                                                         const __grid_constant__ CUtensorMap tm_a2,
+                                                         const __grid_constant__ CUtensorMap tm_b2, int K2,
+                                                         void* __restrict__ c,
                                                          int M, int N, int K, int ldc, float alpha,
                                                          int* __restrict__ err, LmArgs lm) {
   extern __shared__ uint8_t smem_raw[];
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   GemmBars* bars = reinterpret_cast<GemmBars*>(smem + kBarOff);
   const uint32_t sbase = tc::smem_addr(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = (M + kBM - 1) / kBM, nt = (N + kBN - 1) / kBN, kt = (K + kBK - 1) / kBK;
+  const int mt = (M + kBM - 1) / kBM, nt = (N + kBN - 1) / kBN, kt1 = (K + kBK - 1) / kBK, kt = kt1 + (K2 + kBK - 1) / kBK;
   const int tiles = mt * nt;
   volatile int* abort = &bars->abort;
 
@@ -260,6 +263,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     if (lane == 0) {
       tc::prefetch_tmap(&tm_a);
       tc::prefetch_tmap(&tm_b);
+      if (K2 > 0) {
+        tc::prefetch_tmap(&tm_a2);
+        tc::prefetch_tmap(&tm_b2);
+      }
       int it = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
         int mb, nb;
@@ -271,19 +278,24 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           tc::mbar_expect_tx(&bars->full[s], kStageBytes);
           uint8_t* a = smem + s * kStageBytes;
           uint8_t* b = a + kABytes;
+          // K blocks past the first source's come from the second (A2, B2): out = A·B + A2·B2
+          const bool second = kb >= kt1;
+          const CUtensorMap* pa = second ? &tm_a2 : &tm_a;
+          const CUtensorMap* pb = second ? &tm_b2 : &tm_b;
+          const int kx = (second ? kb - kt1 : kb) * kBK;
           if constexpr (!A_MN) {
-            tc::tma_load_2d(a, &tm_a, kb * kBK, mb * kBM, &bars->full[s]);  // box 64 (k) x 128 (m)
+            tc::tma_load_2d(a, pa, kx, mb * kBM, &bars->full[s]);  // box 64 (k) x 128 (m)
           } else {
             // [K][M]: two boxes of 64 m-columns x 64 k-rows
-            tc::tma_load_2d(a, &tm_a, mb * kBM, kb * kBK, &bars->full[s]);
-            tc::tma_load_2d(a + 64 * 128, &tm_a, mb * kBM + 64, kb * kBK, &bars->full[s]);
+            tc::tma_load_2d(a, pa, mb * kBM, kx, &bars->full[s]);
+            tc::tma_load_2d(a + 64 * 128, pa, mb * kBM + 64, kx, &bars->full[s]);
           }
           if constexpr (!B_MN) {
-            tc::tma_load_2d(b, &tm_b, kb * kBK, nb * kBN, &bars->full[s]);  // box 64 (k) x 256 (n)
+            tc::tma_load_2d(b, pb, kx, nb * kBN, &bars->full[s]);  // box 64 (k) x 256 (n)
           } else {
 #pragma unroll
             for (int j = 0; j < kBN / 64; ++j)  // [K][N]: four boxes of 64 n-columns x 64 k-rows
-              tc::tma_load_2d(b + j * 64 * 128, &tm_b, nb * kBN + j * 64, kb * kBK, &bars->full[s]);
+              tc::tma_load_2d(b + j * 64 * 128, pb, nb * kBN + j * 64, kx, &bars->full[s]);
           }
         }
       }
@@ -377,6 +389,7 @@ struct PairBars {
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ CUtensorMap tm_b2, int K2,
                      void* __restrict__ c, int M, int N, int K, int ldc, float alpha, int* __restrict__ err,
                      LmArgs lm) {
   extern __shared__ uint8_t smem_raw[];
@@ -385,7 +398,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   const uint32_t sbase = tc::smem_addr(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_rank();
-  const int mt = (M + 2 * kBM - 1) / (2 * kBM), nt = (N + kBN - 1) / kBN, kt = (K + kBK - 1) / kBK;
+  const int mt = (M + 2 * kBM - 1) / (2 * kBM), nt = (N + kBN - 1) / kBN, kt1 = (K + kBK - 1) / kBK, kt = kt1 + (K2 + kBK - 1) / kBK;
   const int tiles = mt * nt;
   const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
   volatile int* abort = &bars->abort;
@@ -413,6 +426,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     if (lane == 0) {
       tc::prefetch_tmap(&tm_a);
       tc::prefetch_tmap(&tm_b);
+      if (K2 > 0) {
+        tc::prefetch_tmap(&tm_a2);
+        tc::prefetch_tmap(&tm_b2);
+      }
       int it = 0;
       for (int t = cid; t < tiles; t += ncl) {
         int mb, nb;
@@ -427,17 +444,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           const uint32_t full0 = tc::map_cluster(tc::smem_addr(&bars->full[s]), 0);
           uint8_t* a = smem + s * kStagePBytes;
           uint8_t* b = a + kABytes;
+          const bool second = kb >= kt1;
+          const CUtensorMap* pa = second ? &tm_a2 : &tm_a;
+          const CUtensorMap* pb = second ? &tm_b2 : &tm_b;
+          const int kx = (second ? kb - kt1 : kb) * kBK;
           if constexpr (!A_MN) {
-            tc::tma_load_2d_pair(a, &tm_a, kb * kBK, arow, full0);  // box 64 (k) x 128 (m)
+            tc::tma_load_2d_pair(a, pa, kx, arow, full0);  // box 64 (k) x 128 (m)
           } else {
-            tc::tma_load_2d_pair(a, &tm_a, arow, kb * kBK, full0);  // [K][M]: 2 boxes of 64 m x 64 k
-            tc::tma_load_2d_pair(a + 64 * 128, &tm_a, arow + 64, kb * kBK, full0);
+            tc::tma_load_2d_pair(a, pa, arow, kx, full0);  // [K][M]: 2 boxes of 64 m x 64 k
+            tc::tma_load_2d_pair(a + 64 * 128, pa, arow + 64, kx, full0);
           }
           if constexpr (!B_MN) {
-            tc::tma_load_2d_pair(b, &tm_b, kb * kBK, bcol, full0);  // box 64 (k) x 128 (n)
+            tc::tma_load_2d_pair(b, pb, kx, bcol, full0);  // box 64 (k) x 128 (n)
           } else {
-            tc::tma_load_2d_pair(b, &tm_b, bcol, kb * kBK, full0);  // [K][N]: 2 boxes of 64 n x 64 k
-            tc::tma_load_2d_pair(b + 64 * 128, &tm_b, bcol + 64, kb * kBK, full0);
+            tc::tma_load_2d_pair(b, pb, bcol, kx, full0);  // [K][N]: 2 boxes of 64 n x 64 k
+            tc::tma_load_2d_pair(b + 64 * 128, pb, bcol + 64, kx, full0);
           }
         }
       }
@@ -511,7 +532,8 @@ int g_gemm_pair = 1;
 
 template <bool A_MN, bool B_MN, int EPI>
 void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int ldc, float alpha,
-                 int device, LmArgs lm) {
+                 int device, LmArgs lm, const CUtensorMap* ma2 = nullptr, const CUtensorMap* mb2 = nullptr,
+                 int K2 = 0) {
   const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
   const int smem = kSmemP + 1024;
   static int resident[16] = {0};  // co-resident CTA pairs per device (persistent grid size)
@@ -539,18 +561,21 @@ void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, i
   }
   const int clusters = std::max(1, std::min(tiles, pairs));
   gemm_pair_kernel<A_MN, B_MN, EPI><<<2 * clusters, 192, smem, stream()>>>(
-      ma, mb, c, M, N, K, ldc, alpha, tc_error_flag(at::Device(at::kCUDA, device)).data_ptr<int>(), lm);
+      ma, mb, ma2 ? *ma2 : ma, mb2 ? *mb2 : mb, ma2 ? K2 : 0, c, M, N, K, ldc, alpha,
+      tc_error_flag(at::Device(at::kCUDA, device)).data_ptr<int>(), lm);
 }
 
 template <bool A_MN, bool B_MN, int EPI>
 void launch(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int ldc, float alpha,
-            int device, LmArgs lm = LmArgs{}) {
+            int device, LmArgs lm = LmArgs{}, const CUtensorMap* ma2 = nullptr, const CUtensorMap* mb2 = nullptr,
+            int K2 = 0) {
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int grid = std::max(1, std::min(tiles, sm_count(device)));
   const int smem = kSmem + 1024;
   TS_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      smem));
-  gemm_tc_kernel<A_MN, B_MN, EPI><<<grid, 192, smem, stream()>>>(ma, mb, c, M, N, K, ldc, alpha,
+  gemm_tc_kernel<A_MN, B_MN, EPI><<<grid, 192, smem, stream()>>>(ma, mb, ma2 ? *ma2 : ma, mb2 ? *mb2 : mb,
+                                                                  ma2 ? K2 : 0, c, M, N, K, ldc, alpha,
                                                                   tc_error_flag(at::Device(at::kCUDA, device))
                                                                       .data_ptr<int>(),
                                                                   lm);
@@ -661,13 +686,18 @@ at::Tensor lmhead_dlogits_tc(const at::Tensor& h, const at::Tensor& w, const at:
 // b_t = true takes b as [N, K] (nn.Linear weight); b_t = false as [K, N].
 // mode 0: out bf16 [M, N] = alpha·a·b; mode 1: out fp32 = alpha·a·b;
 // mode 2: out fp32 += alpha·a·b.
-void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
-             double alpha) {
+// out (op)= alpha · (a · b [+ a2 · b2]): the optional second operand pair shares M and N (and the
+// transposition flags) and extends the contraction, its K blocks following the first pair's in the
+// same main loop (a LoRA projection is x·Wᵀ + (s·x·Aᵀ)·Bᵀ in one kernel). With a second pair the
+// first pair's K must be a multiple of 64.
+void gemm_tc_cat(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& a2,
+                 const c10::optional<at::Tensor>& b2, bool a_t, bool b_t, int64_t mode, double alpha) {
   check_cuda(a, "a");
   check_cuda(b, "b");
   check_cuda(out, "out");
   TS_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_tc takes bf16 operands");
   TS_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm_tc takes matrices");
+  TS_CHECK(a.is_contiguous() && b.is_contiguous(), "gemm_tc takes contiguous operands");
   const int M = a_t ? a.size(1) : a.size(0);
   const int K = a_t ? a.size(0) : a.size(1);
   const int N = b_t ? b.size(0) : b.size(1);
@@ -677,30 +707,54 @@ void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t
   // 16-byte TMA strides for every operand layout and 16-byte vector stores of C rows
   TS_CHECK(K % 8 == 0 && N % 8 == 0 && (!a_t || M % 8 == 0), "gemm_tc needs K, N (and M when a is [K, M]) "
            "to be multiples of 8");
+  const bool two = a2.has_value();
+  TS_CHECK(two == b2.has_value(), "gemm_tc: give both second operands or neither");
+  int K2 = 0;
+  if (two) {
+    TS_CHECK(a2->scalar_type() == at::kBFloat16 && b2->scalar_type() == at::kBFloat16 && a2->is_contiguous() &&
+                 b2->is_contiguous() && a2->dim() == 2 && b2->dim() == 2,
+             "gemm_tc: second operands must be contiguous bf16 matrices");
+    K2 = a_t ? a2->size(0) : a2->size(1);
+    TS_CHECK((a_t ? a2->size(1) : a2->size(0)) == M && (b_t ? b2->size(0) : b2->size(1)) == N &&
+                 (b_t ? b2->size(1) : b2->size(0)) == K2,
+             "gemm_tc: second operand pair shapes");
+    TS_CHECK(K % 64 == 0 && K2 % 8 == 0 && K2 > 0, "gemm_tc: with a second pair, K must be a multiple of 64");
+  }
   const c10::cuda::CUDAGuard guard(a.device());
   if (M == 0 || N == 0) return;
-  if (K == 0) {
+  if (K == 0 && K2 == 0) {
     if (mode != 2) out.zero_();
     return;
   }
   // tensor maps: inner dimension first; boxes of 64 inner elements
   const bool pair = g_gemm_pair != 0;
-  const CUtensorMap ma = a_t ? make_bf16_map(a.data_ptr(), M, K, M, 64) : make_bf16_map(a.data_ptr(), K, M, K, 128);
-  const CUtensorMap mb = b_t ? make_bf16_map(b.data_ptr(), K, N, K, pair ? 128 : 256)
-                             : make_bf16_map(b.data_ptr(), N, K, N, 64);
+  auto amap = [&](const at::Tensor& t, int k) {
+    return a_t ? make_bf16_map(t.data_ptr(), M, k, M, 64) : make_bf16_map(t.data_ptr(), k, M, k, 128);
+  };
+  auto bmap = [&](const at::Tensor& t, int k) {
+    return b_t ? make_bf16_map(t.data_ptr(), k, N, k, pair ? 128 : 256) : make_bf16_map(t.data_ptr(), N, k, N, 64);
+  };
+  const CUtensorMap ma = amap(a, K), mb = bmap(b, K);
+  CUtensorMap ma2 = ma, mb2 = mb;
+  if (two) {
+    ma2 = amap(*a2, K2);
+    mb2 = bmap(*b2, K2);
+  }
+  const CUtensorMap* pa2 = two ? &ma2 : nullptr;
+  const CUtensorMap* pb2 = two ? &mb2 : nullptr;
   const int dev = a.get_device();
   void* c = out.data_ptr();
   const float al = (float)alpha;
   const LmArgs none{};
 #define TS_GEMM_CASE(AM, BM)                                                                                  \
   if (pair) {                                                                                                 \
-    if (mode == 0) launch_pair<AM, BM, kStoreBf16>(ma, mb, c, M, N, K, (int)N, al, dev, none);               \
-    else if (mode == 1) launch_pair<AM, BM, kStoreF32>(ma, mb, c, M, N, K, (int)N, al, dev, none);           \
-    else launch_pair<AM, BM, kAccumF32>(ma, mb, c, M, N, K, (int)N, al, dev, none);                          \
+    if (mode == 0) launch_pair<AM, BM, kStoreBf16>(ma, mb, c, M, N, K, (int)N, al, dev, none, pa2, pb2, K2);  \
+    else if (mode == 1) launch_pair<AM, BM, kStoreF32>(ma, mb, c, M, N, K, (int)N, al, dev, none, pa2, pb2, K2); \
+    else launch_pair<AM, BM, kAccumF32>(ma, mb, c, M, N, K, (int)N, al, dev, none, pa2, pb2, K2);             \
   } else {                                                                                                    \
-    if (mode == 0) launch<AM, BM, kStoreBf16>(ma, mb, c, M, N, K, (int)N, al, dev);                          \
-    else if (mode == 1) launch<AM, BM, kStoreF32>(ma, mb, c, M, N, K, (int)N, al, dev);                      \
-    else launch<AM, BM, kAccumF32>(ma, mb, c, M, N, K, (int)N, al, dev);                                     \
+    if (mode == 0) launch<AM, BM, kStoreBf16>(ma, mb, c, M, N, K, (int)N, al, dev, none, pa2, pb2, K2);       \
+    else if (mode == 1) launch<AM, BM, kStoreF32>(ma, mb, c, M, N, K, (int)N, al, dev, none, pa2, pb2, K2);   \
+    else launch<AM, BM, kAccumF32>(ma, mb, c, M, N, K, (int)N, al, dev, none, pa2, pb2, K2);                  \
   }
   if (!a_t && b_t) {
     TS_GEMM_CASE(false, false)
@@ -713,6 +767,11 @@ void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t
   }
 #undef TS_GEMM_CASE
   TS_LAUNCH_CHECK();
+}
+
+void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
+             double alpha) {
+  gemm_tc_cat(out, a, b, c10::nullopt, c10::nullopt, a_t, b_t, mode, alpha);
 }
 
 }  // namespace ts

@@ -341,6 +341,29 @@ def test_gemm_tcgen05(m, n, k, a_t, b_t, pair):
         native().gemm_tc_pair(prev)
 
 
+@pytest.mark.parametrize("pair", [True, False])
+def test_gemm_tcgen05_two_sources(pair):
+    """out = a·b + a2·b2 in one main loop (second K range from a second operand pair)."""
+    from thundersync_b200.ops._ext import native
+
+    prev = native().gemm_tc_pair(1 if pair else 0)
+    try:
+        torch.manual_seed(5)
+        for m, n, k, k2, b_t in ((300, 384, 512, 16, True), (2304, 4096, 4096, 64, True), (1000, 512, 256, 64, False)):
+            a = torch.randn(m, k, device=DEV, dtype=torch.bfloat16)
+            a2 = torch.randn(m, k2, device=DEV, dtype=torch.bfloat16)
+            b = torch.randn((n, k) if b_t else (k, n), device=DEV, dtype=torch.bfloat16)
+            b2 = torch.randn((n, k2) if b_t else (k2, n), device=DEV, dtype=torch.bfloat16)
+            bf = b.float().t() if b_t else b.float()
+            b2f = b2.float().t() if b_t else b2.float()
+            ref = a.float() @ bf + a2.float() @ b2f
+            out = torch.empty(m, n, device=DEV)
+            native().gemm_tc_cat(out, a, b, a2, b2, False, b_t, 1, 1.0)
+            assert _rel(out, ref) < 1e-5, (m, n, k, k2, b_t)
+    finally:
+        native().gemm_tc_pair(prev)
+
+
 def _check_gemm(m, n, k, a_t, b_t):
     from thundersync_b200.ops.gemm import gemm, gemm_accumulate
 
@@ -358,3 +381,37 @@ def _check_gemm(m, n, k, a_t, b_t):
     from thundersync_b200.ops._ext import native
 
     assert int(native().tc_status(a).item()) == 0
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_lora_linear_cuda_bf16_matches_fp32(fused):
+    """The CUDA bf16 LoRA path (one two-source tcgen05 GEMM, or library GEMMs) against fp32 math."""
+    from thundersync_b200.ops import lora as L
+    from thundersync_b200.ops.lora import _LoRALinear
+
+    L.FUSED_TC = fused
+    try:
+        _check_lora()
+    finally:
+        L.FUSED_TC = True
+
+
+def _check_lora():
+    from thundersync_b200.ops.lora import _LoRALinear
+
+    torch.manual_seed(21)
+    t, din, dout, r, s = 300, 512, 384, 16, 2.0
+    x = torch.randn(t, din, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(dout, din, device=DEV) / din ** 0.5).to(torch.bfloat16)
+    a = (torch.randn(r, din, device=DEV) / din ** 0.5).requires_grad_(True)
+    b = (torch.randn(dout, r, device=DEV) / r ** 0.5).requires_grad_(True)
+    y = _LoRALinear.apply(x, w, a, b, s)
+    dy = torch.randn_like(y)
+    gx, ga, gb = torch.autograd.grad(y, (x, a, b), dy)
+    xr = x.detach().float().requires_grad_(True)
+    ar, br = a.detach().clone().requires_grad_(True), b.detach().clone().requires_grad_(True)
+    yr = xr @ w.float().t() + s * (xr @ ar.t()) @ br.t()
+    gxr, gar, gbr = torch.autograd.grad(yr, (xr, ar, br), dy.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(gx, gxr) < 1e-2 and _rel(ga, gar) < 1e-2 and _rel(gb, gbr) < 1e-2
+    assert ga.dtype == torch.float32 and gb.dtype == torch.float32

@@ -338,6 +338,45 @@ def bench_lmhead(args) -> None:
     L.FUSED_TC = True
 
 
+def bench_lora(args) -> None:
+    """LoRA projection (Qwen3-8B q_proj: 4096 -> 4096, rank 64) fwd and fwd+bwd: this package's unmerged op
+    vs the merged-weight form (one base GEMM forward, the reference's fused mode) and the bare base GEMM."""
+    from thundersync_b200.accel.fused_lora import FusedLoRALinear
+    from thundersync_b200.ops.lora import _LoRALinear
+
+    t, din, dout, r, s = args.rows, 4096, 4096, 64, 2.0
+    x = (torch.randn(t, din, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(dout, din, device="cuda") / din ** 0.5).to(torch.bfloat16)
+    a = (torch.randn(r, din, device="cuda") / din ** 0.5).requires_grad_(True)
+    b = (torch.randn(dout, r, device="cuda") * 0.01).requires_grad_(True)
+    dy = torch.randn(t, dout, device="cuda", dtype=torch.bfloat16)
+    flops = 2.0 * t * din * dout
+    from thundersync_b200.ops import lora as L
+
+    cases = (("unmerged, one tcgen05 GEMM", True, lambda: _LoRALinear.apply(x, w, a, b, s)),
+             ("unmerged, library GEMMs", False, lambda: _LoRALinear.apply(x, w, a, b, s)),
+             ("merged weight", True, lambda: FusedLoRALinear.apply(x, w, a, b, s)),
+             ("base GEMM alone", True, lambda: x @ w.t()))
+    for name, fused, fn in cases:
+        L.FUSED_TC = fused
+        with torch.no_grad():
+            f = _time(fn, args.iters)
+        fb = _time(lambda: torch.autograd.grad(fn(), (x, a, b), dy, allow_unused=True), args.iters)
+        print(f"lora {name:28s} T={t}: fwd {f:.3f} ms ({flops / f / 1e9:.0f} TFLOP/s of the base GEMM), "
+              f"fwd+bwd(dx, dA, dB) {fb:.3f} ms")
+    L.FUSED_TC = True
+    if args.trace:  # per-kernel device times of one unmerged forward+backward
+        from torch.profiler import ProfilerActivity, profile
+
+        fn = cases[0][2]
+        torch.autograd.grad(fn(), (x, a, b), dy)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            torch.autograd.grad(fn(), (x, a, b), dy)
+            torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=15, max_name_column_width=70))
+
+
 def bench_gemm_host(args) -> None:
     """Host (CPU) cost of one library GEMM call: repeated shape vs a new row count every call."""
     import time
@@ -366,7 +405,7 @@ def bench_gemm_host(args) -> None:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host", "swiglu", "rope", "dlogits",
-                                       "adamw", "fold", "gemm", "lmhead", "baselines"])
+                                       "adamw", "fold", "gemm", "lmhead", "baselines", "lora"])
     ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
     ap.add_argument("--t", type=int, default=2048)
     ap.add_argument("--s", type=int, default=2560)
@@ -382,7 +421,7 @@ def main(argv=None) -> None:
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
      "gemm_host": bench_gemm_host, "swiglu": bench_swiglu, "rope": bench_rope, "dlogits": bench_dlogits,
      "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm,
-     "lmhead": bench_lmhead, "baselines": bench_baselines}[args.family](args)
+     "lmhead": bench_lmhead, "baselines": bench_baselines, "lora": bench_lora}[args.family](args)
 
 
 if __name__ == "__main__":

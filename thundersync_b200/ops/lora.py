@@ -1,10 +1,12 @@
 """LoRA projection (K11′): ``y = x·Wᵀ + s·(x·Aᵀ)·Bᵀ`` without merging B·A into W.
 
 The frozen base weight W keeps its dtype (bf16); the adapters A [r, in] and
-B [out, r] are fp32 and so is the low-rank path, which is added to the bf16
-base product before the single rounding to the activation dtype — the
-numerics of an unmerged PEFT ``lora.Linear`` (reference:
-src/thundersync/policy_model.py:240-290 builds it through PEFT).
+B [out, r] are fp32 parameters. On CUDA with bf16 activations the rank-r
+products are bf16 tensor-core GEMMs with fp32 accumulation (the adapters are
+read as bf16, as a bf16 PEFT forward reads them) and the base product is the
+C operand of the second one, so the output is rounded once; elsewhere the
+low-rank path runs in fp32 — the numerics of an unmerged PEFT ``lora.Linear``
+(reference: src/thundersync/policy_model.py:240-290 builds it through PEFT).
 
 The reference's fused variant (src/thundersync/accel/fused_lora.py:26-50)
 merges B·A into W in place for one forward GEMM and must unmerge before every
@@ -12,7 +14,7 @@ optimizer step. This op needs neither: the rank-r products are two thin
 GEMMs beside the base GEMM, their fp32 weight gradients go straight into the
 active gradient sink (``dA += s·(dy·B)ᵀ·x``, ``dB += s·dyᵀ·(x·Aᵀ)``), and
 the frozen base never receives a gradient. Saved state is x plus the
-[T, r] fp32 projection ``x·Aᵀ``.
+[T, r] projection ``x·Aᵀ`` (fp32 on the CPU path; s·x·Aᵀ in bf16 on CUDA).
 """
 
 from __future__ import annotations
@@ -34,21 +36,70 @@ def lora_parts(mod: torch.nn.Module, adapter: str = "default"):
 
 
 def _deposit(param: torch.Tensor, lhs: torch.Tensor, rhs: torch.Tensor):
-    """``lhsᵀ·rhs`` into the active sink when it owns ``param``; else return it."""
+    """``lhsᵀ·rhs`` into the active sink when it owns ``param``; else return it (fp32-accumulated)."""
     s = _sink.active()
     if s is not None and s.owns(param):
         s.addmm_(s.view(param), lhs, rhs)
         return None
+    if lhs.is_cuda and lhs.dtype == torch.bfloat16:
+        return torch.mm(lhs.t(), rhs, out_dtype=torch.float32).to(param.dtype)
     return lhs.t().matmul(rhs).to(param.dtype)
+
+
+def _tc(x: torch.Tensor) -> bool:
+    """CUDA bf16 activations: the rank-r products run as bf16 tensor-core GEMMs with fp32 accumulation."""
+    return x.is_cuda and x.dtype == torch.bfloat16
+
+
+# CUDA: the base product and the rank-r update run as ONE tcgen05 GEMM whose main loop continues over a
+# second operand pair (y = x·Wᵀ + (s·u)·Bᵀ, dx = dy·W + (s·g)·A); False: library GEMMs
+FUSED_TC = True
+
+
+def _fused_ok(w: torch.Tensor, r: int) -> bool:
+    return FUSED_TC and w.shape[0] % 64 == 0 and w.shape[1] % 64 == 0 and r % 8 == 0 and w.is_contiguous()
+
+
+_BF16: dict[int, tuple] = {}
+
+
+def _bf16_scaled(p: torch.Tensor, scale: float, dtype: torch.dtype) -> torch.Tensor:
+    """``(scale · p)`` in the activation dtype, reused until ``p`` changes (its version counter moves at
+    every in-place update, i.e. at each optimizer step)."""
+    key = id(p)
+    hit = _BF16.get(key)
+    stamp = (p._version, p.data_ptr(), scale, dtype)
+    if hit is not None and hit[0] == stamp:
+        return hit[1]
+    with torch.no_grad():
+        t = (p.detach() * scale).to(dtype).contiguous() if scale != 1.0 else p.detach().to(dtype).contiguous()
+    if len(_BF16) > 4096:
+        _BF16.clear()
+    _BF16[key] = (stamp, t)
+    return t
 
 
 class _LoRALinear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, a, b, scale):
         x2 = x.reshape(-1, x.shape[-1])
-        base = F.linear(x2, w)
-        u = F.linear(x2.to(a.dtype), a)  # [T, r], adapter precision
-        y = torch.addmm(base.to(u.dtype), u, b.t(), alpha=scale).to(x.dtype)
+        if _tc(x2):
+            # u = s·x·Aᵀ (fp32 accumulation, bf16 result, saved for dB); with the fused GEMM the rank-r
+            # update is the main loop's last K block, otherwise the base product is the C operand of the
+            # rank-r GEMM: either way y is rounded once
+            u = torch.mm(x2, _bf16_scaled(a, scale, x2.dtype).t())
+            bb = _bf16_scaled(b, 1.0, x2.dtype)
+            if _fused_ok(w, a.shape[0]):
+                from thundersync_b200.ops._ext import native
+
+                y = x2.new_empty(x2.shape[0], w.shape[0])
+                native().gemm_tc_cat(y, x2.contiguous(), w, u, bb, False, True, 0, 1.0)
+            else:
+                y = torch.addmm(F.linear(x2, w), u, bb.t())
+        else:
+            base = F.linear(x2, w)
+            u = F.linear(x2.to(a.dtype), a)  # [T, r], adapter precision
+            y = torch.addmm(base.to(u.dtype), u, b.t(), alpha=scale).to(x.dtype)
         ctx.save_for_backward(x2, w, a, b, u)
         ctx.scale = scale
         ctx.in_shape = x.shape
@@ -59,15 +110,32 @@ class _LoRALinear(torch.autograd.Function):
         x2, w, a, b, u = ctx.saved_tensors
         s = ctx.scale
         dy2 = dy.reshape(-1, dy.shape[-1])
-        dyf = dy2.to(b.dtype)
-        g = dyf.matmul(b)  # [T, r]
         dx = da = db = dw = None
-        if ctx.needs_input_grad[0]:
-            dx = torch.addmm(dy2.matmul(w).to(g.dtype), g, a, alpha=s).to(x2.dtype).view(ctx.in_shape)
-        if ctx.needs_input_grad[2]:
-            da = _deposit(a, g * s, x2.to(a.dtype))
-        if ctx.needs_input_grad[3]:
-            db = _deposit(b, dyf, u * s)
+        if _tc(dy2):
+            ab = _bf16_scaled(a, 1.0, dy2.dtype)
+            gs = torch.mm(dy2, _bf16_scaled(b, s, dy2.dtype))  # s·dy·B [T, r]
+            if ctx.needs_input_grad[0]:
+                if _fused_ok(w, a.shape[0]):
+                    from thundersync_b200.ops._ext import native
+
+                    dx = dy2.new_empty(dy2.shape[0], w.shape[1])
+                    native().gemm_tc_cat(dx, dy2.contiguous(), w, gs, ab.contiguous(), False, False, 0, 1.0)
+                    dx = dx.view(ctx.in_shape)
+                else:
+                    dx = torch.addmm(dy2.matmul(w), gs, ab).view(ctx.in_shape)
+            if ctx.needs_input_grad[2]:
+                da = _deposit(a, gs, x2)
+            if ctx.needs_input_grad[3]:
+                db = _deposit(b, dy2, u)  # u already carries s
+        else:
+            dyf = dy2.to(b.dtype)
+            g = dyf.matmul(b)  # [T, r]
+            if ctx.needs_input_grad[0]:
+                dx = torch.addmm(dy2.matmul(w).to(g.dtype), g, a, alpha=s).to(x2.dtype).view(ctx.in_shape)
+            if ctx.needs_input_grad[2]:
+                da = _deposit(a, g * s, x2.to(a.dtype))
+            if ctx.needs_input_grad[3]:
+                db = _deposit(b, dyf, u * s)
         if ctx.needs_input_grad[1]:
             dw = dy2.t().matmul(x2).to(w.dtype)
         return dx, dw, da, db, None
