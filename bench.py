@@ -331,10 +331,13 @@ def main() -> None:
     end = torch.cuda.Event(enable_timing=True)
     wall0 = time.perf_counter()
     start.record()
+    issue_s = 0.0
     for s in range(args.warmup, args.warmup + args.steps):
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
+        h0 = time.perf_counter()
         st = run_step(trainer, works[s], t0)
+        issue_s += time.perf_counter() - h0  # host time to issue the step (before its result is read)
         t1.record()
         tails.append((t0, t1))
         scored_local += works[s]["scored"]
@@ -387,6 +390,7 @@ def main() -> None:
                 "d2h_bytes_per_step": 4 * world,
             },
             "gpu_launches": launches,
+            "host_issue_ms_per_step": round(issue_s * 1e3 / args.steps, 2),
         }
         if args.impl == "reference":
             out["impl"] = "reference"

@@ -494,7 +494,7 @@ void fwd_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, a
   const int T = q.size(0), Hq = q.size(1), S = k.size(0), Hkv = k.size(1);
   const int smem = (64 + 4 * 64) * D * 2;
   auto kern = attn_fwd_kernel<D>;
-  TS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  ensure_smem((const void*)kern, (int)(smem));
   dim3 grid((T + 63) / 64, Hq);
   kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(),
                                       (const bf16*)v.data_ptr(), (bf16*)o.data_ptr(), lse.data_ptr<float>(), T, S, Hq,
@@ -513,7 +513,7 @@ void bwd_launch(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k
   {
     const int smem = (2 * 64 + 4 * 32) * D * 2 + 4 * 32 * 4;
     auto kern = attn_bwd_dkdv_kernel<D>;
-    TS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ensure_smem((const void*)kern, (int)(smem));
     dim3 grid((S + 63) / 64, Hkv);
     kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(),
                                         (const bf16*)v.data_ptr(), (const bf16*)dout.data_ptr(),
@@ -523,7 +523,7 @@ void bwd_launch(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k
   {
     const int smem = (2 * 64 + 4 * 64) * D * 2;
     auto kern = attn_bwd_dq_kernel<D>;
-    TS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ensure_smem((const void*)kern, (int)(smem));
     dim3 grid((T + 63) / 64, Hq);
     kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(),
                                         (const bf16*)v.data_ptr(), (const bf16*)dout.data_ptr(),

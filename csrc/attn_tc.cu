@@ -972,7 +972,7 @@ std::vector<at::Tensor> tc_selftest(const at::Tensor& a, const at::Tensor& bk, c
   CUtensorMap mk = make_bf16_map(bk.data_ptr(), 128, 128, 128, 128);
   CUtensorMap mm = make_bf16_map(bm.data_ptr(), 128, 128, 128, 128);
   const int smem = 6 * 16384 + 64 + 1024;
-  TS_CUDA_CHECK(cudaFuncSetAttribute(tc_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  ensure_smem((const void*)tc_selftest_kernel, (int)(smem));
   tc_selftest_kernel<<<1, 128, smem, stream()>>>(ma, mk, mm, d1.data_ptr<float>(), d2.data_ptr<float>(),
                                                  tc_error_flag(a.device()).data_ptr<int>());
   TS_LAUNCH_CHECK();
@@ -1011,17 +1011,17 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
   int* err = tc_error_flag(q.device()).data_ptr<int>();
   if (D == 128) {
     const int smem = FwdLayout<128>::TOTAL + 1024;
-    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ensure_smem((const void*)attn_fwd_tc_kernel<128>, (int)(smem));
     attn_fwd_tc_kernel<128><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
                                                            S, Hq, Hkv, sl2, err);
   } else if (D == 64) {
     const int smem = FwdLayout<64>::TOTAL + 1024;
-    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ensure_smem((const void*)attn_fwd_tc_kernel<64>, (int)(smem));
     attn_fwd_tc_kernel<64><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
                                                           S, Hq, Hkv, sl2, err);
   } else if (D == 256) {
     const int smem = FwdLayout<256>::TOTAL + 1024;
-    TS_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    ensure_smem((const void*)attn_fwd_tc_kernel<256>, (int)(smem));
     attn_fwd_tc_kernel<256><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
                                                            S, Hq, Hkv, sl2, err);
   } else {
@@ -1080,8 +1080,7 @@ void launch_dkdv(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUt
     if (MODE != 1) pv = at::empty({nsplit, S, Hkv, D}, dv.options().dtype(at::kFloat)), ppv = pv.data_ptr<float>();
   }
   const int smem = DkvLayout<D, MODE>::TOTAL + 1024;
-  TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<D, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem));
+  ensure_smem((const void*)attn_bwd_dkdv_tc_kernel<D, MODE>, smem);
   attn_bwd_dkdv_tc_kernel<D, MODE><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
                                                                delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
                                                                (bf16*)dv.data_ptr(), ppk, ppv, T, S, Hq, Hkv,
@@ -1099,7 +1098,7 @@ void launch_dq(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUten
                const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, int T, int S, int Hq, int Hkv,
                double scale, int* err) {
   const int smem = DqLayout<D>::TOTAL + 1024;
-  TS_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  ensure_smem((const void*)attn_bwd_dq_tc_kernel<D>, (int)(smem));
   attn_bwd_dq_tc_kernel<D><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(), delta.data_ptr<float>(),
                                                        (bf16*)dq.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
 }

@@ -74,6 +74,21 @@ std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& 
                                       const at::Tensor& tsv, const at::Tensor& psv, const at::Tensor& kd,
                                       const at::Tensor& kb);
 int64_t gemm_tc_pair(int64_t on);
+std::vector<at::Tensor> dense_layer_fwd(const at::Tensor& h, const at::Tensor& pos, const at::Tensor& inv_freq,
+                                        const at::Tensor& cos_tab, const at::Tensor& sin_tab, const at::Tensor& ln1,
+                                        const at::Tensor& wqkv, const c10::optional<at::Tensor>& qn,
+                                        const c10::optional<at::Tensor>& kn, const at::Tensor& wo,
+                                        const at::Tensor& ln2, const at::Tensor& wgu, const at::Tensor& wd,
+                                        const std::vector<at::Tensor>& past_k, const std::vector<at::Tensor>& past_v,
+                                        int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov);
+std::vector<at::Tensor> dense_layer_bwd(
+    const at::Tensor& dout, const c10::optional<at::Tensor>& dk_out, const c10::optional<at::Tensor>& dv_out,
+    const at::Tensor& h, const at::Tensor& pos, const at::Tensor& inv_freq, const at::Tensor& cos_tab,
+    const at::Tensor& sin_tab, const at::Tensor& ln1, const at::Tensor& wqkv, const c10::optional<at::Tensor>& qn,
+    const c10::optional<at::Tensor>& kn, const at::Tensor& wo, const at::Tensor& ln2, const at::Tensor& wgu,
+    const at::Tensor& wd, const at::Tensor& kbuf, const at::Tensor& vbuf, const std::vector<at::Tensor>& saved,
+    int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov, int64_t sp,
+    const std::vector<c10::optional<at::Tensor>>& sinks, double sink_scale, int64_t side);
 void gemm_tc_cat(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& a2,
                  const c10::optional<at::Tensor>& b2, bool a_t, bool b_t, int64_t mode, double alpha);
 std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
@@ -143,6 +158,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tc", &ts::gemm_tc);
   m.def("lmhead_lse_tc", &ts::lmhead_lse_tc);
   m.def("gemm_tc_pair", &ts::gemm_tc_pair);
+  m.def("dense_layer_fwd", &ts::dense_layer_fwd);
+  m.def("dense_layer_bwd", &ts::dense_layer_bwd);
   m.def("gemm_tc_cat", &ts::gemm_tc_cat);
   m.def("lmhead_dlogits_tc", &ts::lmhead_dlogits_tc);
   m.def("attn_trace_read", &ts::attn_trace_read);

@@ -5,6 +5,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #define TS_CHECK(cond, ...) TORCH_CHECK(cond, "thundersync_b200: ", __VA_ARGS__)
 #define TS_CUDA_CHECK(expr)                                                                 \
   do {                                                                                      \
@@ -26,6 +30,20 @@ inline int sm_count(int device) {
 }
 
 inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device): the attribute persists, and
+// setting it on every launch cost host time on the layer loop's critical path
+inline void ensure_smem(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  int dev = 0;
+  TS_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = done[{fn, dev}];
+  if (have >= bytes) return;
+  TS_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  have = bytes;
+}
 
 inline void check_cuda(const at::Tensor& t, const char* name) {
   TS_CHECK(t.is_cuda(), name, " must be a CUDA tensor");

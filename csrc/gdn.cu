@@ -620,7 +620,7 @@ std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& dfinal
   auto dbeta = at::empty({T, H}, q.options().dtype(at::kFloat));
   auto ds0 = at::empty({H, kDk, kDv}, q.options().dtype(at::kFloat));
   const int dyn = 2 * kCk * kDv * (int)sizeof(float);
-  TS_CUDA_CHECK(cudaFuncSetAttribute(gdn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+  ensure_smem((const void*)gdn_bwd_kernel, (int)(dyn));
   gdn_bwd_kernel<<<H, kThreads, dyn, stream()>>>(qn.data_ptr<float>(), kn.data_ptr<float>(), (const bf16*)v.data_ptr(),
                                                g.data_ptr<float>(), beta.data_ptr<float>(), ckpt.data_ptr<float>(),
                                                (const bf16*)dout.data_ptr(), dfinal.data_ptr<float>(),

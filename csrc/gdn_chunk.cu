@@ -936,7 +936,7 @@ __global__ void __launch_bounds__(NT) gdn_grads_local_kernel(
 
 template <typename K>
 void set_smem(K kernel, size_t bytes) {
-  TS_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  ensure_smem((const void*)kernel, (int)((int)bytes));
 }
 
 }  // namespace

@@ -572,8 +572,7 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N,
   const int tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   const int grid = std::max(1, std::min(tiles, sm_count(device)));
   const int smem = kSmem + 1024;
-  TS_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem));
+  ensure_smem((const void*)gemm_tc_kernel<A_MN, B_MN, EPI>, smem);
   gemm_tc_kernel<A_MN, B_MN, EPI><<<grid, 192, smem, stream()>>>(ma, mb, ma2 ? *ma2 : ma, mb2 ? *mb2 : mb,
                                                                   ma2 ? K2 : 0, c, M, N, K, ldc, alpha,
                                                                   tc_error_flag(at::Device(at::kCUDA, device))

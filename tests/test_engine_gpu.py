@@ -72,11 +72,16 @@ def test_gpu_single_node_layer_matches_op_by_op(prompt_len, cont_len):
     model = Qwen3ForCausalLM(cfg).to("cuda", torch.bfloat16)
     ids = torch.randint(0, cfg.vocab_size, (prompt_len + cont_len,), device="cuda")
     pos = torch.arange(prompt_len + cont_len, device="cuda")
+    from thundersync_b200.engine import dense_layer as DL
+    from thundersync_b200.engine.streaming import arena_for
+
+    arena = arena_for(model)
     res = []
-    for fused in (True, False):
+    for fused, native in ((True, True), (False, False), (True, False)):
         model.zero_grad(set_to_none=True)
-        ex = Executor(model)
+        ex = Executor(model, arena)
         ex.fused_layers = fused
+        DL.NATIVE = native
         def padded(x):  # pack rows padded to a multiple of 128 as the streaming engine pads them
             return torch.cat((x, x.new_zeros((-x.shape[0]) % 128)))
 
@@ -88,6 +93,11 @@ def test_gpu_single_node_layer_matches_op_by_op(prompt_len, cont_len):
         (h0.float().square().mean() + h1.float().pow(3).mean()).backward()
         res.append((h1.detach().float(), {n: p.grad.float().clone() for n, p in model.named_parameters()
                                           if p.grad is not None}))
+    DL.NATIVE = True
+    # the C++-driven layer issues the same kernels as the Python-driven one: bitwise equal
+    assert torch.equal(res[0][0], res[2][0])
+    for n in res[0][1]:
+        assert torch.equal(res[0][1][n], res[2][1][n]), n
     assert float((res[0][0] - res[1][0]).norm() / res[1][0].norm()) < 2e-2
     assert res[0][1].keys() == res[1][1].keys()
     for n in res[0][1]:

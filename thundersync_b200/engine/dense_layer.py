@@ -25,14 +25,21 @@ from typing import Any
 
 import torch
 
+from thundersync_b200.ops import sink as _sink
 from thundersync_b200.ops._ext import native
 from thundersync_b200.ops.attention import _ChunkedAttention
 from thundersync_b200.ops.linear import _Linear
 from thundersync_b200.ops.norm import _RMSNorm
-from thundersync_b200.ops.rope import _QKNormRope
+from thundersync_b200.ops.rope import _QKNormRope, rope_tables
 from thundersync_b200.ops.swiglu import _SwiGLU
 
 __all__ = ["DenseLayer", "dense_layer"]
+
+# CUDA single-segment packs: run the layer's forward and backward from C++ (csrc/dense_layer.cpp);
+# False keeps the same kernels driven from Python
+NATIVE = True
+# packs with at least this many rows put their weight-gradient GEMMs on the side stream
+SIDE_STREAM_MIN_ROWS = 2048
 
 
 class _Ctx:
@@ -65,11 +72,6 @@ class DenseLayer(torch.autograd.Function):
         need_w = any(ctx.needs_input_grad[4 + n_past:])
         t = h.shape[0]
 
-        c_n1 = _Ctx((True, need_w, False, False))
-        x1 = _RMSNorm.forward(c_n1, h, ln1, eps, False)
-        c_qkv = _Ctx((True, False, need_w, need_w, need_w))
-        qkv = _Linear.forward(c_qkv, x1, qkv_fused, wq, wk, wv)
-        c_rope = _Ctx((True, need_w, need_w) + (False,) * 9)
         # one segment from row 0 with no own-pack key ranges (a trajectory or prompt pack): on CUDA the
         # ancestors' keys/values and this pack's are laid out in one buffer, the rope kernel writes the
         # pack's rows in place and attention reads / writes every operand where it lives (no concatenation,
@@ -77,6 +79,31 @@ class DenseLayer(torch.autograd.Function):
         fast = (h.is_cuda and len(segs) == 1 and segs[0][0] == 0 and not segs[0][3]
                 and segs[0][2] == n_past // 2)
         ctx.fast = fast
+        ctx.native = fast and NATIVE and qkv_fused is not None and gu_fused is not None
+        if ctx.native:
+            # the whole layer from C++ (same kernels and GEMMs, no per-op Python dispatch)
+            npast = segs[0][2]
+            pk, pv = list(past[:npast]), list(past[npast:])
+            cov = segs[0][1]
+            ct, st = rope_tables(inv_freq)
+            hc = h.contiguous()
+            out, kbuf, vbuf, *saved = native().dense_layer_fwd(
+                hc, pos, inv_freq, ct, st, ln1, qkv_fused, qn, kn, wo, ln2, gu_fused, wd, pk, pv,
+                hq, hkv, d, float(eps), float(scale), int(cov))
+            sp = sum(x.shape[0] for x in pk)
+            ctx.att = (hc, pos, inv_freq, ct, st, kbuf, vbuf, saved, sp, int(cov), [x.shape[0] for x in pk])
+            ctx.params = (ln1, (wq, wk, wv), qn, kn, wo, ln2, (wg, wu), wd, qkv_fused, gu_fused)
+            ctx.stages = (None,) * 9
+            ctx.set_materialize_grads(False)
+            ctx.meta = meta
+            ctx.t = t
+            ctx.out_shape, ctx.out_dtype, ctx.out_device = out.shape, out.dtype, out.device
+            return out, kbuf[sp:], vbuf[sp:]
+        c_n1 = _Ctx((True, need_w, False, False))
+        x1 = _RMSNorm.forward(c_n1, h, ln1, eps, False)
+        c_qkv = _Ctx((True, False, need_w, need_w, need_w))
+        qkv = _Linear.forward(c_qkv, x1, qkv_fused, wq, wk, wv)
+        c_rope = _Ctx((True, need_w, need_w) + (False,) * 9)
         if fast:
             npast = segs[0][2]
             pk, pv = past[:npast], past[npast:]
@@ -143,11 +170,13 @@ class DenseLayer(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout, dk_out, dv_out):
+        if dout is None:
+            dout = torch.zeros(ctx.out_shape, dtype=ctx.out_dtype, device=ctx.out_device)
+        if ctx.native:
+            return DenseLayer._native_backward(ctx, dout, dk_out, dv_out)
         c_n1, c_qkv, c_rope, c_att, c_o, c_n2, c_gu, c_sw, c_dn = ctx.stages
         hq, hkv, d, eps, scale, segs, n_past, qkv_fused, gu_fused, has_qk = ctx.meta
         t = ctx.t
-        if dout is None:
-            dout = torch.zeros(ctx.out_shape, dtype=ctx.out_dtype, device=ctx.out_device)
         # h_out = h1 + down(swiglu(gu(norm2(h1))))
         da, _, gwd = _Linear.backward(c_dn, dout)
         dgu = _SwiGLU.backward(c_sw, da)
@@ -211,6 +240,64 @@ class DenseLayer(torch.autograd.Function):
             dk[s0:s1] += gks[-1]
             dv[s0:s1] += gvs[-1]
         return DenseLayer._finish(ctx, dq, dk, dv, dpast_k, dpast_v, dh1, gln2, gwo, gwg, gwu, gwd)
+
+    @staticmethod
+    def _native_backward(ctx, dout, dk_out, dv_out):
+        hq, hkv, d, eps, scale, segs, n_past, qkv_fused, gu_fused, has_qk = ctx.meta
+        h, pos, inv_freq, ct, st, kbuf, vbuf, saved, sp, cov, lens = ctx.att
+        ctx.att = None
+        ln1, wqkv_list, qn, kn, wo, ln2, wgu_list, wd, qkv_fused, gu_fused = ctx.params
+        ctx.params = None
+        need_w = any(ctx.needs_input_grad[4 + n_past:])
+        s = _sink.active() if need_w else None
+        dev = h.device
+
+        def view(p):
+            if s is None or p is None or not s.owns(p):
+                return None
+            v = s.view(p)
+            return v if v.dtype == torch.float32 else None
+
+        def span(ps):
+            if s is None or not all(s.owns(p) for p in ps):
+                return None
+            v = s.span_view(list(ps))
+            return v if v is not None and v.dtype == torch.float32 else None
+
+        sinks = [view(ln1), span(wqkv_list), view(qn), view(kn), view(wo), view(ln2), span(wgu_list), view(wd)]
+        side = 0
+        # short packs are bound by host issue time, where the side stream's extra stream bookkeeping only costs
+        if s is not None and _sink.SIDE_STREAM_WEIGHT_GRADS and ctx.t >= SIDE_STREAM_MIN_ROWS:
+            side = _sink._side_stream(dev).cuda_stream
+            s._side_devices = getattr(s, "_side_devices", set())
+            s._side_devices.add(dev)
+        res = native().dense_layer_bwd(
+            dout, dk_out, dv_out, h, pos, inv_freq, ct, st, ln1, qkv_fused, qn, kn, wo, ln2, gu_fused, wd,
+            kbuf, vbuf, saved, hq, hkv, d, float(eps), float(scale), cov, sp, sinks,
+            float(s.scale) if s is not None else 1.0, side)
+        dh, dkp, dvp, g_ln1, g_qkv, g_qn, g_kn, g_o, g_ln2, g_gu, g_d = res
+        if s is not None:
+            s.deposits += sum(1 for x in sinks if x is not None)
+        dpast_k = list(torch.split(dkp, lens, 0)) if lens else []
+        dpast_v = list(torch.split(dvp, lens, 0)) if lens else []
+
+        def cast(g, p):
+            return None if g is None or p is None else g.to(p.dtype)
+
+        def split(g, ps):
+            if g is None:
+                return [None] * len(ps)
+            out, r0 = [], 0
+            for p in ps:
+                out.append(g[r0:r0 + p.shape[0]].to(p.dtype))
+                r0 += p.shape[0]
+            return out
+
+        gq, gk, gv = split(g_qkv, wqkv_list)
+        gg, gu = split(g_gu, wgu_list)
+        params = [cast(g_ln1, ln1), gq, gk, gv] + ([cast(g_qn, qn), cast(g_kn, kn)] if has_qk else [])
+        params += [cast(g_o, wo), cast(g_ln2, ln2), gg, gu, cast(g_d, wd)]
+        return (dh, None, None, None, *dpast_k, *dpast_v, *params)
 
     @staticmethod
     def _finish(ctx, dq, dk, dv, dpast_k, dpast_v, dh1, gln2, gwo, gwg, gwu, gwd):

@@ -377,6 +377,54 @@ def bench_lora(args) -> None:
         print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=15, max_name_column_width=70))
 
 
+def bench_layer_host(args) -> None:
+    """Host time vs device time of one pack through all decoder layers (Qwen3-1.7B shapes), forward + backward
+    into a gradient sink, for several pack lengths: where host time exceeds device time the GPU waits."""
+    import time
+
+    from thundersync_b200.engine.layers import Executor, Segment
+    from thundersync_b200.engine.streaming import arena_for
+    from thundersync_b200.models.qwen3 import PRESETS, Qwen3ForCausalLM
+    from thundersync_b200.ops.sink import GradSink, grad_sink
+
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        model = Qwen3ForCausalLM(PRESETS["qwen3-1.7b"])
+    model.to(torch.bfloat16)
+    arena = arena_for(model)
+    ex = Executor(model, arena)
+    buf = torch.zeros(arena.numel, device="cuda")
+    prompt = 512
+    ids_p = torch.randint(0, 1000, (prompt,), device="cuda")
+    with torch.no_grad():
+        _, st = ex.run(ids_p, torch.arange(prompt, device="cuda"), [Segment(0, prompt, [])])
+    past = [([k], [v]) for (k, v) in st[0]]
+    for n in (256, 1024, 2176, 4096):
+        pad = (-n) % 128
+        ids = torch.randint(0, 1000, (n + pad,), device="cuda")
+        pos = torch.cat((torch.arange(prompt, prompt + n, device="cuda"), torch.zeros(pad, dtype=torch.long,
+                                                                                        device="cuda")))
+
+        def once():
+            h, _ = ex.run(ids, pos, [Segment(0, n, past)])
+            with grad_sink(GradSink(arena, buf)):
+                h[:n].float().square().mean().backward()
+
+        for _ in range(2):
+            once()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        t0 = time.perf_counter()
+        for _ in range(args.iters):
+            once()
+        t1 = time.perf_counter()
+        b.record()
+        torch.cuda.synchronize()
+        print(f"pack of {n} tokens (+{pad} padding) over a {prompt}-token prompt: host issue {1e3 * (t1 - t0) / args.iters:.2f} ms, "
+              f"device {a.elapsed_time(b) / args.iters:.2f} ms per forward+backward")
+
+
 def bench_gemm_host(args) -> None:
     """Host (CPU) cost of one library GEMM call: repeated shape vs a new row count every call."""
     import time
@@ -400,12 +448,49 @@ def bench_gemm_host(args) -> None:
             t2 = time.perf_counter()
             print(f"{fn_name:10s} {name:8s}: host {1e6 * (t1 - t0) / len(seq):7.1f} us/call, "
                   f"device+host {1e6 * (t2 - t0) / len(seq):7.1f} us/call")
+    # host issue cost of single small launches (a 256-row pack): library GEMM vs this package's kernels
+    ext = native()
+    x = torch.randn(256, 2048, device="cuda", dtype=torch.bfloat16)
+    wq = torch.randn(4096, 2048, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(256, 4096, device="cuda", dtype=torch.bfloat16)
+    ln = torch.ones(2048, device="cuda", dtype=torch.bfloat16)
+    q = torch.randn(256, 16, 128, device="cuda", dtype=torch.bfloat16)
+    kv = torch.randn(768, 8, 128, device="cuda", dtype=torch.bfloat16)
+    acc = torch.zeros(4096, 2048, device="cuda")
+    dy = torch.randn(256, 4096, device="cuda", dtype=torch.bfloat16)
+    side = torch.cuda.Stream()
+
+    def deposit_side():
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            torch.addmm(acc, dy.t(), x, out_dtype=torch.float32, out=acc)
+        torch.cuda.current_stream().wait_stream(side)
+
+    cases = (("F.linear 256x4096x2048", lambda: torch.nn.functional.linear(x, wq)),
+             ("torch.mm out_dtype fp32", lambda: torch.mm(x, wq.t(), out_dtype=torch.float32)),
+             ("tcgen05 gemm_tc", lambda: ext.gemm_tc(y, x, wq, False, True, 0, 1.0)),
+             ("addmm fp32 sink deposit", lambda: torch.addmm(acc, dy.t(), x, out_dtype=torch.float32, out=acc)),
+             ("deposit on a side stream", deposit_side),
+             ("rms_norm_fwd", lambda: ext.rms_norm_fwd(x, ln, 1e-6, False)),
+             ("attn_fwd_tc 256 over 768", lambda: ext.attn_fwd_tc(q, kv, kv, 0.088)),
+             ("torch.empty", lambda: torch.empty(256, 4096, device="cuda", dtype=torch.bfloat16)))
+    for name, fn in cases:
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(200):
+            fn()
+        t1 = time.perf_counter()
+        torch.cuda.synchronize()
+        t2 = time.perf_counter()
+        print(f"{name:28s}: host {1e6 * (t1 - t0) / 200:7.1f} us/call, device+host {1e6 * (t2 - t0) / 200:7.1f} us/call")
 
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host", "swiglu", "rope", "dlogits",
-                                       "adamw", "fold", "gemm", "lmhead", "baselines", "lora"])
+                                       "adamw", "fold", "gemm", "lmhead", "baselines", "lora", "layer_host"])
     ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
     ap.add_argument("--t", type=int, default=2048)
     ap.add_argument("--s", type=int, default=2560)
@@ -421,7 +506,8 @@ def main(argv=None) -> None:
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
      "gemm_host": bench_gemm_host, "swiglu": bench_swiglu, "rope": bench_rope, "dlogits": bench_dlogits,
      "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm,
-     "lmhead": bench_lmhead, "baselines": bench_baselines, "lora": bench_lora}[args.family](args)
+     "lmhead": bench_lmhead, "baselines": bench_baselines, "lora": bench_lora,
+     "layer_host": bench_layer_host}[args.family](args)
 
 
 if __name__ == "__main__":

@@ -57,13 +57,14 @@ class _Linear(torch.autograd.Function):
             x2 = x.reshape(-1, x.shape[-1])
             s = _sink.active()
             if s is not None and all(s.owns(t) for t in weights):
+                # projection weights receive only this deposit: it may run on the side stream
                 span = s.span_view(list(weights))
                 if span is not None:
-                    s.addmm_(span, dy2, x2)
+                    s.addmm_(span, dy2, x2, side=True)
                 else:
                     r0 = 0
                     for t, r in zip(weights, ctx.rows):
-                        s.addmm_(s.view(t), dy2[:, r0 : r0 + r], x2)
+                        s.addmm_(s.view(t), dy2[:, r0 : r0 + r], x2, side=True)
                         r0 += r
             else:
                 dw = dy2.t().matmul(x2)

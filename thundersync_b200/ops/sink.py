@@ -22,6 +22,21 @@ import torch
 
 _ACTIVE: "GradSink | None" = None
 
+# CUDA: projection weight gradients (dW += dYᵀ·X into the sink) run on a side stream, so they fill the
+# SMs that the dependent chain (dX, attention, norms) leaves idle; the stream that leaves a grad_sink
+# block waits for them, so anything that reads the sink afterwards sees every deposit
+SIDE_STREAM_WEIGHT_GRADS = True
+_SIDE: dict[int, "torch.cuda.Stream"] = {}
+
+
+def _side_stream(device: torch.device) -> "torch.cuda.Stream":
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _SIDE.get(idx)
+    if st is None:
+        st = torch.cuda.Stream(device=idx)
+        _SIDE[idx] = st
+    return st
+
 
 def active() -> "GradSink | None":
     return _ACTIVE
@@ -36,6 +51,8 @@ def grad_sink(sink: "GradSink | None"):
         yield sink
     finally:
         _ACTIVE = prev
+        if sink is not None:
+            sink.join_side_stream()
 
 
 def _redirect_hook(p: torch.Tensor) -> None:
@@ -188,13 +205,39 @@ class GradSink:
             v.add_(grad)
         self.deposits += 1
 
-    def addmm_(self, target: torch.Tensor, dy: torch.Tensor, x: torch.Tensor) -> None:
-        """``target += scale · dyᵀ x`` with fp32 accumulation, in place."""
+    def addmm_(self, target: torch.Tensor, dy: torch.Tensor, x: torch.Tensor, *, side: bool = False) -> None:
+        """``target += scale · dyᵀ x`` with fp32 accumulation, in place.
+
+        ``side``: the caller guarantees no other deposit touches ``target`` before the sink block ends
+        (a projection weight, which no native op or hook also writes), so on CUDA the GEMM may run on
+        the side stream.
+        """
         if dy.shape[0] == 0:
             return
         if target.is_cuda and dy.dtype != target.dtype:
-            torch.addmm(target, dy.t(), x, beta=1.0, alpha=self.scale,
-                        out_dtype=target.dtype, out=target)
+            if side and SIDE_STREAM_WEIGHT_GRADS:
+                main = torch.cuda.current_stream(target.device)
+                st = _side_stream(target.device)
+                st.wait_stream(main)
+                with torch.cuda.stream(st):
+                    torch.addmm(target, dy.t(), x, beta=1.0, alpha=self.scale,
+                                out_dtype=target.dtype, out=target)
+                # the operands' memory must outlive the side-stream GEMM
+                dy.record_stream(st)
+                x.record_stream(st)
+                self._side_devices = getattr(self, "_side_devices", set())
+                self._side_devices.add(target.device)
+            else:
+                torch.addmm(target, dy.t(), x, beta=1.0, alpha=self.scale,
+                            out_dtype=target.dtype, out=target)
         else:
             target.addmm_(dy.t().to(target.dtype), x.to(target.dtype), alpha=self.scale)
         self.deposits += 1
+
+    def join_side_stream(self) -> None:
+        """Make the current stream wait for this sink's side-stream deposits."""
+        devs = getattr(self, "_side_devices", None)
+        if devs:
+            for d in devs:
+                torch.cuda.current_stream(d).wait_stream(_side_stream(d))
+            devs.clear()
