@@ -218,23 +218,31 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       const int k0 = j * L::BN;
       int nvis = min(lim, S - 1) - k0 + 1;  // visible columns of this tile for this row
       nvis = nvis < 0 ? 0 : (nvis > L::BN ? L::BN : nvis);
-      float raw = -INFINITY;
+      // row max over the tile as 8 independent chains (a single fmaxf chain of BN links serialises on
+      // the instruction latency; the chains are combined at the end)
+      float mx8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
       if (nvis == L::BN) {
 #pragma unroll
-        for (int i = 0; i < L::BN; ++i) raw = fmaxf(raw, sv[i]);
+        for (int i = 0; i < L::BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < L::BN; ++i) raw = fmaxf(raw, i < nvis ? sv[i] : -INFINITY);
+        for (int i = 0; i < L::BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], i < nvis ? sv[i] : -INFINITY);
       }
+      const float raw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mx = fmaxf(m, raw * sl2);
       const float ref = mx == -INFINITY ? 0.f : mx;
-      const float alpha = exp2f(m - ref);
+      const float alpha = ex2(m - ref);
       // this warp's half of the tile's columns, reloaded into registers with static indices
 #pragma unroll
       for (int c = 0; c < L::HALF / 32; ++c) tc::tmem_ld32(lane_base + scol + hc * L::HALF + c * 32, sv + c * 32);
       tc::tmem_ld_wait();
       const int nv_half = nvis - hc * L::HALF;
-      float rs = 0.f;
+      float rs8[8];  // 8 independent partial sums, for the same reason as the max
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rs8[e] = 0.f;
       const uint32_t pbase = sbase + L::P0 + s * L::P_BYTES;
 #pragma unroll
       for (int c8 = 0; c8 < L::HALF / 8; ++c8) {
@@ -243,11 +251,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         for (int e = 0; e < 8; ++e) {
           const int i = c8 * 8 + e;
           p[e] = i < nv_half ? ex2(fmaf(sv[i], sl2, -ref)) : 0.f;
-          rs += p[e];
+          rs8[e] += p[e];
         }
         st_shared_v4(pbase + tc::kmajor_off(r, hc * L::HALF + c8 * 8, 128), pack2(p[0], p[1]), pack2(p[2], p[3]),
                      pack2(p[4], p[5]), pack2(p[6], p[7]));
       }
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
       if (j > 0) {
         if (!warp_wait(&bars->pv, (j - 1) & 1, abort, err, 32)) { ok = false; break; }

@@ -314,29 +314,37 @@ class DenseLayer(torch.autograd.Function):
 def dense_layer(ex, i: int, h: torch.Tensor, pos: torch.Tensor, segs) -> tuple[torch.Tensor, list]:
     """Run dense attention layer ``i`` of executor ``ex`` as one autograd node; returns (h, per-seg (k, v))."""
     spec = ex.spec
-    layer = ex.model.model.layers[i]
-    sa, mlp = layer.self_attn, layer.mlp
-    qn = getattr(sa, "q_norm", None)
-    kn = getattr(sa, "k_norm", None)
-    has_qk = qn is not None
-    weights_qkv = [sa.q_proj.weight, sa.k_proj.weight, sa.v_proj.weight]
-    weights_gu = [mlp.gate_proj.weight, mlp.up_proj.weight]
     arena = ex.arena
-    qkv_fused = arena.fused_weight(weights_qkv) if arena is not None else None
-    gu_fused = arena.fused_weight(weights_gu) if arena is not None else None
+    # the layer's parameter list, fused weight views and scalars do not change between calls (the same
+    # parameter objects, the same arena): build them once per layer
+    cache = ex.__dict__.setdefault("_dense_static", {})
+    layer = ex.model.model.layers[i]
+    st = cache.get(i)
+    if st is None or st[0] is not arena or st[1] is not layer.input_layernorm.weight:
+        sa, mlp = layer.self_attn, layer.mlp
+        qn = getattr(sa, "q_norm", None)
+        kn = getattr(sa, "k_norm", None)
+        has_qk = qn is not None
+        weights_qkv = [sa.q_proj.weight, sa.k_proj.weight, sa.v_proj.weight]
+        weights_gu = [mlp.gate_proj.weight, mlp.up_proj.weight]
+        qkv_fused = arena.fused_weight(weights_qkv) if arena is not None else None
+        gu_fused = arena.fused_weight(weights_gu) if arena is not None else None
+        eps = getattr(layer.input_layernorm, "variance_epsilon", None) or spec.eps
+        params = [layer.input_layernorm.weight, *weights_qkv]
+        if has_qk:
+            params += [qn.weight, kn.weight]
+        params += [sa.o_proj.weight, layer.post_attention_layernorm.weight, *weights_gu, mlp.down_proj.weight]
+        st = (arena, layer.input_layernorm.weight, tuple(params), qkv_fused, gu_fused, eps, has_qk)
+        cache[i] = st
+    _, _, params, qkv_fused, gu_fused, eps, has_qk = st
     past_k, past_v, seg_meta = [], [], []
     for seg in segs:
         ks, vs = seg.past[i] if seg.past and seg.past[i] is not None else ([], [])
         past_k.extend(ks)
         past_v.extend(vs)
         seg_meta.append((seg.start, seg.start + seg.length, len(ks), tuple(seg.key_ranges)))
-    eps = getattr(layer.input_layernorm, "variance_epsilon", None) or spec.eps
     meta = (spec.n_heads, spec.n_kv, spec.head_dim, eps, 1.0 / math.sqrt(spec.head_dim), tuple(seg_meta),
             len(past_k) + len(past_v), qkv_fused, gu_fused, has_qk)
-    params = [layer.input_layernorm.weight, *weights_qkv]
-    if has_qk:
-        params += [qn.weight, kn.weight]
-    params += [sa.o_proj.weight, layer.post_attention_layernorm.weight, *weights_gu, mlp.down_proj.weight]
     out, k, v = DenseLayer.apply(h, pos, ex.inv_freq(h.device), meta, *past_k, *past_v, *params)
     new_state = [(k[s.start:s.start + s.length], v[s.start:s.start + s.length]) for s in segs]
     return out, new_state
