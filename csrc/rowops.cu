@@ -375,6 +375,54 @@ void rms_dx_dispatch(const at::Tensor& dy, const at::Tensor& x, const at::Tensor
 // ----------------------------------------------------------------- QK-norm + RoPE
 // One warp per (token, head) row of q or k; lane owns EPL = D/32 consecutive
 // elements, so the rotate-half partner (element i +- D/2) lives on lane ^ 16.
+// EPL consecutive elements of one lane as one vector access (8 bytes for 4 bf16 at head_dim 128)
+template <typename T, int EPL>
+TS_DEVICE void load_lane(const T* __restrict__ p, float (&out)[EPL]) {
+  if constexpr (sizeof(T) * EPL == 8) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = to_f(e[i]);
+  } else if constexpr (sizeof(T) * EPL == 16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = to_f(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = to_f(p[i]);
+  }
+}
+template <typename T, int EPL>
+TS_DEVICE void store_lane(T* __restrict__ p, const float (&in)[EPL]) {
+  if constexpr (sizeof(T) * EPL == 8) {
+    uint2 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) e[i] = from_f<T>(in[i]);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else if constexpr (sizeof(T) * EPL == 16) {
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) e[i] = from_f<T>(in[i]);
+    *reinterpret_cast<uint4*>(p) = u;
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) p[i] = from_f<T>(in[i]);
+  }
+}
+template <int EPL>
+TS_DEVICE void load_f32_lane(const float* __restrict__ p, float (&out)[EPL]) {
+  if constexpr (EPL == 4) {
+    const float4 u = *reinterpret_cast<const float4*>(p);
+    out[0] = u.x; out[1] = u.y; out[2] = u.z; out[3] = u.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = p[i];
+  }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
     const T* __restrict__ qkv, const T* __restrict__ qw, const T* __restrict__ kw, const int64_t* __restrict__ pos,
@@ -390,12 +438,9 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
   const int h = (int)(item % heads);
   const T* src = qkv + (size_t)t * heads * D + (size_t)h * D + lane * EPL;
   float xv[EPL];
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) xv[e] = to_f(src[e]);
+  load_lane<T, EPL>(src, xv);
   if (h >= hq + hkv) {  // value head: plain copy
-    T* dst = v + ((size_t)t * hkv + (h - hq - hkv)) * D + lane * EPL;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) dst[e] = from_f<T>(xv[e]);
+    store_lane<T, EPL>(v + ((size_t)t * hkv + (h - hq - hkv)) * D + lane * EPL, xv);
     return;
   }
   const bool is_q = h < hq;
@@ -407,11 +452,11 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
     for (int e = 0; e < EPL; ++e) ss += xv[e] * xv[e];
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / (float)D + eps);
+    float wv[EPL];
+    load_lane<T, EPL>(wt + lane * EPL, wv);
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const float wv = to_f(wt[lane * EPL + e]);
-      y[e] = unit ? round_to<T>(xv[e] * r * (1.f + wv)) : round_to<T>(wv * round_to<T>(xv[e] * r));
-    }
+    for (int e = 0; e < EPL; ++e)
+      y[e] = unit ? round_to<T>(xv[e] * r * (1.f + wv[e])) : round_to<T>(wv[e] * round_to<T>(xv[e] * r));
   } else {
 #pragma unroll
     for (int e = 0; e < EPL; ++e) y[e] = xv[e];
@@ -426,24 +471,27 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_fwd_kernel(
   const int half_mask = rot_lanes >> 1;
   const bool rotary = lane < rot_lanes;
   const bool low = (lane & half_mask) == 0;
+  const int f0 = (lane & (half_mask - 1)) * EPL;  // first frequency index of this lane
+  float cs[EPL], sn[EPL];
+  if (rotary && tab) {  // cos/sin of the fp32 angle, precomputed per (position, frequency)
+    load_f32_lane<EPL>(cos_tab + pi * nfreq + f0, cs);
+    load_f32_lane<EPL>(sin_tab + pi * nfreq + f0, sn);
+  } else if (rotary) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      float s_, c_;
+      sincosf(p * inv_freq[f0 + e], &s_, &c_);
+      sn[e] = s_;
+      cs[e] = c_;
+    }
+  }
+  float out[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
     const float partner = __shfl_xor_sync(0xffffffffu, y[e], half_mask);
-    if (rotary) {
-      const int fi = (lane & (half_mask - 1)) * EPL + e;  // frequency index
-      float s, c;
-      if (tab) {  // cos/sin of the fp32 angle, precomputed per (position, frequency)
-        c = cos_tab[pi * nfreq + fi];
-        s = sin_tab[pi * nfreq + fi];
-      } else {
-        sincosf(p * inv_freq[fi], &s, &c);
-      }
-      const float rot = low ? -partner : partner;
-      dst[e] = from_f<T>(y[e] * c + rot * s);
-    } else {
-      dst[e] = from_f<T>(y[e]);
-    }
+    out[e] = rotary ? y[e] * cs[e] + (low ? -partner : partner) * sn[e] : y[e];
   }
+  store_lane<T, EPL>(dst, out);
 }
 
 template <typename T, int D>
@@ -471,9 +519,9 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
     const int h = (int)(item % heads);
     T* out = dqkv + (size_t)t * heads * D + (size_t)h * D + lane * EPL;
     if (h >= hq + hkv) {
-      const T* g = dv + ((size_t)t * hkv + (h - hq - hkv)) * D + lane * EPL;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) out[e] = g[e];
+      float gv[EPL];
+      load_lane<T, EPL>(dv + ((size_t)t * hkv + (h - hq - hkv)) * D + lane * EPL, gv);
+      store_lane<T, EPL>(out, gv);
       continue;
     }
     const bool is_q = h < hq;
@@ -486,39 +534,41 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
     const int half_mask = rot_lanes >> 1;
     const bool rotary = lane < rot_lanes;
     const bool low = (lane & half_mask) == 0;
+    const T* wt = is_q ? qw : kw;
+    // all of this row's loads issue together: the gradient, the input row, the norm weight, cos/sin
+    float go[EPL], xv[EPL], wv[EPL], cs[EPL], sn[EPL];
+    load_lane<T, EPL>(g, go);
+    if (wt != nullptr) {
+      load_lane<T, EPL>(src, xv);
+      load_lane<T, EPL>(wt + lane * EPL, wv);
+    }
+    const int f0 = (lane & (half_mask - 1)) * EPL;
+    if (rotary && tab) {
+      load_f32_lane<EPL>(cos_tab + pi * nfreq + f0, cs);
+      load_f32_lane<EPL>(sin_tab + pi * nfreq + f0, sn);
+    } else if (rotary) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        float s_, c_;
+        sincosf(p * inv_freq[f0 + e], &s_, &c_);
+        sn[e] = s_;
+        cs[e] = c_;
+      }
+    }
     float dy[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
-      const float go = to_f(g[e]);
-      const float partner = __shfl_xor_sync(0xffffffffu, go, half_mask);
-      if (rotary) {
-        const int fi = (lane & (half_mask - 1)) * EPL + e;
-        float s, c;
-        if (tab) {
-          c = cos_tab[pi * nfreq + fi];
-          s = sin_tab[pi * nfreq + fi];
-        } else {
-          sincosf(p * inv_freq[fi], &s, &c);
-        }
-        // d/dy_i of sum_j go_j * (y_j c_j + rot(y)_j s_j)
-        dy[e] = go * c + (low ? partner : -partner) * s;
-      } else {
-        dy[e] = go;
-      }
+      const float partner = __shfl_xor_sync(0xffffffffu, go[e], half_mask);
+      // d/dy_i of sum_j go_j * (y_j c_j + rot(y)_j s_j)
+      dy[e] = rotary ? go[e] * cs[e] + (low ? partner : -partner) * sn[e] : go[e];
     }
-    const T* wt = is_q ? qw : kw;
     if (wt == nullptr) {
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) out[e] = from_f<T>(dy[e]);
+      store_lane<T, EPL>(out, dy);
       continue;
     }
-    float xv[EPL];
     float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      xv[e] = to_f(src[e]);
-      ss += xv[e] * xv[e];
-    }
+    for (int e = 0; e < EPL; ++e) ss += xv[e] * xv[e];
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / (float)D + eps);
     float dot = 0.f;
@@ -526,13 +576,15 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_bwd_kernel(
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
       const float n = xv[e] * r;
-      dn[e] = dy[e] * (to_f(wt[lane * EPL + e]) + (unit ? 1.f : 0.f));
+      dn[e] = dy[e] * (wv[e] + (unit ? 1.f : 0.f));
       dot += dn[e] * n;
       if (is_q) aq[e] += dy[e] * n; else ak[e] += dy[e] * n;
     }
     dot = warp_sum(dot) / (float)D;
+    float res[EPL];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) out[e] = from_f<T>(r * (dn[e] - xv[e] * r * dot));
+    for (int e = 0; e < EPL; ++e) res[e] = r * (dn[e] - xv[e] * r * dot);
+    store_lane<T, EPL>(out, res);
   }
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
