@@ -1,0 +1,123 @@
+"""Streaming invariants on CPU fp32 (the reference's streaming-exactness battery, restated for this engine).
+
+Each test runs the same GRPO batch through the streaming engine twice under two settings that must
+not change the gradient: trajectory arrival order, per-layer activation checkpointing, source offload
+placement, rebuild block size, chunked key/value streaming, parameter-adjoint reduction order.
+"""
+
+from __future__ import annotations
+
+import copy
+
+import pytest
+import torch
+
+from tests.grpo_fixtures import EPS, build_model, make_batch
+from thundersync_b200.engine.streaming import StreamingRun
+from thundersync_b200.grpo.reward_linear import RewardLinearBackward
+
+
+def _grads(model, batch, order, *, run_kw=None, bw_kw=None, binary=False, stream_turns=False):
+    model.zero_grad(set_to_none=True)
+    run = StreamingRun(model, boundary_cut=True, stream_turns=stream_turns, **(run_kw or {}))
+    bw = RewardLinearBackward(run, model, eps=EPS, **(bw_kw or {}))
+    if binary:
+        bw.configure_binary_rewards()
+    for g, prompt, trajs in batch:
+        bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    for g, (tid, turns, reward) in order:
+        for tk, sc in turns:
+            run.append_turn(g, tid, tk, sc)
+        bw.close_trajectory(tid, reward)
+    for g, _, _ in batch:
+        bw.close_group(g)
+    bw.assert_safe_to_step()
+    return {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+
+
+def _close(a, b, rtol=1e-5, atol=5e-6):
+    assert a.keys() == b.keys()
+    for n in a:
+        torch.testing.assert_close(a[n], b[n], rtol=rtol, atol=atol, msg=n)
+
+
+def _orders(order):
+    """The fixture's shuffled order, its reverse, and a round-robin interleave across groups."""
+    by_group: dict[int, list] = {}
+    for g, item in order:
+        by_group.setdefault(g, []).append((g, item))
+    rr = []
+    while any(by_group.values()):
+        for g in sorted(by_group):
+            if by_group[g]:
+                rr.append(by_group[g].pop(0))
+    return [order, list(reversed(order)), rr]
+
+
+@pytest.mark.parametrize("binary", [False, True])
+def test_gradient_independent_of_arrival_order(binary):
+    model = build_model(3)
+    batch, order = make_batch(3)
+    res = [_grads(copy.deepcopy(model), batch, o, binary=binary) for o in _orders(order)]
+    _close(res[0], res[1])
+    _close(res[0], res[2])
+
+
+def test_checkpointed_executor_matches_plain():
+    model = build_model(4)
+    batch, order = make_batch(4)
+    a = _grads(copy.deepcopy(model), batch, order)
+    b = _grads(copy.deepcopy(model), batch, order, run_kw={"checkpoint": True})
+    _close(a, b, rtol=0, atol=0)  # recomputation on CPU repeats the same arithmetic: bitwise
+
+
+def test_source_offload_modes_agree():
+    model = build_model(5)
+    batch, order = make_batch(5)
+    a = _grads(copy.deepcopy(model), batch, order, bw_kw={"source_offload_mode": "blocking"})
+    b = _grads(copy.deepcopy(model), batch, order, bw_kw={"source_offload_mode": "device_resident",
+                                                          "source_offload_device": None})
+    _close(a, b)
+
+
+@pytest.mark.parametrize("block", [8, 64])
+def test_rebuild_block_size_does_not_change_gradient(block):
+    model = build_model(6)
+    batch, order = make_batch(6, multi_turn=True)
+    a = _grads(copy.deepcopy(model), batch, order, stream_turns=True)
+    b = _grads(copy.deepcopy(model), batch, order, stream_turns=True, run_kw={"rebuild_block_tokens": block})
+    _close(a, b)
+
+
+def test_turn_streaming_matches_whole_trajectories():
+    model = build_model(7)
+    batch, order = make_batch(7, multi_turn=True)
+    a = _grads(copy.deepcopy(model), batch, order, stream_turns=True)
+    b = _grads(copy.deepcopy(model), batch, order, stream_turns=False)
+    _close(a, b, rtol=2e-4, atol=2e-6)
+
+
+@pytest.mark.parametrize("reduction", ["arrival", "canonical_source"])
+def test_parameter_adjoint_reduction_modes(reduction):
+    model = build_model(8)
+    batch, order = make_batch(8)
+    a = _grads(copy.deepcopy(model), batch, order)
+    b = _grads(copy.deepcopy(model), batch, order, run_kw={"parameter_adjoint_reduction": reduction})
+    _close(a, b)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    ({"turn_boundary_rebuild": True, "stream_turns": False}, "stream_turns"),
+    ({"chunk": 0}, "chunk"),
+    ({"rebuild_block_tokens": 0}, "rebuild_block_tokens"),
+    ({"boundary_adjoint_backend": "cuda_graph"}, "boundary_adjoint_backend"),
+    ({"boundary_adjoint_max_degree": 17}, "boundary_adjoint_max_degree"),
+    ({"shared_prefix_vjp_mode": "eager"}, "shared_prefix_vjp_mode"),
+    ({"parameter_adjoint_reduction": "sorted"}, "parameter_adjoint_reduction"),
+])
+def test_streaming_run_refuses_bad_settings(kw, msg):
+    model = build_model(0)
+    kw = dict(kw)
+    stream_turns = kw.pop("stream_turns", True)
+    with pytest.raises((ValueError, NotImplementedError), match=msg.split("_")[0]):
+        StreamingRun(model, boundary_cut=True, stream_turns=stream_turns, **kw)
