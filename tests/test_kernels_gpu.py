@@ -415,3 +415,25 @@ def _check_lora():
     assert _rel(y, yr) < 1e-2
     assert _rel(gx, gxr) < 1e-2 and _rel(ga, gar) < 1e-2 and _rel(gb, gbr) < 1e-2
     assert ga.dtype == torch.float32 and gb.dtype == torch.float32
+
+
+@pytest.mark.parametrize("n_adj,dtype", [(3, torch.float32), (16, torch.float32), (37, torch.float32),
+                                         (5, torch.bfloat16)])
+def test_boundary_adjoint_native_fixed_order(n_adj, dtype):
+    """The native boundary-adjoint reduction adds in a fixed order into fp32 and rounds once: it equals a host
+    fp32 accumulation in the same order bitwise, and repeated runs agree bitwise."""
+    from thundersync_b200.engine.boundary_adjoint import reduce_boundary_adjoints
+
+    torch.manual_seed(n_adj)
+    shape = (257, 129)
+    adj = [torch.randn(shape, device=DEV).to(dtype) for _ in range(n_adj)]
+    existing = torch.randn(shape, device=DEV).to(dtype)
+    got = reduce_boundary_adjoints(adj, existing=existing, backend="native")
+    acc = existing.float().cpu().clone()
+    for a in adj:
+        acc += a.float().cpu()
+    assert got.dtype == dtype
+    assert torch.equal(got.cpu(), acc.to(dtype))
+    again = reduce_boundary_adjoints(adj, existing=existing, backend="native")
+    assert torch.equal(got, again)
+    assert torch.equal(reduce_boundary_adjoints([None, adj[0]], backend="native").cpu(), adj[0].cpu())
