@@ -121,3 +121,23 @@ def test_streaming_run_refuses_bad_settings(kw, msg):
     stream_turns = kw.pop("stream_turns", True)
     with pytest.raises((ValueError, NotImplementedError), match=msg.split("_")[0]):
         StreamingRun(model, boundary_cut=True, stream_turns=stream_turns, **kw)
+
+
+def test_shared_prefix_timing_and_adjoint_storage_diagnostics():
+    model = build_model(9)
+    batch, order = make_batch(9)
+    a = _grads(copy.deepcopy(model), batch, order, run_kw={"parameter_adjoint_reduction": "canonical_source"})
+    m = copy.deepcopy(model)
+    b = _grads(m, batch, order, run_kw={"parameter_adjoint_reduction": "canonical_source",
+                                        "parameter_adjoint_storage_device": "cpu",
+                                        "shared_prefix_vjp_timing": True})
+    _close(a, b, rtol=0, atol=0)
+
+
+def test_rebuild_reserve_option_is_accepted_on_cpu():
+    model = build_model(10)
+    batch, order = make_batch(10, multi_turn=True)
+    a = _grads(copy.deepcopy(model), batch, order, stream_turns=True)
+    b = _grads(copy.deepcopy(model), batch, order, stream_turns=True,
+               run_kw={"rebuild_plain_reserve_bytes": 1 << 30, "rebuild_block_tokens": 8})
+    _close(a, b)

@@ -30,6 +30,7 @@ backward flows through, so ``old == new`` holds bitwise.
 from __future__ import annotations
 
 import contextlib
+import time
 import hashlib
 from dataclasses import dataclass, field
 from typing import Any, Iterable
@@ -227,6 +228,13 @@ class StreamingRun:
         self.boundary_adjoint_max_degree = boundary_adjoint_max_degree
         self.parameter_adjoint_reduction = parameter_adjoint_reduction
         self.shared_prefix_vjp_backend = shared_prefix_vjp_backend
+        self.shared_prefix_vjp_timing = bool(shared_prefix_vjp_timing)
+        self._shared_prefix_times: list[float] = []
+        # staged parameter adjoints (canonical-source reduction) live here until they are applied
+        self._param_adjoint_device = (
+            None if parameter_adjoint_storage_device is None else torch.device(parameter_adjoint_storage_device)
+        )
+        self.rebuild_plain_reserve_bytes = rebuild_plain_reserve_bytes
         self.dependency_ready_shared_prefix_vjp = dependency_ready_shared_prefix_vjp or (
             shared_prefix_vjp_mode == "source_ready_serial"
         )
@@ -662,6 +670,14 @@ class StreamingRun:
         block = self.rebuild_block_tokens
         if executor == "plain":
             block = None
+        elif executor == "auto" and self.rebuild_plain_reserve_bytes is not None and self.device.type == "cuda":
+            # the plain rung (one pack per branch) when the device keeps the reserve free after the
+            # branch's activations: per token, every layer saves about 16 hidden-width bf16 rows
+            n_tok = sum(len(x) for t in trajs for x, _ in t.turns)
+            need = n_tok * self.spec.n_layers * self.spec.hidden * 2 * 16
+            free, _ = torch.cuda.mem_get_info(self.device)
+            if free - need >= self.rebuild_plain_reserve_bytes:
+                block = None
         toks = []
         masks = []
         for t in trajs:
@@ -797,8 +813,13 @@ class StreamingRun:
             if node.boundary is not None:
                 pairs = [(r, a) for r, a in node.boundary.consume() if r.requires_grad]
                 if pairs:
+                    t0 = time.perf_counter() if self.shared_prefix_vjp_timing else 0.0
                     with self.capture_source(("shared_prefix", node.idx)), grad_sink(sink):
                         torch.autograd.backward([r for r, _ in pairs], [a for _, a in pairs])
+                    if self.shared_prefix_vjp_timing:
+                        if self.device.type == "cuda":
+                            torch.cuda.synchronize(self.device)
+                        self._shared_prefix_times.append(time.perf_counter() - t0)
                 node.boundary.release()
                 node.boundary = None
             node.finalized = True
@@ -812,8 +833,10 @@ class StreamingRun:
 
     def accumulate_parameter_adjoints(self, pairs, *, source: Any = None) -> None:
         if self.parameter_adjoint_reduction == "canonical_source":
+            dev = self._param_adjoint_device
             self._param_adjoint_staged.setdefault(source, []).extend(
-                (p, v.detach().float().clone()) for p, v in pairs
+                (p, v.detach().float().clone() if dev is None else v.detach().float().to(dev, copy=True))
+                for p, v in pairs
             )
             return
         with torch.no_grad():
@@ -837,9 +860,9 @@ class StreamingRun:
         with torch.no_grad():
             for p, v in acc.values():
                 if p.grad is None:
-                    p.grad = v.to(p.dtype)
+                    p.grad = v.to(device=p.device, dtype=p.dtype)
                 else:
-                    p.grad.add_(v.to(p.grad.dtype))
+                    p.grad.add_(v.to(device=p.grad.device, dtype=p.grad.dtype))
         self._param_adjoint_staged.clear()
 
     # ------------------------------------------------------------ lifecycle
@@ -937,14 +960,21 @@ class StreamingRun:
         return {
             "reduction": self.parameter_adjoint_reduction,
             "staged_sources": len(self._param_adjoint_staged),
+            "storage_device": None if self._param_adjoint_device is None else str(self._param_adjoint_device),
+            "staged_bytes": sum(v.numel() * v.element_size() for st in self._param_adjoint_staged.values()
+                                for _, v in st),
         }
 
     def shared_prefix_vjp_diagnostics(self) -> dict[str, Any]:
-        return {
+        out = {
             "backend": self.shared_prefix_vjp_backend,
             "nodes": len(self._shared),
             "finalized": sum(1 for n in self._shared if n.finalized),
         }
+        if self.shared_prefix_vjp_timing:  # wall seconds per shared-prefix backward (device-synchronised)
+            out["vjp_seconds"] = list(self._shared_prefix_times)
+            out["vjp_seconds_total"] = float(sum(self._shared_prefix_times))
+        return out
 
     def turn_memory_windows(self) -> list[dict[str, Any]]:
         return list(self._memory_windows)
