@@ -114,3 +114,58 @@ def test_turn_stream_rejects_bad_inputs():
         obj.assert_safe_to_step()
     with pytest.raises(ValueError):
         OPDTurnStream(StreamingRun(model, boundary_cut=True), model)
+
+
+def test_turn_packs_and_closure_cohorts_match_single_turns():
+    """Scored turns appended as cross-trajectory packs, and trajectories closed as one cohort, give the same
+    update as one turn / one close at a time (the OPD deferred-replay invariants)."""
+    model = build_model(8).eval()
+    eps = _episodes(3, groups=2, per_group=2)
+    res = []
+    for packed in (False, True):
+        m = copy.deepcopy(model)
+        run = StreamingRun(m, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True)
+        obj = OPDTurnStream(run, m)
+        for g, prompt, _ in eps:
+            obj.open_group(g, prompt)
+        queues = [(g, tid, list(turns)) for g, _, trajs in eps for tid, turns in trajs]
+        while any(q[2] for q in queues):
+            items = []
+            for g, tid, turns in queues:
+                if turns:
+                    tk, sc, teacher = turns.pop(0)
+                    items.append((g, tid, tk, sc, teacher, None))
+            if packed:
+                obj.append_scored_turns(items)
+            else:
+                for g, tid, tk, sc, teacher, _ in items:
+                    obj.append_scored_turn(g, tid, tk, sc, teacher_logprobs=teacher)
+        for g, _, trajs in eps:
+            if packed:
+                obj.close_trajectories([tid for tid, _ in trajs])
+            else:
+                for tid, _ in trajs:
+                    obj.close_trajectory(tid)
+            obj.close_group(g)
+        obj.assert_safe_to_step()
+        res.append({n: p.grad.clone() for n, p in m.named_parameters()})
+    for n in res[0]:
+        torch.testing.assert_close(res[0][n], res[1][n], rtol=1e-5, atol=5e-6, msg=n)
+
+
+def test_turn_stream_refuses_duplicates_and_late_turns():
+    model = build_model(0).eval()
+    run = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True)
+    obj = OPDTurnStream(run, model)
+    obj.open_group(0, [1, 2, 3])
+    t = torch.tensor([-1.0])
+    with pytest.raises(ValueError, match="twice"):
+        obj.append_scored_turns([(0, 0, [4], [True], t, None), (0, 0, [5], [True], t, None)])
+    with pytest.raises(ValueError):
+        obj.append_scored_turns([])
+    obj.append_scored_turn(0, 0, [4, 6], [True, False], teacher_logprobs=t)
+    obj.close_trajectory(0)
+    with pytest.raises(RuntimeError, match="closed"):
+        obj.append_scored_turn(0, 0, [7], [True], teacher_logprobs=t)
+    with pytest.raises(ValueError, match="twice"):
+        obj.close_trajectories([1, 1])
