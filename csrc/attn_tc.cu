@@ -653,6 +653,323 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
   }
 }
 
+// dK/dV for head dims 64 and 128 with 128-query steps (every MMA is 128 x 128 x 16 or wider: narrower MMAs
+// leave the tensor pipe idle between instructions). Per step (query head, 128-query tile):
+//   S^T = K Q^T and dP^T = V dO^T (A = K / V from shared memory) into two 128-column TMEM regions;
+//   the compute warps load S^T, form P^T = exp2(S^T*sl2 - lse2) and write it back as bf16 pairs over the
+//   first 64 columns of the S^T region; the MMA thread accumulates dV += P^T dO with P^T as a
+//   tensor-memory A operand; meanwhile the compute warps load dP^T and write dS^T = P^T (dP^T - delta) the
+//   same way, and the MMA thread accumulates dK += dS^T Q.
+// MMA issue order dV(i), S(i+1), dK(i), dP(i+1): the tensor pipe computes S(i+1) while the compute warps
+// form dS(i), and dP(i+1) / dV(i+1) while they form P(i+1). MMAs from one thread run in issue order, so
+// S(i+1) overwrites P^T(i) only after dV(i) has read it. Q/dO tiles run NQ stages ahead.
+template <int D>
+struct DkvTLayout {
+  static constexpr int BN = 128, BQ = 128, NB = D / 64, NQ = D <= 64 ? 4 : 2;
+  static constexpr uint32_t KV_BYTES = BN * D * 2;
+  static constexpr uint32_t QT_BYTES = BQ * D * 2;
+  static constexpr uint32_t K = 0, V = KV_BYTES;
+  static constexpr uint32_t Q0 = 2 * KV_BYTES;        // [NQ] Q tiles
+  static constexpr uint32_t O0 = Q0 + NQ * QT_BYTES;  // [NQ] dO tiles
+  static constexpr uint32_t LD0 = O0 + NQ * QT_BYTES; // [NQ][2][BQ] floats: lse2, delta
+  static constexpr uint32_t BAR = LD0 + NQ * 2 * BQ * 4;
+  static constexpr uint32_t TOTAL = BAR + 512;
+  static constexpr uint32_t DK_COL = 0, DV_COL = D, S_COL = 2 * D, DP_COL = 2 * D + BQ;
+  static_assert(DP_COL + BQ <= 512, "dK/dV tensor-memory columns");
+};
+static_assert(DkvTLayout<128>::TOTAL + 1024 <= 232448, "dK/dV shared memory exceeds 227 KB");
+static_assert(DkvTLayout<64>::TOTAL + 1024 <= 232448, "dK/dV shared memory exceeds 227 KB");
+
+struct DkvTBars {
+  uint64_t kv, q_full[4], q_empty[4], s_full, dp_full, p_full, ds_full, fin;
+  uint64_t s_read[4], dp_read[4];  // per TMEM sub-partition: warp (w & 3) has loaded its S^T / dP^T columns
+  uint32_t tmem_slot;
+  int abort;
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dk, bf16* __restrict__ dv,
+    float* __restrict__ part_k, float* __restrict__ part_v, int T, int S, int Hq, int Hkv, float scale,
+    int* __restrict__ err) {
+  using L = DkvTLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DkvTBars* bars = reinterpret_cast<DkvTBars*>(smem + L::BAR);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hk = blockIdx.y, nsplit = gridDim.z, grp = Hq / Hkv / nsplit;
+  const int hbase = hk * (Hq / Hkv) + blockIdx.z * grp;
+  const int k0 = blockIdx.x * L::BN;
+  const int off = S - T;
+  const float sl2 = scale * kLog2e;
+  int qstart = k0 - off;
+  if (qstart < 0) qstart = 0;
+  qstart = (qstart / L::BQ) * L::BQ;
+  const int n_qt = qstart < T ? (T - qstart + L::BQ - 1) / L::BQ : 0;
+  const int total = n_qt * grp;
+  volatile int* abort = &bars->abort;
+  float* ld = reinterpret_cast<float*>(smem + L::LD0);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bars->kv, 1);
+    for (int i = 0; i < L::NQ; ++i) {
+      tc::mbar_init(&bars->q_full[i], 2);
+      tc::mbar_init(&bars->q_empty[i], 1);
+    }
+    tc::mbar_init(&bars->s_full, 1);
+    tc::mbar_init(&bars->dp_full, 1);
+    tc::mbar_init(&bars->p_full, 256);
+    tc::mbar_init(&bars->ds_full, 256);
+    tc::mbar_init(&bars->fin, 1);
+    for (int i = 0; i < 4; ++i) {
+      tc::mbar_init(&bars->s_read[i], 32);
+      tc::mbar_init(&bars->dp_read[i], 32);
+    }
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 8) {
+    // producer: K, V once; per step Q and dO tiles (TMA) plus lse2 / delta (plain loads, issued for the
+    // next step before waiting for its stage so their latency overlaps the wait)
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars->kv, 2 * L::KV_BYTES);
+      for (int b = 0; b < L::NB; ++b) {
+        tc::tma_load_2d(smem + L::K + b * L::BN * 128, &tm_k, hk * D + b * 64, k0, &bars->kv);
+        tc::tma_load_2d(smem + L::V + b * L::BN * 128, &tm_v, hk * D + b * 64, k0, &bars->kv);
+      }
+    }
+    constexpr int PER = L::BQ / 32;
+    float nl[PER], nd[PER];
+    auto fetch = [&](int i) {
+      const int hh = hbase + i / n_qt;
+      const int qt = qstart + (i % n_qt) * L::BQ;
+#pragma unroll
+      for (int x = 0; x < PER; ++x) {
+        const int qi = qt + x * 32 + lane;
+        nl[x] = qi < T ? lse[(long long)hh * T + qi] : 0.f;
+        nd[x] = qi < T ? delta[(long long)hh * T + qi] : 0.f;
+      }
+    };
+    if (total > 0) fetch(0);
+    for (int i = 0; i < total; ++i) {
+      const int qs = i % L::NQ;
+      if (i >= L::NQ && !warp_wait(&bars->q_empty[qs], ((i - L::NQ) / L::NQ) & 1, abort, err, 151)) break;
+      const int hh = hbase + i / n_qt;
+      const int qt = qstart + (i % n_qt) * L::BQ;
+      if (lane == 0) {
+        tc::mbar_expect_tx(&bars->q_full[qs], 2 * L::QT_BYTES);
+        for (int b = 0; b < L::NB; ++b) {
+          tc::tma_load_2d(smem + L::Q0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_q, hh * D + b * 64, qt,
+                          &bars->q_full[qs]);
+          tc::tma_load_2d(smem + L::O0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qt,
+                          &bars->q_full[qs]);
+        }
+      }
+#pragma unroll
+      for (int x = 0; x < PER; ++x) {
+        ld[(qs * 2 + 0) * L::BQ + x * 32 + lane] = nl[x] * kLog2e;
+        ld[(qs * 2 + 1) * L::BQ + x * 32 + lane] = nd[x];
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->q_full[qs]);
+      if (i + 1 < total) fetch(i + 1);
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      const uint32_t id_s = tc::idesc_bf16(128, L::BQ, false, false);
+      const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
+      // S^T / dP^T of one step: A = K or V (K-major, shared), B = Q or dO (K-major, shared)
+      auto mma_t = [&](uint32_t col, uint32_t a_base, uint32_t b_base) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t kv_off = (kk >> 2) * L::BN * 128 + (kk & 3) * 32;
+          const uint32_t q_off = (kk >> 2) * L::BQ * 128 + (kk & 3) * 32;
+          tc::mma_bf16(tmem + col, tc::sdesc_sw128(a_base + kv_off, 16, 1024),
+                       tc::sdesc_sw128(b_base + q_off, 16, 1024), id_s, kk > 0);
+        }
+      };
+      // dV / dK accumulation: A = P^T / dS^T (bf16 pairs in TMEM), B = dO / Q (MN-major, shared)
+      auto mma_acc = [&](uint32_t dcol, uint32_t acol, uint32_t b_base, bool first) {
+#pragma unroll
+        for (int kk = 0; kk < L::BQ / 16; ++kk)
+          tc::mma_bf16_ts(tmem + dcol, tmem + acol + kk * 8,
+                          tc::sdesc_sw128(b_base + kk * 16 * 128, L::BQ * 128, 1024), id_acc, !first || kk > 0);
+      };
+      bool ok = tc::mbar_wait(&bars->kv, 0, abort, err, 161);
+      if (ok && total > 0) {
+        ok = tc::mbar_wait(&bars->q_full[0], 0, abort, err, 162);
+        if (ok) {
+          tc::tc_fence_after();
+          mma_t(L::S_COL, sbase + L::K, sbase + L::Q0);
+          tc::mma_commit(&bars->s_full);
+          mma_t(L::DP_COL, sbase + L::V, sbase + L::O0);
+          tc::mma_commit(&bars->dp_full);
+        }
+      }
+      for (int i = 0; ok && i < total; ++i) {
+        const int qs = i % L::NQ, qn = (i + 1) % L::NQ;
+        const uint32_t qb = sbase + L::Q0 + qs * L::QT_BYTES, ob = sbase + L::O0 + qs * L::QT_BYTES;
+        if (!tc::mbar_wait(&bars->p_full, i & 1, abort, err, 163)) { ok = false; break; }
+        tc::tc_fence_after();
+        mma_acc(L::DV_COL, L::S_COL, ob, i == 0);
+        if (i + 1 < total) {
+          if (!tc::mbar_wait(&bars->q_full[qn], ((i + 1) / L::NQ) & 1, abort, err, 164)) { ok = false; break; }
+          tc::tc_fence_after();
+          mma_t(L::S_COL, sbase + L::K, sbase + L::Q0 + qn * L::QT_BYTES);
+          tc::mma_commit(&bars->s_full);
+        }
+        if (!tc::mbar_wait(&bars->ds_full, i & 1, abort, err, 165)) { ok = false; break; }
+        tc::tc_fence_after();
+        mma_acc(L::DK_COL, L::DP_COL, qb, i == 0);
+        tc::mma_commit(&bars->q_empty[qs]);
+        if (i + 1 < total) {
+          mma_t(L::DP_COL, sbase + L::V, sbase + L::O0 + qn * L::QT_BYTES);
+          tc::mma_commit(&bars->dp_full);
+        }
+      }
+      if (ok) tc::mma_commit(&bars->fin);
+    }
+  } else {
+    // warps 0-7: warp w reads TMEM lanes of sub-partition (w & 3) (key row r) and query columns
+    // [64 * (w >> 2), +64) of each step. The bf16 P^T / dS^T pairs of warp hc = 1 land on columns that
+    // warp hc = 0 of the same sub-partition reads, so it writes them once that warp has loaded its own.
+    const int sp = warp & 3, hc = warp >> 2;
+    const int r = sp * 32 + lane;
+    const int kr = k0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(sp * 32) << 16);
+    bool ok = true;
+    for (int i = 0; i < total && ok; ++i) {
+      const int qs = i % L::NQ;
+      const int qt = qstart + (i % n_qt) * L::BQ;
+      const int qc0 = qt + hc * 64;
+      const int lo = kr < S ? kr - off - qc0 : 64;  // query qc0+c sees key kr iff c >= lo
+      const int hi = T - qc0;                       // and c < hi (query exists)
+      const float* l2p = ld + (qs * 2 + 0) * L::BQ + hc * 64;
+      const float* dlp = ld + (qs * 2 + 1) * L::BQ + hc * 64;
+      if (!warp_wait(&bars->q_full[qs], (i / L::NQ) & 1, abort, err, 171)) { ok = false; break; }
+      if (!warp_wait(&bars->s_full, i & 1, abort, err, 172)) { ok = false; break; }
+      tc::tc_fence_after();
+      float p[64];
+      tc::tmem_ld32(lane_base + L::S_COL + hc * 64, p);
+      tc::tmem_ld32(lane_base + L::S_COL + hc * 64 + 32, p + 32);
+      tc::tmem_ld_wait();
+      if (hc == 0) {
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars->s_read[sp]);
+      }
+#pragma unroll
+      for (int c4 = 0; c4 < 16; ++c4) {
+        const float4 l = *reinterpret_cast<const float4*>(l2p + c4 * 4);
+        const float lv[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = c4 * 4 + e;
+          p[c] = (c >= lo && c < hi) ? ex2(fmaf(p[c], sl2, -lv[e])) : 0.f;
+        }
+      }
+      if (hc == 1 && !warp_wait(&bars->s_read[sp], i & 1, abort, err, 173)) { ok = false; break; }
+      tc::tc_fence_after();
+      {
+        float w[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = __uint_as_float(pack2(p[2 * j], p[2 * j + 1]));
+        tc::tmem_st32(lane_base + L::S_COL + hc * 32, w);
+      }
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->p_full);
+
+      if (!warp_wait(&bars->dp_full, i & 1, abort, err, 174)) { ok = false; break; }
+      tc::tc_fence_after();
+      {
+        float dp[64];
+        tc::tmem_ld32(lane_base + L::DP_COL + hc * 64, dp);
+        tc::tmem_ld32(lane_base + L::DP_COL + hc * 64 + 32, dp + 32);
+        tc::tmem_ld_wait();
+        if (hc == 0) {
+          tc::tc_fence_before();
+          tc::mbar_arrive(&bars->dp_read[sp]);
+        }
+#pragma unroll
+        for (int c4 = 0; c4 < 16; ++c4) {
+          const float4 d = *reinterpret_cast<const float4*>(dlp + c4 * 4);
+          p[c4 * 4 + 0] *= dp[c4 * 4 + 0] - d.x;
+          p[c4 * 4 + 1] *= dp[c4 * 4 + 1] - d.y;
+          p[c4 * 4 + 2] *= dp[c4 * 4 + 2] - d.z;
+          p[c4 * 4 + 3] *= dp[c4 * 4 + 3] - d.w;
+        }
+      }
+      if (hc == 1 && !warp_wait(&bars->dp_read[sp], i & 1, abort, err, 175)) { ok = false; break; }
+      tc::tc_fence_after();
+      {
+        float w[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = __uint_as_float(pack2(p[2 * j], p[2 * j + 1]));
+        tc::tmem_st32(lane_base + L::DP_COL + hc * 32, w);
+      }
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->ds_full);
+    }
+    if (ok && total > 0 && warp_wait(&bars->fin, 0, abort, err, 176)) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
+        float a[32], b[32];
+        tc::tmem_ld32(lane_base + L::DK_COL + c * 32, a);
+        tc::tmem_ld32(lane_base + L::DV_COL + c * 32, b);
+        tc::tmem_ld_wait();
+        if (kr < S && nsplit > 1) {
+          const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 4) {
+            *reinterpret_cast<float4*>(part_k + o + x) = make_float4(a[x], a[x + 1], a[x + 2], a[x + 3]);
+            *reinterpret_cast<float4*>(part_v + o + x) = make_float4(b[x], b[x + 1], b[x + 2], b[x + 3]);
+          }
+        } else if (kr < S) {
+          bf16* pk = dk + ((long long)kr * Hkv + hk) * D + c * 32;
+          bf16* pv = dv + ((long long)kr * Hkv + hk) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 u, w;
+            u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
+            u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
+            w.x = pack2(b[x], b[x + 1]); w.y = pack2(b[x + 2], b[x + 3]);
+            w.z = pack2(b[x + 4], b[x + 5]); w.w = pack2(b[x + 6], b[x + 7]);
+            *reinterpret_cast<uint4*>(pk + x) = u;
+            *reinterpret_cast<uint4*>(pv + x) = w;
+          }
+        }
+      }
+    } else if (ok && total == 0 && kr < S && nsplit > 1) {
+      const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D;
+      for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 4) {
+        *reinterpret_cast<float4*>(part_k + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(part_v + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    } else if (ok && total == 0 && kr < S) {
+      for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 8) {
+        *reinterpret_cast<uint4*>(dk + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(dv + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
 // dQ: CTA = 128 queries of one head; thread r of warps 0-3 owns query row r.
 // Per 64-key tile: S = Q K^T and dP = dO V^T into a TMEM buffer pair, the
 // compute warps form dS = P (dP - delta) (bf16, K-major), the MMA thread
@@ -1106,16 +1423,11 @@ at::Tensor attn_trace_read() {
 }
 
 namespace {
-template <int D, int MODE>
-void launch_dkdv(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
-                 const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dk, at::Tensor& dv, int T, int S, int Hq,
-                 int Hkv, double scale, int* err) {
-  // split the query heads of a KV head across CTAs when that fills the SMs'
-  // waves markedly better (the split costs an fp32 partial round trip and a
-  // sum kernel): e.g. 168 CTAs on 148 SMs run as two waves at 57% occupancy,
-  // 336 as three at 76%
-  const int grp = Hq / Hkv;
-  const int sms = sm_count(dk.get_device());
+// Split the query heads of a KV head across CTAs when that fills the SMs' waves markedly better (the split
+// costs an fp32 partial round trip and a sum kernel): e.g. 168 CTAs on 148 SMs run as two waves at 57%
+// occupancy, 336 as three at 76%.
+int dkdv_split(const dim3& g, int grp, int device) {
+  const int sms = sm_count(device);
   const int ctas = (int)(g.x * g.y);
   auto util = [&](int n) {
     const int c = ctas * n;
@@ -1129,6 +1441,43 @@ void launch_dkdv(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUt
       nsplit = n;
     }
   }
+  return nsplit;
+}
+
+template <int D>
+void launch_dkdv_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                   const CUtensorMap& mo, const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dk,
+                   at::Tensor& dv, int T, int S, int Hq, int Hkv, double scale, int* err) {
+  const int nsplit = dkdv_split(g, Hq / Hkv, dk.get_device());
+  g.z = nsplit;
+  at::Tensor pk, pv;
+  float* ppk = nullptr;
+  float* ppv = nullptr;
+  if (nsplit > 1) {
+    pk = at::empty({nsplit, S, Hkv, D}, dk.options().dtype(at::kFloat));
+    pv = at::empty({nsplit, S, Hkv, D}, dv.options().dtype(at::kFloat));
+    ppk = pk.data_ptr<float>();
+    ppv = pv.data_ptr<float>();
+  }
+  const int smem = DkvTLayout<D>::TOTAL + 1024;
+  ensure_smem((const void*)attn_bwd_dkdv_t_kernel<D>, smem);
+  attn_bwd_dkdv_t_kernel<D><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
+                                                        delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
+                                                        (bf16*)dv.data_ptr(), ppk, ppv, T, S, Hq, Hkv, (float)scale,
+                                                        err);
+  if (nsplit > 1) {
+    const long long n = (long long)S * Hkv * D;
+    const int blocks = (int)((n / 4 + 255) / 256);
+    attn_split_sum_kernel<<<blocks, 256, 0, stream()>>>(ppk, (bf16*)dk.data_ptr(), n, nsplit, (float)scale);
+    attn_split_sum_kernel<<<blocks, 256, 0, stream()>>>(ppv, (bf16*)dv.data_ptr(), n, nsplit, 1.f);
+  }
+}
+
+template <int D, int MODE>
+void launch_dkdv(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+                 const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dk, at::Tensor& dv, int T, int S, int Hq,
+                 int Hkv, double scale, int* err) {
+  const int nsplit = dkdv_split(g, Hq / Hkv, dk.get_device());
   g.z = nsplit;
   at::Tensor pk, pv;
   float* ppk = nullptr;
@@ -1200,10 +1549,10 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
   CUtensorMap mv_t = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, bn);
   dim3 g1((S + 127) / 128, Hkv), g2((T + 127) / 128, Hq);
   if (D == 128) {
-    launch_dkdv<128, 0>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
+    launch_dkdv_t<128>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
     launch_dq<128>(g2, mq128, mk_t, mv_t, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   } else if (D == 64) {
-    launch_dkdv<64, 0>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
+    launch_dkdv_t<64>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
     launch_dq<64>(g2, mq128, mk_t, mv_t, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   } else {
     launch_dkdv<256, 1>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);

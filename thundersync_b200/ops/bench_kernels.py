@@ -56,6 +56,13 @@ def bench_attn(args) -> None:
         do = torch.randn(o.shape, device="cuda", dtype=torch.bfloat16, generator=g)
         ms = _time(lambda: ext.attn_bwd_tc(do, q, k, v, o, lse, scale), args.iters)
         print(f"attn bwd: {ms:.3f} ms  {2.5 * flops / ms / 1e9:.1f} TFLOP/s (5 GEMM-equivalents)")
+        if args.kernels:  # device time of each kernel of one backward
+            from torch.profiler import ProfilerActivity, profile
+
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                ext.attn_bwd_tc(do, q, k, v, o, lse, scale)
+                torch.cuda.synchronize()
+            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=8, max_name_column_width=60))
         if args.trace:
             ext.attn_trace_enable(True)
             ext.attn_bwd_tc(do, q, k, v, o, lse, scale)
@@ -502,6 +509,7 @@ def main(argv=None) -> None:
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--trace", action="store_true", help="print the dK/dV kernel's per-step timeline")
+    ap.add_argument("--kernels", action="store_true", help="attn: per-kernel device times of one backward")
     args = ap.parse_args(argv)
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
      "gemm_host": bench_gemm_host, "swiglu": bench_swiglu, "rope": bench_rope, "dlogits": bench_dlogits,
