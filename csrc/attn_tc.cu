@@ -1223,6 +1223,254 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
   }
 }
 
+// dQ for head dims 64 and 128 with 128-key steps (MMAs of N = 128). CTA = 128 queries of one head; thread
+// r of warps 0-3 owns query row r. The CTA's Q and dO tiles sit in tensor memory as A operands of
+// S = Q K^T and dP = dO V^T (two 128-column TMEM regions); the compute warps load S, release its region,
+// exponentiate, load dP and write dS = P (dP - delta) back as bf16 pairs over the first 64 columns of the
+// dP region, where the MMA thread reads it as the A operand of dQ += dS K.
+// MMA issue order S(j+1), dQ(j), dP(j+1): S(j+1) runs while the compute warps exponentiate S(j), and
+// dQ(j) / dP(j+1) while they exponentiate S(j+1). K/V tiles run NK stages ahead.
+template <int D>
+struct DqTLayout {
+  static constexpr int BM = 128, BN = 128, NB = D / 64, NK = D <= 64 ? 4 : 2;
+  static constexpr uint32_t Q_BYTES = BM * D * 2;
+  static constexpr uint32_t KT_BYTES = BN * D * 2;
+  static constexpr uint32_t Q = 0, O = Q_BYTES;
+  static constexpr uint32_t K0 = 2 * Q_BYTES;         // [NK] K tiles
+  static constexpr uint32_t V0 = K0 + NK * KT_BYTES;  // [NK] V tiles
+  static constexpr uint32_t BAR = V0 + NK * KT_BYTES;
+  static constexpr uint32_t TOTAL = BAR + 512;
+  static constexpr uint32_t DQ_COL = 0, S_COL = D, DP_COL = D + BN, QTM_COL = D + 2 * BN, OTM_COL = QTM_COL + D / 2;
+  static_assert(OTM_COL + D / 2 <= 512, "dQ tensor-memory columns");
+};
+static_assert(DqTLayout<128>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
+static_assert(DqTLayout<64>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
+
+struct DqTBars {
+  uint64_t q, kv_full[4], kv_empty[4], s_full, dp_full, s_free, ds_full, fin, qo_tm;
+  uint64_t dp_read[4];  // per TMEM sub-partition: warp (w & 3) has loaded its dP columns
+  uint32_t tmem_slot;
+  int abort;
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T, int S, int Hq,
+    int Hkv, float scale, int* __restrict__ err) {
+  using L = DqTLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DqTBars* bars = reinterpret_cast<DqTBars*>(smem + L::BAR);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (T + L::BM - 1) / L::BM;
+  const int qt = n_qt - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, hk = h / (Hq / Hkv);
+  const int q0 = qt * L::BM;
+  const int off = S - T;
+  const int kv_end = min(S, q0 + L::BM + off);
+  const int n = (kv_end + L::BN - 1) / L::BN;
+  const float sl2 = scale * kLog2e;
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bars->q, 1);
+    for (int i = 0; i < L::NK; ++i) {
+      tc::mbar_init(&bars->kv_full[i], 1);
+      tc::mbar_init(&bars->kv_empty[i], 1);
+    }
+    tc::mbar_init(&bars->s_full, 1);
+    tc::mbar_init(&bars->dp_full, 1);
+    tc::mbar_init(&bars->s_free, 256);
+    tc::mbar_init(&bars->ds_full, 256);
+    tc::mbar_init(&bars->fin, 1);
+    tc::mbar_init(&bars->qo_tm, 128);
+    for (int i = 0; i < 4; ++i) tc::mbar_init(&bars->dp_read[i], 32);
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars->q, 2 * L::Q_BYTES);
+      for (int b = 0; b < L::NB; ++b) {
+        tc::tma_load_2d(smem + L::Q + b * L::BM * 128, &tm_q, h * D + b * 64, q0, &bars->q);
+        tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, q0, &bars->q);
+      }
+      for (int j = 0; j < n; ++j) {
+        const int ks = j % L::NK;
+        if (j >= L::NK && !tc::mbar_wait(&bars->kv_empty[ks], ((j - L::NK) / L::NK) & 1, abort, err, 181)) break;
+        tc::mbar_expect_tx(&bars->kv_full[ks], 2 * L::KT_BYTES);
+        for (int b = 0; b < L::NB; ++b) {
+          tc::tma_load_2d(smem + L::K0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN,
+                          &bars->kv_full[ks]);
+          tc::tma_load_2d(smem + L::V0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
+                          &bars->kv_full[ks]);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
+      const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
+      // S = Q K^T or dP = dO V^T: A = Q / dO (tensor memory), B = K / V tile (K-major, shared)
+      auto mma_s = [&](uint32_t col, uint32_t a_col, uint32_t b_base) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_bf16_ts(tmem + col, tmem + a_col + kk * 8,
+                          tc::sdesc_sw128(b_base + (kk >> 2) * L::BN * 128 + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
+      };
+      bool ok = tc::mbar_wait(&bars->q, 0, abort, err, 191);
+      ok = ok && tc::mbar_wait(&bars->qo_tm, 0, abort, err, 192);
+      if (ok && n > 0) {
+        ok = tc::mbar_wait(&bars->kv_full[0], 0, abort, err, 193);
+        if (ok) {
+          tc::tc_fence_after();
+          mma_s(L::S_COL, L::QTM_COL, sbase + L::K0);
+          tc::mma_commit(&bars->s_full);
+          mma_s(L::DP_COL, L::OTM_COL, sbase + L::V0);
+          tc::mma_commit(&bars->dp_full);
+        }
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        const int ks = j % L::NK, kn = (j + 1) % L::NK;
+        if (j + 1 < n) {
+          if (!tc::mbar_wait(&bars->s_free, j & 1, abort, err, 194)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars->kv_full[kn], ((j + 1) / L::NK) & 1, abort, err, 195)) { ok = false; break; }
+          tc::tc_fence_after();
+          mma_s(L::S_COL, L::QTM_COL, sbase + L::K0 + kn * L::KT_BYTES);
+          tc::mma_commit(&bars->s_full);
+        }
+        if (!tc::mbar_wait(&bars->ds_full, j & 1, abort, err, 196)) { ok = false; break; }
+        tc::tc_fence_after();
+        const uint32_t kb = sbase + L::K0 + ks * L::KT_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < L::BN / 16; ++kk)
+          tc::mma_bf16_ts(tmem + L::DQ_COL, tmem + L::DP_COL + kk * 8,
+                          tc::sdesc_sw128(kb + kk * 16 * 128, L::BN * 128, 1024), id_acc, j > 0 || kk > 0);
+        tc::mma_commit(&bars->kv_empty[ks]);
+        if (j + 1 < n) {
+          mma_s(L::DP_COL, L::OTM_COL, sbase + L::V0 + kn * L::KT_BYTES);
+          tc::mma_commit(&bars->dp_full);
+        }
+      }
+      if (ok) tc::mma_commit(&bars->fin);
+    }
+  } else {
+    // warps 0-7: sub-partition (w & 3) rows, key columns [64 * (w >> 2), +64) of each step. The bf16 dS
+    // pairs of warp hc = 1 land on dP columns that warp hc = 0 of the same sub-partition reads, so it
+    // writes them once that warp has loaded its own.
+    const int sp = warp & 3, hc = warp >> 2;
+    const int r = sp * 32 + lane;
+    const int qi = q0 + r;
+    const int lim = qi + off;
+    const float l2 = qi < T ? lse[(long long)h * T + qi] * kLog2e : 0.f;
+    const float dl = qi < T ? delta[(long long)h * T + qi] : 0.f;
+    const uint32_t lane_base = tmem + ((uint32_t)(sp * 32) << 16);
+    bool ok = true;
+    // warps 0-3: copy this row of the Q and dO tiles (K-major, 128B-swizzled in shared memory) into the
+    // A-operand columns of tensor memory, bf16 pairs per 32-bit column
+    if (hc == 0) {
+      if (warp_wait(&bars->q, 0, abort, err, 204)) {
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          const uint32_t base = sbase + (which ? L::O : L::Q);
+#pragma unroll
+          for (int c0 = 0; c0 < D; c0 += 64) {
+            float w[32];
+#pragma unroll
+            for (int q8 = 0; q8 < 8; ++q8) {
+              uint32_t a, b, c, d;
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n"
+                           : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+                           : "r"(base + tc::kmajor_off(r, c0 + q8 * 8, L::BM)));
+              w[q8 * 4 + 0] = __uint_as_float(a);
+              w[q8 * 4 + 1] = __uint_as_float(b);
+              w[q8 * 4 + 2] = __uint_as_float(c);
+              w[q8 * 4 + 3] = __uint_as_float(d);
+            }
+            tc::tmem_st32(lane_base + (which ? L::OTM_COL : L::QTM_COL) + c0 / 2, w);
+          }
+        }
+        tc::tmem_st_wait();
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->qo_tm);
+    }
+    for (int j = 0; j < n && ok; ++j) {
+      if (!warp_wait(&bars->s_full, j & 1, abort, err, 201)) { ok = false; break; }
+      tc::tc_fence_after();
+      float p[64];
+      tc::tmem_ld32(lane_base + L::S_COL + hc * 64, p);
+      tc::tmem_ld32(lane_base + L::S_COL + hc * 64 + 32, p + 32);
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->s_free);
+      const int kc0 = j * L::BN + hc * 64;
+      // key kc0+c is visible iff c < nvis (key <= lim, key < S, query exists)
+      const int nvis = qi < T ? min(lim, S - 1) - kc0 + 1 : 0;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) p[c] = c < nvis ? ex2(fmaf(p[c], sl2, -l2)) : 0.f;
+      if (!warp_wait(&bars->dp_full, j & 1, abort, err, 202)) { ok = false; break; }
+      tc::tc_fence_after();
+      {
+        float dp[64];
+        tc::tmem_ld32(lane_base + L::DP_COL + hc * 64, dp);
+        tc::tmem_ld32(lane_base + L::DP_COL + hc * 64 + 32, dp + 32);
+        tc::tmem_ld_wait();
+        if (hc == 0) {
+          tc::tc_fence_before();
+          tc::mbar_arrive(&bars->dp_read[sp]);
+        }
+#pragma unroll
+        for (int c = 0; c < 64; ++c) p[c] *= dp[c] - dl;
+      }
+      if (hc == 1 && !warp_wait(&bars->dp_read[sp], j & 1, abort, err, 203)) { ok = false; break; }
+      tc::tc_fence_after();
+      {
+        float w[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) w[x] = __uint_as_float(pack2(p[2 * x], p[2 * x + 1]));
+        tc::tmem_st32(lane_base + L::DP_COL + hc * 32, w);
+      }
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->ds_full);
+    }
+    if (ok && warp_wait(&bars->fin, 0, abort, err, 205)) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
+        float a[32];
+        tc::tmem_ld32(lane_base + L::DQ_COL + c * 32, a);
+        tc::tmem_ld_wait();
+        if (qi < T) {
+          bf16* pq = dq + ((long long)qi * Hq + h) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 u;
+            u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
+            u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
+            *reinterpret_cast<uint4*>(pq + x) = u;
+          }
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
 // ------------------------------------------------------------------ self-test
 // D1 = A * Bk^T (Bk [N][K], K-major), D2 = A * Bm (Bm [K][N], MN-major); 128x128x128.
 __global__ void __launch_bounds__(128, 1) tc_selftest_kernel(const __grid_constant__ CUtensorMap tm_a,
@@ -1501,6 +1749,17 @@ void launch_dkdv(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUt
 }
 
 template <int D>
+void launch_dq_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+                 const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, int T, int S, int Hq, int Hkv,
+                 double scale, int* err) {
+  const int smem = DqTLayout<D>::TOTAL + 1024;
+  ensure_smem((const void*)attn_bwd_dq_t_kernel<D>, smem);
+  attn_bwd_dq_t_kernel<D><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
+                                                      delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq, Hkv,
+                                                      (float)scale, err);
+}
+
+template <int D>
 void launch_dq(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
                const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, int T, int S, int Hq, int Hkv,
                double scale, int* err) {
@@ -1550,10 +1809,10 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
   dim3 g1((S + 127) / 128, Hkv), g2((T + 127) / 128, Hq);
   if (D == 128) {
     launch_dkdv_t<128>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
-    launch_dq<128>(g2, mq128, mk_t, mv_t, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
+    launch_dq_t<128>(g2, mq128, mk128, mv128, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   } else if (D == 64) {
     launch_dkdv_t<64>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
-    launch_dq<64>(g2, mq128, mk_t, mv_t, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
+    launch_dq_t<64>(g2, mq128, mk128, mv128, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   } else {
     launch_dkdv<256, 1>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
     launch_dkdv<256, 2>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
