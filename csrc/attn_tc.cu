@@ -351,16 +351,17 @@ __global__ void attn_split_sum_kernel(const float* __restrict__ part, bf16* __re
   *reinterpret_cast<uint2*>(out + i4) = o;
 }
 
-// dK/dV: CTA = 128 keys of one KV head; thread r of warps 0-3 owns key row r.
-// Per step (query head, 64-query tile): S^T = K Q^T and dP^T = V dO^T into a
+// dK/dV for head dim 256 (head dims 64 and 128 use attn_bwd_dkdv_t_kernel below).
+// CTA = 128 keys of one KV head; thread r of warps 0-3 owns key row r.
+// Per step (query head, query tile): S^T = K Q^T and dP^T = V dO^T into a
 // TMEM buffer pair; the compute warps form P^T = exp2(S^T*sl2 - lse2) and
 // dS^T = P^T (dP^T - delta) as bf16 K-major tiles; the MMA thread accumulates
 // dV += P^T dO and dK += dS^T Q into TMEM, which hold them across all steps.
 // Q/dO tiles run NQ stages ahead so their TMA latency stays off the MMA
 // thread's critical path; P^T/dS^T and the TMEM S^T/dP^T pairs are double
-// buffered. MODE 0 accumulates dK and dV together (head dims up to 128); for
-// D = 256 the two accumulators alone fill TMEM, so MODE 1 (dK) and MODE 2 (dV)
-// run as two launches over 32-query tiles, each keeping only the tile it needs.
+// buffered. MODE 0 accumulates dK and dV together; for D = 256 the two
+// accumulators alone fill TMEM, so MODE 1 (dK) and MODE 2 (dV) run as two
+// launches over 32-query tiles, each keeping only the tile it needs.
 template <int D, int MODE = 0>
 struct DkvLayout {
   static constexpr int BN = 128, BQ = D <= 128 ? 64 : 32, NB = D / 64, NQ = D <= 128 ? 3 : 2;
@@ -382,7 +383,6 @@ struct DkvLayout {
   static constexpr uint32_t ST_COL0 = MODE == 0 ? 2 * D : D;  // ST/DPT pairs follow
 };
 
-static_assert(DkvLayout<128>::TOTAL + 1024 <= 232448, "dK/dV shared memory exceeds 227 KB");
 static_assert(DkvLayout<256, 1>::TOTAL + 1024 <= 232448, "dK shared memory exceeds 227 KB");
 static_assert(DkvLayout<256, 2>::TOTAL + 1024 <= 232448, "dV shared memory exceeds 227 KB");
 
@@ -970,7 +970,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
   }
 }
 
-// dQ: CTA = 128 queries of one head; thread r of warps 0-3 owns query row r.
+// dQ for head dim 256 (head dims 64 and 128 use attn_bwd_dq_t_kernel below).
+// CTA = 128 queries of one head; thread r of warps 0-3 owns query row r.
 // Per 64-key tile: S = Q K^T and dP = dO V^T into a TMEM buffer pair, the
 // compute warps form dS = P (dP - delta) (bf16, K-major), the MMA thread
 // accumulates dQ += dS K into TMEM.
@@ -991,19 +992,12 @@ struct DqLayout {
   static constexpr uint32_t BAR = DS0 + 2 * DS_BYTES;
   static constexpr uint32_t TOTAL = BAR + 256;
   static constexpr uint32_t DQ_COL = 0, S_COL0 = D;
-  // head dims up to 128: the CTA's Q and dO tiles are copied once into the free TMEM columns and feed the
-  // S = Q K^T and dP = dO V^T MMAs as tensor-memory A operands, so those MMAs read only the K / V tiles from
-  // shared memory (with both operands in shared memory they need ~192 B/cycle of it, more than it delivers)
-  static constexpr bool A_TMEM = D <= 128;
-  static constexpr uint32_t QTM_COL = S_COL0 + 4 * BN, OTM_COL = QTM_COL + D / 2;
-  static_assert(!A_TMEM || OTM_COL + D / 2 <= 512, "dQ tensor-memory columns");
 };
 
-static_assert(DqLayout<128>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
 static_assert(DqLayout<256>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
 
 struct DqBars {
-  uint64_t q, kv_full[4], kv_empty[4], s_full[2], p_full[2], mma_done[2], fin, qo_tm;
+  uint64_t q, kv_full[4], kv_empty[4], s_full[2], p_full[2], mma_done[2], fin;
   uint32_t tmem_slot;
   int abort;
 };
@@ -1042,7 +1036,6 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
       tc::mbar_init(&bars->mma_done[i], 1);
     }
     tc::mbar_init(&bars->fin, 1);
-    tc::mbar_init(&bars->qo_tm, 128);
     bars->abort = 0;
     tc::fence_barrier_init();
   }
@@ -1075,10 +1068,6 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
       const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
       const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
       bool ok = tc::mbar_wait(&bars->q, 0, abort, err, 91);
-      if constexpr (L::A_TMEM) {
-        ok = ok && tc::mbar_wait(&bars->qo_tm, 0, abort, err, 94);
-        tc::tc_fence_after();
-      }
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1, ks = j % L::NK;
         if (!tc::mbar_wait(&bars->kv_full[ks], (j / L::NK) & 1, abort, err, 92)) return false;
@@ -1089,17 +1078,10 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t q_off = (kk >> 2) * L::BM * 128 + (kk & 3) * 32;
           const uint32_t k_off = (kk >> 2) * L::BN * 128 + (kk & 3) * 32;
-          if constexpr (L::A_TMEM) {
-            tc::mma_bf16_ts(tmem + col, tmem + L::QTM_COL + kk * 8, tc::sdesc_sw128(kb + k_off, 16, 1024), id_s,
-                            kk > 0);
-            tc::mma_bf16_ts(tmem + col + L::BN, tmem + L::OTM_COL + kk * 8, tc::sdesc_sw128(vb + k_off, 16, 1024),
-                            id_s, kk > 0);
-          } else {
-            tc::mma_bf16(tmem + col, tc::sdesc_sw128(sbase + L::Q + q_off, 16, 1024),
-                         tc::sdesc_sw128(kb + k_off, 16, 1024), id_s, kk > 0);
-            tc::mma_bf16(tmem + col + L::BN, tc::sdesc_sw128(sbase + L::O + q_off, 16, 1024),
-                         tc::sdesc_sw128(vb + k_off, 16, 1024), id_s, kk > 0);
-          }
+          tc::mma_bf16(tmem + col, tc::sdesc_sw128(sbase + L::Q + q_off, 16, 1024),
+                       tc::sdesc_sw128(kb + k_off, 16, 1024), id_s, kk > 0);
+          tc::mma_bf16(tmem + col + L::BN, tc::sdesc_sw128(sbase + L::O + q_off, 16, 1024),
+                       tc::sdesc_sw128(vb + k_off, 16, 1024), id_s, kk > 0);
         }
         tc::mma_commit(&bars->s_full[st]);
         return true;
@@ -1133,37 +1115,6 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
     const float dl = qi < T ? delta[(long long)h * T + qi] : 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool ok = true;
-    if constexpr (L::A_TMEM) {
-      // warps 0-3: copy this row of the Q and dO tiles (K-major, 128B-swizzled in shared memory) into the
-      // A-operand columns of tensor memory, bf16 pairs per 32-bit column
-      if (hc == 0) {
-        if (warp_wait(&bars->q, 0, abort, err, 104)) {
-#pragma unroll
-          for (int which = 0; which < 2; ++which) {
-            const uint32_t base = sbase + (which ? L::O : L::Q);
-#pragma unroll
-            for (int c0 = 0; c0 < D; c0 += 64) {
-              float w[32];
-#pragma unroll
-              for (int q8 = 0; q8 < 8; ++q8) {
-                uint32_t a, b, c, d;
-                asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n"
-                             : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
-                             : "r"(base + tc::kmajor_off(r, c0 + q8 * 8, L::BM)));
-                w[q8 * 4 + 0] = __uint_as_float(a);
-                w[q8 * 4 + 1] = __uint_as_float(b);
-                w[q8 * 4 + 2] = __uint_as_float(c);
-                w[q8 * 4 + 3] = __uint_as_float(d);
-              }
-              tc::tmem_st32(lane_base + (which ? L::OTM_COL : L::QTM_COL) + c0 / 2, w);
-            }
-          }
-          tc::tmem_st_wait();
-        }
-        tc::tc_fence_before();
-        tc::mbar_arrive(&bars->qo_tm);
-      }
-    }
     for (int j = 0; j < n && ok; ++j) {
       const int st = j & 1;
       if (!warp_wait(&bars->s_full[st], (j >> 1) & 1, abort, err, 101)) { ok = false; break; }

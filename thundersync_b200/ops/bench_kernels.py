@@ -508,7 +508,7 @@ def main(argv=None) -> None:
     ap.add_argument("--rows", type=int, default=16384)
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--trace", action="store_true", help="print the dK/dV kernel's per-step timeline")
+    ap.add_argument("--trace", action="store_true", help="print the head-dim-256 dK/dV kernel's per-step timeline")
     ap.add_argument("--kernels", action="store_true", help="attn: per-kernel device times of one backward")
     args = ap.parse_args(argv)
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
