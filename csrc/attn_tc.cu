@@ -970,210 +970,6 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
   }
 }
 
-// dQ for head dim 256 (head dims 64 and 128 use attn_bwd_dq_t_kernel below).
-// CTA = 128 queries of one head; thread r of warps 0-3 owns query row r.
-// Per 64-key tile: S = Q K^T and dP = dO V^T into a TMEM buffer pair, the
-// compute warps form dS = P (dP - delta) (bf16, K-major), the MMA thread
-// accumulates dQ += dS K into TMEM.
-// K/V tiles run NK = 4 stages ahead of the MMA thread; dS tiles and the TMEM
-// S/dP pairs are double buffered.
-template <int D>
-struct DqLayout {
-  // D = 256: 32-key tiles and 2 stages keep Q, dO and the K/V ring inside 227 KB
-  static constexpr int BM = 128, BN = D <= 128 ? 64 : 32, NB = D / 64, NK = D <= 128 ? 4 : 2;
-  static constexpr int CW = BN / 2;  // key columns per compute warp
-  static constexpr uint32_t Q_BYTES = BM * D * 2;
-  static constexpr uint32_t KT_BYTES = BN * D * 2;
-  static constexpr uint32_t Q = 0, O = Q_BYTES;
-  static constexpr uint32_t K0 = 2 * Q_BYTES;             // [NK] K tiles
-  static constexpr uint32_t V0 = K0 + NK * KT_BYTES;      // [NK] V tiles
-  static constexpr uint32_t DS0 = V0 + NK * KT_BYTES;     // [2] dS tiles (128 rows of 128 bytes)
-  static constexpr uint32_t DS_BYTES = BM * 64 * 2;
-  static constexpr uint32_t BAR = DS0 + 2 * DS_BYTES;
-  static constexpr uint32_t TOTAL = BAR + 256;
-  static constexpr uint32_t DQ_COL = 0, S_COL0 = D;
-};
-
-static_assert(DqLayout<256>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
-
-struct DqBars {
-  uint64_t q, kv_full[4], kv_empty[4], s_full[2], p_full[2], mma_done[2], fin;
-  uint32_t tmem_slot;
-  int abort;
-};
-
-template <int D>
-__global__ void __launch_bounds__(320, 1) attn_bwd_dq_tc_kernel(
-    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T, int S, int Hq,
-    int Hkv, float scale, int* __restrict__ err) {
-  using L = DqLayout<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  DqBars* bars = reinterpret_cast<DqBars*>(smem + L::BAR);
-  const uint32_t sbase = tc::smem_addr(smem);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_qt = (T + L::BM - 1) / L::BM;
-  const int qt = n_qt - 1 - (int)blockIdx.x;
-  const int h = blockIdx.y, hk = h / (Hq / Hkv);
-  const int q0 = qt * L::BM;
-  const int off = S - T;
-  const int kv_end = min(S, q0 + L::BM + off);
-  const int n = (kv_end + L::BN - 1) / L::BN;
-  const float sl2 = scale * kLog2e;
-  volatile int* abort = &bars->abort;
-
-  if (threadIdx.x == 0) {
-    tc::mbar_init(&bars->q, 1);
-    for (int i = 0; i < L::NK; ++i) {
-      tc::mbar_init(&bars->kv_full[i], 1);
-      tc::mbar_init(&bars->kv_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&bars->s_full[i], 1);
-      tc::mbar_init(&bars->p_full[i], 256);
-      tc::mbar_init(&bars->mma_done[i], 1);
-    }
-    tc::mbar_init(&bars->fin, 1);
-    bars->abort = 0;
-    tc::fence_barrier_init();
-  }
-  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
-  __syncthreads();
-  tc::tc_fence_after();
-  const uint32_t tmem = bars->tmem_slot;
-
-  if (warp == 8) {
-    if (lane == 0) {
-      tc::mbar_expect_tx(&bars->q, 2 * L::Q_BYTES);
-      for (int b = 0; b < L::NB; ++b) {
-        tc::tma_load_2d(smem + L::Q + b * L::BM * 128, &tm_q, h * D + b * 64, q0, &bars->q);
-        tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, q0, &bars->q);
-      }
-      for (int j = 0; j < n; ++j) {
-        const int ks = j % L::NK;
-        if (j >= L::NK && !tc::mbar_wait(&bars->kv_empty[ks], ((j - L::NK) / L::NK) & 1, abort, err, 81)) break;
-        tc::mbar_expect_tx(&bars->kv_full[ks], 2 * L::KT_BYTES);
-        for (int b = 0; b < L::NB; ++b) {
-          tc::tma_load_2d(smem + L::K0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN,
-                          &bars->kv_full[ks]);
-          tc::tma_load_2d(smem + L::V0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
-                          &bars->kv_full[ks]);
-        }
-      }
-    }
-  } else if (warp == 9) {
-    if (lane == 0) {
-      const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
-      const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
-      bool ok = tc::mbar_wait(&bars->q, 0, abort, err, 91);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1, ks = j % L::NK;
-        if (!tc::mbar_wait(&bars->kv_full[ks], (j / L::NK) & 1, abort, err, 92)) return false;
-        tc::tc_fence_after();
-        const uint32_t kb = sbase + L::K0 + ks * L::KT_BYTES, vb = sbase + L::V0 + ks * L::KT_BYTES;
-        const uint32_t col = L::S_COL0 + st * 2 * L::BN;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t q_off = (kk >> 2) * L::BM * 128 + (kk & 3) * 32;
-          const uint32_t k_off = (kk >> 2) * L::BN * 128 + (kk & 3) * 32;
-          tc::mma_bf16(tmem + col, tc::sdesc_sw128(sbase + L::Q + q_off, 16, 1024),
-                       tc::sdesc_sw128(kb + k_off, 16, 1024), id_s, kk > 0);
-          tc::mma_bf16(tmem + col + L::BN, tc::sdesc_sw128(sbase + L::O + q_off, 16, 1024),
-                       tc::sdesc_sw128(vb + k_off, 16, 1024), id_s, kk > 0);
-        }
-        tc::mma_commit(&bars->s_full[st]);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      if (ok && n > 1) ok = issue_s(1);
-      for (int j = 0; ok && j < n; ++j) {
-        const int st = j & 1, ks = j % L::NK;
-        if (!tc::mbar_wait(&bars->p_full[st], (j >> 1) & 1, abort, err, 93)) break;
-        tc::tc_fence_after();
-        const uint32_t db = sbase + L::DS0 + st * L::DS_BYTES;
-        const uint32_t kb = sbase + L::K0 + ks * L::KT_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < L::BN / 16; ++kk) {
-          tc::mma_bf16(tmem + L::DQ_COL, tc::sdesc_sw128(db + kk * 32, 16, 1024),
-                       tc::sdesc_sw128(kb + kk * 16 * 128, L::BN * 128, 1024), id_acc, j > 0 || kk > 0);
-        }
-        tc::mma_commit(&bars->mma_done[st]);
-        tc::mma_commit(&bars->kv_empty[ks]);
-        if (j + 2 < n) ok = issue_s(j + 2);
-      }
-      if (ok) tc::mma_commit(&bars->fin);
-    }
-  } else {
-    // warps 0-7: sub-partition (w & 3) rows, key columns [32 * (w >> 2), +32)
-    const int r = (warp & 3) * 32 + lane;
-    const int hc = warp >> 2;
-    const int qi = q0 + r;
-    const int lim = qi + off;
-    const float l2 = qi < T ? lse[(long long)h * T + qi] * kLog2e : 0.f;
-    const float dl = qi < T ? delta[(long long)h * T + qi] : 0.f;
-    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    bool ok = true;
-    for (int j = 0; j < n && ok; ++j) {
-      const int st = j & 1;
-      if (!warp_wait(&bars->s_full[st], (j >> 1) & 1, abort, err, 101)) { ok = false; break; }
-      if (j >= 2 && !warp_wait(&bars->mma_done[st], ((j - 2) >> 1) & 1, abort, err, 102)) { ok = false; break; }
-      tc::tc_fence_after();
-      constexpr int CW = L::CW;
-      float sv[CW], dp[CW];
-      const uint32_t col = L::S_COL0 + st * 2 * L::BN + hc * CW;
-      tc::tmem_ld<CW>(lane_base + col, sv);
-      tc::tmem_ld<CW>(lane_base + col + L::BN, dp);
-      tc::tmem_ld_wait();
-      const int k0 = j * L::BN + hc * CW;
-      // key k0+c is visible iff c < nvis (key <= lim, key < S, query exists)
-      const int nvis = qi < T ? min(lim, S - 1) - k0 + 1 : 0;
-      const uint32_t db = sbase + L::DS0 + st * L::DS_BYTES;
-#pragma unroll
-      for (int c8 = 0; c8 < CW / 8; ++c8) {
-        float ds[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int c = c8 * 8 + e;
-          const float p = c < nvis ? ex2(fmaf(sv[c], sl2, -l2)) : 0.f;
-          ds[e] = p * (dp[c] - dl);
-        }
-        st_shared_v4(db + tc::kmajor_off(r, hc * CW + c8 * 8, 128), pack2(ds[0], ds[1]), pack2(ds[2], ds[3]),
-                     pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
-      }
-      tc::fence_async_smem();
-      tc::tc_fence_before();
-      tc::mbar_arrive(&bars->p_full[st]);
-    }
-    if (ok && warp_wait(&bars->fin, 0, abort, err, 103)) {
-      tc::tc_fence_after();
-#pragma unroll
-      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
-        float a[32];
-        tc::tmem_ld32(lane_base + L::DQ_COL + c * 32, a);
-        tc::tmem_ld_wait();
-        if (qi < T) {
-          bf16* pq = dq + ((long long)qi * Hq + h) * D + c * 32;
-#pragma unroll
-          for (int x = 0; x < 32; x += 8) {
-            uint4 u;
-            u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
-            u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
-            *reinterpret_cast<uint4*>(pq + x) = u;
-          }
-        }
-      }
-    }
-  }
-  tc::tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, 512);
-  }
-}
-
 // dQ for head dims 64 and 128 with 128-key steps (MMAs of N = 128). CTA = 128 queries of one head; thread
 // r of warps 0-3 owns query row r. The CTA's Q and dO tiles sit in tensor memory as A operands of
 // S = Q K^T and dP = dO V^T (two 128-column TMEM regions); the compute warps load S, release its region,
@@ -1395,6 +1191,245 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
       tc::mbar_arrive(&bars->ds_full);
     }
     if (ok && warp_wait(&bars->fin, 0, abort, err, 205)) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
+        float a[32];
+        tc::tmem_ld32(lane_base + L::DQ_COL + c * 32, a);
+        tc::tmem_ld_wait();
+        if (qi < T) {
+          bf16* pq = dq + ((long long)qi * Hq + h) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 u;
+            u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
+            u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
+            *reinterpret_cast<uint4*>(pq + x) = u;
+          }
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ for head dim 256 with 64-key steps. TMEM columns: dQ [0, 256), the CTA's Q tile as the A operand of
+// S = Q K^T [256, 384), S [384, 448), dP [448, 512). dP = dO V^T takes dO from shared memory. The compute
+// warps load S (releasing its columns), exponentiate, load dP and write dS = P (dP - delta) back as bf16
+// pairs over the first 32 dP columns, where dQ += dS K (N = 256) reads it as its A operand. Shared memory
+// holds dO and two K/V stages (192 KB); Q arrives in the second stage's space and is copied to TMEM
+// before that stage takes K/V. MMA issue order S(j+1), dQ(j), dP(j+1), as in attn_bwd_dq_t_kernel.
+struct Dq256Layout {
+  static constexpr int D = 256, BM = 128, BN = 64, NB = 4, NK = 2;
+  static constexpr uint32_t Q_BYTES = BM * D * 2;     // 64 KB
+  static constexpr uint32_t KT_BYTES = BN * D * 2;    // 32 KB
+  static constexpr uint32_t ST_BYTES = 2 * KT_BYTES;  // one K/V stage
+  static constexpr uint32_t O = 0;
+  static constexpr uint32_t ST0 = Q_BYTES;            // [NK] stages: K tile, then V tile
+  static constexpr uint32_t QLOAD = ST0 + ST_BYTES;   // Q lands in stage 1 first
+  static constexpr uint32_t BAR = ST0 + NK * ST_BYTES;
+  static constexpr uint32_t TOTAL = BAR + 512;
+  static constexpr uint32_t DQ_COL = 0, QTM_COL = 256, S_COL = 384, DP_COL = 448;
+  static_assert(Q_BYTES == ST_BYTES, "Q is staged through one K/V stage");
+};
+static_assert(Dq256Layout::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 227 KB");
+
+template <int D_>
+__global__ void __launch_bounds__(320, 1) attn_bwd_dq256_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T, int S, int Hq,
+    int Hkv, float scale, int* __restrict__ err) {
+  using L = Dq256Layout;
+  constexpr int D = L::D;
+  static_assert(D_ == D, "head dim 256 only");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DqTBars* bars = reinterpret_cast<DqTBars*>(smem + L::BAR);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (T + L::BM - 1) / L::BM;
+  const int qt = n_qt - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, hk = h / (Hq / Hkv);
+  const int q0 = qt * L::BM;
+  const int off = S - T;
+  const int kv_end = min(S, q0 + L::BM + off);
+  const int n = (kv_end + L::BN - 1) / L::BN;
+  const float sl2 = scale * kLog2e;
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bars->q, 1);
+    for (int i = 0; i < L::NK; ++i) {
+      tc::mbar_init(&bars->kv_full[i], 1);
+      tc::mbar_init(&bars->kv_empty[i], 1);
+    }
+    tc::mbar_init(&bars->s_full, 1);
+    tc::mbar_init(&bars->dp_full, 1);
+    tc::mbar_init(&bars->s_free, 256);
+    tc::mbar_init(&bars->ds_full, 256);
+    tc::mbar_init(&bars->fin, 1);
+    tc::mbar_init(&bars->qo_tm, 128);
+    for (int i = 0; i < 4; ++i) tc::mbar_init(&bars->dp_read[i], 32);
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars->q, 2 * L::Q_BYTES);
+      for (int b = 0; b < L::NB; ++b) {
+        tc::tma_load_2d(smem + L::QLOAD + b * L::BM * 128, &tm_q, h * D + b * 64, q0, &bars->q);
+        tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, q0, &bars->q);
+      }
+      for (int j = 0; j < n; ++j) {
+        const int ks = j % L::NK;
+        if (j == 1 && !tc::mbar_wait(&bars->qo_tm, 0, abort, err, 211)) break;  // Q has left stage 1
+        if (j >= L::NK && !tc::mbar_wait(&bars->kv_empty[ks], ((j - L::NK) / L::NK) & 1, abort, err, 212)) break;
+        uint8_t* st = smem + L::ST0 + ks * L::ST_BYTES;
+        tc::mbar_expect_tx(&bars->kv_full[ks], 2 * L::KT_BYTES);
+        for (int b = 0; b < L::NB; ++b) {
+          tc::tma_load_2d(st + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN, &bars->kv_full[ks]);
+          tc::tma_load_2d(st + L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
+                          &bars->kv_full[ks]);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
+      const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
+      auto mma_s = [&](uint32_t kb) {  // S = Q K^T, A = Q from tensor memory
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_bf16_ts(tmem + L::S_COL, tmem + L::QTM_COL + kk * 8,
+                          tc::sdesc_sw128(kb + (kk >> 2) * L::BN * 128 + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
+      };
+      auto mma_dp = [&](uint32_t vb) {  // dP = dO V^T, A = dO from shared memory
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_bf16(tmem + L::DP_COL, tc::sdesc_sw128(sbase + L::O + (kk >> 2) * L::BM * 128 + (kk & 3) * 32, 16, 1024),
+                       tc::sdesc_sw128(vb + (kk >> 2) * L::BN * 128 + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
+      };
+      bool ok = tc::mbar_wait(&bars->q, 0, abort, err, 221);
+      ok = ok && tc::mbar_wait(&bars->qo_tm, 0, abort, err, 222);
+      if (ok && n > 0) {
+        ok = tc::mbar_wait(&bars->kv_full[0], 0, abort, err, 223);
+        if (ok) {
+          tc::tc_fence_after();
+          mma_s(sbase + L::ST0);
+          tc::mma_commit(&bars->s_full);
+          mma_dp(sbase + L::ST0 + L::KT_BYTES);
+          tc::mma_commit(&bars->dp_full);
+        }
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        const int ks = j % L::NK, kn = (j + 1) % L::NK;
+        const uint32_t sn = sbase + L::ST0 + kn * L::ST_BYTES;
+        if (j + 1 < n) {
+          if (!tc::mbar_wait(&bars->s_free, j & 1, abort, err, 224)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars->kv_full[kn], ((j + 1) / L::NK) & 1, abort, err, 225)) { ok = false; break; }
+          tc::tc_fence_after();
+          mma_s(sn);
+          tc::mma_commit(&bars->s_full);
+        }
+        if (!tc::mbar_wait(&bars->ds_full, j & 1, abort, err, 226)) { ok = false; break; }
+        tc::tc_fence_after();
+        const uint32_t kb = sbase + L::ST0 + ks * L::ST_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < L::BN / 16; ++kk)
+          tc::mma_bf16_ts(tmem + L::DQ_COL, tmem + L::DP_COL + kk * 8,
+                          tc::sdesc_sw128(kb + kk * 16 * 128, L::BN * 128, 1024), id_acc, j > 0 || kk > 0);
+        tc::mma_commit(&bars->kv_empty[ks]);
+        if (j + 1 < n) {
+          mma_dp(sn + L::KT_BYTES);
+          tc::mma_commit(&bars->dp_full);
+        }
+      }
+      if (ok) tc::mma_commit(&bars->fin);
+    }
+  } else {
+    // warps 0-7: sub-partition (w & 3) rows, key columns [32 * (w >> 2), +32) of each step; warp hc = 1
+    // writes its dS pairs over dP columns of warp hc = 0, once that warp has loaded them.
+    const int sp = warp & 3, hc = warp >> 2;
+    const int r = sp * 32 + lane;
+    const int qi = q0 + r;
+    const int lim = qi + off;
+    const float l2 = qi < T ? lse[(long long)h * T + qi] * kLog2e : 0.f;
+    const float dl = qi < T ? delta[(long long)h * T + qi] : 0.f;
+    const uint32_t lane_base = tmem + ((uint32_t)(sp * 32) << 16);
+    bool ok = true;
+    if (hc == 0) {
+      // warps 0-3: copy this row of Q (K-major, 128B-swizzled, in stage 1) into tensor memory
+      if (warp_wait(&bars->q, 0, abort, err, 234)) {
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 64) {
+          float w[32];
+#pragma unroll
+          for (int q8 = 0; q8 < 8; ++q8) {
+            uint32_t a, b, c, d;
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n"
+                         : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+                         : "r"(sbase + L::QLOAD + tc::kmajor_off(r, c0 + q8 * 8, L::BM)));
+            w[q8 * 4 + 0] = __uint_as_float(a);
+            w[q8 * 4 + 1] = __uint_as_float(b);
+            w[q8 * 4 + 2] = __uint_as_float(c);
+            w[q8 * 4 + 3] = __uint_as_float(d);
+          }
+          tc::tmem_st32(lane_base + L::QTM_COL + c0 / 2, w);
+        }
+        tc::tmem_st_wait();
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->qo_tm);
+    }
+    for (int j = 0; j < n && ok; ++j) {
+      if (!warp_wait(&bars->s_full, j & 1, abort, err, 231)) { ok = false; break; }
+      tc::tc_fence_after();
+      float p[32];
+      tc::tmem_ld32(lane_base + L::S_COL + hc * 32, p);
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->s_free);
+      const int kc0 = j * L::BN + hc * 32;
+      const int nvis = qi < T ? min(lim, S - 1) - kc0 + 1 : 0;  // key kc0+c visible iff c < nvis
+#pragma unroll
+      for (int c = 0; c < 32; ++c) p[c] = c < nvis ? ex2(fmaf(p[c], sl2, -l2)) : 0.f;
+      if (!warp_wait(&bars->dp_full, j & 1, abort, err, 232)) { ok = false; break; }
+      tc::tc_fence_after();
+      {
+        float dp[32];
+        tc::tmem_ld32(lane_base + L::DP_COL + hc * 32, dp);
+        tc::tmem_ld_wait();
+        if (hc == 0) {
+          tc::tc_fence_before();
+          tc::mbar_arrive(&bars->dp_read[sp]);
+        }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) p[c] *= dp[c] - dl;
+      }
+      if (hc == 1 && !warp_wait(&bars->dp_read[sp], j & 1, abort, err, 233)) { ok = false; break; }
+      tc::tc_fence_after();
+      {
+        float w[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x) w[x] = __uint_as_float(pack2(p[2 * x], p[2 * x + 1]));
+        tc::tmem_st16(lane_base + L::DP_COL + hc * 16, w);
+      }
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->ds_full);
+    }
+    if (ok && warp_wait(&bars->fin, 0, abort, err, 235)) {
       tc::tc_fence_after();
 #pragma unroll
       for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
@@ -1710,15 +1745,16 @@ void launch_dq_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUt
                                                       (float)scale, err);
 }
 
-template <int D>
-void launch_dq(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
-               const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, int T, int S, int Hq, int Hkv,
-               double scale, int* err) {
-  const int smem = DqLayout<D>::TOTAL + 1024;
-  ensure_smem((const void*)attn_bwd_dq_tc_kernel<D>, (int)(smem));
-  attn_bwd_dq_tc_kernel<D><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(), delta.data_ptr<float>(),
-                                                       (bf16*)dq.data_ptr(), T, S, Hq, Hkv, (float)scale, err);
+void launch_dq256(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+                  const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, int T, int S, int Hq, int Hkv,
+                  double scale, int* err) {
+  const int smem = Dq256Layout::TOTAL + 1024;
+  ensure_smem((const void*)attn_bwd_dq256_kernel<256>, smem);
+  attn_bwd_dq256_kernel<256><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
+                                                         delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq, Hkv,
+                                                         (float)scale, err);
 }
+
 }  // namespace
 
 // dq/dk/dv (optional): contiguous tensors shaped like q/k/v that receive the gradients.
@@ -1747,16 +1783,10 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
                                                                   (const bf16*)dout.data_ptr(),
                                                                   delta.data_ptr<float>(), T, Hq, D);
   int* err = tc_error_flag(q.device()).data_ptr<int>();
-  const uint32_t bq = D <= 128 ? 64 : 32;   // dK/dV query tile
-  const uint32_t bn = D <= 128 ? 64 : 32;   // dQ key tile
-  CUtensorMap mq_t = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, bq);
-  CUtensorMap mo_t = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, bq);
   CUtensorMap mk128 = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
   CUtensorMap mv128 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
   CUtensorMap mq128 = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
   CUtensorMap mo128 = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
-  CUtensorMap mk_t = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, bn);
-  CUtensorMap mv_t = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, bn);
   dim3 g1((S + 127) / 128, Hkv), g2((T + 127) / 128, Hq);
   if (D == 128) {
     launch_dkdv_t<128>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
@@ -1765,9 +1795,14 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
     launch_dkdv_t<64>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
     launch_dq_t<64>(g2, mq128, mk128, mv128, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   } else {
+    // dK/dV passes step over 32-query tiles, dQ over 64-key tiles
+    CUtensorMap mq_t = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 32);
+    CUtensorMap mo_t = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 32);
     launch_dkdv<256, 1>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
     launch_dkdv<256, 2>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
-    launch_dq<256>(g2, mq128, mk_t, mv_t, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
+    CUtensorMap mk64 = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
+    CUtensorMap mv64 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
+    launch_dq256(g2, mq128, mk64, mv64, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   }
   TS_LAUNCH_CHECK();
   return {dq, dk, dv};
