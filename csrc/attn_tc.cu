@@ -52,16 +52,6 @@ TS_DEVICE bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, in
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
-// Optional per-step timeline of one CTA (blockIdx 0,0) of the backward
-// kernels: clock64 stamps [role][step][event], switched on from the host for a
-// diagnostic run and off otherwise (one predicated branch per stamp).
-__device__ int g_attn_trace_on = 0;
-__device__ long long g_attn_trace[4 * 128 * 8];
-#define TS_TRACE(role, step, ev)                                                      \
-  do {                                                                                \
-    if (trace && (step) < 128) g_attn_trace[((role) * 128 + (step)) * 8 + (ev)] = clock64(); \
-  } while (0)
-
 template <int D>
 struct FwdLayout {
   // D = 256 halves the key tile so two K/V stages still fit in shared memory
@@ -349,308 +339,6 @@ __global__ void attn_split_sum_kernel(const float* __restrict__ part, bf16* __re
   o.x = pack2(acc.x * scale, acc.y * scale);
   o.y = pack2(acc.z * scale, acc.w * scale);
   *reinterpret_cast<uint2*>(out + i4) = o;
-}
-
-// dK/dV for head dim 256 (head dims 64 and 128 use attn_bwd_dkdv_t_kernel below).
-// CTA = 128 keys of one KV head; thread r of warps 0-3 owns key row r.
-// Per step (query head, query tile): S^T = K Q^T and dP^T = V dO^T into a
-// TMEM buffer pair; the compute warps form P^T = exp2(S^T*sl2 - lse2) and
-// dS^T = P^T (dP^T - delta) as bf16 K-major tiles; the MMA thread accumulates
-// dV += P^T dO and dK += dS^T Q into TMEM, which hold them across all steps.
-// Q/dO tiles run NQ stages ahead so their TMA latency stays off the MMA
-// thread's critical path; P^T/dS^T and the TMEM S^T/dP^T pairs are double
-// buffered. MODE 0 accumulates dK and dV together; for D = 256 the two
-// accumulators alone fill TMEM, so MODE 1 (dK) and MODE 2 (dV) run as two
-// launches over 32-query tiles, each keeping only the tile it needs.
-template <int D, int MODE = 0>
-struct DkvLayout {
-  static constexpr int BN = 128, BQ = D <= 128 ? 64 : 32, NB = D / 64, NQ = D <= 128 ? 3 : 2;
-  static constexpr int CW = BQ / 2;                          // query columns per compute warp
-  static constexpr bool WANT_DK = MODE != 2, WANT_DV = MODE != 1;
-  static constexpr bool WANT_P = WANT_DV, WANT_DS = WANT_DK;
-  static constexpr uint32_t KV_BYTES = BN * D * 2;
-  static constexpr uint32_t QT_BYTES = BQ * D * 2;
-  static constexpr uint32_t K = 0, V = KV_BYTES;
-  static constexpr uint32_t Q0 = 2 * KV_BYTES;               // [NQ] Q tiles
-  static constexpr uint32_t O0 = Q0 + NQ * QT_BYTES;         // [NQ] dO tiles
-  static constexpr uint32_t PT_BYTES = BN * 64 * 2;          // one 128-byte-row K-major tile
-  static constexpr uint32_t P0 = O0 + NQ * QT_BYTES;         // [2] P^T tiles
-  static constexpr uint32_t DS0 = P0 + (WANT_P ? 2 * PT_BYTES : 0);  // [2] dS^T tiles
-  static constexpr uint32_t LD0 = DS0 + (WANT_DS ? 2 * PT_BYTES : 0);  // [NQ][2][BQ] floats: lse2, delta
-  static constexpr uint32_t BAR = LD0 + NQ * 2 * BQ * 4;
-  static constexpr uint32_t TOTAL = BAR + 256;
-  static constexpr uint32_t DK_COL = 0, DV_COL = MODE == 0 ? D : 0;
-  static constexpr uint32_t ST_COL0 = MODE == 0 ? 2 * D : D;  // ST/DPT pairs follow
-};
-
-static_assert(DkvLayout<256, 1>::TOTAL + 1024 <= 232448, "dK shared memory exceeds 227 KB");
-static_assert(DkvLayout<256, 2>::TOTAL + 1024 <= 232448, "dV shared memory exceeds 227 KB");
-
-struct DkvBars {
-  uint64_t kv, q_full[3], q_empty[3], s_full[2], p_full[2], mma_done[2], fin;
-  uint32_t tmem_slot;
-  int abort;
-};
-
-template <int D, int MODE>
-__global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_tc_kernel(
-    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dk, bf16* __restrict__ dv,
-    float* __restrict__ part_k, float* __restrict__ part_v, int T, int S, int Hq, int Hkv, float scale,
-    int* __restrict__ err) {
-  using L = DkvLayout<D, MODE>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  DkvBars* bars = reinterpret_cast<DkvBars*>(smem + L::BAR);
-  const uint32_t sbase = tc::smem_addr(smem);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // blockIdx.z splits the query heads of this KV head across CTAs; with more
-  // than one split each CTA writes fp32 partial sums that a second kernel adds
-  // in split order (deterministic) and rounds.
-  const int hk = blockIdx.y, nsplit = gridDim.z, grp = Hq / Hkv / nsplit;
-  const int hbase = hk * (Hq / Hkv) + blockIdx.z * grp;
-  const int k0 = blockIdx.x * L::BN;
-  const int off = S - T;
-  const float sl2 = scale * kLog2e;
-  int qstart = k0 - off;
-  if (qstart < 0) qstart = 0;
-  qstart = (qstart / L::BQ) * L::BQ;
-  const int n_qt = qstart < T ? (T - qstart + L::BQ - 1) / L::BQ : 0;
-  const int total = n_qt * grp;
-  volatile int* abort = &bars->abort;
-  float* ld = reinterpret_cast<float*>(smem + L::LD0);
-  const bool trace = g_attn_trace_on && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-
-  if (threadIdx.x == 0) {
-    tc::mbar_init(&bars->kv, 1);
-    for (int i = 0; i < L::NQ; ++i) {
-      tc::mbar_init(&bars->q_full[i], 2);
-      tc::mbar_init(&bars->q_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&bars->s_full[i], 1);
-      tc::mbar_init(&bars->p_full[i], 256);
-      tc::mbar_init(&bars->mma_done[i], 1);
-    }
-    tc::mbar_init(&bars->fin, 1);
-    bars->abort = 0;
-    tc::fence_barrier_init();
-  }
-  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
-  __syncthreads();
-  tc::tc_fence_after();
-  const uint32_t tmem = bars->tmem_slot;
-
-  if (warp == 8) {
-    // producer: K, V once; per step Q and dO tiles (TMA) plus lse2 / delta (plain loads)
-    if (lane == 0) {
-      tc::mbar_expect_tx(&bars->kv, (L::WANT_DK ? 2 : 1) * L::KV_BYTES);
-      for (int b = 0; b < L::NB; ++b) {
-        tc::tma_load_2d(smem + L::K + b * L::BN * 128, &tm_k, hk * D + b * 64, k0, &bars->kv);
-        if constexpr (L::WANT_DK)
-          tc::tma_load_2d(smem + L::V + b * L::BN * 128, &tm_v, hk * D + b * 64, k0, &bars->kv);
-      }
-    }
-    for (int i = 0; i < total; ++i) {
-      const int qs = i % L::NQ;
-      if (lane == 0) TS_TRACE(0, i, 0);
-      if (i >= L::NQ && !warp_wait(&bars->q_empty[qs], ((i - L::NQ) / L::NQ) & 1, abort, err, 51)) break;
-      if (lane == 0) TS_TRACE(0, i, 1);
-      const int hh = hbase + i / n_qt;
-      const int qt = qstart + (i % n_qt) * L::BQ;
-      if (lane == 0) {
-        tc::mbar_expect_tx(&bars->q_full[qs], 2 * L::QT_BYTES);
-        for (int b = 0; b < L::NB; ++b) {
-          tc::tma_load_2d(smem + L::Q0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_q, hh * D + b * 64, qt,
-                          &bars->q_full[qs]);
-          tc::tma_load_2d(smem + L::O0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qt,
-                          &bars->q_full[qs]);
-        }
-      }
-      for (int c = lane; c < L::BQ; c += 32) {
-        const int qi = qt + c;
-        ld[(qs * 2 + 0) * L::BQ + c] = qi < T ? lse[(long long)hh * T + qi] * kLog2e : 0.f;
-        ld[(qs * 2 + 1) * L::BQ + c] = qi < T ? delta[(long long)hh * T + qi] : 0.f;
-      }
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars->q_full[qs]);
-      if (lane == 0) TS_TRACE(0, i, 2);
-    }
-  } else if (warp == 9) {
-    if (lane == 0) {
-      const uint32_t id_s = tc::idesc_bf16(128, L::BQ, false, false);
-      const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
-      bool ok = tc::mbar_wait(&bars->kv, 0, abort, err, 61);
-      auto issue_s = [&](int i) -> bool {
-        const int st = i & 1, qs = i % L::NQ;
-        TS_TRACE(1, i, 3);
-        if (!tc::mbar_wait(&bars->q_full[qs], (i / L::NQ) & 1, abort, err, 62)) return false;
-        TS_TRACE(1, i, 4);
-        tc::tc_fence_after();
-        const uint32_t qb = sbase + L::Q0 + qs * L::QT_BYTES, ob = sbase + L::O0 + qs * L::QT_BYTES;
-        const uint32_t col = L::ST_COL0 + st * 2 * L::BQ;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t kv_off = (kk >> 2) * L::BN * 128 + (kk & 3) * 32;
-          const uint32_t q_off = (kk >> 2) * L::BQ * 128 + (kk & 3) * 32;
-          tc::mma_bf16(tmem + col, tc::sdesc_sw128(sbase + L::K + kv_off, 16, 1024),
-                       tc::sdesc_sw128(qb + q_off, 16, 1024), id_s, kk > 0);
-          if constexpr (L::WANT_DK)
-            tc::mma_bf16(tmem + col + L::BQ, tc::sdesc_sw128(sbase + L::V + kv_off, 16, 1024),
-                         tc::sdesc_sw128(ob + q_off, 16, 1024), id_s, kk > 0);
-        }
-        tc::mma_commit(&bars->s_full[st]);
-        TS_TRACE(1, i, 5);
-        return true;
-      };
-      if (ok && total > 0) ok = issue_s(0);
-      if (ok && total > 1) ok = issue_s(1);
-      for (int i = 0; ok && i < total; ++i) {
-        const int st = i & 1, qs = i % L::NQ;
-        TS_TRACE(1, i, 0);
-        if (!tc::mbar_wait(&bars->p_full[st], (i >> 1) & 1, abort, err, 63)) break;
-        TS_TRACE(1, i, 1);
-        tc::tc_fence_after();
-        const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
-        const uint32_t qb = sbase + L::Q0 + qs * L::QT_BYTES, ob = sbase + L::O0 + qs * L::QT_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < L::BQ / 16; ++kk) {
-          const uint64_t ap = tc::sdesc_sw128(pb + kk * 32, 16, 1024);
-          const uint64_t ad = tc::sdesc_sw128(db + kk * 32, 16, 1024);
-          const uint64_t bo = tc::sdesc_sw128(ob + kk * 16 * 128, L::BQ * 128, 1024);
-          const uint64_t bq = tc::sdesc_sw128(qb + kk * 16 * 128, L::BQ * 128, 1024);
-          if constexpr (L::WANT_DV) tc::mma_bf16(tmem + L::DV_COL, ap, bo, id_acc, i > 0 || kk > 0);
-          if constexpr (L::WANT_DK) tc::mma_bf16(tmem + L::DK_COL, ad, bq, id_acc, i > 0 || kk > 0);
-        }
-        tc::mma_commit(&bars->mma_done[st]);
-        tc::mma_commit(&bars->q_empty[qs]);
-        TS_TRACE(1, i, 2);
-        if (i + 2 < total) ok = issue_s(i + 2);
-      }
-      if (ok) tc::mma_commit(&bars->fin);
-    }
-  } else {
-    // warps 0-7: warp w reads TMEM lanes of sub-partition (w & 3) and handles
-    // query columns [32 * (w >> 2), +32) of each step
-    const int r = (warp & 3) * 32 + lane;
-    const int hc = warp >> 2;
-    const int kr = k0 + r;
-    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    bool ok = true;
-    for (int i = 0; i < total && ok; ++i) {
-      const int st = i & 1, qs = i % L::NQ;
-      const int qt = qstart + (i % n_qt) * L::BQ;
-      const bool tw = threadIdx.x == 0;
-      if (tw) TS_TRACE(2, i, 0);
-      if (!warp_wait(&bars->q_full[qs], (i / L::NQ) & 1, abort, err, 71)) { ok = false; break; }
-      if (tw) TS_TRACE(2, i, 1);
-      if (!warp_wait(&bars->s_full[st], (i >> 1) & 1, abort, err, 72)) { ok = false; break; }
-      if (tw) TS_TRACE(2, i, 2);
-      if (i >= 2 && !warp_wait(&bars->mma_done[st], ((i - 2) >> 1) & 1, abort, err, 73)) { ok = false; break; }
-      if (tw) TS_TRACE(2, i, 3);
-      tc::tc_fence_after();
-      constexpr int CW = L::CW;
-      float sv[CW], dp[CW];
-      const uint32_t col = L::ST_COL0 + st * 2 * L::BQ + hc * CW;
-      tc::tmem_ld<CW>(lane_base + col, sv);
-      if constexpr (L::WANT_DK) tc::tmem_ld<CW>(lane_base + col + L::BQ, dp);
-      tc::tmem_ld_wait();
-      if (tw) TS_TRACE(2, i, 4);
-      // this step's query columns: lse2 and delta into registers (broadcast
-      // shared loads), and the visible range [lo, hi) of column indices
-      float l2[CW], dl[CW];
-      const float4* l2v = reinterpret_cast<const float4*>(ld + (qs * 2 + 0) * L::BQ + hc * CW);
-      const float4* dlv = reinterpret_cast<const float4*>(ld + (qs * 2 + 1) * L::BQ + hc * CW);
-#pragma unroll
-      for (int x = 0; x < CW / 4; ++x) {
-        const float4 a = l2v[x], b = dlv[x];
-        l2[4 * x] = a.x; l2[4 * x + 1] = a.y; l2[4 * x + 2] = a.z; l2[4 * x + 3] = a.w;
-        dl[4 * x] = b.x; dl[4 * x + 1] = b.y; dl[4 * x + 2] = b.z; dl[4 * x + 3] = b.w;
-      }
-      const int qc0 = qt + hc * CW;
-      const int lo = kr < S ? kr - off - qc0 : CW;  // query qc0+c sees key kr iff c >= lo
-      const int hi = T - qc0;                       // and c < hi (query exists)
-      const uint32_t pb = sbase + L::P0 + st * L::PT_BYTES, db = sbase + L::DS0 + st * L::PT_BYTES;
-#pragma unroll
-      for (int c8 = 0; c8 < CW / 8; ++c8) {
-        float p[8], ds[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int c = c8 * 8 + e;
-          p[e] = (c >= lo && c < hi) ? ex2(fmaf(sv[c], sl2, -l2[c])) : 0.f;
-          if constexpr (L::WANT_DK) ds[e] = p[e] * (dp[c] - dl[c]);
-        }
-        const uint32_t o8 = tc::kmajor_off(r, hc * CW + c8 * 8, 128);
-        if constexpr (L::WANT_P)
-          st_shared_v4(pb + o8, pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]), pack2(p[6], p[7]));
-        if constexpr (L::WANT_DS)
-          st_shared_v4(db + o8, pack2(ds[0], ds[1]), pack2(ds[2], ds[3]), pack2(ds[4], ds[5]), pack2(ds[6], ds[7]));
-      }
-      if (tw) TS_TRACE(2, i, 5);
-      tc::fence_async_smem();
-      tc::tc_fence_before();
-      tc::mbar_arrive(&bars->p_full[st]);
-      if (tw) TS_TRACE(2, i, 6);
-    }
-    if (ok && total > 0 && warp_wait(&bars->fin, 0, abort, err, 74)) {
-      tc::tc_fence_after();
-#pragma unroll
-      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
-        float a[32], b[32];
-        if constexpr (L::WANT_DK) tc::tmem_ld32(lane_base + L::DK_COL + c * 32, a);
-        if constexpr (L::WANT_DV) tc::tmem_ld32(lane_base + L::DV_COL + c * 32, b);
-        tc::tmem_ld_wait();
-        if (kr < S && nsplit > 1) {
-          const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D + c * 32;
-#pragma unroll
-          for (int x = 0; x < 32; x += 4) {
-            if constexpr (L::WANT_DK)
-              *reinterpret_cast<float4*>(part_k + o + x) = make_float4(a[x], a[x + 1], a[x + 2], a[x + 3]);
-            if constexpr (L::WANT_DV)
-              *reinterpret_cast<float4*>(part_v + o + x) = make_float4(b[x], b[x + 1], b[x + 2], b[x + 3]);
-          }
-        } else if (kr < S) {
-          bf16* pk = dk + ((long long)kr * Hkv + hk) * D + c * 32;
-          bf16* pv = dv + ((long long)kr * Hkv + hk) * D + c * 32;
-#pragma unroll
-          for (int x = 0; x < 32; x += 8) {
-            if constexpr (L::WANT_DK) {
-              uint4 u;
-              u.x = pack2(a[x] * scale, a[x + 1] * scale); u.y = pack2(a[x + 2] * scale, a[x + 3] * scale);
-              u.z = pack2(a[x + 4] * scale, a[x + 5] * scale); u.w = pack2(a[x + 6] * scale, a[x + 7] * scale);
-              *reinterpret_cast<uint4*>(pk + x) = u;
-            }
-            if constexpr (L::WANT_DV) {
-              uint4 w;
-              w.x = pack2(b[x], b[x + 1]); w.y = pack2(b[x + 2], b[x + 3]);
-              w.z = pack2(b[x + 4], b[x + 5]); w.w = pack2(b[x + 6], b[x + 7]);
-              *reinterpret_cast<uint4*>(pv + x) = w;
-            }
-          }
-        }
-      }
-    } else if (ok && total == 0 && kr < S && nsplit > 1) {
-      const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D;
-      for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 4) {
-        if constexpr (L::WANT_DK) *reinterpret_cast<float4*>(part_k + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-        if constexpr (L::WANT_DV) *reinterpret_cast<float4*>(part_v + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    } else if (ok && total == 0 && kr < S) {
-      for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 8) {
-        if constexpr (L::WANT_DK)
-          *reinterpret_cast<uint4*>(dk + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
-        if constexpr (L::WANT_DV)
-          *reinterpret_cast<uint4*>(dv + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
-      }
-    }
-  }
-  tc::tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, 512);
-  }
 }
 
 // dK/dV for head dims 64 and 128 with 128-query steps (every MMA is 128 x 128 x 16 or wider: narrower MMAs
@@ -960,6 +648,355 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
         *reinterpret_cast<uint4*>(dk + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(dv + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
       }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// dK (MODE 1) or dV (MODE 2) for head dim 256, whose dK and dV accumulators (256 TMEM columns each) do not
+// fit together. CTA = 128 keys of one KV head; per step (query head, 64-query tile):
+//   S^T = K Q^T with the CTA's K tile as a tensor-memory A operand (copied once from shared memory);
+//   MODE 2: the compute warps write P^T back over the S^T columns (bf16 pairs) and the MMA thread
+//           accumulates dV += P^T dO (N = 256) from there; two S^T buffers let S^T(i+1) run while the
+//           compute warps exponentiate S^T(i);
+//   MODE 1: dP^T = V dO^T (V resident in shared memory) into a second region; the compute warps write
+//           dS^T = P^T (dP^T - delta) over the dP^T columns and the MMA thread accumulates dK += dS^T Q,
+//           with issue order S^T(i+1), dK(i), dP^T(i+1).
+// Q/dO tiles run NQ stages ahead; K is loaded into the last stage's space and copied to TMEM before that
+// stage takes Q/dO.
+template <int MODE>
+struct Dkv256Layout {
+  static constexpr int D = 256, BN = 128, BQ = 64, NB = 4, NQ = MODE == 1 ? 2 : 3;
+  static constexpr uint32_t KV_BYTES = BN * D * 2;            // 64 KB
+  static constexpr uint32_t QT_BYTES = BQ * D * 2;            // 32 KB
+  static constexpr uint32_t ST_BYTES = 2 * QT_BYTES;          // one stage: Q tile, then dO tile
+  static constexpr uint32_t V = 0;                            // MODE 1 only
+  static constexpr uint32_t ST0 = MODE == 1 ? KV_BYTES : 0;   // [NQ] stages
+  static constexpr uint32_t KLOAD = ST0 + (NQ - 1) * ST_BYTES;
+  static constexpr uint32_t LD0 = ST0 + NQ * ST_BYTES;        // [NQ][2][BQ] floats: lse2, delta
+  static constexpr uint32_t BAR = LD0 + NQ * 2 * BQ * 4;
+  static constexpr uint32_t TOTAL = BAR + 512;
+  static constexpr uint32_t ACC_COL = 0, KTM_COL = 256, S_COL = 384, DP_COL = 448;  // MODE 2: S buffers 384, 448
+  static_assert(ST_BYTES == KV_BYTES, "K is staged through one Q/dO stage");
+};
+static_assert(Dkv256Layout<1>::TOTAL + 1024 <= 232448, "dK shared memory exceeds 227 KB");
+static_assert(Dkv256Layout<2>::TOTAL + 1024 <= 232448, "dV shared memory exceeds 227 KB");
+
+struct Dkv256Bars {
+  uint64_t kv, kv_tm, q_full[3], q_empty[3], s_full[2], p_full[2], dp_full, s_free, fin;
+  uint64_t rd[2][4];  // per buffer and TMEM sub-partition: warp (w & 3) has loaded its S^T / dP^T columns
+  uint32_t tmem_slot;
+  int abort;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ out,
+    float* __restrict__ part, int T, int S, int Hq, int Hkv, float scale, int* __restrict__ err) {
+  using L = Dkv256Layout<MODE>;
+  constexpr int D = L::D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Dkv256Bars* bars = reinterpret_cast<Dkv256Bars*>(smem + L::BAR);
+  const uint32_t sbase = tc::smem_addr(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hk = blockIdx.y, nsplit = gridDim.z, grp = Hq / Hkv / nsplit;
+  const int hbase = hk * (Hq / Hkv) + blockIdx.z * grp;
+  const int k0 = blockIdx.x * L::BN;
+  const int off = S - T;
+  const float sl2 = scale * kLog2e;
+  int qstart = k0 - off;
+  if (qstart < 0) qstart = 0;
+  qstart = (qstart / L::BQ) * L::BQ;
+  const int n_qt = qstart < T ? (T - qstart + L::BQ - 1) / L::BQ : 0;
+  const int total = n_qt * grp;
+  volatile int* abort = &bars->abort;
+  float* ld = reinterpret_cast<float*>(smem + L::LD0);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bars->kv, 1);
+    tc::mbar_init(&bars->kv_tm, 256);
+    for (int i = 0; i < L::NQ; ++i) {
+      tc::mbar_init(&bars->q_full[i], 2);
+      tc::mbar_init(&bars->q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bars->s_full[i], 1);
+      tc::mbar_init(&bars->p_full[i], 256);
+      for (int j = 0; j < 4; ++j) tc::mbar_init(&bars->rd[i][j], 32);
+    }
+    tc::mbar_init(&bars->dp_full, 1);
+    tc::mbar_init(&bars->s_free, 256);
+    tc::mbar_init(&bars->fin, 1);
+    bars->abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 8) {
+    // producer: K (into the last stage's space) and, for dK, V once; per step Q and dO tiles plus
+    // lse2 / delta (plain loads issued one step ahead)
+    if (lane == 0) {
+      tc::mbar_expect_tx(&bars->kv, (MODE == 1 ? 2 : 1) * L::KV_BYTES);
+      for (int b = 0; b < L::NB; ++b) {
+        tc::tma_load_2d(smem + L::KLOAD + b * L::BN * 128, &tm_k, hk * D + b * 64, k0, &bars->kv);
+        if constexpr (MODE == 1)
+          tc::tma_load_2d(smem + L::V + b * L::BN * 128, &tm_v, hk * D + b * 64, k0, &bars->kv);
+      }
+    }
+    constexpr int PER = L::BQ / 32;
+    float nl[PER], nd[PER];
+    auto fetch = [&](int i) {
+      const int hh = hbase + i / n_qt;
+      const int qt = qstart + (i % n_qt) * L::BQ;
+#pragma unroll
+      for (int x = 0; x < PER; ++x) {
+        const int qi = qt + x * 32 + lane;
+        nl[x] = qi < T ? lse[(long long)hh * T + qi] : 0.f;
+        nd[x] = qi < T ? delta[(long long)hh * T + qi] : 0.f;
+      }
+    };
+    if (total > 0) fetch(0);
+    for (int i = 0; i < total; ++i) {
+      const int qs = i % L::NQ;
+      if (i == L::NQ - 1 && !warp_wait(&bars->kv_tm, 0, abort, err, 241)) break;  // K has left this stage
+      if (i >= L::NQ && !warp_wait(&bars->q_empty[qs], ((i - L::NQ) / L::NQ) & 1, abort, err, 242)) break;
+      const int hh = hbase + i / n_qt;
+      const int qt = qstart + (i % n_qt) * L::BQ;
+      uint8_t* st = smem + L::ST0 + qs * L::ST_BYTES;
+      if (lane == 0) {
+        tc::mbar_expect_tx(&bars->q_full[qs], 2 * L::QT_BYTES);
+        for (int b = 0; b < L::NB; ++b) {
+          tc::tma_load_2d(st + b * L::BQ * 128, &tm_q, hh * D + b * 64, qt, &bars->q_full[qs]);
+          tc::tma_load_2d(st + L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qt, &bars->q_full[qs]);
+        }
+      }
+#pragma unroll
+      for (int x = 0; x < PER; ++x) {
+        ld[(qs * 2 + 0) * L::BQ + x * 32 + lane] = nl[x] * kLog2e;
+        ld[(qs * 2 + 1) * L::BQ + x * 32 + lane] = nd[x];
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->q_full[qs]);
+      if (i + 1 < total) fetch(i + 1);
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      const uint32_t id_s = tc::idesc_bf16(128, L::BQ, false, false);
+      const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
+      auto stage = [&](int i) { return sbase + L::ST0 + (i % L::NQ) * L::ST_BYTES; };
+      auto mma_st = [&](uint32_t col, uint32_t qb) {  // S^T = K Q^T, A = K from tensor memory
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_bf16_ts(tmem + col, tmem + L::KTM_COL + kk * 8,
+                          tc::sdesc_sw128(qb + (kk >> 2) * L::BQ * 128 + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
+      };
+      auto mma_dpt = [&](uint32_t ob) {  // dP^T = V dO^T, A = V from shared memory
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_bf16(tmem + L::DP_COL,
+                       tc::sdesc_sw128(sbase + L::V + (kk >> 2) * L::BN * 128 + (kk & 3) * 32, 16, 1024),
+                       tc::sdesc_sw128(ob + (kk >> 2) * L::BQ * 128 + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
+      };
+      auto mma_acc = [&](uint32_t acol, uint32_t bb, bool first) {  // dK += dS^T Q or dV += P^T dO
+#pragma unroll
+        for (int kk = 0; kk < L::BQ / 16; ++kk)
+          tc::mma_bf16_ts(tmem + L::ACC_COL, tmem + acol + kk * 8,
+                          tc::sdesc_sw128(bb + kk * 16 * 128, L::BQ * 128, 1024), id_acc, !first || kk > 0);
+      };
+      bool ok = tc::mbar_wait(&bars->kv, 0, abort, err, 251);
+      ok = ok && tc::mbar_wait(&bars->kv_tm, 0, abort, err, 252);
+      tc::tc_fence_after();
+      if constexpr (MODE == 2) {
+        auto issue_s = [&](int i) -> bool {
+          if (!tc::mbar_wait(&bars->q_full[i % L::NQ], (i / L::NQ) & 1, abort, err, 253)) return false;
+          tc::tc_fence_after();
+          mma_st(L::S_COL + (i & 1) * 64, stage(i));
+          tc::mma_commit(&bars->s_full[i & 1]);
+          return true;
+        };
+        if (ok && total > 0) ok = issue_s(0);
+        if (ok && total > 1) ok = issue_s(1);
+        for (int i = 0; ok && i < total; ++i) {
+          if (!tc::mbar_wait(&bars->p_full[i & 1], (i >> 1) & 1, abort, err, 254)) { ok = false; break; }
+          tc::tc_fence_after();
+          mma_acc(L::S_COL + (i & 1) * 64, stage(i) + L::QT_BYTES, i == 0);
+          tc::mma_commit(&bars->q_empty[i % L::NQ]);
+          if (i + 2 < total) ok = issue_s(i + 2);
+        }
+      } else {
+        if (ok && total > 0) {
+          ok = tc::mbar_wait(&bars->q_full[0], 0, abort, err, 255);
+          if (ok) {
+            tc::tc_fence_after();
+            mma_st(L::S_COL, stage(0));
+            tc::mma_commit(&bars->s_full[0]);
+            mma_dpt(stage(0) + L::QT_BYTES);
+            tc::mma_commit(&bars->dp_full);
+          }
+        }
+        for (int i = 0; ok && i < total; ++i) {
+          if (i + 1 < total) {
+            if (!tc::mbar_wait(&bars->s_free, i & 1, abort, err, 256)) { ok = false; break; }
+            if (!tc::mbar_wait(&bars->q_full[(i + 1) % L::NQ], ((i + 1) / L::NQ) & 1, abort, err, 257)) {
+              ok = false;
+              break;
+            }
+            tc::tc_fence_after();
+            mma_st(L::S_COL, stage(i + 1));
+            tc::mma_commit(&bars->s_full[0]);
+          }
+          if (!tc::mbar_wait(&bars->p_full[0], i & 1, abort, err, 258)) { ok = false; break; }
+          tc::tc_fence_after();
+          mma_acc(L::DP_COL, stage(i), i == 0);
+          tc::mma_commit(&bars->q_empty[i % L::NQ]);
+          if (i + 1 < total) {
+            mma_dpt(stage(i + 1) + L::QT_BYTES);
+            tc::mma_commit(&bars->dp_full);
+          }
+        }
+      }
+      if (ok) tc::mma_commit(&bars->fin);
+    }
+  } else {
+    // warps 0-7: key rows of sub-partition (w & 3), query columns [32 * (w >> 2), +32) of each step. The
+    // bf16 pairs of warp hc = 1 land on columns that warp hc = 0 of the same sub-partition reads, so it
+    // writes them once that warp has loaded its own.
+    const int sp = warp & 3, hc = warp >> 2;
+    const int r = sp * 32 + lane;
+    const int kr = k0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(sp * 32) << 16);
+    bool ok = true;
+    // K tile -> tensor memory: warp hc copies D columns [128 hc, +128) of key row r
+    if (warp_wait(&bars->kv, 0, abort, err, 261)) {
+#pragma unroll
+      for (int c0 = hc * 128; c0 < hc * 128 + 128; c0 += 64) {
+        float w[32];
+#pragma unroll
+        for (int q8 = 0; q8 < 8; ++q8) {
+          uint32_t a, b, c, d;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n"
+                       : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+                       : "r"(sbase + L::KLOAD + tc::kmajor_off(r, c0 + q8 * 8, L::BN)));
+          w[q8 * 4 + 0] = __uint_as_float(a);
+          w[q8 * 4 + 1] = __uint_as_float(b);
+          w[q8 * 4 + 2] = __uint_as_float(c);
+          w[q8 * 4 + 3] = __uint_as_float(d);
+        }
+        tc::tmem_st32(lane_base + L::KTM_COL + c0 / 2, w);
+      }
+      tc::tmem_st_wait();
+    }
+    tc::tc_fence_before();
+    tc::mbar_arrive(&bars->kv_tm);
+    for (int i = 0; i < total && ok; ++i) {
+      const int qs = i % L::NQ, b = MODE == 2 ? (i & 1) : 0;
+      const uint32_t scol = L::S_COL + b * 64;
+      const int qt = qstart + (i % n_qt) * L::BQ;
+      const int qc0 = qt + hc * 32;
+      const int lo = kr < S ? kr - off - qc0 : 32;  // query qc0+c sees key kr iff c >= lo
+      const int hi = T - qc0;                       // and c < hi (query exists)
+      if (!warp_wait(&bars->q_full[qs], (i / L::NQ) & 1, abort, err, 262)) { ok = false; break; }
+      if (!warp_wait(&bars->s_full[b], MODE == 2 ? (i >> 1) & 1 : i & 1, abort, err, 263)) { ok = false; break; }
+      tc::tc_fence_after();
+      float p[32];
+      tc::tmem_ld32(lane_base + scol + hc * 32, p);
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      if constexpr (MODE == 2) {
+        if (hc == 0) tc::mbar_arrive(&bars->rd[b][sp]);
+      } else {
+        tc::mbar_arrive(&bars->s_free);
+      }
+      const float* l2p = ld + (qs * 2 + 0) * L::BQ + hc * 32;
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4) {
+        const float4 l = *reinterpret_cast<const float4*>(l2p + c4 * 4);
+        const float lv[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = c4 * 4 + e;
+          p[c] = (c >= lo && c < hi) ? ex2(fmaf(p[c], sl2, -lv[e])) : 0.f;
+        }
+      }
+      uint32_t wcol = scol;  // where this step's bf16 A operand goes
+      if constexpr (MODE == 1) {
+        if (!warp_wait(&bars->dp_full, i & 1, abort, err, 264)) { ok = false; break; }
+        tc::tc_fence_after();
+        float dp[32];
+        tc::tmem_ld32(lane_base + L::DP_COL + hc * 32, dp);
+        tc::tmem_ld_wait();
+        if (hc == 0) {
+          tc::tc_fence_before();
+          tc::mbar_arrive(&bars->rd[0][sp]);
+        }
+        const float* dlp = ld + (qs * 2 + 1) * L::BQ + hc * 32;
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 d = *reinterpret_cast<const float4*>(dlp + c4 * 4);
+          p[c4 * 4 + 0] *= dp[c4 * 4 + 0] - d.x;
+          p[c4 * 4 + 1] *= dp[c4 * 4 + 1] - d.y;
+          p[c4 * 4 + 2] *= dp[c4 * 4 + 2] - d.z;
+          p[c4 * 4 + 3] *= dp[c4 * 4 + 3] - d.w;
+        }
+        wcol = L::DP_COL;
+      }
+      if (hc == 1 && !warp_wait(&bars->rd[b][sp], MODE == 2 ? (i >> 1) & 1 : i & 1, abort, err, 265)) {
+        ok = false;
+        break;
+      }
+      tc::tc_fence_after();
+      {
+        float w[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x) w[x] = __uint_as_float(pack2(p[2 * x], p[2 * x + 1]));
+        tc::tmem_st16(lane_base + wcol + hc * 16, w);
+      }
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->p_full[b]);
+    }
+    const float osc = MODE == 1 ? scale : 1.f;
+    if (ok && total > 0 && warp_wait(&bars->fin, 0, abort, err, 266)) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = hc * 4; c < hc * 4 + 4; ++c) {
+        float a[32];
+        tc::tmem_ld32(lane_base + L::ACC_COL + c * 32, a);
+        tc::tmem_ld_wait();
+        if (kr < S && nsplit > 1) {
+          const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 4)
+            *reinterpret_cast<float4*>(part + o + x) = make_float4(a[x], a[x + 1], a[x + 2], a[x + 3]);
+        } else if (kr < S) {
+          bf16* po = out + ((long long)kr * Hkv + hk) * D + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 u;
+            u.x = pack2(a[x] * osc, a[x + 1] * osc); u.y = pack2(a[x + 2] * osc, a[x + 3] * osc);
+            u.z = pack2(a[x + 4] * osc, a[x + 5] * osc); u.w = pack2(a[x + 6] * osc, a[x + 7] * osc);
+            *reinterpret_cast<uint4*>(po + x) = u;
+          }
+        }
+      }
+    } else if (ok && total == 0 && kr < S && nsplit > 1) {
+      const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D;
+      for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 4)
+        *reinterpret_cast<float4*>(part + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else if (ok && total == 0 && kr < S) {
+      for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 8)
+        *reinterpret_cast<uint4*>(out + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
     }
   }
   tc::tc_fence_before();
@@ -1640,22 +1677,6 @@ std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, co
   return {o, lse};
 }
 
-void attn_trace_enable(bool on) {
-  const int v = on ? 1 : 0;
-  TS_CUDA_CHECK(cudaMemcpyToSymbol(g_attn_trace_on, &v, sizeof(int)));
-  if (on) {
-    void* p = nullptr;
-    TS_CUDA_CHECK(cudaGetSymbolAddress(&p, g_attn_trace));
-    TS_CUDA_CHECK(cudaMemset(p, 0, sizeof(long long) * 4 * 128 * 8));
-  }
-}
-
-at::Tensor attn_trace_read() {
-  auto out = at::empty({4, 128, 8}, at::TensorOptions().dtype(at::kLong));
-  TS_CUDA_CHECK(cudaMemcpyFromSymbol(out.data_ptr<int64_t>(), g_attn_trace, sizeof(long long) * 4 * 128 * 8));
-  return out;
-}
-
 namespace {
 // Split the query heads of a KV head across CTAs when that fills the SMs' waves markedly better (the split
 // costs an fp32 partial round trip and a sum kernel): e.g. 168 CTAs on 148 SMs run as two waves at 57%
@@ -1707,30 +1728,28 @@ void launch_dkdv_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const C
   }
 }
 
-template <int D, int MODE>
-void launch_dkdv(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
-                 const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dk, at::Tensor& dv, int T, int S, int Hq,
-                 int Hkv, double scale, int* err) {
-  const int nsplit = dkdv_split(g, Hq / Hkv, dk.get_device());
+template <int MODE>
+void launch_dkdv256(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                    const CUtensorMap& mo, const at::Tensor& lse, const at::Tensor& delta, at::Tensor& out, int T,
+                    int S, int Hq, int Hkv, double scale, int* err) {
+  const int nsplit = dkdv_split(g, Hq / Hkv, out.get_device());
   g.z = nsplit;
-  at::Tensor pk, pv;
-  float* ppk = nullptr;
-  float* ppv = nullptr;
+  at::Tensor part;
+  float* pp = nullptr;
   if (nsplit > 1) {
-    if (MODE != 2) pk = at::empty({nsplit, S, Hkv, D}, dk.options().dtype(at::kFloat)), ppk = pk.data_ptr<float>();
-    if (MODE != 1) pv = at::empty({nsplit, S, Hkv, D}, dv.options().dtype(at::kFloat)), ppv = pv.data_ptr<float>();
+    part = at::empty({nsplit, S, Hkv, 256}, out.options().dtype(at::kFloat));
+    pp = part.data_ptr<float>();
   }
-  const int smem = DkvLayout<D, MODE>::TOTAL + 1024;
-  ensure_smem((const void*)attn_bwd_dkdv_tc_kernel<D, MODE>, smem);
-  attn_bwd_dkdv_tc_kernel<D, MODE><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
-                                                               delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
-                                                               (bf16*)dv.data_ptr(), ppk, ppv, T, S, Hq, Hkv,
-                                                               (float)scale, err);
+  const int smem = Dkv256Layout<MODE>::TOTAL + 1024;
+  ensure_smem((const void*)attn_bwd_dkdv256_kernel<MODE>, smem);
+  attn_bwd_dkdv256_kernel<MODE><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
+                                                            delta.data_ptr<float>(), (bf16*)out.data_ptr(), pp, T, S,
+                                                            Hq, Hkv, (float)scale, err);
   if (nsplit > 1) {
-    const long long n = (long long)S * Hkv * D;
+    const long long n = (long long)S * Hkv * 256;
     const int blocks = (int)((n / 4 + 255) / 256);
-    if (ppk) attn_split_sum_kernel<<<blocks, 256, 0, stream()>>>(ppk, (bf16*)dk.data_ptr(), n, nsplit, (float)scale);
-    if (ppv) attn_split_sum_kernel<<<blocks, 256, 0, stream()>>>(ppv, (bf16*)dv.data_ptr(), n, nsplit, 1.f);
+    attn_split_sum_kernel<<<blocks, 256, 0, stream()>>>(pp, (bf16*)out.data_ptr(), n, nsplit,
+                                                        MODE == 1 ? (float)scale : 1.f);
   }
 }
 
@@ -1795,11 +1814,11 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
     launch_dkdv_t<64>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
     launch_dq_t<64>(g2, mq128, mk128, mv128, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
   } else {
-    // dK/dV passes step over 32-query tiles, dQ over 64-key tiles
-    CUtensorMap mq_t = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 32);
-    CUtensorMap mo_t = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 32);
-    launch_dkdv<256, 1>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
-    launch_dkdv<256, 2>(g1, mq_t, mk128, mv128, mo_t, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
+    // dK and dV passes step over 64-query tiles, dQ over 64-key tiles
+    CUtensorMap mq64 = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 64);
+    CUtensorMap mo64 = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 64);
+    launch_dkdv256<1>(g1, mq64, mk128, mv128, mo64, lse, delta, dk, T, S, Hq, Hkv, scale, err);
+    launch_dkdv256<2>(g1, mq64, mk128, mv128, mo64, lse, delta, dv, T, S, Hq, Hkv, scale, err);
     CUtensorMap mk64 = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
     CUtensorMap mv64 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
     launch_dq256(g2, mq128, mk64, mv64, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);

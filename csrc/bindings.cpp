@@ -62,10 +62,8 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
                                     const c10::optional<at::Tensor>& dv_out);
 void register_ipc(pybind11::module& m);
 void register_pinned(pybind11::module& m);
-void attn_trace_enable(bool on);
 void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
              double alpha);
-at::Tensor attn_trace_read();
 std::vector<at::Tensor> gdn_chunk_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                       const at::Tensor& g, const at::Tensor& beta, const at::Tensor& state);
 std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& dfinal, const at::Tensor& q,
@@ -154,7 +152,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv1d_silu_fwd", &ts::conv1d_silu_fwd);
   m.def("conv1d_silu_bwd", &ts::conv1d_silu_bwd);
   m.def("gdn_fwd", &ts::gdn_fwd);
-  m.def("attn_trace_enable", &ts::attn_trace_enable);
   m.def("gemm_tc", &ts::gemm_tc);
   m.def("lmhead_lse_tc", &ts::lmhead_lse_tc);
   m.def("gemm_tc_pair", &ts::gemm_tc_pair);
@@ -162,7 +159,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dense_layer_bwd", &ts::dense_layer_bwd);
   m.def("gemm_tc_cat", &ts::gemm_tc_cat);
   m.def("lmhead_dlogits_tc", &ts::lmhead_dlogits_tc);
-  m.def("attn_trace_read", &ts::attn_trace_read);
   m.def("gdn_bwd", &ts::gdn_bwd);
   m.def("gdn_chunk_fwd", &ts::gdn_chunk_fwd);
   m.def("gdn_chunk_bwd", &ts::gdn_chunk_bwd);

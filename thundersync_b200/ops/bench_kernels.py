@@ -63,34 +63,7 @@ def bench_attn(args) -> None:
                 ext.attn_bwd_tc(do, q, k, v, o, lse, scale)
                 torch.cuda.synchronize()
             print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=8, max_name_column_width=60))
-        if args.trace:
-            ext.attn_trace_enable(True)
-            ext.attn_bwd_tc(do, q, k, v, o, lse, scale)
-            torch.cuda.synchronize()
-            ext.attn_trace_enable(False)
-            _print_trace(ext.attn_trace_read())
     print("kernel status", int(ext.tc_status(q).item()))
-
-
-def _print_trace(tr) -> None:
-    """Per-step clock64 deltas of the dK/dV kernel's first CTA (producer / MMA / compute warp 0)."""
-    t = tr.clone()
-    base = int(t[t > 0].min()) if bool((t > 0).any()) else 0
-    t = torch.where(t > 0, t - base, torch.zeros_like(t))
-    names = {0: "prod[wait_empty,got_empty,issued]", 1: "mma[wait_p,got_p,dkdv_issued,wait_q,got_q,s_issued]",
-             2: "cmp[start,q,s,mma_done,tmem_ld,computed,arrived]"}
-    for role, name in names.items():
-        print("role", name)
-        for i in range(0, 24):
-            row = [int(x) for x in t[role, i, :7].tolist()]
-            if any(row):
-                print(f"  step {i:3d}: " + " ".join(f"{x:9d}" for x in row))
-    cmp = t[2]
-    steps = int((cmp[:, 6] > 0).sum())
-    if steps > 2:
-        d = lambda a, b: float((cmp[2:steps, b] - cmp[2:steps, a]).double().mean())  # noqa: E731
-        print(f"compute: wait_s {d(1, 2):.0f}  wait_mma_done {d(2, 3):.0f}  tmem_ld {d(3, 4):.0f}  "
-              f"math+st {d(4, 5):.0f}  arrive {d(5, 6):.0f}  cycle {float((cmp[3:steps, 0] - cmp[2:steps - 1, 0]).double().mean()):.0f}")
 
 
 def bench_rms(args) -> None:
@@ -508,7 +481,7 @@ def main(argv=None) -> None:
     ap.add_argument("--rows", type=int, default=16384)
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--trace", action="store_true", help="print the head-dim-256 dK/dV kernel's per-step timeline")
+    ap.add_argument("--trace", action="store_true", help="lora: per-kernel device times of one forward+backward")
     ap.add_argument("--kernels", action="store_true", help="attn: per-kernel device times of one backward")
     args = ap.parse_args(argv)
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
