@@ -74,7 +74,7 @@ struct FwdLayout {
 static_assert(FwdLayout<256>::TOTAL + 1024 <= 232448, "forward shared memory exceeds 227 KB");
 
 struct FwdBars {
-  uint64_t q, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv;
+  uint64_t q, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv[2];
   uint32_t tmem_slot;
   int abort;
 };
@@ -109,8 +109,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       tc::mbar_init(&bars->kv_empty[i], 1);
       tc::mbar_init(&bars->s_full[i], 1);
       tc::mbar_init(&bars->p_full[i], 256);
+      tc::mbar_init(&bars->pv[i], 1);
     }
-    tc::mbar_init(&bars->pv, 1);
     bars->abort = 0;
     tc::fence_barrier_init();
   }
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
           const uint64_t b = tc::sdesc_sw128(vb + kk * 16 * 128, L::BN * 128, 1024);
           tc::mma_bf16(tmem + L::O_COL, a, b, id_o, j > 0 || kk > 0);
         }
-        tc::mma_commit(&bars->pv);
+        tc::mma_commit(&bars->pv[s]);
         tc::mma_commit(&bars->kv_empty[s]);
         if (j + 2 < n) ok = issue_s(j + 2);
       }
@@ -222,9 +222,15 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       }
       const float raw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      const float mx = fmaxf(m, raw * sl2);
+      // the exponent reference moves only when the running max grows by more than 8 (a factor 2^8): P
+      // stays <= 256 (exact in bf16's range, and the fp32 sums absorb it), and O is rescaled only then
+      const float cand = fmaxf(m, raw * sl2);
+      const bool bump = cand > m + 8.f;
+      const float mx = bump ? cand : m;
       const float ref = mx == -INFINITY ? 0.f : mx;
-      const float alpha = ex2(m - ref);
+      const float alpha = bump ? ex2(m - ref) : 1.f;
+      // P buffer s is free once PV(j - 2) has read it
+      if (j >= 2 && !warp_wait(&bars->pv[s], ((j - 2) >> 1) & 1, abort, err, 34)) { ok = false; break; }
       // this warp's half of the tile's columns, reloaded into registers with static indices
 #pragma unroll
       for (int c = 0; c < L::HALF / 32; ++c) tc::tmem_ld32(lane_base + scol + hc * L::HALF + c * 32, sv + c * 32);
@@ -248,10 +254,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       }
       const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
-      if (j > 0) {
-        if (!warp_wait(&bars->pv, (j - 1) & 1, abort, err, 32)) { ok = false; break; }
+      if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
+        if (!warp_wait(&bars->pv[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, err, 32)) { ok = false; break; }
         tc::tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+        {
 #pragma unroll
           for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
             float o[32];
@@ -273,7 +279,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
     lsum[hc * 128 + r] = l;
     asm volatile("bar.sync 1, 256;\n" ::: "memory");
     const float lt = lsum[r] + lsum[128 + r];
-    if (ok && warp_wait(&bars->pv, (n - 1) & 1, abort, err, 33)) {
+    if (ok && warp_wait(&bars->pv[(n - 1) & 1], ((n - 1) >> 1) & 1, abort, err, 33)) {
       tc::tc_fence_after();
       const float inv = 1.f / lt;
 #pragma unroll

@@ -301,6 +301,32 @@ def test_attention_tcgen05_forward(t, s, hq, hkv, d):
     torch.testing.assert_close(lse, lser, atol=2e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("d", [128, 256])
+def test_attention_tcgen05_forward_growing_max(d):
+    """Scores that grow along the keys: the forward's exponent reference moves only when a row's running max
+    grows by more than 8 (log2 units), so P reaches up to 2^8 between moves and O is rescaled only then.
+    Slopes below and above that step per key tile exercise both branches against the fp32 reference."""
+    from thundersync_b200.ops._ext import native
+    from thundersync_b200.ops.attention import attention_reference
+
+    torch.manual_seed(12)
+    t, s, hq, hkv = 200, 1000, 4, 2
+    q = torch.zeros(t, hq, d, device=DEV)
+    q[:, :, 0] = 1.0
+    k = torch.randn(s, hkv, d, device=DEV) * 0.1
+    # score of key j ~ slope * j (per head): gentle growth for one KV head, steep for the other
+    slope = torch.tensor([0.02, 0.3], device=DEV)
+    k[:, :, 0] = torch.arange(s, device=DEV)[:, None] * slope[None, :] * math.sqrt(d)
+    q, k = q.to(torch.bfloat16), k.to(torch.bfloat16)
+    v = torch.randn(s, hkv, d, device=DEV, dtype=torch.bfloat16)
+    o, lse = native().attn_fwd_tc(q, k, v, 1 / math.sqrt(d))
+    torch.cuda.synchronize()
+    assert int(native().tc_status(q).item()) == 0
+    orf, lser = attention_reference(q.float(), k.float(), v.float(), 1 / math.sqrt(d))
+    torch.testing.assert_close(o.float(), orf, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(lse, lser, atol=2e-3, rtol=1e-3)
+
+
 @pytest.mark.parametrize("t,s,hq,hkv,d", ATTN_CASES + [(2048, 2560, 16, 8, 128), (300, 4396, 16, 8, 128)])
 def test_attention_tcgen05_backward(t, s, hq, hkv, d):
     from thundersync_b200.ops._ext import native
