@@ -38,6 +38,7 @@ import random
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -47,7 +48,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "scored tokens/sec/box per GRPO step"
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric
+BASELINE_VALUE = None  # the reference publishes no number for this metric
 
 
 # ----------------------------------------------------------------------------- workload
@@ -178,70 +179,107 @@ def build_ours(args, device):
     return model, trainer
 
 
+def _reference_snapshot(args, device, c) -> str:
+    """Write a random-init Hugging Face snapshot of the benchmark model once per host.
+
+    The reference's builder loads its policy from a snapshot directory
+    (``load_policy_model`` -> ``from_pretrained``); there is no network, so the
+    snapshot is the architecture's own random init (N(0, 0.02), seeded), saved
+    in bf16. Local rank 0 writes it; the other ranks wait on the barrier, and the
+    reference's ``init_from_env`` broadcasts rank 0's weights anyway.
+    """
+    from transformers import AutoConfig, AutoModelForCausalLM
+
+    path = os.path.join(args.ref_snapshot_dir, f"{args.model}-seed{args.seed}")
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if local == 0 and not os.path.isfile(os.path.join(path, "config.json")):
+        hf_cfg = AutoConfig.for_model(
+            "qwen3", vocab_size=c.vocab_size, hidden_size=c.hidden_size, intermediate_size=c.intermediate_size,
+            num_hidden_layers=c.num_hidden_layers, num_attention_heads=c.num_attention_heads,
+            num_key_value_heads=c.num_key_value_heads, head_dim=c.head_dim, rms_norm_eps=c.rms_norm_eps,
+            rope_theta=c.rope_theta, tie_word_embeddings=c.tie_word_embeddings,
+            max_position_embeddings=c.max_position_embeddings, initializer_range=c.initializer_range,
+        )
+        torch.manual_seed(args.seed)
+        with torch.device(device):
+            model = AutoModelForCausalLM.from_config(hf_cfg, dtype=torch.bfloat16)
+        tmp = path + f".tmp{os.getpid()}"
+        model.save_pretrained(tmp)
+        del model
+        torch.cuda.empty_cache()
+        os.replace(tmp, path)
+    if dist.is_initialized():
+        dist.barrier()
+    return path
+
+
 def build_reference(args, device):
+    """The unmodified reference, built by its own production builder.
+
+    Path: ``GrpoTrainerConfig.from_namespace`` (the reference's entry-point
+    translation) -> ``thundersync.grpo.runtime.load_trainer`` (reference
+    ``src/thundersync/grpo/runtime.py:151-319``), which loads the policy from a
+    snapshot, picks the source-attention backend after its own device trial,
+    builds AdamW(maximize) or, at N > 1, its ZeRO-1 ``ShardedOptimizerStep``,
+    places the group statistics (``statistic_device="auto"``) and returns its
+    ``DataParallelThunderSync``. Nothing from this package runs on that path;
+    only the model preset's numbers are read from here.
+    """
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "thundersync")):
         raise RuntimeError("reference not installed under baseline/_ref")
     sys.path.insert(0, ref)
-    from transformers import AutoConfig, AutoModelForCausalLM
+    from types import SimpleNamespace
 
-    from thundersync import STREAM_ATTENTION_NAME, register_stream_attention
-    from thundersync.engine.streaming import StreamingRun
-    from thundersync.grpo.data_parallel import DataParallelThunderSync
+    from thundersync import register_stream_attention
+    from thundersync.grpo.config import GrpoTrainerConfig
+    from thundersync.grpo.runtime import load_trainer
 
     from thundersync_b200.models.qwen3 import PRESETS
 
-    c = PRESETS[args.model]
-    register_stream_attention()
-    hf_cfg = AutoConfig.for_model(
-        "qwen3", vocab_size=c.vocab_size, hidden_size=c.hidden_size, intermediate_size=c.intermediate_size,
-        num_hidden_layers=c.num_hidden_layers, num_attention_heads=c.num_attention_heads,
-        num_key_value_heads=c.num_key_value_heads, head_dim=c.head_dim, rms_norm_eps=c.rms_norm_eps,
-        rope_theta=c.rope_theta, tie_word_embeddings=c.tie_word_embeddings,
-        max_position_embeddings=c.max_position_embeddings, initializer_range=c.initializer_range,
-    )
-    torch.manual_seed(args.seed)
-    model = AutoModelForCausalLM.from_config(hf_cfg, attn_implementation=STREAM_ATTENTION_NAME,
-                                             dtype=torch.bfloat16).to(device)
-    model.train()
-    opt = torch.optim.AdamW([p for p in model.parameters() if p.requires_grad], lr=args.lr,
-                            betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, maximize=True)
-
-    def factory(m):
-        return StreamingRun(m, boundary_cut=True, checkpoint=True, stream_turns=False,
-                            rebuild_block_tokens=args.block_tokens)
-
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if not dist.is_initialized():
         os.environ.setdefault("RANK", "0")
         os.environ.setdefault("WORLD_SIZE", "1")
         os.environ.setdefault("LOCAL_RANK", "0")
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", str(29500 + os.getpid() % 1000))
-    # Statistic placement as the reference's own builder does it for
-    # device-resident sources with statistic_device "auto"
-    # (grpo/runtime.py statistic_placement): as many open groups' fp32 (G1, G2)
-    # pairs on the device as its device_statistic_slots finds room for, the
-    # rest on the host. Host-only statistics for 8 open groups need ~109 GB per
-    # rank, which two ranks on one box do not have.
-    from thundersync.grpo.device_statistics import device_statistic_slots
-
-    trainable = [p for p in model.parameters() if p.requires_grad]
-    src = sum(p.numel() * p.element_size() for p in trainable)
-    slots = device_statistic_slots(
-        device_total_bytes=int(torch.cuda.get_device_properties(device).total_memory),
-        parameter_bytes=sum(p.numel() * p.element_size() for p in model.parameters())
-        + sum(b.numel() * b.element_size() for b in model.buffers()),
-        gradient_bytes=src, optimizer_state_bytes=2 * src, source_bytes=src, device_held_sources=1,
-        statistic_pair_bytes=2 * sum(p.numel() * 4 for p in trainable), reserve_bytes=0,
-        open_groups=args.groups_per_rank,
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=900))
+    snapshot = _reference_snapshot(args, device, PRESETS[args.model])
+    if args.ref_deterministic:
+        os.environ.setdefault("CUBLAS_WORKSPACE_CONFIG", ":4096:8")
+    ns = SimpleNamespace(
+        model_path=snapshot,
+        learning_rate=args.lr,
+        rebuild_block_tokens=args.block_tokens,
+        grad_clip=1.0,
+        optimizer_state_sharding=world > 1,
+        deterministic_algorithms=bool(args.ref_deterministic),
+        compile_pointwise_modules=bool(args.ref_compile),
+        source_offload_device="cpu",
+        source_offload_mode="device_resident",
+        statistic_device="auto",
+        statistic_open_groups=args.groups_per_rank,
+        source_attention_backend=args.ref_attention,
     )
-    trainer = DataParallelThunderSync.init_from_env(
-        model, opt, run_factory=factory, grad_clip=1.0,
-        source_offload_device="cpu", source_offload_mode="device_resident",
-        statistic_device=device, device_statistic_slots=slots,
-    )
+    config = GrpoTrainerConfig.from_namespace(ns)
+    # the builder's "auto" backend names the stream attention, which the
+    # reference's entry points register with transformers first
+    register_stream_attention()
+    model, _optimizer, trainer = load_trainer(config, device)
     trainer.configure_binary_rewards()
     return model, trainer
+
+
+def reference_diagnostics() -> dict:
+    """Which attention paths and kernel trials the reference's run used."""
+    from thundersync.accel.capability import kernel_probe_records
+    from thundersync.engine.streaming import attention_path_counts
+
+    probes = []
+    for rec in kernel_probe_records():
+        probes.append({k: rec.get(k) for k in ("kernel", "runs", "error") if k in rec})
+    return {"attention_path_counts": attention_path_counts(), "kernel_probes": probes}
 
 
 # ----------------------------------------------------------------------------- main
@@ -263,7 +301,17 @@ def main() -> None:
     ap.add_argument("--lr", type=float, default=1e-5)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--vocab", type=int, default=151936)
-    ap.add_argument("--clocks-file", default=os.path.join(ROOT, "gpurun_out", "bench_clocks.csv"))
+    ap.add_argument("--clocks-file", default=None,
+                    help="where nvidia-smi clock samples of the timed region are written (default: a temp file)")
+    ap.add_argument("--ref-attention", default="cudnn_graph", choices=["auto", "cudnn", "cudnn_graph"],
+                    help="reference arm: source_attention_backend given to its builder (cudnn_graph, its fastest "
+                         "measured on B200, if its device trial passes)")
+    ap.add_argument("--ref-compile", type=int, default=0,
+                    help="reference arm: compile_pointwise_modules (torch.compile of MLP and norms)")
+    ap.add_argument("--ref-deterministic", type=int, default=0,
+                    help="reference arm: deterministic_algorithms")
+    ap.add_argument("--ref-snapshot-dir", default=os.path.join(tempfile.gettempdir(), "thundersync_ref_snapshots"),
+                    help="reference arm: where the random-init snapshot its builder loads is written")
     ap.add_argument("--profile-out", default=None,
                     help="after the timed region, run one more step under torch.profiler and write the per-kernel "
                          "CUDA time table to this file (rank 0; not part of any reported number)")
@@ -315,9 +363,11 @@ def main() -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    if args.clocks_file is None:
+        args.clocks_file = os.path.join(tempfile.gettempdir(), f"bench_clocks_{os.getpid()}.csv")
     sampler = ClockSampler(args.clocks_file) if rank == 0 else None
     if sampler:
-        os.makedirs(os.path.dirname(args.clocks_file), exist_ok=True)
+        os.makedirs(os.path.dirname(os.path.abspath(args.clocks_file)), exist_ok=True)
         sampler.start()
     _ext.reset_launch_counts()
     tails = []
@@ -395,6 +445,22 @@ def main() -> None:
         if args.impl == "reference":
             out["impl"] = "reference"
             out["gpu_launches"] = 0
+            out["config"]["reference_build"] = {
+                "builder": "thundersync.grpo.runtime.load_trainer(GrpoTrainerConfig.from_namespace(...))",
+                "source_attention_backend": args.ref_attention,
+                "compile_pointwise_modules": bool(args.ref_compile),
+                "deterministic_algorithms": bool(args.ref_deterministic),
+                "optimizer_state_sharding": world > 1,
+                "checkpoint": True,
+                "statistics": "device_resident sources, statistic_device auto",
+                **reference_diagnostics(),
+            }
+        else:
+            out["config"]["build"] = {
+                "checkpoint": False,
+                "statistics": "device-resident fp32 group statistics",
+                "optimizer": "fused flat AdamW" + (" (ZeRO-1 sharded)" if getattr(trainer, "sharded", False) else ""),
+            }
         print(json.dumps(out))
     if args.profile_out:
         from torch.profiler import ProfilerActivity, profile
