@@ -148,6 +148,25 @@ def test_backend_resolution_rules():
         resolve_sandbox_backend("podman")
 
 
+def test_backend_resolution_falls_back_to_udocker_and_records_both_probes():
+    def run(argv, **kw):
+        if argv[1:] == ["version"]:
+            assert "UDOCKER_DIR" in kw["env"]  # the probe never touches the real udocker store
+            return subprocess.CompletedProcess(argv, 0, "udocker 1.3.17\nversion: 1.3.17\n", "")
+        return subprocess.CompletedProcess(argv, 1, "", "Cannot connect to the Docker daemon")
+
+    exe = shutil.which("true")
+    r = resolve_sandbox_backend("auto", docker_bin=exe, udocker_bin=exe, runner=run)
+    rec = r.as_record()
+    assert r.backend == "udocker" and r.decided_by == "auto_docker_unusable_udocker_available"
+    assert rec["schema"] == "thundersync-sandbox-backend-v1" and rec["version"] == "1.3.17"
+    assert rec["docker"]["usable"] is False and "Docker daemon" in rec["docker"]["detail"]
+    with pytest.raises(SandboxBackendError):
+        resolve_sandbox_backend("auto", docker_bin="/nonexistent/docker", udocker_bin="/nonexistent/udocker")
+    r = resolve_sandbox_backend("udocker", udocker_bin=exe, runner=run)
+    assert r.decided_by == "explicit_request" and r.docker is None
+
+
 # ---------------------------------------------------------------------------- pool
 def test_pool_gate_reuses_pristine_and_discards_dirty():
     task = Task("t1", "p", "img")

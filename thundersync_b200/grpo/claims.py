@@ -18,6 +18,7 @@ from collections.abc import Callable, Sequence
 from typing import Any, Protocol
 
 from thundersync_b200.grpo.admission import FinalFirstAdmission, GroupLedgerTrainer
+from thundersync_b200.scheduling.admission import Close
 from thundersync_b200.scheduling.admission import CloseCoefficient, TrainerCall, direct_call
 from thundersync_b200.scheduling.work_claims import Offer, StoreWorkClaims
 
@@ -79,12 +80,12 @@ class ClaimingFinalFirstAdmission(FinalFirstAdmission):
 
     # owner --------------------------------------------------------------
     def _offer_final_work(self) -> None:
-        for gid, tid, _ in self._ready_close_queue:
-            if not self._group_final(gid) or self._claims.is_offered(tid):
+        for c in self._closes:
+            if not self._is_final(c.group) or self._claims.is_offered(c.trajectory):
                 continue
-            tokens, price, payload = self._ct.final_work(tid)
-            self._sizes[tid] = (tokens, price)
-            self._claims.offer(tid, price, payload)
+            tokens, price, payload = self._ct.final_work(c.trajectory)
+            self._sizes[c.trajectory] = (tokens, price)
+            self._claims.offer(c.trajectory, price, payload)
 
     def drain_ready_closes(self) -> None:
         self._offer_final_work()
@@ -99,52 +100,52 @@ class ClaimingFinalFirstAdmission(FinalFirstAdmission):
 
     def close_ready_groups(self) -> None:
         super().close_ready_groups()
-        if FinalFirstAdmission.deferred_work_reason.fget(self) is None and not self._should_yield():
+        if FinalFirstAdmission.deferred_work_reason.fget(self) is None and not self._events_pending():
             self._claim_peer_batch()
 
-    def _claim(self, chunk):
-        won_ids, lost_ids = self._claims.claim_own([t for _, t, _ in chunk])
+    def _claim(self, chunk: list[Close]) -> list[Close]:
+        """Claim our own offered closes; hand the ones a peer took to the trainer as ceded."""
+        won_ids, lost_ids = self._claims.claim_own([c.trajectory for c in chunk])
         lost = set(lost_ids)
         if lost:
-            ceded = [x for x in chunk if x[1] in lost]
-            self._ct.cede_final_closes([(t, r) for _, t, r in ceded])
-            for g, _, _ in ceded:
-                self._record_bound(g)
+            ceded = [c for c in chunk if c.trajectory in lost]
+            self._ct.cede_final_closes([(c.trajectory, c.coefficient) for c in ceded])
+            for c in ceded:
+                self._mark_bound(c.group)
         won = set(won_ids)
-        return [x for x in chunk if x[1] in won]
+        return [c for c in chunk if c.trajectory in won]
 
-    def _run_final_forest(self, backlog) -> None:
+    def _final_forest(self, closes: list[Close]) -> None:
         cap = self._ct.final_forest_max_tokens
-        queue = list(backlog)
+        queue = list(closes)
         while queue:
             chunk, tokens = [], 0
             while queue:
-                size = self._sizes.get(queue[0][1], (0, 0))[0]
+                size = self._sizes.get(queue[0].trajectory, (0, 0))[0]
                 if chunk and tokens + size > cap:
                     break
                 chunk.append(queue.pop(0))
                 tokens += size
             won = self._claim(chunk)
             if won:
-                super()._run_final_forest(won)
-                self._claims.finish_own([t for _, t, _ in won])
-            if queue and self._should_yield():
-                self._ready_close_queue = queue + self._ready_close_queue
+                super()._final_forest(won)
+                self._claims.finish_own([c.trajectory for c in won])
+            if queue and self._interrupted():
+                self._closes = queue + self._closes
                 return
 
-    def _drain_closes(self, queue, *, gated: bool, **labels) -> None:
+    def _drain(self, closes: list[Close], *, gated: bool, **labels: Any) -> list[Close]:
         if labels.get("job_class") != "final":
-            super()._drain_closes(queue, gated=gated, **labels)
-            return
-        size = self._max_prepare_pack or max(1, len(queue))
-        while queue:
-            chunk = queue[:size]
-            del queue[: len(chunk)]
+            return super()._drain(closes, gated=gated, **labels)
+        rest = list(closes)
+        size = self._pack_size(len(rest))
+        while rest:
+            chunk, rest = rest[:size], rest[size:]
             won = self._claim(chunk)
             if won:
-                ids = [t for _, t, _ in won]
-                super()._drain_closes(won, gated=gated, **labels)
-                self._claims.finish_own(ids)
+                super()._drain(won, gated=gated, **labels)
+                self._claims.finish_own([c.trajectory for c in won])
+        return []
 
     # step end -------------------------------------------------------------
     def drain_group_closes(self) -> None:

@@ -30,6 +30,8 @@ B200-first execution:
 
 from __future__ import annotations
 
+import contextlib
+
 import logging
 import math
 import time
@@ -255,20 +257,15 @@ class RewardLinearBackward:
                 raise ValueError(f"trajectory {tid} closed without a finite reward")
             norm.append((int(tid), float(reward), w))
         prof = self._close_profiler
-        window = False
+        window = contextlib.nullcontext()
         if prof is not None:
-            toks = [self.run.trajectory_tokens(t) for t, _, _ in norm]
-            if prof.selects(rank=self._profile_rank, step=self._profile_step, branch_tokens=toks):
-                prof.start(rank=self._profile_rank, step=self._profile_step,
-                           trajectory_ids=[t for t, _, _ in norm], branch_tokens=toks)
-                window = True
-        try:
+            window = prof.capture(rank=self._profile_rank, step=self._profile_step,
+                                  trajectory_ids=[t for t, _, _ in norm],
+                                  branch_tokens=[self.run.trajectory_tokens(t) for t, _, _ in norm])
+        with window:
             for tid, reward, w in norm:
                 self._record(tid, reward)
                 self._differentiate(tid, reward, w)
-        finally:
-            if window:
-                prof.stop()
 
     def prepare_trajectory(self, traj_id: int, token_weights=None) -> None:
         self.prepare_trajectories([(traj_id, token_weights)] if token_weights is not None else [traj_id])

@@ -75,8 +75,9 @@ SOURCE_EXTENSIONS = ("py", "go", "js", "ts", "jsx", "tsx", "java", "rb", "rs", "
                      "php", "scala", "kt", "swift", "m", "sh")
 ORDERINGS = ("grep", "path")
 TEST_FRAMEWORKS = ("pytest", "go")
-# The closing fence is a line holding only ``` (trailing blanks allowed), so a
-# body with ``` inside a line (a heredoc writing Markdown) is not cut short.
+# An action is the body of a ```bash fence. Only a line that is nothing but
+# ``` (plus spaces or tabs) ends it: backticks in the middle of a command line
+# -- say a heredoc that writes Markdown -- stay part of the command.
 ACTION_RE = re.compile(r"```bash[ \t]*\n(.*?)^```[ \t]*$", re.DOTALL | re.MULTILINE)
 
 

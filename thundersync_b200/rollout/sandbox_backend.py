@@ -1,14 +1,19 @@
 """Which container runtime a site's sandboxes run on (C53).
 
-Docker when this user's Docker daemon answers, udocker otherwise. ``auto``
-applies that rule; an explicit ``docker`` or ``udocker`` request is honoured
-only when that runtime is usable and is refused otherwise — never swapped for
-the other. Resolve once per site and hand the result to every process
-(reference: src/thundersync/rollout/sandbox_backend.py:1-239; the JSON record
-schema name is kept so tooling that reads it still does).
+Rule: Docker when this user's Docker daemon answers, udocker otherwise. A
+request of ``auto`` applies the rule; a request naming a runtime gets that
+runtime or an error, never the other one. A site resolves once and hands the
+record to every process (the record's schema name, its ``decided_by`` labels
+and the ``THUNDERSYNC_DOCKER_BIN`` / ``THUNDERSYNC_UDOCKER_BIN`` variables are
+the interface of reference src/thundersync/rollout/sandbox_backend.py:1-239;
+tooling that reads the record keeps working).
+
+Design: each runtime is described by a :class:`_Runtime` row (how to ask it
+for its version, how to read the answer); one generic checker runs any row
+with a timeout; resolution walks a short list of (runtime, label) candidates.
 
 ``python -m thundersync_b200.rollout.sandbox_backend --requested auto`` prints
-the resolution record.
+the resolution record as one JSON line.
 """
 
 from __future__ import annotations
@@ -20,6 +25,7 @@ import shutil
 import subprocess
 import sys
 import tempfile
+from contextlib import ExitStack
 from dataclasses import dataclass
 from pathlib import Path
 from typing import Any, Callable
@@ -35,11 +41,13 @@ Runner = Callable[..., subprocess.CompletedProcess]
 
 
 class SandboxBackendError(RuntimeError):
-    pass
+    """No usable runtime for the request."""
 
 
 @dataclass(frozen=True, slots=True)
 class Probe:
+    """Outcome of asking one runtime for its version."""
+
     usable: bool
     version: str | None
     detail: str
@@ -50,6 +58,8 @@ class Probe:
 
 @dataclass(frozen=True, slots=True)
 class ResolvedSandboxBackend:
+    """The chosen runtime, why it was chosen, and the probes that were run."""
+
     requested: str
     backend: str
     decided_by: str
@@ -58,124 +68,153 @@ class ResolvedSandboxBackend:
 
     @property
     def version(self) -> str | None:
-        p = self.docker if self.backend == "docker" else self.udocker
-        return None if p is None else p.version
+        chosen = {"docker": self.docker, "udocker": self.udocker}[self.backend]
+        return chosen.version if chosen is not None else None
 
     def as_record(self) -> dict[str, Any]:
-        return {"schema": RECORD_SCHEMA, "requested": self.requested, "backend": self.backend,
-                "decided_by": self.decided_by, "version": self.version,
-                "docker": None if self.docker is None else self.docker.as_record(),
-                "udocker": None if self.udocker is None else self.udocker.as_record()}
+        rec: dict[str, Any] = {"schema": RECORD_SCHEMA, "requested": self.requested, "backend": self.backend,
+                               "decided_by": self.decided_by, "version": self.version}
+        for name in BACKENDS:
+            probe = getattr(self, name)
+            rec[name] = probe.as_record() if probe is not None else None
+        return rec
 
     def factory(self):
-        """The sandbox class of the resolved backend."""
+        """The sandbox class that runs on the chosen runtime."""
         if self.backend == "docker":
-            from thundersync_b200.rollout.docker_sandbox import DockerSandbox
-
-            return DockerSandbox
-        from thundersync_b200.rollout.udocker_sandbox import UDockerSandbox
-
-        return UDockerSandbox
+            from thundersync_b200.rollout.docker_sandbox import DockerSandbox as cls
+        else:
+            from thundersync_b200.rollout.udocker_sandbox import UDockerSandbox as cls
+        return cls
 
 
-def _exe(path: str) -> str | None:
-    found = shutil.which(path)
-    if found:
-        return found
-    p = Path(path)
-    return str(p) if p.is_file() and os.access(p, os.X_OK) else None
+# ----------------------------------------------------------------------------- runtime rows
+def _docker_version(stdout: str) -> str | None:
+    # `docker version --format {{.Server.Version}}` prints the daemon's version, or nothing when the client
+    # cannot reach a daemon (some clients still exit 0 then)
+    lines = [ln.strip() for ln in stdout.splitlines() if ln.strip()]
+    return lines[-1] if lines else None
 
 
-def _call(runner: Runner, argv: list[str], timeout_s: float, env=None):
-    try:
-        kw = {"capture_output": True, "text": True, "timeout": timeout_s}
-        if env is not None:
-            kw["env"] = env
-        return runner(argv, **kw)
-    except subprocess.TimeoutExpired:
-        return f"`{' '.join(argv)}` did not answer within {timeout_s:g} s"
-    except OSError as exc:
-        return f"`{' '.join(argv)}` could not start: {exc}"
+def _udocker_version(stdout: str) -> str | None:
+    lines = [ln.strip() for ln in stdout.splitlines() if ln.strip()]
+    for ln in lines:
+        key, sep, val = ln.partition(":")
+        if sep and key.strip().lower() == "version":
+            return val.strip()
+    return lines[0] if lines else "unknown"
 
 
-def _last_line(cp) -> str:
-    lines = (cp.stderr or cp.stdout or "").strip().splitlines()
-    return lines[-1][:300] if lines else "no output"
+@dataclass(frozen=True)
+class _Runtime:
+    name: str
+    argv_tail: tuple[str, ...]
+    read_version: Callable[[str], str | None]
+    private_store: bool  # point UDOCKER_DIR at a throwaway directory so the probe never touches the real store
+
+
+_RUNTIMES = {
+    "docker": _Runtime("docker", ("version", "--format", "{{.Server.Version}}"), _docker_version, False),
+    "udocker": _Runtime("udocker", ("version",), _udocker_version, True),
+}
+_ENV_BIN = {"docker": "THUNDERSYNC_DOCKER_BIN", "udocker": "THUNDERSYNC_UDOCKER_BIN"}
+
+
+def _locate(binary: str) -> str | None:
+    hit = shutil.which(binary)
+    if hit is not None:
+        return hit
+    path = Path(binary)
+    if path.is_file() and os.access(path, os.X_OK):
+        return str(path)
+    return None
+
+
+def _tail(text: str | None) -> str:
+    for ln in reversed((text or "").splitlines()):
+        if ln.strip():
+            return ln.strip()[:300]
+    return "(no output)"
+
+
+def _check(rt: _Runtime, binary: str, timeout_s: float, runner: Runner) -> Probe:
+    exe = _locate(binary)
+    if exe is None:
+        return Probe(False, None, f"{rt.name}: executable {binary!r} not found")
+    argv = [exe, *rt.argv_tail]
+    with ExitStack() as stack:
+        kwargs: dict[str, Any] = {"capture_output": True, "text": True, "timeout": timeout_s}
+        if rt.private_store:
+            scratch = stack.enter_context(tempfile.TemporaryDirectory(prefix="ts-udocker-probe-"))
+            kwargs["env"] = dict(os.environ, UDOCKER_DIR=scratch)
+        try:
+            done = runner(argv, **kwargs)
+        except subprocess.TimeoutExpired:
+            return Probe(False, None, f"{rt.name}: no answer from {exe} after {timeout_s:g} s")
+        except OSError as exc:
+            return Probe(False, None, f"{rt.name}: {exe} failed to start ({exc})")
+    version = rt.read_version(done.stdout or "") if done.returncode == 0 else None
+    if version is None:
+        why = _tail(done.stderr) if (done.stderr or "").strip() else _tail(done.stdout)
+        return Probe(False, None, f"{rt.name}: {exe} exited {done.returncode} without a version ({why})")
+    return Probe(True, version, f"{rt.name}: {exe}")
 
 
 def probe_docker(bin_path: str = "docker", *, timeout_s: float = DEFAULT_PROBE_TIMEOUT_S,
                  runner: Runner = subprocess.run) -> Probe:
-    """Usable iff ``docker version`` reports a *server* version (the daemon answers this user)."""
-    exe = _exe(bin_path)
-    if exe is None:
-        return Probe(False, None, f"no {bin_path!r} executable on PATH")
-    cp = _call(runner, [exe, "version", "--format", "{{.Server.Version}}"], timeout_s)
-    if isinstance(cp, str):
-        return Probe(False, None, cp)
-    ver = cp.stdout.strip()
-    if cp.returncode != 0 or not ver:
-        return Probe(False, None, f"docker daemon unusable (exit {cp.returncode}): {_last_line(cp)}")
-    return Probe(True, ver.splitlines()[-1], f"server {exe}")
+    """Usable when the Docker daemon reports a server version to this user."""
+    return _check(_RUNTIMES["docker"], bin_path, timeout_s, runner)
 
 
 def probe_udocker(bin_path: str = "udocker", *, timeout_s: float = DEFAULT_PROBE_TIMEOUT_S,
                   runner: Runner = subprocess.run) -> Probe:
-    """Usable iff ``udocker version`` runs (against a throwaway UDOCKER_DIR, never the real store)."""
-    exe = _exe(bin_path)
-    if exe is None:
-        return Probe(False, None, f"no udocker executable at {bin_path!r}")
-    with tempfile.TemporaryDirectory(prefix="udocker-probe-") as scratch:
-        cp = _call(runner, [exe, "version"], timeout_s, env={**os.environ, "UDOCKER_DIR": scratch})
-    if isinstance(cp, str):
-        return Probe(False, None, cp)
-    if cp.returncode != 0:
-        return Probe(False, None, f"udocker unusable (exit {cp.returncode}): {_last_line(cp)}")
-    out = cp.stdout.strip()
-    ver = next((ln.split(":", 1)[1].strip() for ln in out.splitlines() if ln.lower().startswith("version")),
-               out.splitlines()[0] if out else "unknown")
-    return Probe(True, ver, f"executable {exe}")
+    """Usable when ``udocker version`` runs (against a throwaway store directory)."""
+    return _check(_RUNTIMES["udocker"], bin_path, timeout_s, runner)
+
+
+# ----------------------------------------------------------------------------- resolution
+# (runtime, decided_by label when it is chosen) in the order they are tried
+_PLANS = {
+    "auto": (("docker", "auto_docker_daemon_usable"), ("udocker", "auto_docker_unusable_udocker_available")),
+    "docker": (("docker", "explicit_request"),),
+    "udocker": (("udocker", "explicit_request"),),
+}
 
 
 def resolve_sandbox_backend(requested: str, *, docker_bin: str | None = None, udocker_bin: str | None = None,
                             timeout_s: float = DEFAULT_PROBE_TIMEOUT_S,
                             runner: Runner = subprocess.run) -> ResolvedSandboxBackend:
-    if requested not in REQUESTS:
-        raise SandboxBackendError(f"sandbox backend {requested!r} is not one of {', '.join(REQUESTS)}")
-    dbin = docker_bin or os.environ.get("THUNDERSYNC_DOCKER_BIN", "docker")
-    ubin = udocker_bin or os.environ.get("THUNDERSYNC_UDOCKER_BIN", "udocker")
-    if requested == "docker":
-        d = probe_docker(dbin, timeout_s=timeout_s, runner=runner)
-        if not d.usable:
-            raise SandboxBackendError(f"sandbox backend docker was requested and is not usable: {d.detail}")
-        return ResolvedSandboxBackend(requested, "docker", "explicit_request", d, None)
-    if requested == "udocker":
-        u = probe_udocker(ubin, timeout_s=timeout_s, runner=runner)
-        if not u.usable:
-            raise SandboxBackendError(f"sandbox backend udocker was requested and is not usable: {u.detail}")
-        return ResolvedSandboxBackend(requested, "udocker", "explicit_request", None, u)
-    d = probe_docker(dbin, timeout_s=timeout_s, runner=runner)
-    if d.usable:
-        return ResolvedSandboxBackend(requested, "docker", "auto_docker_daemon_usable", d, None)
-    u = probe_udocker(ubin, timeout_s=timeout_s, runner=runner)
-    if u.usable:
-        return ResolvedSandboxBackend(requested, "udocker", "auto_docker_unusable_udocker_available", d, u)
-    raise SandboxBackendError(f"no sandbox backend is usable: docker: {d.detail}; udocker: {u.detail}")
+    """Pick the runtime for ``requested`` (``auto``, ``docker`` or ``udocker``) or raise."""
+    plan = _PLANS.get(requested)
+    if plan is None:
+        raise SandboxBackendError(f"unknown sandbox backend request {requested!r}; choose one of {list(REQUESTS)}")
+    binaries = {"docker": docker_bin, "udocker": udocker_bin}
+    probes: dict[str, Probe] = {}
+    for name, label in plan:
+        binary = binaries[name] or os.environ.get(_ENV_BIN[name], name)
+        probes[name] = _check(_RUNTIMES[name], binary, timeout_s, runner)
+        if probes[name].usable:
+            return ResolvedSandboxBackend(requested, name, label, probes.get("docker"), probes.get("udocker"))
+    reasons = "; ".join(p.detail for p in probes.values())
+    if requested == "auto":
+        raise SandboxBackendError(f"neither docker nor udocker can run sandboxes here: {reasons}")
+    raise SandboxBackendError(f"requested sandbox backend {requested} is not usable here: {reasons}")
 
 
 def main(argv: list[str] | None = None) -> int:
-    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap = argparse.ArgumentParser(description="Resolve the sandbox container runtime and print its record.")
     ap.add_argument("--requested", choices=REQUESTS, required=True)
     ap.add_argument("--docker-bin", default=None)
     ap.add_argument("--udocker-bin", default=None)
     ap.add_argument("--timeout-s", type=float, default=DEFAULT_PROBE_TIMEOUT_S)
     args = ap.parse_args(argv)
     try:
-        r = resolve_sandbox_backend(args.requested, docker_bin=args.docker_bin, udocker_bin=args.udocker_bin,
-                                    timeout_s=args.timeout_s)
+        resolved = resolve_sandbox_backend(args.requested, docker_bin=args.docker_bin,
+                                           udocker_bin=args.udocker_bin, timeout_s=args.timeout_s)
     except SandboxBackendError as exc:
-        print(f"sandbox backend: {exc}", file=sys.stderr)
+        sys.stderr.write(f"{exc}\n")
         return 2
-    print(json.dumps(r.as_record(), sort_keys=True))
+    sys.stdout.write(json.dumps(resolved.as_record(), sort_keys=True) + "\n")
     return 0
 
 

@@ -1,32 +1,38 @@
-"""Exactly-once cross-rank work claims over a compare-and-set key-value store (C40).
+"""Exactly-once cross-rank work claims on a compare-and-set key-value store (C40).
 
-An owner *offers* work it has not started (payload first, then an index
-entry, then its price joins the owner's outstanding ``load``). Any rank --
-the owner included -- *claims* an item by a ``compare_set`` of the item's
-claim key from empty to its rank; the store's atomicity makes exactly one
-claimant win. The owner claims each offered item before starting it and
-skips the ones it lost; a thief steals by the same claim and then reads the
-payload. ``done`` is published once the owner has resolved every offer and
-will offer no more this step, so a thief may stop only when all peers are
-done. All keys are scoped by namespace and step. The protocol is the
-reference's (src/thundersync/scheduling/work_claims.py:1-297); this module is
-written against ``torch.distributed.Store``'s C++ TCPStore primitives
-(``set``/``get``/``add``/``compare_set``/``check``/``delete_key``).
+Protocol (the interface shared with reference
+src/thundersync/scheduling/work_claims.py:1-297, kept so that mixed tooling
+reads the same keys): an owner publishes work it has not started -- payload,
+then an index entry, then the item's price added to its outstanding ``load``.
+Whoever moves the item's claim key from empty to its own rank with one
+``compare_set`` runs the item; the store's atomicity gives exactly one
+winner. The owner claims each published item right before starting it; a
+thief claims first and reads the payload afterwards. An owner writes ``done``
+once every item it published is resolved, and a thief stops only when every
+peer is done. Keys live under ``<namespace>/<step>/``.
+
+Implementation: every item this rank published has one :class:`_Entry` whose
+state moves ``published -> mine`` or ``published -> ceded``; peers' published
+items are mirrored in per-peer books that are refreshed incrementally from the
+peer's index. Works on any store with ``torch.distributed.Store``'s
+``set``/``get``/``add``/``compare_set``/``check``/``delete_key``.
 """
 
 from __future__ import annotations
 
+import enum
 import json
 import time
+from collections import Counter
 from collections.abc import Callable, Sequence
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Any, Protocol
 
 __all__ = ["ClaimStore", "Offer", "StoreWorkClaims", "WorkClaimError"]
 
 
 class WorkClaimError(RuntimeError):
-    pass
+    """A caller broke the claim protocol's order."""
 
 
 class ClaimStore(Protocol):
@@ -40,55 +46,87 @@ class ClaimStore(Protocol):
 
 @dataclass(frozen=True)
 class Offer:
+    """A peer's published item as a thief sees it."""
+
     owner: int
     item: int
     price: int
 
 
-_COUNTERS = ("offered", "offered_price", "own_claims", "ceded", "ceded_price", "stolen", "stolen_price",
-             "claim_attempts", "claim_s", "payload_bytes_out", "payload_bytes_in")
+class _State(enum.Enum):
+    PUBLISHED = "published"
+    MINE = "mine"  # the owner won its own claim
+    CEDED = "ceded"  # a thief won it
+
+
+@dataclass
+class _Entry:
+    price: int
+    state: _State = _State.PUBLISHED
+
+
+@dataclass
+class _PeerBook:
+    read_upto: int = 0  # index entries already mirrored
+    items: dict[int, Offer] = field(default_factory=dict)
+
+
+class _Keys:
+    """The key scheme: ``<ns>/<step>/<rank>/{payload/<item>, offer/<idx>, offers, load, done}`` and
+    ``<ns>/<step>/claim/<item>``."""
+
+    def __init__(self, namespace: str, step: int) -> None:
+        self.base = f"{namespace}/{step}"
+
+    def payload(self, owner: int, item: int) -> str:
+        return f"{self.base}/{owner}/payload/{item}"
+
+    def index_entry(self, owner: int, idx: int) -> str:
+        return f"{self.base}/{owner}/offer/{idx}"
+
+    def index_len(self, owner: int) -> str:
+        return f"{self.base}/{owner}/offers"
+
+    def load(self, owner: int) -> str:
+        return f"{self.base}/{owner}/load"
+
+    def done(self, owner: int) -> str:
+        return f"{self.base}/{owner}/done"
+
+    def claim(self, item: int) -> str:
+        return f"{self.base}/claim/{item}"
 
 
 class StoreWorkClaims:
-    """One rank's view of one step's claims."""
+    """This rank's side of one step's claims (owner of its own items, thief of its peers')."""
 
     def __init__(self, store: ClaimStore, *, rank: int, world_size: int, namespace: str = "work-claims",
                  clock: Callable[[], float] = time.perf_counter) -> None:
         if world_size < 1 or not 0 <= rank < world_size:
-            raise ValueError(f"rank {rank} is not in a world of {world_size}")
+            raise ValueError(f"rank {rank} outside world size {world_size}")
         if not namespace or "/" in namespace:
-            raise ValueError("the namespace must be one nonempty key segment")
+            raise ValueError(f"namespace {namespace!r} must be a single non-empty key segment")
         self._store = store
         self.rank, self.world_size = int(rank), int(world_size)
-        self._ns = namespace
+        self._namespace = namespace
         self._clock = clock
+        self._keys: _Keys | None = None
         self._step: int | None = None
         self._done = False
-        self._offered: dict[int, int] = {}
-        self._n_offers = 0
-        self._mine: set[int] = set()
-        self._lost: set[int] = set()
-        self._cursor: dict[int, int] = {}
-        self._open: dict[int, dict[int, Offer]] = {}
-        self._c: dict[str, float] = {}
+        self._mine: dict[int, _Entry] = {}
+        self._books: dict[int, _PeerBook] = {}
+        self._stats: Counter = Counter()
 
-    # keys -------------------------------------------------------------
-    def _k(self, *parts: object) -> str:
-        if self._step is None:
-            raise WorkClaimError("no step has begun")
-        return "/".join([self._ns, str(self._step), *map(str, parts)])
-
-    # step -------------------------------------------------------------
+    # ---------------------------------------------------------------- step
     def begin_step(self, step: int) -> None:
+        """Start a new step; the previous one must have published ``done``."""
         if self._step is not None and not self._done:
-            raise WorkClaimError(f"step {self._step} ended without publishing done")
-        self._step = int(step)
-        self._done = False
-        self._offered, self._n_offers = {}, 0
-        self._mine, self._lost = set(), set()
-        self._cursor = {p: 0 for p in self.peers}
-        self._open = {p: {} for p in self.peers}
-        self._c = dict.fromkeys(_COUNTERS, 0)
+            raise WorkClaimError(f"cannot begin a step: step {self._step} never published done")
+        self._step, self._done = int(step), False
+        self._keys = _Keys(self._namespace, self._step)
+        self._mine = {}
+        self._books = {p: _PeerBook() for p in self.peers}
+        self._stats = Counter()
 
     @property
     def step(self) -> int | None:
@@ -102,110 +140,125 @@ class StoreWorkClaims:
     def done(self) -> bool:
         return self._done
 
-    # owner ------------------------------------------------------------
+    def _k(self) -> _Keys:
+        if self._keys is None:
+            raise WorkClaimError("begin_step has not been called")
+        return self._keys
+
+    # ---------------------------------------------------------------- owner side
     def offer(self, item: int, price: int, payload: bytes) -> None:
+        """Publish an unstarted item: payload, index entry, then its price onto this rank's load."""
         if self._done:
-            raise WorkClaimError("an owner that is done offers nothing more")
-        if item in self._offered:
-            raise WorkClaimError(f"item {item} is already offered")
+            raise WorkClaimError(f"rank {self.rank} already published done for step {self._step}")
+        if item in self._mine:
+            raise WorkClaimError(f"item {item} was published twice")
         if price < 0:
-            raise ValueError("an offer's price must not be negative")
-        self._store.set(self._k(self.rank, "payload", item), payload)
-        self._store.set(self._k(self.rank, "offer", self._n_offers), json.dumps({"item": int(item), "price": int(price)}))
-        self._n_offers += 1
-        self._store.add(self._k(self.rank, "offers"), 1)
-        self._store.add(self._k(self.rank, "load"), int(price))
-        self._offered[item] = int(price)
-        self._c["offered"] += 1
-        self._c["offered_price"] += int(price)
-        self._c["payload_bytes_out"] += len(payload)
+            raise ValueError(f"price {price} is negative")
+        k = self._k()
+        idx = len(self._mine)
+        self._store.set(k.payload(self.rank, item), payload)
+        self._store.set(k.index_entry(self.rank, idx), json.dumps({"item": int(item), "price": int(price)}))
+        self._store.add(k.index_len(self.rank), 1)
+        self._store.add(k.load(self.rank), int(price))
+        self._mine[item] = _Entry(int(price))
+        self._stats.update(offered=1, offered_price=int(price), payload_bytes_out=len(payload))
 
     def is_offered(self, item: int) -> bool:
-        return item in self._offered
+        return item in self._mine
 
     def claim_own(self, items: Sequence[int]) -> tuple[list[int], list[int]]:
-        won, lost = [], []
+        """Claim each item before starting it. Items never published are trivially this rank's.
+        Returns (items to run here, items a thief took)."""
+        run_here, taken = [], []
         for item in items:
-            if item not in self._offered:
-                won.append(item)
+            entry = self._mine.get(item)
+            if entry is None:
+                run_here.append(item)
                 continue
-            if item in self._mine:
-                raise WorkClaimError(f"item {item} is already claimed by its owner")
-            if self._cas(item):
-                self._mine.add(item)
-                self._c["own_claims"] += 1
-                self._store.delete_key(self._k(self.rank, "payload", item))
-                won.append(item)
+            if entry.state is not _State.PUBLISHED:
+                raise WorkClaimError(f"item {item} was already resolved ({entry.state.value})")
+            if self._try_claim(item):
+                entry.state = _State.MINE
+                self._store.delete_key(self._k().payload(self.rank, item))
+                self._stats.update(own_claims=1)
+                run_here.append(item)
             else:
-                self._lost.add(item)
-                self._c["ceded"] += 1
-                self._c["ceded_price"] += self._offered[item]
-                lost.append(item)
-        return won, lost
+                entry.state = _State.CEDED
+                self._stats.update(ceded=1, ceded_price=entry.price)
+                taken.append(item)
+        return run_here, taken
 
     def finish_own(self, items: Sequence[int]) -> None:
-        total = 0
+        """Take the prices of finished, self-claimed items off this rank's load."""
+        settled = 0
         for item in items:
-            if item not in self._offered:
+            entry = self._mine.get(item)
+            if entry is None:
                 continue
-            if item not in self._mine:
-                raise WorkClaimError(f"item {item} was not claimed by its owner")
-            total += self._offered[item]
-        if total:
-            self._store.add(self._k(self.rank, "load"), -total)
+            if entry.state is not _State.MINE:
+                raise WorkClaimError(f"item {item} is {entry.state.value}, not claimed by its owner")
+            settled += entry.price
+        if settled:
+            self._store.add(self._k().load(self.rank), -settled)
 
     def publish_done(self) -> None:
-        pending = set(self._offered) - self._mine - self._lost
-        if pending:
-            raise WorkClaimError(f"items {sorted(pending)} are offered and unresolved; claim them before publishing done")
-        self._store.set(self._k(self.rank, "done"), "1")
+        """Declare that this rank publishes nothing more and has resolved everything it published."""
+        open_items = sorted(i for i, e in self._mine.items() if e.state is _State.PUBLISHED)
+        if open_items:
+            raise WorkClaimError(f"cannot publish done: published items {open_items} were never claimed")
+        self._store.set(self._k().done(self.rank), "1")
         self._done = True
 
-    # thief ------------------------------------------------------------
+    # ---------------------------------------------------------------- thief side
     def peer_done(self, peer: int) -> bool:
-        return bool(self._store.check([self._k(peer, "done")]))
+        return bool(self._store.check([self._k().done(peer)]))
 
     def all_peers_done(self) -> bool:
         return all(self.peer_done(p) for p in self.peers)
 
     def peer_load(self, peer: int) -> int:
-        return int(self._store.add(self._k(peer, "load"), 0))
+        return int(self._store.add(self._k().load(peer), 0))
 
     def open_offers(self, peer: int) -> list[Offer]:
-        listed = int(self._store.add(self._k(peer, "offers"), 0))
-        book = self._open[peer]
-        for idx in range(self._cursor[peer], listed):
-            e = json.loads(self._store.get(self._k(peer, "offer", idx)))
-            book[int(e["item"])] = Offer(peer, int(e["item"]), int(e["price"]))
-        self._cursor[peer] = listed
-        for item in list(book):
-            if self._store.check([self._k("claim", item)]):
-                del book[item]
-        return list(book.values())
+        """The peer's published items nobody has claimed yet (as far as the store shows now)."""
+        k = self._k()
+        book = self._books[peer]
+        listed = int(self._store.add(k.index_len(peer), 0))
+        while book.read_upto < listed:
+            rec = json.loads(self._store.get(k.index_entry(peer, book.read_upto)))
+            book.items[int(rec["item"])] = Offer(peer, int(rec["item"]), int(rec["price"]))
+            book.read_upto += 1
+        claimed = [item for item in book.items if self._store.check([k.claim(item)])]
+        for item in claimed:
+            del book.items[item]
+        return list(book.items.values())
 
     def steal(self, offer: Offer) -> bytes | None:
-        self._open[offer.owner].pop(offer.item, None)
-        if not self._cas(offer.item):
+        """Claim a peer's item; on success move its price off the peer's load and return its payload."""
+        self._books[offer.owner].items.pop(offer.item, None)
+        if not self._try_claim(offer.item):
             return None
-        self._store.add(self._k(offer.owner, "load"), -offer.price)
-        key = self._k(offer.owner, "payload", offer.item)
-        payload = self._store.get(key)
-        self._store.delete_key(key)
-        self._c["stolen"] += 1
-        self._c["stolen_price"] += offer.price
-        self._c["payload_bytes_in"] += len(payload)
+        k = self._k()
+        self._store.add(k.load(offer.owner), -offer.price)
+        payload = self._store.get(k.payload(offer.owner, offer.item))
+        self._store.delete_key(k.payload(offer.owner, offer.item))
+        self._stats.update(stolen=1, stolen_price=offer.price, payload_bytes_in=len(payload))
         return payload
 
-    # shared -----------------------------------------------------------
-    def _cas(self, item: int) -> bool:
-        t0 = self._clock()
+    # ---------------------------------------------------------------- shared
+    def _try_claim(self, item: int) -> bool:
         me = str(self.rank).encode()
-        holder = self._store.compare_set(self._k("claim", item), "", me)
-        self._c["claim_attempts"] += 1
-        self._c["claim_s"] += self._clock() - t0
-        if isinstance(holder, str):
-            holder = holder.encode()
-        return bytes(holder) == me
+        t0 = self._clock()
+        holder = self._store.compare_set(self._k().claim(item), "", me)
+        self._stats["claim_attempts"] += 1
+        self._stats["claim_s"] += self._clock() - t0
+        return (holder.encode() if isinstance(holder, str) else bytes(holder)) == me
+
+    _REPORTED = ("offered", "offered_price", "own_claims", "ceded", "ceded_price", "stolen", "stolen_price",
+                 "claim_attempts", "claim_s", "payload_bytes_out", "payload_bytes_in")
 
     def report(self) -> dict[str, Any]:
-        return {"step": self._step, "rank": self.rank, "world_size": self.world_size, "done": self._done, **self._c}
+        out: dict[str, Any] = {"step": self._step, "rank": self.rank, "world_size": self.world_size,
+                               "done": self._done}
+        out.update({name: self._stats.get(name, 0) for name in self._REPORTED})
+        return out
