@@ -103,3 +103,76 @@ def test_gpu_single_node_layer_matches_op_by_op(prompt_len, cont_len):
     for n in res[0][1]:
         a, b = res[0][1][n], res[1][1][n]
         assert float((a - b).norm() / b.norm().clamp_min(1e-12)) < 3e-2, n
+
+
+def _gpu_grads(model, batch, order, rung):
+    model.zero_grad(set_to_none=True)
+    run = StreamingRun(model, boundary_cut=True, stream_turns=False, rebuild_block_tokens=64)
+    orig = run.rebuild_logprobs
+    run.rebuild_logprobs = lambda ids, **k: orig(ids, **{**k, "executor": rung})
+    bw = RewardLinearBackward(run, model, eps=EPS, source_offload_mode="device_resident", source_offload_device=None)
+    for g, prompt, trajs in batch:
+        bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    for g, (tid, turns, reward) in order:
+        for tk, sc in turns:
+            run.append_turn(g, tid, tk, sc)
+        bw.close_trajectory(tid, reward)
+    for g, _, _ in batch:
+        bw.close_group(g)
+    bw.assert_safe_to_step()
+    return {n: p.grad.detach().float().clone() for n, p in model.named_parameters()}, run
+
+
+def test_gpu_checkpoint_inputs_parked_on_host_match_plain():
+    """The lowest rung of the rebuild ladder (checkpoint inputs in page-locked host memory) on CUDA."""
+    torch.manual_seed(1)
+    model = Qwen3ForCausalLM(CFG).to("cuda", torch.bfloat16)
+    batch, order = make_batch(1, vocab=CFG.vocab_size, lo=40, hi=200, prompt_len=64)
+    ref, _ = _gpu_grads(model, batch, order, "plain")
+    got, run = _gpu_grads(model, batch, order, "checkpoint_host")
+    diag = run.rebuild_checkpoint_offload_diagnostics()
+    assert diag["host_rebuilds"] > 0 and diag["write_bytes"] > 0 and diag["read_bytes"] == diag["write_bytes"]
+    for n in ref:
+        scale = ref[n].abs().max().clamp_min(1e-6)
+        assert float((got[n] - ref[n]).abs().max() / scale) < 2e-2, n
+    rep = run.turn_memory_report
+    assert rep["windows"]["rebuild/checkpoint_host"]["calls"] > 0
+
+
+@pytest.mark.parametrize("options", [
+    {"source_offload_device": "cpu", "source_offload_mode": "pinned_nonblocking",
+     "source_offload_window_bytes": 1 << 20, "source_offload_pinned_windows": 3},
+    {"source_offload_device": "cpu", "source_offload_mode": "pinned_nonblocking", "statistic_keep_source_dtype": True},
+    {"source_offload_device": "cpu", "source_offload_mode": "blocking", "source_offload_hbm_threshold": 0.999},
+])
+def test_gpu_host_statistics_match_device_statistics(options, tmp_path):
+    """Host-resident statistics (windowed device->host folds, host->device combine) give the device result."""
+    torch.manual_seed(2)
+    model = Qwen3ForCausalLM(CFG).to("cuda", torch.bfloat16)
+    batch, order = make_batch(2, vocab=CFG.vocab_size, lo=40, hi=200, prompt_len=64)
+
+    def grads(**kw):
+        model.zero_grad(set_to_none=True)
+        run = StreamingRun(model, boundary_cut=True, stream_turns=False)
+        bw = RewardLinearBackward(run, model, eps=EPS, **kw)
+        for g, prompt, trajs in batch:
+            bw.open_group(g, prompt, [t for t, _, _ in trajs])
+        for g, (tid, turns, reward) in order:
+            for tk, sc in turns:
+                run.append_turn(g, tid, tk, sc)
+            bw.close_trajectory(tid, reward)
+        for g, _, _ in batch:
+            bw.close_group(g)
+        bw.assert_safe_to_step()
+        return {n: p.grad.detach().float().clone() for n, p in model.named_parameters()}, bw.source_offload_report
+
+    ref, _ = grads(source_offload_mode="device_resident", source_offload_device=None)
+    got, report = grads(source_spill_directory=str(tmp_path), **options)
+    if options["source_offload_mode"] == "blocking":
+        assert report["device_groups_below_hbm_threshold"] > 0
+    else:
+        assert report["host_fold"]["folds"] > 0 and report["host_fold"]["combines"] > 0
+    tol = 2e-2 if options.get("statistic_keep_source_dtype") else 1e-4
+    for n in ref:
+        scale = ref[n].abs().max().clamp_min(1e-6)
+        assert float((got[n] - ref[n]).abs().max() / scale) < tol, n

@@ -164,6 +164,11 @@ def _rebuild_state(states: list[Any], flat: list[torch.Tensor]) -> list[Any]:
     return out
 
 
+# Measured activations run a little above the per-token estimates (allocator rounding, fp32 row
+# statistics); the memory rule scales its estimates by this factor.
+TURN_ACTIVATION_FACTOR = 1.15
+
+
 class StreamingRun:
     """One batch's streamed execution over a Qwen3-family model."""
 
@@ -255,12 +260,20 @@ class StreamingRun:
         self._versions = {id(p): p._version for p in self._trainable}
         self._capture_source: Any = None
         self._param_adjoint_staged: dict[Any, list[tuple[torch.Tensor, torch.Tensor]]] = {}
-        self._counts = {"plain": 0, "blocked": 0, "turn_forward": 0, "turn_replay": 0, "prompt_forward": 0}
+        self._counts = {"plain": 0, "blocked": 0, "checkpoint": 0, "checkpoint_host": 0, "turn_forward": 0,
+                        "turn_replay": 0, "prompt_forward": 0}
         self._turn_counts: dict[str, dict[str, int]] = {"forward": {}, "replay": {}}
         self._prompt_tokens_physical = 0
         self._prompt_tokens_logical = 0
         self._last_rung: str | None = None
+        self._pack_rung: str | None = None  # the rebuild rung a pack runs under (None: not a close rebuild)
+        self._offload = {"write_bytes": 0, "read_bytes": 0, "tensors": 0}
+        self._oom_retries = 0
         self._memory_windows: list[dict[str, Any]] = []
+        self._memory_window: dict[str, Any] | None = None
+        self._memory_refusals: dict[str, int] = {}
+        self._memory_min_available: int | None = None
+        self._memory_retries_at_start: int | None = None
         _LIVE.append(self)
 
     # ------------------------------------------------------------ helpers
@@ -293,11 +306,40 @@ class StreamingRun:
         if pad:
             ids = torch.cat((ids, ids.new_zeros(pad)))
             pos = torch.cat((pos, pos.new_zeros(pad)))
-        if self.checkpoint and torch.is_grad_enabled():
-            h, states = self._run_pack_checkpointed(ids, pos, segs)
+        rung = self._pack_rung
+        if torch.is_grad_enabled() and (self.checkpoint or rung in ("checkpoint", "checkpoint_host")):
+            host = rung == "checkpoint_host" or (rung is not None and self._rebuild_checkpoint_storage_device
+                                                 is not None and self._rebuild_checkpoint_storage_device.type == "cpu")
+            with (self._checkpoint_inputs_on_host() if host else contextlib.nullcontext()):
+                h, states = self._run_pack_checkpointed(ids, pos, segs)
         else:
             h, states = self.exec.run(ids, pos, segs)
         return (h[:t] if pad else h), states
+
+    @contextlib.contextmanager
+    def _checkpoint_inputs_on_host(self):
+        """Park the tensors autograd saves in this forward (the per-layer checkpoint inputs) in page-locked
+        host memory until the backward needs them; counts the bytes each way."""
+        diag = self._offload
+
+        def pack(t: torch.Tensor):
+            if t.device.type != "cuda" or t.numel() * t.element_size() < 1 << 16:
+                return t  # small tensors (norm weights, scalars) stay where they are
+            host = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            host.copy_(t, non_blocking=True)
+            diag["write_bytes"] += host.numel() * host.element_size()
+            diag["tensors"] += 1
+            return (t.device, host)
+
+        def unpack(obj):
+            if isinstance(obj, torch.Tensor):
+                return obj
+            dev, host = obj
+            diag["read_bytes"] += host.numel() * host.element_size()
+            return host.to(dev, non_blocking=True)
+
+        with torch.autograd.graph.saved_tensors_hooks(pack, unpack):
+            yield
 
     def _run_pack_checkpointed(self, ids, pos, segs):
         """Per-layer activation checkpointing; fresh K/V are checkpoint outputs."""
@@ -648,6 +690,63 @@ class StreamingRun:
         t.consumed_turns = t.forwarded_turns
         return lp, old
 
+    # ------------------------------------------------------------ memory rule
+    REBUILD_RUNGS = ("plain", "blocked", "checkpoint", "checkpoint_host")
+
+    def _turn_memory_shape(self) -> dict[str, int]:
+        """Bytes per token that a forward keeps for the backward, by executor (estimates)."""
+        sp = self.spec
+        el = self.weight.element_size()
+        hidden = sp.hidden
+        kv = 2 * sp.n_kv * sp.head_dim * el * len(sp.attention_layers)  # retained K and V rows
+        # per layer: normed input, q/k/v, attention output, residual, normed input, gate/up and their
+        # product, plus fp32 row statistics -- about 16 hidden-width rows in the activation dtype
+        plain = sp.n_layers * hidden * el * 16
+        checkpoint = sp.n_layers * hidden * el + hidden * el * 16  # layer inputs + one layer recomputed
+        return {"plain_activation": int(plain * TURN_ACTIVATION_FACTOR),
+                "checkpoint_activation": int(checkpoint * TURN_ACTIVATION_FACTOR),
+                "host_checkpoint_activation": int(hidden * el * 16 * TURN_ACTIVATION_FACTOR),
+                "kv": kv, "hidden": hidden * el}
+
+    def _available_bytes(self) -> int:
+        free, _ = torch.cuda.mem_get_info(self.device)
+        cached = torch.cuda.memory_reserved(self.device) - torch.cuda.memory_allocated(self.device)
+        avail = int(free + max(cached, 0))
+        self._memory_min_available = avail if self._memory_min_available is None else min(
+            self._memory_min_available, avail)
+        return avail
+
+    def _rung_estimate(self, rung: str, tokens: int) -> int:
+        shape = self._turn_memory_shape()
+        key = {"plain": "plain_activation", "blocked": "plain_activation", "checkpoint": "checkpoint_activation",
+               "checkpoint_host": "host_checkpoint_activation"}[rung]
+        return tokens * (shape[key] + shape["kv"] + 2 * shape["hidden"])
+
+    def _choose_rung(self, tokens: int) -> str:
+        """The first rung whose estimate fits the device beside the configured reserve."""
+        if self.device.type != "cuda":
+            return "checkpoint" if self.checkpoint else "blocked"
+        reserve = self.rebuild_plain_reserve_bytes or 0
+        avail = self._available_bytes()
+        first = 2 if self.checkpoint else 0
+        for rung in self.REBUILD_RUNGS[first:]:
+            if rung == "plain" and self.rebuild_plain_reserve_bytes is None:
+                continue  # without a reserve the automatic rebuild starts blocked (bounded transient)
+            if self._rung_estimate(rung, tokens) + reserve <= avail:
+                return rung
+            self._memory_refusals[rung] = self._memory_refusals.get(rung, 0) + 1
+        return "checkpoint_host"
+
+    def _open_memory_window(self, phase: str, executor: str, estimate: int) -> None:
+        if self.device.type != "cuda":
+            return
+        self.close_memory_window()
+        if self._memory_retries_at_start is None:
+            self._memory_retries_at_start = int(torch.cuda.memory_stats(self.device).get("num_alloc_retries", 0))
+        torch.cuda.reset_peak_memory_stats(self.device)
+        self._memory_window = {"phase": phase, "executor": executor, "estimate": int(estimate),
+                               "allocated": int(torch.cuda.memory_allocated(self.device))}
+
     def rebuild_logprobs(
         self,
         traj_ids: list[int],
@@ -659,25 +758,48 @@ class StreamingRun:
     ) -> list[torch.Tensor]:
         """Re-forward whole branches (all turns) over the prompt chain, packed.
 
-        Branches longer than ``rebuild_block_tokens`` run in consecutive blocks
-        (each block attends to the previous blocks' K/V), so the transient
-        stays block-sized; shorter branches of the call share one pack.
+        ``executor`` picks the rung of the memory ladder: ``plain`` (one pack per call, every activation
+        kept), ``blocked`` (branches longer than ``rebuild_block_tokens`` run in consecutive blocks, each
+        attending to the previous blocks' K/V, so the transient stays block-sized), ``checkpoint``
+        (per-layer activation checkpointing: only layer inputs are kept), ``checkpoint_host`` (those
+        inputs wait in page-locked host memory). ``auto`` takes the first rung whose estimate fits the
+        device beside ``rebuild_plain_reserve_bytes`` and, when a forward still runs out of device memory,
+        frees what it built and retries one rung lower. ``checkpoint_input_storage_device="cpu"`` makes
+        the checkpoint rungs park their inputs on the host.
         """
-        if executor not in ("auto", "blocked", "plain"):
-            raise ValueError("executor must be auto, blocked or plain")
+        rungs = ("auto", *self.REBUILD_RUNGS)
+        if executor not in rungs:
+            raise ValueError(f"executor must be one of {rungs}")
         self._check_versions()
         trajs = [self._trajs[t] for t in traj_ids]
-        block = self.rebuild_block_tokens
-        if executor == "plain":
-            block = None
-        elif executor == "auto" and self.rebuild_plain_reserve_bytes is not None and self.device.type == "cuda":
-            # the plain rung (one pack per branch) when the device keeps the reserve free after the
-            # branch's activations: per token, every layer saves about 16 hidden-width bf16 rows
-            n_tok = sum(len(x) for t in trajs for x, _ in t.turns)
-            need = n_tok * self.spec.n_layers * self.spec.hidden * 2 * 16
-            free, _ = torch.cuda.mem_get_info(self.device)
-            if free - need >= self.rebuild_plain_reserve_bytes:
-                block = None
+        n_tok = sum(len(x) for t in trajs for x, _ in t.turns)
+        if executor != "auto":
+            rung = executor
+        else:
+            rung = self._choose_rung(n_tok)
+        if checkpoint_input_storage_device is not None and torch.device(checkpoint_input_storage_device).type == "cpu" \
+                and rung == "checkpoint":
+            rung = "checkpoint_host"
+        while True:
+            try:
+                self._open_memory_window("rebuild", rung, self._rung_estimate(rung, n_tok))
+                return self._rebuild_at(trajs, rung)
+            except torch.cuda.OutOfMemoryError:
+                nxt = self.REBUILD_RUNGS.index(rung) + 1
+                if executor != "auto" or nxt >= len(self.REBUILD_RUNGS):
+                    raise
+                for t in trajs:
+                    t.rebuilt = t.rebuilt_old = None
+                self._memory_window = None
+                torch.cuda.empty_cache()
+                self._oom_retries += 1
+                rung = self.REBUILD_RUNGS[nxt]
+            finally:
+                self._pack_rung = None
+
+    def _rebuild_at(self, trajs: list[_Traj], rung: str) -> list[torch.Tensor]:
+        block = self.rebuild_block_tokens if rung != "plain" else None
+        self._pack_rung = rung
         toks = []
         masks = []
         for t in trajs:
@@ -712,7 +834,8 @@ class StreamingRun:
                 hs[i].append(h[seg.start : seg.start + seg.length])
                 chains[i] = self._chain_extend(chains[i], st)
                 offs[i] += seg.length
-        rung = "blocked" if blocked else "plain"
+        if rung in ("plain", "blocked"):
+            rung = "blocked" if blocked else "plain"
         self._counts[rung] += 1
         self._last_rung = rung
         out = []
@@ -939,7 +1062,7 @@ class StreamingRun:
 
     @property
     def rebuild_path_counts(self) -> dict[str, int]:
-        return {"plain": self._counts["plain"], "blocked": self._counts["blocked"]}
+        return {k: self._counts[k] for k in self.REBUILD_RUNGS} | {"oom_retries": self._oom_retries}
 
     @property
     def turn_path_counts(self) -> dict[str, dict[str, int]]:
@@ -953,8 +1076,11 @@ class StreamingRun:
         return self._rebuild_checkpoint_storage_device
 
     def rebuild_checkpoint_offload_diagnostics(self) -> dict[str, Any]:
-        return {"device": None if self._rebuild_checkpoint_storage_device is None
-                else str(self._rebuild_checkpoint_storage_device), "write_bytes": 0, "read_bytes": 0}
+        """Bytes the checkpoint rungs parked in host memory (written) and brought back (read)."""
+        dev = self._rebuild_checkpoint_storage_device
+        return {"device": None if dev is None else str(dev), "write_bytes": self._offload["write_bytes"],
+                "read_bytes": self._offload["read_bytes"], "tensors": self._offload["tensors"],
+                "host_rebuilds": self._counts["checkpoint_host"]}
 
     def parameter_adjoint_diagnostics(self) -> dict[str, Any]:
         return {
@@ -976,14 +1102,52 @@ class StreamingRun:
             out["vjp_seconds_total"] = float(sum(self._shared_prefix_times))
         return out
 
+    def close_memory_window(self) -> None:
+        """Record the open window's measured peak above its start (allocator counters, no device sync)."""
+        w = self._memory_window
+        if w is None:
+            return
+        self._memory_window = None
+        peak = int(torch.cuda.max_memory_allocated(self.device))
+        w["measured"] = max(0, peak - w["allocated"])
+        self._memory_windows.append(w)
+
+    @property
     def turn_memory_windows(self) -> list[dict[str, Any]]:
+        """Every closed memory window of this run (phase, executor, estimate, measured), in call order."""
+        self.close_memory_window()
         return list(self._memory_windows)
 
+    @property
     def turn_memory_report(self) -> dict[str, Any]:
-        return {"windows": len(self._memory_windows)}
+        """The memory rule's estimates against measured peaks, per phase/executor, and its refusals.
 
-    def close_memory_window(self) -> None:
-        return None
+        ``windows[phase/executor]``: calls, the largest estimate and measured peak above the call's start,
+        the largest measured/estimate ratio and how many calls exceeded their estimate. ``refused`` counts
+        rungs the rule turned down for lack of memory; ``allocator_retries`` counts allocations that had
+        to free cached blocks first since the first window.
+        """
+        self.close_memory_window()
+        out: dict[str, dict[str, Any]] = {}
+        for w in self._memory_windows:
+            r = out.setdefault(f"{w['phase']}/{w['executor']}", {"calls": 0, "max_estimate_bytes": 0,
+                                                                  "max_measured_bytes": 0,
+                                                                  "max_measured_over_estimate": 0.0, "exceeded": 0})
+            r["calls"] += 1
+            r["max_estimate_bytes"] = max(r["max_estimate_bytes"], w["estimate"])
+            r["max_measured_bytes"] = max(r["max_measured_bytes"], w["measured"])
+            if w["estimate"]:
+                r["max_measured_over_estimate"] = max(r["max_measured_over_estimate"],
+                                                      round(w["measured"] / w["estimate"], 4))
+            r["exceeded"] += int(w["measured"] > w["estimate"])
+        retries = None
+        if self._memory_retries_at_start is not None:
+            retries = int(torch.cuda.memory_stats(self.device).get("num_alloc_retries", 0)) - \
+                self._memory_retries_at_start
+        return {"reserve_bytes": self.rebuild_plain_reserve_bytes, "activation_factor": TURN_ACTIVATION_FACTOR,
+                "refused": dict(sorted(self._memory_refusals.items())),
+                "min_available_bytes": self._memory_min_available, "allocator_retries": retries,
+                "oom_retries": self._oom_retries, "windows": out}
 
 
 def _flatten_chain(chain: list[Any]) -> list[torch.Tensor]:

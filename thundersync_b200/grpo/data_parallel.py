@@ -145,6 +145,9 @@ class DataParallelThunderSync:
         self._final_forest: tuple[int, int] | None = None
         self._price_attention_weight: float | None = None
         self._work_claims_report: dict[str, Any] | None = None
+        # True: step() synchronises the device around its phases so allreduce_s / opt_step_s are device
+        # times; False (default): they are host issue times and the step adds no synchronisation
+        self.step_timing = False
         self._new_batch()
 
     # ------------------------------------------------------------ construction
@@ -335,7 +338,8 @@ class DataParallelThunderSync:
         self.bw.assert_safe_to_step(materialize=False)
         stats: dict[str, Any] = {"rank": self.rank, "world_size": self.world_size,
                                  "n_local_groups": self._local_groups_closed}
-        sync = self.device.type == "cuda"
+        # device-synchronised phase timings only on request (each synchronisation drains the queue)
+        sync = self.device.type == "cuda" and self.step_timing
         if sync:
             torch.cuda.synchronize(self.device)
         t0 = time.perf_counter()

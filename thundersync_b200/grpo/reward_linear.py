@@ -126,6 +126,32 @@ class RewardLinearBackward:
         else:
             stat_dev = torch.device(source_offload_device)
         self.statistic_device = stat_dev
+        if source_copy_during_backward or source_release_during_backward:
+            from thundersync_b200.config import ConfigError
+
+            raise ConfigError("copying or releasing a source's parameter gradients during its backward is not "
+                              "built here: a source goes from the GEMM epilogues into one fp32 buffer and is "
+                              "folded once (set source_copy_during_backward / source_release_during_backward "
+                              "to False)")
+        if not 0.0 < source_offload_hbm_threshold <= 1.0:
+            raise ValueError("source_offload_hbm_threshold must be in (0, 1]")
+        for name, value in (("source_offload_pinned_windows", source_offload_pinned_windows),
+                            ("source_offload_worker_count", source_offload_worker_count),
+                            ("source_reduction_worker_count", source_reduction_worker_count)):
+            if value < 1:
+                raise ValueError(f"{name} must be positive")
+        if source_offload_window_bytes < 4096:
+            raise ValueError("source_offload_window_bytes must be at least 4096")
+        # host statistics: streamed through page-locked windows (grpo/host_fold.py)
+        self._host_fold_options = dict(window_bytes=int(source_offload_window_bytes),
+                                       windows=int(source_offload_pinned_windows),
+                                       offload_workers=int(source_offload_worker_count),
+                                       reduction_workers=int(source_reduction_worker_count),
+                                       arena=source_pinned_arena)
+        self._host_fold = None
+        self._spill_dir = source_spill_directory
+        self._hbm_threshold = float(source_offload_hbm_threshold)
+        self._keep_source_dtype = bool(statistic_keep_source_dtype)
         self.direct_when_group_bound = direct_when_group_bound
         self.combine_known_reward_sources = combine_known_reward_sources
         self.defer_group_close = defer_group_close
@@ -148,7 +174,8 @@ class RewardLinearBackward:
         self._report = {
             "sources": 0, "direct_sources": 0, "binary_sources": 0, "folds": 0,
             "group_closes": 0, "uniform_reward_groups": 0, "fold_s": 0.0, "backward_s": 0.0,
-            "statistic_device": str(stat_dev),
+            "statistic_device": str(stat_dev), "device_groups_below_hbm_threshold": 0, "host_groups": 0,
+            "combined_sources": 0,
         }
         self._versions = {id(p): p._version for p in run._trainable}
 
@@ -170,6 +197,13 @@ class RewardLinearBackward:
             self._profile_step = int(scope["step"])
 
     # ------------------------------------------------------------ buffers
+    def _pipeline(self):
+        if self._host_fold is None:
+            from thundersync_b200.grpo.host_fold import HostFoldPipeline
+
+            self._host_fold = HostFoldPipeline.shared(self.run.device, **self._host_fold_options)
+        return self._host_fold
+
     def _main_grad(self) -> torch.Tensor:
         if self._main is None:
             self._main = self.arena.new_buffer(torch.float32)
@@ -190,11 +224,33 @@ class RewardLinearBackward:
         """The flat fp32 batch gradient (arena layout); None before any close."""
         return self._main
 
-    def _stat(self) -> torch.Tensor:
-        return torch.zeros(self.arena.numel, dtype=torch.float32, device=self.statistic_device)
+    def _stat(self, device: torch.device | None = None) -> torch.Tensor:
+        device = self.statistic_device if device is None else device
+        if device.type == "cpu":
+            from thundersync_b200.grpo.host_fold import host_statistic
+
+            dtype = self.arena.dtype if self._keep_source_dtype else torch.float32
+            return host_statistic(self.arena.numel, dtype, self._spill_dir)
+        return torch.zeros(self.arena.numel, dtype=torch.float32, device=device)
+
+    def _device_has_room(self) -> bool:
+        """Blocking sources: a group's statistics stay on the device while the device's reserved memory,
+        plus the pair, stays below ``source_offload_hbm_threshold`` of its capacity."""
+        dev = self.run.device
+        if self.source_offload_mode != "blocking" or dev.type != "cuda":
+            return False
+        free, total = torch.cuda.mem_get_info(dev)
+        pair = 2 * 4 * self.arena.numel
+        used = total - free
+        return used + pair <= self._hbm_threshold * total
 
     def _stat_pair(self, acc) -> tuple[torch.Tensor, torch.Tensor]:
         """(reward-weighted, unit) statistics of a group: a preallocated device home when one is free."""
+        if self.statistic_device.type == "cpu" and self._device_has_room():
+            self._report["device_groups_below_hbm_threshold"] += 1
+            return self._stat(self.run.device), self._stat(self.run.device)
+        if self.statistic_device.type == "cpu":
+            self._report["host_groups"] += 1
         if self._stat_slots and self.statistic_device.type == "cuda":
             if self._stat_pool is None:
                 from thundersync_b200.grpo.device_statistics import DeviceStatisticPool
@@ -396,11 +452,17 @@ class RewardLinearBackward:
         t0 = time.perf_counter()
         if acc.g2 is None:
             acc.g1, acc.g2 = self._stat_pair(acc)
-        src_dev = src if src.device == acc.g2.device else src.to(acc.g2.device)
-        if self._binary:
-            (acc.g1 if reward == 1.0 else acc.g2).add_(src_dev)
+        if acc.g2.device.type == "cpu" and src.is_cuda:
+            # host statistics: windowed device->host copies, host adds in the background
+            pipe = self._pipeline()
+            if self._binary:
+                pipe.fold(src, None, acc.g1 if reward == 1.0 else acc.g2, 0.0)
+            else:
+                pipe.fold(src, acc.g1, acc.g2, reward)
+        elif self._binary:
+            (acc.g1 if reward == 1.0 else acc.g2).add_(src.to(acc.g2.device))
         else:
-            fold_(acc.g1, acc.g2, src_dev, reward)
+            fold_(acc.g1, acc.g2, src if src.device == acc.g2.device else src.to(acc.g2.device), reward)
         self._fold_boundary(acc, reward, bnd)
         acc.folded.append(tid)
         self._report["folds"] += 1
@@ -480,7 +542,18 @@ class RewardLinearBackward:
         if uniform:
             self._report["uniform_reward_groups"] += 1
         adjoints: list[torch.Tensor | None] = []
-        if acc.g2 is not None:
+        if acc.g2 is not None and acc.g2.device.type == "cpu" and main.is_cuda:
+            # host statistics: combined on the host window by window and added on the device
+            inv = 1.0 / std
+            pipe = self._pipeline()
+            if self._binary:
+                a, b = (a_uni, a_uni) if uniform else ((1.0 - mean) * inv, -mean * inv)
+                pipe.combine_into(main, acc.g1, acc.g2, a, b)
+            elif uniform:
+                pipe.combine_into(main, acc.g2, None, a_uni, 0.0)
+            else:
+                pipe.combine_into(main, acc.g1, acc.g2, inv, -mean * inv)
+        elif acc.g2 is not None:
             g1 = acc.g1 if acc.g1.device == main.device else acc.g1.to(main.device)
             g2 = acc.g2 if acc.g2.device == main.device else acc.g2.to(main.device)
             inv = 1.0 / std
@@ -568,6 +641,8 @@ class RewardLinearBackward:
         if open_:
             raise RuntimeError(f"cannot step: groups {open_} are still open")
         self._check_versions()
+        if self._host_fold is not None:
+            self._host_fold.drain()
         main = self._main_grad()
         self.run.finalize_shared_prefixes(sink=GradSink(self.arena, main))
         self.run.materialize_parameter_adjoints()
@@ -590,6 +665,11 @@ class RewardLinearBackward:
 
     def abort(self) -> None:
         self._aborted = True
+        if self._host_fold is not None:
+            self._host_fold.drain()
+            if self._host_fold_options.get("arena") is not None:
+                self._host_fold.close()  # return the arena's slabs
+            self._host_fold = None
         for gid, acc in self._groups.items():
             self._drop_stats(acc)
             acc.prepared.clear()
@@ -612,4 +692,7 @@ class RewardLinearBackward:
 
     @property
     def source_offload_report(self) -> dict[str, Any]:
-        return {**self._report, **self._scope, "mode": self.source_offload_mode, "binary": self._binary}
+        out = {**self._report, **self._scope, "mode": self.source_offload_mode, "binary": self._binary}
+        if self._host_fold is not None:
+            out["host_fold"] = dict(self._host_fold.report)
+        return out
