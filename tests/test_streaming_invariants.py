@@ -141,3 +141,35 @@ def test_rebuild_reserve_option_is_accepted_on_cpu():
     b = _grads(copy.deepcopy(model), batch, order, stream_turns=True,
                run_kw={"rebuild_plain_reserve_bytes": 1 << 30, "rebuild_block_tokens": 8})
     _close(a, b)
+
+
+@pytest.mark.parametrize("binary", [False, True])
+def test_combined_known_reward_sources_give_the_same_gradient(binary):
+    """Closes of one group that share a reward run as one packed source; the gradient is unchanged."""
+    model = build_model(21)
+    batch, _ = make_batch(21)
+
+    def grads(combine):
+        model.zero_grad(set_to_none=True)
+        run = StreamingRun(model, boundary_cut=True, stream_turns=False)
+        bw = RewardLinearBackward(run, model, eps=EPS, combine_known_reward_sources=combine)
+        if binary:
+            bw.configure_binary_rewards()
+        for g, prompt, trajs in batch:
+            bw.open_group(g, prompt, [t for t, _, _ in trajs])
+        for g, _, trajs in batch:
+            items = []
+            for j, (tid, turns, reward) in enumerate(trajs):
+                for tk, sc in turns:
+                    run.append_turn(g, tid, tk, sc)
+                r = float(j % 2) if binary else (0.25 if j % 2 else 0.75)
+                items.append((tid, r))
+            bw.close_trajectories(items)
+            bw.close_group(g)
+        bw.assert_safe_to_step()
+        return {n: p.grad.detach().clone() for n, p in model.named_parameters()}, bw.source_offload_report
+
+    ref, r0 = grads(False)
+    got, r1 = grads(True)
+    assert r0["combined_sources"] == 0 and r1["combined_sources"] > 0 and r1["sources"] < r0["sources"]
+    _close(got, ref)

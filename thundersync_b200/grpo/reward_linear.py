@@ -319,9 +319,74 @@ class RewardLinearBackward:
                                   trajectory_ids=[t for t, _, _ in norm],
                                   branch_tokens=[self.run.trajectory_tokens(t) for t, _, _ in norm])
         with window:
-            for tid, reward, w in norm:
+            for tid, reward, _ in norm:
                 self._record(tid, reward)
-                self._differentiate(tid, reward, w)
+            for cohort in self._cohorts(norm):
+                if len(cohort) > 1:
+                    self._differentiate_cohort([t for t, _, _ in cohort], cohort[0][1])
+                else:
+                    tid, reward, w = cohort[0]
+                    self._differentiate(tid, reward, w)
+
+    def _cohorts(self, items: list[tuple[int, float, Any]]) -> list[list[tuple[int, float, Any]]]:
+        """With ``combine_known_reward_sources``: closes of one group that share a reward (and carry no
+        token weights) run as one source -- one packed rebuild, one backward, one fold -- since the
+        statistics only ever see ``r·Σ∇S`` and ``Σ∇S`` of them. Otherwise one cohort per close."""
+        if not self.combine_known_reward_sources or len(items) < 2:
+            return [[it] for it in items]
+        out: list[list[tuple[int, float, Any]]] = []
+        index: dict[tuple[int, float], int] = {}
+        for it in items:
+            tid, reward, w = it
+            acc = self._acc(tid)
+            direct = acc.direct or (self.direct_when_group_bound and self.group_fully_bound(acc.gid))
+            if w is not None or direct or tid in acc.closed:
+                out.append([it])
+                continue
+            key = (acc.gid, reward)
+            if key in index:
+                out[index[key]].append(it)
+            else:
+                index[key] = len(out)
+                out.append([it])
+        return out
+
+    def _differentiate_cohort(self, tids: list[int], reward: float) -> None:
+        acc = self._acc(tids[0])
+        self._check_versions()
+        t0 = time.perf_counter()
+        if self.run.stream_turns:
+            lps = [self._logprobs(t) for t in tids]
+        else:
+            lps = self.run.rebuild_logprobs(tids)  # one packed forward over every branch
+        s = torch.cat([lp.reshape(-1) for lp in lps]).sum()
+        binary_sink = self._binary and self.statistic_device == self.run.device
+        if binary_sink:
+            if acc.g2 is None:
+                acc.g1, acc.g2 = self._stat_pair(acc)
+            sink = GradSink(self.arena, acc.g1 if reward == 1.0 else acc.g2)
+        else:
+            if self._scratch is None or self._scratch.device != self.run.device:
+                self._scratch = self.arena.new_buffer(torch.float32)
+            else:
+                self._scratch.zero_()
+            sink = GradSink(self.arena, self._scratch)
+        if s.requires_grad:
+            self.run.backward_with_boundary_adjoint_capture(s, source=("cohort", tuple(tids)), sink=sink)
+        bnd = self.run.boundary(acc.gid).drain()
+        for t in tids:
+            self.run.free_trajectory(t)
+        self._report["backward_s"] += time.perf_counter() - t0
+        self._report["sources"] += 1
+        self._report["combined_sources"] += len(tids)
+        if binary_sink:
+            self._fold_boundary(acc, reward, bnd)
+            acc.folded.extend(tids)
+            self._report["binary_sources"] += 1
+        else:
+            self._fold(acc, tids[0], reward, self._scratch, bnd)
+            acc.folded.extend(tids[1:])
+        acc.closed.update(tids)
 
     def prepare_trajectory(self, traj_id: int, token_weights=None) -> None:
         self.prepare_trajectories([(traj_id, token_weights)] if token_weights is not None else [traj_id])
