@@ -98,3 +98,21 @@ def test_regressions_gate_the_reward(sandbox_factory):
 def test_no_targets_is_never_a_pass(sandbox_factory):
     box = sandbox_factory({"test_e.py": "def test_ok():\n    pass\n"})
     assert grade(box, _task([]), restore_tests=False).reward == 0.0
+
+
+def test_reports_with_a_doctype_or_entities_are_malformed():
+    from thundersync_b200.rollout.engine import _parse_junit
+
+    good = '<testsuites><testsuite><testcase classname="test_a" name="test_x"/></testsuite></testsuites>'
+    assert _parse_junit(good) is not None
+    evil = ('<?xml version="1.0"?><!DOCTYPE r [<!ENTITY a "aaaa">]>'
+            '<testsuites><testsuite><testcase classname="test_a" name="&a;"/></testsuite></testsuites>')
+    assert _parse_junit(evil) is None and _parse_junit("") is None and _parse_junit("<broken") is None
+
+
+def test_report_paths_are_fresh_per_grade(sandbox_factory):
+    box = sandbox_factory({"test_o.py": "def test_ok():\n    pass\n"})
+    grade(box, _task(["test_o.py::test_ok"]), restore_tests=False)
+    grade(box, _task(["test_o.py::test_ok"]), restore_tests=False)
+    paths = {c.split("--junitxml=")[1].split()[0] for c in box.commands if "--junitxml=" in c}
+    assert len(paths) == 2

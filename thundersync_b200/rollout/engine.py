@@ -33,6 +33,7 @@ import json
 import logging
 import os
 import queue
+import secrets
 import shlex
 import struct
 import subprocess
@@ -236,7 +237,13 @@ def _read_report(sandbox: Any, path: str) -> str | None:
 
 
 def _parse_junit(xml: str | None) -> ET.Element | None:
+    """The report's root element, or None when it is empty, malformed, or declares a document type or
+    entities (a report is written inside the policy's sandbox; entity expansion is never needed to read
+    one and is refused rather than trusted)."""
     if not xml or not xml.strip():
+        return None
+    head = xml.upper()
+    if "<!DOCTYPE" in head or "<!ENTITY" in head:
         return None
     try:
         return ET.fromstring(xml)
@@ -280,8 +287,9 @@ def _selector_batches(ids: list[str], max_chars: int = 60000) -> list[list[str]]
 
 def _run_pytest(sandbox: Any, ids: list[str], timeout: float) -> tuple[dict[str, bool] | None, str]:
     results: dict[str, bool] = {}
+    grade_token = secrets.token_hex(6)  # a fresh report path per grade: never read an earlier grade's report
     for k, batch in enumerate(_selector_batches(ids)):
-        report = f"/tmp/ts-junit-{k}.xml"
+        report = f"/tmp/ts-junit-{grade_token}-{k}.xml"
         sel = " ".join(shlex.quote(t) for t in batch)
         out = command_output(sandbox, f"rm -f {report}; python -m pytest -p no:cacheprovider -q -rN "
                                       f"--junitxml={report} {sel} >/dev/null 2>&1; true", timeout=timeout)
