@@ -77,3 +77,30 @@ def test_forest_logprobs_match_per_trajectory_reference():
     ref_total.backward()
     for n, p in model.named_parameters():
         torch.testing.assert_close(got[n], p.grad, rtol=2e-4, atol=2e-6)
+
+
+def _forest_grads(model, plan, **kw):
+    model.zero_grad(set_to_none=True)
+    lp = forest_logprobs(model, plan, **kw)
+    (lp * torch.linspace(0.5, 1.5, lp.numel())).sum().backward()
+    return lp.detach(), {n: p.grad.clone() for n, p in model.named_parameters()}
+
+
+def test_checkpointed_forest_with_attention_cache_is_exact():
+    """Checkpointed forest: identical log-probs and gradients; the recompute reuses kept attention outputs."""
+    from thundersync_b200.ops.attention import AttentionOutputCache
+
+    model = build_model(4)
+    plan = compile_plan(build_forest(_batch(2)))
+    lp0, g0 = _forest_grads(model, plan)
+    for budget, expect_replay in ((1 << 30, True), (0, False)):
+        cache = AttentionOutputCache(budget)
+        lp1, g1 = _forest_grads(model, plan, checkpoint=True, attention_cache=cache)
+        torch.testing.assert_close(lp1, lp0, rtol=0, atol=0)
+        for n in g0:
+            torch.testing.assert_close(g1[n], g0[n], rtol=1e-6, atol=1e-7)
+        rep = cache.report()
+        if expect_replay:
+            assert rep["saved"] > 0 and rep["replayed"] == rep["saved"] and rep["declined"] == 0
+        else:
+            assert rep["saved"] == 0 and rep["declined"] > 0 and rep["replayed"] == 0

@@ -55,6 +55,58 @@ class _Ctx:
         self.saved_tensors = tensors
 
 
+class _Slot:
+    """Placeholder for the i-th tensor handed to ``ctx.save_for_backward``."""
+
+    __slots__ = ("i",)
+
+    def __init__(self, i: int) -> None:
+        self.i = i
+
+
+def _stash(ctx) -> None:
+    """Move every tensor the layer keeps for its backward (the native path's activations, the inner ops'
+    saved tensors) into one ``ctx.save_for_backward`` call, leaving index slots behind. Saved-tensor hooks
+    -- activation checkpointing, host offload of checkpoint inputs -- then see all of them."""
+    flat: list[torch.Tensor] = []
+
+    def enc(x):
+        if isinstance(x, torch.Tensor):
+            flat.append(x)
+            return _Slot(len(flat) - 1)
+        if isinstance(x, _Ctx):
+            x.saved_tensors = tuple(enc(t) for t in x.saved_tensors)
+            return x
+        if isinstance(x, list):
+            return [enc(y) for y in x]
+        if isinstance(x, tuple) and not isinstance(x, torch.Size):
+            return tuple(enc(y) for y in x)
+        return x
+
+    ctx.att = enc(getattr(ctx, "att", None))
+    ctx.stages = enc(getattr(ctx, "stages", None))
+    ctx.save_for_backward(*flat)
+
+
+def _unstash(ctx) -> None:
+    flat = ctx.saved_tensors
+
+    def dec(x):
+        if isinstance(x, _Slot):
+            return flat[x.i]
+        if isinstance(x, _Ctx):
+            x.saved_tensors = tuple(dec(t) for t in x.saved_tensors)
+            return x
+        if isinstance(x, list):
+            return [dec(y) for y in x]
+        if isinstance(x, tuple) and not isinstance(x, torch.Size):
+            return tuple(dec(y) for y in x)
+        return x
+
+    ctx.att = dec(ctx.att)
+    ctx.stages = dec(ctx.stages)
+
+
 class DenseLayer(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, pos, inv_freq, meta, *tensors):
@@ -98,6 +150,7 @@ class DenseLayer(torch.autograd.Function):
             ctx.meta = meta
             ctx.t = t
             ctx.out_shape, ctx.out_dtype, ctx.out_device = out.shape, out.dtype, out.device
+            _stash(ctx)
             return out, kbuf[sp:], vbuf[sp:]
         c_n1 = _Ctx((True, need_w, False, False))
         x1 = _RMSNorm.forward(c_n1, h, ln1, eps, False)
@@ -166,10 +219,14 @@ class DenseLayer(torch.autograd.Function):
         ctx.meta = meta
         ctx.t = t
         ctx.out_shape, ctx.out_dtype, ctx.out_device = out.shape, out.dtype, out.device
+        if not isinstance(getattr(ctx, "att", None), tuple):
+            ctx.att = None
+        _stash(ctx)
         return out, k, v
 
     @staticmethod
     def backward(ctx, dout, dk_out, dv_out):
+        _unstash(ctx)
         if dout is None:
             dout = torch.zeros(ctx.out_shape, dtype=ctx.out_dtype, device=ctx.out_device)
         if ctx.native:

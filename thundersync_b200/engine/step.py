@@ -11,6 +11,7 @@ reference src/thundersync/engine/step.py:383-470.
 
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 from typing import Any
 
@@ -66,8 +67,29 @@ def assert_supported(model: torch.nn.Module, *, allow_hybrid: bool = False) -> N
         )
 
 
+def _run_checkpointed(ex, ids: torch.Tensor, pos: torch.Tensor, segs: list[Segment], cache) -> torch.Tensor:
+    """Per-layer activation checkpointing over one forest pass; attention outputs may come from ``cache``."""
+    from torch.utils.checkpoint import checkpoint
+
+    h = ex.embed(ids)
+    for i, kind in enumerate(ex.spec.kinds):
+        fn = ex.attention_layer if kind == "full_attention" else ex.linear_layer
+
+        def body(h_in, _i=i, _fn=fn):
+            ctx = cache.layer(_i) if cache is not None else contextlib.nullcontext()
+            with ctx:
+                return _fn(_i, h_in, pos, segs)[0]
+
+        h = checkpoint(body, h, use_reentrant=False)
+    return ex.final_norm(h)
+
+
 def forest_logprobs(model: torch.nn.Module, plan: ExecutionPlan, *, gate: bool = True,
-                    stats: list[StepStats] | None = None) -> torch.Tensor:
+                    stats: list[StepStats] | None = None, checkpoint: bool = False,
+                    attention_cache: Any = None) -> torch.Tensor:
+    """Log-probs of the plan's scored tokens. ``checkpoint`` keeps only layer inputs for the backward
+    (each layer is recomputed there); an :class:`~thundersync_b200.ops.attention.AttentionOutputCache`
+    lets that recompute reuse attention outputs within its byte budget."""
     assert_supported(model)
     dev = next(model.parameters()).device
     plan = plan.to(dev)
@@ -78,7 +100,10 @@ def forest_logprobs(model: torch.nn.Module, plan: ExecutionPlan, *, gate: bool =
         if e > s:
             segs.append((s, Segment(s, e - s, [], plan.key_ranges[n][:-1])))
     segs = [sg for _, sg in sorted(segs, key=lambda x: x[0])]
-    h, _ = ex.run(plan.token_ids, plan.position_ids, segs)
+    if checkpoint and torch.is_grad_enabled():
+        h = _run_checkpointed(ex, plan.token_ids, plan.position_ids, segs, attention_cache)
+    else:
+        h, _ = ex.run(plan.token_ids, plan.position_ids, segs)
     w = ex.head_weight()
     if gate:
         lp = lm_head_logprob(h.index_select(0, plan.score_src), w, plan.score_tgt)

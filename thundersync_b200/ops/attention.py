@@ -16,7 +16,10 @@ saved LSE (no ``S × T`` buffers) and produces dQ without atomics.
 
 from __future__ import annotations
 
+import contextlib
 import math
+import threading
+from typing import Any
 
 import torch
 
@@ -42,16 +45,88 @@ def attention_reference(q, k, v, scale):
     return out.to(q.dtype), lse
 
 
+class AttentionOutputCache:
+    """Bounded store of attention outputs for checkpointed forwards (reference behaviour:
+    src/thundersync/grpo/final_forest.py:182-239).
+
+    Under per-layer activation checkpointing the backward recomputes each layer, attention included.
+    Inside :meth:`layer` the first run of a layer *records*: every attention call keeps its output and
+    row log-sum-exp while the charged bytes stay within ``budget_bytes`` (calls beyond it are declined
+    and recomputed as usual). A later run of the same layer -- the recompute in the backward -- *replays*
+    the calls in order and skips the kernel for every kept output. Results are bitwise those of a
+    recompute: the same kernel produced them.
+    """
+
+    def __init__(self, budget_bytes: int) -> None:
+        self.budget_bytes = int(budget_bytes)
+        self.charged_bytes = 0
+        self.saved = self.declined = self.replayed = 0
+        self._layers: dict[Any, list] = {}
+        self._active: list | None = None
+        self._recording = False
+
+    @contextlib.contextmanager
+    def layer(self, key: Any):
+        """Run one layer's body: records on the first entry for ``key``, replays on later entries."""
+        first = key not in self._layers
+        if first:
+            self._layers[key] = []
+        prev = (self._active, self._recording, getattr(_CACHE, "current", None))
+        self._active = list(self._layers[key]) if not first else self._layers[key]
+        self._recording = first
+        _CACHE.current = self
+        try:
+            yield
+        finally:
+            self._active, self._recording, _CACHE.current = prev
+
+    def _take(self, q: torch.Tensor):
+        if self._active is None:
+            return None, False
+        if self._recording:
+            return None, True
+        if not self._active:
+            raise RuntimeError("attention recompute issued more calls than the recorded forward")
+        hit = self._active.pop(0)
+        if hit is not None:
+            self.replayed += 1
+        return hit, False
+
+    def _keep(self, out: torch.Tensor, lse: torch.Tensor) -> None:
+        size = out.numel() * out.element_size() + lse.numel() * lse.element_size()
+        if self.charged_bytes + size <= self.budget_bytes:
+            self.charged_bytes += size
+            self.saved += 1
+            self._active.append((out.detach(), lse.detach()))
+        else:
+            self.declined += 1
+            self._active.append(None)
+
+    def report(self) -> dict[str, int]:
+        return {"budget_bytes": self.budget_bytes, "charged_bytes": self.charged_bytes, "saved": self.saved,
+                "declined": self.declined, "replayed": self.replayed}
+
+
+_CACHE = threading.local()
+
+
 class _ChunkedAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, scale, n, *kv):
         ks, vs = kv[:n], kv[n:]
-        k = ks[0] if n == 1 else torch.cat(ks, 0)
-        v = vs[0] if n == 1 else torch.cat(vs, 0)
-        if q.is_cuda:
-            out, lse = native().attn_fwd_tc(q.contiguous(), k.contiguous(), v.contiguous(), float(scale))
+        cache = getattr(_CACHE, "current", None)
+        hit, record = cache._take(q) if cache is not None else (None, False)
+        if hit is not None:
+            out, lse = hit[0].detach(), hit[1].detach()  # fresh tensor objects over the kept storage
         else:
-            out, lse = attention_reference(q, k, v, scale)
+            k = ks[0] if n == 1 else torch.cat(ks, 0)
+            v = vs[0] if n == 1 else torch.cat(vs, 0)
+            if q.is_cuda:
+                out, lse = native().attn_fwd_tc(q.contiguous(), k.contiguous(), v.contiguous(), float(scale))
+            else:
+                out, lse = attention_reference(q, k, v, scale)
+            if record:
+                cache._keep(out, lse)
         ctx.scale = scale
         ctx.n = n
         ctx.lens = [t.shape[0] for t in ks]

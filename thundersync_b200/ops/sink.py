@@ -20,6 +20,8 @@ from dataclasses import dataclass
 
 import torch
 
+from thundersync_b200.ops.gemm import gemm_accumulate
+
 _ACTIVE: "GradSink | None" = None
 
 # CUDA: projection weight gradients (dW += dYᵀ·X into the sink) run on a side stream, so they fill the
@@ -138,11 +140,28 @@ class ParamArena:
                 p.data = flat[o : o + p.numel()].view_as(p)
         self.flat = flat[: self.numel]
 
+    def resolve(self, t: torch.Tensor) -> torch.Tensor | None:
+        """The arena parameter ``t`` is, or aliases exactly (same storage start and shape): activation
+        checkpointing hands a recomputed backward detached aliases of the parameters it saved."""
+        if id(t) in self.offsets:
+            return t
+        by_ptr = getattr(self, "_by_ptr", None)
+        if by_ptr is None or getattr(self, "_by_ptr_flat", None) != self.flat.data_ptr():
+            by_ptr = {p.data_ptr(): p for p in self.params}
+            self._by_ptr, self._by_ptr_flat = by_ptr, self.flat.data_ptr()
+        p = by_ptr.get(t.data_ptr()) if t.device == self.device else None
+        return p if p is not None and p.shape == t.shape else None
+
     def offset(self, p: torch.Tensor) -> int:
         return self.offsets[id(p)]
 
     def view(self, buf: torch.Tensor, p: torch.Tensor) -> torch.Tensor:
-        o = self.offsets[id(p)]
+        o = self.offsets.get(id(p))
+        if o is None:
+            q = self.resolve(p)
+            if q is None:
+                raise KeyError("tensor is not an arena parameter")
+            o = self.offsets[id(q)]
         return buf[o : o + p.numel()].view(p.shape)
 
     def span(self, params: list[torch.Tensor]) -> tuple[int, int] | None:
@@ -185,7 +204,7 @@ class GradSink:
     deposits: int = 0
 
     def owns(self, p: torch.Tensor) -> bool:
-        return id(p) in self.arena.offsets
+        return id(p) in self.arena.offsets or self.arena.resolve(p) is not None
 
     def view(self, p: torch.Tensor) -> torch.Tensor:
         return self.arena.view(self.buffer, p)
@@ -220,16 +239,14 @@ class GradSink:
                 st = _side_stream(target.device)
                 st.wait_stream(main)
                 with torch.cuda.stream(st):
-                    torch.addmm(target, dy.t(), x, beta=1.0, alpha=self.scale,
-                                out_dtype=target.dtype, out=target)
+                    gemm_accumulate(target, dy, x, a_t=True, b_t=False, alpha=self.scale)
                 # the operands' memory must outlive the side-stream GEMM
                 dy.record_stream(st)
                 x.record_stream(st)
                 self._side_devices = getattr(self, "_side_devices", set())
                 self._side_devices.add(target.device)
             else:
-                torch.addmm(target, dy.t(), x, beta=1.0, alpha=self.scale,
-                            out_dtype=target.dtype, out=target)
+                gemm_accumulate(target, dy, x, a_t=True, b_t=False, alpha=self.scale)
         else:
             target.addmm_(dy.t().to(target.dtype), x.to(target.dtype), alpha=self.scale)
         self.deposits += 1
