@@ -72,6 +72,30 @@ class _ImmediateBackward(_StreamAdapter):
         self._versions = [p._version for p in self.params]
         self._closed: dict[int, set[int]] = {}
         self._finalized = False
+        # every backward deposits into one fp32 buffer in the parameter-arena layout (bf16 parameters
+        # would otherwise sum hundreds of per-action gradients in bf16 .grad tensors)
+        self.arena = getattr(run, "arena", None)
+        self._main: torch.Tensor | None = None
+
+    def _sink(self):
+        if self.arena is None:
+            return None
+        from thundersync_b200.ops.sink import GradSink
+
+        if self._main is None:
+            self._main = self.arena.new_buffer(torch.float32)
+        return GradSink(self.arena, self._main)
+
+    def use_main_grad_buffer(self, buf: torch.Tensor) -> None:
+        """Accumulate into ``buf`` (fp32, arena layout, zeroed here), e.g. a data-parallel peer buffer."""
+        if self.arena is None or buf.dtype != torch.float32 or buf.numel() < self.arena.numel:
+            raise ValueError("the main gradient buffer must be fp32 and cover the parameter arena")
+        buf.zero_()
+        self._main = buf[: self.arena.numel]
+
+    def main_grad(self) -> torch.Tensor | None:
+        """The flat fp32 gradient (arena layout); normalised once the step is safe."""
+        return self._main
 
     def _check_versions(self) -> None:
         if any(p._version != v for p, v in zip(self.params, self._versions)):
@@ -99,7 +123,7 @@ class _ImmediateBackward(_StreamAdapter):
         if open_t:
             raise RuntimeError(f"group {group_id}: trajectories {open_t} not closed")
         self._closed.pop(group_id, None)
-        self.run.finalize_group_boundary(group_id)
+        self.run.finalize_group_boundary(group_id, sink=self._sink())
         self.run.free_group(group_id)
 
     @property
@@ -113,7 +137,7 @@ class _ImmediateBackward(_StreamAdapter):
                 f"optimizer step with open groups {self.open_groups}: their retained graphs reference "
                 "current parameter values"
             )
-        self.run.finalize_shared_prefixes()
+        self.run.finalize_shared_prefixes(sink=self._sink())
         self.run.materialize_parameter_adjoints()
 
 
@@ -166,15 +190,29 @@ class _TokenLoss:
         self._mass += n if weights is None else float(weights.detach().double().sum())
         return float(loss.detach()) if return_loss else None
 
-    def _finalize_normalization(self, params: list[torch.Tensor]) -> None:
+    def _finalize_normalization(self, params: list[torch.Tensor], *, materialize: bool = True) -> None:
         for flag in self._finite.values():
             if not bool(flag):
                 raise ValueError("teacher logprobs must be finite")
         div = self.normalization_divisor
-        if div != 1.0:
-            with torch.no_grad():
+        main = getattr(self, "_main", None)
+        with torch.no_grad():
+            if main is not None:
+                if div != 1.0:
+                    from thundersync_b200.ops.fold import scale_
+
+                    scale_(main, 1.0 / div)
+                if materialize:
+                    for p in params:
+                        v = self.arena.view(main, p)
+                        if p.grad is None:
+                            p.grad = v.to(p.dtype, copy=True)
+                        else:
+                            p.grad.add_(v.to(p.grad.dtype))
+            if div != 1.0:
+                # contributions that reached .grad outside the sink (parameters the arena does not hold)
                 for p in params:
-                    if p.grad is not None:
+                    if p.grad is not None and (main is None or not materialize):
                         p.grad.div_(div)
         if self._numerator_dev is not None:
             self._numerator = float(self._numerator_dev)
@@ -235,7 +273,7 @@ class OPDTurnStream(_TokenLoss, _ImmediateBackward):
             meta.append((loss, lp.numel(), weights))
         if losses:
             src = ("trajectory_turn_pack", tuple(t for _, t, *_ in items))
-            self.run.backward_with_boundary_adjoint_capture(losses, source=src)
+            self.run.backward_with_boundary_adjoint_capture(losses, source=src, sink=self._sink())
         return [None if m is None else self._record(m[0], m[1], m[2], return_loss) for m in meta]
 
     def close_trajectory(self, traj_id: int) -> None:
@@ -248,15 +286,15 @@ class OPDTurnStream(_TokenLoss, _ImmediateBackward):
             raise ValueError("a trajectory appears twice in one closure cohort")
         for t in traj_ids:
             self._register_close(t)
-        self.run.finalize_trajectories_turn_boundaries(list(traj_ids))
+        self.run.finalize_trajectories_turn_boundaries(list(traj_ids), sink=self._sink())
         for t in traj_ids:
             self.run.free_trajectory(t)
 
-    def assert_safe_to_step(self) -> None:
+    def assert_safe_to_step(self, *, materialize: bool = True) -> None:
         if self._finalized:
             return
         _ImmediateBackward.assert_safe_to_step(self)
-        self._finalize_normalization(self.params)
+        self._finalize_normalization(self.params, materialize=materialize)
         self._finalized = True
 
 
@@ -345,17 +383,17 @@ class OPDStream(_TokenLoss, _ImmediateBackward):
             self._note_finite(teacher)
             if lp.numel():
                 loss = self._loss(lp, old, teacher, weights)
-                self.run.backward_with_boundary_adjoint_capture(loss, source=("trajectory", tid))
+                self.run.backward_with_boundary_adjoint_capture(loss, source=("trajectory", tid), sink=self._sink())
                 self._record(loss, lp.numel(), weights, False)
             self.run.free_trajectory(tid)
 
-    def assert_safe_to_step(self) -> None:
+    def assert_safe_to_step(self, *, materialize: bool = True) -> None:
         if self._poison is not None:
             raise RuntimeError("a concurrent teacher replay failed; this step is poisoned") from self._poison
         if self._finalized:
             return
         _ImmediateBackward.assert_safe_to_step(self)
-        self._finalize_normalization(self.params)
+        self._finalize_normalization(self.params, materialize=materialize)
         self._finalized = True
         if self._pool is not None:
             self._pool.shutdown(wait=True)
