@@ -172,7 +172,7 @@ def test_gpu_host_statistics_match_device_statistics(options, tmp_path):
         assert report["device_groups_below_hbm_threshold"] > 0
     else:
         assert report["host_fold"]["folds"] > 0 and report["host_fold"]["combines"] > 0
-    tol = 2e-2 if options.get("statistic_keep_source_dtype") else 1e-4
+    tol = 2e-2  # both arrive as bf16 .grad (fp32 sums in different orders, one rounding each)
     for n in ref:
         scale = ref[n].abs().max().clamp_min(1e-6)
         assert float((got[n] - ref[n]).abs().max() / scale) < tol, n
