@@ -8,6 +8,9 @@ Modes:
              equals a fixed-order host sum; reduce-scatter + fused AdamW gather
              leaves identical parameters on every rank.
   timeout    a barrier whose peer never arrives sets the status word (bounded).
+  sharded    the ZeRO-1 step (FlatAdamW.sharded: native reduce-scatter, fused AdamW on each shard,
+             bf16 parameter gather into every rank) leaves every rank with the parameters one
+             replicated FlatAdamW step produces from the same averaged gradient.
 Rank 0 writes a JSON verdict to --out.
 """
 
@@ -88,6 +91,41 @@ def mode_equality(rank, world, device):
             "norm": stats["global_grad_norm"]}
 
 
+def mode_sharded(rank, world, device):
+    batch, _ = make_batch(0, groups=world, per_group=4, vocab=CFG.vocab_size, lo=40, hi=120, prompt_len=64)
+    model = _model(1, device, torch.bfloat16)
+    ref = copy.deepcopy(model)
+    opt = FlatAdamW.sharded(arena_for(model), lr=1e-3, maximize=True)
+    run_factory = lambda m: StreamingRun(m, boundary_cut=True, stream_turns=False)  # noqa: E731
+    dp = DataParallelThunderSync.init_from_env(model, opt, run_factory=run_factory, grad_clip=1.0,
+                                               source_offload_mode="device_resident", source_offload_device=None)
+    g, prompt, trajs = batch[rank]
+    _stream(dp, g, prompt, trajs, trajs)
+    captured = {}
+    stats = dp.step(gradient_observer=lambda tag, grad: captured.setdefault(tag, grad.clone()))
+    torch.cuda.synchronize()
+    # the reduce-scatter leaves only this rank's shard reduced: gather the shards into the full mean gradient
+    arena = arena_for(model)
+    lo, hi = opt.lo, opt.hi
+    full = torch.zeros(arena.numel, device=device, dtype=torch.float32)
+    full[lo:hi] = captured["raw_reduced"][lo:hi]
+    dist.all_reduce(full)
+    # one replicated update from the same gradient
+    ref_arena = arena_for(ref)
+    ref_opt = FlatAdamW(ref_arena, lr=1e-3, maximize=True)
+    from thundersync_b200.parallel.optimizer import global_sq_norm
+
+    coef, nrm = ref_opt.clip_coefficient(global_sq_norm(full), 1.0)
+    ref_opt.step(full, clip_coef=coef)
+    torch.cuda.synchronize()
+    diff = float((arena.flat.float() - ref_arena.flat.float()).abs().max())
+    h = torch.tensor([float(arena.flat.float().sum())], device=device, dtype=torch.float64)
+    hs = [torch.zeros_like(h) for _ in range(world)]
+    dist.all_gather(hs, h)
+    return {"max_param_diff": diff, "path": stats.get("reduction_path"), "norm": stats["global_grad_norm"],
+            "ref_norm": float(nrm), "replicas_equal": all(float(x) == float(hs[0]) for x in hs)}
+
+
 def mode_native(rank, world, device):
     from thundersync_b200.parallel.symm import SymmetricWorkspace, shard_bounds
 
@@ -158,7 +196,8 @@ def main():
     torch.cuda.set_device(device)
     dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     try:
-        res = {"equality": mode_equality, "native": mode_native, "timeout": mode_timeout}[a.mode](rank, world, device)
+        res = {"equality": mode_equality, "native": mode_native, "timeout": mode_timeout,
+               "sharded": mode_sharded}[a.mode](rank, world, device)
         if rank == 0:
             Path(a.out).write_text(json.dumps(res))
     finally:

@@ -40,3 +40,12 @@ def test_native_collectives_are_exact_and_deterministic(tmp_path):
 def test_device_wait_times_out_with_status(tmp_path):
     res = _run("timeout", tmp_path)
     assert res["status_code"] >= 1000, res
+
+
+def test_sharded_step_equals_replicated_update(tmp_path):
+    """ZeRO-1 over the native collectives: every rank ends with the replicated update's parameters."""
+    res = _run("sharded", tmp_path)
+    assert res["path"] == "native", res
+    assert res["replicas_equal"], res
+    assert abs(res["norm"] - res["ref_norm"]) <= 1e-3 * max(1.0, res["ref_norm"]), res
+    assert res["max_param_diff"] <= 2e-2, res  # bf16 parameters: at most a rounding apart

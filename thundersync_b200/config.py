@@ -42,12 +42,12 @@ class PolicyModelConfig:
 
     def __post_init__(self) -> None:
         if not (self.learning_rate > 0.0):
-            raise ConfigError("learning_rate must be positive")
+            raise ConfigError("learning_rate: expected a positive value")
         if self.lora_rank < 0:
-            raise ConfigError("lora_rank must not be negative")
+            raise ConfigError("lora_rank: expected 0 (full fine-tune) or a positive rank")
         if self.lora_alpha is not None and self.lora_alpha <= 0:
-            raise ConfigError("lora_alpha must be positive when given")
+            raise ConfigError("lora_alpha: expected a positive value or None")
         if not isinstance(self.deterministic_algorithms, bool):
-            raise ConfigError("deterministic_algorithms must be true or false")
+            raise ConfigError("deterministic_algorithms: expected a bool")
         if not (self.grad_clip > 0.0):
-            raise ConfigError("grad_clip must be positive")
+            raise ConfigError("grad_clip: expected a positive max norm")

@@ -78,48 +78,48 @@ class StreamingTrainerConfig:
 
     def __post_init__(self) -> None:
         if self.rebuild_block_tokens < 1:
-            raise ConfigError("rebuild_block_tokens must be positive")
+            raise ConfigError("rebuild_block_tokens: expected a positive token count")
         if self.source_offload_mode not in SOURCE_OFFLOAD_MODES:
-            raise ConfigError("source_offload_mode must be one of " + ", ".join(SOURCE_OFFLOAD_MODES))
+            raise ConfigError(f"source_offload_mode: expected one of {SOURCE_OFFLOAD_MODES}, got {self.source_offload_mode!r}")
         if self.source_reduction_mode not in SOURCE_REDUCTION_MODES:
-            raise ConfigError("source_reduction_mode must be one of " + ", ".join(SOURCE_REDUCTION_MODES))
+            raise ConfigError(f"source_reduction_mode: expected one of {SOURCE_REDUCTION_MODES}, got {self.source_reduction_mode!r}")
         if self.retained_bytes_log_every < 0:
-            raise ConfigError("retained_bytes_log_every must not be negative")
+            raise ConfigError("retained_bytes_log_every: expected 0 (off) or a positive interval")
         if self.statistic_dtype not in STATISTIC_DTYPES:
-            raise ConfigError("statistic_dtype must be one of " + ", ".join(STATISTIC_DTYPES))
+            raise ConfigError(f"statistic_dtype: expected one of {STATISTIC_DTYPES}, got {self.statistic_dtype!r}")
         if not 0.0 <= self.source_pinned_host_fraction <= 1.0:
-            raise ConfigError("source_pinned_host_fraction must be in [0, 1]")
+            raise ConfigError("source_pinned_host_fraction: expected a fraction between 0 and 1")
         if self.source_pinned_min_slabs < 1:
-            raise ConfigError("source_pinned_min_slabs must be positive")
+            raise ConfigError("source_pinned_min_slabs: expected at least one slab")
         if self.source_pinned_max_slabs is not None and self.source_pinned_max_slabs < self.source_pinned_min_slabs:
-            raise ConfigError("source_pinned_max_slabs must not be below source_pinned_min_slabs")
+            raise ConfigError("source_pinned_max_slabs: expected a cap of at least source_pinned_min_slabs")
         if self.statistic_open_groups < 0:
-            raise ConfigError("statistic_open_groups must not be negative")
+            raise ConfigError("statistic_open_groups: expected 0 (unset) or a positive group count")
         if self.statistic_device == "auto" and self.source_offload_mode != "device_resident":
-            raise ConfigError("statistic_device auto requires source_offload_mode device_resident")
+            raise ConfigError("statistic_device='auto' sizes device homes for device_resident sources; set source_offload_mode='device_resident'")
         if self.device_statistic_reserve_gib < 0.0:
-            raise ConfigError("device_statistic_reserve_gib must not be negative")
+            raise ConfigError("device_statistic_reserve_gib: expected a non-negative reserve in GiB")
         if not _is_bool(self.direct_when_group_bound):
-            raise ConfigError("direct_when_group_bound must be true or false")
+            raise ConfigError("direct_when_group_bound: expected a bool")
         if self.source_rebuild_block_tokens < 0:
-            raise ConfigError("source_rebuild_block_tokens must not be negative")
+            raise ConfigError("source_rebuild_block_tokens: expected 0 (inherit) or a positive token count")
         if self.source_attention_backend not in ("auto", "cudnn", "cudnn_graph"):
-            raise ConfigError("source_attention_backend must be auto, cudnn or cudnn_graph")
+            raise ConfigError(f"source_attention_backend: expected 'auto', 'cudnn' or 'cudnn_graph', got {self.source_attention_backend!r}")
         for name in ("source_attention_query_chunk", "source_attention_kv_bucket"):
             v = getattr(self, name)
             if not isinstance(v, int) or isinstance(v, bool) or v < 0:
-                raise ConfigError(f"{name} must be a non-negative integer")
+                raise ConfigError(f"{name}: expected a non-negative int")
         if self.source_attention_kv_bucket and not self.source_attention_query_chunk:
-            raise ConfigError("source_attention_kv_bucket requires source_attention_query_chunk")
+            raise ConfigError("source_attention_kv_bucket only applies with a source_attention_query_chunk")
         if (self.source_attention_query_chunk or self.source_attention_kv_bucket) and (
             self.source_attention_backend != "cudnn_graph"
         ):
-            raise ConfigError("source attention chunk and bucket require cudnn_graph")
+            raise ConfigError("source_attention_query_chunk / source_attention_kv_bucket apply to the cudnn_graph backend only")
         for name in ("release_source_gradients", "combine_known_reward_sources"):
             if not _is_bool(getattr(self, name)):
-                raise ConfigError(f"{name} must be true or false")
+                raise ConfigError(f"{name}: expected a bool")
         if self.release_source_gradients and self.source_offload_mode != "pinned_nonblocking":
-            raise ConfigError("release_source_gradients requires pinned_nonblocking sources")
+            raise ConfigError("release_source_gradients applies to pinned_nonblocking sources only")
 
 
 @dataclass(frozen=True, slots=True)
@@ -142,7 +142,7 @@ class GrpoTrainerConfig:
 
         def required(name: str) -> Any:
             if not hasattr(args, name):
-                raise ConfigError(f"trainer build configuration requires {name}, which the entry point does not define")
+                raise ConfigError(f"the trainer configuration needs {name!r}; the parsed arguments do not provide it")
             return getattr(args, name)
 
         def probe(name: str, default: Any) -> Any:
