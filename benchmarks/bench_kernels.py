@@ -260,15 +260,19 @@ def bench_fold(args) -> None:
 
 
 def bench_gemm(args) -> None:
-    """tcgen05 GEMM (CTA-pair, then single-CTA kernel) vs the library GEMM on the decoder's projection shapes."""
+    """tcgen05 GEMM variants vs the library GEMM on the decoder's projection shapes: CTA pairs with the automatic
+    256x256 / 256x512 tile choice (the default), 256x256 only, 256x512 only, and the single-CTA 128x256 kernel."""
     ext = native()
-    for pair in (1, 0):
-        prev = ext.gemm_tc_pair(pair)
-        print(f"-- tcgen05 kernel: {'CTA pair, 256x256 tiles' if pair else 'single CTA, 128x256 tiles'}")
+    variants = [("CTA pair, automatic tile (default)", 1, 1), ("CTA pair, 256x256 tiles", 1, 0),
+                ("CTA pair, 256x512 tiles", 1, 2), ("single CTA, 128x256 tiles", 0, 0)]
+    for name, pair, wide in variants:
+        prev, prev_w = ext.gemm_tc_pair(pair), ext.gemm_tc_wide(wide)
+        print(f"-- tcgen05 kernel: {name}")
         try:
             _bench_gemm_shapes(args)
         finally:
             ext.gemm_tc_pair(prev)
+            ext.gemm_tc_wide(prev_w)
 
 
 def _bench_gemm_shapes(args) -> None:

@@ -1604,6 +1604,23 @@ CUtensorMap make_bf16_map(const void* base, uint64_t inner, uint64_t outer, uint
   return map;
 }
 
+CUtensorMap make_out_map(void* base, bool f32, uint64_t cols, uint64_t rows, uint64_t ld) {
+  const uint64_t es = f32 ? 4 : 2;
+  TS_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TS_CHECK((ld * es) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * es};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base,
+                           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TS_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (output map) failed with ", (int)r);
+  return map;
+}
+
 at::Tensor& tc_error_flag(const at::Device& dev) {
   static std::vector<at::Tensor> flags(64);
   const int i = dev.index();

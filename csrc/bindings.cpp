@@ -34,9 +34,6 @@ std::vector<c10::optional<at::Tensor>> lse_gather(const at::Tensor& logits, cons
 at::Tensor logprob_dlogits(const at::Tensor& logits, const at::Tensor& tgt, const at::Tensor& lse,
                            const at::Tensor& g_lp, const c10::optional<at::Tensor>& g_ent,
                            const c10::optional<at::Tensor>& ent, bool out_bf16);
-std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale);
-std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
-                                 const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale);
 at::Tensor sq_norm(const at::Tensor& x);
 std::vector<at::Tensor> clip_coef(const at::Tensor& sq, double max_norm);
 void adamw_flat(at::Tensor& master, at::Tensor& param, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
@@ -61,9 +58,11 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
                                     const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
                                     const c10::optional<at::Tensor>& dv_out);
 void register_ipc(pybind11::module& m);
+uint64_t bounds_word_rowops(bool reset);
+uint64_t bounds_word_fold(bool reset);
 void register_pinned(pybind11::module& m);
 void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
-             double alpha);
+             double alpha, const c10::optional<at::Tensor>& residual);
 std::vector<at::Tensor> gdn_chunk_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                       const at::Tensor& g, const at::Tensor& beta, const at::Tensor& state);
 std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& dfinal, const at::Tensor& q,
@@ -72,6 +71,11 @@ std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& 
                                       const at::Tensor& tsv, const at::Tensor& psv, const at::Tensor& kd,
                                       const at::Tensor& kb);
 int64_t gemm_tc_pair(int64_t on);
+int64_t gemm_tc_wide(int64_t mode);
+int64_t gemm_tc_direct(int64_t on);
+int64_t gemm_tc_pdl(int64_t on);
+void gemm_tc_profile(int64_t on);
+at::Tensor gemm_tc_profile_read();
 std::vector<at::Tensor> dense_layer_fwd(const at::Tensor& h, const at::Tensor& pos, const at::Tensor& inv_freq,
                                         const at::Tensor& cos_tab, const at::Tensor& sin_tab, const at::Tensor& ln1,
                                         const at::Tensor& wqkv, const c10::optional<at::Tensor>& qn,
@@ -88,7 +92,8 @@ std::vector<at::Tensor> dense_layer_bwd(
     int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov, int64_t sp,
     const std::vector<c10::optional<at::Tensor>>& sinks, double sink_scale, int64_t side);
 void gemm_tc_cat(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& a2,
-                 const c10::optional<at::Tensor>& b2, bool a_t, bool b_t, int64_t mode, double alpha);
+                 const c10::optional<at::Tensor>& b2, bool a_t, bool b_t, int64_t mode, double alpha,
+                 const c10::optional<at::Tensor>& residual);
 std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt,
                                       bool with_entropy);
 at::Tensor lmhead_dlogits_tc(const at::Tensor& h, const at::Tensor& w, const at::Tensor& tgt, const at::Tensor& lse,
@@ -132,8 +137,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("reduce_into", &ts::reduce_into);
   m.def("lse_gather", &ts::lse_gather);
   m.def("logprob_dlogits", &ts::logprob_dlogits);
-  m.def("attn_fwd", &ts::attn_fwd);
-  m.def("attn_bwd", &ts::attn_bwd);
   m.def("sq_norm", &ts::sq_norm);
   m.def("clip_coef", &ts::clip_coef);
   m.def("adamw_flat", &ts::adamw_flat);
@@ -152,12 +155,46 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv1d_silu_fwd", &ts::conv1d_silu_fwd);
   m.def("conv1d_silu_bwd", &ts::conv1d_silu_bwd);
   m.def("gdn_fwd", &ts::gdn_fwd);
-  m.def("gemm_tc", &ts::gemm_tc);
+  m.def("gemm_tc", &ts::gemm_tc, pybind11::arg("out"), pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("a_t"),
+        pybind11::arg("b_t"), pybind11::arg("mode"), pybind11::arg("alpha"),
+        pybind11::arg("residual") = pybind11::none());
   m.def("lmhead_lse_tc", &ts::lmhead_lse_tc);
   m.def("gemm_tc_pair", &ts::gemm_tc_pair);
+  m.def("gemm_tc_wide", &ts::gemm_tc_wide);
+  m.def("gemm_tc_direct", &ts::gemm_tc_direct);
+  m.def("gemm_tc_pdl", &ts::gemm_tc_pdl);
+  m.def("gemm_tc_profile", &ts::gemm_tc_profile);
+  m.def("gemm_tc_profile_read", &ts::gemm_tc_profile_read);
   m.def("dense_layer_fwd", &ts::dense_layer_fwd);
   m.def("dense_layer_bwd", &ts::dense_layer_bwd);
-  m.def("gemm_tc_cat", &ts::gemm_tc_cat);
+  m.def(
+      "bounds_status",
+      [](bool reset) {
+        // failed index checks per source file: {file: (site, index)}; empty when every check passed
+        pybind11::dict out;
+        const std::pair<const char*, uint64_t (*)(bool)> units[] = {{"rowops", &ts::bounds_word_rowops},
+                                                                   {"fold", &ts::bounds_word_fold}};
+        for (const auto& u : units) {
+          const uint64_t w = u.second(reset);
+          if (w != 0) {
+            int64_t idx = (int64_t)(w & 0xFFFFFFFFFFFFull);
+            if (idx & (int64_t(1) << 47)) idx -= int64_t(1) << 48;  // sign-extend a negative index
+            out[u.first] = pybind11::make_tuple((int)(w >> 48), idx);
+          }
+        }
+        return out;
+      },
+      pybind11::arg("reset") = true);
+  m.def("bounds_checked_build", []() {
+#ifdef TS_BOUNDS_CHECK
+    return true;
+#else
+    return false;
+#endif
+  });
+  m.def("gemm_tc_cat", &ts::gemm_tc_cat, pybind11::arg("out"), pybind11::arg("a"), pybind11::arg("b"),
+        pybind11::arg("a2"), pybind11::arg("b2"), pybind11::arg("a_t"), pybind11::arg("b_t"), pybind11::arg("mode"),
+        pybind11::arg("alpha"), pybind11::arg("residual") = pybind11::none());
   m.def("lmhead_dlogits_tc", &ts::lmhead_dlogits_tc);
   m.def("gdn_bwd", &ts::gdn_bwd);
   m.def("gdn_chunk_fwd", &ts::gdn_chunk_fwd);

@@ -1,10 +1,13 @@
 // One Qwen3 decoder layer (forward and backward) issued from C++ (C16, the per-layer executor op).
 //
-// The same kernels and library GEMMs, in the same order and with the same
-// operands, as the Python single-segment path of engine/dense_layer.py; what
-// moves to C++ is the host work between launches (Python op dispatch, view
+// The same kernels and GEMMs, in the same order and with the same operands,
+// as the Python single-segment path of engine/dense_layer.py; what moves to
+// C++ is the host work between launches (Python op dispatch, view
 // bookkeeping, gradient-sink routing). For packs up to ~2k tokens that host
 // work, not the GPU, set the step's pace: about 24 ms per pack of 28 layers.
+// Every projection product is this package's tcgen05 GEMM (gemm_tc.cu): the
+// residual adds ride its epilogue and the weight gradients are TMA
+// reduce-adds into the fp32 gradient sink.
 //
 // Layer: h1 = h + o_proj(attn(rope(norm(qkv(rmsnorm1(h)))))),
 //        out = h1 + down(swiglu(gate_up(rmsnorm2(h1)))).
@@ -48,13 +51,37 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
                                     const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
                                     const c10::optional<at::Tensor>& dv_out);
 
+void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
+             double alpha, const c10::optional<at::Tensor>& residual);
+
 namespace {
+
+// x [M, K] · Wᵀ (W [N, K]) [+ residual], bf16
+at::Tensor lin(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& residual = c10::nullopt) {
+  auto out = at::empty({x.size(0), w.size(0)}, x.options());
+  gemm_tc(out, x, w, false, true, 0, 1.0, residual);
+  return out;
+}
+
+// dy [M, N] · W (W [N, K]), bf16
+at::Tensor mm_w(const at::Tensor& dy, const at::Tensor& w) {
+  auto out = at::empty({dy.size(0), w.size(1)}, dy.options());
+  gemm_tc(out, dy, w, false, false, 0, 1.0, c10::nullopt);
+  return out;
+}
+
+// dyᵀ x (dy [T, N], x [T, K]) -> [N, K] bf16
+at::Tensor mm_tn(const at::Tensor& dy, const at::Tensor& x) {
+  auto out = at::empty({dy.size(1), x.size(1)}, dy.options());
+  gemm_tc(out, dy, x, true, false, 0, 1.0, c10::nullopt);
+  return out;
+}
 
 // target += scale · dyᵀ x (fp32 accumulation into a gradient-sink view); with a side stream the GEMM runs
 // there after the producing work of the current stream, and the operands' memory is kept until it ends
 void deposit(at::Tensor target, const at::Tensor& dy, const at::Tensor& x, double scale, int64_t side) {
   if (side == 0) {
-    at::addmm_out(target, target, dy.t(), x, at::kFloat, 1.0, scale);
+    gemm_tc(target, dy, x, true, false, 2, scale, c10::nullopt);
     return;
   }
   auto main = at::cuda::getCurrentCUDAStream();
@@ -66,7 +93,7 @@ void deposit(at::Tensor target, const at::Tensor& dy, const at::Tensor& x, doubl
   ev.block(st);
   {
     c10::cuda::CUDAStreamGuard guard(st);
-    at::addmm_out(target, target, dy.t(), x, at::kFloat, 1.0, scale);
+    gemm_tc(target, dy, x, true, false, 2, scale, c10::nullopt);
   }
   c10::cuda::CUDACachingAllocator::recordStream(dy.storage().data_ptr(), st);
   c10::cuda::CUDACachingAllocator::recordStream(x.storage().data_ptr(), st);
@@ -88,7 +115,7 @@ std::vector<at::Tensor> dense_layer_fwd(const at::Tensor& h, const at::Tensor& p
   const c10::cuda::CUDAGuard guard(h.device());
   auto r1 = rms_norm_fwd(h, ln1, eps, false);
   const at::Tensor& x1 = r1[0];
-  auto qkv = at::linear(x1, wqkv);
+  auto qkv = lin(x1, wqkv);
   int64_t sp = 0;
   for (const auto& x : past_k) sp += x.size(0);
   auto kbuf = at::empty({sp + t, hkv, d}, h.options());
@@ -105,11 +132,11 @@ std::vector<at::Tensor> dense_layer_fwd(const at::Tensor& h, const at::Tensor& p
   auto att = attn_fwd_tc(q.narrow(0, 0, cov), kbuf.narrow(0, 0, sp + cov), vbuf.narrow(0, 0, sp + cov), scale,
                          o.narrow(0, 0, cov));
   if (cov < t) o.narrow(0, cov, t - cov).zero_();  // pack padding rows: no attention output
-  auto h1 = at::addmm(h, o.view({t, hq * d}), wo.t());
+  auto h1 = lin(o.view({t, hq * d}), wo, h);
   auto r2 = rms_norm_fwd(h1, ln2, eps, false);
-  auto gu = at::linear(r2[0], wgu);
+  auto gu = lin(r2[0], wgu);
   auto a = swiglu_fwd(gu);
-  auto out = at::addmm(h1, a, wd.t());
+  auto out = lin(a, wd, h1);
   return {out, kbuf, vbuf, x1, r1[1], qkv, q, o, att[1], h1, r2[0], r2[1], gu, a};
 }
 
@@ -137,22 +164,22 @@ std::vector<at::Tensor> dense_layer_bwd(
   at::Tensor g_ln1, g_qkv, g_qn, g_kn, g_o, g_ln2, g_gu, g_d;
   auto dout_c = dout.contiguous();
   // out = h1 + down(a)
-  auto da = dout_c.matmul(wd);
+  auto da = mm_w(dout_c, wd);
   if (s_d) deposit(*s_d, dout_c, a, sink_scale, side);
-  else g_d = dout_c.t().matmul(a);
+  else g_d = mm_tn(dout_c, a);
   auto dgu = swiglu_bwd(da, gu);
-  auto dx2 = dgu.matmul(wgu);
+  auto dx2 = mm_w(dgu, wgu);
   if (s_gu) deposit(*s_gu, dgu, x2, sink_scale, side);
-  else g_gu = dgu.t().matmul(x2);
+  else g_gu = mm_tn(dgu, x2);
   // h1 -> rmsnorm2, plus the residual branch's gradient
   auto r2 = rms_norm_bwd(dx2, h1, ln2, rstd2, false, dout_c, s_ln2, s_ln2 ? sink_scale : 1.0);
   const at::Tensor dh1 = r2[0];
   if (!s_ln2) g_ln2 = r2[1];
   // h1 = h + o_proj(o)
-  auto do2 = dh1.matmul(wo);
+  auto do2 = mm_w(dh1, wo);
   auto o2 = o.view({t, hq * d});
   if (s_o) deposit(*s_o, dh1, o2, sink_scale, side);
-  else g_o = dh1.t().matmul(o2);
+  else g_o = mm_tn(dh1, o2);
   auto do3 = do2.view({t, hq, d});
   // attention over [ancestors | own rows]; gradients land where the operands live
   auto dq = at::empty_like(q);
@@ -175,9 +202,9 @@ std::vector<at::Tensor> dense_layer_bwd(
   const at::Tensor dqkv = *rq[0];
   if (qn && !s_qn) g_qn = *rq[1];
   if (kn && !s_kn) g_kn = *rq[2];
-  auto dx1 = dqkv.matmul(wqkv);
+  auto dx1 = mm_w(dqkv, wqkv);
   if (s_qkv) deposit(*s_qkv, dqkv, x1, sink_scale, side);
-  else g_qkv = dqkv.t().matmul(x1);
+  else g_qkv = mm_tn(dqkv, x1);
   // h -> rmsnorm1, plus the residual gradient dh1
   auto r1 = rms_norm_bwd(dx1, h, ln1, rstd1, false, dh1, s_ln1, s_ln1 ? sink_scale : 1.0);
   if (!s_ln1) g_ln1 = r1[1];

@@ -12,9 +12,13 @@
 // SM; they are HBM-bound and issue one load per operand per element.
 #include "common.cuh"
 #include "common.h"
+#include "bounds.cuh"
 
 namespace ts {
 namespace {
+
+constexpr int kSiteGatherTarget = 2;  // bounds site: log-prob gather target id
+constexpr int kSiteFlatVector = 3;   // bounds site (debug build): a flat kernel's float4 index past the end
 
 template <typename S>
 __global__ void fold_kernel(float* __restrict__ g1, float* __restrict__ g2, const S* __restrict__ src, long long n,
@@ -22,6 +26,7 @@ __global__ void fold_kernel(float* __restrict__ g1, float* __restrict__ g2, cons
   const long long nv = n / 4;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv; i += stride) {
+    TS_BOUND_DEBUG(4 * i + 3 < n, kSiteFlatVector, i);
     float s[4];
     if constexpr (std::is_same<S, float>::value) {
       float4 v = reinterpret_cast<const float4*>(src)[i];
@@ -53,6 +58,7 @@ __global__ void axpby_kernel(float* __restrict__ out, const float* __restrict__ 
   const long long nv = n / 4;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv; i += stride) {
+    TS_BOUND_DEBUG(4 * i + 3 < n, kSiteFlatVector, i);
     float4 o = reinterpret_cast<float4*>(out)[i];
     const float4 xv = reinterpret_cast<const float4*>(x)[i];
     if (y != nullptr) {
@@ -148,7 +154,13 @@ __global__ void __launch_bounds__(512) lse_gather_kernel(const float* __restrict
     if (lane == 0) {
       const float L = m + logf(s);
       lse[row] = L;
-      lp[row] = l[tgt[row]] - L;
+      const int64_t target = tgt[row];
+      if (target < 0 || target >= V) {  // a target id outside the vocabulary: recorded, log-prob NaN, no read
+        TS_BOUND_RECORD(kSiteGatherTarget, target);
+        lp[row] = __int_as_float(0x7fc00000);
+      } else {
+        lp[row] = l[target] - L;
+      }
       if (ent != nullptr) ent[row] = L - t / s;
     }
   }
@@ -295,3 +307,5 @@ at::Tensor logprob_dlogits(const at::Tensor& logits, const at::Tensor& tgt, cons
 }
 
 }  // namespace ts
+
+TS_BOUNDS_ACCESSOR(bounds_word_fold)

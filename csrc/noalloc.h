@@ -13,8 +13,11 @@
 extern "C" {
 #endif
 
-// Largest problem the fixed scratch array can serve.
-#define TS_NOALLOC_RMS_MAX_COLS 4096
+// Widest rows served: 4096 columns for bf16, 2048 for fp32 (the fp32 dx
+// kernel keeps a row in registers, 4 floats per 16-byte vector). Wider rows
+// are rejected with error 2 before anything launches.
+#define TS_NOALLOC_RMS_MAX_COLS_BF16 4096
+#define TS_NOALLOC_RMS_MAX_COLS_FP32 2048
 #define TS_NOALLOC_RMS_MAX_CHUNKS 128
 
 // RMSNorm backward without allocating anything.
@@ -23,8 +26,12 @@ extern "C" {
 //   rstd      : [rows] fp32, the forward's reciprocal RMS
 //   dw        : [cols] fp32 output (overwritten, not accumulated)
 //   stream    : the cudaStream_t to launch on
+// dy, x, w and dx must be 16-byte aligned; rstd and dw 4-byte aligned.
 // Returns 0 on success, or a nonzero code whose text ts_noalloc_last_error()
-// returns (sizes beyond the maximum above are rejected before any launch).
+// returns: 1 bad argument (null or misaligned pointer, bad shape or dtype),
+// 2 row width beyond the limit above, 4 no device / symbol lookup failed,
+// 5 a launch of this call failed, 6 a CUDA error from earlier work was
+// already pending (nothing was launched). Codes 1, 2 and 6 launch nothing.
 int ts_rms_norm_bwd_noalloc(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw,
                             int rows, int cols, int dtype, void* stream);
 

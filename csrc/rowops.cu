@@ -8,9 +8,15 @@
 #include "common.cuh"
 #include "common.h"
 #include "noalloc.h"
+#include "bounds.cuh"
+
+#include <atomic>
+#include <cstdint>
 
 namespace ts {
 namespace {
+
+constexpr int kSiteEmbeddingId = 1;  // bounds site: embedding backward token id
 
 constexpr int kWarps = 8;
 
@@ -656,10 +662,12 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ da, const T* __restrict_
 // scale * sum into target[id]. No two blocks touch the same target row.
 template <typename T>
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ order,
-                                     const T* __restrict__ dy, float* __restrict__ target, int n, int D, float scale) {
+                                     const T* __restrict__ dy, float* __restrict__ target, int n, int D, float scale,
+                                     int64_t vocab) {
   const int i = blockIdx.x;
   if (i >= n) return;
   const int64_t id = sorted_ids[i];
+  TS_BOUND(id >= 0 && id < vocab, kSiteEmbeddingId, id);  // a token id outside the embedding table
   if (i > 0 && sorted_ids[i - 1] == id) return;
   int j_end = i + 1;
   while (j_end < n && sorted_ids[j_end] == id) ++j_end;
@@ -966,11 +974,11 @@ void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const a
   if (dy.scalar_type() == at::kBFloat16) {
     embedding_bwd_kernel<__nv_bfloat16><<<n, threads, 0, stream()>>>(
         sid.data_ptr<int64_t>(), order.data_ptr<int64_t>(), (const __nv_bfloat16*)dy.data_ptr(),
-        target.data_ptr<float>(), n, D, (float)scale);
+        target.data_ptr<float>(), n, D, (float)scale, target.size(0));
   } else if (dy.scalar_type() == at::kFloat) {
     embedding_bwd_kernel<float><<<n, threads, 0, stream()>>>(sid.data_ptr<int64_t>(), order.data_ptr<int64_t>(),
                                                             (const float*)dy.data_ptr(), target.data_ptr<float>(), n,
-                                                            D, (float)scale);
+                                                            D, (float)scale, target.size(0));
   } else {
     TS_CHECK(false, "embedding_bwd: unsupported dtype");
   }
@@ -985,7 +993,7 @@ void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const a
 // file-scope array below instead of a caching-allocator buffer.
 //
 // * The array is a fixed 2 MiB (TS_NOALLOC_RMS_MAX_CHUNKS x
-//   TS_NOALLOC_RMS_MAX_COLS floats); every GPU that loads this library holds
+//   TS_NOALLOC_RMS_MAX_COLS_BF16 floats); every GPU that loads this library holds
 //   it until the process exits.
 // * Host code cannot pass the array's name to a kernel (on the host it is only
 //   a stand-in symbol), so the first call on each device, with that device
@@ -999,9 +1007,9 @@ void embedding_bwd_accumulate(at::Tensor& target, const at::Tensor& ids, const a
 namespace ts {
 namespace {
 
-static __device__ __align__(256) float g_noalloc_rms_partial[TS_NOALLOC_RMS_MAX_CHUNKS * TS_NOALLOC_RMS_MAX_COLS];
+static __device__ __align__(256) float g_noalloc_rms_partial[TS_NOALLOC_RMS_MAX_CHUNKS * TS_NOALLOC_RMS_MAX_COLS_BF16];
 
-float* g_noalloc_rms_ptr[64] = {nullptr};
+std::atomic<float*> g_noalloc_rms_ptr[64];
 thread_local char g_noalloc_msg[256] = "";
 
 int noalloc_fail(int code, const char* msg) {
@@ -1012,6 +1020,16 @@ int noalloc_fail(int code, const char* msg) {
 template <typename T, int V>
 void noalloc_dx(const T* dy, const T* x, const T* w, const float* rstd, T* dx, int rows, int H, cudaStream_t st) {
   rms_bwd_dx_kernel<T, V><<<(rows + kWarps - 1) / kWarps, kWarps * 32, 0, st>>>(dy, x, w, rstd, dx, rows, H, 0.f);
+}
+
+// No error was pending when the entry point started (it checks), so an error
+// seen right after a launch belongs to that launch.
+int noalloc_launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return 0;
+  char buf[200];
+  snprintf(buf, sizeof(buf), "ts_rms_norm_bwd_noalloc: %s launch failed: %s", what, cudaGetErrorString(e));
+  return noalloc_fail(5, buf);
 }
 
 template <typename T>
@@ -1026,6 +1044,7 @@ int noalloc_run(const T* dy, const T* x, const T* w, const float* rstd, T* dx, f
   else if (nv <= 12) noalloc_dx<T, 12>(dy, x, w, rstd, dx, rows, H, st);
   else if (nv <= 16) noalloc_dx<T, 16>(dy, x, w, rstd, dx, rows, H, st);
   else return noalloc_fail(3, "ts_rms_norm_bwd_noalloc: row width too large for the register path");
+  if (int rc = noalloc_launch_status("dx")) return rc;
   const int col_blocks = (H + 32 * E - 1) / (32 * E);
   const int target = 2 * sm_count(device);
   int chunks = std::max(1, std::min((rows + 7) / 8, target / std::max(col_blocks, 1)));
@@ -1034,10 +1053,9 @@ int noalloc_run(const T* dy, const T* x, const T* w, const float* rstd, T* dx, f
   chunks = (rows + rows_per_chunk - 1) / rows_per_chunk;
   rms_dw_partial_kernel<T><<<dim3(col_blocks, chunks), dim3(32, 8), 0, st>>>(dy, x, rstd, partial, rows, H,
                                                                             rows_per_chunk);
+  if (int rc = noalloc_launch_status("weight-gradient partials")) return rc;
   sum_partials_kernel<<<(H + 31) / 32, dim3(32, 8), 0, st>>>(partial, dw, chunks, H);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return noalloc_fail(5, cudaGetErrorString(e));
-  return 0;
+  return noalloc_launch_status("weight-gradient sum");
 }
 
 }  // namespace
@@ -1054,24 +1072,51 @@ extern "C" __attribute__((visibility("default"))) int ts_rms_norm_bwd_noalloc(co
   using namespace ts;
   g_noalloc_msg[0] = '\0';
   if (rows < 0 || cols <= 0) return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: rows must be >= 0 and cols > 0");
-  if (cols > TS_NOALLOC_RMS_MAX_COLS) {
+  if (dtype != 0 && dtype != 1) return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: dtype must be 0 (bf16) or 1 (fp32)");
+  const int max_cols = dtype == 0 ? TS_NOALLOC_RMS_MAX_COLS_BF16 : TS_NOALLOC_RMS_MAX_COLS_FP32;
+  if (cols > max_cols) {
     char buf[160];
-    snprintf(buf, sizeof(buf), "ts_rms_norm_bwd_noalloc: cols=%d exceeds the fixed scratch limit of %d columns", cols,
-             TS_NOALLOC_RMS_MAX_COLS);
+    snprintf(buf, sizeof(buf), "ts_rms_norm_bwd_noalloc: cols=%d exceeds the limit of %d columns for %s", cols,
+             max_cols, dtype == 0 ? "bf16" : "fp32");
     return noalloc_fail(2, buf);
   }
-  if (dtype != 0 && dtype != 1) return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: dtype must be 0 (bf16) or 1 (fp32)");
   if ((dtype == 0 && cols % 8) || (dtype == 1 && cols % 4))
     return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: cols must be a multiple of 8 (bf16) or 4 (fp32)");
+  // dw is always written; the row operands only when there are rows. The
+  // kernels move rows in 16-byte vectors, so those pointers must be 16-byte
+  // aligned (an offset view of a tensor may not be).
+  auto misaligned = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; };
+  if (dw == nullptr || misaligned(dw, 4)) return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: dw is null or not 4-byte aligned");
+  if (rows > 0) {
+    if (!dy || !x || !w || !dx || !rstd)
+      return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: dy, x, w, rstd and dx must not be null");
+    if (misaligned(dy, 16) || misaligned(x, 16) || misaligned(w, 16) || misaligned(dx, 16))
+      return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: dy, x, w and dx must be 16-byte aligned");
+    if (misaligned(rstd, 4)) return noalloc_fail(1, "ts_rms_norm_bwd_noalloc: rstd must be 4-byte aligned");
+  }
+  {
+    // an error left by earlier work on this thread would otherwise be
+    // reported (and cleared) as if one of this call's launches had failed
+    const cudaError_t pending = cudaPeekAtLastError();
+    if (pending != cudaSuccess) {
+      char buf[200];
+      snprintf(buf, sizeof(buf), "ts_rms_norm_bwd_noalloc: a CUDA error from earlier work is pending: %s",
+               cudaGetErrorString(pending));
+      return noalloc_fail(6, buf);
+    }
+  }
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
     return noalloc_fail(4, "ts_rms_norm_bwd_noalloc: no current CUDA device");
-  if (g_noalloc_rms_ptr[device] == nullptr) {
-    // once per device, with that device current: the array's device address
+  float* scratch = g_noalloc_rms_ptr[device].load(std::memory_order_acquire);
+  if (scratch == nullptr) {
+    // once per device, with that device current: the array's device address.
+    // Threads that race here all store the same address.
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_rms_partial);
     if (e != cudaSuccess || p == nullptr) return noalloc_fail(4, cudaGetErrorString(e));
-    g_noalloc_rms_ptr[device] = static_cast<float*>(p);
+    scratch = static_cast<float*>(p);
+    g_noalloc_rms_ptr[device].store(scratch, std::memory_order_release);
   }
   if (rows == 0) {
     return cudaMemsetAsync(dw, 0, sizeof(float) * cols, static_cast<cudaStream_t>(stream)) == cudaSuccess
@@ -1081,8 +1126,9 @@ extern "C" __attribute__((visibility("default"))) int ts_rms_norm_bwd_noalloc(co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == 0)
     return noalloc_run<__nv_bfloat16>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w,
-                                      rstd, (__nv_bfloat16*)dx, dw, rows, cols, g_noalloc_rms_ptr[device], device,
-                                      st);
+                                      rstd, (__nv_bfloat16*)dx, dw, rows, cols, scratch, device, st);
   return noalloc_run<float>((const float*)dy, (const float*)x, (const float*)w, rstd, (float*)dx, dw, rows, cols,
-                            g_noalloc_rms_ptr[device], device, st);
+                            scratch, device, st);
 }
+
+TS_BOUNDS_ACCESSOR(bounds_word_rowops)

@@ -27,8 +27,11 @@ NVCC_FLAGS = [
     "-U__CUDA_NO_BFLOAT16_OPERATORS__",
     "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
 ]
+CXX_FLAGS = ["-O3", "-std=c++17"]
 if os.environ.get("TS_BOUNDS_CHECK"):
+    # bounds-checked debug build: the TS_BOUND_DEBUG index checks (csrc/bounds.cuh) are compiled in
     NVCC_FLAGS.append("-DTS_BOUNDS_CHECK=1")
+    CXX_FLAGS.append("-DTS_BOUNDS_CHECK=1")
 if os.environ.get("TS_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
 
@@ -52,7 +55,7 @@ setup(
             "thundersync_b200._C",
             SOURCES,
             include_dirs=[os.path.join(ROOT, "csrc")],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
         )
     ],
     cmdclass={"build_ext": Build},

@@ -352,19 +352,24 @@ def test_attention_tcgen05_backward(t, s, hq, hkv, d):
     assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)
 
 
-@pytest.mark.parametrize("pair", [True, False])
-@pytest.mark.parametrize("m,n,k", [(256, 512, 128), (304, 200, 72), (2304, 4096, 2048), (128, 151936 // 8, 256)])
+@pytest.mark.parametrize("kernel", ["pair", "pair_tma_store", "wide", "single"])
+@pytest.mark.parametrize("m,n,k", [(256, 512, 128), (304, 200, 72), (2304, 4096, 2048), (128, 151936 // 8, 256),
+                                   (600, 1288, 264)])
 @pytest.mark.parametrize("a_t,b_t", [(False, True), (False, False), (True, False), (True, True)])
-def test_gemm_tcgen05(m, n, k, a_t, b_t, pair):
-    """Single-CTA and CTA-pair (cta_group::2) kernels against an fp32 PyTorch matmul."""
+def test_gemm_tcgen05(m, n, k, a_t, b_t, kernel):
+    """Single-CTA, CTA-pair (cta_group::2, 256 x 256 tiles; register or TMA-store epilogue) and wide CTA-pair
+    (256 x 512 tiles) kernels against an fp32 PyTorch matmul."""
     from thundersync_b200.ops._ext import native
-    from thundersync_b200.ops.gemm import gemm, gemm_accumulate
 
-    prev = native().gemm_tc_pair(1 if pair else 0)
+    prev = native().gemm_tc_pair(0 if kernel == "single" else 1)
+    prev_w = native().gemm_tc_wide(2 if kernel == "wide" else 0)
+    prev_d = native().gemm_tc_direct(0 if kernel == "pair_tma_store" else 1)
     try:
         _check_gemm(m, n, k, a_t, b_t)
     finally:
         native().gemm_tc_pair(prev)
+        native().gemm_tc_wide(prev_w)
+        native().gemm_tc_direct(prev_d)
 
 
 @pytest.mark.parametrize("pair", [True, False])
@@ -404,6 +409,14 @@ def _check_gemm(m, n, k, a_t, b_t):
     acc = torch.ones(m, n, device=DEV)
     gemm_accumulate(acc, a, b, a_t=a_t, b_t=b_t, alpha=2.0)
     assert _rel(acc, 1.0 + 2.0 * ref) < 1e-5
+    # residual operand added in the epilogue (out = a·b + R, one rounding)
+    res = torch.randn(m, n, device=DEV, dtype=torch.bfloat16)
+    got_r = gemm(a, b, a_t=a_t, b_t=b_t, residual=res)
+    assert _rel(got_r, ref + res.float()) < 1e-2
+    # output rows inside a wider buffer (row stride > N): the TMA store writes only the view
+    wide = torch.full((m, n + 8), 3.0, device=DEV)
+    gemm(a, b, a_t=a_t, b_t=b_t, out_dtype=torch.float32, out=wide[:, :n])
+    assert _rel(wide[:, :n], ref) < 1e-5 and bool((wide[:, n:] == 3.0).all())
     from thundersync_b200.ops._ext import native
 
     assert int(native().tc_status(a).item()) == 0
@@ -463,3 +476,28 @@ def test_boundary_adjoint_native_fixed_order(n_adj, dtype):
     again = reduce_boundary_adjoints(adj, existing=existing, backend="native")
     assert torch.equal(got, again)
     assert torch.equal(reduce_boundary_adjoints([None, adj[0]], backend="native").cpu(), adj[0].cpu())
+
+
+def test_index_checks_record_out_of_range_ids_without_faulting():
+    """Token and target ids outside their tables are skipped on the device and reported to the host."""
+    from thundersync_b200.ops._ext import native
+
+    ext = native()
+    ext.bounds_status(True)  # clear anything an earlier test left
+    vocab, d = 64, 128
+    target = torch.zeros(vocab, d, device=DEV)
+    ids = torch.tensor([3, 70, 3, 5], device=DEV, dtype=torch.long)  # 70 is outside the 64-row table
+    dy = torch.ones(4, d, device=DEV, dtype=torch.bfloat16)
+    ext.embedding_bwd_accumulate(target, ids, dy, 1.0)
+    torch.cuda.synchronize()
+    status = ext.bounds_status(True)
+    assert status == {"rowops": (1, 70)}, status
+    assert torch.equal(target[3], torch.full((d,), 2.0, device=DEV)) and torch.equal(target[5], torch.ones(d, device=DEV))
+    logits = torch.randn(3, 256, device=DEV)
+    tgt = torch.tensor([1, -2, 255], device=DEV, dtype=torch.long)
+    lp, lse, _ = ext.lse_gather(logits, tgt, False)
+    torch.cuda.synchronize()
+    assert ext.bounds_status(True) == {"fold": (2, -2)}
+    ref = torch.log_softmax(logits, -1)
+    assert torch.isnan(lp[1]) and torch.allclose(lp[0], ref[0, 1], atol=1e-5) and torch.allclose(lp[2], ref[2, 255], atol=1e-5)
+    assert ext.bounds_status(False) == {}

@@ -292,6 +292,8 @@ def full_causal_logits(model, input_ids: torch.Tensor, position_ids: torch.Tenso
     ex = Executor(model)
     h, _ = ex.run(ids, pos, [Segment(0, t, [])])
     w = ex.head_weight()
-    if h.dtype in (torch.bfloat16, torch.float16) and h.is_cuda:
-        return torch.mm(h, w.t(), out_dtype=torch.float32)
+    if h.dtype == torch.bfloat16 and h.is_cuda:
+        from thundersync_b200.ops.gemm import gemm
+
+        return gemm(h, w, out_dtype=torch.float32)
     return h.float() @ w.float().t()

@@ -1,10 +1,10 @@
 """Projection GEMMs with gradient-sink-aware weight gradients.
 
-Plain projections are library GEMMs (cuBLAS through ``torch.nn.functional.linear``).
-What this module adds is where the weight gradient goes: under an active
-:class:`~thundersync_b200.ops.sink.GradSink` the backward accumulates
-``dW += dYᵀ·X`` straight into the sink's fp32 buffer (cuBLASLt with an fp32
-C operand and beta = 1), so no per-call weight gradient is ever allocated.
+On CUDA every projection product (``y = x·Wᵀ [+ residual]``, ``dx = dy·W``,
+``dW += dyᵀ·x``) runs on this package's tcgen05 GEMM (``ops/gemm.py``). Under
+an active :class:`~thundersync_b200.ops.sink.GradSink` the backward
+accumulates ``dW += dYᵀ·X`` straight into the sink's fp32 buffer (the GEMM
+epilogue's TMA reduce-add), so no per-call weight gradient is ever allocated.
 Several weights that sit back to back in the parameter arena (q/k/v,
 gate/up) run as one GEMM over a single weight view.
 """
@@ -12,9 +12,9 @@ gate/up) run as one GEMM over a single weight view.
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from thundersync_b200.ops import sink as _sink
+from thundersync_b200.ops.gemm import gemm, matmul
 
 
 class _Linear(torch.autograd.Function):
@@ -31,12 +31,10 @@ class _Linear(torch.autograd.Function):
             w = weights[0]
         else:
             w = torch.cat(weights, 0)
-        if residual is None:
-            y = F.linear(x, w)
-        elif x.is_cuda and x.dim() == 2:
-            y = torch.addmm(residual, x, w.t())
-        else:
-            y = residual + F.linear(x, w)
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        r2 = None if residual is None else residual.reshape(-1, residual.shape[-1])
+        y = gemm(x2, w, residual=r2).reshape(*lead, w.shape[0])
         ctx.save_for_backward(x, w)
         ctx.n_weights = len(weights)
         ctx.rows = [t.shape[0] for t in weights]
@@ -49,7 +47,7 @@ class _Linear(torch.autograd.Function):
         weights = ctx.weights
         dx = None
         if ctx.needs_input_grad[0]:
-            dx = dy.matmul(w)
+            dx = matmul(dy, w)
         grads = [None] * ctx.n_weights
         need_w = any(ctx.needs_input_grad[2:])
         if need_w:
@@ -67,7 +65,8 @@ class _Linear(torch.autograd.Function):
                         s.addmm_(s.view(t), dy2[:, r0 : r0 + r], x2, side=True)
                         r0 += r
             else:
-                dw = dy2.t().matmul(x2)
+                dw = gemm(dy2, x2, a_t=True, b_t=False,
+                          out_dtype=torch.float32 if dy2.is_cuda else dy2.dtype)
                 r0 = 0
                 for i, r in enumerate(ctx.rows):
                     if ctx.needs_input_grad[2 + i]:

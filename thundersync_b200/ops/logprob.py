@@ -21,6 +21,7 @@ import torch
 
 from thundersync_b200.ops import sink as _sink
 from thundersync_b200.ops._ext import native
+from thundersync_b200.ops.gemm import gemm, gemm_accumulate
 
 DEFAULT_ROWS = 2048
 # tcgen05 GEMM with fused log-sum-exp / dlogits epilogues on CUDA bf16 (False: cuBLAS logits + row kernels)
@@ -34,7 +35,9 @@ def _fused_ok(hidden: torch.Tensor, weight: torch.Tensor) -> bool:
 
 
 def _logits_fp32(h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    if h.is_cuda and h.dtype in (torch.bfloat16, torch.float16):
+    if h.is_cuda and h.dtype == torch.bfloat16:
+        return gemm(h, w, out_dtype=torch.float32)
+    if h.is_cuda and h.dtype == torch.float16:
         return torch.mm(h, w.t(), out_dtype=torch.float32)
     acc = torch.float64 if h.dtype == torch.float64 else torch.float32
     return torch.mm(h.to(acc), w.to(acc).t())
@@ -152,14 +155,14 @@ class _LMHeadLogprob(torch.autograd.Function):
                 d_mm = d
             if need_h:
                 if d_mm.dtype == hidden.dtype:
-                    dh[r0:r1] = d_mm.matmul(weight)
+                    gemm(d_mm, weight, b_t=False, out=dh[r0:r1])
                 else:
                     dh[r0:r1] = d_mm.matmul(weight.to(d_mm.dtype)).to(hidden.dtype)
             if need_w:
                 if sink_w:
                     s.addmm_(s.view(weight), d_mm, h)
                 elif d_mm.is_cuda and d_mm.dtype != dw_acc.dtype:
-                    torch.addmm(dw_acc, d_mm.t(), h, out_dtype=dw_acc.dtype, out=dw_acc)
+                    gemm_accumulate(dw_acc, d_mm, h, a_t=True, b_t=False)
                 else:
                     dw_acc.addmm_(d_mm.t().to(dw_acc.dtype), h.to(dw_acc.dtype))
         ctx.weight = None

@@ -1,10 +1,10 @@
 """LoRA projection (K11′): ``y = x·Wᵀ + s·(x·Aᵀ)·Bᵀ`` without merging B·A into W.
 
 The frozen base weight W keeps its dtype (bf16); the adapters A [r, in] and
-B [out, r] are fp32 parameters. On CUDA with bf16 activations the rank-r
-products are bf16 tensor-core GEMMs with fp32 accumulation (the adapters are
-read as bf16, as a bf16 PEFT forward reads them) and the base product is the
-C operand of the second one, so the output is rounded once; elsewhere the
+B [out, r] are fp32 parameters. On CUDA with bf16 activations every product
+is this package's tcgen05 GEMM with fp32 accumulation (the adapters are read
+as bf16, as a bf16 PEFT forward reads them) and the base product enters the
+rank-r GEMM's epilogue, so the output is rounded once; elsewhere the
 low-rank path runs in fp32 — the numerics of an unmerged PEFT ``lora.Linear``
 (reference: src/thundersync/policy_model.py:240-290 builds it through PEFT).
 
@@ -23,6 +23,7 @@ import torch
 import torch.nn.functional as F
 
 from thundersync_b200.ops import sink as _sink
+from thundersync_b200.ops.gemm import gemm
 
 __all__ = ["lora_linear", "lora_parts"]
 
@@ -42,7 +43,7 @@ def _deposit(param: torch.Tensor, lhs: torch.Tensor, rhs: torch.Tensor):
         s.addmm_(s.view(param), lhs, rhs)
         return None
     if lhs.is_cuda and lhs.dtype == torch.bfloat16:
-        return torch.mm(lhs.t(), rhs, out_dtype=torch.float32).to(param.dtype)
+        return gemm(lhs, rhs, a_t=True, b_t=False, out_dtype=torch.float32).to(param.dtype)
     return lhs.t().matmul(rhs).to(param.dtype)
 
 
@@ -87,7 +88,7 @@ class _LoRALinear(torch.autograd.Function):
             # u = s·x·Aᵀ (fp32 accumulation, bf16 result, saved for dB); with the fused GEMM the rank-r
             # update is the main loop's last K block, otherwise the base product is the C operand of the
             # rank-r GEMM: either way y is rounded once
-            u = torch.mm(x2, _bf16_scaled(a, scale, x2.dtype).t())
+            u = gemm(x2, _bf16_scaled(a, scale, x2.dtype))
             bb = _bf16_scaled(b, 1.0, x2.dtype)
             if _fused_ok(w, a.shape[0]):
                 from thundersync_b200.ops._ext import native
@@ -95,7 +96,7 @@ class _LoRALinear(torch.autograd.Function):
                 y = x2.new_empty(x2.shape[0], w.shape[0])
                 native().gemm_tc_cat(y, x2.contiguous(), w, u, bb, False, True, 0, 1.0)
             else:
-                y = torch.addmm(F.linear(x2, w), u, bb.t())
+                y = gemm(u, bb, residual=gemm(x2, w))
         else:
             base = F.linear(x2, w)
             u = F.linear(x2.to(a.dtype), a)  # [T, r], adapter precision
@@ -113,7 +114,7 @@ class _LoRALinear(torch.autograd.Function):
         dx = da = db = dw = None
         if _tc(dy2):
             ab = _bf16_scaled(a, 1.0, dy2.dtype)
-            gs = torch.mm(dy2, _bf16_scaled(b, s, dy2.dtype))  # s·dy·B [T, r]
+            gs = gemm(dy2, _bf16_scaled(b, s, dy2.dtype), b_t=False)  # s·dy·B [T, r]
             if ctx.needs_input_grad[0]:
                 if _fused_ok(w, a.shape[0]):
                     from thundersync_b200.ops._ext import native
@@ -122,7 +123,7 @@ class _LoRALinear(torch.autograd.Function):
                     native().gemm_tc_cat(dx, dy2.contiguous(), w, gs, ab.contiguous(), False, False, 0, 1.0)
                     dx = dx.view(ctx.in_shape)
                 else:
-                    dx = torch.addmm(dy2.matmul(w), gs, ab).view(ctx.in_shape)
+                    dx = gemm(gs, ab, b_t=False, residual=gemm(dy2, w, b_t=False)).view(ctx.in_shape)
             if ctx.needs_input_grad[2]:
                 da = _deposit(a, gs, x2)
             if ctx.needs_input_grad[3]:
@@ -137,7 +138,7 @@ class _LoRALinear(torch.autograd.Function):
             if ctx.needs_input_grad[3]:
                 db = _deposit(b, dyf, u * s)
         if ctx.needs_input_grad[1]:
-            dw = dy2.t().matmul(x2).to(w.dtype)
+            dw = gemm(dy2, x2, a_t=True, b_t=False, out_dtype=torch.float32).to(w.dtype)
         return dx, dw, da, db, None
 
 
