@@ -1,6 +1,14 @@
-"""Streaming-GRPO throughput benchmark (Qwen3-1.7B full fine-tune).
+"""Streaming-GRPO throughput benchmark (default: config 2, Qwen3-1.7B full fine-tune).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|5]
+
+``--config 3``: Qwen3-8B architecture with LoRA r64/alpha 128 on q/k/v/o/gate/up/down (frozen bf16 base,
+fp32 adapters), agentic multi-turn GRPO: per rank 4 groups x 16 trajectories (32 x 16 at 8 GPUs), a
+2048-token prompt, 4-16 turns of U[128,1024] scored action tokens followed by U[64,2048] unscored tool
+tokens, context capped at 32768, rewards U[0,1].
+``--config 5``: hybrid 48-layer model (3x gated DeltaNet + 1x gated attention, GQA 16/2, head_dim 256),
+per rank 2 groups x 8 trajectories (16 x 8 at 8 GPUs), 1024-token prompt, completions U[4096,32768],
+rewards Bernoulli(0.5).
 
 For N > 1 launch one process per GPU with torch.distributed.run; every rank
 reads RANK / LOCAL_RANK / WORLD_SIZE / MASTER_* from the environment.
@@ -52,6 +60,126 @@ BASELINE_VALUE = None  # the reference publishes no number for this metric
 
 
 # ----------------------------------------------------------------------------- workload
+CONFIGS = {
+    2: dict(model="qwen3-1.7b", groups_per_rank=8, group_size=8, prompt_len=512, min_len=256, max_len=4096,
+            rewards="bernoulli", reward_p=0.3, lora=0),
+    3: dict(model="qwen3-8b", groups_per_rank=4, group_size=16, prompt_len=2048, rewards="uniform", lora=64,
+            lora_alpha=128, turns=(4, 16), scored=(128, 1024), unscored=(64, 2048), context_cap=32768),
+    4: dict(model="qwen3-4b", groups_per_rank=32, group_size=1, prompt_len=512, rewards="teacher", lora=0,
+            actions=(8, 32), action_tokens=(64, 512), observation_tokens=(32, 512), teacher_mean=1.5,
+            teacher_latency_s=0.5),
+    5: dict(model="hybrid-48l", groups_per_rank=2, group_size=8, prompt_len=1024, min_len=4096, max_len=32768,
+            rewards="bernoulli", reward_p=0.5, lora=0),
+}
+
+
+def make_step_opd(rank: int, step: int, args) -> dict:
+    """Config 4: per rank 32 single-trajectory groups (256 at 8 GPUs), each 8-32 actions of U[64,512] scored
+    tokens after U[32,512] unscored observation tokens; teacher log-probs -Exp(mean 1.5) clipped to [-20, 0]
+    arrive per action after Exp(mean 0.5 s); actions are delivered in that arrival order."""
+    c = CONFIGS[4]
+    rng = random.Random(args.seed * 1_000_003 + rank * 10_007 + step)
+    groups, events = [], []
+    for g in range(args.groups_per_rank):
+        prompt = [rng.randrange(args.vocab) for _ in range(args.prompt_len)]
+        groups.append((g, prompt, [g]))
+        t = 0.0
+        n_act = rng.randint(*c["actions"])
+        for k in range(n_act):
+            obs = [rng.randrange(args.vocab) for _ in range(rng.randint(*c["observation_tokens"]))] if k else []
+            act = [rng.randrange(args.vocab) for _ in range(rng.randint(*c["action_tokens"]))]
+            teacher = [max(-20.0, -rng.expovariate(1.0 / c["teacher_mean"])) for _ in act]
+            t += rng.expovariate(1.0 / c["teacher_latency_s"])
+            events.append((t, g, k, obs + act, [False] * len(obs) + [True] * len(act), teacher, k == n_act - 1))
+    events.sort(key=lambda e: e[0])
+    scored = sum(sum(e[4]) for e in events)
+    tokens = sum(len(e[3]) for e in events) + sum(len(p) for _, p, _ in groups)
+    return {"groups": groups, "events": events, "scored": scored, "tokens": tokens}
+
+
+class OPDTrainer:
+    """Config 4 driver over either package's public OPD API: a run and an ``OPDTurnStream`` per batch, the
+    step's gradient (normalised by the batch's scored-token count across ranks) and the optimizer."""
+
+    def __init__(self, model, make_run, make_objective, optimizer, device, world, flat=None, reducer=None):
+        self.model, self.make_run, self.make_objective = model, make_run, make_objective
+        self.opt, self.device, self.world = optimizer, device, world
+        self.flat, self.reducer = flat, reducer
+        self._new()
+
+    def _new(self):
+        self.run = self.make_run(self.model)
+        self.obj = self.make_objective(self.run, self.model)
+        if self.reducer is not None:
+            self.obj.use_main_grad_buffer(self.reducer.main_grad_buffer())
+
+    def step_batch(self, work, tail_start=None) -> dict:
+        for g, prompt, _ in work["groups"]:
+            self.obj.open_group(g, prompt)
+        n = len(work["events"])
+        for i, (_, g, k, toks, mask, teacher, last) in enumerate(work["events"]):
+            if i == n - 1 and tail_start is not None:
+                tail_start.record()  # the step's last teacher score arrives: the tail starts
+            self.obj.append_scored_turn(g, g, toks, mask,
+                                        teacher_logprobs=torch.tensor(teacher, dtype=torch.float32).to(
+                                            self.device, non_blocking=True), return_loss=False)
+            if last:
+                self.obj.close_trajectory(g)
+                self.obj.close_group(g)
+        return self.finish()
+
+    def finish(self) -> dict:
+        if self.flat:
+            self.obj.assert_safe_to_step(materialize=False)
+            grad = self.obj.main_grad()
+            if self.world > 1:
+                # the objective divided by its local scored-token mass; the step wants the global mass
+                mass = torch.tensor([self.obj.normalization_divisor], dtype=torch.float64, device=self.device)
+                dist.all_reduce(mass)
+                scale = self.world * self.obj.normalization_divisor / float(mass)
+                self.reducer.all_reduce_mean(grad, pre_scale=scale)
+            from thundersync_b200.parallel.optimizer import global_sq_norm
+
+            coef, nrm = self.opt.clip_coefficient(global_sq_norm(grad), 1.0)
+            self.opt.step(grad, clip_coef=coef)
+        else:
+            self.obj.assert_safe_to_step()
+            params = [p for p in self.model.parameters() if p.requires_grad]
+            if self.world > 1:
+                for p in params:
+                    dist.all_reduce(p.grad)
+                    p.grad.div_(self.world)
+            nrm = torch.nn.utils.clip_grad_norm_(params, 1.0)
+            self.opt.step()
+            self.opt.zero_grad(set_to_none=True)
+        self.run.close() if hasattr(self.run, "close") else None
+        self._new()
+        return {"global_grad_norm": float(nrm)}
+
+
+def _turns(rng: random.Random, args) -> list[tuple[list[int], list[bool]]]:
+    """One trajectory's turns: one scored completion (configs 2, 5) or agentic (scored action, unscored
+    tool output) turns within the context cap (config 3)."""
+    c = CONFIGS[args.config]
+    if "turns" not in c:
+        n = rng.randint(args.min_len, args.max_len)
+        return [([rng.randrange(args.vocab) for _ in range(n)], [True] * n)]
+    room = c["context_cap"] - args.prompt_len
+    out = []
+    for _ in range(rng.randint(*c["turns"])):
+        a = rng.randint(*c["scored"])
+        o = rng.randint(*c["unscored"])
+        if a + o > room:
+            a = min(a, room)
+            o = max(0, min(o, room - a))
+        if a <= 0:
+            break
+        toks = [rng.randrange(args.vocab) for _ in range(a + o)]
+        out.append((toks, [True] * a + [False] * o))
+        room -= a + o
+    return out
+
+
 def make_step(rank: int, step: int, args) -> dict:
     rng = random.Random(args.seed * 1_000_003 + rank * 10_007 + step)
     groups = []
@@ -61,27 +189,32 @@ def make_step(rank: int, step: int, args) -> dict:
         tids = []
         for j in range(args.group_size):
             tid = g * args.group_size + j
-            n = rng.randint(args.min_len, args.max_len)
-            tokens = [rng.randrange(args.vocab) for _ in range(n)]
-            reward = 1.0 if rng.random() < args.reward_p else 0.0
+            turns = _turns(rng, args)
+            if CONFIGS[args.config]["rewards"] == "uniform":
+                reward = rng.random()
+            else:
+                reward = 1.0 if rng.random() < args.reward_p else 0.0
             t_arrive = rng.expovariate(1.0 / args.mean_arrival_s)
-            arrivals.append((t_arrive, g, tid, tokens, reward))
+            arrivals.append((t_arrive, g, tid, turns, reward))
             tids.append(tid)
         groups.append((g, prompt, tids))
     arrivals.sort(key=lambda a: a[0])
-    scored = sum(len(a[3]) for a in arrivals)
-    tokens = scored + sum(len(p) for _, p, _ in groups)
+    scored = sum(sum(m) for a in arrivals for _, mask in a[3] for m in [mask])
+    tokens = sum(len(t) for a in arrivals for t, _ in a[3]) + sum(len(p) for _, p, _ in groups)
     return {"groups": groups, "arrivals": arrivals, "scored": scored, "tokens": tokens}
 
 
 def run_step(trainer, work, tail_start: torch.cuda.Event | None):
+    if isinstance(trainer, OPDTrainer):
+        return trainer.step_batch(work, tail_start)
     remaining = {g: len(tids) for g, _, tids in work["groups"]}
     for g, prompt, tids in work["groups"]:
         trainer.open_group(g, prompt)
         trainer.register_group_trajectories(g, tids)
     n = len(work["arrivals"])
-    for i, (_, g, tid, tokens, reward) in enumerate(work["arrivals"]):
-        trainer.append_turn(g, tid, tokens, [True] * len(tokens))
+    for i, (_, g, tid, turns, reward) in enumerate(work["arrivals"]):
+        for tokens, mask in turns:
+            trainer.append_turn(g, tid, tokens, mask)
         if i == n - 1 and tail_start is not None:
             tail_start.record()
         trainer.close_trajectory(tid, reward)
@@ -160,12 +293,25 @@ def build_ours(args, device):
     from thundersync_b200.parallel.optimizer import FlatAdamW
 
     torch.manual_seed(args.seed)
-    cfg = PRESETS[args.model]
-    with torch.device(device):
-        model = Qwen3ForCausalLM(cfg)
+    if args.model.startswith("hybrid"):
+        from thundersync_b200.models.hybrid import HYBRID_PRESETS, HybridForCausalLM
+
+        with torch.device(device):
+            model = HybridForCausalLM(HYBRID_PRESETS[args.model])
+    else:
+        with torch.device(device):
+            model = Qwen3ForCausalLM(PRESETS[args.model])
     model.to(dtype=torch.bfloat16)
+    c = CONFIGS[args.config]
+    if c["lora"]:
+        from thundersync_b200.policy_model import apply_lora
+
+        _, model = apply_lora(model, rank=c["lora"], alpha=c["lora_alpha"])
     arena = arena_for(model)
-    opt = FlatAdamW(arena, lr=args.lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, maximize=True)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    # config 2: data parallel with a sharded optimizer (ZeRO-1: reduce-scatter -> shard AdamW -> bf16 gather)
+    make = FlatAdamW.sharded if world > 1 else FlatAdamW
+    opt = make(arena, lr=args.lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, maximize=True)
 
     def factory(m):
         return StreamingRun(m, boundary_cut=True, checkpoint=False, stream_turns=False,
@@ -175,7 +321,8 @@ def build_ours(args, device):
         model, opt, run_factory=factory, grad_clip=1.0,
         source_offload_device=None, source_offload_mode="device_resident",
     )
-    trainer.configure_binary_rewards()
+    if CONFIGS[args.config]["rewards"] == "bernoulli":
+        trainer.configure_binary_rewards()
     return model, trainer
 
 
@@ -213,6 +360,58 @@ def _reference_snapshot(args, device, c) -> str:
     return path
 
 
+def build_ours_opd(args, device, world):
+    from thundersync_b200.engine.streaming import StreamingRun, arena_for
+    from thundersync_b200.models.qwen3 import PRESETS, Qwen3ForCausalLM
+    from thundersync_b200.opd.objectives import OPDTurnStream
+    from thundersync_b200.parallel.optimizer import FlatAdamW
+
+    torch.manual_seed(args.seed)
+    with torch.device(device):
+        model = Qwen3ForCausalLM(PRESETS[args.model])
+    model.to(dtype=torch.bfloat16).eval()  # turn replay needs a deterministic forward
+    arena = arena_for(model)
+    reducer = None
+    if world > 1:
+        from thundersync_b200.parallel.reduce import GradientReducer
+
+        with torch.no_grad():
+            dist.broadcast(arena.flat, src=0)
+        reducer = GradientReducer(arena.numel, device, arena=arena)
+    opt = FlatAdamW(arena, lr=args.lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0)
+    return model, OPDTrainer(
+        model, lambda m: StreamingRun(m, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True),
+        lambda r, m: OPDTurnStream(r, m), opt, device, world, flat=True, reducer=reducer)
+
+
+def build_reference_opd(args, device, world):
+    """The reference's OPD objective through its public API (``StreamingRun`` + ``OPDTurnStream``, torch
+    AdamW; reference src/thundersync/opd/objectives.py:947-1180) on the same random-init snapshot."""
+    from thundersync import STREAM_ATTENTION_NAME, register_stream_attention
+    from thundersync.engine.streaming import StreamingRun
+    from thundersync.opd.objectives import OPDTurnStream
+    from transformers import AutoModelForCausalLM
+
+    from thundersync_b200.models.qwen3 import PRESETS
+
+    snapshot = _reference_snapshot(args, device, PRESETS[args.model])
+    register_stream_attention()
+    model = AutoModelForCausalLM.from_pretrained(snapshot, dtype=torch.bfloat16,
+                                                 attn_implementation=STREAM_ATTENTION_NAME,
+                                                 local_files_only=True).to(device)
+    model.config.use_cache = False
+    model.eval()
+    if world > 1:
+        with torch.no_grad():
+            for t in model.state_dict().values():
+                dist.broadcast(t, src=0)
+    opt = torch.optim.AdamW([p for p in model.parameters() if p.requires_grad], lr=args.lr, betas=(0.9, 0.999),
+                            eps=1e-8, weight_decay=0.0)
+    return model, OPDTrainer(
+        model, lambda m: StreamingRun(m, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True),
+        lambda r, m: OPDTurnStream(r, m), opt, device, world, flat=False)
+
+
 def build_reference(args, device):
     """The unmodified reference, built by its own production builder.
 
@@ -228,6 +427,16 @@ def build_reference(args, device):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "thundersync")):
         raise RuntimeError("reference not installed under baseline/_ref")
+    if args.config == 3:
+        import importlib.util
+
+        if importlib.util.find_spec("peft") is None:
+            raise RuntimeError("config 3 needs the reference's LoRA path (thundersync.policy_model.apply_lora), "
+                               "which imports peft; peft is not installed on this image")
+    if args.config == 5:
+        raise RuntimeError("config 5 runs the reference's hybrid layers through flash-linear-attention's "
+                           "chunk_gated_delta_rule, which raised a misaligned-address fault on this pool's "
+                           "B200s; it is not run again")
     sys.path.insert(0, ref)
     from types import SimpleNamespace
 
@@ -289,13 +498,15 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--model", default="qwen3-1.7b")
-    ap.add_argument("--groups-per-rank", type=int, default=8)
-    ap.add_argument("--group-size", type=int, default=8)
-    ap.add_argument("--prompt-len", type=int, default=512)
-    ap.add_argument("--min-len", type=int, default=256)
-    ap.add_argument("--max-len", type=int, default=4096)
-    ap.add_argument("--reward-p", type=float, default=0.3)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS),
+                    help="BASELINE workload: 2 (Qwen3-1.7B full FT), 3 (Qwen3-8B LoRA agentic), 5 (hybrid)")
+    ap.add_argument("--model", default=None)
+    ap.add_argument("--groups-per-rank", type=int, default=None)
+    ap.add_argument("--group-size", type=int, default=None)
+    ap.add_argument("--prompt-len", type=int, default=None)
+    ap.add_argument("--min-len", type=int, default=None)
+    ap.add_argument("--max-len", type=int, default=None)
+    ap.add_argument("--reward-p", type=float, default=None)
     ap.add_argument("--mean-arrival-s", type=float, default=2.0)
     ap.add_argument("--block-tokens", type=int, default=4096)
     ap.add_argument("--lr", type=float, default=1e-5)
@@ -319,6 +530,10 @@ def main() -> None:
                     help="after the timed region, run one more step under cProfile and write the host-side "
                          "function table (by own time) to this file (rank 0; not part of any reported number)")
     args = ap.parse_args()
+    for key, value in CONFIGS[args.config].items():  # the config's shape unless a flag overrides it
+        if key in ("model", "groups_per_rank", "group_size", "prompt_len", "min_len", "max_len", "reward_p") \
+                and getattr(args, key) is None:
+            setattr(args, key, value)
     if args.warmup < 3:
         raise SystemExit("at least 3 warm-up steps are required")
 
@@ -334,16 +549,43 @@ def main() -> None:
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=900))
 
+    c = CONFIGS[args.config]
+    if c["lora"]:
+        model_desc = (f"{args.model} architecture, random init N(0,0.02), frozen bf16 base, LoRA r{c['lora']} "
+                      f"alpha {c['lora_alpha']} on q/k/v/o/gate/up/down (fp32 adapters, fp32 Adam)")
+        seq = (f"prompt {args.prompt_len} + {c['turns'][0]}-{c['turns'][1]} turns of U{list(c['scored'])} scored "
+               f"+ U{list(c['unscored'])} unscored tokens, context cap {c['context_cap']}")
+    else:
+        model_desc = f"{args.model} architecture, random init N(0,0.02), bf16 weights, fp32 master/Adam"
+        seq = f"prompt {args.prompt_len} + completion U[{args.min_len},{args.max_len}]"
+    if args.config == 4:
+        model_desc = f"{args.model} architecture (OPD student), random init N(0,0.02), bf16 weights, fp32 master/Adam"
+        seq = (f"prompt {args.prompt_len} + {c['actions'][0]}-{c['actions'][1]} actions of U{list(c['action_tokens'])} "
+               f"scored tokens after U{list(c['observation_tokens'])} unscored observation tokens")
+    rewards = ("U[0,1]" if c["rewards"] == "uniform" else
+               "teacher log-probs -Exp(mean 1.5) clipped to [-20,0], per action after Exp(mean 0.5 s)"
+               if c["rewards"] == "teacher" else f"Bernoulli({args.reward_p})")
     cfg_block = {
-        "model": f"{args.model} architecture, random init N(0,0.02), bf16 weights, fp32 master/Adam",
-        "global_batch": f"{args.groups_per_rank * world} groups x {args.group_size} trajectories",
-        "seq_len": f"prompt {args.prompt_len} + completion U[{args.min_len},{args.max_len}]",
+        "baseline_config": args.config,
+        "model": model_desc,
+        "global_batch": (f"{args.groups_per_rank * world} trajectories" if args.config == 4 else
+                         f"{args.groups_per_rank * world} groups x {args.group_size} trajectories"),
+        "seq_len": seq,
         "parallelism": f"dp{world}",
-        "rewards": f"Bernoulli({args.reward_p}), arrival order Exp(mean {args.mean_arrival_s}s)",
+        "rewards": rewards if args.config == 4 else f"{rewards}, arrival order Exp(mean {args.mean_arrival_s}s)",
         "l2": "no flush needed: every step streams > 3 GB of weights and GBs of statistics (L2 126 MB)",
     }
     try:
-        if args.impl == "ours":
+        if args.config == 4:
+            if args.impl == "reference":
+                ref = os.path.join(ROOT, "baseline", "_ref")
+                if not os.path.isdir(os.path.join(ref, "thundersync")):
+                    raise RuntimeError("reference not installed under baseline/_ref")
+                sys.path.insert(0, ref)
+                model, trainer = build_reference_opd(args, device, world)
+            else:
+                model, trainer = build_ours_opd(args, device, world)
+        elif args.impl == "ours":
             model, trainer = build_ours(args, device)
         else:
             model, trainer = build_reference(args, device)
@@ -355,7 +597,8 @@ def main() -> None:
         raise
 
     extra = (1 if args.profile_out else 0) + (1 if args.cprofile_out else 0)
-    works = [make_step(rank, s, args) for s in range(args.warmup + args.steps + extra)]
+    mk = make_step_opd if args.config == 4 else make_step
+    works = [mk(rank, s, args) for s in range(args.warmup + args.steps + extra)]
     from thundersync_b200.ops import _ext
 
     for s in range(args.warmup):
@@ -445,7 +688,14 @@ def main() -> None:
         if args.impl == "reference":
             out["impl"] = "reference"
             out["gpu_launches"] = 0
-            out["config"]["reference_build"] = {
+            if args.config == 4:
+                out["config"]["reference_build"] = {
+                    "builder": "thundersync.engine.streaming.StreamingRun(stream_turns=True, turn_boundary_rebuild="
+                               "True) + thundersync.opd.objectives.OPDTurnStream, torch AdamW",
+                    **reference_diagnostics(),
+                }
+            else:
+                out["config"]["reference_build"] = {
                 "builder": "thundersync.grpo.runtime.load_trainer(GrpoTrainerConfig.from_namespace(...))",
                 "source_attention_backend": args.ref_attention,
                 "compile_pointwise_modules": bool(args.ref_compile),
@@ -454,12 +704,16 @@ def main() -> None:
                 "checkpoint": True,
                 "statistics": "device_resident sources, statistic_device auto",
                 **reference_diagnostics(),
-            }
+                }
+        elif args.config == 4:
+            out["config"]["build"] = {"objective": "OPDTurnStream into an fp32 flat gradient",
+                                      "optimizer": "fused flat AdamW", "turn_replay": "deferred at close"}
         else:
             out["config"]["build"] = {
                 "checkpoint": False,
                 "statistics": "device-resident fp32 group statistics",
-                "optimizer": "fused flat AdamW" + (" (ZeRO-1 sharded)" if getattr(trainer, "sharded", False) else ""),
+                "optimizer": "fused flat AdamW" + (" (ZeRO-1 sharded)" if getattr(trainer, "_sharded_flat", False)
+                                                   else ""),
             }
         print(json.dumps(out))
     if args.profile_out:
@@ -473,7 +727,6 @@ def main() -> None:
             with open(args.profile_out, "w") as fh:
                 fh.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=45,
                                                    max_name_column_width=100))
-            prof.export_chrome_trace(args.profile_out + ".trace.json")
     if args.cprofile_out:
         import cProfile
         import io
