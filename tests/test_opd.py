@@ -149,8 +149,34 @@ def test_turn_packs_and_closure_cohorts_match_single_turns():
             obj.close_group(g)
         obj.assert_safe_to_step()
         res.append({n: p.grad.clone() for n, p in m.named_parameters()})
+        if packed:  # the cohort's ready turns replayed as joint packs of two
+            assert "2" in run.turn_path_counts["replay"], run.turn_path_counts
     for n in res[0]:
         torch.testing.assert_close(res[0][n], res[1][n], rtol=1e-5, atol=5e-6, msg=n)
+
+
+def test_joint_turn_pack_rule():
+    """joint_turn_pack_ready / joint_turn_replay_ready and the pack width (reference semantics: every turn
+    without the checkpoint flag, none without a reserve, none when adjoints need a per-source order)."""
+    model = build_model(9).eval()
+    items = [(0, 0, [1, 2], [True, True]), (0, 1, [3], [True]), (0, 2, [4, 5, 6], [True, False, True])]
+    run = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True)
+    assert run.joint_turn_pack_ready and run.joint_turn_replay_ready
+    assert run.joint_turn_pack_width(items) == 3
+    assert run.joint_turn_pack_width(items[:1]) == 1
+    assert run._turn_replay_pack([(2, 5), (1, 7)]) == [0, 1]
+    ck = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True, checkpoint=True)
+    assert ck.joint_turn_pack_width(items) == 1 and ck._turn_replay_pack([(2, 5), (1, 7)]) == [0]
+    ck_reserve = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True,
+                              checkpoint=True, rebuild_plain_reserve_bytes=0)
+    assert ck_reserve.joint_turn_pack_width(items) == 3  # no device memory to read on the CPU: everything fits
+    for kw in ({"parameter_adjoint_reduction": "canonical_source"}, {"shared_prefix_vjp_mode": "source_ready_serial"},
+               {"explicit_adjoint_vjp": True}):
+        other = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True, **kw)
+        assert not other.joint_turn_pack_ready and other.joint_turn_pack_width(items) == 1
+    plain = StreamingRun(model, boundary_cut=True)
+    assert not plain.joint_turn_pack_ready and not plain.joint_turn_replay_ready
+    assert run.shared_prefix_finalization_diagnostics() == run.shared_prefix_vjp_diagnostics()
 
 
 def test_turn_stream_refuses_duplicates_and_late_turns():

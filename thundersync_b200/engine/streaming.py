@@ -232,6 +232,8 @@ class StreamingRun:
         self.boundary_adjoint_backend = boundary_adjoint_backend
         self.boundary_adjoint_max_degree = boundary_adjoint_max_degree
         self.parameter_adjoint_reduction = parameter_adjoint_reduction
+        self.shared_prefix_vjp_mode = shared_prefix_vjp_mode
+        self.explicit_adjoint_vjp = bool(explicit_adjoint_vjp)
         self.shared_prefix_vjp_backend = shared_prefix_vjp_backend
         self.shared_prefix_vjp_timing = bool(shared_prefix_vjp_timing)
         self._shared_prefix_times: list[float] = []
@@ -603,15 +605,99 @@ class StreamingRun:
                 t.n_tokens += len(tokens)
             return
         self._check_versions()
-        # a trajectory appearing twice in one call forwards in rounds
+        # a trajectory appearing twice in one call forwards in rounds; with a turn memory rule a round runs
+        # as the widest leading packs the device admits (joint_turn_pack_width)
         while pending:
             seen: set[int] = set()
             this, rest = [], []
             for item in pending:
                 (rest if item[0].tid in seen else this).append(item)
                 seen.add(item[0].tid)
-            self._forward_turns(this)
+            while this:
+                width = self.joint_turn_pack_width(
+                    [(t.gid, t.tid, tokens, scored) for t, tokens, scored in this]) if len(this) > 1 else 1
+                if width == 1 and len(this) > 1 and not self.joint_turn_pack_ready:
+                    width = len(this)  # without turn-boundary replay a round is one pack, as before
+                self._forward_turns(this[:width])
+                this = this[width:]
             pending = rest
+
+    # ------------------------------------------------------------ joint turn packs
+    def _joint_conditions(self) -> bool:
+        # a joint pack's one backward belongs to several trajectories: the parameter adjoints must
+        # accumulate in arrival order (no per-source reduction, no per-source serial drain, no explicit
+        # per-source VJP), the turns' outgoing state must be cut for replay, and every layer must be an
+        # attention layer (a linear-attention state carries no per-segment boundary here)
+        return (self.stream_turns and self.turn_boundary_rebuild and self.chunked_sdpa
+                and all(k == "full_attention" for k in self.spec.kinds)
+                and self.parameter_adjoint_reduction != "canonical_source"
+                and self.shared_prefix_vjp_mode != "source_ready_serial"
+                and not self.explicit_adjoint_vjp)
+
+    @property
+    def joint_turn_pack_ready(self) -> bool:
+        """Whether several ready turns may forward as one plain, jointly backwarded pack (reference:
+        src/thundersync/engine/streaming.py:3898-3919)."""
+        return self._joint_conditions()
+
+    @property
+    def joint_turn_replay_ready(self) -> bool:
+        """Whether the turn replays of several closed trajectories may run as one joint pack (same
+        conditions as :attr:`joint_turn_pack_ready`)."""
+        return self._joint_conditions()
+
+    def _turn_pack_estimate(self, tokens: int, past_tokens: int) -> int:
+        """Peak bytes a plain pack of ``tokens`` new tokens over ``past_tokens`` ancestor rows keeps."""
+        shape = self._turn_memory_shape()
+        return tokens * (shape["plain_activation"] + shape["kv"] + 2 * shape["hidden"]) + past_tokens * shape["kv"]
+
+    def _pack_fits(self, needs: list[tuple[int, int]], avail: int | None) -> bool:
+        if avail is None:
+            return True
+        tokens = sum(n for n, _ in needs)
+        past = sum(p for _, p in needs)
+        return self._turn_pack_estimate(tokens, past) + (self.rebuild_plain_reserve_bytes or 0) <= avail
+
+    def joint_turn_pack_width(self, items: list[tuple[int, int, list[int], list[bool]]]) -> int:
+        """How many leading turns of ``items`` one plain joint pack carries (reference:
+        src/thundersync/engine/streaming.py:3921-3955): every turn without the checkpoint flag (full
+        activations are retained by construction); with it, the widest prefix whose estimated peak plus
+        ``rebuild_plain_reserve_bytes`` fits the memory available now (read once), else 1."""
+        if len(items) < 2 or not self.joint_turn_pack_ready:
+            return 1
+        if not self.checkpoint:
+            return len(items)
+        if self.rebuild_plain_reserve_bytes is None:
+            return 1
+        avail = self._available_bytes() if self.device.type == "cuda" else None
+        needs = []
+        for gid, tid, tokens, _ in items:
+            t = self._trajs.get(tid)  # n_tokens: the turn's first position (prompt included)
+            past = t.n_tokens if t is not None else (self._groups[gid].prompt_len if gid in self._groups else 0)
+            needs.append((len(tokens), past))
+        for width in range(len(items), 1, -1):
+            if self._pack_fits(needs[:width], avail):
+                if width < len(items):
+                    self._memory_refusals["pack_narrowed"] = self._memory_refusals.get("pack_narrowed", 0) + 1
+                return width
+        self._memory_refusals["pack_refused"] = self._memory_refusals.get("pack_refused", 0) + 1
+        return 1
+
+    def _turn_replay_pack(self, needs: list[tuple[int, int]]) -> list[int]:
+        """Which of the ready replays (one per cohort member, in order) one model call carries: each joins
+        while the pack's estimate plus the reserve fits; fewer than two admitted is no pack ([0])."""
+        if len(needs) < 2 or not self.joint_turn_replay_ready:
+            return [0]
+        if not self.checkpoint:
+            return list(range(len(needs)))
+        if self.rebuild_plain_reserve_bytes is None:
+            return [0]
+        avail = self._available_bytes() if self.device.type == "cuda" else None
+        chosen: list[int] = []
+        for i, need in enumerate(needs):
+            if self._pack_fits([needs[j] for j in chosen] + [need], avail):
+                chosen.append(i)
+        return chosen if len(chosen) >= 2 else [0]
 
     def trajectory_tokens(self, traj_id: int) -> int:
         """Tokens of a trajectory's own branch (its turns, not the shared prompt)."""
@@ -903,29 +989,48 @@ class StreamingRun:
         g.real_graph = []
 
     def finalize_trajectories_turn_boundaries(self, traj_ids: list[int], *, sink: GradSink | None = None) -> None:
-        """Replay each trajectory's cut turns in reverse, carrying later turns' adjoints back."""
-        for tid in traj_ids:
-            t = self._trajs.get(tid)
-            if t is None:
-                continue
-            while t.cuts:
-                cut = t.cuts.pop()
-                if not cut.boundary.has_adjoint():
-                    cut.boundary.release()
-                    continue
-                self._check_versions()
-                h, states = self._run_pack(
-                    self._ids(cut.tokens), self._positions(cut.pos0, len(cut.tokens)),
-                    [Segment(0, len(cut.tokens), cut.parent_chain)],
-                )
-                real = _flatten_state(states[0], self.spec.kinds) + [h[-1]]
-                adj = cut.boundary.peek()
-                pairs = [(r, a.to(r.dtype)) for r, a in zip(real, adj) if a is not None]
-                self._counts["turn_replay"] += 1
-                if pairs:
-                    with self.capture_source(("turn_replay", tid)), grad_sink(sink):
-                        torch.autograd.backward([r for r, _ in pairs], [a for _, a in pairs])
-                cut.boundary.release()
+        """Replay a closure cohort's cut turns last to first, carrying later turns' adjoints back (reference
+        behaviour: src/thundersync/engine/streaming.py:6241-6330). Each round takes the latest unreplayed
+        turn of every member; those the turn memory rule admits together (:meth:`_turn_replay_pack`) run
+        as one joint pack with one backward, the rest wait for a later round."""
+        members = [self._trajs[t] for t in traj_ids if t in self._trajs]
+        while True:
+            ready = []
+            for t in members:
+                while t.cuts and not t.cuts[-1].boundary.has_adjoint():
+                    t.cuts.pop().boundary.release()
+                if t.cuts:
+                    ready.append(t)
+            if not ready:
+                return
+            pick = self._turn_replay_pack([(len(t.cuts[-1].tokens), t.cuts[-1].pos0) for t in ready])
+            batch = [ready[i] for i in pick]
+            cuts = [t.cuts.pop() for t in batch]
+            self._check_versions()
+            ids: list[int] = []
+            pos, segs, cur = [], [], 0
+            for c in cuts:
+                ids.extend(c.tokens)
+                pos.append(self._positions(c.pos0, len(c.tokens)))
+                segs.append(Segment(cur, len(c.tokens), c.parent_chain))
+                cur += len(c.tokens)
+            h, states = self._run_pack(self._ids(ids), torch.cat(pos), segs)
+            reals, adjs = [], []
+            for c, seg, st in zip(cuts, segs, states):
+                real = _flatten_state(st, self.spec.kinds) + [h[seg.start + seg.length - 1]]
+                for r, a in zip(real, c.boundary.peek()):
+                    if a is not None:
+                        reals.append(r)
+                        adjs.append(a.to(r.dtype))
+            self._counts["turn_replay"] += len(cuts)
+            key = str(len(cuts))
+            self._turn_counts["replay"][key] = self._turn_counts["replay"].get(key, 0) + 1
+            if reals:
+                src = ("turn_replay", batch[0].tid if len(batch) == 1 else tuple(t.tid for t in batch))
+                with self.capture_source(src), grad_sink(sink):
+                    torch.autograd.backward(reals, adjs)
+            for c in cuts:
+                c.boundary.release()
 
     def finalize_shared_prefixes(self, *, sink: GradSink | None = None) -> int:
         """Backward every shared prompt node once, children before parents."""
@@ -1101,6 +1206,11 @@ class StreamingRun:
             out["vjp_seconds"] = list(self._shared_prefix_times)
             out["vjp_seconds_total"] = float(sum(self._shared_prefix_times))
         return out
+
+    def shared_prefix_finalization_diagnostics(self) -> dict[str, Any]:
+        """The shared-prefix VJP state under the reference's older name (same record as
+        :meth:`shared_prefix_vjp_diagnostics`)."""
+        return self.shared_prefix_vjp_diagnostics()
 
     def close_memory_window(self) -> None:
         """Record the open window's measured peak above its start (allocator counters, no device sync)."""
