@@ -14,7 +14,12 @@ the maximum over ranks:
 * ``nccl all-reduce``: ``dist.all_reduce`` (SUM) plus the scale, on a plain
   fp32 tensor;
 * ``native reduce-scatter``: the same kernel writing only this rank's shard
-  (the sharded optimizer's first half).
+  (the sharded optimizer's first half);
+* ``native one-shot all-reduce``: every rank reads every rank's whole buffer
+  and writes the mean locally (one phase; compare with the two-shot to place
+  the crossover ``ONESHOT_MAX_ELEMS``).
+
+Sizes are in KiB (``--sizes-kib``) so the latency-bound range is covered.
 
 Each line reports milliseconds, bus bandwidth and the fraction of the NVLink
 roofline (bus bandwidth ÷ the per-direction link bandwidth). For the two-shot
@@ -60,7 +65,7 @@ def _time(fn, iters: int, device) -> float:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--sizes-mib", default="16,64,256,1024,4096")
+    ap.add_argument("--sizes-kib", default="16,64,256,1024,4096,16384,65536,262144,1048576,4194304")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--link-gbs", type=float, default=770.0, help="measured peer-copy GB/s per direction")
     args = ap.parse_args(argv)
@@ -71,13 +76,16 @@ def main(argv=None) -> None:
     world, rank = dist.get_world_size(), dist.get_rank()
     ws = SymmetricWorkspace(device)
     rows = []
-    for mib in (int(x) for x in args.sizes_mib.split(",")):
-        n = (mib << 20) // 4
+    for kib in (int(x) for x in args.sizes_kib.split(",")):
+        n = (kib << 10) // 4
         buf, ptrs = ws.alloc(n, torch.float32)
         buf.normal_()
         plain = torch.randn(n, device=device)
+        out = torch.empty(n, device=device)
         nbytes = n * 4
         t_native = _time(lambda: ws.all_reduce_mean(buf, ptrs), args.iters, device)
+        ws.check()
+        t_one = _time(lambda: ws.all_reduce_mean_oneshot(buf, ptrs, out), args.iters, device)
         ws.check()
 
         def nccl():
@@ -88,14 +96,16 @@ def main(argv=None) -> None:
         t_rs = _time(lambda: ws.reduce_scatter(buf, ptrs), args.iters, device)
         ws.check()
         frac = (world - 1) / world
-        for name, t in (("native all-reduce", t_native), ("nccl all-reduce", t_nccl),
-                        ("native reduce-scatter", t_rs)):
+        for name, t in (("native all-reduce", t_native), ("native one-shot all-reduce", t_one),
+                        ("nccl all-reduce", t_nccl), ("native reduce-scatter", t_rs)):
+            # bus bandwidth in the usual all-reduce convention (2(n-1)/n of the buffer per rank), so the
+            # one-shot and two-shot lines compare directly; the reduce-scatter moves (n-1)/n
             link_bytes = (2 if "all-reduce" in name else 1) * frac * nbytes
             bus = link_bytes / (t / 1e3) / 1e9
             roof = bus / args.link_gbs
-            rows.append({"op": name, "mib": mib, "ms": round(t, 4), "bus_gbs": round(bus, 1),
+            rows.append({"op": name, "kib": kib, "ms": round(t, 4), "bus_gbs": round(bus, 1),
                          "nvlink_roofline_fraction": round(roof, 3), "world": world})
-        del buf, plain
+        del buf, plain, out
     if rank == 0:
         for r in rows:
             print(json.dumps(r))

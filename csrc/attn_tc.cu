@@ -52,6 +52,151 @@ TS_DEVICE bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, in
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+// ------------------------------------------------------------------ packed (variable-length) work tables
+// A pack holds several segments; queries of segment s are rows [q0_s, q0_s + T_s) of Q, and its keys are
+// rows of one key buffer: zero or more *far* ranges (ancestors every query of s sees) and one *near* range
+// whose key b is visible to local query i iff b <= i + off (bottom-right causal; off = length of an
+// ancestor prefix stored right before the own keys, 0 when the own keys stand alone).
+//
+// Query-side item (forward and dQ; one per segment and BM-query tile), 8 ints:
+//   q_row0 (Q row of the tile's first query), q_loc0 (its index within the segment), T, near_row0, off,
+//   far0, nfar (slice of the far-range table, int2 {row0, len}), unused.
+// Key-side item (dK/dV; one per key tile), 4 ints: k_row0, cnt (keys in the tile), cons0, ncons (slice of
+// the consumer table). Consumer (4 ints): q_row0 and T of a segment whose queries read this tile, and
+// vis_base: key row r of the tile is visible to that segment's local query i iff i >= vis_base + r
+// (kFullVis: every query sees every key). A key tile lies inside one range with one consumer set, so a
+// shared ancestor's dK/dV sum over every segment that reads it inside one CTA, without atomics.
+// A launch without tables is the single-segment case: item = BM-tile of [0, T), near range = [0, S) with
+// off = S - T, one consumer per key tile.
+struct QItem {
+  int q_row0, q_loc0, T, near_row0, off, far0, nfar, pad;
+};
+struct KItem {
+  int k_row0, cnt, cons0, ncons;
+};
+constexpr int kFullVis = -(1 << 30);
+
+TS_DEVICE QItem load_qitem(const int* tab, int idx) {
+  const int4* p = reinterpret_cast<const int4*>(tab) + 2 * idx;
+  const int4 a = p[0], b = p[1];
+  return QItem{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+}
+TS_DEVICE QItem dense_qitem(int BM, int T, int S) {
+  const int n_qt = (T + BM - 1) / BM;
+  const int qt = n_qt - 1 - (int)blockIdx.x;  // longest tiles first
+  return QItem{qt * BM, qt * BM, T, 0, S - T, 0, 0, 0};
+}
+
+// The key tiles a query item visits, in order: every far range in BN-key tiles, then the near range up to
+// the tile's last query. One walker per role; next() moves to the following tile.
+template <int BN>
+struct KeyWalk {
+  const int2* far;
+  int nfar, near_row0, off, T;
+  int f, jj, row0, len;
+
+  TS_DEVICE void init(const QItem& it, const int2* far_tab) {
+    far = far_tab + it.far0;
+    nfar = it.nfar;
+    near_row0 = it.near_row0;
+    off = it.off;
+    T = it.T;
+    f = 0;
+    jj = 0;
+    load();
+  }
+  TS_DEVICE void load() {
+    while (f < nfar) {
+      const int2 r = far[f];
+      if (r.y > 0) {
+        row0 = r.x;
+        len = r.y;
+        return;
+      }
+      ++f;
+    }
+    row0 = near_row0;
+    len = off + T;
+  }
+  TS_DEVICE void next() {
+    ++jj;
+    if (f < nfar && jj * BN >= len) {
+      ++f;
+      jj = 0;
+      load();
+    }
+  }
+  TS_DEVICE int row() const { return row0 + jj * BN; }
+  // keys of the current tile visible to local query qi (< T)
+  TS_DEVICE int nvis(int qi) const {
+    if (f < nfar) return min(BN, len - jj * BN);
+    const int v = min(qi + off, off + T - 1) - jj * BN + 1;
+    return v < 0 ? 0 : (v > BN ? BN : v);
+  }
+  // tiles for an item whose queries end at local index q_end (exclusive)
+  TS_DEVICE int count(int q_end) const {
+    int n = 0;
+    for (int i = 0; i < nfar; ++i) n += (far[i].y + BN - 1) / BN;
+    const int kv_end = min(off + T, off + q_end);
+    return n + (kv_end + BN - 1) / BN;
+  }
+};
+
+// Consumers of one key tile and the (head, consumer, query tile) steps a dK/dV CTA runs over them, heads
+// outermost. Without a consumer table the single consumer is the one given to init.
+template <int BQ>
+struct StepWalk {
+  const int4* cons;
+  int ncons, hh, c, t, qstart, nqt;
+  int4 cur;  // {q_row0, T, vis_base, 0} of the current consumer
+
+  TS_DEVICE int4 consumer(int i) const { return cons != nullptr ? cons[i] : cur; }
+  TS_DEVICE static int first_tile(int vis_base) {
+    const int s = vis_base < 0 ? 0 : vis_base;
+    return (s / BQ) * BQ;
+  }
+  TS_DEVICE static int tiles(const int4& cn) {
+    const int s = first_tile(cn.z);
+    return s < cn.y ? (cn.y - s + BQ - 1) / BQ : 0;
+  }
+  TS_DEVICE void init(const int4* cons_tab, int n, int4 dense_cons, int grp) {
+    cons = cons_tab;
+    ncons = n;
+    cur = dense_cons;
+    hh = 0;
+    c = -1;
+    t = 0;
+    nqt = 0;
+    advance_consumer(grp);
+  }
+  TS_DEVICE void advance_consumer(int grp) {
+    for (;;) {
+      ++c;
+      if (c >= ncons) {
+        c = 0;
+        ++hh;
+        if (hh >= grp || ncons == 0) return;
+      }
+      cur = consumer(c);
+      nqt = tiles(cur);
+      qstart = first_tile(cur.z);
+      t = 0;
+      if (nqt > 0) return;
+    }
+  }
+  TS_DEVICE int per_head() const {
+    int n = 0;
+    for (int i = 0; i < ncons; ++i) n += tiles(consumer(i));
+    return n;
+  }
+  TS_DEVICE void next(int grp) {
+    ++t;
+    if (t >= nqt) advance_consumer(grp);
+  }
+  TS_DEVICE int q_loc() const { return qstart + t * BQ; }  // local index of the step's first query
+  TS_DEVICE int q_row() const { return cur.x + q_loc(); }  // its row in Q / dO
+};
+
 template <int D>
 struct FwdLayout {
   // D = 256 halves the key tile so two K/V stages still fit in shared memory
@@ -84,7 +229,9 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
                                                              const __grid_constant__ CUtensorMap tm_k,
                                                              const __grid_constant__ CUtensorMap tm_v,
                                                              bf16* __restrict__ out, float* __restrict__ lse,
-                                                             int T, int S, int Hq, int Hkv, float sl2,
+                                                             int T_in, int S_in, int Hq, int Hkv, float sl2,
+                                                             const int* __restrict__ qtab,
+                                                             const int2* __restrict__ far_tab, int Ttot,
                                                              int* __restrict__ err) {
   using L = FwdLayout<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -92,13 +239,13 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
   FwdBars* bars = reinterpret_cast<FwdBars*>(smem + L::BAR);
   const uint32_t sbase = tc::smem_addr(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_qt = (T + L::BM - 1) / L::BM;
-  const int qt = n_qt - 1 - (int)blockIdx.x;  // longest tiles first
+  const QItem it = qtab != nullptr ? load_qitem(qtab, blockIdx.x) : dense_qitem(L::BM, T_in, S_in);
+  const int T = it.T;
   const int h = blockIdx.y, hk = h / (Hq / Hkv);
-  const int q0 = qt * L::BM;
-  const int off = S - T;
-  const int kv_end = min(S, q0 + L::BM + off);
-  const int n = (kv_end + L::BN - 1) / L::BN;
+  const int q0 = it.q_loc0;  // local index of the tile's first query
+  KeyWalk<L::BN> walk;
+  walk.init(it, far_tab);
+  const int n = walk.count(q0 + L::BM);
   volatile int* abort = &bars->abort;
 
   if (threadIdx.x == 0) {
@@ -127,17 +274,18 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       tc::prefetch_tmap(&tm_v);
       tc::mbar_expect_tx(&bars->q, L::Q_BYTES);
       for (int b = 0; b < L::NB; ++b)
-        tc::tma_load_2d(smem + L::Q + b * L::BM * 128, &tm_q, h * D + b * 64, q0, &bars->q);
-      for (int j = 0; j < n; ++j) {
+        tc::tma_load_2d(smem + L::Q + b * L::BM * 128, &tm_q, h * D + b * 64, it.q_row0, &bars->q);
+      for (int j = 0; j < n; ++j, walk.next()) {
         const int s = j & 1;
         if (j >= 2 && !tc::mbar_wait(&bars->kv_empty[s], ((j - 2) >> 1) & 1, abort, err, 11)) break;
+        const int krow = walk.row();
         tc::mbar_expect_tx(&bars->k_full[s], L::K_BYTES);
         for (int b = 0; b < L::NB; ++b)
-          tc::tma_load_2d(smem + L::K0 + s * L::K_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN,
+          tc::tma_load_2d(smem + L::K0 + s * L::K_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, krow,
                           &bars->k_full[s]);
         tc::mbar_expect_tx(&bars->v_full[s], L::K_BYTES);
         for (int b = 0; b < L::NB; ++b)
-          tc::tma_load_2d(smem + L::V0 + s * L::K_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
+          tc::tma_load_2d(smem + L::V0 + s * L::K_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, krow,
                           &bars->v_full[s]);
       }
     }
@@ -190,13 +338,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
     // only its 64-column half (hc) and rescales half of the O row.
     const int r = (warp & 3) * 32 + lane;
     const int hc = warp >> 2;
-    const int qi = q0 + r;
-    const int lim = qi + off;   // keys <= lim are visible
+    const int qi = q0 + r;  // local query index (rows at or past T belong to the next segment: not stored)
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     float* lsum = reinterpret_cast<float*>(smem + L::RED);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n && ok; ++j) {
+    for (int j = 0; j < n && ok; ++j, walk.next()) {
       const int s = j & 1;
       if (!warp_wait(&bars->s_full[s], (j >> 1) & 1, abort, err, 31)) { ok = false; break; }
       tc::tc_fence_after();
@@ -205,9 +352,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
 #pragma unroll
       for (int c = 0; c < L::BN / 32; ++c) tc::tmem_ld32(lane_base + scol + c * 32, sv + c * 32);
       tc::tmem_ld_wait();
-      const int k0 = j * L::BN;
-      int nvis = min(lim, S - 1) - k0 + 1;  // visible columns of this tile for this row
-      nvis = nvis < 0 ? 0 : (nvis > L::BN ? L::BN : nvis);
+      const int nvis = walk.nvis(qi);  // visible columns of this tile for this row
       // row max over the tile as 8 independent chains (a single fmaxf chain of BN links serialises on
       // the instruction latency; the chains are combined at the end)
       float mx8[8];
@@ -288,7 +433,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         tc::tmem_ld32(lane_base + L::O_COL + c * 32, o);
         tc::tmem_ld_wait();
         if (qi < T) {
-          bf16* dst = out + ((long long)qi * Hq + h) * D + c * 32;
+          bf16* dst = out + ((long long)(it.q_row0 + r) * Hq + h) * D + c * 32;
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 v;
@@ -300,7 +445,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
           }
         }
       }
-      if (qi < T && hc == 0) lse[(long long)h * T + qi] = (m + log2f(lt)) * kLn2;
+      if (qi < T && hc == 0) lse[(long long)h * Ttot + it.q_row0 + r] = (m + log2f(lt)) * kLn2;
     }
   }
   tc::tc_fence_before();
@@ -379,15 +524,17 @@ struct DkvTBars {
   uint64_t s_read[4], dp_read[4];  // per TMEM sub-partition: warp (w & 3) has loaded its S^T / dP^T columns
   uint32_t tmem_slot;
   int abort;
+  int4 info[4];  // per Q stage: {local index of the first query, T, vis_base, 0} of the step it holds
 };
+static_assert(sizeof(DkvTBars) <= 512, "dK/dV barrier block");
 
 template <int D>
 __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
     const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dk, bf16* __restrict__ dv,
-    float* __restrict__ part_k, float* __restrict__ part_v, int T, int S, int Hq, int Hkv, float scale,
-    int* __restrict__ err) {
+    float* __restrict__ part_k, float* __restrict__ part_v, int T_in, int S_in, int Hq, int Hkv, float scale,
+    const int* __restrict__ ktab, const int4* __restrict__ cons_tab, int Ttot, int Stot, int* __restrict__ err) {
   using L = DkvTLayout<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -396,14 +543,14 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.y, nsplit = gridDim.z, grp = Hq / Hkv / nsplit;
   const int hbase = hk * (Hq / Hkv) + blockIdx.z * grp;
-  const int k0 = blockIdx.x * L::BN;
-  const int off = S - T;
+  const KItem ki = ktab != nullptr ? reinterpret_cast<const KItem*>(ktab)[blockIdx.x]
+                                    : KItem{(int)blockIdx.x * L::BN, min(L::BN, S_in - (int)blockIdx.x * L::BN), 0, 1};
+  const int k0 = ki.k_row0;  // key row of the tile's first key
   const float sl2 = scale * kLog2e;
-  int qstart = k0 - off;
-  if (qstart < 0) qstart = 0;
-  qstart = (qstart / L::BQ) * L::BQ;
-  const int n_qt = qstart < T ? (T - qstart + L::BQ - 1) / L::BQ : 0;
-  const int total = n_qt * grp;
+  StepWalk<L::BQ> steps;
+  steps.init(ktab != nullptr ? cons_tab + ki.cons0 : nullptr, ki.ncons, make_int4(0, T_in, k0 - (S_in - T_in), 0),
+             grp);
+  const int total = steps.per_head() * grp;
   volatile int* abort = &bars->abort;
   float* ld = reinterpret_cast<float*>(smem + L::LD0);
 
@@ -442,28 +589,31 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
     }
     constexpr int PER = L::BQ / 32;
     float nl[PER], nd[PER];
-    auto fetch = [&](int i) {
-      const int hh = hbase + i / n_qt;
-      const int qt = qstart + (i % n_qt) * L::BQ;
+    StepWalk<L::BQ> ahead = steps;  // one step ahead of `steps`: the lse / delta prefetch
+    auto fetch = [&]() {
+      const int hh = hbase + ahead.hh;
+      const int qt = ahead.q_loc();
 #pragma unroll
       for (int x = 0; x < PER; ++x) {
         const int qi = qt + x * 32 + lane;
-        nl[x] = qi < T ? lse[(long long)hh * T + qi] : 0.f;
-        nd[x] = qi < T ? delta[(long long)hh * T + qi] : 0.f;
+        const long long at = (long long)hh * Ttot + ahead.cur.x + qi;
+        nl[x] = qi < ahead.cur.y ? lse[at] : 0.f;
+        nd[x] = qi < ahead.cur.y ? delta[at] : 0.f;
       }
+      ahead.next(grp);
     };
-    if (total > 0) fetch(0);
-    for (int i = 0; i < total; ++i) {
+    if (total > 0) fetch();
+    for (int i = 0; i < total; ++i, steps.next(grp)) {
       const int qs = i % L::NQ;
       if (i >= L::NQ && !warp_wait(&bars->q_empty[qs], ((i - L::NQ) / L::NQ) & 1, abort, err, 151)) break;
-      const int hh = hbase + i / n_qt;
-      const int qt = qstart + (i % n_qt) * L::BQ;
+      const int hh = hbase + steps.hh;
+      const int qrow = steps.q_row();
       if (lane == 0) {
         tc::mbar_expect_tx(&bars->q_full[qs], 2 * L::QT_BYTES);
         for (int b = 0; b < L::NB; ++b) {
-          tc::tma_load_2d(smem + L::Q0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_q, hh * D + b * 64, qt,
+          tc::tma_load_2d(smem + L::Q0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_q, hh * D + b * 64, qrow,
                           &bars->q_full[qs]);
-          tc::tma_load_2d(smem + L::O0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qt,
+          tc::tma_load_2d(smem + L::O0 + qs * L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qrow,
                           &bars->q_full[qs]);
         }
       }
@@ -472,9 +622,10 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
         ld[(qs * 2 + 0) * L::BQ + x * 32 + lane] = nl[x] * kLog2e;
         ld[(qs * 2 + 1) * L::BQ + x * 32 + lane] = nd[x];
       }
+      if (lane == 0) bars->info[qs] = make_int4(steps.q_loc(), steps.cur.y, steps.cur.z, 0);
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->q_full[qs]);
-      if (i + 1 < total) fetch(i + 1);
+      if (i + 1 < total) fetch();
     }
   } else if (warp == 9) {
     if (lane == 0) {
@@ -542,13 +693,13 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
     bool ok = true;
     for (int i = 0; i < total && ok; ++i) {
       const int qs = i % L::NQ;
-      const int qt = qstart + (i % n_qt) * L::BQ;
-      const int qc0 = qt + hc * 64;
-      const int lo = kr < S ? kr - off - qc0 : 64;  // query qc0+c sees key kr iff c >= lo
-      const int hi = T - qc0;                       // and c < hi (query exists)
       const float* l2p = ld + (qs * 2 + 0) * L::BQ + hc * 64;
       const float* dlp = ld + (qs * 2 + 1) * L::BQ + hc * 64;
       if (!warp_wait(&bars->q_full[qs], (i / L::NQ) & 1, abort, err, 171)) { ok = false; break; }
+      const int4 inf = bars->info[qs];  // written by the producer before it released the stage
+      const int qc0 = inf.x + hc * 64;
+      const int lo = r < ki.cnt ? inf.z + r - qc0 : 64;  // local query qc0+c sees key kr iff c >= lo
+      const int hi = inf.y - qc0;                        // and c < hi (query exists)
       if (!warp_wait(&bars->s_full, i & 1, abort, err, 172)) { ok = false; break; }
       tc::tc_fence_after();
       float p[64];
@@ -621,14 +772,14 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
         tc::tmem_ld32(lane_base + L::DK_COL + c * 32, a);
         tc::tmem_ld32(lane_base + L::DV_COL + c * 32, b);
         tc::tmem_ld_wait();
-        if (kr < S && nsplit > 1) {
-          const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D + c * 32;
+        if (r < ki.cnt && nsplit > 1) {
+          const long long o = (((long long)blockIdx.z * Stot + kr) * Hkv + hk) * D + c * 32;
 #pragma unroll
           for (int x = 0; x < 32; x += 4) {
             *reinterpret_cast<float4*>(part_k + o + x) = make_float4(a[x], a[x + 1], a[x + 2], a[x + 3]);
             *reinterpret_cast<float4*>(part_v + o + x) = make_float4(b[x], b[x + 1], b[x + 2], b[x + 3]);
           }
-        } else if (kr < S) {
+        } else if (r < ki.cnt) {
           bf16* pk = dk + ((long long)kr * Hkv + hk) * D + c * 32;
           bf16* pv = dv + ((long long)kr * Hkv + hk) * D + c * 32;
 #pragma unroll
@@ -643,13 +794,13 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
           }
         }
       }
-    } else if (ok && total == 0 && kr < S && nsplit > 1) {
-      const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D;
+    } else if (ok && total == 0 && r < ki.cnt && nsplit > 1) {
+      const long long o = (((long long)blockIdx.z * Stot + kr) * Hkv + hk) * D;
       for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 4) {
         *reinterpret_cast<float4*>(part_k + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
         *reinterpret_cast<float4*>(part_v + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    } else if (ok && total == 0 && kr < S) {
+    } else if (ok && total == 0 && r < ki.cnt) {
       for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 8) {
         *reinterpret_cast<uint4*>(dk + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(dv + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
@@ -705,7 +856,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
     const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ out,
-    float* __restrict__ part, int T, int S, int Hq, int Hkv, float scale, int* __restrict__ err) {
+    float* __restrict__ part, int T_in, int S_in, int Hq, int Hkv, float scale, const int* __restrict__ ktab,
+    const int4* __restrict__ cons_tab, int Ttot, int Stot, int* __restrict__ err) {
   using L = Dkv256Layout<MODE>;
   constexpr int D = L::D;
   extern __shared__ uint8_t smem_raw[];
@@ -715,14 +867,14 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.y, nsplit = gridDim.z, grp = Hq / Hkv / nsplit;
   const int hbase = hk * (Hq / Hkv) + blockIdx.z * grp;
-  const int k0 = blockIdx.x * L::BN;
-  const int off = S - T;
+  const KItem ki = ktab != nullptr ? reinterpret_cast<const KItem*>(ktab)[blockIdx.x]
+                                    : KItem{(int)blockIdx.x * L::BN, min(L::BN, S_in - (int)blockIdx.x * L::BN), 0, 1};
+  const int k0 = ki.k_row0;  // key row of the tile's first key
   const float sl2 = scale * kLog2e;
-  int qstart = k0 - off;
-  if (qstart < 0) qstart = 0;
-  qstart = (qstart / L::BQ) * L::BQ;
-  const int n_qt = qstart < T ? (T - qstart + L::BQ - 1) / L::BQ : 0;
-  const int total = n_qt * grp;
+  StepWalk<L::BQ> steps;
+  steps.init(ktab != nullptr ? cons_tab + ki.cons0 : nullptr, ki.ncons, make_int4(0, T_in, k0 - (S_in - T_in), 0),
+             grp);
+  const int total = steps.per_head() * grp;
   volatile int* abort = &bars->abort;
   float* ld = reinterpret_cast<float*>(smem + L::LD0);
 
@@ -762,29 +914,32 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
     }
     constexpr int PER = L::BQ / 32;
     float nl[PER], nd[PER];
-    auto fetch = [&](int i) {
-      const int hh = hbase + i / n_qt;
-      const int qt = qstart + (i % n_qt) * L::BQ;
+    StepWalk<L::BQ> ahead = steps;  // one step ahead of `steps`: the lse / delta prefetch
+    auto fetch = [&]() {
+      const int hh = hbase + ahead.hh;
+      const int qt = ahead.q_loc();
 #pragma unroll
       for (int x = 0; x < PER; ++x) {
         const int qi = qt + x * 32 + lane;
-        nl[x] = qi < T ? lse[(long long)hh * T + qi] : 0.f;
-        nd[x] = qi < T ? delta[(long long)hh * T + qi] : 0.f;
+        const long long at = (long long)hh * Ttot + ahead.cur.x + qi;
+        nl[x] = qi < ahead.cur.y ? lse[at] : 0.f;
+        nd[x] = qi < ahead.cur.y ? delta[at] : 0.f;
       }
+      ahead.next(grp);
     };
-    if (total > 0) fetch(0);
-    for (int i = 0; i < total; ++i) {
+    if (total > 0) fetch();
+    for (int i = 0; i < total; ++i, steps.next(grp)) {
       const int qs = i % L::NQ;
       if (i == L::NQ - 1 && !warp_wait(&bars->kv_tm, 0, abort, err, 241)) break;  // K has left this stage
       if (i >= L::NQ && !warp_wait(&bars->q_empty[qs], ((i - L::NQ) / L::NQ) & 1, abort, err, 242)) break;
-      const int hh = hbase + i / n_qt;
-      const int qt = qstart + (i % n_qt) * L::BQ;
+      const int hh = hbase + steps.hh;
+      const int qrow = steps.q_row();
       uint8_t* st = smem + L::ST0 + qs * L::ST_BYTES;
       if (lane == 0) {
         tc::mbar_expect_tx(&bars->q_full[qs], 2 * L::QT_BYTES);
         for (int b = 0; b < L::NB; ++b) {
-          tc::tma_load_2d(st + b * L::BQ * 128, &tm_q, hh * D + b * 64, qt, &bars->q_full[qs]);
-          tc::tma_load_2d(st + L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qt, &bars->q_full[qs]);
+          tc::tma_load_2d(st + b * L::BQ * 128, &tm_q, hh * D + b * 64, qrow, &bars->q_full[qs]);
+          tc::tma_load_2d(st + L::QT_BYTES + b * L::BQ * 128, &tm_do, hh * D + b * 64, qrow, &bars->q_full[qs]);
         }
       }
 #pragma unroll
@@ -794,7 +949,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->q_full[qs]);
-      if (i + 1 < total) fetch(i + 1);
+      if (i + 1 < total) fetch();
     }
   } else if (warp == 9) {
     if (lane == 0) {
@@ -905,13 +1060,12 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
     }
     tc::tc_fence_before();
     tc::mbar_arrive(&bars->kv_tm);
-    for (int i = 0; i < total && ok; ++i) {
+    for (int i = 0; i < total && ok; ++i, steps.next(grp)) {
       const int qs = i % L::NQ, b = MODE == 2 ? (i & 1) : 0;
       const uint32_t scol = L::S_COL + b * 64;
-      const int qt = qstart + (i % n_qt) * L::BQ;
-      const int qc0 = qt + hc * 32;
-      const int lo = kr < S ? kr - off - qc0 : 32;  // query qc0+c sees key kr iff c >= lo
-      const int hi = T - qc0;                       // and c < hi (query exists)
+      const int qc0 = steps.q_loc() + hc * 32;
+      const int lo = r < ki.cnt ? steps.cur.z + r - qc0 : 32;  // local query qc0+c sees key kr iff c >= lo
+      const int hi = steps.cur.y - qc0;                        // and c < hi (query exists)
       if (!warp_wait(&bars->q_full[qs], (i / L::NQ) & 1, abort, err, 262)) { ok = false; break; }
       if (!warp_wait(&bars->s_full[b], MODE == 2 ? (i >> 1) & 1 : i & 1, abort, err, 263)) { ok = false; break; }
       tc::tc_fence_after();
@@ -980,12 +1134,12 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
         float a[32];
         tc::tmem_ld32(lane_base + L::ACC_COL + c * 32, a);
         tc::tmem_ld_wait();
-        if (kr < S && nsplit > 1) {
-          const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D + c * 32;
+        if (r < ki.cnt && nsplit > 1) {
+          const long long o = (((long long)blockIdx.z * Stot + kr) * Hkv + hk) * D + c * 32;
 #pragma unroll
           for (int x = 0; x < 32; x += 4)
             *reinterpret_cast<float4*>(part + o + x) = make_float4(a[x], a[x + 1], a[x + 2], a[x + 3]);
-        } else if (kr < S) {
+        } else if (r < ki.cnt) {
           bf16* po = out + ((long long)kr * Hkv + hk) * D + c * 32;
 #pragma unroll
           for (int x = 0; x < 32; x += 8) {
@@ -996,11 +1150,11 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
           }
         }
       }
-    } else if (ok && total == 0 && kr < S && nsplit > 1) {
-      const long long o = (((long long)blockIdx.z * S + kr) * Hkv + hk) * D;
+    } else if (ok && total == 0 && r < ki.cnt && nsplit > 1) {
+      const long long o = (((long long)blockIdx.z * Stot + kr) * Hkv + hk) * D;
       for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 4)
         *reinterpret_cast<float4*>(part + o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-    } else if (ok && total == 0 && kr < S) {
+    } else if (ok && total == 0 && r < ki.cnt) {
       for (int c = hc * (D / 2); c < (hc + 1) * (D / 2); c += 8)
         *reinterpret_cast<uint4*>(out + ((long long)kr * Hkv + hk) * D + c) = make_uint4(0, 0, 0, 0);
     }
@@ -1047,21 +1201,22 @@ template <int D>
 __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T, int S, int Hq,
-    int Hkv, float scale, int* __restrict__ err) {
+    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T_in, int S_in,
+    int Hq, int Hkv, float scale, const int* __restrict__ qtab, const int2* __restrict__ far_tab, int Ttot,
+    int* __restrict__ err) {
   using L = DqTLayout<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   DqTBars* bars = reinterpret_cast<DqTBars*>(smem + L::BAR);
   const uint32_t sbase = tc::smem_addr(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_qt = (T + L::BM - 1) / L::BM;
-  const int qt = n_qt - 1 - (int)blockIdx.x;
+  const QItem it = qtab != nullptr ? load_qitem(qtab, blockIdx.x) : dense_qitem(L::BM, T_in, S_in);
+  const int T = it.T;
   const int h = blockIdx.y, hk = h / (Hq / Hkv);
-  const int q0 = qt * L::BM;
-  const int off = S - T;
-  const int kv_end = min(S, q0 + L::BM + off);
-  const int n = (kv_end + L::BN - 1) / L::BN;
+  const int q0 = it.q_loc0;
+  KeyWalk<L::BN> walk;
+  walk.init(it, far_tab);
+  const int n = walk.count(q0 + L::BM);
   const float sl2 = scale * kLog2e;
   volatile int* abort = &bars->abort;
 
@@ -1090,17 +1245,18 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
     if (lane == 0) {
       tc::mbar_expect_tx(&bars->q, 2 * L::Q_BYTES);
       for (int b = 0; b < L::NB; ++b) {
-        tc::tma_load_2d(smem + L::Q + b * L::BM * 128, &tm_q, h * D + b * 64, q0, &bars->q);
-        tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, q0, &bars->q);
+        tc::tma_load_2d(smem + L::Q + b * L::BM * 128, &tm_q, h * D + b * 64, it.q_row0, &bars->q);
+        tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, it.q_row0, &bars->q);
       }
-      for (int j = 0; j < n; ++j) {
+      for (int j = 0; j < n; ++j, walk.next()) {
         const int ks = j % L::NK;
         if (j >= L::NK && !tc::mbar_wait(&bars->kv_empty[ks], ((j - L::NK) / L::NK) & 1, abort, err, 181)) break;
+        const int krow = walk.row();
         tc::mbar_expect_tx(&bars->kv_full[ks], 2 * L::KT_BYTES);
         for (int b = 0; b < L::NB; ++b) {
-          tc::tma_load_2d(smem + L::K0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN,
+          tc::tma_load_2d(smem + L::K0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_k, hk * D + b * 64, krow,
                           &bars->kv_full[ks]);
-          tc::tma_load_2d(smem + L::V0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
+          tc::tma_load_2d(smem + L::V0 + ks * L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, krow,
                           &bars->kv_full[ks]);
         }
       }
@@ -1159,9 +1315,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
     const int sp = warp & 3, hc = warp >> 2;
     const int r = sp * 32 + lane;
     const int qi = q0 + r;
-    const int lim = qi + off;
-    const float l2 = qi < T ? lse[(long long)h * T + qi] * kLog2e : 0.f;
-    const float dl = qi < T ? delta[(long long)h * T + qi] : 0.f;
+    const long long lrow = (long long)h * Ttot + it.q_row0 + r;
+    const float l2 = qi < T ? lse[lrow] * kLog2e : 0.f;
+    const float dl = qi < T ? delta[lrow] : 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)(sp * 32) << 16);
     bool ok = true;
     // warps 0-3: copy this row of the Q and dO tiles (K-major, 128B-swizzled in shared memory) into the
@@ -1193,7 +1349,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->qo_tm);
     }
-    for (int j = 0; j < n && ok; ++j) {
+    for (int j = 0; j < n && ok; ++j, walk.next()) {
       if (!warp_wait(&bars->s_full, j & 1, abort, err, 201)) { ok = false; break; }
       tc::tc_fence_after();
       float p[64];
@@ -1202,9 +1358,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
       tc::tmem_ld_wait();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->s_free);
-      const int kc0 = j * L::BN + hc * 64;
-      // key kc0+c is visible iff c < nvis (key <= lim, key < S, query exists)
-      const int nvis = qi < T ? min(lim, S - 1) - kc0 + 1 : 0;
+      // key hc*64+c of the tile is visible iff c < nvis (the query exists and sees it)
+      const int nvis = qi < T ? walk.nvis(qi) - hc * 64 : 0;
 #pragma unroll
       for (int c = 0; c < 64; ++c) p[c] = c < nvis ? ex2(fmaf(p[c], sl2, -l2)) : 0.f;
       if (!warp_wait(&bars->dp_full, j & 1, abort, err, 202)) { ok = false; break; }
@@ -1241,7 +1396,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
         tc::tmem_ld32(lane_base + L::DQ_COL + c * 32, a);
         tc::tmem_ld_wait();
         if (qi < T) {
-          bf16* pq = dq + ((long long)qi * Hq + h) * D + c * 32;
+          bf16* pq = dq + ((long long)(it.q_row0 + r) * Hq + h) * D + c * 32;
 #pragma unroll
           for (int x = 0; x < 32; x += 8) {
             uint4 u;
@@ -1286,8 +1441,9 @@ template <int D_>
 __global__ void __launch_bounds__(320, 1) attn_bwd_dq256_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T, int S, int Hq,
-    int Hkv, float scale, int* __restrict__ err) {
+    const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T_in, int S_in,
+    int Hq, int Hkv, float scale, const int* __restrict__ qtab, const int2* __restrict__ far_tab, int Ttot,
+    int* __restrict__ err) {
   using L = Dq256Layout;
   constexpr int D = L::D;
   static_assert(D_ == D, "head dim 256 only");
@@ -1296,13 +1452,13 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq256_kernel(
   DqTBars* bars = reinterpret_cast<DqTBars*>(smem + L::BAR);
   const uint32_t sbase = tc::smem_addr(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_qt = (T + L::BM - 1) / L::BM;
-  const int qt = n_qt - 1 - (int)blockIdx.x;
+  const QItem it = qtab != nullptr ? load_qitem(qtab, blockIdx.x) : dense_qitem(L::BM, T_in, S_in);
+  const int T = it.T;
   const int h = blockIdx.y, hk = h / (Hq / Hkv);
-  const int q0 = qt * L::BM;
-  const int off = S - T;
-  const int kv_end = min(S, q0 + L::BM + off);
-  const int n = (kv_end + L::BN - 1) / L::BN;
+  const int q0 = it.q_loc0;
+  KeyWalk<L::BN> walk;
+  walk.init(it, far_tab);
+  const int n = walk.count(q0 + L::BM);
   const float sl2 = scale * kLog2e;
   volatile int* abort = &bars->abort;
 
@@ -1331,18 +1487,19 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq256_kernel(
     if (lane == 0) {
       tc::mbar_expect_tx(&bars->q, 2 * L::Q_BYTES);
       for (int b = 0; b < L::NB; ++b) {
-        tc::tma_load_2d(smem + L::QLOAD + b * L::BM * 128, &tm_q, h * D + b * 64, q0, &bars->q);
-        tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, q0, &bars->q);
+        tc::tma_load_2d(smem + L::QLOAD + b * L::BM * 128, &tm_q, h * D + b * 64, it.q_row0, &bars->q);
+        tc::tma_load_2d(smem + L::O + b * L::BM * 128, &tm_do, h * D + b * 64, it.q_row0, &bars->q);
       }
-      for (int j = 0; j < n; ++j) {
+      for (int j = 0; j < n; ++j, walk.next()) {
         const int ks = j % L::NK;
         if (j == 1 && !tc::mbar_wait(&bars->qo_tm, 0, abort, err, 211)) break;  // Q has left stage 1
         if (j >= L::NK && !tc::mbar_wait(&bars->kv_empty[ks], ((j - L::NK) / L::NK) & 1, abort, err, 212)) break;
         uint8_t* st = smem + L::ST0 + ks * L::ST_BYTES;
+        const int krow = walk.row();
         tc::mbar_expect_tx(&bars->kv_full[ks], 2 * L::KT_BYTES);
         for (int b = 0; b < L::NB; ++b) {
-          tc::tma_load_2d(st + b * L::BN * 128, &tm_k, hk * D + b * 64, j * L::BN, &bars->kv_full[ks]);
-          tc::tma_load_2d(st + L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, j * L::BN,
+          tc::tma_load_2d(st + b * L::BN * 128, &tm_k, hk * D + b * 64, krow, &bars->kv_full[ks]);
+          tc::tma_load_2d(st + L::KT_BYTES + b * L::BN * 128, &tm_v, hk * D + b * 64, krow,
                           &bars->kv_full[ks]);
         }
       }
@@ -1406,9 +1563,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq256_kernel(
     const int sp = warp & 3, hc = warp >> 2;
     const int r = sp * 32 + lane;
     const int qi = q0 + r;
-    const int lim = qi + off;
-    const float l2 = qi < T ? lse[(long long)h * T + qi] * kLog2e : 0.f;
-    const float dl = qi < T ? delta[(long long)h * T + qi] : 0.f;
+    const long long lrow = (long long)h * Ttot + it.q_row0 + r;
+    const float l2 = qi < T ? lse[lrow] * kLog2e : 0.f;
+    const float dl = qi < T ? delta[lrow] : 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)(sp * 32) << 16);
     bool ok = true;
     if (hc == 0) {
@@ -1435,7 +1592,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq256_kernel(
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->qo_tm);
     }
-    for (int j = 0; j < n && ok; ++j) {
+    for (int j = 0; j < n && ok; ++j, walk.next()) {
       if (!warp_wait(&bars->s_full, j & 1, abort, err, 231)) { ok = false; break; }
       tc::tc_fence_after();
       float p[32];
@@ -1443,8 +1600,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq256_kernel(
       tc::tmem_ld_wait();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->s_free);
-      const int kc0 = j * L::BN + hc * 32;
-      const int nvis = qi < T ? min(lim, S - 1) - kc0 + 1 : 0;  // key kc0+c visible iff c < nvis
+      const int nvis = qi < T ? walk.nvis(qi) - hc * 32 : 0;  // key hc*32+c of the tile visible iff c < nvis
 #pragma unroll
       for (int c = 0; c < 32; ++c) p[c] = c < nvis ? ex2(fmaf(p[c], sl2, -l2)) : 0.f;
       if (!warp_wait(&bars->dp_full, j & 1, abort, err, 232)) { ok = false; break; }
@@ -1480,7 +1636,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq256_kernel(
         tc::tmem_ld32(lane_base + L::DQ_COL + c * 32, a);
         tc::tmem_ld_wait();
         if (qi < T) {
-          bf16* pq = dq + ((long long)qi * Hq + h) * D + c * 32;
+          bf16* pq = dq + ((long long)(it.q_row0 + r) * Hq + h) * D + c * 32;
 #pragma unroll
           for (int x = 0; x < 32; x += 8) {
             uint4 u;
@@ -1657,46 +1813,108 @@ static at::Tensor out_or_new(const c10::optional<at::Tensor>& out, const at::Ten
   return *out;
 }
 
-std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
-                                    const c10::optional<at::Tensor>& out) {
+namespace {
+
+// Q-side / K-side work tables of a packed launch (all null for the single-segment launch).
+struct PackTabs {
+  const int* qtab = nullptr;
+  const int2* far = nullptr;
+  int nq = 0;
+  const int* ktab = nullptr;
+  const int4* cons = nullptr;
+  int nk = 0;
+};
+
+template <int D>
+void launch_fwd(dim3 grid, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, bf16* o,
+                float* lse, int T, int S, int Hq, int Hkv, float sl2, const PackTabs& tb, int Ttot, int* err) {
+  const int smem = FwdLayout<D>::TOTAL + 1024;
+  ensure_smem((const void*)attn_fwd_tc_kernel<D>, smem);
+  attn_fwd_tc_kernel<D><<<grid, 320, smem, stream()>>>(mq, mk, mv, o, lse, T, S, Hq, Hkv, sl2, tb.qtab, tb.far, Ttot,
+                                                       err);
+}
+
+void run_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+             double scale, const PackTabs& tb) {
+  const int Ttot = q.size(0), Hq = q.size(1), D = q.size(2), S = k.size(0), Hkv = k.size(1);
+  CUtensorMap mq = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, Ttot, (uint64_t)Hq * D, 128);
+  const uint32_t kv_rows = D <= 128 ? 128 : 64;
+  CUtensorMap mk = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, kv_rows);
+  CUtensorMap mv = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, kv_rows);
+  const dim3 grid(tb.qtab != nullptr ? tb.nq : (Ttot + 127) / 128, Hq);
+  const float sl2 = (float)scale * kLog2e;
+  int* err = tc_error_flag(q.device()).data_ptr<int>();
+  bf16* po = (bf16*)o.data_ptr();
+  float* pl = lse.data_ptr<float>();
+  if (D == 128) launch_fwd<128>(grid, mq, mk, mv, po, pl, Ttot, S, Hq, Hkv, sl2, tb, Ttot, err);
+  else if (D == 64) launch_fwd<64>(grid, mq, mk, mv, po, pl, Ttot, S, Hq, Hkv, sl2, tb, Ttot, err);
+  else if (D == 256) launch_fwd<256>(grid, mq, mk, mv, po, pl, Ttot, S, Hq, Hkv, sl2, tb, Ttot, err);
+  else TS_CHECK(false, "tcgen05 attention supports head_dim 64, 128 and 256");
+  TS_LAUNCH_CHECK();
+}
+
+void check_attn_inputs(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
   check_cuda(q, "q");
   check_cuda(k, "k");
   check_cuda(v, "v");
   TS_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
            "attention runs in bf16");
-  const c10::cuda::CUDAGuard guard(q.device());
-  const int T = q.size(0), Hq = q.size(1), D = q.size(2), S = k.size(0), Hkv = k.size(1);
-  TS_CHECK(S >= T && Hq % Hkv == 0 && k.sizes() == v.sizes() && k.size(2) == D, "attention shapes");
+  TS_CHECK(q.dim() == 3 && k.dim() == 3 && k.sizes() == v.sizes() && k.size(2) == q.size(2) &&
+               q.size(1) % k.size(1) == 0,
+           "attention shapes: q [T, Hq, d], k/v [S, Hkv, d] with Hq a multiple of Hkv");
   TS_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), "attention inputs must be contiguous");
+}
+
+// Reads the work tables of a packed launch: int32 CUDA tensors on q's device.
+PackTabs pack_tabs(const at::Tensor& q, const at::Tensor& qtab, const at::Tensor& far,
+                   const c10::optional<at::Tensor>& ktab, const c10::optional<at::Tensor>& cons) {
+  auto ok = [&](const at::Tensor& t, int per) {
+    return t.is_cuda() && t.device() == q.device() && t.scalar_type() == at::kInt && t.is_contiguous() &&
+           t.numel() % per == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0;
+  };
+  TS_CHECK(ok(qtab, 8) && ok(far, 2), "packed attention: qtab (8 ints per item) and far (2 ints per range) must "
+                                      "be contiguous, 16-byte aligned int32 CUDA tensors on q's device");
+  PackTabs tb;
+  tb.qtab = qtab.data_ptr<int>();
+  tb.far = reinterpret_cast<const int2*>(far.data_ptr<int>());
+  tb.nq = (int)(qtab.numel() / 8);
+  if (ktab) {
+    TS_CHECK(cons && ok(*ktab, 4) && ok(*cons, 4), "packed attention: ktab and cons (4 ints per entry) must be "
+                                                   "contiguous, 16-byte aligned int32 CUDA tensors on q's device");
+    tb.ktab = ktab->data_ptr<int>();
+    tb.cons = reinterpret_cast<const int4*>(cons->data_ptr<int>());
+    tb.nk = (int)(ktab->numel() / 4);
+  }
+  return tb;
+}
+
+}  // namespace
+
+std::vector<at::Tensor> attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
+                                    const c10::optional<at::Tensor>& out) {
+  check_attn_inputs(q, k, v);
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int T = q.size(0), Hq = q.size(1), S = k.size(0);
+  TS_CHECK(S >= T, "attention shapes: more queries than keys");
   auto o = out_or_new(out, q, "attention out");
   auto lse = at::empty({Hq, T}, q.options().dtype(at::kFloat));
   if (T == 0) return {o, lse};
-  CUtensorMap mq = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
-  const uint32_t kv_rows = D <= 128 ? 128 : 64;
-  CUtensorMap mk = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, kv_rows);
-  CUtensorMap mv = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, kv_rows);
-  dim3 grid((T + 127) / 128, Hq);
-  const float sl2 = (float)scale * kLog2e;
-  int* err = tc_error_flag(q.device()).data_ptr<int>();
-  if (D == 128) {
-    const int smem = FwdLayout<128>::TOTAL + 1024;
-    ensure_smem((const void*)attn_fwd_tc_kernel<128>, (int)(smem));
-    attn_fwd_tc_kernel<128><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
-                                                           S, Hq, Hkv, sl2, err);
-  } else if (D == 64) {
-    const int smem = FwdLayout<64>::TOTAL + 1024;
-    ensure_smem((const void*)attn_fwd_tc_kernel<64>, (int)(smem));
-    attn_fwd_tc_kernel<64><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
-                                                          S, Hq, Hkv, sl2, err);
-  } else if (D == 256) {
-    const int smem = FwdLayout<256>::TOTAL + 1024;
-    ensure_smem((const void*)attn_fwd_tc_kernel<256>, (int)(smem));
-    attn_fwd_tc_kernel<256><<<grid, 320, smem, stream()>>>(mq, mk, mv, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T,
-                                                           S, Hq, Hkv, sl2, err);
-  } else {
-    TS_CHECK(false, "tcgen05 attention supports head_dim 64, 128 and 256");
-  }
-  TS_LAUNCH_CHECK();
+  run_fwd(q, k, v, o, lse, scale, PackTabs{});
+  return {o, lse};
+}
+
+// Packed forward: q [Ttot, Hq, d] holds every segment's queries, k/v [Stot, Hkv, d] every key range;
+// qtab / far describe the work (see QItem). Rows of q no item covers are left untouched in `out` and lse.
+std::vector<at::Tensor> attn_fwd_packed(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                        const at::Tensor& qtab, const at::Tensor& far, double scale,
+                                        const c10::optional<at::Tensor>& out) {
+  check_attn_inputs(q, k, v);
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto o = out_or_new(out, q, "attention out");
+  auto lse = at::empty({q.size(1), q.size(0)}, q.options().dtype(at::kFloat));
+  const PackTabs tb = pack_tabs(q, qtab, far, c10::nullopt, c10::nullopt);
+  if (q.size(0) == 0 || tb.nq == 0) return {o, lse};
+  run_fwd(q, k, v, o, lse, scale, tb);
   return {o, lse};
 }
 
@@ -1725,7 +1943,7 @@ int dkdv_split(const dim3& g, int grp, int device) {
 template <int D>
 void launch_dkdv_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                    const CUtensorMap& mo, const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dk,
-                   at::Tensor& dv, int T, int S, int Hq, int Hkv, double scale, int* err) {
+                   at::Tensor& dv, int T, int S, int Hq, int Hkv, double scale, const PackTabs& tb, int* err) {
   const int nsplit = dkdv_split(g, Hq / Hkv, dk.get_device());
   g.z = nsplit;
   at::Tensor pk, pv;
@@ -1742,8 +1960,10 @@ void launch_dkdv_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const C
   attn_bwd_dkdv_t_kernel<D><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
                                                         delta.data_ptr<float>(), (bf16*)dk.data_ptr(),
                                                         (bf16*)dv.data_ptr(), ppk, ppv, T, S, Hq, Hkv, (float)scale,
-                                                        err);
+                                                        tb.ktab, tb.cons, T, S, err);
   if (nsplit > 1) {
+    // with tables the key items cover every key row (rows nobody reads get an item without consumers,
+    // which writes zeros), so every partial row summed here was written
     const long long n = (long long)S * Hkv * D;
     const int blocks = (int)((n / 4 + 255) / 256);
     attn_split_sum_kernel<<<blocks, 256, 0, stream()>>>(ppk, (bf16*)dk.data_ptr(), n, nsplit, (float)scale);
@@ -1754,7 +1974,7 @@ void launch_dkdv_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const C
 template <int MODE>
 void launch_dkdv256(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                     const CUtensorMap& mo, const at::Tensor& lse, const at::Tensor& delta, at::Tensor& out, int T,
-                    int S, int Hq, int Hkv, double scale, int* err) {
+                    int S, int Hq, int Hkv, double scale, const PackTabs& tb, int* err) {
   const int nsplit = dkdv_split(g, Hq / Hkv, out.get_device());
   g.z = nsplit;
   at::Tensor part;
@@ -1767,7 +1987,7 @@ void launch_dkdv256(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const 
   ensure_smem((const void*)attn_bwd_dkdv256_kernel<MODE>, smem);
   attn_bwd_dkdv256_kernel<MODE><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
                                                             delta.data_ptr<float>(), (bf16*)out.data_ptr(), pp, T, S,
-                                                            Hq, Hkv, (float)scale, err);
+                                                            Hq, Hkv, (float)scale, tb.ktab, tb.cons, T, S, err);
   if (nsplit > 1) {
     const long long n = (long long)S * Hkv * 256;
     const int blocks = (int)((n / 4 + 255) / 256);
@@ -1779,46 +1999,29 @@ void launch_dkdv256(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const 
 template <int D>
 void launch_dq_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
                  const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, int T, int S, int Hq, int Hkv,
-                 double scale, int* err) {
+                 double scale, const PackTabs& tb, int* err) {
   const int smem = DqTLayout<D>::TOTAL + 1024;
   ensure_smem((const void*)attn_bwd_dq_t_kernel<D>, smem);
   attn_bwd_dq_t_kernel<D><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
                                                       delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq, Hkv,
-                                                      (float)scale, err);
+                                                      (float)scale, tb.qtab, tb.far, T, err);
 }
 
 void launch_dq256(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
                   const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq, int T, int S, int Hq, int Hkv,
-                  double scale, int* err) {
+                  double scale, const PackTabs& tb, int* err) {
   const int smem = Dq256Layout::TOTAL + 1024;
   ensure_smem((const void*)attn_bwd_dq256_kernel<256>, smem);
   attn_bwd_dq256_kernel<256><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
                                                          delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq, Hkv,
-                                                         (float)scale, err);
+                                                         (float)scale, tb.qtab, tb.far, T, err);
 }
 
-}  // namespace
-
-// dq/dk/dv (optional): contiguous tensors shaped like q/k/v that receive the gradients.
-std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
-                                    const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale,
-                                    const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
-                                    const c10::optional<at::Tensor>& dv_out) {
-  check_cuda(q, "q");
-  check_cuda(k, "k");
-  check_cuda(v, "v");
-  check_cuda(o, "o");
-  check_cuda(dout, "dout");
-  check_cuda(lse, "lse");
-  const c10::cuda::CUDAGuard guard(q.device());
+// T / S: total query and key rows (one segment without tables)
+void run_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+             const at::Tensor& o, const at::Tensor& lse, double scale, at::Tensor& dq, at::Tensor& dk,
+             at::Tensor& dv, const PackTabs& tb) {
   const int T = q.size(0), Hq = q.size(1), D = q.size(2), S = k.size(0), Hkv = k.size(1);
-  TS_CHECK(S >= T && Hq % Hkv == 0 && (D == 64 || D == 128 || D == 256), "attention backward shapes");
-  TS_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous() && dout.is_contiguous(),
-           "attention backward inputs must be contiguous");
-  auto dq = out_or_new(dq_out, q, "attention dq");
-  auto dk = out_or_new(dk_out, k, "attention dk");
-  auto dv = out_or_new(dv_out, v, "attention dv");
-  if (T == 0) return {dq, dk.zero_(), dv.zero_()};
   auto delta = at::empty({Hq, T}, q.options().dtype(at::kFloat));
   const long long items = (long long)T * Hq;
   attn_delta_kernel<<<(int)((items + 7) / 8), 256, 0, stream()>>>((const bf16*)o.data_ptr(),
@@ -1829,24 +2032,80 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
   CUtensorMap mv128 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 128);
   CUtensorMap mq128 = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
   CUtensorMap mo128 = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 128);
-  dim3 g1((S + 127) / 128, Hkv), g2((T + 127) / 128, Hq);
+  const bool packed = tb.qtab != nullptr;
+  dim3 g1(packed ? tb.nk : (S + 127) / 128, Hkv), g2(packed ? tb.nq : (T + 127) / 128, Hq);
   if (D == 128) {
-    launch_dkdv_t<128>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
-    launch_dq_t<128>(g2, mq128, mk128, mv128, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
+    if (g1.x) launch_dkdv_t<128>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, tb, err);
+    if (g2.x) launch_dq_t<128>(g2, mq128, mk128, mv128, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, tb, err);
   } else if (D == 64) {
-    launch_dkdv_t<64>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, err);
-    launch_dq_t<64>(g2, mq128, mk128, mv128, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
+    if (g1.x) launch_dkdv_t<64>(g1, mq128, mk128, mv128, mo128, lse, delta, dk, dv, T, S, Hq, Hkv, scale, tb, err);
+    if (g2.x) launch_dq_t<64>(g2, mq128, mk128, mv128, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, tb, err);
   } else {
     // dK and dV passes step over 64-query tiles, dQ over 64-key tiles
     CUtensorMap mq64 = make_bf16_map(q.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 64);
     CUtensorMap mo64 = make_bf16_map(dout.data_ptr(), (uint64_t)Hq * D, T, (uint64_t)Hq * D, 64);
-    launch_dkdv256<1>(g1, mq64, mk128, mv128, mo64, lse, delta, dk, T, S, Hq, Hkv, scale, err);
-    launch_dkdv256<2>(g1, mq64, mk128, mv128, mo64, lse, delta, dv, T, S, Hq, Hkv, scale, err);
+    if (g1.x) {
+      launch_dkdv256<1>(g1, mq64, mk128, mv128, mo64, lse, delta, dk, T, S, Hq, Hkv, scale, tb, err);
+      launch_dkdv256<2>(g1, mq64, mk128, mv128, mo64, lse, delta, dv, T, S, Hq, Hkv, scale, tb, err);
+    }
     CUtensorMap mk64 = make_bf16_map(k.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
     CUtensorMap mv64 = make_bf16_map(v.data_ptr(), (uint64_t)Hkv * D, S, (uint64_t)Hkv * D, 64);
-    launch_dq256(g2, mq128, mk64, mv64, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, err);
+    if (g2.x) launch_dq256(g2, mq128, mk64, mv64, mo128, lse, delta, dq, T, S, Hq, Hkv, scale, tb, err);
   }
   TS_LAUNCH_CHECK();
+}
+
+void check_bwd_inputs(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                      const at::Tensor& o, const at::Tensor& lse) {
+  check_attn_inputs(q, k, v);
+  check_cuda(o, "o");
+  check_cuda(dout, "dout");
+  check_cuda(lse, "lse");
+  const int D = q.size(2);
+  TS_CHECK(D == 64 || D == 128 || D == 256, "attention backward: head_dim 64, 128 or 256");
+  TS_CHECK(o.sizes() == q.sizes() && dout.sizes() == q.sizes() && o.is_contiguous() && dout.is_contiguous(),
+           "attention backward: o and dout must be contiguous and shaped like q");
+  TS_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.dim() == 2 && lse.size(0) == q.size(1) &&
+               lse.size(1) == q.size(0),
+           "attention backward: lse must be a contiguous fp32 [Hq, T] tensor");
+}
+
+}  // namespace
+
+// dq/dk/dv (optional): contiguous tensors shaped like q/k/v that receive the gradients.
+std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                    const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale,
+                                    const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
+                                    const c10::optional<at::Tensor>& dv_out) {
+  check_bwd_inputs(dout, q, k, v, o, lse);
+  const c10::cuda::CUDAGuard guard(q.device());
+  TS_CHECK(k.size(0) >= q.size(0), "attention backward: more queries than keys");
+  auto dq = out_or_new(dq_out, q, "attention dq");
+  auto dk = out_or_new(dk_out, k, "attention dk");
+  auto dv = out_or_new(dv_out, v, "attention dv");
+  if (q.size(0) == 0) return {dq, dk.zero_(), dv.zero_()};
+  run_bwd(dout, q, k, v, o, lse, scale, dq, dk, dv, PackTabs{});
+  return {dq, dk, dv};
+}
+
+// Packed backward over the tables of attn_fwd_packed plus the key-side tables (KItem / consumers). The key
+// items must cover every row of k (an item without consumers writes zero gradients); rows of dq that no
+// query item covers are left untouched.
+std::vector<at::Tensor> attn_bwd_packed(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                                        const at::Tensor& qtab, const at::Tensor& far, const at::Tensor& ktab,
+                                        const at::Tensor& cons, double scale,
+                                        const c10::optional<at::Tensor>& dq_out,
+                                        const c10::optional<at::Tensor>& dk_out,
+                                        const c10::optional<at::Tensor>& dv_out) {
+  check_bwd_inputs(dout, q, k, v, o, lse);
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto dq = out_or_new(dq_out, q, "attention dq");
+  auto dk = out_or_new(dk_out, k, "attention dk");
+  auto dv = out_or_new(dv_out, v, "attention dv");
+  const PackTabs tb = pack_tabs(q, qtab, far, ktab, cons);
+  if (q.size(0) == 0 || (tb.nq == 0 && tb.nk == 0)) return {dq, dk, dv};
+  run_bwd(dout, q, k, v, o, lse, scale, dq, dk, dv, tb);
   return {dq, dk, dv};
 }
 

@@ -43,6 +43,7 @@ void symm_barrier(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t s
                   at::Tensor& status, double timeout_s);
 at::Tensor symm_reduce(const std::vector<int64_t>& buf_ptrs, int64_t rank, int64_t lo, int64_t hi, double scale,
                        bool write_all, const at::Tensor& like);
+void symm_reduce_oneshot(const std::vector<int64_t>& buf_ptrs, int64_t n, double scale, at::Tensor& out);
 void symm_norm_put(const at::Tensor& partial, const std::vector<int64_t>& flag_ptrs, int64_t rank,
                    int64_t norm_offset);
 void symm_adamw_gather(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tensor& grad,
@@ -57,6 +58,16 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
                                     const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, double scale,
                                     const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
                                     const c10::optional<at::Tensor>& dv_out);
+std::vector<at::Tensor> attn_fwd_packed(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                        const at::Tensor& qtab, const at::Tensor& far, double scale,
+                                        const c10::optional<at::Tensor>& out);
+std::vector<at::Tensor> attn_bwd_packed(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                                        const at::Tensor& qtab, const at::Tensor& far, const at::Tensor& ktab,
+                                        const at::Tensor& cons, double scale,
+                                        const c10::optional<at::Tensor>& dq_out,
+                                        const c10::optional<at::Tensor>& dk_out,
+                                        const c10::optional<at::Tensor>& dv_out);
 void register_ipc(pybind11::module& m);
 uint64_t bounds_word_rowops(bool reset);
 uint64_t bounds_word_fold(bool reset);
@@ -82,15 +93,18 @@ std::vector<at::Tensor> dense_layer_fwd(const at::Tensor& h, const at::Tensor& p
                                         const c10::optional<at::Tensor>& kn, const at::Tensor& wo,
                                         const at::Tensor& ln2, const at::Tensor& wgu, const at::Tensor& wd,
                                         const std::vector<at::Tensor>& past_k, const std::vector<at::Tensor>& past_v,
-                                        int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov);
+                                        int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov,
+                                        const std::vector<at::Tensor>& tabs);
 std::vector<at::Tensor> dense_layer_bwd(
     const at::Tensor& dout, const c10::optional<at::Tensor>& dk_out, const c10::optional<at::Tensor>& dv_out,
     const at::Tensor& h, const at::Tensor& pos, const at::Tensor& inv_freq, const at::Tensor& cos_tab,
     const at::Tensor& sin_tab, const at::Tensor& ln1, const at::Tensor& wqkv, const c10::optional<at::Tensor>& qn,
     const c10::optional<at::Tensor>& kn, const at::Tensor& wo, const at::Tensor& ln2, const at::Tensor& wgu,
-    const at::Tensor& wd, const at::Tensor& kbuf, const at::Tensor& vbuf, const std::vector<at::Tensor>& saved,
+    const at::Tensor& wd, const at::Tensor& k_own, const at::Tensor& v_own, const std::vector<at::Tensor>& past_k,
+    const std::vector<at::Tensor>& past_v, const std::vector<at::Tensor>& saved,
     int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov, int64_t sp,
-    const std::vector<c10::optional<at::Tensor>>& sinks, double sink_scale, int64_t side);
+    const std::vector<c10::optional<at::Tensor>>& sinks, double sink_scale, int64_t side,
+    const std::vector<at::Tensor>& tabs);
 void gemm_tc_cat(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& a2,
                  const c10::optional<at::Tensor>& b2, bool a_t, bool b_t, int64_t mode, double alpha,
                  const c10::optional<at::Tensor>& residual);
@@ -149,8 +163,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("v"), pybind11::arg("o"), pybind11::arg("lse"), pybind11::arg("scale"),
         pybind11::arg("dq") = pybind11::none(), pybind11::arg("dk") = pybind11::none(),
         pybind11::arg("dv") = pybind11::none());
+  m.def("attn_fwd_packed", &ts::attn_fwd_packed, pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"),
+        pybind11::arg("qtab"), pybind11::arg("far"), pybind11::arg("scale"), pybind11::arg("out") = pybind11::none());
+  m.def("attn_bwd_packed", &ts::attn_bwd_packed, pybind11::arg("dout"), pybind11::arg("q"), pybind11::arg("k"),
+        pybind11::arg("v"), pybind11::arg("o"), pybind11::arg("lse"), pybind11::arg("qtab"), pybind11::arg("far"),
+        pybind11::arg("ktab"), pybind11::arg("cons"), pybind11::arg("scale"), pybind11::arg("dq") = pybind11::none(),
+        pybind11::arg("dk") = pybind11::none(), pybind11::arg("dv") = pybind11::none());
   m.def("symm_reduce", &ts::symm_reduce);
   m.def("symm_norm_put", &ts::symm_norm_put);
+  m.def("symm_reduce_oneshot", &ts::symm_reduce_oneshot);
   m.def("symm_adamw_gather", &ts::symm_adamw_gather);
   m.def("conv1d_silu_fwd", &ts::conv1d_silu_fwd);
   m.def("conv1d_silu_bwd", &ts::conv1d_silu_bwd);

@@ -16,6 +16,12 @@
 //                      and, for an all-reduce, to every peer's chunk r. A
 //                      per-CTA partial of the squared norm of the reduced
 //                      chunk is written for the clip.
+// symm_reduce_oneshot: one-shot all-reduce for short buffers: every rank reads
+//                      the whole buffer of every rank (fixed rank order, so
+//                      bitwise identical everywhere) and writes the scaled sum
+//                      to a local output; one NVLink read phase, no second
+//                      write phase (latency-bound sizes; the two-shot moves
+//                      fewer bytes per rank at large sizes).
 // symm_norm_put      : sum of the partials (fixed order) stored into every
 //                      peer's norm slot r.
 // symm_adamw_gather  : fused AdamW on this rank's shard (fp32 master and
@@ -114,6 +120,29 @@ __global__ void symm_reduce_kernel(PeerPtrs bufs, int rank, int world, long long
   }
 }
 
+__global__ void symm_reduce_oneshot_kernel(PeerPtrs bufs, int world, long long n, float scale,
+                                           float* __restrict__ out) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long nv = n / 4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv; i += stride) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r < world) {
+        const float4 v = reinterpret_cast<const float4*>(bufs.p[r])[i];
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+    }
+    acc.x *= scale; acc.y *= scale; acc.z *= scale; acc.w *= scale;
+    reinterpret_cast<float4*>(out)[i] = acc;
+  }
+  for (long long e = nv * 4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += stride) {
+    float acc = 0.f;
+    for (int r = 0; r < world; ++r) acc += reinterpret_cast<const float*>(bufs.p[r])[e];
+    out[e] = acc * scale;
+  }
+}
+
 // norm slots live in each rank's flag buffer after the barrier slots, as floats
 __global__ void symm_norm_put_kernel(const float* __restrict__ partial, int n, PeerPtrs flags, int rank, int world,
                                      int norm_offset) {
@@ -161,6 +190,55 @@ __global__ void symm_adamw_gather_kernel(float* __restrict__ master, float* __re
   __threadfence_system();
 }
 
+// symm_adamw_gather_kernel with four elements per 16-byte access and 8-byte bf16 stores to each peer
+// (2-byte stores would cross NVLink as one small packet per element). Needs n4 = n / 4 groups,
+// 16-byte aligned fp32 shards and lo % 4 == 0 (8-byte aligned bf16 destinations).
+__global__ void symm_adamw_gather_vec_kernel(float4* __restrict__ master, float4* __restrict__ m,
+                                             float4* __restrict__ v, const float4* __restrict__ grad, PeerPtrs params,
+                                             int world, long long lo, long long n4, float lr, float b1, float b2,
+                                             float eps, float wd, float bc1, float bc2, int maximize,
+                                             const float* __restrict__ norm_slots, float max_norm,
+                                             float* __restrict__ norm_out) {
+  float sq = 0.f;
+  for (int r = 0; r < world; ++r) sq += norm_slots[r];
+  const float nrm = sqrtf(sq);
+  float coef = 1.f;
+  if (max_norm > 0.f) {
+    coef = max_norm / (nrm + 1e-6f);
+    coef = coef < 1.f ? coef : 1.f;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && norm_out != nullptr) norm_out[0] = nrm;
+  const float decay = 1.f - lr * wd;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 gv = grad[i];
+    float4 mv = m[i], vv = v[i], wv = master[i];
+    float* gp = const_cast<float*>(&gv.x);
+    float* mp = &mv.x;
+    float* vp = &vv.x;
+    float* wp = &wv.x;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float g = gp[e] * coef;
+      if (maximize) g = -g;
+      const float mi = b1 * mp[e] + (1.f - b1) * g;
+      const float vi = b2 * vp[e] + (1.f - b2) * g * g;
+      mp[e] = mi;
+      vp[e] = vi;
+      wp[e] = wp[e] * decay - lr * (mi / bc1) / (sqrtf(vi / bc2) + eps);
+    }
+    m[i] = mv;
+    v[i] = vv;
+    master[i] = wv;
+    __nv_bfloat162 lo2 = __floats2bfloat162_rn(wv.x, wv.y), hi2 = __floats2bfloat162_rn(wv.z, wv.w);
+    const uint2 packed = make_uint2(*reinterpret_cast<unsigned*>(&lo2), *reinterpret_cast<unsigned*>(&hi2));
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(params.p[r]) + lo)[i] = packed;
+  }
+  __threadfence_system();
+}
+
 PeerPtrs to_peers(const std::vector<int64_t>& ptrs) {
   TS_CHECK(!ptrs.empty() && ptrs.size() <= (size_t)kMaxRanks, "1..8 ranks supported, got ", ptrs.size());
   PeerPtrs pp{};
@@ -194,6 +272,18 @@ at::Tensor symm_reduce(const std::vector<int64_t>& buf_ptrs, int64_t rank, int64
   return partial;
 }
 
+void symm_reduce_oneshot(const std::vector<int64_t>& buf_ptrs, int64_t n, double scale, at::Tensor& out) {
+  TS_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() >= n,
+           "one-shot all-reduce: out must be a contiguous fp32 CUDA tensor of at least n elements");
+  TS_CHECK((reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0, "one-shot all-reduce: out must be 16-byte aligned");
+  const c10::cuda::CUDAGuard guard(out.device());
+  if (n == 0) return;
+  const int blocks = (int)std::min<long long>((n / 4 + 511) / 512 + 1, 2LL * sm_count(out.get_device()));
+  symm_reduce_oneshot_kernel<<<blocks, 512, 0, stream()>>>(to_peers(buf_ptrs), (int)buf_ptrs.size(), n,
+                                                           (float)scale, out.data_ptr<float>());
+  TS_LAUNCH_CHECK();
+}
+
 void symm_norm_put(const at::Tensor& partial, const std::vector<int64_t>& flag_ptrs, int64_t rank,
                    int64_t norm_offset) {
   const c10::cuda::CUDAGuard guard(partial.device());
@@ -216,10 +306,22 @@ void symm_adamw_gather(at::Tensor& master, at::Tensor& m, at::Tensor& v, const a
   const float bc1 = 1.f - (float)std::pow(b1, (double)step);
   const float bc2 = 1.f - (float)std::pow(b2, (double)step);
   const int blocks = 4 * sm_count(master.get_device());
-  symm_adamw_gather_kernel<<<blocks, 256, 0, stream()>>>(
-      master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), grad.data_ptr<float>(),
-      to_peers(param_ptrs), (int)param_ptrs.size(), lo, n, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
-      bc1, bc2, maximize ? 1 : 0, norm_slots.data_ptr<float>(), (float)max_norm, norm_out.data_ptr<float>());
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  bool vec = n % 4 == 0 && lo % 4 == 0 && al(master.data_ptr()) && al(m.data_ptr()) && al(v.data_ptr()) &&
+             al(grad.data_ptr());
+  for (int64_t p : param_ptrs) vec = vec && (p % 8 == 0);
+  if (vec) {
+    symm_adamw_gather_vec_kernel<<<blocks, 256, 0, stream()>>>(
+        (float4*)master.data_ptr<float>(), (float4*)m.data_ptr<float>(), (float4*)v.data_ptr<float>(),
+        (const float4*)grad.data_ptr<float>(), to_peers(param_ptrs), (int)param_ptrs.size(), lo, n / 4, (float)lr,
+        (float)b1, (float)b2, (float)eps, (float)wd, bc1, bc2, maximize ? 1 : 0, norm_slots.data_ptr<float>(),
+        (float)max_norm, norm_out.data_ptr<float>());
+  } else {
+    symm_adamw_gather_kernel<<<blocks, 256, 0, stream()>>>(
+        master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), grad.data_ptr<float>(),
+        to_peers(param_ptrs), (int)param_ptrs.size(), lo, n, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
+        bc1, bc2, maximize ? 1 : 0, norm_slots.data_ptr<float>(), (float)max_norm, norm_out.data_ptr<float>());
+  }
   TS_LAUNCH_CHECK();
 }
 

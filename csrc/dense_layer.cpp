@@ -11,9 +11,15 @@
 //
 // Layer: h1 = h + o_proj(attn(rope(norm(qkv(rmsnorm1(h)))))),
 //        out = h1 + down(swiglu(gate_up(rmsnorm2(h1)))).
-// The ancestors' keys/values and the pack's own sit in one buffer
-// [S_past + t, hkv, d] that the rope kernel writes in place; attention reads
-// the first S_past + cov rows. Rows [cov, t) are pack padding.
+// Attention reads the ancestors' keys/values and the pack's own from one
+// buffer [S_past + t, hkv, d] built for the call (forward and again in the
+// backward) from the ancestor chunks and the pack's own rows, which stay
+// tensors of their own: descendants keep only those, never a copy of the
+// ancestors. Single segment: attention reads the first S_past + cov rows;
+// rows [cov, t) are pack padding. A pack of several segments passes its
+// packed-attention work tables (`tabs`): the ancestor part then holds each
+// unique ancestor chunk once and attention is one packed launch over all
+// segments.
 #include "common.h"
 
 #include <ATen/cuda/CUDAEvent.h>
@@ -51,10 +57,28 @@ std::vector<at::Tensor> attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q,
                                     const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
                                     const c10::optional<at::Tensor>& dv_out);
 
+std::vector<at::Tensor> attn_fwd_packed(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                        const at::Tensor& qtab, const at::Tensor& far, double scale,
+                                        const c10::optional<at::Tensor>& out);
+std::vector<at::Tensor> attn_bwd_packed(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                        const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+                                        const at::Tensor& qtab, const at::Tensor& far, const at::Tensor& ktab,
+                                        const at::Tensor& cons, double scale,
+                                        const c10::optional<at::Tensor>& dq_out,
+                                        const c10::optional<at::Tensor>& dk_out,
+                                        const c10::optional<at::Tensor>& dv_out);
+
 void gemm_tc(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, bool a_t, bool b_t, int64_t mode,
              double alpha, const c10::optional<at::Tensor>& residual);
 
 namespace {
+
+// [chunks... | own] along rows, one copy kernel
+at::Tensor join_rows(const std::vector<at::Tensor>& chunks, const at::Tensor& own) {
+  std::vector<at::Tensor> all(chunks.begin(), chunks.end());
+  all.push_back(own);
+  return at::cat(all, 0);
+}
 
 // x [M, K] · Wᵀ (W [N, K]) [+ residual], bf16
 at::Tensor lin(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& residual = c10::nullopt) {
@@ -101,14 +125,15 @@ void deposit(at::Tensor target, const at::Tensor& dy, const at::Tensor& x, doubl
 
 }  // namespace
 
-// Returns {out, kbuf, vbuf, x1, rstd1, qkv, q, o, lse, h1, x2, rstd2, gu, a}.
+// Returns {out, k, v, x1, rstd1, qkv, q, o, lse, h1, x2, rstd2, gu, a}; k / v are the pack's own rows.
 std::vector<at::Tensor> dense_layer_fwd(const at::Tensor& h, const at::Tensor& pos, const at::Tensor& inv_freq,
                                         const at::Tensor& cos_tab, const at::Tensor& sin_tab, const at::Tensor& ln1,
                                         const at::Tensor& wqkv, const c10::optional<at::Tensor>& qn,
                                         const c10::optional<at::Tensor>& kn, const at::Tensor& wo,
                                         const at::Tensor& ln2, const at::Tensor& wgu, const at::Tensor& wd,
                                         const std::vector<at::Tensor>& past_k, const std::vector<at::Tensor>& past_v,
-                                        int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov) {
+                                        int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov,
+                                        const std::vector<at::Tensor>& tabs) {
   check_cuda(h, "h");
   const int64_t t = h.size(0);
   TS_CHECK(cov > 0 && cov <= t && past_k.size() == past_v.size(), "dense_layer_fwd: rows / ancestor chunks");
@@ -118,26 +143,27 @@ std::vector<at::Tensor> dense_layer_fwd(const at::Tensor& h, const at::Tensor& p
   auto qkv = lin(x1, wqkv);
   int64_t sp = 0;
   for (const auto& x : past_k) sp += x.size(0);
-  auto kbuf = at::empty({sp + t, hkv, d}, h.options());
-  auto vbuf = at::empty({sp + t, hkv, d}, h.options());
-  if (sp > 0) {
-    auto kp = kbuf.narrow(0, 0, sp), vp = vbuf.narrow(0, 0, sp);
-    at::cat_out(kp, past_k, 0);
-    at::cat_out(vp, past_v, 0);
-  }
-  auto rr = qk_norm_rope_fwd(qkv, qn, kn, pos, inv_freq, hq, hkv, d, eps, false, cos_tab, sin_tab,
-                             kbuf.narrow(0, sp, t), vbuf.narrow(0, sp, t));
-  const at::Tensor& q = rr[0];
+  auto rr = qk_norm_rope_fwd(qkv, qn, kn, pos, inv_freq, hq, hkv, d, eps, false, cos_tab, sin_tab, c10::nullopt,
+                             c10::nullopt);
+  const at::Tensor &q = rr[0], &k_own = rr[1], &v_own = rr[2];
+  at::Tensor kbuf = k_own, vbuf = v_own;
+  if (sp > 0) kbuf = join_rows(past_k, k_own), vbuf = join_rows(past_v, v_own);
   auto o = at::empty({t, hq, d}, h.options());
-  auto att = attn_fwd_tc(q.narrow(0, 0, cov), kbuf.narrow(0, 0, sp + cov), vbuf.narrow(0, 0, sp + cov), scale,
-                         o.narrow(0, 0, cov));
+  std::vector<at::Tensor> att;
+  if (tabs.empty()) {
+    att = attn_fwd_tc(q.narrow(0, 0, cov), kbuf.narrow(0, 0, sp + cov), vbuf.narrow(0, 0, sp + cov), scale,
+                      o.narrow(0, 0, cov));
+  } else {
+    // several segments: one packed launch over [unique ancestor chunks | own rows]
+    att = attn_fwd_packed(q, kbuf, vbuf, tabs[0], tabs[1], scale, o);
+  }
   if (cov < t) o.narrow(0, cov, t - cov).zero_();  // pack padding rows: no attention output
   auto h1 = lin(o.view({t, hq * d}), wo, h);
   auto r2 = rms_norm_fwd(h1, ln2, eps, false);
   auto gu = lin(r2[0], wgu);
   auto a = swiglu_fwd(gu);
   auto out = lin(a, wd, h1);
-  return {out, kbuf, vbuf, x1, r1[1], qkv, q, o, att[1], h1, r2[0], r2[1], gu, a};
+  return {out, k_own, v_own, x1, r1[1], qkv, q, o, att[1], h1, r2[0], r2[1], gu, a};
 }
 
 // Sink targets (fp32 views: ln1, qkv span, q-norm, k-norm, o, ln2, gate/up span, down) receive the weight
@@ -150,9 +176,11 @@ std::vector<at::Tensor> dense_layer_bwd(
     const at::Tensor& h, const at::Tensor& pos, const at::Tensor& inv_freq, const at::Tensor& cos_tab,
     const at::Tensor& sin_tab, const at::Tensor& ln1, const at::Tensor& wqkv, const c10::optional<at::Tensor>& qn,
     const c10::optional<at::Tensor>& kn, const at::Tensor& wo, const at::Tensor& ln2, const at::Tensor& wgu,
-    const at::Tensor& wd, const at::Tensor& kbuf, const at::Tensor& vbuf, const std::vector<at::Tensor>& saved,
+    const at::Tensor& wd, const at::Tensor& k_own, const at::Tensor& v_own, const std::vector<at::Tensor>& past_k,
+    const std::vector<at::Tensor>& past_v, const std::vector<at::Tensor>& saved,
     int64_t hq, int64_t hkv, int64_t d, double eps, double scale, int64_t cov, int64_t sp,
-    const std::vector<c10::optional<at::Tensor>>& sinks, double sink_scale, int64_t side) {
+    const std::vector<c10::optional<at::Tensor>>& sinks, double sink_scale, int64_t side,
+    const std::vector<at::Tensor>& tabs) {
   TS_CHECK(saved.size() == 11 && sinks.size() == 8, "dense_layer_bwd: saved / sink lists");
   const c10::cuda::CUDAGuard guard(h.device());
   const at::Tensor &x1 = saved[0], &rstd1 = saved[1], &qkv = saved[2], &q = saved[3], &o = saved[4],
@@ -181,18 +209,27 @@ std::vector<at::Tensor> dense_layer_bwd(
   if (s_o) deposit(*s_o, dh1, o2, sink_scale, side);
   else g_o = mm_tn(dh1, o2);
   auto do3 = do2.view({t, hq, d});
-  // attention over [ancestors | own rows]; gradients land where the operands live
+  // attention over [ancestors | own rows] (the buffer is rebuilt here: no event keeps a copy of its
+  // ancestors' rows between its forward and backward); gradients land in one buffer of the same layout
+  at::Tensor kbuf = k_own, vbuf = v_own;
+  if (sp > 0) kbuf = join_rows(past_k, k_own), vbuf = join_rows(past_v, v_own);
   auto dq = at::empty_like(q);
   auto dkbuf = at::empty_like(kbuf);
   auto dvbuf = at::empty_like(vbuf);
-  if (cov < t) {
-    dq.narrow(0, cov, t - cov).zero_();
-    dkbuf.narrow(0, sp + cov, t - cov).zero_();
-    dvbuf.narrow(0, sp + cov, t - cov).zero_();
+  if (cov < t) dq.narrow(0, cov, t - cov).zero_();
+  if (tabs.empty()) {
+    if (cov < t) {
+      dkbuf.narrow(0, sp + cov, t - cov).zero_();
+      dvbuf.narrow(0, sp + cov, t - cov).zero_();
+    }
+    attn_bwd_tc(do3.narrow(0, 0, cov).contiguous(), q.narrow(0, 0, cov), kbuf.narrow(0, 0, sp + cov),
+                vbuf.narrow(0, 0, sp + cov), o.narrow(0, 0, cov), lse, scale, dq.narrow(0, 0, cov),
+                dkbuf.narrow(0, 0, sp + cov), dvbuf.narrow(0, 0, sp + cov));
+  } else {
+    // the key items cover every key row (padding rows get zero gradients)
+    TS_CHECK(tabs.size() == 4, "dense_layer_bwd: packed attention needs qtab, far, ktab and cons");
+    attn_bwd_packed(do3, q, kbuf, vbuf, o, lse, tabs[0], tabs[1], tabs[2], tabs[3], scale, dq, dkbuf, dvbuf);
   }
-  attn_bwd_tc(do3.narrow(0, 0, cov).contiguous(), q.narrow(0, 0, cov), kbuf.narrow(0, 0, sp + cov),
-              vbuf.narrow(0, 0, sp + cov), o.narrow(0, 0, cov), lse, scale, dq.narrow(0, 0, cov),
-              dkbuf.narrow(0, 0, sp + cov), dvbuf.narrow(0, 0, sp + cov));
   auto dk = dkbuf.narrow(0, sp, t), dv = dvbuf.narrow(0, sp, t);
   if (dk_out) dk.add_(*dk_out);
   if (dv_out) dv.add_(*dv_out);

@@ -151,6 +151,18 @@ def mode_native(rank, world, device):
     ds = [torch.zeros_like(d) for _ in range(world)]
     dist.all_gather(ds, d)
     bitwise_same = all(float(x) == float(ds[0]) for x in ds)
+    # one-shot all-reduce: same fixed rank order, so bitwise equal to the two-shot result
+    small = 70_001
+    sbuf, sptrs = ws.alloc(small, torch.float32)
+    sbuf.copy_(mine[:small].to(device))
+    out = torch.empty(small, device=device)
+    ws.all_reduce_mean_oneshot(sbuf, sptrs, out, pre_scale=0.5)
+    torch.cuda.synchronize()
+    ws.check()
+    ws.all_reduce_mean(sbuf, sptrs, pre_scale=0.5)  # the two-shot over the same (unchanged) input
+    torch.cuda.synchronize()
+    ws.check()
+    oneshot_equal = bool(torch.equal(out, sbuf)) and bool(torch.allclose(out.cpu(), ref[:small], rtol=1e-6, atol=1e-6))
     # reduce-scatter + fused AdamW gather
     model = _model(2, device, torch.bfloat16)
     arena = arena_for(model)
@@ -167,7 +179,7 @@ def mode_native(rank, world, device):
     s = torch.tensor([float(arena.flat.float().double().sum())], device=device, dtype=torch.float64)
     ss = [torch.zeros_like(s) for _ in range(world)]
     dist.all_gather(ss, s)
-    return {"allreduce_close": close, "allreduce_bitwise_same": bitwise_same,
+    return {"allreduce_close": close, "allreduce_bitwise_same": bitwise_same, "oneshot_equal": oneshot_equal,
             "params_same_after_gather": all(float(x) == float(ss[0]) for x in ss)}
 
 

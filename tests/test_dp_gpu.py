@@ -35,6 +35,7 @@ def test_dp_step_equals_single_process(tmp_path):
 def test_native_collectives_are_exact_and_deterministic(tmp_path):
     res = _run("native", tmp_path)
     assert res["allreduce_close"] and res["allreduce_bitwise_same"] and res["params_same_after_gather"], res
+    assert res["oneshot_equal"], res
 
 
 def test_device_wait_times_out_with_status(tmp_path):

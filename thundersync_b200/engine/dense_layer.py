@@ -30,6 +30,7 @@ from thundersync_b200.ops._ext import native
 from thundersync_b200.ops.attention import _ChunkedAttention
 from thundersync_b200.ops.linear import _Linear
 from thundersync_b200.ops.norm import _RMSNorm
+from thundersync_b200.ops.packed_attention import packed_plan, unique_chunks
 from thundersync_b200.ops.rope import _QKNormRope, rope_tables
 from thundersync_b200.ops.swiglu import _SwiGLU
 
@@ -107,6 +108,16 @@ def _unstash(ctx) -> None:
     ctx.stages = dec(ctx.stages)
 
 
+def _past_grads(plan, lens, buf) -> list:
+    """Gradients of the ancestor inputs from the ancestor rows of a key-buffer gradient: one slice per input
+    (single segment), or per unique chunk with None for its repeated inputs (packed; autograd sums the
+    inputs of one tensor, and a packed chunk's slice already holds every reader's contribution)."""
+    if plan is None:
+        return list(torch.split(buf, lens, 0)) if lens else []
+    rows = plan.chunk_rows
+    return [buf[rows[u][0]:rows[u][0] + rows[u][1]] if f else None for u, f in zip(plan.slots, plan.first)]
+
+
 class DenseLayer(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, pos, inv_freq, meta, *tensors):
@@ -127,23 +138,33 @@ class DenseLayer(torch.autograd.Function):
         # one segment from row 0 with no own-pack key ranges (a trajectory or prompt pack): on CUDA the
         # ancestors' keys/values and this pack's are laid out in one buffer, the rope kernel writes the
         # pack's rows in place and attention reads / writes every operand where it lives (no concatenation,
-        # no zero-filled gradient buffers beyond the padding rows)
+        # no zero-filled gradient buffers beyond the padding rows). Any other CUDA pack (several segments,
+        # forest key ranges) runs the same way with packed attention: the buffer holds each unique ancestor
+        # chunk once and one launch covers every segment.
         fast = (h.is_cuda and len(segs) == 1 and segs[0][0] == 0 and not segs[0][3]
                 and segs[0][2] == n_past // 2)
-        ctx.fast = fast
-        ctx.native = fast and NATIVE and qkv_fused is not None and gu_fused is not None
+        packed = h.is_cuda and not fast
+        plan = packed_plan(segs, past[:n_past // 2], past[n_past // 2:], t) if packed else None
+        ctx.fast = fast or packed
+        ctx.native = ctx.fast and NATIVE and qkv_fused is not None and gu_fused is not None
+        if ctx.fast:
+            if plan is None:
+                pk, pv = list(past[:n_past // 2]), list(past[n_past // 2:])
+                cov = segs[0][1]
+            else:
+                pk, pv = unique_chunks(plan, past[:n_past // 2]), unique_chunks(plan, past[n_past // 2:])
+                cov = plan.covered
+            lens = [x.shape[0] for x in pk]
+            sp = sum(lens)
         if ctx.native:
             # the whole layer from C++ (same kernels and GEMMs, no per-op Python dispatch)
-            npast = segs[0][2]
-            pk, pv = list(past[:npast]), list(past[npast:])
-            cov = segs[0][1]
             ct, st = rope_tables(inv_freq)
             hc = h.contiguous()
-            out, kbuf, vbuf, *saved = native().dense_layer_fwd(
+            tabs = [] if plan is None else list(plan.tables(h.device)[:2])
+            out, k, v, *saved = native().dense_layer_fwd(
                 hc, pos, inv_freq, ct, st, ln1, qkv_fused, qn, kn, wo, ln2, gu_fused, wd, pk, pv,
-                hq, hkv, d, float(eps), float(scale), int(cov))
-            sp = sum(x.shape[0] for x in pk)
-            ctx.att = (hc, pos, inv_freq, ct, st, kbuf, vbuf, saved, sp, int(cov), [x.shape[0] for x in pk])
+                hq, hkv, d, float(eps), float(scale), int(cov), tabs)
+            ctx.att = (hc, pos, inv_freq, ct, st, k, v, list(pk), list(pv), saved, sp, int(cov), lens, plan)
             ctx.params = (ln1, (wq, wk, wv), qn, kn, wo, ln2, (wg, wu), wd, qkv_fused, gu_fused)
             ctx.stages = (None,) * 9
             ctx.set_materialize_grads(False)
@@ -151,29 +172,29 @@ class DenseLayer(torch.autograd.Function):
             ctx.t = t
             ctx.out_shape, ctx.out_dtype, ctx.out_device = out.shape, out.dtype, out.device
             _stash(ctx)
-            return out, kbuf[sp:], vbuf[sp:]
+            return out, k, v
         c_n1 = _Ctx((True, need_w, False, False))
         x1 = _RMSNorm.forward(c_n1, h, ln1, eps, False)
         c_qkv = _Ctx((True, False, need_w, need_w, need_w))
         qkv = _Linear.forward(c_qkv, x1, qkv_fused, wq, wk, wv)
         c_rope = _Ctx((True, need_w, need_w) + (False,) * 9)
-        if fast:
-            npast = segs[0][2]
-            pk, pv = past[:npast], past[npast:]
-            sp = sum(x.shape[0] for x in pk)
-            kbuf = h.new_empty(sp + t, hkv, d)
-            vbuf = h.new_empty(sp + t, hkv, d)
-            if npast:
-                torch.cat(pk, 0, out=kbuf[:sp])
-                torch.cat(pv, 0, out=vbuf[:sp])
-            q, k, v = _QKNormRope.forward(c_rope, qkv, qn, kn, pos, inv_freq, hq, hkv, d, eps, False,
-                                          kbuf[sp:], vbuf[sp:])
-            cov = segs[0][1]
+        if ctx.fast:
+            # the pack's own k / v are tensors of their own (descendants keep them as state); the
+            # [ancestors | own] buffer attention reads is a temporary, rebuilt in the backward, so no
+            # event retains a copy of its ancestors' keys
+            q, k, v = _QKNormRope.forward(c_rope, qkv, qn, kn, pos, inv_freq, hq, hkv, d, eps, False)
+            kbuf = torch.cat([*pk, k], 0) if pk else k
+            vbuf = torch.cat([*pv, v], 0) if pv else v
             o = q.new_empty(t, hq, d)
-            _, lse = native().attn_fwd_tc(q[:cov], kbuf[:sp + cov], vbuf[:sp + cov], scale, o[:cov])
+            if plan is None:
+                _, lse = native().attn_fwd_tc(q[:cov], kbuf[:sp + cov], vbuf[:sp + cov], scale, o[:cov])
+            else:
+                qtab, far, _, _ = plan.tables(h.device)
+                _, lse = native().attn_fwd_packed(q, kbuf, vbuf, qtab, far, scale, o)
+            del kbuf, vbuf
             if cov < t:  # pack padding rows: no attention output
                 o[cov:].zero_()
-            ctx.att = (q, kbuf, vbuf, o, lse, sp, cov, [x.shape[0] for x in pk])
+            ctx.att = (q, k, v, list(pk), list(pv), o, lse, sp, cov, lens, plan)
             c_att = None
             return DenseLayer._forward_tail(ctx, h, o, t, hq, d, eps, need_w, c_n1, c_qkv, c_rope, c_att,
                                             wo, ln2, wg, wu, wd, gu_fused, meta, k, v)
@@ -243,24 +264,31 @@ class DenseLayer(torch.autograd.Function):
         do_, _, gwo = _Linear.backward(c_o, dh1)
         do_ = do_.reshape(t, hq, d)
         if ctx.fast:
-            q, kbuf, vbuf, o, lse, sp, cov, lens = ctx.att
+            q, k, v, pk, pv, o, lse, sp, cov, lens, plan = ctx.att
             ctx.att = None
+            kbuf = torch.cat([*pk, k], 0) if pk else k
+            vbuf = torch.cat([*pv, v], 0) if pv else v
             dq = torch.empty_like(q)
             dkbuf = torch.empty_like(kbuf)
             dvbuf = torch.empty_like(vbuf)
             if cov < t:
                 dq[cov:].zero_()
-                dkbuf[sp + cov:].zero_()
-                dvbuf[sp + cov:].zero_()
-            native().attn_bwd_tc(do_[:cov].contiguous(), q[:cov], kbuf[:sp + cov], vbuf[:sp + cov], o[:cov], lse,
-                                 scale, dq[:cov], dkbuf[:sp + cov], dvbuf[:sp + cov])
+            if plan is None:
+                if cov < t:
+                    dkbuf[sp + cov:].zero_()
+                    dvbuf[sp + cov:].zero_()
+                native().attn_bwd_tc(do_[:cov].contiguous(), q[:cov], kbuf[:sp + cov], vbuf[:sp + cov], o[:cov],
+                                     lse, scale, dq[:cov], dkbuf[:sp + cov], dvbuf[:sp + cov])
+            else:
+                native().attn_bwd_packed(do_.contiguous(), q, kbuf, vbuf, o, lse, *plan.tables(q.device), scale, dq,
+                                         dkbuf, dvbuf)
             dk, dv = dkbuf[sp:], dvbuf[sp:]
             if dk_out is not None:
                 dk.add_(dk_out)
             if dv_out is not None:
                 dv.add_(dv_out)
-            dpast_k = list(torch.split(dkbuf[:sp], lens, 0)) if lens else []
-            dpast_v = list(torch.split(dvbuf[:sp], lens, 0)) if lens else []
+            dpast_k = _past_grads(plan, lens, dkbuf[:sp])
+            dpast_v = _past_grads(plan, lens, dvbuf[:sp])
             return DenseLayer._finish(ctx, dq, dk, dv, dpast_k, dpast_v, dh1, gln2, gwo, gwg, gwu, gwd)
         covered = sum(s1 - s0 for _, s0, s1, _, _ in c_att)
         single = len(c_att) == 1 and covered == t
@@ -301,7 +329,7 @@ class DenseLayer(torch.autograd.Function):
     @staticmethod
     def _native_backward(ctx, dout, dk_out, dv_out):
         hq, hkv, d, eps, scale, segs, n_past, qkv_fused, gu_fused, has_qk = ctx.meta
-        h, pos, inv_freq, ct, st, kbuf, vbuf, saved, sp, cov, lens = ctx.att
+        h, pos, inv_freq, ct, st, k_own, v_own, pk, pv, saved, sp, cov, lens, plan = ctx.att
         ctx.att = None
         ln1, wqkv_list, qn, kn, wo, ln2, wgu_list, wd, qkv_fused, gu_fused = ctx.params
         ctx.params = None
@@ -330,13 +358,13 @@ class DenseLayer(torch.autograd.Function):
             s._side_devices.add(dev)
         res = native().dense_layer_bwd(
             dout, dk_out, dv_out, h, pos, inv_freq, ct, st, ln1, qkv_fused, qn, kn, wo, ln2, gu_fused, wd,
-            kbuf, vbuf, saved, hq, hkv, d, float(eps), float(scale), cov, sp, sinks,
-            float(s.scale) if s is not None else 1.0, side)
+            k_own, v_own, pk, pv, saved, hq, hkv, d, float(eps), float(scale), cov, sp, sinks,
+            float(s.scale) if s is not None else 1.0, side, [] if plan is None else list(plan.tables(dev)))
         dh, dkp, dvp, g_ln1, g_qkv, g_qn, g_kn, g_o, g_ln2, g_gu, g_d = res
         if s is not None:
             s.deposits += sum(1 for x in sinks if x is not None)
-        dpast_k = list(torch.split(dkp, lens, 0)) if lens else []
-        dpast_v = list(torch.split(dvp, lens, 0)) if lens else []
+        dpast_k = _past_grads(plan, lens, dkp)
+        dpast_v = _past_grads(plan, lens, dvp)
 
         def cast(g, p):
             return None if g is None or p is None else g.to(p.dtype)

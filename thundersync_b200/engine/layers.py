@@ -24,6 +24,7 @@ from typing import Any
 import torch
 
 from thundersync_b200.ops.attention import chunked_attention
+from thundersync_b200.ops.packed_attention import packed_attention
 from thundersync_b200.ops.embedding import embedding
 from thundersync_b200.ops.linear import linear
 from thundersync_b200.ops.norm import rms_norm
@@ -223,21 +224,29 @@ class Executor:
             pos, self.inv_freq(h.device), hq, hkv, d, spec.eps, unit_offset=qn is not None and _is_unit(qn),
         )
         scale = 1.0 / math.sqrt(d)
-        outs = []
-        new_state = []
-        for seg in segs:
-            s0, s1 = seg.start, seg.start + seg.length
-            ks, vs = seg.past[i] if seg.past and seg.past[i] is not None else ([], [])
-            if seg.key_ranges:
-                ks = [*ks, *(k[a:b] for a, b in seg.key_ranges)]
-                vs = [*vs, *(v[a:b] for a, b in seg.key_ranges)]
-            kn_, vn_ = k[s0:s1], v[s0:s1]
-            outs.append(chunked_attention(q[s0:s1], [*ks, kn_], [*vs, vn_], scale))
-            new_state.append((kn_, vn_))
-        covered = sum(seg.length for seg in segs)
-        if covered < qkv.shape[0]:  # pack padding rows: no attention output
-            outs.append(q.new_zeros(qkv.shape[0] - covered, hq, d))
-        o = outs[0] if len(outs) == 1 else torch.cat(outs, 0)
+        new_state = [(k[seg.start:seg.start + seg.length], v[seg.start:seg.start + seg.length]) for seg in segs]
+        if q.is_cuda and (len(segs) > 1 or segs[0].key_ranges):
+            # every segment in one packed launch (shared ancestor chunks stored and differentiated once)
+            meta, pk, pv = [], [], []
+            for seg in segs:
+                ks, vs = seg.past[i] if seg.past and seg.past[i] is not None else ([], [])
+                pk.extend(ks)
+                pv.extend(vs)
+                meta.append((seg.start, seg.start + seg.length, len(ks), tuple(seg.key_ranges)))
+            o = packed_attention(q, k, v, meta, pk, pv, scale)
+        else:
+            outs = []
+            for seg in segs:
+                s0, s1 = seg.start, seg.start + seg.length
+                ks, vs = seg.past[i] if seg.past and seg.past[i] is not None else ([], [])
+                if seg.key_ranges:
+                    ks = [*ks, *(k[a:b] for a, b in seg.key_ranges)]
+                    vs = [*vs, *(v[a:b] for a, b in seg.key_ranges)]
+                outs.append(chunked_attention(q[s0:s1], [*ks, k[s0:s1]], [*vs, v[s0:s1]], scale))
+            covered = sum(seg.length for seg in segs)
+            if covered < qkv.shape[0]:  # pack padding rows: no attention output
+                outs.append(q.new_zeros(qkv.shape[0] - covered, hq, d))
+            o = outs[0] if len(outs) == 1 else torch.cat(outs, 0)
         o = o.reshape(o.shape[0], hq * d)
         if gate is not None:
             o = o * torch.sigmoid(gate.float()).to(o.dtype)

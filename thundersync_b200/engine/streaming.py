@@ -224,7 +224,7 @@ class StreamingRun:
         self.model = model
         self.chunk = chunk
         self.boundary_cut = boundary_cut
-        self.chunked_sdpa = chunked_sdpa
+        self.chunked_sdpa = chunked_sdpa  # False: the concatenating baseline (see _retain_concatenated_chains)
         self.checkpoint = checkpoint
         self.stream_turns = stream_turns
         self.rebuild_block_tokens = rebuild_block_tokens
@@ -316,7 +316,23 @@ class StreamingRun:
                 h, states = self._run_pack_checkpointed(ids, pos, segs)
         else:
             h, states = self.exec.run(ids, pos, segs)
+        if not self.chunked_sdpa and h.grad_fn is not None:
+            self._retain_concatenated_chains(h, segs, states)
         return (h[:t] if pad else h), states
+
+    def _retain_concatenated_chains(self, h: torch.Tensor, segs: list[Segment], states: list[Any]) -> None:
+        """``chunked_sdpa=False``: keep, for as long as this pack's graph lives, each segment's concatenated
+        [ancestors | own] key/value chain per attention layer -- what a concatenate-then-attend op saves for
+        its backward. The streamed path never does this; the mode exists as the baseline that the memory
+        regression gate measures it against."""
+        keep = []
+        for seg, st in zip(segs, states):
+            for i in self.spec.attention_layers:
+                past = seg.past[i] if seg.past and seg.past[i] is not None else ([], [])
+                own = st[i]
+                keep.append(torch.cat([*past[0], own[0]], 0))
+                keep.append(torch.cat([*past[1], own[1]], 0))
+        h.grad_fn.metadata["concatenated_chains"] = keep
 
     @contextlib.contextmanager
     def _checkpoint_inputs_on_host(self):

@@ -12,6 +12,10 @@ peer memory over NVLink:
                          (``check()`` raises :class:`CollectiveTimeout`);
 * ``all_reduce_mean``    in-place deterministic two-shot all-reduce of a flat
                          fp32 buffer with the pre-scale fused into the load;
+* ``all_reduce_mean_oneshot``  every rank reads every rank's whole buffer
+                         and writes the mean to a local output: one NVLink
+                         phase instead of two, for buffers below
+                         ``ONESHOT_MAX_ELEMS`` (latency-bound sizes);
 * ``reduce_scatter``     the first half only, plus the squared norm of each
                          reduced shard exchanged through the flag buffer;
 * ``adamw_gather``       fused AdamW on this rank's shard that writes the
@@ -30,7 +34,12 @@ import torch.distributed as dist
 
 from thundersync_b200.ops._ext import native
 
-__all__ = ["SymmetricWorkspace", "NativeAllReduce", "CollectiveTimeout", "shard_bounds"]
+__all__ = ["SymmetricWorkspace", "NativeAllReduce", "CollectiveTimeout", "shard_bounds", "ONESHOT_MAX_ELEMS"]
+
+# Crossover between the one-shot and the two-shot all-reduce (fp32 elements). Below it the second
+# barrier-separated phase of the two-shot costs more than the extra (world - 1) / world of the buffer
+# that each rank reads in the one-shot; benchmarks/bench_collectives.py measures both.
+ONESHOT_MAX_ELEMS = 1 << 18
 
 _SLOTS = 64
 _MAX_RANKS = 8
@@ -109,6 +118,14 @@ class SymmetricWorkspace:
         native().symm_reduce(ptrs, self.rank, lo, hi, pre_scale / self.world, True, buf)
         self.barrier(1)
 
+    def all_reduce_mean_oneshot(self, buf: torch.Tensor, ptrs: list[int], out: torch.Tensor, *,
+                                pre_scale: float = 1.0) -> None:
+        """``out`` (local, contiguous fp32) becomes the mean over ranks of ``pre_scale * buf``; ``buf`` is
+        left as it was. The closing barrier keeps ``buf`` unchanged until every peer has read it."""
+        self.barrier(0)
+        native().symm_reduce_oneshot(ptrs, buf.numel(), pre_scale / self.world, out)
+        self.barrier(1)
+
     def reduce_scatter(self, buf: torch.Tensor, ptrs: list[int], *, pre_scale: float = 1.0) -> tuple[int, int]:
         """This rank's shard of ``buf`` becomes the mean; its squared norm goes to every rank's slot."""
         lo, hi = shard_bounds(buf.numel(), self.world, self.rank)
@@ -144,8 +161,18 @@ class NativeAllReduce:
     def create(cls, bucket_elems: int, device: torch.device, group=None) -> "NativeAllReduce":
         return cls(SymmetricWorkspace(device, group), bucket_elems)
 
-    def all_reduce_mean(self, grad: torch.Tensor, *, pre_scale: float = 1.0) -> None:
+    def all_reduce_mean(self, grad: torch.Tensor, *, pre_scale: float = 1.0, oneshot: bool | None = None) -> None:
+        """Mean over ranks of ``pre_scale * grad``, in place; one-shot below ``ONESHOT_MAX_ELEMS`` elements
+        (``oneshot`` forces either algorithm)."""
         n = grad.numel()
+        if oneshot is None:
+            oneshot = n <= ONESHOT_MAX_ELEMS
+        if oneshot and n <= self.bucket_elems and grad.is_contiguous() and grad.data_ptr() % 16 == 0:
+            view = self.bucket[:n]
+            view.copy_(grad)
+            self.ws.all_reduce_mean_oneshot(view, self.ptrs, grad, pre_scale=pre_scale)
+            self.ws.check()
+            return
         b = self.bucket_elems
         for lo in range(0, n, b):
             hi = min(n, lo + b)
