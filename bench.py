@@ -97,6 +97,33 @@ def make_step_opd(rank: int, step: int, args) -> dict:
     return {"groups": groups, "events": events, "scored": scored, "tokens": tokens}
 
 
+def opd_open_budget(args, device) -> int:
+    """How many config-4 trajectories fit on the device at once: the memory left beside the model (bf16
+    weights, fp32 master / Adam moments / gradient) over an open trajectory's retained bytes at 1.5x the
+    expected length (its K/V in bf16 plus fp32 adjoint ledgers of the same rows: 3x the K/V bytes)."""
+    from thundersync_b200.models.qwen3 import PRESETS
+
+    cfg = PRESETS[args.model]
+    c = CONFIGS[4]
+    n_params = sum(p.numel() for p in _param_shapes(cfg))
+    static = n_params * (2 + 4 + 4 + 4 + 4)
+    head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+    kv_token = 2 * cfg.num_key_value_heads * head_dim * 2 * cfg.num_hidden_layers
+    mean_actions = sum(c["actions"]) / 2
+    mean_tokens = args.prompt_len + mean_actions * (sum(c["action_tokens"]) / 2 + sum(c["observation_tokens"]) / 2)
+    total = torch.cuda.get_device_properties(device).total_memory
+    room = 0.85 * (total - static) - (8 << 30)  # 8 GB for activations and workspaces
+    return max(1, int(room // (1.5 * mean_tokens * 3 * kv_token)))
+
+
+def _param_shapes(cfg):
+    """Parameter tensors of the Qwen3 architecture ``cfg`` (meta device: shapes only)."""
+    from thundersync_b200.models.qwen3 import Qwen3ForCausalLM
+
+    with torch.device("meta"):
+        return list(Qwen3ForCausalLM(cfg).parameters())
+
+
 class OPDTrainer:
     """Config 4 driver over either package's public OPD API: a run and an ``OPDTurnStream`` per batch, the
     step's gradient (normalised by the batch's scored-token count across ranks) and the optimizer."""
@@ -105,6 +132,8 @@ class OPDTrainer:
         self.model, self.make_run, self.make_objective = model, make_run, make_objective
         self.opt, self.device, self.world = optimizer, device, world
         self.flat, self.reducer = flat, reducer
+        self.open_budget = None  # most trajectories streaming at once (None: all of the batch's)
+        self.deferred_events = 0
         self._new()
 
     def _new(self):
@@ -114,18 +143,61 @@ class OPDTrainer:
             self.obj.use_main_grad_buffer(self.reducer.main_grad_buffer())
 
     def step_batch(self, work, tail_start=None) -> dict:
-        for g, prompt, _ in work["groups"]:
-            self.obj.open_group(g, prompt)
+        """Deliver the actions in arrival order. With ``open_budget`` the rollout side streams at most that
+        many trajectories at once (each open trajectory keeps its K/V and its turn boundaries' fp32 adjoint
+        ledgers on the device until it closes): actions of a trajectory beyond the budget wait, in order,
+        until one closes. The work is unchanged; only when it reaches the trainer moves."""
+        opened: set = set()
+        waiting: dict = {}  # trajectory -> its queued events, arrival order
+        order: list = []  # trajectories waiting to open, first arrival first
         n = len(work["events"])
-        for i, (_, g, k, toks, mask, teacher, last) in enumerate(work["events"]):
-            if i == n - 1 and tail_start is not None:
-                tail_start.record()  # the step's last teacher score arrives: the tail starts
+        prompts = {g: prompt for g, prompt, _ in work["groups"]}
+        budget = self.open_budget
+        done = 0
+
+        def deliver(ev):
+            nonlocal done
+            _, g, k, toks, mask, teacher, last = ev
+            if g not in opened:
+                opened.add(g)
+                self.obj.open_group(g, prompts[g])
+            done += 1
+            if done == n and tail_start is not None:
+                tail_start.record()  # the step's last teacher score reaches the trainer: the tail starts
             self.obj.append_scored_turn(g, g, toks, mask,
                                         teacher_logprobs=torch.tensor(teacher, dtype=torch.float32).to(
                                             self.device, non_blocking=True), return_loss=False)
             if last:
                 self.obj.close_trajectory(g)
                 self.obj.close_group(g)
+                opened.discard(g)
+                return True
+            return False
+
+        def admit_waiting():
+            while order and (budget is None or len(opened) < budget):
+                g = order.pop(0)
+                for ev in waiting.pop(g):
+                    if deliver(ev):
+                        break
+
+        for ev in work["events"]:
+            g = ev[1]
+            if g in waiting:
+                waiting[g].append(ev)
+                self.deferred_events += 1
+            elif g in opened or budget is None or len(opened) < budget:
+                if deliver(ev):
+                    admit_waiting()
+            else:
+                waiting[g] = [ev]
+                order.append(g)
+                self.deferred_events += 1
+        while order:
+            before = len(order)
+            admit_waiting()
+            if len(order) == before:
+                raise RuntimeError("open-trajectory budget admits nothing")
         return self.finish()
 
     def finish(self) -> dict:
@@ -509,6 +581,8 @@ def main() -> None:
     ap.add_argument("--reward-p", type=float, default=None)
     ap.add_argument("--mean-arrival-s", type=float, default=2.0)
     ap.add_argument("--block-tokens", type=int, default=4096)
+    ap.add_argument("--opd-open-trajectories", type=int, default=0,
+                    help="config 4: most trajectories streaming at once per rank (0: from the device memory)")
     ap.add_argument("--lr", type=float, default=1e-5)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--vocab", type=int, default=151936)
@@ -596,6 +670,12 @@ def main() -> None:
             return
         raise
 
+    if args.config == 4:
+        trainer.open_budget = args.opd_open_trajectories or opd_open_budget(args, device)
+        cfg_block["open_trajectories"] = (
+            f"at most {trainer.open_budget} trajectories stream at once per rank (each keeps its K/V and fp32 "
+            f"turn-boundary adjoint ledgers on the device until it closes); later trajectories' actions wait in "
+            f"arrival order; same budget for both arms")
     extra = (1 if args.profile_out else 0) + (1 if args.cprofile_out else 0)
     mk = make_step_opd if args.config == 4 else make_step
     works = [mk(rank, s, args) for s in range(args.warmup + args.steps + extra)]

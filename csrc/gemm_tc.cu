@@ -121,10 +121,14 @@ TS_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: 
 TS_DEVICE void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory"); }
 TS_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 
-// Per-warp epilogue state: two staging buffers used alternately.
+TS_DEVICE void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+
+// Per-warp epilogue state: `nbuf` (1 or 2) staging buffers of `stride` bytes used in turn.
 struct EpiStage {
-  uint32_t buf0;  // shared::cta address of buffer 0 (buffer 1 follows at +kEpiBufBytes)
+  uint32_t buf0;  // shared::cta address of buffer 0
   int n;          // chunks issued so far
+  uint32_t stride = kEpiBufBytes;
+  int nbuf = 2;
 };
 
 // Stage this lane's 32 values (row `lane` of the chunk) and TMA-store the 32 x 32 chunk at (col, row0).
@@ -133,9 +137,13 @@ struct EpiStage {
 template <int EPI>
 TS_DEVICE void emit_chunk(EpiStage& st, const CUtensorMap* tm_c, const float* o, int col, int row0) {
   const int lane = threadIdx.x & 31;
-  const uint32_t buf = st.buf0 + (uint32_t)(st.n & 1) * kEpiBufBytes;
-  if (st.n >= 2) {
-    if (lane == 0) bulk_wait_read1();  // the store that used this buffer two chunks ago has read it
+  const uint32_t buf = st.buf0 + (uint32_t)(st.nbuf == 2 ? (st.n & 1) : 0) * st.stride;
+  if (st.n >= st.nbuf) {
+    // the store that last used this buffer has read it
+    if (lane == 0) {
+      if (st.nbuf == 2) bulk_wait_read1();
+      else bulk_wait_read0();
+    }
     __syncwarp();
   }
   if constexpr (EPI == kStoreF32 || EPI == kAccumF32) {
@@ -220,8 +228,8 @@ TS_DEVICE void emit_direct(void* c, int ldc, const float* o, int row, int col, i
 template <int EPI, bool DIRECT = false>
 TS_DEVICE void epilogue_tile(uint32_t tacc, int row, int row0, int nb, int M, int N, int ldc, float alpha,
                              const bf16* __restrict__ res, const CUtensorMap* tm_c, EpiStage& st, const LmArgs& lm,
-                             void* c = nullptr) {
-  if (row0 >= M) return;  // warp-uniform: the warp's 32-row slab lies below the output (no store is issued)
+                             void* c = nullptr, int c_begin = 0, int c_end = kBN) {
+  if (row0 >= M || c_begin >= c_end) return;  // warp-uniform: nothing of the output in this slab / range
   const int col0 = nb * kBN;
   // LM-head row state (one row per thread)
   float run_m = -INFINITY, run_s = 0.f, run_t = 0.f, row_lse = 0.f, row_g = 0.f, row_ge = 0.f, row_h = 0.f;
@@ -310,7 +318,7 @@ TS_DEVICE void epilogue_tile(uint32_t tacc, int row, int row0, int nb, int M, in
   };
   // two chunks per round: both TMEM loads (and residual loads) are in flight together, one wait
 #pragma unroll 1
-  for (int cc = 0; cc < kBN; cc += 64) {
+  for (int cc = c_begin; cc < c_end; cc += 64) {
     const int col = col0 + cc;
     if (col >= N) break;  // warp-uniform: nothing of this pair of chunks is inside the output
     const bool second = col + 32 < N;
@@ -530,8 +538,15 @@ TS_DEVICE unsigned long long gtime() {
 }
 __device__ int g_gemm_prof_on = 0;
 
+// The pair kernel's epilogue runs on 8 warps (two per TMEM sub-partition, each taking half of a tile's
+// columns; the LM-head modes keep a row's online reduction in one warp, so their second four warps only
+// take part in the barriers). Staging per warp: two 2 KB buffers for bf16 chunks, one 4 KB buffer for
+// fp32 chunks -- 32 KB in all, as with four warps.
+constexpr int kPairEpiWarps = 8;
+constexpr int kPairThreads = 64 + 32 * kPairEpiWarps;
+
 template <bool A_MN, bool B_MN, int EPI, int NT, bool DIRECT>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ CUtensorMap tm_b2, int K2,
                      const __grid_constant__ CUtensorMap tm_c, const bf16* __restrict__ res, int M, int N, int K,
@@ -561,7 +576,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&bars->acc_full[b], 1);
-      tc::mbar_init(&bars->acc_empty[b], 8);  // one arrival per epilogue warp of the pair
+      tc::mbar_init(&bars->acc_empty[b], 2 * kPairEpiWarps);  // one arrival per epilogue warp of the pair
     }
     bars->abort = 0;
     tc::fence_barrier_init();
@@ -697,10 +712,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     }
   } else {
     const int sub = warp & 3;
+    const int ew = warp - 2;         // epilogue warp 0..7
+    const int colhalf = ew >> 2;     // 0: columns [0, 128) of a tile, 1: [128, 256)
+    constexpr bool kSplit = !(EPI == kLse || EPI == kDlogits);
+    const int c_begin = kSplit ? colhalf * (kBN / 2) : (colhalf ? kBN : 0);
+    const int c_end = kSplit ? c_begin + kBN / 2 : (colhalf ? kBN : kBN);
     const uint32_t lane_base = tmem + ((uint32_t)(sub * 32) << 16);
     const uint32_t acc_empty0 = tc::map_cluster(tc::smem_addr(&bars->acc_empty[0]), 0);
     const uint32_t acc_empty1 = tc::map_cluster(tc::smem_addr(&bars->acc_empty[1]), 0);
-    EpiStage est{sbase + C::kEpiOff + (uint32_t)sub * 2 * kEpiBufBytes, 0};
+    constexpr bool kF32Out = EPI == kStoreF32 || EPI == kAccumF32;
+    EpiStage est{sbase + C::kEpiOff + (uint32_t)ew * (kEpiBytes / kPairEpiWarps), 0,
+                 kF32Out ? kEpiBufBytes : kEpiBufBytes / 2, kF32Out ? 1 : 2};
     int local = 0;
     for (int t = cid; t < tiles; t += ncl, ++local) {
       const int buf = NT == 1 ? (local & 1) : 0;
@@ -717,7 +739,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       for (int j = 0; j < NT; ++j) {
         const int half = NT == 1 ? buf : j;
         epilogue_tile<EPI, DIRECT>(lane_base + half * kBN, row0 + lane, row0, nb * NT + j, M, N, ldc, alpha, res,
-                                   &tm_c, est, lm, c);
+                                   &tm_c, est, lm, c, c_begin, c_end);
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive_cluster(half ? acc_empty1 : acc_empty0);
@@ -725,7 +747,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     }
     if (!DIRECT && lane == 0) bulk_wait_all();  // staged stores done before shared memory goes away
     __syncwarp();
-    if (prof && rank == 0 && lane == 0 && sub == 0) atomicAdd(&g_gemm_prof[cid * kProfSlots + 9], gtime() - t_entry_s);
+    if (prof && rank == 0 && lane == 0 && ew == 0) atomicAdd(&g_gemm_prof[cid * kProfSlots + 9], gtime() - t_entry_s);
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -758,7 +780,7 @@ int resident_pairs(int device, int smem) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * sm_count(device));
-    cfg.blockDim = dim3(192);
+    cfg.blockDim = dim3(kPairThreads);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -812,7 +834,7 @@ void launch_pair_cfg(int tiles, const CUtensorMap& ma, const CUtensorMap& mb, co
   const int clusters = std::max(1, std::min(tiles, pairs));
   const CUtensorMap& a2 = ma2 ? *ma2 : ma;
   const CUtensorMap& b2 = mb2 ? *mb2 : mb;
-  launch_pdl(gemm_pair_kernel<A_MN, B_MN, EPI, NT, DIRECT>, 2 * clusters, 192, smem, ma, mb, a2, b2,
+  launch_pdl(gemm_pair_kernel<A_MN, B_MN, EPI, NT, DIRECT>, 2 * clusters, kPairThreads, smem, ma, mb, a2, b2,
              ma2 ? K2 : 0, mc, res, M, N, K, ldc, alpha, tc_error_flag(at::Device(at::kCUDA, device)).data_ptr<int>(),
              lm, c);
 }
