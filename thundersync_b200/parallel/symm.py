@@ -15,7 +15,7 @@ peer memory over NVLink:
 * ``all_reduce_mean_oneshot``  every rank reads every rank's whole buffer
                          and writes the mean to a local output: one NVLink
                          phase instead of two, for buffers below
-                         ``ONESHOT_MAX_ELEMS`` (latency-bound sizes);
+                         ``oneshot_max_elems(world)`` (latency-bound sizes);
 * ``reduce_scatter``     the first half only, plus the squared norm of each
                          reduced shard exchanged through the flag buffer;
 * ``adamw_gather``       fused AdamW on this rank's shard that writes the
@@ -34,12 +34,22 @@ import torch.distributed as dist
 
 from thundersync_b200.ops._ext import native
 
-__all__ = ["SymmetricWorkspace", "NativeAllReduce", "CollectiveTimeout", "shard_bounds", "ONESHOT_MAX_ELEMS"]
+__all__ = ["SymmetricWorkspace", "NativeAllReduce", "CollectiveTimeout", "shard_bounds", "ONESHOT_MAX_ELEMS",
+           "oneshot_max_elems"]
 
-# Crossover between the one-shot and the two-shot all-reduce (fp32 elements). Below it the second
-# barrier-separated phase of the two-shot costs more than the extra (world - 1) / world of the buffer
-# that each rank reads in the one-shot; benchmarks/bench_collectives.py measures both.
-ONESHOT_MAX_ELEMS = 1 << 18
+# Crossover between the one-shot and the two-shot all-reduce, in fp32 elements per rank count. Below it
+# the second barrier-separated phase of the two-shot costs more than the extra (world - 1) / world of the
+# buffer each rank reads in the one-shot. Measured on two B200s (benchmarks/bench_collectives.py): the
+# one-shot is faster through 16 MiB (0.050 vs 0.052 ms) and slower at 256 MiB (0.443 vs 0.422 ms); the
+# one-shot's read volume grows with the world size, so the threshold scales as 1 / world.
+ONESHOT_MAX_BYTES_X_WORLD = 32 << 20
+
+
+def oneshot_max_elems(world: int) -> int:
+    return ONESHOT_MAX_BYTES_X_WORLD // (4 * max(1, world))
+
+
+ONESHOT_MAX_ELEMS = oneshot_max_elems(2)
 
 _SLOTS = 64
 _MAX_RANKS = 8
@@ -166,7 +176,7 @@ class NativeAllReduce:
         (``oneshot`` forces either algorithm)."""
         n = grad.numel()
         if oneshot is None:
-            oneshot = n <= ONESHOT_MAX_ELEMS
+            oneshot = n <= oneshot_max_elems(self.ws.world)
         if oneshot and n <= self.bucket_elems and grad.is_contiguous() and grad.data_ptr() % 16 == 0:
             view = self.bucket[:n]
             view.copy_(grad)
