@@ -48,6 +48,7 @@ import subprocess
 import sys
 import tempfile
 import time
+import time
 
 import torch
 import torch.distributed as dist
@@ -133,7 +134,8 @@ class OPDTrainer:
         self.opt, self.device, self.world = optimizer, device, world
         self.flat, self.reducer = flat, reducer
         self.open_budget = None  # most trajectories streaming at once (None: all of the batch's)
-        self.deferred_events = 0
+        self.pack_limit = 16  # most actions in one joint scored-turn pack
+        self.packs = self.packed_actions = 0
         self._new()
 
     def _new(self):
@@ -143,61 +145,68 @@ class OPDTrainer:
             self.obj.use_main_grad_buffer(self.reducer.main_grad_buffer())
 
     def step_batch(self, work, tail_start=None) -> dict:
-        """Deliver the actions in arrival order. With ``open_budget`` the rollout side streams at most that
-        many trajectories at once (each open trajectory keeps its K/V and its turn boundaries' fp32 adjoint
-        ledgers on the device until it closes): actions of a trajectory beyond the budget wait, in order,
-        until one closes. The work is unchanged; only when it reaches the trainer moves."""
-        opened: set = set()
-        waiting: dict = {}  # trajectory -> its queued events, arrival order
-        order: list = []  # trajectories waiting to open, first arrival first
-        n = len(work["events"])
+        """Deliver the actions as they arrive. The step keeps a clock: each event's arrival time is its
+        teacher score's latency after the step starts; the clock advances by the host time the trainer spends
+        on each call (idle time before an arrival is skipped, not counted). Everything that has arrived by
+        the clock and is not yet delivered is *ready*; each call hands the ready actions of distinct
+        trajectories (a trajectory's actions in order) to the objective as one joint scored-turn pack, up to
+        ``pack_limit`` actions. With ``open_budget`` at most that many trajectories stream at once (each
+        open trajectory keeps its K/V and its turn boundaries' fp32 adjoint ledgers on the device until it
+        closes); the others' actions stay ready until one closes. Same driver for both arms."""
+        events = list(work["events"])
+        n = len(events)
         prompts = {g: prompt for g, prompt, _ in work["groups"]}
         budget = self.open_budget
-        done = 0
-
-        def deliver(ev):
-            nonlocal done
-            _, g, k, toks, mask, teacher, last = ev
-            if g not in opened:
-                opened.add(g)
-                self.obj.open_group(g, prompts[g])
-            done += 1
+        opened: set = set()
+        ready: list = []
+        nxt, done, clock = 0, 0, 0.0
+        while done < n:
+            while nxt < n and events[nxt][0] <= clock:
+                ready.append(events[nxt])
+                nxt += 1
+            if not ready:
+                clock = events[nxt][0]
+                continue
+            pack, taken, blocked = [], set(), set()
+            for ev in ready:
+                g = ev[1]
+                if g in taken or g in blocked:
+                    blocked.add(g)  # this trajectory's later actions wait for the earlier one
+                    continue
+                if g not in opened and budget is not None and len(opened) + len(
+                        [x for x in taken if x not in opened]) >= budget:
+                    blocked.add(g)
+                    continue
+                pack.append(ev)
+                taken.add(g)
+                if len(pack) >= self.pack_limit:
+                    break
+            if not pack:  # every ready action waits for a slot: the open trajectories' next actions come later
+                if nxt >= n:
+                    raise RuntimeError("open-trajectory budget admits nothing")
+                clock = max(clock, events[nxt][0])
+                continue
+            t0 = time.perf_counter()
+            for ev in pack:
+                ready.remove(ev)
+                if ev[1] not in opened:
+                    opened.add(ev[1])
+                    self.obj.open_group(ev[1], prompts[ev[1]])
+            done += len(pack)
             if done == n and tail_start is not None:
                 tail_start.record()  # the step's last teacher score reaches the trainer: the tail starts
-            self.obj.append_scored_turn(g, g, toks, mask,
-                                        teacher_logprobs=torch.tensor(teacher, dtype=torch.float32).to(
-                                            self.device, non_blocking=True), return_loss=False)
-            if last:
-                self.obj.close_trajectory(g)
-                self.obj.close_group(g)
-                opened.discard(g)
-                return True
-            return False
-
-        def admit_waiting():
-            while order and (budget is None or len(opened) < budget):
-                g = order.pop(0)
-                for ev in waiting.pop(g):
-                    if deliver(ev):
-                        break
-
-        for ev in work["events"]:
-            g = ev[1]
-            if g in waiting:
-                waiting[g].append(ev)
-                self.deferred_events += 1
-            elif g in opened or budget is None or len(opened) < budget:
-                if deliver(ev):
-                    admit_waiting()
-            else:
-                waiting[g] = [ev]
-                order.append(g)
-                self.deferred_events += 1
-        while order:
-            before = len(order)
-            admit_waiting()
-            if len(order) == before:
-                raise RuntimeError("open-trajectory budget admits nothing")
+            items = [(g, g, toks, mask, torch.tensor(teacher, dtype=torch.float32).to(self.device, non_blocking=True),
+                      None) for _, g, _, toks, mask, teacher, _ in pack]
+            self.obj.append_scored_turns(items, return_loss=False)
+            closing = [ev[1] for ev in pack if ev[6]]
+            if closing:
+                self.obj.close_trajectories(closing)
+                for g in closing:
+                    self.obj.close_group(g)
+                    opened.discard(g)
+            self.packs += 1
+            self.packed_actions += len(pack)
+            clock += time.perf_counter() - t0
         return self.finish()
 
     def finish(self) -> dict:
@@ -672,6 +681,10 @@ def main() -> None:
 
     if args.config == 4:
         trainer.open_budget = args.opd_open_trajectories or opd_open_budget(args, device)
+        cfg_block["delivery"] = (
+            "each action reaches the trainer at its teacher-score arrival time on a clock advanced by the "
+            f"trainer's host time per call; the ready actions of distinct trajectories go in one joint "
+            f"scored-turn pack (at most {trainer.pack_limit}); same driver for both arms")
         cfg_block["open_trajectories"] = (
             f"at most {trainer.open_budget} trajectories stream at once per rank (each keeps its K/V and fp32 "
             f"turn-boundary adjoint ledgers on the device until it closes); later trajectories' actions wait in "
