@@ -261,9 +261,10 @@ def bench_fold(args) -> None:
 
 def bench_gemm(args) -> None:
     """tcgen05 GEMM variants vs the library GEMM on the decoder's projection shapes: CTA pairs with the automatic
-    256x256 / 256x512 tile choice (the default), 256x256 only, 256x512 only, and the single-CTA 128x256 kernel."""
+    256x256 / 256x512 tile choice, 256x256 only, 256x512 only, and the single-CTA 128x256 kernel. Variants run
+    one after another: compare within a line (``gemm_ab`` interleaves them)."""
     ext = native()
-    variants = [("CTA pair, automatic tile (default)", 1, 1), ("CTA pair, 256x256 tiles", 1, 0),
+    variants = [("CTA pair, automatic 256x256 / 256x512 choice", 1, 1), ("CTA pair, 256x256 tiles", 1, 0),
                 ("CTA pair, 256x512 tiles", 1, 2), ("single CTA, 128x256 tiles", 0, 0)]
     for name, pair, wide in variants:
         prev, prev_w = ext.gemm_tc_pair(pair), ext.gemm_tc_wide(wide)
@@ -273,6 +274,71 @@ def bench_gemm(args) -> None:
         finally:
             ext.gemm_tc_pair(prev)
             ext.gemm_tc_wide(prev_w)
+
+
+def bench_gemm_ab(args) -> None:
+    """Interleaved A/B of tcgen05 GEMM launch variants at the projection shapes: for each shape the variants
+    (kernel selection settings) alternate, ``--rounds`` rounds of ``--iters`` launches each, and the median
+    per variant is reported next to the library GEMM timed in the same rounds. Clock changes under the power
+    cap then shift every variant of a shape alike, which a variant-by-variant sweep does not guarantee."""
+    from thundersync_b200.ops.gemm import gemm, gemm_accumulate
+
+    ext = native()
+    variants = {"by output mode (default)": dict(pair=2, wide=0, epi=1),
+                "pair 256x256, 4 epilogue warps": dict(pair=1, wide=0, epi=0),
+                "pair 256x256, 8 epilogue warps for bf16": dict(pair=1, wide=0, epi=1),
+                "single CTA 128x256": dict(pair=0, wide=0, epi=1)}
+    m = args.rows
+    cases = []
+    for name, n, k in [("qkv fwd", 4096, 2048), ("o fwd", 2048, 2048), ("gate/up fwd", 12288, 2048),
+                       ("down fwd", 2048, 6144)]:
+        x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16)
+        cases.append((f"{name} {m}x{n}x{k}", 2.0 * m * n * k, (lambda x=x, w=w: gemm(x, w)),
+                      (lambda x=x, w=w: torch.nn.functional.linear(x, w))))
+    for name, n, k in (("dW qkv", 4096, 2048), ("dW gate/up", 12288, 2048)):
+        dy = torch.randn(m, n, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        acc = torch.zeros(n, k, device="cuda")
+        cases.append((f"{name} {n}x{k}x{m} fp32+=", 2.0 * m * n * k,
+                      (lambda a=acc, dy=dy, x=x: gemm_accumulate(a, dy, x, a_t=True, b_t=False)),
+                      (lambda a=acc, dy=dy, x=x: torch.addmm(a, dy.t(), x, out_dtype=torch.float32, out=a))))
+    for name, n, k in (("dx qkv", 2048, 4096), ("dx down", 6144, 2048)):
+        dy = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(k, n, device="cuda", dtype=torch.bfloat16)  # the weight [out, in]: dx = dy · W
+        cases.append((f"{name} {m}x{n}x{k}", 2.0 * m * n * k, (lambda dy=dy, w=w: gemm(dy, w, b_t=False)),
+                      (lambda dy=dy, w=w: torch.matmul(dy, w))))
+    prev = (ext.gemm_tc_pair(-1), ext.gemm_tc_wide(-1), ext.gemm_tc_epi8(-1))
+    try:
+        for label, flops, ours, lib in cases:
+            times = {v: [] for v in variants}
+            times["library"] = []
+            for _ in range(args.rounds):
+                for v, cfg in variants.items():
+                    ext.gemm_tc_pair(cfg["pair"])
+                    ext.gemm_tc_wide(cfg["wide"])
+                    ext.gemm_tc_epi8(cfg["epi"])
+                    times[v].append(_time(ours, args.iters))
+                times["library"].append(_time(lib, args.iters))
+            med = {v: sorted(t)[len(t) // 2] for v, t in times.items()}
+            cells = ", ".join(f"{v}: {flops / med[v] / 1e9:.0f}" for v in times)
+            print(f"{label}: TFLOP/s {cells}")
+    finally:
+        ext.gemm_tc_pair(prev[0])
+        ext.gemm_tc_wide(prev[1])
+        ext.gemm_tc_epi8(prev[2])
+
+
+def bench_gemm_one(args) -> None:
+    """One projection GEMM, x [rows, cols] · Wᵀ with W [n, cols] (bf16 out), with the default kernel selection;
+    the small case an ncu capture of a single launch runs on."""
+    from thundersync_b200.ops.gemm import gemm
+
+    x = torch.randn(args.rows, args.cols, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(args.n, args.cols, device="cuda", dtype=torch.bfloat16)
+    ms = _time(lambda: gemm(x, w), args.iters)
+    print(f"gemm {args.rows}x{args.n}x{args.cols}: {ms:.4f} ms  {2.0 * args.rows * args.n * args.cols / ms / 1e9:.1f} "
+          "TFLOP/s")
 
 
 def _bench_gemm_shapes(args) -> None:
@@ -479,7 +545,7 @@ def bench_gemm_host(args) -> None:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host", "swiglu", "rope", "dlogits",
-                                       "adamw", "fold", "gemm", "lmhead", "baselines", "lora", "layer_host"])
+                                       "adamw", "fold", "gemm", "gemm_ab", "gemm_one", "lmhead", "baselines", "lora", "layer_host"])
     ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
     ap.add_argument("--t", type=int, default=2048)
     ap.add_argument("--s", type=int, default=2560)
@@ -489,13 +555,15 @@ def main(argv=None) -> None:
     ap.add_argument("--h", type=int, default=16)
     ap.add_argument("--rows", type=int, default=16384)
     ap.add_argument("--cols", type=int, default=2048)
+    ap.add_argument("--n", type=int, default=4096, help="gemm_one: output columns")
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--rounds", type=int, default=5, help="gemm_ab: interleaved rounds per variant")
     ap.add_argument("--trace", action="store_true", help="lora: per-kernel device times of one forward+backward")
     ap.add_argument("--kernels", action="store_true", help="attn: per-kernel device times of one backward")
     args = ap.parse_args(argv)
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
      "gemm_host": bench_gemm_host, "swiglu": bench_swiglu, "rope": bench_rope, "dlogits": bench_dlogits,
-     "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm,
+     "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm, "gemm_ab": bench_gemm_ab, "gemm_one": bench_gemm_one,
      "lmhead": bench_lmhead, "baselines": bench_baselines, "lora": bench_lora,
      "layer_host": bench_layer_host}[args.family](args)
 

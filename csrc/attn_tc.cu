@@ -7,11 +7,13 @@
 //               S buffers, O += P V into the TMEM O accumulator; commits
 //               signal the other roles through mbarriers
 //   warps 0-7   softmax: a pair of warps owns 32 query rows (one TMEM
-//               sub-partition); both read the full S row for the max, each
-//               exponentiates one 64-column half (online max/sum in the log2
-//               domain, bottom-right mask), writes its half of P (bf16) into
-//               a double-buffered K-major SW128 shared tile, and rescales its
-//               half of the O row in TMEM only when the row max moved
+//               sub-partition); each reads one half of the S row, the two
+//               half maxima are exchanged through shared memory (an
+//               mbarrier per pair), each exponentiates its half (online
+//               max/sum in the log2 domain, bottom-right mask) and writes P
+//               back into tensor memory as bf16 pairs over the S columns it
+//               read -- the A operand of O += P V -- and rescales its half
+//               of the O row only when the row max moved
 // The tensor core computes S(j+1) while the softmax warps work on S(j), and
 // PV(j) while they work on S(j+1). Epilogue: O / l (bf16) and the natural-log
 // LSE. Every mbarrier wait is bounded (see tc.cuh).
@@ -30,9 +32,6 @@ typedef __nv_bfloat16 bf16;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-TS_DEVICE void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
 // 2^x with the SM's native ex2 unit (flush-to-zero); inputs here are <= 0 after the
 // max/LSE shift, and outputs below the normal range contribute nothing in bf16.
 TS_DEVICE float ex2(float x) {
@@ -208,21 +207,27 @@ struct FwdLayout {
   static constexpr uint32_t K_BYTES = BN * D * 2;
   static constexpr uint32_t K0 = Q + Q_BYTES;
   static constexpr uint32_t V0 = K0 + 2 * K_BYTES;
-  static constexpr uint32_t P0 = V0 + 2 * K_BYTES;
-  static constexpr uint32_t P_BYTES = BM * BN * 2;
-  static constexpr uint32_t BAR = P0 + 2 * P_BYTES;
-  static constexpr uint32_t RED = BAR + 256;  // [2][128] floats: the pair's partial row sums
-  static constexpr uint32_t TOTAL = RED + 1024;
-  // TMEM columns
+  static constexpr uint32_t BAR = V0 + 2 * K_BYTES;
+  static constexpr uint32_t RED = BAR + 256;     // [2][128] floats: the pair's partial row sums
+  static constexpr uint32_t XMAX = RED + 1024;   // [2 tile parities][2 halves][128] floats: half-row maxima
+  static constexpr uint32_t TOTAL = XMAX + 2048;
+  // TMEM columns: two S buffers (P is written back over the S columns its warp read, as bf16 pairs, and is
+  // the A operand of O += P V from there) and the O accumulator
   static constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256;
+  // TMEM column of the A operand for the kk-th 16-key step of P: half h = kk*16 / HALF lives at
+  // S + h*HALF (HALF / 2 columns of bf16 pairs)
+  static TS_DEVICE uint32_t p_col(int kk) { return (kk * 16 / HALF) * HALF + ((kk * 16) % HALF) / 2; }
 };
 static_assert(FwdLayout<256>::TOTAL + 1024 <= 232448, "forward shared memory exceeds 227 KB");
 
 struct FwdBars {
   uint64_t q, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv[2];
+  uint64_t xbar[4][2];  // per TMEM sub-partition and tile parity: both warps of the pair posted their half max
   uint32_t tmem_slot;
   int abort;
 };
+
+static_assert(sizeof(FwdBars) <= 256, "forward barrier block");
 
 template <int D>
 __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -257,6 +262,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       tc::mbar_init(&bars->s_full[i], 1);
       tc::mbar_init(&bars->p_full[i], 256);
       tc::mbar_init(&bars->pv[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      tc::mbar_init(&bars->xbar[i][0], 64);
+      tc::mbar_init(&bars->xbar[i][1], 64);
     }
     bars->abort = 0;
     tc::fence_barrier_init();
@@ -318,13 +327,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         if (!tc::mbar_wait(&bars->p_full[s], (j >> 1) & 1, abort, err, 23)) break;
         if (!tc::mbar_wait(&bars->v_full[s], (j >> 1) & 1, abort, err, 24)) break;
         tc::tc_fence_after();
-        const uint32_t pb = sbase + L::P0 + s * L::P_BYTES;
+        const uint32_t pcol = tmem + (s ? L::S_COL1 : L::S_COL0);
         const uint32_t vb = sbase + L::V0 + s * L::K_BYTES;
 #pragma unroll
         for (int kk = 0; kk < L::BN / 16; ++kk) {
-          const uint64_t a = tc::sdesc_sw128(pb + (kk >> 2) * L::BM * 128 + (kk & 3) * 32, 16, 1024);
           const uint64_t b = tc::sdesc_sw128(vb + kk * 16 * 128, L::BN * 128, 1024);
-          tc::mma_bf16(tmem + L::O_COL, a, b, id_o, j > 0 || kk > 0);
+          tc::mma_bf16_ts(tmem + L::O_COL, pcol + L::p_col(kk), b, id_o, j > 0 || kk > 0);
         }
         tc::mma_commit(&bars->pv[s]);
         tc::mma_commit(&bars->kv_empty[s]);
@@ -343,30 +351,38 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
     float* lsum = reinterpret_cast<float*>(smem + L::RED);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
+    float* xmax = reinterpret_cast<float*>(smem + L::XMAX);
+    uint64_t* xbar = bars->xbar[warp & 3];
     for (int j = 0; j < n && ok; ++j, walk.next()) {
       const int s = j & 1;
       if (!warp_wait(&bars->s_full[s], (j >> 1) & 1, abort, err, 31)) { ok = false; break; }
       tc::tc_fence_after();
-      float sv[L::BN];
+      // this warp's half of the tile's columns
+      float sv[L::HALF];
       const uint32_t scol = s ? L::S_COL1 : L::S_COL0;
+      const uint32_t hcol = lane_base + scol + hc * L::HALF;
 #pragma unroll
-      for (int c = 0; c < L::BN / 32; ++c) tc::tmem_ld32(lane_base + scol + c * 32, sv + c * 32);
+      for (int c = 0; c < L::HALF; c += 32) tc::tmem_ld<(L::HALF < 32 ? L::HALF : 32)>(hcol + c, sv + c);
       tc::tmem_ld_wait();
-      const int nvis = walk.nvis(qi);  // visible columns of this tile for this row
-      // row max over the tile as 8 independent chains (a single fmaxf chain of BN links serialises on
-      // the instruction latency; the chains are combined at the end)
+      const int nv_half = walk.nvis(qi) - hc * L::HALF;  // visible columns of this warp's half for this row
+      // half-row max as 8 independent chains (a single fmaxf chain serialises on the instruction latency)
       float mx8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
-      if (nvis == L::BN) {
+      if (nv_half >= L::HALF) {
 #pragma unroll
-        for (int i = 0; i < L::BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+        for (int i = 0; i < L::HALF; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < L::BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], i < nvis ? sv[i] : -INFINITY);
+        for (int i = 0; i < L::HALF; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], i < nv_half ? sv[i] : -INFINITY);
       }
-      const float raw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float hmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      // the partner warp (same rows, other half) posts its half max; both then hold the same row max
+      xmax[(s * 2 + hc) * 128 + r] = hmax;
+      tc::mbar_arrive(&xbar[s]);
+      if (!warp_wait(&xbar[s], (j >> 1) & 1, abort, err, 35)) { ok = false; break; }
+      const float raw = fmaxf(hmax, xmax[(s * 2 + (hc ^ 1)) * 128 + r]);
       // the exponent reference moves only when the running max grows by more than 8 (a factor 2^8): P
       // stays <= 256 (exact in bf16's range, and the fp32 sums absorb it), and O is rescaled only then
       const float cand = fmaxf(m, raw * sl2);
@@ -374,17 +390,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       const float mx = bump ? cand : m;
       const float ref = mx == -INFINITY ? 0.f : mx;
       const float alpha = bump ? ex2(m - ref) : 1.f;
-      // P buffer s is free once PV(j - 2) has read it
-      if (j >= 2 && !warp_wait(&bars->pv[s], ((j - 2) >> 1) & 1, abort, err, 34)) { ok = false; break; }
-      // this warp's half of the tile's columns, reloaded into registers with static indices
-#pragma unroll
-      for (int c = 0; c < L::HALF / 32; ++c) tc::tmem_ld32(lane_base + scol + hc * L::HALF + c * 32, sv + c * 32);
-      tc::tmem_ld_wait();
-      const int nv_half = nvis - hc * L::HALF;
+      // P of this half, as bf16 pairs over the first HALF / 2 columns of the same half of S (columns this
+      // warp has already read; the S(j + 2) MMA that next writes them is issued after PV(j) has read them)
       float rs8[8];  // 8 independent partial sums, for the same reason as the max
 #pragma unroll
       for (int e = 0; e < 8; ++e) rs8[e] = 0.f;
-      const uint32_t pbase = sbase + L::P0 + s * L::P_BYTES;
+      float pw[L::HALF / 2];
 #pragma unroll
       for (int c8 = 0; c8 < L::HALF / 8; ++c8) {
         float p[8];
@@ -394,9 +405,11 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
           p[e] = i < nv_half ? ex2(fmaf(sv[i], sl2, -ref)) : 0.f;
           rs8[e] += p[e];
         }
-        st_shared_v4(pbase + tc::kmajor_off(r, hc * L::HALF + c8 * 8, 128), pack2(p[0], p[1]), pack2(p[2], p[3]),
-                     pack2(p[4], p[5]), pack2(p[6], p[7]));
+#pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) pw[c8 * 4 + q2] = __uint_as_float(pack2(p[2 * q2], p[2 * q2 + 1]));
       }
+      if constexpr (L::HALF / 2 == 32) tc::tmem_st32(hcol, pw);
+      else tc::tmem_st16(hcol, pw);
       const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
       if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
@@ -412,11 +425,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
             tc::tmem_st32(lane_base + L::O_COL + c * 32, o);
           }
-          tc::tmem_st_wait();
         }
       }
+      tc::tmem_st_wait();
       m = mx;
-      tc::fence_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->p_full[s]);
     }

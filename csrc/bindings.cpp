@@ -82,6 +82,7 @@ std::vector<at::Tensor> gdn_chunk_bwd(const at::Tensor& dout, const at::Tensor& 
                                       const at::Tensor& tsv, const at::Tensor& psv, const at::Tensor& kd,
                                       const at::Tensor& kb);
 int64_t gemm_tc_pair(int64_t on);
+int64_t gemm_tc_epi8(int64_t mode);
 int64_t gemm_tc_wide(int64_t mode);
 int64_t gemm_tc_direct(int64_t on);
 int64_t gemm_tc_pdl(int64_t on);
@@ -181,6 +182,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("residual") = pybind11::none());
   m.def("lmhead_lse_tc", &ts::lmhead_lse_tc);
   m.def("gemm_tc_pair", &ts::gemm_tc_pair);
+  m.def("gemm_tc_epi8", &ts::gemm_tc_epi8);
   m.def("gemm_tc_wide", &ts::gemm_tc_wide);
   m.def("gemm_tc_direct", &ts::gemm_tc_direct);
   m.def("gemm_tc_pdl", &ts::gemm_tc_pdl);

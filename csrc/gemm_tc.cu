@@ -538,11 +538,12 @@ TS_DEVICE unsigned long long gtime() {
 }
 __device__ int g_gemm_prof_on = 0;
 
-// The pair kernel's epilogue runs on 8 warps (two per TMEM sub-partition, each taking half of a tile's
-// columns; the LM-head modes keep a row's online reduction in one warp, so their second four warps only
-// take part in the barriers). Staging per warp: two 2 KB buffers for bf16 chunks, one 4 KB buffer for
-// fp32 chunks -- 32 KB in all, as with four warps.
-constexpr int kPairEpiWarps = 8;
+// The pair kernel's epilogue runs on `epi_warps` warps, 4 or 8 (chosen per launch). With 8, two warps
+// share each TMEM sub-partition and take half of a tile's columns each; staging per warp is two 2 KB
+// buffers for bf16 chunks or one 4 KB buffer for fp32 chunks. With 4 (and in the LM-head modes, which
+// keep a row's online reduction in one warp), one warp per sub-partition covers all columns with two 4 KB
+// buffers. Either way the staging takes 32 KB.
+constexpr int kPairEpiWarps = 8;  // most epilogue warps of a launch
 constexpr int kPairThreads = 64 + 32 * kPairEpiWarps;
 
 template <bool A_MN, bool B_MN, int EPI, int NT, bool DIRECT>
@@ -550,7 +551,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ CUtensorMap tm_b2, int K2,
                      const __grid_constant__ CUtensorMap tm_c, const bf16* __restrict__ res, int M, int N, int K,
-                     int ldc, float alpha, int* __restrict__ err, LmArgs lm, void* __restrict__ c) {
+                     int ldc, float alpha, int* __restrict__ err, LmArgs lm, void* __restrict__ c, int epi_warps) {
   using C = PairCfg<NT, DIRECT>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -576,7 +577,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&bars->acc_full[b], 1);
-      tc::mbar_init(&bars->acc_empty[b], 2 * kPairEpiWarps);  // one arrival per epilogue warp of the pair
+      tc::mbar_init(&bars->acc_empty[b], 2 * epi_warps);  // one arrival per epilogue warp of the pair
     }
     bars->abort = 0;
     tc::fence_barrier_init();
@@ -712,17 +713,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
   } else {
     const int sub = warp & 3;
-    const int ew = warp - 2;         // epilogue warp 0..7
-    const int colhalf = ew >> 2;     // 0: columns [0, 128) of a tile, 1: [128, 256)
-    constexpr bool kSplit = !(EPI == kLse || EPI == kDlogits);
-    const int c_begin = kSplit ? colhalf * (kBN / 2) : (colhalf ? kBN : 0);
-    const int c_end = kSplit ? c_begin + kBN / 2 : (colhalf ? kBN : kBN);
+    const int ew = warp - 2;         // epilogue warp 0 .. epi_warps-1
+    const int colhalf = ew >> 2;     // with 8 warps: 0 for columns [0, 128) of a tile, 1 for [128, 256)
+    const bool split = epi_warps == 8 && !(EPI == kLse || EPI == kDlogits);
+    const int c_begin = split ? colhalf * (kBN / 2) : (colhalf ? kBN : 0);
+    const int c_end = split ? c_begin + kBN / 2 : kBN;
     const uint32_t lane_base = tmem + ((uint32_t)(sub * 32) << 16);
     const uint32_t acc_empty0 = tc::map_cluster(tc::smem_addr(&bars->acc_empty[0]), 0);
     const uint32_t acc_empty1 = tc::map_cluster(tc::smem_addr(&bars->acc_empty[1]), 0);
     constexpr bool kF32Out = EPI == kStoreF32 || EPI == kAccumF32;
-    EpiStage est{sbase + C::kEpiOff + (uint32_t)ew * (kEpiBytes / kPairEpiWarps), 0,
-                 kF32Out ? kEpiBufBytes : kEpiBufBytes / 2, kF32Out ? 1 : 2};
+    EpiStage est = split ? EpiStage{sbase + C::kEpiOff + (uint32_t)ew * (kEpiBytes / 8), 0,
+                                    kF32Out ? kEpiBufBytes : kEpiBufBytes / 2, kF32Out ? 1 : 2}
+                         : EpiStage{sbase + C::kEpiOff + (uint32_t)(ew & 3) * (kEpiBytes / 4), 0, kEpiBufBytes, 2};
     int local = 0;
     for (int t = cid; t < tiles; t += ncl, ++local) {
       const int buf = NT == 1 ? (local & 1) : 0;
@@ -759,8 +761,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   if (prof && rank == 0 && threadIdx.x == 0) atomicAdd(&g_gemm_prof[cid * kProfSlots + 10], gtime() - t_entry_s);
 }
 
-// 0: single-CTA 128 x 256 tiles; 1: CTA-pair 256 x 256 tiles (default)
-int g_gemm_pair = 1;
+// 0: single-CTA 128 x 256 tiles; 1: CTA-pair 256 x 256 tiles; 2 (default): by output mode -- single-CTA
+// tiles for bf16 / fp32 stores (projections, dx), CTA pairs for fp32 accumulation into a gradient sink
+// (dW) and the LM-head epilogues. Interleaved measurements at the decoder's shapes
+// (benchmarks/bench_kernels.py gemm_ab): the single-CTA kernel is 9-16% faster on the forward projections
+// at 2304 rows and 19-80% faster at 1152 rows (twice the tiles: far better wave fill for short packs),
+// the pair kernel 3-7% faster on the fp32-accumulate dW products.
+int g_gemm_pair = 2;
+
+inline bool use_pair(int epi) { return g_gemm_pair == 1 || (g_gemm_pair == 2 && epi != kStoreBf16 && epi != kStoreF32); }
 
 // 0: never the wide (256 x 512) pair tile (default: measured slower than 256 x 256 at every decoder
 // shape); 1: when it fills the SMs' waves at least as well; 2: always (measurement)
@@ -800,6 +809,10 @@ int resident_pairs(int device, int smem) {
   return pairs;
 }
 
+// Epilogue warps of the pair kernel: 0 = four everywhere; 1 (default) = eight for bf16 outputs (fp32 and
+// LM-head modes keep four with double-buffered 4 KB staging); 2 = eight for every store / accumulate mode.
+int g_gemm_epi8 = 1;
+
 // 1 (default): launch the GEMM kernels with programmatic stream serialization, so a GEMM's launch and set-up
 // overlap the previous kernel's completion when that kernel allows it (ours do); 0: plain stream order.
 int g_gemm_pdl = 1;
@@ -834,9 +847,13 @@ void launch_pair_cfg(int tiles, const CUtensorMap& ma, const CUtensorMap& mb, co
   const int clusters = std::max(1, std::min(tiles, pairs));
   const CUtensorMap& a2 = ma2 ? *ma2 : ma;
   const CUtensorMap& b2 = mb2 ? *mb2 : mb;
-  launch_pdl(gemm_pair_kernel<A_MN, B_MN, EPI, NT, DIRECT>, 2 * clusters, kPairThreads, smem, ma, mb, a2, b2,
+  int epi = 4;
+  if (!DIRECT && ((g_gemm_epi8 >= 1 && EPI == kStoreBf16) ||
+                  (g_gemm_epi8 == 2 && (EPI == kStoreF32 || EPI == kAccumF32))))
+    epi = 8;
+  launch_pdl(gemm_pair_kernel<A_MN, B_MN, EPI, NT, DIRECT>, 2 * clusters, 64 + 32 * epi, smem, ma, mb, a2, b2,
              ma2 ? K2 : 0, mc, res, M, N, K, ldc, alpha, tc_error_flag(at::Device(at::kCUDA, device)).data_ptr<int>(),
-             lm, c);
+             lm, c, epi);
 }
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -953,10 +970,18 @@ int64_t gemm_tc_wide(int64_t mode) {
   return prev;
 }
 
-// Select the GEMM kernel: 1 = CTA-pair 256 x 256 tiles, 0 = single-CTA 128 x 256 tiles. Returns the previous value.
+// Epilogue warps of the pair kernel (see g_gemm_epi8): 0, 1 or 2; returns the previous value (-1 reads it).
+int64_t gemm_tc_epi8(int64_t mode) {
+  const int prev = g_gemm_epi8;
+  if (mode >= 0) g_gemm_epi8 = (int)std::min<int64_t>(mode, 2);
+  return prev;
+}
+
+// Select the GEMM kernel: 1 = CTA-pair 256 x 256 tiles, 0 = single-CTA 128 x 256 tiles, 2 = by output mode
+// (g_gemm_pair). Returns the previous value (-1 reads it).
 int64_t gemm_tc_pair(int64_t on) {
   const int prev = g_gemm_pair;
-  if (on >= 0) g_gemm_pair = on ? 1 : 0;
+  if (on >= 0) g_gemm_pair = (int)std::min<int64_t>(on, 2);
   return prev;
 }
 
@@ -983,7 +1008,7 @@ std::vector<at::Tensor> lmhead_lse_tc(const at::Tensor& h, const at::Tensor& w, 
   LmArgs lm{tgt.data_ptr<int64_t>(), pm.data_ptr<float>(), ps.data_ptr<float>(),
             with_entropy ? pt.data_ptr<float>() : nullptr, tl.data_ptr<float>(), nullptr, nullptr, nullptr, nullptr,
             ntiles};
-  const bool pair = g_gemm_pair != 0;
+  const bool pair = use_pair(kLse);
   const CUtensorMap ma = make_bf16_map(h.data_ptr(), D, R, D, 128);
   const CUtensorMap mb = make_bf16_map(w.data_ptr(), D, V, D, pair ? 128 : 256);
   // the LSE epilogue stores nothing; its output map is a placeholder
@@ -1010,7 +1035,7 @@ at::Tensor lmhead_dlogits_tc(const at::Tensor& h, const at::Tensor& w, const at:
   if (R == 0) return d;
   LmArgs lm{tgt.data_ptr<int64_t>(), nullptr, nullptr, nullptr, nullptr, lse.data_ptr<float>(), glp.data_ptr<float>(),
             gent ? gent->data_ptr<float>() : nullptr, ent ? ent->data_ptr<float>() : nullptr, 0};
-  const bool pair = g_gemm_pair != 0;
+  const bool pair = use_pair(kDlogits);
   const CUtensorMap ma = make_bf16_map(h.data_ptr(), D, R, D, 128);
   const CUtensorMap mb = make_bf16_map(w.data_ptr(), D, V, D, pair ? 128 : 256);
   const CUtensorMap md = make_out_map(d.data_ptr(), false, V, R, V);
@@ -1085,7 +1110,7 @@ void gemm_tc_cat(at::Tensor& out, const at::Tensor& a, const at::Tensor& b, cons
     return;
   }
   // tensor maps: inner dimension first; boxes of 64 inner elements
-  const bool pair = g_gemm_pair != 0;
+  const bool pair = use_pair(mode == 0 ? kStoreBf16 : mode == 1 ? kStoreF32 : kAccumF32);
   auto amap = [&](const at::Tensor& t, int k) {
     return a_t ? make_bf16_map(t.data_ptr(), M, k, M, 64) : make_bf16_map(t.data_ptr(), k, M, k, 128);
   };

@@ -238,15 +238,18 @@ __global__ void __launch_bounds__(256) rms_dw_partial_kernel(const T* __restrict
   }
 }
 
-// out[c] = sum_k partial[k, c]: block (32 x 8) covers 32 columns; warp row y
-// sums chunks y, y+8, ... and the 8 row sums are added in y order, so the
-// result is the same every run.
+// out[c] = sum_k partial[k, c]: block (32 x kSumRows) covers 32 columns; warp row y
+// sums chunks y, y + kSumRows, ... and the kSumRows row sums are added in y
+// order, so the result is the same every run. (32 warps per block: these
+// grids have only H / 32 blocks, so the loads in flight per block set the pace.)
 // lane_e > 0: partial rows are in the lane-major order of rms_bwd_fused_kernel (row length H, an index
 // p there is column ((p / 32) / lane_e * 32 + p % 32) * lane_e + (p / 32) % lane_e; out has `cols` entries).
-__global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restrict__ partial, float* __restrict__ out,
-                                                           int chunks, int H, float scale = 1.f, int accumulate = 0,
-                                                           int lane_e = 0, int cols = 0) {
-  __shared__ float red[8][33];
+constexpr int kSumRows = 32;
+__global__ void __launch_bounds__(32 * kSumRows) sum_partials_kernel(const float* __restrict__ partial,
+                                                                    float* __restrict__ out, int chunks, int H,
+                                                                    float scale = 1.f, int accumulate = 0,
+                                                                    int lane_e = 0, int cols = 0) {
+  __shared__ float red[kSumRows][33];
   const int p = blockIdx.x * 32 + threadIdx.x;
   int c = p;
   if (lane_e > 0) {
@@ -255,13 +258,13 @@ __global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restri
   }
   float s = 0.f;
   if (p < H)
-    for (int k = threadIdx.y; k < chunks; k += 8) s += partial[(size_t)k * H + p];
+    for (int k = threadIdx.y; k < chunks; k += kSumRows) s += partial[(size_t)k * H + p];
   red[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
   if (threadIdx.y == 0 && p < H && (lane_e == 0 || c < cols)) {
     float t = 0.f;
 #pragma unroll
-    for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
+    for (int y = 0; y < kSumRows; ++y) t += red[y][threadIdx.x];
     out[c] = accumulate ? out[c] + scale * t : t;  // accumulate: into a gradient sink, scaled
   }
 }
@@ -300,7 +303,7 @@ at::Tensor column_weight_grad(const at::Tensor& dy, const at::Tensor& x, const a
   rms_dw_partial_kernel<T><<<dim3(col_blocks, chunks), dim3(32, 8), 0, stream()>>>(
       (const T*)dy.data_ptr(), (const T*)x.data_ptr(), rstd.data_ptr<float>(), partial.data_ptr<float>(), rows, H,
       rows_per_chunk);
-  sum_partials_kernel<<<(H + 31) / 32, dim3(32, 8), 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
+  sum_partials_kernel<<<(H + 31) / 32, dim3(32, kSumRows), 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
                                                                      chunks, H);
   return dw;
 }
@@ -343,7 +346,7 @@ at::Tensor launch_rms_bwd_fused(const at::Tensor& dy, const at::Tensor& x, const
   rms_bwd_fused_kernel<T, V><<<grid, kWarps * 32, smem, stream()>>>(
       (const T*)dy.data_ptr(), (const T*)x.data_ptr(), (const T*)w.data_ptr(), rstd.data_ptr<float>(), dres,
       (T*)dx.data_ptr(), partial.data_ptr<float>(), rows, H, woff);
-  sum_partials_kernel<<<(P + 31) / 32, dim3(32, 8), 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
+  sum_partials_kernel<<<(P + 31) / 32, dim3(32, kSumRows), 0, stream()>>>(partial.data_ptr<float>(), dw.data_ptr<float>(),
                                                                      grid, P, dw_scale, dw_acc ? 1 : 0, E, H);
   return dw;
 }
@@ -891,7 +894,7 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
       // one reduction over both weights (sink targets that sit back to back, or fresh outputs)
       at::Tensor both = adjacent ? at::from_blob(dqw_acc->data_ptr<float>(), {2 * d}, dqw_acc->options())
                                  : at::empty({2 * d}, qkv.options().dtype(at::kFloat));
-      sum_partials_kernel<<<(2 * d + 31) / 32, dim3(32, 8), 0, stream()>>>(
+      sum_partials_kernel<<<(2 * d + 31) / 32, dim3(32, kSumRows), 0, stream()>>>(
           pqk.data_ptr<float>(), both.data_ptr<float>(), blocks, 2 * d, (float)dw_scale, adjacent ? 1 : 0);
       oq = adjacent ? *dqw_acc : both.narrow(0, 0, d);
       ok = adjacent ? *dkw_acc : both.narrow(0, d, d);
@@ -900,9 +903,9 @@ std::vector<c10::optional<at::Tensor>> qk_norm_rope_bwd(const at::Tensor& dq, co
       auto pk = pqk.narrow(1, d, d).contiguous();
       oq = dqw_acc ? *dqw_acc : at::empty({d}, qkv.options().dtype(at::kFloat));
       ok = dkw_acc ? *dkw_acc : at::empty({d}, qkv.options().dtype(at::kFloat));
-      sum_partials_kernel<<<(d + 31) / 32, dim3(32, 8), 0, stream()>>>(pq.data_ptr<float>(), oq.data_ptr<float>(),
+      sum_partials_kernel<<<(d + 31) / 32, dim3(32, kSumRows), 0, stream()>>>(pq.data_ptr<float>(), oq.data_ptr<float>(),
                                                                       blocks, d, (float)dw_scale, dqw_acc ? 1 : 0);
-      sum_partials_kernel<<<(d + 31) / 32, dim3(32, 8), 0, stream()>>>(pk.data_ptr<float>(), ok.data_ptr<float>(),
+      sum_partials_kernel<<<(d + 31) / 32, dim3(32, kSumRows), 0, stream()>>>(pk.data_ptr<float>(), ok.data_ptr<float>(),
                                                                       blocks, d, (float)dw_scale, dkw_acc ? 1 : 0);
     }
     TS_LAUNCH_CHECK();
@@ -1054,7 +1057,7 @@ int noalloc_run(const T* dy, const T* x, const T* w, const float* rstd, T* dx, f
   rms_dw_partial_kernel<T><<<dim3(col_blocks, chunks), dim3(32, 8), 0, st>>>(dy, x, rstd, partial, rows, H,
                                                                             rows_per_chunk);
   if (int rc = noalloc_launch_status("weight-gradient partials")) return rc;
-  sum_partials_kernel<<<(H + 31) / 32, dim3(32, 8), 0, st>>>(partial, dw, chunks, H);
+  sum_partials_kernel<<<(H + 31) / 32, dim3(32, kSumRows), 0, st>>>(partial, dw, chunks, H);
   return noalloc_launch_status("weight-gradient sum");
 }
 

@@ -20,7 +20,7 @@ KERNELS_PER_CALL = {
     "swiglu_fwd": 1, "swiglu_bwd": 1, "embedding_bwd_accumulate": 1, "fold_stats": 1, "axpby": 1,
     "scale": 1, "reduce_into": 1, "lse_gather": 1, "logprob_dlogits": 1,
     "sq_norm": 2, "clip_coef": 1, "adamw_flat": 1,
-    "symm_barrier": 1, "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0, "pinned_slab_alloc": 0, "gemm_tc": 1, "gemm_tc_pair": 0, "gemm_tc_wide": 0, "gemm_tc_direct": 0, "gemm_tc_pdl": 0, "gemm_tc_profile": 0, "gemm_tc_profile_read": 0, "dense_layer_fwd": 10, "dense_layer_bwd": 22, "gemm_tc_cat": 1, "lmhead_lse_tc": 2, "lmhead_dlogits_tc": 1, "tc_selftest": 1, "attn_fwd_tc": 1, "attn_bwd_tc": 3, "attn_fwd_packed": 1, "attn_bwd_packed": 3, "tc_status": 0, "symm_reduce": 1, "symm_reduce_oneshot": 1, "symm_norm_put": 1, "symm_adamw_gather": 1,
+    "symm_barrier": 1, "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0, "pinned_slab_alloc": 0, "gemm_tc": 1, "gemm_tc_pair": 0, "gemm_tc_wide": 0, "gemm_tc_epi8": 0, "gemm_tc_direct": 0, "gemm_tc_pdl": 0, "gemm_tc_profile": 0, "gemm_tc_profile_read": 0, "dense_layer_fwd": 10, "dense_layer_bwd": 22, "gemm_tc_cat": 1, "lmhead_lse_tc": 2, "lmhead_dlogits_tc": 1, "tc_selftest": 1, "attn_fwd_tc": 1, "attn_bwd_tc": 3, "attn_fwd_packed": 1, "attn_bwd_packed": 3, "tc_status": 0, "symm_reduce": 1, "symm_reduce_oneshot": 1, "symm_norm_put": 1, "symm_adamw_gather": 1,
     "conv1d_silu_fwd": 1, "conv1d_silu_bwd": 2, "gdn_fwd": 2, "gdn_bwd": 2, "gdn_chunk_fwd": 3, "gdn_chunk_bwd": 3,
 }
 
