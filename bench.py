@@ -113,7 +113,10 @@ def opd_open_budget(args, device) -> int:
     mean_actions = sum(c["actions"]) / 2
     mean_tokens = args.prompt_len + mean_actions * (sum(c["action_tokens"]) / 2 + sum(c["observation_tokens"]) / 2)
     total = torch.cuda.get_device_properties(device).total_memory
-    room = 0.85 * (total - static) - (8 << 30)  # 8 GB for activations and workspaces
+    # a joint pack's activations (about 16 hidden-width bf16 rows per token and layer, up to 4096 tokens)
+    # plus 8 GB for workspaces
+    pack_act = 4096 * cfg.num_hidden_layers * cfg.hidden_size * 2 * 16
+    room = 0.85 * (total - static) - pack_act - (8 << 30)
     return max(1, int(room // (1.5 * mean_tokens * 3 * kv_token)))
 
 
@@ -135,6 +138,7 @@ class OPDTrainer:
         self.flat, self.reducer = flat, reducer
         self.open_budget = None  # most trajectories streaming at once (None: all of the batch's)
         self.pack_limit = 16  # most actions in one joint scored-turn pack
+        self.pack_tokens = 4096  # most tokens in one joint pack (its activations live until its backward)
         self.packs = self.packed_actions = 0
         self._new()
 
@@ -150,7 +154,7 @@ class OPDTrainer:
         on each call (idle time before an arrival is skipped, not counted). Everything that has arrived by
         the clock and is not yet delivered is *ready*; each call hands the ready actions of distinct
         trajectories (a trajectory's actions in order) to the objective as one joint scored-turn pack, up to
-        ``pack_limit`` actions. With ``open_budget`` at most that many trajectories stream at once (each
+        ``pack_limit`` actions and ``pack_tokens`` tokens. With ``open_budget`` at most that many trajectories stream at once (each
         open trajectory keeps its K/V and its turn boundaries' fp32 adjoint ledgers on the device until it
         closes); the others' actions stay ready until one closes. Same driver for both arms."""
         events = list(work["events"])
@@ -177,6 +181,8 @@ class OPDTrainer:
                         [x for x in taken if x not in opened]) >= budget:
                     blocked.add(g)
                     continue
+                if pack and sum(len(e[3]) for e in pack) + len(ev[3]) > self.pack_tokens:
+                    break
                 pack.append(ev)
                 taken.add(g)
                 if len(pack) >= self.pack_limit:
@@ -619,6 +625,10 @@ def main() -> None:
             setattr(args, key, value)
     if args.warmup < 3:
         raise SystemExit("at least 3 warm-up steps are required")
+    if args.config == 4:
+        # open trajectories of unequal lengths free and allocate blocks of every size; expandable segments keep
+        # the freed space usable (set before the first CUDA allocation; both arms)
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -684,7 +694,8 @@ def main() -> None:
         cfg_block["delivery"] = (
             "each action reaches the trainer at its teacher-score arrival time on a clock advanced by the "
             f"trainer's host time per call; the ready actions of distinct trajectories go in one joint "
-            f"scored-turn pack (at most {trainer.pack_limit}); same driver for both arms")
+            f"scored-turn pack (at most {trainer.pack_limit} actions, {trainer.pack_tokens} tokens); same driver for "
+            "both arms")
         cfg_block["open_trajectories"] = (
             f"at most {trainer.open_budget} trajectories stream at once per rank (each keeps its K/V and fp32 "
             f"turn-boundary adjoint ledgers on the device until it closes); later trajectories' actions wait in "

@@ -46,6 +46,7 @@ class _FakeObjective:
 
     def append_scored_turns(self, items, return_loss):
         assert len({it[1] for it in items}) == len(items), "a trajectory twice in one pack"
+        assert len(items) == 1 or sum(len(it[2]) for it in items) <= 1500, "pack over its token limit"
         self.pack_sizes.append(len(items))
         for g, tid, tokens, mask, teacher, weights in items:
             assert g in self.open and len(teacher) == sum(mask)
@@ -59,7 +60,7 @@ class _FakeObjective:
         self.open.discard(g)
 
 
-@pytest.mark.parametrize("budget,delay", [(None, 0.0), (5, 0.0), (11, 0.002)])
+@pytest.mark.parametrize("budget,delay", [(None, 0.0), (5, 0.0), (11, 0.002), (11, 0.02)])
 def test_opd_driver_delivers_every_action_once_in_order(budget, delay):
     bench = _bench()
     args = argparse.Namespace(seed=3, groups_per_rank=12, prompt_len=4, vocab=50)
@@ -69,6 +70,7 @@ def test_opd_driver_delivers_every_action_once_in_order(budget, delay):
     trainer.device = "cpu"
     trainer.open_budget = budget
     trainer.pack_limit = 4
+    trainer.pack_tokens = 1500
     trainer.packs = trainer.packed_actions = 0
     trainer.finish = lambda: {}
     trainer.step_batch(work)
