@@ -1,19 +1,21 @@
 // Bottom-right causal attention forward on the 5th-generation tensor cores.
 //
-// One CTA computes a 128-query tile of one head:
-//   warp 8      TMA producer: Q once, then K/V 128-key tiles through a
-//               2-stage ring (128B-swizzled boxes of 64 columns)
-//   warp 9      MMA issuer (one thread): S = Q K^T into one of two TMEM
-//               S buffers, O += P V into the TMEM O accumulator; commits
-//               signal the other roles through mbarriers
-//   warps 0-7   softmax: a pair of warps owns 32 query rows (one TMEM
-//               sub-partition); each reads one half of the S row, the two
-//               half maxima are exchanged through shared memory (an
-//               mbarrier per pair), each exponentiates its half (online
-//               max/sum in the log2 domain, bottom-right mask) and writes P
-//               back into tensor memory as bf16 pairs over the S columns it
-//               read -- the A operand of O += P V -- and rescales its half
-//               of the O row only when the row max moved
+// One CTA computes a 128-query tile of one head (SW = 4 softmax warps per
+// 32-row slab for head_dim 128, 2 otherwise):
+//   warp 4*SW    TMA producer: Q once, then K/V key tiles through a 2-stage
+//                ring (128B-swizzled boxes of 64 columns)
+//   warp 4*SW+1  MMA issuer (one thread): S = Q K^T into one of two TMEM
+//                S buffers, O += P V into the TMEM O accumulator; commits
+//                signal the other roles through mbarriers
+//   warps 0..4*SW-1  softmax: the SW warps of a TMEM sub-partition share its
+//                32 query rows and split each tile's key columns; each reads
+//                its part of the S row, the partial maxima are exchanged
+//                through shared memory (an mbarrier per slab), each
+//                exponentiates its part (online max/sum in the log2 domain,
+//                bottom-right mask) and writes P back into tensor memory as
+//                bf16 pairs over the S columns it read -- the A operand of
+//                O += P V -- and rescales its part of the O row only when the
+//                row max moved
 // The tensor core computes S(j+1) while the softmax warps work on S(j), and
 // PV(j) while they work on S(j+1). Epilogue: O / l (bf16) and the natural-log
 // LSE. Every mbarrier wait is bounded (see tc.cuh).
@@ -200,7 +202,14 @@ template <int D>
 struct FwdLayout {
   // D = 256 halves the key tile so two K/V stages still fit in shared memory
   static constexpr int BM = 128, BN = D <= 128 ? 128 : 64;
-  static constexpr int HALF = BN / 2;  // key columns each softmax warp of a pair exponentiates
+  // softmax warps per TMEM sub-partition (32 query rows): each takes CW = BN / SW key columns of a tile and
+  // D / SW columns of the O row. Four for head_dim 128 (16 softmax warps: twice the warps per scheduler to
+  // hide the dependent chains of the exp / max / sum work), two otherwise.
+  static constexpr int SW = D == 128 ? 4 : 2;
+  static constexpr int CW = BN / SW;
+  static constexpr int SOFT = 4 * SW;                 // softmax warps
+  static constexpr int PROD = SOFT, MMA = SOFT + 1;   // producer and MMA warps
+  static constexpr int THREADS = 32 * (SOFT + 2);
   static constexpr int NB = D / 64;    // 64-column boxes per row
   static constexpr uint32_t Q = 0;
   static constexpr uint32_t Q_BYTES = BM * D * 2;
@@ -208,21 +217,22 @@ struct FwdLayout {
   static constexpr uint32_t K0 = Q + Q_BYTES;
   static constexpr uint32_t V0 = K0 + 2 * K_BYTES;
   static constexpr uint32_t BAR = V0 + 2 * K_BYTES;
-  static constexpr uint32_t RED = BAR + 256;     // [2][128] floats: the pair's partial row sums
-  static constexpr uint32_t XMAX = RED + 1024;   // [2 tile parities][2 halves][128] floats: half-row maxima
-  static constexpr uint32_t TOTAL = XMAX + 2048;
+  static constexpr uint32_t RED = BAR + 256;             // [SW][128] floats: the partial row sums
+  static constexpr uint32_t XMAX = RED + SW * 512;       // [2 tile parities][SW][128] floats: partial row maxima
+  static constexpr uint32_t TOTAL = XMAX + 2 * SW * 512;
   // TMEM columns: two S buffers (P is written back over the S columns its warp read, as bf16 pairs, and is
   // the A operand of O += P V from there) and the O accumulator
   static constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256;
-  // TMEM column of the A operand for the kk-th 16-key step of P: half h = kk*16 / HALF lives at
-  // S + h*HALF (HALF / 2 columns of bf16 pairs)
-  static TS_DEVICE uint32_t p_col(int kk) { return (kk * 16 / HALF) * HALF + ((kk * 16) % HALF) / 2; }
+  // TMEM column of the A operand for the kk-th 16-key step of P: part w = kk*16 / CW lives at
+  // S + w*CW (CW / 2 columns of bf16 pairs)
+  static TS_DEVICE uint32_t p_col(int kk) { return (kk * 16 / CW) * CW + ((kk * 16) % CW) / 2; }
 };
 static_assert(FwdLayout<256>::TOTAL + 1024 <= 232448, "forward shared memory exceeds 227 KB");
+static_assert(FwdLayout<128>::TOTAL + 1024 <= 232448, "forward shared memory exceeds 227 KB");
 
 struct FwdBars {
   uint64_t q, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv[2];
-  uint64_t xbar[4][2];  // per TMEM sub-partition and tile parity: both warps of the pair posted their half max
+  uint64_t xbar[4][2];  // per TMEM sub-partition and tile parity: every warp of the row slab posted its max
   uint32_t tmem_slot;
   int abort;
 };
@@ -230,7 +240,7 @@ struct FwdBars {
 static_assert(sizeof(FwdBars) <= 256, "forward barrier block");
 
 template <int D>
-__global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+__global__ void __launch_bounds__(FwdLayout<D>::THREADS, 1) attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                              const __grid_constant__ CUtensorMap tm_k,
                                                              const __grid_constant__ CUtensorMap tm_v,
                                                              bf16* __restrict__ out, float* __restrict__ lse,
@@ -260,22 +270,22 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       tc::mbar_init(&bars->v_full[i], 1);
       tc::mbar_init(&bars->kv_empty[i], 1);
       tc::mbar_init(&bars->s_full[i], 1);
-      tc::mbar_init(&bars->p_full[i], 256);
+      tc::mbar_init(&bars->p_full[i], 32 * L::SOFT);
       tc::mbar_init(&bars->pv[i], 1);
     }
     for (int i = 0; i < 4; ++i) {
-      tc::mbar_init(&bars->xbar[i][0], 64);
-      tc::mbar_init(&bars->xbar[i][1], 64);
+      tc::mbar_init(&bars->xbar[i][0], 32 * L::SW);
+      tc::mbar_init(&bars->xbar[i][1], 32 * L::SW);
     }
     bars->abort = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
+  if (warp == L::MMA) tc::tmem_alloc(&bars->tmem_slot, 512);
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
 
-  if (warp == 8) {
+  if (warp == L::PROD) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tc::prefetch_tmap(&tm_q);
@@ -298,7 +308,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
                           &bars->v_full[s]);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == L::MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
@@ -340,14 +350,15 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax (warps 0-7)
-    // warp w owns rows of TMEM sub-partition (w & 3); both warps of a pair read
-    // the whole S row for the max, but each exponentiates, sums and stores
-    // only its 64-column half (hc) and rescales half of the O row.
+    // ------------------------------------------------------------ softmax (warps 0 .. SOFT-1)
+    // warp w owns the rows of TMEM sub-partition (w & 3) and part pw = w >> 2 of each tile: key columns
+    // [pw*CW, +CW) and O columns [pw*D/SW, +D/SW). The SW warps of a row slab exchange their partial maxima
+    // per tile and their partial sums at the end through shared memory.
     const int r = (warp & 3) * 32 + lane;
-    const int hc = warp >> 2;
+    const int pw = warp >> 2;
     const int qi = q0 + r;  // local query index (rows at or past T belong to the next segment: not stored)
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    constexpr int OCH = D / (32 * L::SW);  // 32-column chunks of the O row per warp
     float* lsum = reinterpret_cast<float*>(smem + L::RED);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
@@ -357,32 +368,34 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       const int s = j & 1;
       if (!warp_wait(&bars->s_full[s], (j >> 1) & 1, abort, err, 31)) { ok = false; break; }
       tc::tc_fence_after();
-      // this warp's half of the tile's columns
-      float sv[L::HALF];
+      // this warp's part of the tile's columns
+      float sv[L::CW];
       const uint32_t scol = s ? L::S_COL1 : L::S_COL0;
-      const uint32_t hcol = lane_base + scol + hc * L::HALF;
+      const uint32_t pcol = lane_base + scol + pw * L::CW;
 #pragma unroll
-      for (int c = 0; c < L::HALF; c += 32) tc::tmem_ld<(L::HALF < 32 ? L::HALF : 32)>(hcol + c, sv + c);
+      for (int c = 0; c < L::CW; c += 32) tc::tmem_ld<(L::CW < 32 ? L::CW : 32)>(pcol + c, sv + c);
       tc::tmem_ld_wait();
-      const int nv_half = walk.nvis(qi) - hc * L::HALF;  // visible columns of this warp's half for this row
-      // half-row max as 8 independent chains (a single fmaxf chain serialises on the instruction latency)
+      const int nv_part = walk.nvis(qi) - pw * L::CW;  // visible columns of this warp's part for this row
+      // partial row max as 8 independent chains (a single fmaxf chain serialises on the instruction latency)
       float mx8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
-      if (nv_half >= L::HALF) {
+      if (nv_part >= L::CW) {
 #pragma unroll
-        for (int i = 0; i < L::HALF; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+        for (int i = 0; i < L::CW; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < L::HALF; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], i < nv_half ? sv[i] : -INFINITY);
+        for (int i = 0; i < L::CW; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], i < nv_part ? sv[i] : -INFINITY);
       }
-      const float hmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+      const float pmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      // the partner warp (same rows, other half) posts its half max; both then hold the same row max
-      xmax[(s * 2 + hc) * 128 + r] = hmax;
+      // the slab's other warps post their partial maxima; all of them then hold the same row max
+      xmax[(s * L::SW + pw) * 128 + r] = pmax;
       tc::mbar_arrive(&xbar[s]);
       if (!warp_wait(&xbar[s], (j >> 1) & 1, abort, err, 35)) { ok = false; break; }
-      const float raw = fmaxf(hmax, xmax[(s * 2 + (hc ^ 1)) * 128 + r]);
+      float raw = xmax[(s * L::SW) * 128 + r];
+#pragma unroll
+      for (int w2 = 1; w2 < L::SW; ++w2) raw = fmaxf(raw, xmax[(s * L::SW + w2) * 128 + r]);
       // the exponent reference moves only when the running max grows by more than 8 (a factor 2^8): P
       // stays <= 256 (exact in bf16's range, and the fp32 sums absorb it), and O is rescaled only then
       const float cand = fmaxf(m, raw * sl2);
@@ -390,41 +403,39 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       const float mx = bump ? cand : m;
       const float ref = mx == -INFINITY ? 0.f : mx;
       const float alpha = bump ? ex2(m - ref) : 1.f;
-      // P of this half, as bf16 pairs over the first HALF / 2 columns of the same half of S (columns this
-      // warp has already read; the S(j + 2) MMA that next writes them is issued after PV(j) has read them)
+      // P of this part, as bf16 pairs over the first CW / 2 columns of the same part of S (columns this warp
+      // has already read; the S(j + 2) MMA that next writes them is issued after PV(j) has read them)
       float rs8[8];  // 8 independent partial sums, for the same reason as the max
 #pragma unroll
       for (int e = 0; e < 8; ++e) rs8[e] = 0.f;
-      float pw[L::HALF / 2];
+      float pv_[L::CW / 2];
 #pragma unroll
-      for (int c8 = 0; c8 < L::HALF / 8; ++c8) {
+      for (int c8 = 0; c8 < L::CW / 8; ++c8) {
         float p[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int i = c8 * 8 + e;
-          p[e] = i < nv_half ? ex2(fmaf(sv[i], sl2, -ref)) : 0.f;
+          p[e] = i < nv_part ? ex2(fmaf(sv[i], sl2, -ref)) : 0.f;
           rs8[e] += p[e];
         }
 #pragma unroll
-        for (int q2 = 0; q2 < 4; ++q2) pw[c8 * 4 + q2] = __uint_as_float(pack2(p[2 * q2], p[2 * q2 + 1]));
+        for (int q2 = 0; q2 < 4; ++q2) pv_[c8 * 4 + q2] = __uint_as_float(pack2(p[2 * q2], p[2 * q2 + 1]));
       }
-      if constexpr (L::HALF / 2 == 32) tc::tmem_st32(hcol, pw);
-      else tc::tmem_st16(hcol, pw);
+      if constexpr (L::CW / 2 == 32) tc::tmem_st32(pcol, pv_);
+      else tc::tmem_st16(pcol, pv_);
       const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
       if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
         if (!warp_wait(&bars->pv[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, err, 32)) { ok = false; break; }
         tc::tc_fence_after();
-        {
 #pragma unroll
-          for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
-            float o[32];
-            tc::tmem_ld32(lane_base + L::O_COL + c * 32, o);
-            tc::tmem_ld_wait();
+        for (int c = pw * OCH; c < (pw + 1) * OCH; ++c) {
+          float o[32];
+          tc::tmem_ld32(lane_base + L::O_COL + c * 32, o);
+          tc::tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tc::tmem_st32(lane_base + L::O_COL + c * 32, o);
-          }
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tc::tmem_st32(lane_base + L::O_COL + c * 32, o);
         }
       }
       tc::tmem_st_wait();
@@ -432,15 +443,17 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->p_full[s]);
     }
-    // the pair's half sums: exchanged once through shared memory
-    lsum[hc * 128 + r] = l;
-    asm volatile("bar.sync 1, 256;\n" ::: "memory");
-    const float lt = lsum[r] + lsum[128 + r];
+    // the slab's partial sums: exchanged once through shared memory
+    lsum[pw * 128 + r] = l;
+    asm volatile("bar.sync 1, %0;\n" ::"n"(32 * L::SOFT) : "memory");
+    float lt = lsum[r];
+#pragma unroll
+    for (int w2 = 1; w2 < L::SW; ++w2) lt += lsum[w2 * 128 + r];
     if (ok && warp_wait(&bars->pv[(n - 1) & 1], ((n - 1) >> 1) & 1, abort, err, 33)) {
       tc::tc_fence_after();
       const float inv = 1.f / lt;
 #pragma unroll
-      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
+      for (int c = pw * OCH; c < (pw + 1) * OCH; ++c) {
         float o[32];
         tc::tmem_ld32(lane_base + L::O_COL + c * 32, o);
         tc::tmem_ld_wait();
@@ -457,12 +470,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
           }
         }
       }
-      if (qi < T && hc == 0) lse[(long long)h * Ttot + it.q_row0 + r] = (m + log2f(lt)) * kLn2;
+      if (qi < T && pw == 0) lse[(long long)h * Ttot + it.q_row0 + r] = (m + log2f(lt)) * kLn2;
     }
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == L::MMA) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -1842,8 +1855,8 @@ void launch_fwd(dim3 grid, const CUtensorMap& mq, const CUtensorMap& mk, const C
                 float* lse, int T, int S, int Hq, int Hkv, float sl2, const PackTabs& tb, int Ttot, int* err) {
   const int smem = FwdLayout<D>::TOTAL + 1024;
   ensure_smem((const void*)attn_fwd_tc_kernel<D>, smem);
-  attn_fwd_tc_kernel<D><<<grid, 320, smem, stream()>>>(mq, mk, mv, o, lse, T, S, Hq, Hkv, sl2, tb.qtab, tb.far, Ttot,
-                                                       err);
+  attn_fwd_tc_kernel<D><<<grid, FwdLayout<D>::THREADS, smem, stream()>>>(mq, mk, mv, o, lse, T, S, Hq, Hkv, sl2,
+                                                                          tb.qtab, tb.far, Ttot, err);
 }
 
 void run_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
