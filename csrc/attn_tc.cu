@@ -1,7 +1,7 @@
 // Bottom-right causal attention forward on the 5th-generation tensor cores.
 //
-// One CTA computes a 128-query tile of one head (SW = 4 softmax warps per
-// 32-row slab for head_dim 128, 2 otherwise):
+// One CTA computes a 128-query tile of one head (SW = 2 softmax warps per
+// 32-row slab):
 //   warp 4*SW    TMA producer: Q once, then K/V key tiles through a 2-stage
 //                ring (128B-swizzled boxes of 64 columns)
 //   warp 4*SW+1  MMA issuer (one thread): S = Q K^T into one of two TMEM
@@ -203,9 +203,9 @@ struct FwdLayout {
   // D = 256 halves the key tile so two K/V stages still fit in shared memory
   static constexpr int BM = 128, BN = D <= 128 ? 128 : 64;
   // softmax warps per TMEM sub-partition (32 query rows): each takes CW = BN / SW key columns of a tile and
-  // D / SW columns of the O row. Four for head_dim 128 (16 softmax warps: twice the warps per scheduler to
-  // hide the dependent chains of the exp / max / sum work), two otherwise.
-  static constexpr int SW = D == 128 ? 4 : 2;
+  // D / SW columns of the O row. Two: four (16 softmax warps, 576 threads) measured 6-7% slower at head_dim
+  // 128 (377 vs 403 TFLOP/s at T=2176, 586 vs 619 at T=9288).
+  static constexpr int SW = 2;
   static constexpr int CW = BN / SW;
   static constexpr int SOFT = 4 * SW;                 // softmax warps
   static constexpr int PROD = SOFT, MMA = SOFT + 1;   // producer and MMA warps
@@ -228,7 +228,6 @@ struct FwdLayout {
   static TS_DEVICE uint32_t p_col(int kk) { return (kk * 16 / CW) * CW + ((kk * 16) % CW) / 2; }
 };
 static_assert(FwdLayout<256>::TOTAL + 1024 <= 232448, "forward shared memory exceeds 227 KB");
-static_assert(FwdLayout<128>::TOTAL + 1024 <= 232448, "forward shared memory exceeds 227 KB");
 
 struct FwdBars {
   uint64_t q, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv[2];
@@ -1202,6 +1201,13 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv256_kernel(
 template <int D>
 struct DqTLayout {
   static constexpr int BM = 128, BN = 128, NB = D / 64, NK = D <= 64 ? 4 : 2;
+  // compute warps per TMEM sub-partition: each takes CW = BN / SW key columns of a step and D / SW columns
+  // of the dQ row; it writes its dS pairs over the first CW / 2 of its own dP columns (no warp waits for
+  // another's read). Two (four spill registers at 576 threads).
+  static constexpr int SW = 2;
+  static constexpr int CW = BN / SW;
+  static constexpr int SOFT = 4 * SW, PROD = SOFT, MMA = SOFT + 1, THREADS = 32 * (SOFT + 2);
+  static TS_DEVICE uint32_t ds_col(int kk) { return (kk * 16 / CW) * CW + ((kk * 16) % CW) / 2; }
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KT_BYTES = BN * D * 2;
   static constexpr uint32_t Q = 0, O = Q_BYTES;
@@ -1217,13 +1223,13 @@ static_assert(DqTLayout<64>::TOTAL + 1024 <= 232448, "dQ shared memory exceeds 2
 
 struct DqTBars {
   uint64_t q, kv_full[4], kv_empty[4], s_full, dp_full, s_free, ds_full, fin, qo_tm;
-  uint64_t dp_read[4];  // per TMEM sub-partition: warp (w & 3) has loaded its dP columns
+  uint64_t dp_read[4];  // head_dim 256 kernel: per TMEM sub-partition, warp (w & 3) has loaded its dP columns
   uint32_t tmem_slot;
   int abort;
 };
 
 template <int D>
-__global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
+__global__ void __launch_bounds__(DqTLayout<D>::THREADS, 1) attn_bwd_dq_t_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
     const float* __restrict__ lse, const float* __restrict__ delta, bf16* __restrict__ dq, int T_in, int S_in,
@@ -1253,20 +1259,20 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
     }
     tc::mbar_init(&bars->s_full, 1);
     tc::mbar_init(&bars->dp_full, 1);
-    tc::mbar_init(&bars->s_free, 256);
-    tc::mbar_init(&bars->ds_full, 256);
+    tc::mbar_init(&bars->s_free, 32 * L::SOFT);
+    tc::mbar_init(&bars->ds_full, 32 * L::SOFT);
     tc::mbar_init(&bars->fin, 1);
     tc::mbar_init(&bars->qo_tm, 128);
     for (int i = 0; i < 4; ++i) tc::mbar_init(&bars->dp_read[i], 32);
     bars->abort = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 9) tc::tmem_alloc(&bars->tmem_slot, 512);
+  if (warp == L::MMA) tc::tmem_alloc(&bars->tmem_slot, 512);
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_slot;
 
-  if (warp == 8) {
+  if (warp == L::PROD) {
     if (lane == 0) {
       tc::mbar_expect_tx(&bars->q, 2 * L::Q_BYTES);
       for (int b = 0; b < L::NB; ++b) {
@@ -1286,7 +1292,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == L::MMA) {
     if (lane == 0) {
       const uint32_t id_s = tc::idesc_bf16(128, L::BN, false, false);
       const uint32_t id_acc = tc::idesc_bf16(128, D, false, true);
@@ -1323,7 +1329,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
         const uint32_t kb = sbase + L::K0 + ks * L::KT_BYTES;
 #pragma unroll
         for (int kk = 0; kk < L::BN / 16; ++kk)
-          tc::mma_bf16_ts(tmem + L::DQ_COL, tmem + L::DP_COL + kk * 8,
+          tc::mma_bf16_ts(tmem + L::DQ_COL, tmem + L::DP_COL + L::ds_col(kk),
                           tc::sdesc_sw128(kb + kk * 16 * 128, L::BN * 128, 1024), id_acc, j > 0 || kk > 0);
         tc::mma_commit(&bars->kv_empty[ks]);
         if (j + 1 < n) {
@@ -1334,10 +1340,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
       if (ok) tc::mma_commit(&bars->fin);
     }
   } else {
-    // warps 0-7: sub-partition (w & 3) rows, key columns [64 * (w >> 2), +64) of each step. The bf16 dS
-    // pairs of warp hc = 1 land on dP columns that warp hc = 0 of the same sub-partition reads, so it
-    // writes them once that warp has loaded its own.
-    const int sp = warp & 3, hc = warp >> 2;
+    // compute warps: sub-partition (w & 3) rows, key columns [CW * pw, +CW) of each step (pw = w >> 2); each
+    // writes its bf16 dS pairs over the first CW / 2 of its own dP columns, where dQ += dS K reads them
+    const int sp = warp & 3, pw = warp >> 2;
     const int r = sp * 32 + lane;
     const int qi = q0 + r;
     const long long lrow = (long long)h * Ttot + it.q_row0 + r;
@@ -1347,7 +1352,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
     bool ok = true;
     // warps 0-3: copy this row of the Q and dO tiles (K-major, 128B-swizzled in shared memory) into the
     // A-operand columns of tensor memory, bf16 pairs per 32-bit column
-    if (hc == 0) {
+    if (pw == 0) {
       if (warp_wait(&bars->q, 0, abort, err, 204)) {
 #pragma unroll
         for (int which = 0; which < 2; ++which) {
@@ -1377,37 +1382,33 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
     for (int j = 0; j < n && ok; ++j, walk.next()) {
       if (!warp_wait(&bars->s_full, j & 1, abort, err, 201)) { ok = false; break; }
       tc::tc_fence_after();
-      float p[64];
-      tc::tmem_ld32(lane_base + L::S_COL + hc * 64, p);
-      tc::tmem_ld32(lane_base + L::S_COL + hc * 64 + 32, p + 32);
+      constexpr int CW = L::CW;
+      float p[CW];
+#pragma unroll
+      for (int c = 0; c < CW; c += 32) tc::tmem_ld32(lane_base + L::S_COL + pw * CW + c, p + c);
       tc::tmem_ld_wait();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->s_free);
-      // key hc*64+c of the tile is visible iff c < nvis (the query exists and sees it)
-      const int nvis = qi < T ? walk.nvis(qi) - hc * 64 : 0;
+      // key pw*CW+c of the tile is visible iff c < nvis (the query exists and sees it)
+      const int nvis = qi < T ? walk.nvis(qi) - pw * CW : 0;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) p[c] = c < nvis ? ex2(fmaf(p[c], sl2, -l2)) : 0.f;
+      for (int c = 0; c < CW; ++c) p[c] = c < nvis ? ex2(fmaf(p[c], sl2, -l2)) : 0.f;
       if (!warp_wait(&bars->dp_full, j & 1, abort, err, 202)) { ok = false; break; }
       tc::tc_fence_after();
       {
-        float dp[64];
-        tc::tmem_ld32(lane_base + L::DP_COL + hc * 64, dp);
-        tc::tmem_ld32(lane_base + L::DP_COL + hc * 64 + 32, dp + 32);
+        float dp[CW];
+#pragma unroll
+        for (int c = 0; c < CW; c += 32) tc::tmem_ld32(lane_base + L::DP_COL + pw * CW + c, dp + c);
         tc::tmem_ld_wait();
-        if (hc == 0) {
-          tc::tc_fence_before();
-          tc::mbar_arrive(&bars->dp_read[sp]);
-        }
 #pragma unroll
-        for (int c = 0; c < 64; ++c) p[c] *= dp[c] - dl;
+        for (int c = 0; c < CW; ++c) p[c] *= dp[c] - dl;
       }
-      if (hc == 1 && !warp_wait(&bars->dp_read[sp], j & 1, abort, err, 203)) { ok = false; break; }
-      tc::tc_fence_after();
       {
-        float w[32];
+        float w[CW / 2];
 #pragma unroll
-        for (int x = 0; x < 32; ++x) w[x] = __uint_as_float(pack2(p[2 * x], p[2 * x + 1]));
-        tc::tmem_st32(lane_base + L::DP_COL + hc * 32, w);
+        for (int x = 0; x < CW / 2; ++x) w[x] = __uint_as_float(pack2(p[2 * x], p[2 * x + 1]));
+        if constexpr (CW / 2 == 32) tc::tmem_st32(lane_base + L::DP_COL + pw * CW, w);
+        else tc::tmem_st16(lane_base + L::DP_COL + pw * CW, w);
       }
       tc::tmem_st_wait();
       tc::tc_fence_before();
@@ -1416,7 +1417,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
     if (ok && warp_wait(&bars->fin, 0, abort, err, 205)) {
       tc::tc_fence_after();
 #pragma unroll
-      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
+      for (int c = pw * (D / (32 * L::SW)); c < (pw + 1) * (D / (32 * L::SW)); ++c) {
         float a[32];
         tc::tmem_ld32(lane_base + L::DQ_COL + c * 32, a);
         tc::tmem_ld_wait();
@@ -1435,7 +1436,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_t_kernel(
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == L::MMA) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -2027,7 +2028,7 @@ void launch_dq_t(dim3 g, const CUtensorMap& mq, const CUtensorMap& mk, const CUt
                  double scale, const PackTabs& tb, int* err) {
   const int smem = DqTLayout<D>::TOTAL + 1024;
   ensure_smem((const void*)attn_bwd_dq_t_kernel<D>, smem);
-  attn_bwd_dq_t_kernel<D><<<g, 320, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
+  attn_bwd_dq_t_kernel<D><<<g, DqTLayout<D>::THREADS, smem, stream()>>>(mq, mk, mv, mo, lse.data_ptr<float>(),
                                                       delta.data_ptr<float>(), (bf16*)dq.data_ptr(), T, S, Hq, Hkv,
                                                       (float)scale, tb.qtab, tb.far, T, err);
 }
