@@ -545,7 +545,6 @@ static_assert(DkvTLayout<64>::TOTAL + 1024 <= 232448, "dK/dV shared memory excee
 
 struct DkvTBars {
   uint64_t kv, q_full[4], q_empty[4], s_full, dp_full, p_full, ds_full, fin;
-  uint64_t s_read[4], dp_read[4];  // per TMEM sub-partition: warp (w & 3) has loaded its S^T / dP^T columns
   uint32_t tmem_slot;
   int abort;
   int4 info[4];  // per Q stage: {local index of the first query, T, vis_base, 0} of the step it holds
@@ -589,10 +588,6 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
     tc::mbar_init(&bars->p_full, 256);
     tc::mbar_init(&bars->ds_full, 256);
     tc::mbar_init(&bars->fin, 1);
-    for (int i = 0; i < 4; ++i) {
-      tc::mbar_init(&bars->s_read[i], 32);
-      tc::mbar_init(&bars->dp_read[i], 32);
-    }
     bars->abort = 0;
     tc::fence_barrier_init();
   }
@@ -665,11 +660,12 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
                        tc::sdesc_sw128(b_base + q_off, 16, 1024), id_s, kk > 0);
         }
       };
-      // dV / dK accumulation: A = P^T / dS^T (bf16 pairs in TMEM), B = dO / Q (MN-major, shared)
+      // dV / dK accumulation: A = P^T / dS^T (bf16 pairs in TMEM: queries [64h, 64h + 64) of a step at
+      // columns [64h, 64h + 32) of the region), B = dO / Q (MN-major, shared)
       auto mma_acc = [&](uint32_t dcol, uint32_t acol, uint32_t b_base, bool first) {
 #pragma unroll
         for (int kk = 0; kk < L::BQ / 16; ++kk)
-          tc::mma_bf16_ts(tmem + dcol, tmem + acol + kk * 8,
+          tc::mma_bf16_ts(tmem + dcol, tmem + acol + (kk >> 2) * 64 + (kk & 3) * 8,
                           tc::sdesc_sw128(b_base + kk * 16 * 128, L::BQ * 128, 1024), id_acc, !first || kk > 0);
       };
       bool ok = tc::mbar_wait(&bars->kv, 0, abort, err, 161);
@@ -708,8 +704,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
     }
   } else {
     // warps 0-7: warp w reads TMEM lanes of sub-partition (w & 3) (key row r) and query columns
-    // [64 * (w >> 2), +64) of each step. The bf16 P^T / dS^T pairs of warp hc = 1 land on columns that
-    // warp hc = 0 of the same sub-partition reads, so it writes them once that warp has loaded its own.
+    // [64 * (w >> 2), +64) of each step, and writes its bf16 P^T / dS^T pairs over the first 32 of those
+    // columns (its own: no warp waits for another's read).
     const int sp = warp & 3, hc = warp >> 2;
     const int r = sp * 32 + lane;
     const int kr = k0 + r;
@@ -730,10 +726,6 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
       tc::tmem_ld32(lane_base + L::S_COL + hc * 64, p);
       tc::tmem_ld32(lane_base + L::S_COL + hc * 64 + 32, p + 32);
       tc::tmem_ld_wait();
-      if (hc == 0) {
-        tc::tc_fence_before();
-        tc::mbar_arrive(&bars->s_read[sp]);
-      }
 #pragma unroll
       for (int c4 = 0; c4 < 16; ++c4) {
         const float4 l = *reinterpret_cast<const float4*>(l2p + c4 * 4);
@@ -744,13 +736,11 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
           p[c] = (c >= lo && c < hi) ? ex2(fmaf(p[c], sl2, -lv[e])) : 0.f;
         }
       }
-      if (hc == 1 && !warp_wait(&bars->s_read[sp], i & 1, abort, err, 173)) { ok = false; break; }
-      tc::tc_fence_after();
       {
         float w[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) w[j] = __uint_as_float(pack2(p[2 * j], p[2 * j + 1]));
-        tc::tmem_st32(lane_base + L::S_COL + hc * 32, w);
+        tc::tmem_st32(lane_base + L::S_COL + hc * 64, w);
       }
       tc::tmem_st_wait();
       tc::tc_fence_before();
@@ -763,10 +753,6 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
         tc::tmem_ld32(lane_base + L::DP_COL + hc * 64, dp);
         tc::tmem_ld32(lane_base + L::DP_COL + hc * 64 + 32, dp + 32);
         tc::tmem_ld_wait();
-        if (hc == 0) {
-          tc::tc_fence_before();
-          tc::mbar_arrive(&bars->dp_read[sp]);
-        }
 #pragma unroll
         for (int c4 = 0; c4 < 16; ++c4) {
           const float4 d = *reinterpret_cast<const float4*>(dlp + c4 * 4);
@@ -776,13 +762,11 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_t_kernel(
           p[c4 * 4 + 3] *= dp[c4 * 4 + 3] - d.w;
         }
       }
-      if (hc == 1 && !warp_wait(&bars->dp_read[sp], i & 1, abort, err, 175)) { ok = false; break; }
-      tc::tc_fence_after();
       {
         float w[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) w[j] = __uint_as_float(pack2(p[2 * j], p[2 * j + 1]));
-        tc::tmem_st32(lane_base + L::DP_COL + hc * 32, w);
+        tc::tmem_st32(lane_base + L::DP_COL + hc * 64, w);
       }
       tc::tmem_st_wait();
       tc::tc_fence_before();
