@@ -173,3 +173,31 @@ def test_combined_known_reward_sources_give_the_same_gradient(binary):
     got, r1 = grads(True)
     assert r0["combined_sources"] == 0 and r1["combined_sources"] > 0 and r1["sources"] < r0["sources"]
     _close(got, ref)
+
+
+def test_concatenating_baseline_keeps_chains_and_same_logprobs():
+    """``chunked_sdpa=False`` (the memory gate's baseline) keeps each pack's concatenated K/V chains alive with
+    its graph, and changes no number: log-probs and gradients equal the streamed path's."""
+    import copy
+
+    from tests.grpo_fixtures import build_model
+    from thundersync_b200.engine.streaming import StreamingRun
+
+    base = build_model(11)
+    out = []
+    for chunked in (True, False):
+        model = copy.deepcopy(base)
+        run = StreamingRun(model, chunked_sdpa=chunked)
+        run.open_group(0, [1, 2, 3, 4, 5])
+        run.append_turn(0, 0, [6, 7, 8], [True, True, True])
+        run.append_turn(0, 0, [9, 10], [True, False])
+        lp = run.logprobs(0)
+        if not chunked:
+            kept = [t for t in run._trajs[0].logprobs if t.grad_fn is not None]
+            assert kept, "turn log-probs carry a graph"
+        lp.sum().backward()
+        out.append((lp.detach().clone(), {n: p.grad.clone() for n, p in model.named_parameters()}))
+        run.close()
+    torch.testing.assert_close(out[0][0], out[1][0])
+    for n in out[0][1]:
+        torch.testing.assert_close(out[0][1][n], out[1][1][n])
