@@ -23,11 +23,12 @@ from thundersync_b200.ops import sink as _sink
 from thundersync_b200.ops._ext import native
 from thundersync_b200.ops.gemm import gemm, gemm_accumulate
 
-# Rows per chunk. The backward materialises a chunk's bf16 dlogits ([rows, V]: 2.5 GB at 8192 rows of a
+# Rows per chunk. The backward materialises a chunk's bf16 dlogits ([rows, V]: 622 MB at 2048 rows of a
 # 151,936-token vocabulary) and reduce-adds one fp32 [V, D] weight gradient per chunk into the sink (1.2 GB
-# at D = 2048, read and written), so fewer, larger chunks move fewer bytes; a trajectory of up to 8192
-# scored tokens is one chunk.
-DEFAULT_ROWS = 8192
+# at D = 2048, read and written). Larger chunks move fewer sink bytes, but the streamed step keeps most of
+# the device busy with retained graphs: 8192-row chunks (a 2.5 GB dlogits buffer) ran the hybrid config
+# (32k-token completions) out of memory, so chunks stay at 2048 rows.
+DEFAULT_ROWS = 2048
 # tcgen05 GEMM with fused log-sum-exp / dlogits epilogues on CUDA bf16 (False: cuBLAS logits + row kernels)
 FUSED_TC = True
 
