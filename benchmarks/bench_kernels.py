@@ -341,6 +341,48 @@ def bench_gemm_one(args) -> None:
           "TFLOP/s")
 
 
+def bench_packed(args) -> None:
+    """Packed attention vs per-segment attention on a close-rebuild pack: ``--segs`` trajectories of one group
+    (lengths spread over [--t / 4, --t]) that share a 512-token prompt chunk, 16 q / 8 kv heads, d = 128.
+    Times forward + backward of `packed_attention` (one launch each way, the shared prompt stored once) against
+    one `chunked_attention` call per segment (the prompt concatenated into each segment's chain)."""
+    import random
+
+    from thundersync_b200.ops.attention import chunked_attention
+    from thundersync_b200.ops.packed_attention import packed_attention
+
+    hq, hkv, d = 16, 8, 128
+    rng = random.Random(0)
+    lens = [rng.randint(args.t // 4, args.t) for _ in range(args.segs)]
+    t = sum(lens)
+    dev = "cuda"
+    prompt_k = torch.randn(512, hkv, d, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    prompt_v = torch.randn(512, hkv, d, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    q = torch.randn(t, hq, d, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(t, hkv, d, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(t, hkv, d, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    meta, s0 = [], 0
+    for n in lens:
+        meta.append((s0, s0 + n, 1, ()))
+        s0 += n
+    pk, pv = [prompt_k] * len(lens), [prompt_v] * len(lens)
+    g = torch.randn(t, hq, d, device=dev, dtype=torch.bfloat16)
+
+    def packed():
+        o = packed_attention(q, k, v, meta, pk, pv)
+        torch.autograd.backward(o, g)
+
+    def per_segment():
+        outs = [chunked_attention(q[a:b], [prompt_k, k[a:b]], [prompt_v, v[a:b]]) for a, b, _, _ in meta]
+        torch.autograd.backward(torch.cat(outs, 0), g)
+
+    pairs = sum(n * 512 + n * (n + 1) / 2 for n in lens)
+    flops = 3.5 * 4 * hq * d * pairs  # forward (2 GEMMs) + backward (5): 7 GEMM-equivalents of 2*pairs*hq*d
+    for name, fn in (("packed (one launch each way)", packed), ("per segment", per_segment)):
+        ms = _time(fn, args.iters)
+        print(f"{name:30s} {len(lens)} segments, {t} queries: {ms:.3f} ms fwd+bwd  {flops / ms / 1e9:.1f} TFLOP/s")
+
+
 def _bench_gemm_shapes(args) -> None:
     from thundersync_b200.ops.gemm import gemm, gemm_accumulate
 
@@ -545,7 +587,7 @@ def bench_gemm_host(args) -> None:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("family", choices=["attn", "rms", "lse", "gdn", "conv", "gemm_host", "swiglu", "rope", "dlogits",
-                                       "adamw", "fold", "gemm", "gemm_ab", "gemm_one", "lmhead", "baselines", "lora", "layer_host"])
+                                       "adamw", "fold", "gemm", "gemm_ab", "gemm_one", "packed", "lmhead", "baselines", "lora", "layer_host"])
     ap.add_argument("--mode", choices=["fwd", "bwd"], default="bwd")
     ap.add_argument("--t", type=int, default=2048)
     ap.add_argument("--s", type=int, default=2560)
@@ -556,6 +598,7 @@ def main(argv=None) -> None:
     ap.add_argument("--rows", type=int, default=16384)
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--n", type=int, default=4096, help="gemm_one: output columns")
+    ap.add_argument("--segs", type=int, default=8, help="packed: segments per pack")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--rounds", type=int, default=5, help="gemm_ab: interleaved rounds per variant")
     ap.add_argument("--trace", action="store_true", help="lora: per-kernel device times of one forward+backward")
@@ -563,7 +606,7 @@ def main(argv=None) -> None:
     args = ap.parse_args(argv)
     {"attn": bench_attn, "rms": bench_rms, "lse": bench_lse, "gdn": bench_gdn, "conv": bench_conv,
      "gemm_host": bench_gemm_host, "swiglu": bench_swiglu, "rope": bench_rope, "dlogits": bench_dlogits,
-     "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm, "gemm_ab": bench_gemm_ab, "gemm_one": bench_gemm_one,
+     "adamw": bench_adamw, "fold": bench_fold, "gemm": bench_gemm, "gemm_ab": bench_gemm_ab, "gemm_one": bench_gemm_one, "packed": bench_packed,
      "lmhead": bench_lmhead, "baselines": bench_baselines, "lora": bench_lora,
      "layer_host": bench_layer_host}[args.family](args)
 
