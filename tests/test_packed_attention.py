@@ -169,3 +169,25 @@ def test_packed_kernels_match_fp32(d, seed):
     for a, b in zip(ga, gb):
         assert rel(a, b) < 3e-2
     assert out[covered:].abs().max().item() == 0
+
+
+def test_plan_is_cached_per_layout_and_repeat_pattern():
+    """One plan per (segment layout, which ancestor inputs repeat, chunk lengths): every attention layer of a
+    pack reuses it, and a different sharing pattern gets its own tables."""
+    a = torch.zeros(7, 2, 16)
+    b = torch.zeros(7, 2, 16)
+    meta = ((0, 5, 1, ()), (5, 9, 1, ()))
+    shared = packed_plan(meta, [a, a], [a, a], 12)
+    again = packed_plan(meta, [b, b], [b, b], 12)  # another layer's tensors, same sharing pattern
+    distinct = packed_plan(meta, [a, b], [a, b], 12)
+    assert shared is again
+    assert distinct is not shared
+    assert len(shared.chunk_rows) == 1 and len(distinct.chunk_rows) == 2
+    assert shared.first == (True, False) and distinct.first == (True, True)
+
+
+def test_oneshot_threshold_scales_with_world():
+    from thundersync_b200.parallel.symm import ONESHOT_MAX_ELEMS, oneshot_max_elems
+
+    assert oneshot_max_elems(2) == ONESHOT_MAX_ELEMS == (16 << 20) // 4
+    assert oneshot_max_elems(8) * 4 == oneshot_max_elems(2)
