@@ -28,10 +28,14 @@
 //
 // The algebra and the hand-derived backward are the ones of
 // thundersync_b200/ops/gdn_chunked.py (checked there against autograd through
-// the token recurrence). All arithmetic is fp32 on the CUDA cores: the chunk
-// products are small (64 x 128 x 128) and sit on the serial chain, where
-// latency, not tensor throughput, bounds the time; fp32 operands keep the
-// final state within 1e-3 of the fp32 recurrence.
+// the token recurrence). Every matrix product runs on the tensor cores as
+// warp-level mma.sync m16n8k8 with tf32 operands split in two (x = hi + lo,
+// a·b ≈ hi·hi + hi·lo + lo·hi, three MMAs per fragment): the dropped lo·lo
+// term is below 2^-21 of the product, so the products keep fp32 accuracy and
+// the final state stays within 1e-3 of the fp32 recurrence. The products are
+// 64- and 128-row tiles held in registers by their epilogues (masks, decays,
+// row sums), so they stay warp-level: each thread owns a fixed set of product
+// elements (Tile) that the MMA fragments produce in place.
 #include "common.cuh"
 #include "common.h"
 
@@ -41,39 +45,107 @@ namespace {
 constexpr int C = 64;          // chunk length
 constexpr int D = 128;         // dk = dv
 constexpr int NT = 256;        // threads per CTA
-constexpr int LD = D + 1;      // padded leading dimensions (odd: conflict-free column walks)
-constexpr int LC = C + 1;
+constexpr int LD = D + 4;      // padded leading dimensions (≡ 4 mod 32: MMA fragment loads hit
+constexpr int LC = C + 4;      // distinct banks, or two ways for transposed operands)
 constexpr float kNormEps = 1e-6f;
 
 typedef __nv_bfloat16 bf16;
 
-// acc[r][c] += Σ_k a(i, k) · b(k, j) for this thread's rows i = ti + r·(M/TM) and columns
-// j = tj + c·(N/TN); a(i, k) = TA ? A[k·lda + i] : A[i·lda + k], b(k, j) = TB ? B[j·ldb + k] : B[k·ldb + j].
+// Ownership of a product's M x N elements: the CTA's 8 warps form a WM x WN grid of warp tiles of
+// 8·TM rows x 4·TN columns, each covered by (TM/2) x (TN/2) m16n8 MMA fragments. Lane (g = lane/4,
+// t = lane%4) owns rows g, g + 8 of every 16-row block and columns 2t, 2t + 1 of every 8-column
+// block: element (r, c) of acc[TM][TN] is (row(r), col(c)). The 4 lanes of a quad (same g) and the
+// WN warps of a warp row share each row.
+template <int M, int N, int TM, int TN>
+struct Tile {
+  static constexpr int WM = M / (8 * TM), WN = N / (4 * TN);
+  static_assert(WM * WN == NT / 32 && TM % 2 == 0 && TN % 2 == 0, "warp tiles must cover the product");
+  TS_DEVICE static int wn() { return (threadIdx.x >> 5) % WN; }
+  TS_DEVICE static int row(int r) {
+    return ((threadIdx.x >> 5) / WN) * (8 * TM) + (r >> 1) * 16 + (r & 1) * 8 + ((threadIdx.x & 31) >> 2);
+  }
+  TS_DEVICE static int col(int c) {
+    return ((threadIdx.x >> 5) % WN) * (4 * TN) + (c >> 1) * 8 + 2 * (threadIdx.x & 3) + (c & 1);
+  }
+};
+
+// x = hi + lo with hi, lo tf32 (round to nearest; the low 13 bits cleared so hi is exact as fp32)
+TS_DEVICE void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  h &= 0xffffe000u;
+  const float rest = x - __uint_as_float(h);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(rest));
+  hi = h;
+}
+
+TS_DEVICE void mma_tf32(float& d0, float& d1, float& d2, float& d3, const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// acc[r][c] += Σ_k a(row(r), k) · b(k, col(c)) over k < K (a multiple of 8), with
+// a(i, k) = TA ? A[k·lda + i] : A[i·lda + k] and b(k, j) = TB ? B[j·ldb + k] : B[k·ldb + j], fp32 operands
+// in shared memory. Fragment layouts of m16n8k8 (PTX ISA): A a0 (g, t), a1 (g+8, t), a2 (g, t+4),
+// a3 (g+8, t+4); B b0 (t, g), b1 (t+4, g); D d0, d1 (g, 2t + {0, 1}), d2, d3 (g+8, 2t + {0, 1}).
 template <int M, int N, int TM, int TN, bool TA, bool TB>
 TS_DEVICE void mm_acc(float (&acc)[TM][TN], const float* A, int lda, const float* B, int ldb, int K) {
-  constexpr int RM = M / TM, RN = N / TN;
-  static_assert(RM * RN == NT, "tile shape must cover the CTA");
-  const int ti = threadIdx.x / RN, tj = threadIdx.x % RN;
-#pragma unroll 4
-  for (int k = 0; k < K; ++k) {
-    float a[TM], b[TN];
+  using Tl = Tile<M, N, TM, TN>;
+  constexpr int MR = TM / 2, NC = TN / 2;
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int r0 = ((threadIdx.x >> 5) / Tl::WN) * (8 * TM) + g;
+  const int c0 = Tl::wn() * (4 * TN) + g;
+  auto a_at = [&](int i, int k) { return TA ? A[k * lda + i] : A[i * lda + k]; };
+  auto b_at = [&](int k, int j) { return TB ? B[j * ldb + k] : B[k * ldb + j]; };
+#pragma unroll 2
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    uint32_t ah[MR][4], al[MR][4], bh[NC][2], bl[NC][2];
 #pragma unroll
-    for (int r = 0; r < TM; ++r) a[r] = TA ? A[k * lda + ti + r * RM] : A[(ti + r * RM) * lda + k];
+    for (int i = 0; i < MR; ++i) {
+      const int r = r0 + 16 * i;
+      tf32_split(a_at(r, k0 + t), ah[i][0], al[i][0]);
+      tf32_split(a_at(r + 8, k0 + t), ah[i][1], al[i][1]);
+      tf32_split(a_at(r, k0 + t + 4), ah[i][2], al[i][2]);
+      tf32_split(a_at(r + 8, k0 + t + 4), ah[i][3], al[i][3]);
+    }
 #pragma unroll
-    for (int c = 0; c < TN; ++c) b[c] = TB ? B[(tj + c * RN) * ldb + k] : B[k * ldb + tj + c * RN];
+    for (int j = 0; j < NC; ++j) {
+      const int c = c0 + 8 * j;
+      tf32_split(b_at(k0 + t, c), bh[j][0], bl[j][0]);
+      tf32_split(b_at(k0 + t + 4, c), bh[j][1], bl[j][1]);
+    }
 #pragma unroll
-    for (int r = 0; r < TM; ++r)
+    for (int i = 0; i < MR; ++i)
 #pragma unroll
-      for (int c = 0; c < TN; ++c) acc[r][c] = fmaf(a[r], b[c], acc[r][c]);
+      for (int j = 0; j < NC; ++j) {
+        float& d0 = acc[2 * i][2 * j];
+        float& d1 = acc[2 * i][2 * j + 1];
+        float& d2 = acc[2 * i + 1][2 * j];
+        float& d3 = acc[2 * i + 1][2 * j + 1];
+        mma_tf32(d0, d1, d2, d3, al[i], bh[j]);  // small terms first
+        mma_tf32(d0, d1, d2, d3, ah[i], bl[j]);
+        mma_tf32(d0, d1, d2, d3, ah[i], bh[j]);
+      }
   }
 }
 
-template <int M, int N, int TM, int TN>
-struct Tile {
-  static constexpr int RM = M / TM, RN = N / TN;
-  TS_DEVICE static int row(int r) { return threadIdx.x / RN + r * RM; }
-  TS_DEVICE static int col(int c) { return threadIdx.x % RN + c * RN; }
-};
+// Σ over the threads that own row Tl::row(r) of v[r]: the lanes of a quad by shuffles, then the Tl::WN
+// warps of a warp row through part[WN][M] in warp order (fixed order: reproducible). Call with every
+// thread of the CTA; part is complete after the caller's next __syncthreads.
+template <class Tl, int TM>
+TS_DEVICE void row_partials(float (&v)[TM], float* part, int M) {
+#pragma unroll
+  for (int r = 0; r < TM; ++r) {
+    v[r] += __shfl_xor_sync(0xffffffffu, v[r], 1);
+    v[r] += __shfl_xor_sync(0xffffffffu, v[r], 2);
+  }
+  if ((threadIdx.x & 3) == 0)
+#pragma unroll
+    for (int r = 0; r < TM; ++r) part[Tl::wn() * M + Tl::row(r)] = v[r];
+}
 
 template <int TM, int TN>
 TS_DEVICE void zero(float (&acc)[TM][TN]) {
@@ -609,7 +681,7 @@ struct GradStateSmem {
   float Q[C * LD];   // Q, then δ
   float X[C * LD];   // dO
   float Z[C * LD];   // dζ
-  float rowacc[C][4];
+  float part[3][4][C];   // row partials (dβ, dG, E) per warp column of the C x D tiles
   float red[NT / 32];
   ChunkScalars s;
 };
@@ -631,9 +703,9 @@ __global__ void __launch_bounds__(NT) gdn_grads_state_kernel(
   load_bf16<D>(sm.X, LD, dout, t0, n, H, h, 0);
   load_f32<D>(sm.Z, LD, dz, t0, n, H, h, 0);
   load_scalars(sm.s, g, beta, t0, n, H, h);
-  for (int i = threadIdx.x; i < C * 4; i += NT) sm.rowacc[i / 4][i % 4] = 0.f;
   __syncthreads();
   using Tw = Tile<C, D, 4, 8>;
+  static_assert(Tw::WN == 4, "part[][4][] holds one partial per warp column");
   float dq[4][8], dk[4][8];
   float rb[4] = {0.f, 0.f, 0.f, 0.f}, rg[4] = {0.f, 0.f, 0.f, 0.f};
   {
@@ -697,25 +769,12 @@ __global__ void __launch_bounds__(NT) gdn_grads_state_kernel(
       re[r] *= e;
     }
   }
-  // row sums over the 16 threads that share each row (tj = tid % 16 within the same ti)
+  // row sums: the quad's lanes, then one partial per warp column (summed in order below)
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-#pragma unroll
-    for (int o = 8; o; o >>= 1) {
-      rb[r] += __shfl_xor_sync(0xffffffffu, rb[r], o);
-      rg[r] += __shfl_xor_sync(0xffffffffu, rg[r], o);
-      re[r] += __shfl_xor_sync(0xffffffffu, re[r], o);
-    }
-  }
-  if ((threadIdx.x % Tw::RN) == 0) {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int i = Tw::row(r);
-      sm.rowacc[i][0] = rb[r];
-      sm.rowacc[i][1] = rg[r] - re[r];
-      sm.rowacc[i][2] = re[r];
-    }
-  }
+  for (int r = 0; r < 4; ++r) rg[r] -= re[r];
+  row_partials<Tw>(rb, &sm.part[0][0][0], C);
+  row_partials<Tw>(rg, &sm.part[1][0][0], C);
+  row_partials<Tw>(re, &sm.part[2][0][0], C);
   // dγ: e^γ ⟨S0, dS'⟩ + Σ_i E_i
   dot = warp_sum(dot);
   if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = dot;
@@ -724,12 +783,12 @@ __global__ void __launch_bounds__(NT) gdn_grads_state_kernel(
     float tot = 0.f;
     for (int w = 0; w < NT / 32; ++w) tot += sm.red[w];
     float es = 0.f;
-    for (int i = 0; i < n; ++i) es += sm.rowacc[i][2];
+    for (int i = 0; i < n; ++i) es += ((sm.part[2][0][i] + sm.part[2][1][i]) + sm.part[2][2][i]) + sm.part[2][3][i];
     dgam[(size_t)ch * H + h] = __expf(gam) * tot + es;
   }
   for (int i = threadIdx.x; i < n; i += NT) {
-    dbeta[(size_t)(t0 + i) * H + h] = sm.rowacc[i][0];
-    dG[(size_t)(t0 + i) * H + h] = sm.rowacc[i][1];
+    dbeta[(size_t)(t0 + i) * H + h] = ((sm.part[0][0][i] + sm.part[0][1][i]) + sm.part[0][2][i]) + sm.part[0][3][i];
+    dG[(size_t)(t0 + i) * H + h] = ((sm.part[1][0][i] + sm.part[1][1][i]) + sm.part[1][2][i]) + sm.part[1][3][i];
   }
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
@@ -758,6 +817,7 @@ struct GradLocalSmem {
   float dM[C * LC];
   float dN[C * LC];
   float rowacc[C][2];
+  float part[4][C];   // dβ row partials per warp column of the C x C tiles
   ChunkScalars s;
 };
 
@@ -823,14 +883,9 @@ __global__ void __launch_bounds__(NT) gdn_grads_local_kernel(
         rbeta[r] = fmaf(dA * el, kk[r][c], rbeta[r]);
       }
     }
-    // row sums over the 16 threads of a row, then atomics-free accumulation through shared memory
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int o = 8; o; o >>= 1) rbeta[r] += __shfl_xor_sync(0xffffffffu, rbeta[r], o);
-    if ((threadIdx.x % Tl::RN) == 0)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) sm.rowacc[Tl::row(r)][0] = rbeta[r];
+    // row sums: the quad's lanes, then one partial per warp column (summed in order below; no atomics)
+    static_assert(Tl::WN == 4, "part[4][] holds one partial per warp column");
+    row_partials<Tl>(rbeta, &sm.part[0][0], C);
   }
   __syncthreads();
   // dG partial from the C x C terms: rowsum − colsum of (dA⊙A + dP⊙P); a column j's sum is over
@@ -852,6 +907,7 @@ __global__ void __launch_bounds__(NT) gdn_grads_local_kernel(
       cs += Mx[j * LC + i];
     }
     sm.rowacc[i][1] = rs - cs;
+    sm.rowacc[i][0] = ((sm.part[0][i] + sm.part[1][i]) + sm.part[2][i]) + sm.part[3][i];
   }
   __syncthreads();
   // dG total and the reverse cumsum (one warp, two values per lane)
