@@ -104,3 +104,26 @@ def test_checkpointed_forest_with_attention_cache_is_exact():
             assert rep["saved"] > 0 and rep["replayed"] == rep["saved"] and rep["declined"] == 0
         else:
             assert rep["saved"] == 0 and rep["declined"] > 0 and rep["replayed"] == 0
+
+
+def test_forest_context_binds_and_restores_plans():
+    """forest_logprobs without a plan runs the bound one; nested contexts restore the outer plan."""
+    import pytest
+
+    from thundersync_b200.engine.step import bound_plan, forest_context
+
+    model = build_model(5)
+    outer = compile_plan(build_forest(_batch(3)))
+    inner = compile_plan(build_forest(_batch(4)))
+    assert bound_plan("cpu") is None
+    with pytest.raises(RuntimeError):
+        forest_logprobs(model)
+    with forest_context(outer):
+        lp_outer = forest_logprobs(model)
+        with forest_context(inner):
+            assert bound_plan("cpu") is inner
+            torch.testing.assert_close(forest_logprobs(model), forest_logprobs(model, inner), rtol=0, atol=0)
+        assert bound_plan("cpu") is outer
+        lp_outer.sum().backward()  # the step's backward inside the context, as with checkpointing
+    assert bound_plan("cpu") is None
+    torch.testing.assert_close(lp_outer.detach(), forest_logprobs(model, outer).detach(), rtol=0, atol=0)

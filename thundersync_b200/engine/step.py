@@ -23,7 +23,7 @@ from thundersync_b200.engine.streaming import arena_for
 from thundersync_b200.ops.logprob import lm_head_logprob
 
 __all__ = ["forest_logprobs", "split_by_trajectory", "assert_supported", "base_model", "unembedding",
-           "hybrid_layer_kinds", "StepStats"]
+           "hybrid_layer_kinds", "StepStats", "forest_context", "bound_plan"]
 
 
 @dataclass
@@ -84,14 +84,19 @@ def _run_checkpointed(ex, ids: torch.Tensor, pos: torch.Tensor, segs: list[Segme
     return ex.final_norm(h)
 
 
-def forest_logprobs(model: torch.nn.Module, plan: ExecutionPlan, *, gate: bool = True,
+def forest_logprobs(model: torch.nn.Module, plan: ExecutionPlan | None = None, *, gate: bool = True,
                     stats: list[StepStats] | None = None, checkpoint: bool = False,
                     attention_cache: Any = None) -> torch.Tensor:
     """Log-probs of the plan's scored tokens. ``checkpoint`` keeps only layer inputs for the backward
     (each layer is recomputed there); an :class:`~thundersync_b200.ops.attention.AttentionOutputCache`
-    lets that recompute reuse attention outputs within its byte budget."""
+    lets that recompute reuse attention outputs within its byte budget. ``plan=None`` runs the plan that
+    :func:`forest_context` bound for the model's device."""
     assert_supported(model)
     dev = next(model.parameters()).device
+    if plan is None:
+        plan = bound_plan(dev)
+        if plan is None:
+            raise RuntimeError("forest_logprobs without a plan needs one bound by forest_context")
     plan = plan.to(dev)
     ex = executor_for(model, arena_for(model))
     segs = []
@@ -128,10 +133,38 @@ def split_by_trajectory(plan: ExecutionPlan, logical: torch.Tensor) -> dict[int,
     return out
 
 
-def forest_context(*_a: Any, **_k: Any):  # kept for API parity: the executor needs no bound context
-    import contextlib
+_BOUND: dict[str, ExecutionPlan] = {}
 
-    return contextlib.nullcontext()
+
+def _device_key(device: torch.device | str) -> str:
+    d = torch.device(device)
+    if d.type == "cuda" and d.index is None:
+        d = torch.device("cuda", torch.cuda.current_device())
+    return str(d)
+
+
+def bound_plan(device: torch.device | str) -> ExecutionPlan | None:
+    """The plan :func:`forest_context` bound for ``device`` (None outside one)."""
+    return _BOUND.get(_device_key(device))
+
+
+@contextlib.contextmanager
+def forest_context(plan: ExecutionPlan):
+    """Bind ``plan`` to its device for a forward, or a whole step (forward, loss, backward), so that
+    :func:`forest_logprobs` called without a plan runs it. Contexts nest: leaving one restores the plan
+    bound before it. The executor itself takes the plan as an argument, so a checkpointed recompute in
+    the backward needs no binding (reference src/thundersync/engine/step.py:142-164 binds the plan for
+    its attention-interface dispatch instead)."""
+    key = _device_key(plan.token_ids.device)
+    previous = _BOUND.get(key)
+    _BOUND[key] = plan
+    try:
+        yield plan
+    finally:
+        if previous is None:
+            _BOUND.pop(key, None)
+        else:
+            _BOUND[key] = previous
 
 
 def register_attention() -> None:
