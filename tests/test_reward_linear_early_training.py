@@ -1,0 +1,174 @@
+"""Early training: sources computed before their rewards (prepare), folded when the reward arrives (bind).
+
+CPU fp32 on the config-1 tiny model. The behaviours are the ones the reference's early-training battery
+checks (reference tests/test_reward_linear_early_training.py:122-342), stated against this package's
+API: binding order does not change the gradient beyond fp32 summation order; a reward may also arrive
+before its trajectory's content (the known-reward path); duplicate prepares, conflicting rewards,
+non-finite rewards, early group closes and parameter updates inside the batch are refused; abort frees
+held sources.
+"""
+
+from __future__ import annotations
+
+import copy
+
+import pytest
+import torch
+
+from tests.grpo_fixtures import EPS, build_model, make_batch
+from thundersync_b200.engine.streaming import StreamingRun
+from thundersync_b200.grpo.reward_linear import RewardLinearBackward
+
+
+def _setup(model):
+    run = StreamingRun(model, boundary_cut=True, stream_turns=False)
+    return run, RewardLinearBackward(run, model, eps=EPS)
+
+
+def _append(run, g, turns, tid):
+    for tk, sc in turns:
+        run.append_turn(g, tid, tk, sc)
+
+
+def _grads(model):
+    return {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+
+
+def _run(model, batch, drive):
+    m = copy.deepcopy(model)
+    run, bw = _setup(m)
+    for g, prompt, trajs in batch:
+        bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    drive(run, bw)
+    for g, _, _ in batch:
+        bw.close_group(g)
+    bw.assert_safe_to_step()
+    return _grads(m)
+
+
+def _close_path(batch):
+    def drive(run, bw):
+        for g, _, trajs in batch:
+            for tid, turns, reward in trajs:
+                _append(run, g, turns, tid)
+                bw.close_trajectory(tid, reward)
+    return drive
+
+
+def _assert_same(a, b):
+    for n in a:
+        torch.testing.assert_close(a[n], b[n], rtol=1e-5, atol=1e-6, msg=n)
+
+
+def test_binding_in_reverse_order_equals_the_close_path():
+    model = build_model(21)
+    batch, _ = make_batch(21, groups=2, per_group=4)
+
+    def drive(run, bw):
+        for g, _, trajs in batch:
+            for tid, turns, _ in trajs:
+                _append(run, g, turns, tid)
+                bw.prepare_trajectory(tid)
+        assert bw.held_source_count == sum(len(t) for _, _, t in batch)
+        binds = [(tid, reward) for _, _, trajs in batch for tid, _, reward in trajs]
+        for tid, reward in reversed(binds):
+            bw.bind_reward(tid, reward)
+        assert bw.held_source_count == 0
+
+    _assert_same(_run(model, batch, drive), _run(model, batch, _close_path(batch)))
+
+
+def test_reward_before_content_takes_the_known_reward_path():
+    """A reward recorded before the trajectory is prepared is differentiated at prepare time."""
+    model = build_model(22)
+    batch, _ = make_batch(22, groups=1, per_group=4)
+
+    def drive(run, bw):
+        for g, _, trajs in batch:
+            bw.record_rewards([(tid, reward) for tid, _, reward in trajs])
+            for tid, turns, _ in trajs:
+                _append(run, g, turns, tid)
+                bw.prepare_trajectory(tid)
+            assert bw.held_source_count == 0  # nothing waits for a reward
+
+    _assert_same(_run(model, batch, drive), _run(model, batch, _close_path(batch)))
+
+
+def test_a_group_with_every_source_prepared_is_not_bound_until_the_rewards_arrive():
+    model = build_model(23)
+    batch, _ = make_batch(23, groups=1, per_group=3)
+    run, bw = _setup(model)
+    g, prompt, trajs = batch[0]
+    bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    for tid, turns, _ in trajs:
+        _append(run, g, turns, tid)
+        bw.prepare_trajectory(tid)
+    assert not bw.group_fully_bound(g)
+    for tid, _, reward in trajs[:-1]:
+        bw.bind_reward(tid, reward)
+    with pytest.raises(RuntimeError):
+        bw.close_group(g)  # the straggler still holds its group open
+    with pytest.raises(RuntimeError):
+        bw.assert_safe_to_step()
+    tid, _, reward = trajs[-1]
+    bw.bind_reward(tid, reward)
+    assert bw.group_fully_bound(g)
+    bw.close_group(g)
+    bw.assert_safe_to_step()
+
+
+def test_duplicate_prepare_conflicting_or_non_finite_rewards_are_refused():
+    model = build_model(24)
+    batch, _ = make_batch(24, groups=1, per_group=2)
+    run, bw = _setup(model)
+    g, prompt, trajs = batch[0]
+    bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    (t0, turns0, _), (t1, turns1, _) = trajs
+    _append(run, g, turns0, t0)
+    bw.prepare_trajectory(t0)
+    with pytest.raises(ValueError):
+        bw.prepare_trajectory(t0)
+    with pytest.raises(ValueError):
+        bw.bind_reward(t0, float("nan"))
+    with pytest.raises(ValueError):
+        bw.bind_reward(t0, float("inf"))
+    bw.record_rewards([(t1, 1.0)])
+    with pytest.raises(ValueError):
+        bw.record_rewards([(t1, 0.0)])
+    bw.record_rewards([(t1, 1.0)])  # the same reward again is not a conflict
+    with pytest.raises(KeyError):
+        bw.prepare_trajectory(10_000)  # not registered with any group
+
+
+def test_a_parameter_update_between_prepare_and_bind_is_refused():
+    model = build_model(25)
+    batch, _ = make_batch(25, groups=1, per_group=2)
+    run, bw = _setup(model)
+    g, prompt, trajs = batch[0]
+    bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    (t0, turns0, _), (t1, turns1, _) = trajs
+    _append(run, g, turns0, t0)
+    bw.prepare_trajectory(t0)
+    with torch.no_grad():
+        next(model.parameters()).add_(1e-3)  # an optimizer step inside the logical batch
+    _append(run, g, turns1, t1)
+    with pytest.raises(RuntimeError, match="version guard"):
+        bw.prepare_trajectory(t1)
+
+
+def test_abort_frees_held_sources_and_refuses_the_step():
+    model = build_model(26)
+    batch, _ = make_batch(26, groups=2, per_group=2)
+    run, bw = _setup(model)
+    for g, prompt, trajs in batch:
+        bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    g, _, trajs = batch[0]
+    for tid, turns, _ in trajs:
+        _append(run, g, turns, tid)
+        bw.prepare_trajectory(tid)
+    assert bw.held_source_count == 2 and bw.retained_device_bytes()["held_sources"] > 0
+    bw.abort()
+    assert bw.held_source_count == 0 and bw.retained_device_bytes()["held_sources"] == 0
+    assert bw.open_groups() == []
+    with pytest.raises(RuntimeError):
+        bw.assert_safe_to_step()
