@@ -168,3 +168,35 @@ def test_content_ready_admission_flow():
     adm.close_ready_groups()
     assert tr.calls[-1] == ("group", 0)
     adm.drain_group_closes()
+
+
+def _ids(mbs):
+    return [[i.traj_id for i in mb] for mb in mbs]
+
+
+def test_pack_groups_orders_groups_and_members_and_flushes_before_a_split():
+    # groups arrive out of order; whole groups pack greedily in group order under the budget
+    items = [Item(2, 21, 5), Item(0, 1, 4), Item(1, 11, 3), Item(0, 0, 4), Item(2, 20, 5), Item(1, 10, 3)]
+    assert _ids(pack_groups(items, max_tokens_per_microbatch=14)) == [[0, 1, 10, 11], [20, 21]]
+    # an oversized group stays whole unless splitting is asked for
+    big = [Item(0, 0, 2), Item(1, 10, 7), Item(1, 11, 7), Item(1, 12, 7), Item(2, 20, 1)]
+    assert _ids(pack_groups(big, max_tokens_per_microbatch=10)) == [[0], [10, 11, 12], [20]]
+    # with splitting, the open micro-batch flushes first and the group's runs each fit the budget
+    assert _ids(pack_groups(big, max_tokens_per_microbatch=10, split_oversized_groups=True)) == [
+        [0], [10], [11], [12], [20]]
+    assert _ids(pack_groups(big, max_tokens_per_microbatch=14, split_oversized_groups=True)) == [
+        [0], [10, 11], [12], [20]]
+
+
+@pytest.mark.parametrize("split", [False, True])
+def test_pack_groups_places_every_trajectory_once_in_canonical_order(split):
+    import random
+
+    rng = random.Random(5)
+    items = [Item(g, g * 100 + j, rng.randint(1, 9)) for g in rng.sample(range(6), 6) for j in range(rng.randint(1, 5))]
+    rng.shuffle(items)
+    mbs = pack_groups(items, max_tokens_per_microbatch=12, split_oversized_groups=split)
+    flat = [i.traj_id for mb in mbs for i in mb]
+    assert flat == sorted(i.traj_id for i in items)
+    if split:
+        assert all(sum(i.n_tokens for i in mb) <= 12 or len(mb) == 1 for mb in mbs)
