@@ -46,3 +46,33 @@ def test_load_trainer_steps(lora):
     assert stats is not None
     moved = [n for n, p in model.named_parameters() if p.requires_grad and not torch.equal(p, before[n])]
     assert moved
+
+
+@pytest.mark.parametrize("enabled", [True, False])
+def test_load_trainer_applies_determinism_before_the_model_loads(enabled, monkeypatch):
+    """The switch is process-wide and must be in force while the policy model is built."""
+    import thundersync_b200.policy_model as pm
+    from thundersync_b200.determinism import trainer_determinism
+
+    seen = {}
+
+    class Stop(Exception):
+        pass
+
+    def fake_load(policy, device):
+        seen.update(trainer_determinism())
+        raise Stop
+
+    before = trainer_determinism()
+    monkeypatch.setattr(pm, "load_policy_model", fake_load)
+    try:
+        with pytest.raises(Stop):
+            load_trainer(GrpoTrainerConfig.from_namespace(SimpleNamespace(
+                model_path="random:tiny", learning_rate=1e-3, rebuild_block_tokens=64,
+                deterministic_algorithms=enabled)), torch.device("cpu"))
+    finally:
+        torch.use_deterministic_algorithms(before["deterministic_algorithms"], warn_only=before["warn_only"])
+        torch.backends.cudnn.deterministic = before["cudnn_deterministic"]
+        torch.backends.cudnn.benchmark = before["cudnn_benchmark"]
+    assert seen["deterministic_algorithms"] is enabled and seen["cudnn_deterministic"] is enabled
+    assert seen["cudnn_benchmark"] is False and seen["fill_uninitialized_memory"] is False
