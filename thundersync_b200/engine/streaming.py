@@ -584,7 +584,8 @@ class StreamingRun:
         return list(self._groups[group_id].trajs)
 
     # ------------------------------------------------------------ turns
-    def _traj_state(self, group_id: int, traj_id: int) -> _Traj:
+    def _check_traj(self, group_id: int, traj_id: int) -> None:
+        """Raise if a turn of ``traj_id`` in ``group_id`` cannot be recorded (changes nothing)."""
         t = self._trajs.get(traj_id)
         if t is None:
             g = self._groups.get(group_id)
@@ -592,20 +593,32 @@ class StreamingRun:
                 raise KeyError(f"group {group_id} is not open")
             if traj_id in self._traj_group:
                 raise ValueError(f"trajectory {traj_id} was already freed")
+        elif t.gid != group_id:
+            raise ValueError(f"trajectory {traj_id} belongs to group {t.gid}, not {group_id}")
+
+    def _traj_state(self, group_id: int, traj_id: int) -> _Traj:
+        self._check_traj(group_id, traj_id)
+        t = self._trajs.get(traj_id)
+        if t is None:
+            g = self._groups[group_id]
             t = _Traj(tid=traj_id, gid=group_id, chain=g.chain, last=g.last, n_tokens=g.prompt_len)
             self._trajs[traj_id] = t
             self._traj_group[traj_id] = group_id
             g.trajs.append(traj_id)
-        elif t.gid != group_id:
-            raise ValueError(f"trajectory {traj_id} belongs to group {t.gid}, not {group_id}")
         return t
 
     def append_turn(self, group_id: int, traj_id: int, tokens: list[int], scored: list[bool]) -> None:
         self.append_turns([(group_id, traj_id, tokens, scored)])
 
     def append_turns(self, items: list[tuple[int, int, list[int], list[bool]]], *, joint_backward: bool = False) -> None:
-        """Record (and with ``stream_turns``, forward as one pack) arriving turns."""
-        pending: list[tuple[_Traj, list[int], list[bool]]] = []
+        """Record (and with ``stream_turns``, forward) arriving turns.
+
+        ``joint_backward``: the caller backwards the losses of these turns together (one backward per
+        call, as the scored-turn packs of on-policy distillation do), so several trajectories may forward
+        as one pack. Otherwise every trajectory's turn forwards on its own: a per-trajectory backward
+        through a shared pack graph would free the pack's saved tensors under the other trajectories.
+        Every item is checked before any state changes."""
+        checked = []
         for gid, tid, tokens, scored in items:
             tokens = [int(t) for t in tokens]
             scored = [bool(s) for s in scored]
@@ -613,6 +626,10 @@ class StreamingRun:
                 raise ValueError("tokens and scored mask must have equal length")
             if not tokens:
                 raise ValueError("a turn must contain at least one token")
+            self._check_traj(gid, tid)
+            checked.append((gid, tid, tokens, scored))
+        pending: list[tuple[_Traj, list[int], list[bool]]] = []
+        for gid, tid, tokens, scored in checked:
             t = self._traj_state(gid, tid)
             t.turns.append((tokens, scored))
             pending.append((t, tokens, scored))
@@ -621,8 +638,8 @@ class StreamingRun:
                 t.n_tokens += len(tokens)
             return
         self._check_versions()
-        # a trajectory appearing twice in one call forwards in rounds; with a turn memory rule a round runs
-        # as the widest leading packs the device admits (joint_turn_pack_width)
+        # a trajectory appearing twice in one call forwards in rounds; with a turn memory rule a joint
+        # round runs as the widest leading packs the device admits (joint_turn_pack_width)
         while pending:
             seen: set[int] = set()
             this, rest = [], []
@@ -630,10 +647,11 @@ class StreamingRun:
                 (rest if item[0].tid in seen else this).append(item)
                 seen.add(item[0].tid)
             while this:
-                width = self.joint_turn_pack_width(
-                    [(t.gid, t.tid, tokens, scored) for t, tokens, scored in this]) if len(this) > 1 else 1
-                if width == 1 and len(this) > 1 and not self.joint_turn_pack_ready:
-                    width = len(this)  # without turn-boundary replay a round is one pack, as before
+                width = 1
+                if joint_backward and len(this) > 1:
+                    width = self.joint_turn_pack_width([(t.gid, t.tid, tokens, scored) for t, tokens, scored in this])
+                    if not self.joint_turn_pack_ready:
+                        width = len(this)  # without turn-boundary replay a joint round is one pack
                 self._forward_turns(this[:width])
                 this = this[width:]
             pending = rest

@@ -259,7 +259,7 @@ class OPDTurnStream(_TokenLoss, _ImmediateBackward):
             self._check_inputs(sum(bool(s) for s in scored), teacher, weights)
         for *_, teacher, _w in items:
             self._note_finite(teacher)
-        self.run.append_turns([(g, t, tk, sc) for g, t, tk, sc, _, _ in items])
+        self.run.append_turns([(g, t, tk, sc) for g, t, tk, sc, _, _ in items], joint_backward=True)
         losses, meta = [], []
         for gid, tid, tokens, scored, teacher, weights in items:
             lp, old = self.run.consume_latest_turn_logprobs(tid)
