@@ -201,3 +201,31 @@ def test_concatenating_baseline_keeps_chains_and_same_logprobs():
     torch.testing.assert_close(out[0][0], out[1][0])
     for n in out[0][1]:
         torch.testing.assert_close(out[0][1][n], out[1][1][n])
+
+
+def test_lm_head_row_block_changes_blocks_not_results(monkeypatch):
+    """``StreamingRun(chunk=...)`` sets the LM head's rows per block; the values and gradients stay."""
+    import thundersync_b200.engine.streaming as S
+    from thundersync_b200.ops.logprob import _row_block
+
+    assert _row_block(1, True) == 128 and _row_block(129, True) == 256 and _row_block(3, False) == 3
+    with pytest.raises(ValueError):
+        _row_block(0, False)
+    seen = []
+    real = S.lm_head_logprob
+
+    def spy(h, w, t, *, rows):
+        seen.append(rows)
+        return real(h, w, t, rows=rows)
+
+    monkeypatch.setattr(S, "lm_head_logprob", spy)
+    model = build_model(41)
+    batch, order = make_batch(41, groups=1, per_group=3)
+    res = []
+    for chunk in (None, 3):
+        m = copy.deepcopy(model)
+        res.append(_grads(m, batch, order, run_kw={"chunk": chunk}, stream_turns=True))
+    assert 2048 in seen and 3 in seen
+    _close(res[0], res[1])
+    with pytest.raises(ValueError):
+        StreamingRun(model, chunk=0)

@@ -39,7 +39,7 @@ import torch
 
 from thundersync_b200.engine.boundary import Boundary
 from thundersync_b200.engine.layers import Executor, Segment, executor_for
-from thundersync_b200.ops.logprob import lm_head_logprob
+from thundersync_b200.ops.logprob import DEFAULT_ROWS, lm_head_logprob
 from thundersync_b200.ops.sink import GradSink, ParamArena, grad_sink, install_redirect_hooks
 
 __all__ = ["StreamingRun", "STREAM_ATTENTION_NAME", "register_stream_attention", "arena_for", "live_runs"]
@@ -176,7 +176,7 @@ class StreamingRun:
         self,
         model: torch.nn.Module,
         *,
-        chunk: int = 1024,
+        chunk: int | None = None,
         boundary_cut: bool = False,
         chunked_sdpa: bool = True,
         checkpoint: bool = False,
@@ -207,12 +207,12 @@ class StreamingRun:
             raise ValueError("turn-boundary rebuild requires boundary_cut=True")
         if turn_boundary_rebuild and model.training:
             raise ValueError("turn-boundary rebuild replays turns and requires model.eval()")
-        if chunk < 1:
+        if chunk is not None and chunk < 1:
             raise ValueError("chunk must be positive")
         if rebuild_block_tokens is not None and rebuild_block_tokens < 1:
             raise ValueError("rebuild_block_tokens must be positive or None")
         if boundary_adjoint_backend not in ("torch", "native", "triton"):
-            raise ValueError("boundary_adjoint_backend must be torch or native")
+            raise ValueError("boundary_adjoint_backend must be torch or native (triton is accepted as a name for native)")
         if not 1 <= boundary_adjoint_max_degree <= 16:
             raise ValueError("boundary_adjoint_max_degree must be in [1, 16]")
         if shared_prefix_vjp_backend not in ("sequential", "ready_frontier", "isolated_canonical"):
@@ -222,7 +222,7 @@ class StreamingRun:
         if parameter_adjoint_reduction not in ("arrival", "canonical_source"):
             raise ValueError("parameter_adjoint_reduction must be arrival or canonical_source")
         self.model = model
-        self.chunk = chunk
+        self.chunk = DEFAULT_ROWS if chunk is None else int(chunk)  # LM-head rows per logits/dlogits block
         self.boundary_cut = boundary_cut
         self.chunked_sdpa = chunked_sdpa  # False: the concatenating baseline (see _retain_concatenated_chains)
         self.checkpoint = checkpoint
@@ -410,7 +410,7 @@ class StreamingRun:
             picked = rows[idx[0]:idx[-1] + 1]
         else:  # index copied from page-locked memory: no host wait on the device queue
             picked = rows.index_select(0, self._ids(idx))
-        return lm_head_logprob(picked, self.weight, tgt)
+        return lm_head_logprob(picked, self.weight, tgt, rows=self.chunk)
 
     # ------------------------------------------------------------ groups
     def open_group(self, group_id: int, prompt_tokens: list[int]) -> None:

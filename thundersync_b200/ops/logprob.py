@@ -197,17 +197,27 @@ def _padded(hidden, target):
             torch.cat((target, target.new_zeros(pad))), n, pad)
 
 
+def _row_block(rows: int, cuda: bool) -> int:
+    """Rows per LM-head block: positive; on CUDA rounded up to ROW_MULTIPLE (whole GEMM row tiles)."""
+    rows = int(rows)
+    if rows < 1:
+        raise ValueError("the LM-head row block must be positive")
+    return -(-rows // ROW_MULTIPLE) * ROW_MULTIPLE if cuda else rows
+
+
 def lm_head_logprob(hidden, weight, target, *, rows: int = DEFAULT_ROWS):
+    """Log-probs of ``target`` under ``hidden @ weight.T``, ``rows`` rows per block: the backward's
+    dlogits buffer (and, off the fused path, the logits buffer) holds one block."""
     _check(hidden, weight, target)
     h, t, n, pad = _padded(hidden, target)
-    lp = _LMHeadLogprob.apply(h, weight, t, rows, False)
+    lp = _LMHeadLogprob.apply(h, weight, t, _row_block(rows, h.is_cuda), False)
     return lp[:n] if pad else lp
 
 
 def lm_head_logprob_entropy(hidden, weight, target, *, rows: int = DEFAULT_ROWS):
     _check(hidden, weight, target)
     h, t, n, pad = _padded(hidden, target)
-    lp, ent = _LMHeadLogprob.apply(h, weight, t, rows, True)
+    lp, ent = _LMHeadLogprob.apply(h, weight, t, _row_block(rows, h.is_cuda), True)
     return (lp[:n], ent[:n]) if pad else (lp, ent)
 
 
