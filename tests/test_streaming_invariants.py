@@ -229,3 +229,38 @@ def test_lm_head_row_block_changes_blocks_not_results(monkeypatch):
     _close(res[0], res[1])
     with pytest.raises(ValueError):
         StreamingRun(model, chunk=0)
+
+
+@pytest.mark.parametrize("backend,degree", [("native", 1), ("native", 2), ("triton", 16)])
+def test_boundary_adjoint_backend_stages_contributions_without_changing_the_gradient(backend, degree):
+    """Staged ledgers (reduced in arrival order when max_degree wait or the ledger is read) equal the
+    immediate fp32 adds bitwise (CPU: the same sequential adds)."""
+    model = build_model(42)
+    batch, order = make_batch(42, groups=2, per_group=4, multi_turn=True)
+    ref = _grads(copy.deepcopy(model), batch, order, stream_turns=True)
+    got = _grads(copy.deepcopy(model), batch, order, stream_turns=True,
+                 run_kw={"boundary_adjoint_backend": backend, "boundary_adjoint_max_degree": degree})
+    for n in ref:
+        assert torch.equal(ref[n], got[n]), n
+
+
+def test_boundary_ledger_flushes_at_max_degree_and_on_read():
+    from thundersync_b200.engine.boundary import Boundary
+
+    real = [torch.randn(3, 4, requires_grad=True)]
+    b = Boundary.cut([r * 1.0 for r in real], reduce_backend="native", max_degree=3)
+    parts = [torch.randn(3, 4, dtype=torch.bfloat16) for _ in range(5)]
+    for x in parts[:2]:
+        b.accumulate_explicit([x])
+    assert b.has_adjoint() and b._ledgers[0] is None and len(b._pending[0]) == 2
+    b.accumulate_explicit([parts[2]])  # the third waiting contribution triggers the reduction
+    assert b._pending[0] == [] and b._ledgers[0].dtype == torch.float32
+    for x in parts[3:]:
+        b.accumulate_explicit([x])
+    (led,) = b.peek()
+    want = torch.zeros(3, 4)
+    for x in parts:
+        want += x.float()
+    assert torch.equal(led, want)
+    with pytest.raises(ValueError):
+        Boundary.cut([torch.randn(2, requires_grad=True) * 1.0], reduce_backend="native", max_degree=17)

@@ -45,11 +45,20 @@ class Boundary:
     lifetime_contributions: int = field(default=0, init=False)
     drains: int = field(default=0, init=False)
     _sources: set = field(default_factory=set, init=False, repr=False)
+    # "torch": each contribution is added to its ledger when it arrives. "native" / "triton": contributions
+    # wait (at most max_degree per tensor) and are reduced into the ledger in arrival order by one
+    # fixed-order kernel launch (engine/boundary_adjoint.py) when max_degree are waiting or the ledger is read.
+    reduce_backend: str = "torch"
+    max_degree: int = 16
+    _pending: list[list[torch.Tensor]] = field(init=False, repr=False)
 
     def __post_init__(self) -> None:
         if len(self.real) != len(self.proxy):
             raise ValueError("boundary real and proxy tensors must align")
+        if not 1 <= self.max_degree <= 16:
+            raise ValueError("max_degree must be in [1, 16]")
         self._ledgers = [None] * len(self.proxy)
+        self._pending = [[] for _ in self.proxy]
         self._counts = [0] * len(self.proxy)
         self._hooks = []
         for i, p in enumerate(self.proxy):
@@ -68,7 +77,7 @@ class Boundary:
             p.grad = None
             if g is None:
                 return
-            ledger_accumulate(self._ledgers, index, g)
+            self._add(index, g)
             self._counts[index] += 1
             self.lifetime_contributions += 1
             if self.capture_source is not None:
@@ -79,21 +88,56 @@ class Boundary:
         return hook
 
     # ------------------------------------------------------------ adjoints
+    def _add(self, index: int, g: torch.Tensor) -> None:
+        if self.reduce_backend == "torch":
+            ledger_accumulate(self._ledgers, index, g)
+            return
+        self._pending[index].append(g.detach())
+        if len(self._pending[index]) >= self.max_degree:
+            self._flush(index)
+
+    def _flush(self, index: int) -> None:
+        """Reduce the waiting contributions of tensor ``index`` into its ledger, in arrival order."""
+        pend = self._pending[index]
+        if not pend:
+            return
+        self._pending[index] = []
+        acc = self._ledgers[index]
+        if acc is None:
+            dtype = torch.float64 if pend[0].dtype == torch.float64 else torch.float32
+            acc = torch.zeros(pend[0].shape, dtype=dtype, device=pend[0].device)
+        if (acc.is_cuda and acc.dtype == torch.float32 and acc.is_contiguous()
+                and pend[0].dtype in (torch.float32, torch.bfloat16)
+                and all(t.is_cuda and t.dtype == pend[0].dtype for t in pend)):
+            from thundersync_b200.ops._ext import native
+
+            native().reduce_into(acc.view(-1), [t.contiguous().view(-1) for t in pend])
+        else:
+            for t in pend:
+                acc.add_(t)
+        self._ledgers[index] = acc
+
+    def _flush_all(self) -> None:
+        for i in range(len(self._pending)):
+            self._flush(i)
+
     def accumulate_explicit(self, adjoints: list[torch.Tensor | None]) -> None:
         for i, a in enumerate(adjoints):
             if a is not None:
-                ledger_accumulate(self._ledgers, i, a)
+                self._add(i, a)
                 self._counts[i] += 1
                 self.lifetime_contributions += 1
 
     def has_adjoint(self) -> bool:
-        return any(x is not None for x in self._ledgers)
+        return any(x is not None for x in self._ledgers) or any(self._pending)
 
     def peek(self) -> list[torch.Tensor | None]:
+        self._flush_all()
         return list(self._ledgers)
 
     def drain(self) -> list[torch.Tensor | None]:
         """Take the ledgers (and reset them): one consumer's contribution."""
+        self._flush_all()
         out = self._ledgers
         self._ledgers = [None] * len(self.proxy)
         self._counts = [0] * len(self.proxy)
@@ -105,6 +149,7 @@ class Boundary:
         if self._consumed:
             raise RuntimeError("boundary adjoints were already consumed")
         self._consumed = True
+        self._flush_all()
         pairs = []
         for r, a in zip(self.real, self._ledgers):
             if a is not None:
@@ -133,3 +178,4 @@ class Boundary:
         self.real = []
         self.proxy = []
         self._ledgers = []
+        self._pending = []

@@ -231,6 +231,8 @@ class StreamingRun:
         self.turn_boundary_rebuild = turn_boundary_rebuild
         self.boundary_adjoint_backend = boundary_adjoint_backend
         self.boundary_adjoint_max_degree = boundary_adjoint_max_degree
+        # every boundary ledger sums its consumers' adjoints with this backend (engine/boundary.py)
+        self._boundary_kw = {"reduce_backend": boundary_adjoint_backend, "max_degree": boundary_adjoint_max_degree}
         self.parameter_adjoint_reduction = parameter_adjoint_reduction
         self.shared_prefix_vjp_mode = shared_prefix_vjp_mode
         self.explicit_adjoint_vjp = bool(explicit_adjoint_vjp)
@@ -434,7 +436,7 @@ class StreamingRun:
         real_flat = _flatten_chain(chain) + [last]
         boundary = None
         if self.boundary_cut and last.requires_grad:
-            boundary = Boundary.cut(real_flat, capture_source=lambda: self._capture_source)
+            boundary = Boundary.cut(real_flat, capture_source=lambda: self._capture_source, **self._boundary_kw)
             flat = boundary.proxy
             chain = _unflatten_chain(chain, flat[:-1])
             last = flat[-1]
@@ -509,7 +511,8 @@ class StreamingRun:
             last = h[-1]
             own_real = _flatten_state(states[0], self.spec.kinds) + [last]
             if self.boundary_cut and last.requires_grad:
-                node.boundary = Boundary.cut(own_real, capture_source=lambda: self._capture_source)
+                node.boundary = Boundary.cut(own_real, capture_source=lambda: self._capture_source,
+                                             **self._boundary_kw)
                 prox = node.boundary.proxy
                 chain = self._chain_replace_tail(chain, base_chain, prox[:-1])
                 last = prox[-1]
@@ -767,7 +770,7 @@ class StreamingRun:
             last = hs[-1]
             if self.turn_boundary_rebuild:
                 own = _flatten_state(st, self.spec.kinds) + [last]
-                b = Boundary.cut(own, capture_source=lambda: self._capture_source)
+                b = Boundary.cut(own, capture_source=lambda: self._capture_source, **self._boundary_kw)
                 b.real = [x.detach() for x in b.real]  # replay re-forwards; keep no graph
                 t.cuts.append(_TurnCut(b, t.chain, t.last, tokens, pos0))
                 chain = self._chain_replace_tail(chain, t.chain, b.proxy[:-1])
