@@ -170,8 +170,7 @@ def test_joint_turn_pack_rule():
     ck_reserve = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True,
                               checkpoint=True, rebuild_plain_reserve_bytes=0)
     assert ck_reserve.joint_turn_pack_width(items) == 3  # no device memory to read on the CPU: everything fits
-    for kw in ({"parameter_adjoint_reduction": "canonical_source"}, {"shared_prefix_vjp_mode": "source_ready_serial"},
-               {"explicit_adjoint_vjp": True}):
+    for kw in ({"parameter_adjoint_reduction": "canonical_source"}, {"explicit_adjoint_vjp": True}):
         other = StreamingRun(model, boundary_cut=True, stream_turns=True, turn_boundary_rebuild=True, **kw)
         assert not other.joint_turn_pack_ready and other.joint_turn_pack_width(items) == 1
     plain = StreamingRun(model, boundary_cut=True)

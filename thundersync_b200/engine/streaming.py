@@ -219,6 +219,14 @@ class StreamingRun:
             raise ValueError("unknown shared_prefix_vjp_backend")
         if shared_prefix_vjp_mode not in ("aggregate", "source_ready_serial"):
             raise ValueError("unknown shared_prefix_vjp_mode")
+        if shared_prefix_vjp_backend == "isolated_canonical" or shared_prefix_vjp_mode == "source_ready_serial":
+            from thundersync_b200.config import ConfigError
+
+            raise ConfigError(
+                "shared_prefix_vjp_backend='isolated_canonical' and shared_prefix_vjp_mode='source_ready_serial' "
+                "are not built here (both keep per-node parameter contributions or graphs apart until the step): "
+                "use 'sequential' or 'ready_frontier' with the 'aggregate' mode, and "
+                "parameter_adjoint_reduction='canonical_source' for an order-independent sum")
         if parameter_adjoint_reduction not in ("arrival", "canonical_source"):
             raise ValueError("parameter_adjoint_reduction must be arrival or canonical_source")
         self.model = model
@@ -239,6 +247,8 @@ class StreamingRun:
         self.shared_prefix_vjp_backend = shared_prefix_vjp_backend
         self.shared_prefix_vjp_timing = bool(shared_prefix_vjp_timing)
         self._shared_prefix_times: list[float] = []
+        self._shared_prefix_calls = 0  # autograd calls over shared prompt nodes
+        self._shared_prefix_early = 0  # nodes run before the batch barrier (dependency-ready)
         # staged parameter adjoints (canonical-source reduction) live here until they are applied
         self._param_adjoint_device = (
             None if parameter_adjoint_storage_device is None else torch.device(parameter_adjoint_storage_device)
@@ -1024,6 +1034,8 @@ class StreamingRun:
         g.boundary.release()
         g.boundary = None
         g.real_graph = []
+        if self.dependency_ready_shared_prefix_vjp and self.boundary_cut:
+            self._dependency_ready_vjps(list(g.shared_nodes), sink)
 
     def finalize_trajectories_turn_boundaries(self, traj_ids: list[int], *, sink: GradSink | None = None) -> None:
         """Replay a closure cohort's cut turns last to first, carrying later turns' adjoints back (reference
@@ -1069,28 +1081,63 @@ class StreamingRun:
             for c in cuts:
                 c.boundary.release()
 
-    def finalize_shared_prefixes(self, *, sink: GradSink | None = None) -> int:
-        """Backward every shared prompt node once, children before parents."""
-        done = 0
-        for node in reversed(self._shared):
-            if node.finalized:
-                continue
+    def _shared_node_ready(self, node: _SharedNode) -> bool:
+        """Every group under the node has run its prompt backward and every shared child is done."""
+        if node.finalized:
+            return False
+        if any(not self._shared[c].finalized for c in node.children):
+            return False
+        return all(self._groups.get(gid) is None or self._groups[gid].boundary is None for gid in node.groups)
+
+    def _run_shared_vjps(self, nodes: list[_SharedNode], sink: GradSink | None) -> None:
+        """One autograd call over independent nodes (none is an ancestor of another; children are done)."""
+        outs, grads = [], []
+        for node in nodes:
             if node.boundary is not None:
-                pairs = [(r, a) for r, a in node.boundary.consume() if r.requires_grad]
-                if pairs:
-                    t0 = time.perf_counter() if self.shared_prefix_vjp_timing else 0.0
-                    with self.capture_source(("shared_prefix", node.idx)), grad_sink(sink):
-                        torch.autograd.backward([r for r, _ in pairs], [a for _, a in pairs])
-                    if self.shared_prefix_vjp_timing:
-                        if self.device.type == "cuda":
-                            torch.cuda.synchronize(self.device)
-                        self._shared_prefix_times.append(time.perf_counter() - t0)
+                for r, a in node.boundary.consume():
+                    if r.requires_grad:
+                        outs.append(r)
+                        grads.append(a)
+        if outs:
+            src = ("shared_prefix", nodes[0].idx) if len(nodes) == 1 else (
+                "shared_prefix_frontier", tuple(n.idx for n in nodes))
+            t0 = time.perf_counter() if self.shared_prefix_vjp_timing else 0.0
+            with self.capture_source(src), grad_sink(sink):
+                torch.autograd.backward(outs, grads)
+            if self.shared_prefix_vjp_timing:
+                if self.device.type == "cuda":
+                    torch.cuda.synchronize(self.device)
+                self._shared_prefix_times.append(time.perf_counter() - t0)
+        for node in nodes:
+            if node.boundary is not None:
                 node.boundary.release()
                 node.boundary = None
             node.finalized = True
             node.chain = None
-            done += 1
-        return done
+        self._shared_prefix_calls += 1
+
+    def _dependency_ready_vjps(self, start: list[int], sink: GradSink | None) -> None:
+        """After a group's prompt backward: run each ancestor shared node, deepest first, once it is ready."""
+        for idx in start:
+            node = self._shared[idx]
+            if not self._shared_node_ready(node):
+                break
+            self._run_shared_vjps([node], sink)
+            self._shared_prefix_early += 1
+
+    def finalize_shared_prefixes(self, *, sink: GradSink | None = None) -> int:
+        """Backward every remaining shared prompt node once, children before parents: one autograd call
+        per node (``shared_prefix_vjp_backend="sequential"``) or per frontier of nodes whose children are
+        all done (``"ready_frontier"``)."""
+        done = 0
+        while True:
+            pending = [n for n in reversed(self._shared) if not n.finalized]
+            if not pending:
+                return done
+            frontier = [n for n in pending if all(self._shared[c].finalized for c in n.children)]
+            batch = frontier if self.shared_prefix_vjp_backend == "ready_frontier" else frontier[:1]
+            self._run_shared_vjps(batch, sink)
+            done += len(batch)
 
     # ------------------------------------------------------------ parameter adjoints
     def accumulate_parameter_adjoint(self, parameter: torch.Tensor, value: torch.Tensor, *, source: Any = None) -> None:
@@ -1238,6 +1285,9 @@ class StreamingRun:
             "backend": self.shared_prefix_vjp_backend,
             "nodes": len(self._shared),
             "finalized": sum(1 for n in self._shared if n.finalized),
+            "autograd_calls": self._shared_prefix_calls,
+            "dependency_ready": self.dependency_ready_shared_prefix_vjp,
+            "finalized_before_barrier": self._shared_prefix_early,
         }
         if self.shared_prefix_vjp_timing:  # wall seconds per shared-prefix backward (device-synchronised)
             out["vjp_seconds"] = list(self._shared_prefix_times)
