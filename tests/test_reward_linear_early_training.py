@@ -172,3 +172,48 @@ def test_abort_frees_held_sources_and_refuses_the_step():
     assert bw.open_groups() == []
     with pytest.raises(RuntimeError):
         bw.assert_safe_to_step()
+
+
+def test_deferred_group_closes_run_in_request_order_at_later_safe_points(monkeypatch):
+    """defer_group_close: a close that would wait for host folds returns at once and runs later, in
+    request order; the gradient equals closing at once bitwise."""
+    model = build_model(27)
+    batch, _ = make_batch(27, groups=3, per_group=2)
+    ref = _run(model, batch, _close_path(batch))
+
+    m = copy.deepcopy(model)
+    run = StreamingRun(m, boundary_cut=True, stream_turns=False)
+    bw = RewardLinearBackward(run, m, eps=EPS, defer_group_close=True)
+    pending = {"on": True}
+    monkeypatch.setattr(bw, "_folds_pending", lambda: pending["on"])
+    for g, prompt, trajs in batch:
+        bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    order = []
+    real = bw._close_group_now
+    monkeypatch.setattr(bw, "_close_group_now", lambda g: (order.append(g), real(g)))
+    (g0, _, t0), (g1, _, t1), (g2, _, t2) = batch
+    for g, trajs in ((g0, t0), (g1, t1)):
+        for tid, turns, reward in trajs:
+            _append(run, g, turns, tid)
+            bw.close_trajectory(tid, reward)
+        bw.close_group(g)
+    assert order == [] and bw.open_groups() == [g0, g1, g2]
+    assert bw.source_offload_report["group_closes_deferred"] == 2
+    with pytest.raises(RuntimeError):
+        bw.close_group(g0)  # already requested
+    pending["on"] = False
+    tid, turns, reward = t2[0]
+    _append(run, g2, turns, tid)
+    bw.close_trajectory(tid, reward)  # a safe point: both requested closes run, in order
+    assert order == [g0, g1] and bw.open_groups() == [g2]
+    tid, turns, reward = t2[1]
+    _append(run, g2, turns, tid)
+    bw.close_trajectory(tid, reward)
+    pending["on"] = True
+    bw.close_group(g2)
+    assert order == [g0, g1]
+    bw.assert_safe_to_step()  # waits, then runs the last request
+    assert order == [g0, g1, g2]
+    got = {n: p.grad.detach().clone() for n, p in m.named_parameters()}
+    for n in ref:
+        assert torch.equal(got[n], ref[n]), n

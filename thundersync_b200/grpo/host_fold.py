@@ -148,6 +148,10 @@ class HostFoldPipeline:
             self.report["folds"] += 1
             self.report["fold_bytes"] += 4 * n
 
+    def pending(self) -> bool:
+        """Whether host folds are still running (nothing waits)."""
+        return any(not f.done() for w in self._ring for f in w.pending)
+
     def drain(self) -> None:
         """Wait for every host fold and combine still running."""
         for w in self._ring:

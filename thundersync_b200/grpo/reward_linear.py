@@ -175,8 +175,11 @@ class RewardLinearBackward:
             "sources": 0, "direct_sources": 0, "binary_sources": 0, "folds": 0,
             "group_closes": 0, "uniform_reward_groups": 0, "fold_s": 0.0, "backward_s": 0.0,
             "statistic_device": str(stat_dev), "device_groups_below_hbm_threshold": 0, "host_groups": 0,
-            "combined_sources": 0,
+            "combined_sources": 0, "group_closes_deferred": 0,
         }
+        # group closes requested while host folds were still running (defer_group_close); they run in
+        # request order at later safe points
+        self._requested_closes: list[int] = []
         self._versions = {id(p): p._version for p in run._trainable}
 
     # ------------------------------------------------------------ configuration
@@ -327,6 +330,7 @@ class RewardLinearBackward:
                 else:
                     tid, reward, w = cohort[0]
                     self._differentiate(tid, reward, w)
+        self._run_requested_closes(wait=False)
 
     def _cohorts(self, items: list[tuple[int, float, Any]]) -> list[list[tuple[int, float, Any]]]:
         """With ``combine_known_reward_sources``: closes of one group that share a reward (and carry no
@@ -405,6 +409,7 @@ class RewardLinearBackward:
             src = self.arena.new_buffer(torch.float32)
             bnd = self._backward_source(tid, w, GradSink(self.arena, src))
             acc.prepared[tid] = (src, bnd)
+        self._run_requested_closes(wait=False)
 
     def bind_reward(self, traj_id: int, reward: float) -> None:
         self.bind_rewards([(traj_id, reward)])
@@ -421,6 +426,7 @@ class RewardLinearBackward:
                 src, bnd = acc.prepared.pop(tid)
                 self._fold(acc, tid, reward, src, bnd)
                 acc.closed.add(tid)
+        self._run_requested_closes(wait=False)
 
     def record_rewards(self, items: list[tuple[int, float]]) -> None:
         for tid, reward in items:
@@ -585,16 +591,43 @@ class RewardLinearBackward:
     def held_source_count(self) -> int:
         return sum(len(a.prepared) for a in self._groups.values())
 
+    def _folds_pending(self) -> bool:
+        return self._host_fold is not None and self._host_fold.pending()
+
+    def _run_requested_closes(self, *, wait: bool) -> None:
+        """Run requested group closes in request order; without ``wait`` stop at the first one that
+        would have to wait for host folds still running."""
+        while self._requested_closes:
+            if not wait and self._folds_pending():
+                return
+            self._close_group_now(self._requested_closes.pop(0))
+
     def close_group(self, group_id: int) -> None:
-        """All rewards in: combine the statistics, backward the prompt once."""
+        """All rewards in: combine the statistics, backward the prompt once.
+
+        With ``defer_group_close``, a close that would wait for host folds still running is recorded and
+        the call returns; recorded closes run in request order (so the parameter gradient accumulates in
+        the same order as closing at once) at the end of a later prepare, bind or close call, at the next
+        ``close_group``, or in :meth:`assert_safe_to_step`, which waits for the folds (reference
+        src/thundersync/grpo/reward_linear.py:3359-3400)."""
         acc = self._groups.get(group_id)
         if acc is None:
             raise KeyError(f"group {group_id} is not registered")
-        if acc.done:
+        if acc.done or group_id in self._requested_closes:
             raise RuntimeError(f"group {group_id} is already closed")
         missing = [t for t in acc.traj_ids if t not in acc.closed]
         if missing:
             raise RuntimeError(f"group {group_id} still has open trajectories {missing}")
+        if self.defer_group_close:
+            self._requested_closes.append(group_id)
+            self._run_requested_closes(wait=False)
+            if group_id in self._requested_closes:
+                self._report["group_closes_deferred"] += 1
+            return
+        self._close_group_now(group_id)
+
+    def _close_group_now(self, group_id: int) -> None:
+        acc = self._groups[group_id]
         self._check_versions()
         mean, std = self._moments(acc)
         main = self._main_grad()
@@ -702,6 +735,7 @@ class RewardLinearBackward:
         """Refuse while any group is open; otherwise finish the batch gradient."""
         if self._aborted:
             raise RuntimeError("this backward was aborted")
+        self._run_requested_closes(wait=True)
         open_ = [g for g, a in self._groups.items() if not a.done]
         if open_:
             raise RuntimeError(f"cannot step: groups {open_} are still open")
@@ -730,6 +764,7 @@ class RewardLinearBackward:
 
     def abort(self) -> None:
         self._aborted = True
+        self._requested_closes = []
         if self._host_fold is not None:
             self._host_fold.drain()
             if self._host_fold_options.get("arena") is not None:
