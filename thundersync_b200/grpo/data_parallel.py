@@ -356,6 +356,50 @@ class DataParallelThunderSync:
         grad = self.bw.main_grad()
         if grad is None:
             grad = self.arena.new_buffer(torch.float32)
+        if self._sharded_step is not None:
+            # a caller-built ShardedOptimizerStep (engine/sharded_step.py) owns reduction, clipping and the
+            # step over replicated p.grad (reference src/thundersync/grpo/data_parallel.py:721-735)
+            if gradient_observer is not None:
+                raise RuntimeError("gradient observers are not supported under the sharded optimizer step")
+            with torch.no_grad():
+                for p in self._trainable:
+                    p.grad = (self.arena.view(grad, p) * scale).to(p.dtype)
+            shard_stats = self._sharded_step.step()
+            t2 = time.perf_counter()
+            stats["n_global_groups"] = n_global
+            stats["group_counts_by_rank"] = counts_l
+            stats["local_gradient_scale"] = scale
+            stats["grad_bytes"] = grad.numel() * grad.element_size()
+            for k in ("allreduce_s", "global_grad_norm", "grad_clip", "gradient_was_clipped", "opt_step_s"):
+                stats[k] = shard_stats[k]
+            stats["sharded_step"] = shard_stats
+        else:
+            t2 = self._replicated_or_flat_step(grad, scale, stats, n_global, counts_l, gradient_observer, sync)
+        if self.reducer is not None:
+            self.reducer.check()
+        if sync:
+            torch.cuda.synchronize(self.device)
+        t3 = time.perf_counter()
+        if self._sharded_step is None:
+            stats["opt_step_s"] = t3 - t2
+        stats["step_total_s"] = t3 - t0
+        stats["source_offload_report"] = self.bw.source_offload_report
+        stats["rebuild_path_counts"] = self.run.rebuild_path_counts
+        if self._work_claims_report is not None:
+            stats["work_claims"] = self._work_claims_report
+        stats["run_retained_bytes"] = self.run.retained_device_bytes()
+        stats["backward_retained_bytes"] = self.bw.retained_device_bytes()
+        if sync:
+            a = torch.cuda.memory_stats(self.device)
+            stats["cuda_allocator"] = {k: a.get(k) for k in ("num_alloc_retries", "num_ooms", "num_device_alloc",
+                                                              "num_device_free", "num_sync_all_streams")}
+        self._steps_done += 1
+        self._new_batch()
+        return stats
+
+    def _replicated_or_flat_step(self, grad, scale, stats, n_global, counts_l, gradient_observer, sync) -> float:
+        """Reduce the flat gradient (or reduce-scatter it under the sharded flat AdamW), clip, step; returns
+        the time the reduction ended."""
         t1 = time.perf_counter()
         norm_t = None
         if self._sharded_flat:
@@ -395,29 +439,10 @@ class DataParallelThunderSync:
             norm_value = float(nrm)
             self.optimizer.step()
             self.optimizer.zero_grad(set_to_none=True)
-        if self.reducer is not None:
-            self.reducer.check()
-        if sync:
-            torch.cuda.synchronize(self.device)
-        t3 = time.perf_counter()
         stats["global_grad_norm"] = norm_value
         stats["grad_clip"] = self.grad_clip
         stats["gradient_was_clipped"] = self.grad_clip is not None and norm_value > self.grad_clip
-        stats["opt_step_s"] = t3 - t2
-        stats["step_total_s"] = t3 - t0
-        stats["source_offload_report"] = self.bw.source_offload_report
-        stats["rebuild_path_counts"] = self.run.rebuild_path_counts
-        if self._work_claims_report is not None:
-            stats["work_claims"] = self._work_claims_report
-        stats["run_retained_bytes"] = self.run.retained_device_bytes()
-        stats["backward_retained_bytes"] = self.bw.retained_device_bytes()
-        if sync:
-            a = torch.cuda.memory_stats(self.device)
-            stats["cuda_allocator"] = {k: a.get(k) for k in ("num_alloc_retries", "num_ooms", "num_device_alloc",
-                                                              "num_device_free", "num_sync_all_streams")}
-        self._steps_done += 1
-        self._new_batch()
-        return stats
+        return t2
 
     def _sharded_update(self, grad: torch.Tensor, scale: float):
         """ZeRO-1: reduce-scatter, shard-local AdamW, parameter all-gather."""
