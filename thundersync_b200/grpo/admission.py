@@ -6,8 +6,10 @@ reward in the trainer's ledger and makes the trajectory a close. The close is
 fixed) and *known* otherwise. ``drain_ready_closes`` runs final closes first
 and outside the residency budget, then known closes within it; with
 ``final_forest`` a backlog that is all final once the step's last verdict
-landed runs as one shared-prefix forest call. Between packs the admission
-yields to waiting trainer events (``events_waiting``). The policy is that of
+landed runs as one shared-prefix forest call; with ``known_reserve_slabs``
+known closes run outside the held-source budget, up to the reserve per drain.
+Between packs the admission yields to waiting trainer events
+(``events_waiting``). The policy is that of
 reference src/thundersync/grpo/admission.py:77-261; the code is this
 package's: closes are ranked by a class function and drained class by class.
 """
@@ -102,7 +104,21 @@ class FinalFirstAdmission(ContentReadyAdmission):
             if left or (known and self._interrupted()):
                 self._closes = left + known
                 return
+        if self._known_reserve_slabs:
+            self._closes = self._drain_known_reserved(known)
+            return
         self._closes = self._drain(known, gated=True, job_class=KNOWN)
+
+    def _drain_known_reserved(self, known: list[Close]) -> list[Close]:
+        """With ``known_reserve_slabs``: known closes run outside the held-source budget (a known close
+        holds no source that waits for a reward, so it never queues behind content work), at most the
+        reserve per drain -- fewer when the trainer reports fewer free known slabs."""
+        cap_fn = getattr(self._ledger, "known_slab_capacity", None)
+        cap = cap_fn() if cap_fn is not None else None
+        n = self._known_reserve_slabs if cap is None else min(self._known_reserve_slabs, max(0, int(cap)))
+        if n == 0:
+            return known
+        return self._drain(known[:n], gated=False, job_class=KNOWN) + known[n:]
 
     def _drain_final(self, closes: list[Close]) -> list[Close]:
         """Final closes ignore the budget but give way to waiting events between packs."""

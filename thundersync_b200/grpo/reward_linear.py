@@ -299,8 +299,10 @@ class RewardLinearBackward:
     def registered_groups_fully_bound(self) -> bool:
         return all(self.group_fully_bound(g) for g, a in self._groups.items() if not a.done)
 
-    def known_slab_capacity(self) -> int:
-        return 0
+    def known_slab_capacity(self) -> int | None:
+        """Free slabs a known close could take beyond the held-source budget; None: unbounded here (a
+        known close differentiates into one reused scratch buffer and folds at once, holding nothing)."""
+        return None
 
     # ------------------------------------------------------------ trajectory events
     def close_trajectory(self, traj_id: int, reward: float, token_weights: torch.Tensor | None = None) -> None:
