@@ -100,3 +100,37 @@ def test_memory_report_shape_without_a_device():
     assert diag["write_bytes"] == 0 and diag["read_bytes"] == 0
     shape = run._turn_memory_shape()
     assert shape["plain_activation"] > shape["checkpoint_activation"] > shape["host_checkpoint_activation"] > 0
+
+
+def test_several_branches_rebuild_apart_unless_backwarded_jointly():
+    """Without joint_backward each branch's graph is its own: per-branch backwards all work; with it the
+    branches share one pack and one backward. Both give the same log-probs."""
+    import copy
+
+    from tests.grpo_fixtures import build_model, make_batch
+    from thundersync_b200.engine.streaming import StreamingRun
+
+    base = build_model(61)
+    batch, _ = make_batch(61, groups=1, per_group=3)
+    g, prompt, trajs = batch[0]
+    out = []
+    for joint in (False, True):
+        m = copy.deepcopy(base)
+        run = StreamingRun(m, boundary_cut=True, stream_turns=False)
+        run.open_group(g, prompt)
+        for tid, turns, _ in trajs:
+            for tk, sc in turns:
+                run.append_turn(g, tid, tk, sc)
+        tids = [t for t, _, _ in trajs]
+        lps = run.rebuild_logprobs(tids, joint_backward=joint, releasing_bytes=lambda: 1 << 20)
+        if joint:
+            sum(lp.sum() for lp in lps).backward()
+        else:
+            for lp in lps:
+                lp.sum().backward()  # one branch at a time
+        out.append(([lp.detach() for lp in lps], {n: p.grad.clone() for n, p in m.named_parameters()
+                                                   if p.grad is not None}))
+    for a, b in zip(out[0][0], out[1][0]):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+    for n in out[0][1]:
+        torch.testing.assert_close(out[0][1][n], out[1][1][n], rtol=1e-5, atol=1e-6)

@@ -217,3 +217,43 @@ def test_deferred_group_closes_run_in_request_order_at_later_safe_points(monkeyp
     got = {n: p.grad.detach().clone() for n, p in m.named_parameters()}
     for n in ref:
         assert torch.equal(got[n], ref[n]), n
+
+
+def test_reduction_hooks_follow_the_host_fold_pipeline():
+    """group_reduction_complete / pending_reduction_source_count / wait_for_trajectory_reduction read the
+    host fold pipeline (a stand-in here: the real one streams from a CUDA device)."""
+
+    class FakePipe:
+        def __init__(self):
+            self.running = 2
+            self.drains = 0
+
+        def pending_count(self):
+            return self.running
+
+        def pending(self):
+            return self.running > 0
+
+        def drain(self):
+            self.drains += 1
+            self.running = 0
+
+    model = build_model(28)
+    batch, _ = make_batch(28, groups=1, per_group=2)
+    run, bw = _setup(model)
+    g, prompt, trajs = batch[0]
+    bw.open_group(g, prompt, [t for t, _, _ in trajs])
+    for tid, turns, reward in trajs:
+        _append(run, g, turns, tid)
+        bw.close_trajectory(tid, reward)
+    assert bw.group_reduction_complete(g) and bw.pending_reduction_source_count == 0
+    pipe = FakePipe()
+    bw._host_fold = pipe
+    assert not bw.group_reduction_complete(g) and bw.pending_reduction_source_count == 2
+    with pytest.raises(KeyError):
+        bw.wait_for_trajectory_reduction(g, 10_000)
+    bw.wait_for_trajectory_reduction(g, trajs[0][0])
+    assert pipe.drains == 1 and bw.group_reduction_complete(g)
+    bw._host_fold = None
+    bw.close_group(g)
+    bw.assert_safe_to_step()

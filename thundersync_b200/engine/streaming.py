@@ -33,7 +33,7 @@ import contextlib
 import time
 import hashlib
 from dataclasses import dataclass, field
-from typing import Any, Iterable
+from typing import Any, Callable, Iterable
 
 import torch
 
@@ -855,12 +855,13 @@ class StreamingRun:
                "checkpoint_host": "host_checkpoint_activation"}[rung]
         return tokens * (shape[key] + shape["kv"] + 2 * shape["hidden"])
 
-    def _choose_rung(self, tokens: int) -> str:
-        """The first rung whose estimate fits the device beside the configured reserve."""
+    def _choose_rung(self, tokens: int, *, extra: int = 0) -> str:
+        """The first rung whose estimate fits the device beside the configured reserve (``extra``: bytes the
+        caller frees before the backward, counted as available)."""
         if self.device.type != "cuda":
             return "checkpoint" if self.checkpoint else "blocked"
         reserve = self.rebuild_plain_reserve_bytes or 0
-        avail = self._available_bytes()
+        avail = self._available_bytes() + max(0, extra)
         first = 2 if self.checkpoint else 0
         for rung in self.REBUILD_RUNGS[first:]:
             if rung == "plain" and self.rebuild_plain_reserve_bytes is None:
@@ -887,9 +888,15 @@ class StreamingRun:
         joint_backward: bool = False,
         executor: str = "auto",
         checkpoint_input_storage_device: Any = None,
-        releasing_bytes: int | None = None,
+        releasing_bytes: int | Callable[[], int] | None = None,
     ) -> list[torch.Tensor]:
-        """Re-forward whole branches (all turns) over the prompt chain, packed.
+        """Re-forward whole branches (all turns) over the prompt chain.
+
+        With ``joint_backward`` (the caller backwards the branches' log-probs together) several branches
+        forward as one pack; otherwise each branch forwards on its own, so that one branch's backward
+        never frees a graph another branch still needs. ``releasing_bytes`` (bytes, or a callable giving
+        them) is device memory the caller frees before the backward: the automatic rung choice counts it
+        as available.
 
         ``executor`` picks the rung of the memory ladder: ``plain`` (one pack per call, every activation
         kept), ``blocked`` (branches longer than ``rebuild_block_tokens`` run in consecutive blocks, each
@@ -904,12 +911,17 @@ class StreamingRun:
         if executor not in rungs:
             raise ValueError(f"executor must be one of {rungs}")
         self._check_versions()
+        if len(traj_ids) > 1 and not joint_backward:
+            return [self.rebuild_logprobs([t], executor=executor, releasing_bytes=releasing_bytes,
+                                          checkpoint_input_storage_device=checkpoint_input_storage_device)[0]
+                    for t in traj_ids]
         trajs = [self._trajs[t] for t in traj_ids]
         n_tok = sum(len(x) for t in trajs for x, _ in t.turns)
         if executor != "auto":
             rung = executor
         else:
-            rung = self._choose_rung(n_tok)
+            extra = releasing_bytes() if callable(releasing_bytes) else (releasing_bytes or 0)
+            rung = self._choose_rung(n_tok, extra=int(extra))
         if checkpoint_input_storage_device is not None and torch.device(checkpoint_input_storage_device).type == "cpu" \
                 and rung == "checkpoint":
             rung = "checkpoint_host"

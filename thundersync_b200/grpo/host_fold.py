@@ -150,7 +150,11 @@ class HostFoldPipeline:
 
     def pending(self) -> bool:
         """Whether host folds are still running (nothing waits)."""
-        return any(not f.done() for w in self._ring for f in w.pending)
+        return self.pending_count() > 0
+
+    def pending_count(self) -> int:
+        """Host window folds and combines still running."""
+        return sum(1 for w in self._ring for f in w.pending if not f.done())
 
     def drain(self) -> None:
         """Wait for every host fold and combine still running."""

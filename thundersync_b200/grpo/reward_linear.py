@@ -364,7 +364,7 @@ class RewardLinearBackward:
         if self.run.stream_turns:
             lps = [self._logprobs(t) for t in tids]
         else:
-            lps = self.run.rebuild_logprobs(tids)  # one packed forward over every branch
+            lps = self.run.rebuild_logprobs(tids, joint_backward=True)  # one packed forward, one backward
         s = torch.cat([lp.reshape(-1) for lp in lps]).sum()
         binary_sink = self._binary and self.statistic_device == self.run.device
         if binary_sink:
@@ -579,15 +579,23 @@ class RewardLinearBackward:
         return (acc.rewards[traj_id] - mean) / std
 
     def wait_for_trajectory_reduction(self, group_id: int, trajectory_id: int) -> None:
-        return None  # folds are stream-ordered device work
+        """Return once the trajectory's source is folded into its group's statistics: device folds are
+        stream-ordered, host folds (statistics on the host) are waited for."""
+        acc = self._groups[group_id]
+        if int(trajectory_id) not in acc.traj_ids:
+            raise KeyError(f"trajectory {trajectory_id} is not in group {group_id}")
+        if self._host_fold is not None:
+            self._host_fold.drain()
 
     def group_reduction_complete(self, group_id: int) -> bool:
+        """No source of the group waits for its reward and no host fold is still running."""
         acc = self._groups[group_id]
-        return not acc.prepared
+        return not acc.prepared and not self._folds_pending()
 
     @property
     def pending_reduction_source_count(self) -> int:
-        return 0
+        """Host folds still running (0 when statistics stay on the device)."""
+        return 0 if self._host_fold is None else self._host_fold.pending_count()
 
     @property
     def held_source_count(self) -> int:
