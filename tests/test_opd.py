@@ -74,7 +74,9 @@ def test_turn_stream_matches_monolithic():
     assert obj.loss_value == pytest.approx(obj.loss_value)
 
 
-def test_opd_stream_with_teacher_model():
+@pytest.mark.parametrize("joint", [False, True])
+def test_opd_stream_with_teacher_model(joint):
+    """Per-trajectory closes, or one call closing the group's trajectories with one joint backward."""
     model = build_model(6)
     teacher = build_model(7)
     eps = _episodes(1, groups=1, per_group=3)
@@ -87,14 +89,17 @@ def test_opd_stream_with_teacher_model():
             trajs[i] = (tid, [(tk, sc, t) for (tk, sc, _), t in zip(turns, parts)])
     ref = _reference(copy.deepcopy(model), eps)
     run = StreamingRun(model, boundary_cut=True)
-    obj = OPDStream(run, model, teacher=teacher)
+    obj = OPDStream(run, model, teacher=teacher, joint_backward=joint)
     for g, prompt, trajs in eps:
         obj.open_group(g, prompt)
         for tid, turns in trajs:
             for tk, sc, _ in turns:
                 run.append_turn(g, tid, tk, sc)
-        for tid, _ in trajs:
-            obj.close_trajectory(tid)
+        if joint:
+            obj.close_trajectories([tid for tid, _ in trajs])
+        else:
+            for tid, _ in trajs:
+                obj.close_trajectory(tid)
         obj.close_group(g)
     obj.assert_safe_to_step()
     for n, p in model.named_parameters():

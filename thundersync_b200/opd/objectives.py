@@ -324,6 +324,11 @@ class OPDStream(_TokenLoss, _ImmediateBackward):
     itself; with ``concurrent_teacher_replay`` it runs on its own device in a
     worker thread while the student differentiates the previous trajectory.
     A teacher failure poisons the step (``assert_safe_to_step`` re-raises).
+    ``joint_backward``: the trajectories closed by one call run one backward over
+    their summed losses. ``closure_cohort_vjp`` and ``ragged_cohort_attention``
+    are accepted for the reference's signature and change nothing here: a
+    closure cohort's one backward is ``joint_backward``'s, and segments of a
+    pack always attend through the packed attention kernels.
     """
 
     def __init__(self, run, model: torch.nn.Module, *, teacher: torch.nn.Module | None = None,
@@ -341,6 +346,8 @@ class OPDStream(_TokenLoss, _ImmediateBackward):
         self._pool = concurrent.futures.ThreadPoolExecutor(1) if self.concurrent else None
         self._poison: BaseException | None = None
         self._prompts: dict[int, list[int]] = {}
+        # several trajectories closed in one call run one backward over their summed losses
+        self.joint_backward = bool(joint_backward)
 
     def open_group(self, group_id: int, prompt_tokens: list[int]) -> None:
         self._prompts[group_id] = list(prompt_tokens)
@@ -362,6 +369,8 @@ class OPDStream(_TokenLoss, _ImmediateBackward):
             raise RuntimeError("a concurrent teacher replay failed; this step is poisoned") from self._poison
         norm = [(i, None, None) if isinstance(i, int) else (i[0], i[1] if len(i) > 1 else None,
                                                              i[2] if len(i) > 2 else None) for i in items]
+        joint = self.joint_backward and len(norm) > 1
+        losses: list[tuple[torch.Tensor, int, Any]] = []
         futures = {}
         for tid, teacher, _ in norm:
             if teacher is None:
@@ -383,9 +392,22 @@ class OPDStream(_TokenLoss, _ImmediateBackward):
             self._note_finite(teacher)
             if lp.numel():
                 loss = self._loss(lp, old, teacher, weights)
+                if joint:
+                    losses.append((loss, lp.numel(), weights))
+                    continue
                 self.run.backward_with_boundary_adjoint_capture(loss, source=("trajectory", tid), sink=self._sink())
                 self._record(loss, lp.numel(), weights, False)
-            self.run.free_trajectory(tid)
+            if not joint:
+                self.run.free_trajectory(tid)
+        if joint:
+            if losses:
+                self.run.backward_with_boundary_adjoint_capture(
+                    [x for x, _, _ in losses], source=("trajectory_cohort", tuple(t for t, _, _ in norm)),
+                    sink=self._sink())
+                for loss, n, weights in losses:
+                    self._record(loss, n, weights, False)
+            for tid, _, _ in norm:
+                self.run.free_trajectory(tid)
 
     def assert_safe_to_step(self, *, materialize: bool = True) -> None:
         if self._poison is not None:
