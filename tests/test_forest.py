@@ -2,6 +2,7 @@
 
 from __future__ import annotations
 
+import copy
 import random
 
 import torch
@@ -127,3 +128,39 @@ def test_forest_context_binds_and_restores_plans():
         lp_outer.sum().backward()  # the step's backward inside the context, as with checkpointing
     assert bound_plan("cpu") is None
     torch.testing.assert_close(lp_outer.detach(), forest_logprobs(model, outer).detach(), rtol=0, atol=0)
+
+
+def test_every_share_and_gate_setting_is_the_same_computation():
+    """Shared or unshared forest, gated head or every position projected: same log-probs and gradients."""
+    base = build_model(6)
+    trajs = _batch(5)
+    res = []
+    for share in (True, False):
+        for gate in (True, False):
+            m = copy.deepcopy(base)
+            forest = build_forest(trajs if share else unshared(trajs))
+            plan = compile_plan(forest)
+            lp = forest_logprobs(m, plan, gate=gate)
+            (lp * torch.linspace(0.5, 1.5, lp.numel())).sum().backward()
+            res.append((lp.detach(), {n: p.grad for n, p in m.named_parameters()}, plan))
+    lp0, g0, p0 = res[0]
+    for lp, g, plan in res[1:]:
+        torch.testing.assert_close(lp, lp0, rtol=1e-5, atol=1e-6)
+        for n in g0:  # fp32 summation order differs: compare in norm
+            assert float((g[n] - g0[n]).norm() / g0[n].norm().clamp_min(1e-30)) < 1e-5, n
+    shared_plan, unshared_plan = res[0][2], res[2][2]
+    assert shared_plan.n_physical < unshared_plan.n_physical  # the shared forest forwards fewer tokens
+    assert unshared_plan.n_physical == shared_plan.forest.logical_tokens  # unshared shares nothing
+
+
+def test_the_executor_cache_does_not_keep_a_dropped_model_alive():
+    import gc
+    import weakref
+
+    m = build_model(7)
+    plan = compile_plan(build_forest(_batch(6)))
+    forest_logprobs(m, plan).sum().backward()
+    ref = weakref.ref(m)
+    del m
+    gc.collect()
+    assert ref() is None
