@@ -247,6 +247,10 @@ class StreamingRun:
         self.shared_prefix_vjp_backend = shared_prefix_vjp_backend
         self.shared_prefix_vjp_timing = bool(shared_prefix_vjp_timing)
         self._shared_prefix_times: list[float] = []
+        # set by objectives whose unscored turns have no loss of their own (on-policy distillation turns)
+        self.defer_unscored_turns = False
+        self._deferred_turns = 0  # turns held back at arrival
+        self._deferred_forwards = 0  # held-back turns forwarded when a later turn needed their state
         self._shared_prefix_calls = 0  # autograd calls over shared prompt nodes
         self._shared_prefix_early = 0  # nodes run before the batch barrier (dependency-ready)
         # staged parameter adjoints (canonical-source reduction) live here until they are applied
@@ -641,13 +645,13 @@ class StreamingRun:
                 raise ValueError("a turn must contain at least one token")
             self._check_traj(gid, tid)
             checked.append((gid, tid, tokens, scored))
-        pending: list[tuple[_Traj, list[int], list[bool]]] = []
+        pending: list[tuple[_Traj, list[int], list[bool], int]] = []  # (trajectory, tokens, scored, turn index)
         for gid, tid, tokens, scored in checked:
             t = self._traj_state(gid, tid)
             t.turns.append((tokens, scored))
-            pending.append((t, tokens, scored))
+            pending.append((t, tokens, scored, len(t.turns) - 1))
         if not self.stream_turns:
-            for t, tokens, _ in pending:
+            for t, tokens, _, _ in pending:
                 t.n_tokens += len(tokens)
             return
         self._check_versions()
@@ -659,13 +663,16 @@ class StreamingRun:
             for item in pending:
                 (rest if item[0].tid in seen else this).append(item)
                 seen.add(item[0].tid)
+            if self.defer_unscored_turns:
+                this = self._settle_deferred(this)
             while this:
                 width = 1
                 if joint_backward and len(this) > 1:
-                    width = self.joint_turn_pack_width([(t.gid, t.tid, tokens, scored) for t, tokens, scored in this])
+                    width = self.joint_turn_pack_width([(t.gid, t.tid, tokens, scored)
+                                                        for t, tokens, scored, _ in this])
                     if not self.joint_turn_pack_ready:
                         width = len(this)  # without turn-boundary replay a joint round is one pack
-                self._forward_turns(this[:width])
+                self._forward_turns([x[:3] for x in this[:width]])
                 this = this[width:]
             pending = rest
 
@@ -751,6 +758,24 @@ class StreamingRun:
         t = self._trajs[traj_id]
         return sum(len(tk) for tk, _ in t.turns)
 
+    def _settle_deferred(self, items: list[tuple[_Traj, list[int], list[bool], int]]):
+        """With ``defer_unscored_turns``: before a trajectory's new turn forwards, its deferred turns
+        forward first, each as its own single-turn call at its own positions; a new turn without a
+        scored token is itself deferred (its state is read only by a later turn of its trajectory, and a
+        turn that ends the trajectory is never forwarded). Returns the items to forward now."""
+        out = []
+        for item in items:
+            t, _, scored, k = item
+            while t.forwarded_turns < k:
+                tk, sc = t.turns[t.forwarded_turns]
+                self._forward_turns([(t, tk, sc)])
+                self._deferred_forwards += 1
+            if any(scored):
+                out.append(item)
+            else:
+                self._deferred_turns += 1
+        return out
+
     def forward_deferred_turns(self, traj_id: int) -> None:
         t = self._trajs[traj_id]
         if t.forwarded_turns < len(t.turns):
@@ -816,6 +841,9 @@ class StreamingRun:
 
     def consume_latest_turn_logprobs(self, traj_id: int) -> tuple[torch.Tensor, torch.Tensor]:
         t = self._trajs[traj_id]
+        if t.forwarded_turns < len(t.turns):  # the latest turn is deferred: it has no log-probs yet
+            empty = torch.zeros(0, dtype=torch.float32, device=self.device)
+            return empty, empty
         if not t.logprobs:
             raise RuntimeError("no forwarded turn to consume")
         lp, old = t.logprobs[-1], t.old[-1]

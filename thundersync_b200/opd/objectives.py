@@ -237,6 +237,9 @@ class OPDTurnStream(_TokenLoss, _ImmediateBackward):
             raise ValueError("OPDTurnStream requires StreamingRun(turn_boundary_rebuild=True)")
         _ImmediateBackward.__init__(self, run, model)
         self._init_loss(normalization)
+        # a turn without a scored token has no loss: it forwards only when a later turn of its trajectory
+        # needs its state, and a trailing one never does
+        run.defer_unscored_turns = True
 
     def append_scored_turn(self, group_id, traj_id, tokens, scored, *, teacher_logprobs, token_weights=None,
                            return_loss: bool = True):
