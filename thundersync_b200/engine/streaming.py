@@ -1175,6 +1175,8 @@ class StreamingRun:
             if not pending:
                 return done
             frontier = [n for n in pending if all(self._shared[c].finalized for c in n.children)]
+            if not frontier:
+                raise RuntimeError("shared prompt forest has no node whose children are all done")
             batch = frontier if self.shared_prefix_vjp_backend == "ready_frontier" else frontier[:1]
             self._run_shared_vjps(batch, sink)
             done += len(batch)
