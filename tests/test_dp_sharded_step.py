@@ -70,3 +70,29 @@ def test_gradient_observers_are_refused_under_the_sharded_step():
     _feed(dp, batch)
     with pytest.raises(RuntimeError, match="observers"):
         dp.step(gradient_observer=lambda *a: None)
+
+
+class _FailingBackward:
+    def __init__(self, abort_error=None):
+        self.aborted = False
+        self.abort_error = abort_error
+
+    def close_group(self, group_id):
+        raise KeyError(group_id)
+
+    def abort(self):
+        self.aborted = True
+        if self.abort_error is not None:
+            raise self.abort_error
+
+
+@pytest.mark.parametrize("abort_error", [None, OSError("abort failed")])
+def test_a_failed_event_aborts_the_backward_and_reraises_its_own_error(abort_error):
+    dp = _trainer(build_model(53), sharded=False)
+    dp.bw = _FailingBackward(abort_error)
+    before = dp._local_groups_closed
+    with pytest.raises(KeyError) as raised:
+        dp.close_group(3)
+    assert dp.bw.aborted and dp._local_groups_closed == before
+    notes = getattr(raised.value, "__notes__", [])
+    assert (any("abort failed" in n for n in notes)) is (abort_error is not None)

@@ -185,11 +185,13 @@ class DataParallelThunderSync:
     def _abort_on_failure(self) -> Iterator[None]:
         try:
             yield
-        except BaseException:
+        except BaseException as exc:
+            # the event's own error is the one to see; an abort that also fails is noted on it
             try:
                 self.bw.abort()
-            finally:
-                raise
+            except BaseException as abort_exc:  # noqa: BLE001
+                exc.add_note(f"aborting the backward after this error also failed: {abort_exc!r}")
+            raise
 
     # ------------------------------------------------------------ events
     def open_group(self, group_id: int, prompt_tokens: list[int]) -> None:
