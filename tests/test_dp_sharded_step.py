@@ -96,3 +96,23 @@ def test_a_failed_event_aborts_the_backward_and_reraises_its_own_error(abort_err
     assert dp.bw.aborted and dp._local_groups_closed == before
     notes = getattr(raised.value, "__notes__", [])
     assert (any("abort failed" in n for n in notes)) is (abort_error is not None)
+
+
+def test_final_forest_configuration_rules():
+    m = build_model(54)
+    plain = DataParallelThunderSync(m, torch.optim.AdamW([p for p in m.parameters()], lr=1e-3),
+                                    run_factory=_factory, source_offload_mode="device_resident",
+                                    source_offload_device=None)
+    with pytest.raises(ValueError, match="direct_when_group_bound"):
+        plain.configure_final_forest(4096, 256)
+    direct = DataParallelThunderSync(m, torch.optim.AdamW([p for p in m.parameters()], lr=1e-3),
+                                     run_factory=_factory, source_offload_mode="device_resident",
+                                     source_offload_device=None, direct_when_group_bound=True)
+    assert not direct.final_forest_enabled
+    with pytest.raises(RuntimeError, match="not configured"):
+        direct.final_forest_max_tokens
+    for cap, chunk in ((0, 256), (4096, 0)):
+        with pytest.raises(ValueError, match="positive"):
+            direct.configure_final_forest(cap, chunk)
+    direct.configure_final_forest(4096, 256)
+    assert direct.final_forest_enabled and direct.final_forest_max_tokens == 4096

@@ -270,8 +270,13 @@ class DataParallelThunderSync:
 
     # ------------------------------------------------------------ final work
     def configure_final_forest(self, max_tokens_per_microbatch: int, chunk: int = 1024) -> None:
+        """Token cap of the final forest's micro-batches (claimed peer work) and of a claim chunk. ``chunk``
+        is validated and kept for the reference's signature; the forest's LM head uses its default row
+        block."""
         if max_tokens_per_microbatch <= 0 or chunk <= 0:
             raise ValueError("the final forest's token cap and chunk must be positive")
+        if not self.bw.direct_when_group_bound:
+            raise ValueError("the final forest runs direct closes: construct with direct_when_group_bound=True")
         self._final_forest = (int(max_tokens_per_microbatch), int(chunk))
 
     @property
