@@ -81,10 +81,10 @@ def test_single_trajectory_falls_back_to_checkpointing_with_the_attention_cache(
     ref, _ = _sink_grad(model, items)
     real = ff._microbatch
 
-    def no_plain(model_, mb, sink, *, checkpoint=False, cache=None):
+    def no_plain(model_, mb, sink, *, checkpoint=False, cache=None, rows=None):
         if not checkpoint:
             raise torch.OutOfMemoryError("injected: the plain forest does not fit")
-        real(model_, mb, sink, checkpoint=checkpoint, cache=cache)
+        real(model_, mb, sink, checkpoint=checkpoint, cache=cache, rows=rows)
 
     monkeypatch.setattr(ff, "_microbatch", no_plain)
     got, rep = _sink_grad(model, items)

@@ -86,11 +86,11 @@ def _run_checkpointed(ex, ids: torch.Tensor, pos: torch.Tensor, segs: list[Segme
 
 def forest_logprobs(model: torch.nn.Module, plan: ExecutionPlan | None = None, *, gate: bool = True,
                     stats: list[StepStats] | None = None, checkpoint: bool = False,
-                    attention_cache: Any = None) -> torch.Tensor:
+                    attention_cache: Any = None, rows: int | None = None) -> torch.Tensor:
     """Log-probs of the plan's scored tokens. ``checkpoint`` keeps only layer inputs for the backward
     (each layer is recomputed there); an :class:`~thundersync_b200.ops.attention.AttentionOutputCache`
     lets that recompute reuse attention outputs within its byte budget. ``plan=None`` runs the plan that
-    :func:`forest_context` bound for the model's device."""
+    :func:`forest_context` bound for the model's device; ``rows`` sets the LM head's rows per block."""
     assert_supported(model)
     dev = next(model.parameters()).device
     if plan is None:
@@ -111,7 +111,8 @@ def forest_logprobs(model: torch.nn.Module, plan: ExecutionPlan | None = None, *
         h, _ = ex.run(plan.token_ids, plan.position_ids, segs)
     w = ex.head_weight()
     if gate:
-        lp = lm_head_logprob(h.index_select(0, plan.score_src), w, plan.score_tgt)
+        kw = {} if rows is None else {"rows": rows}
+        lp = lm_head_logprob(h.index_select(0, plan.score_src), w, plan.score_tgt, **kw)
     else:  # measurement mode: project every position, then gather
         lp_all = torch.log_softmax(h.float() @ w.float().t(), -1)
         lp = lp_all[plan.score_src].gather(-1, plan.score_tgt[:, None]).squeeze(-1)

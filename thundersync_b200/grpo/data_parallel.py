@@ -270,9 +270,8 @@ class DataParallelThunderSync:
 
     # ------------------------------------------------------------ final work
     def configure_final_forest(self, max_tokens_per_microbatch: int, chunk: int = 1024) -> None:
-        """Token cap of the final forest's micro-batches (claimed peer work) and of a claim chunk. ``chunk``
-        is validated and kept for the reference's signature; the forest's LM head uses its default row
-        block."""
+        """Token cap of the final forest's micro-batches (claimed peer work) and of a claim chunk; ``chunk``
+        is the LM head's rows per block in those forwards."""
         if max_tokens_per_microbatch <= 0 or chunk <= 0:
             raise ValueError("the final forest's token cap and chunk must be positive")
         if not self.bw.direct_when_group_bound:

@@ -65,10 +65,10 @@ def forest_token_budget(device: torch.device, model: torch.nn.Module, *, fractio
 
 
 def _microbatch(model, items: list[FinalItem], sink: GradSink | None, *, checkpoint: bool = False,
-                cache=None) -> None:
+                cache=None, rows: int | None = None) -> None:
     trajs = [forest_trajectory(i) for i in items]
     plan = compile_plan(build_forest(trajs), device=next(model.parameters()).device)
-    lp = forest_logprobs(model, plan, checkpoint=checkpoint, attention_cache=cache)
+    lp = forest_logprobs(model, plan, checkpoint=checkpoint, attention_cache=cache, rows=rows)
     per = split_by_trajectory(plan, lp)
     total = None
     for it in items:
@@ -103,7 +103,7 @@ def _attention_cache_budget(device: torch.device) -> int:
 
 def backward_final_forest(model, items: list[FinalItem], *, max_tokens_per_microbatch: int,
                           sink: GradSink | None = None, transactional: bool | None = None,
-                          report: FinalForestReport | None = None) -> int:
+                          report: FinalForestReport | None = None, rows: int | None = None) -> int:
     """Backward ``Σ A_i S_i`` over ``items``; returns the number of micro-batches run.
 
     Memory ladder per micro-batch: run it as one forest; when that runs out of device memory, halve it
@@ -139,7 +139,7 @@ def backward_final_forest(model, items: list[FinalItem], *, max_tokens_per_micro
             target = GradSink(sink.arena, scratch, scale=sink.scale)
         cache = AttentionOutputCache(_attention_cache_budget(device)) if ckpt else None
         try:
-            _microbatch(model, mb, target, checkpoint=ckpt, cache=cache)
+            _microbatch(model, mb, target, checkpoint=ckpt, cache=cache, rows=rows)
         except torch.OutOfMemoryError:
             rep.out_of_memory += 1
             if scratch is None and sink is not None:
@@ -173,6 +173,7 @@ def backward_claimed_payloads(trainer: Any, payloads: list[bytes]) -> None:
     for p in payloads:
         gid, tid, adv, prompt, turns = decode_final_work(p)
         items.append(FinalItem(gid, tid, adv, tuple(prompt), tuple((tuple(t), tuple(s)) for t, s in turns)))
-    cap = trainer._final_forest[0] if getattr(trainer, "_final_forest", None) else 1 << 16
+    cfg = getattr(trainer, "_final_forest", None)
+    cap, rows = cfg if cfg else (1 << 16, None)
     sink = GradSink(trainer.arena, trainer.bw._main_grad())
-    backward_final_forest(trainer.model, items, max_tokens_per_microbatch=cap, sink=sink)
+    backward_final_forest(trainer.model, items, max_tokens_per_microbatch=cap, sink=sink, rows=rows)
