@@ -133,7 +133,9 @@ def attach_publication_handle(model: torch.nn.Module, peft_model: torch.nn.Modul
 
 
 def load_hybrid_causal_lm(snapshot: Path, *, device: torch.device, attn_implementation: str = "native"):
-    """Text model + lm_head of a local hybrid vision-language snapshot (keys remapped, coverage checked)."""
+    """Text model + lm_head of a local hybrid vision-language snapshot (keys remapped, coverage checked).
+    ``attn_implementation`` is accepted for the reference's signature: attention always runs through this
+    package's kernels."""
     if not Path(snapshot).is_dir():
         raise ValueError(f"the hybrid snapshot loader reads a local snapshot directory; {str(snapshot)!r} is not "
                          "one (download the snapshot first)")
@@ -156,7 +158,9 @@ def _random_model(name: str, device: torch.device):
 
 
 def load_policy_model(config: PolicyModelConfig, device: torch.device, *, attn_implementation: str = "native"):
-    """Policy model of one trainer rank in training mode, with its adapter (if any) attached."""
+    """Policy model of one trainer rank in training mode, with its adapter (if any) attached.
+    ``attn_implementation`` is accepted for the reference's signature: attention always runs through this
+    package's kernels."""
     device = torch.device(device)
     require_native_bf16(device)
     path = str(config.model_path)
